@@ -1,0 +1,163 @@
+/* nh_kernels.h — C ABI of the sm_100a kernels behind nuthatch's per-token
+ * OLMoE forward.
+ *
+ * Every entry point launches on `stream` (a cudaStream_t passed as void*),
+ * never synchronises and never allocates.  Device buffers are owned by the
+ * caller.  Return value: NH_OK or a negative NH_E_* code (argument checks are
+ * done on the host before any launch).  Citations name the reference call
+ * site (file:line within chen3feng/nuthatch) each kernel replaces; the
+ * reference runs those ops on ggml's CPU backend.
+ *
+ * Weights stay in their native GGUF super-block layout (Q4_K: 144 bytes per
+ * 256 values, Q6_K: 210 bytes per 256 values, or F32).  Device regions that
+ * hold weights must carry at least 32 bytes of readable tail padding: rows are
+ * staged with 16-byte copies rounded outwards.
+ *
+ * Activations that meet a quantised weight are quantised to Q8_K inside the
+ * kernel exactly as ggml's CPU mul_mat does (per 256 values: the element of
+ * largest magnitude maps to -127, round half to even), and each 256-value
+ * super-block contributes an exact integer dot product scaled in f32.
+ */
+#ifndef NH_KERNELS_H_
+#define NH_KERNELS_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NH_TYPE_F32 0
+#define NH_TYPE_Q4_K 12
+#define NH_TYPE_Q6_K 14
+
+#define NH_OK 0
+#define NH_E_ARG (-1)         /* bad argument (null pointer, size, unsupported shape) */
+#define NH_E_CUDA (-2)        /* a CUDA launch or API call failed */
+#define NH_E_TYPE (-3)        /* unsupported tensor type for this kernel */
+#define NH_E_IO (-4)          /* file or read error (host API) */
+#define NH_E_STATE (-5)       /* object in the wrong state (host API) */
+#define NH_E_NOMEM (-6)       /* device or host allocation failed (host API) */
+#define NH_E_CAPACITY (-7)    /* request beyond a stated capacity */
+
+/* Per-sequence decode cursor, resident in device memory.  The kernels read
+ * `pos` (tokens already in the KV cache); nh_lm_head_argmax advances it, so a
+ * captured step can be replayed without the host.  Token ids for positions
+ * below n_prompt come from the prompt array; later ones from `token`, the id
+ * the last argmax fed back (generate.cc:93-102). */
+typedef struct NhDecodeState {
+  int32_t pos;
+  int32_t n_prompt;
+  int32_t n_predict;
+  int32_t n_out;   /* generated ids written so far */
+  int32_t token;   /* id fed back by the last argmax */
+  int32_t error;   /* first kernel-side error code, 0 if none */
+  int32_t pad0;
+  int32_t pad1;
+} NhDecodeState;
+
+/* Query helpers. */
+int nh_device_sm_count(int device);
+/* Bytes of scratch the split attention / argmax reductions need; see the
+ * kernels below. */
+int64_t nh_attention_scratch_bytes(int n_head, int head_dim, int max_seq);
+int64_t nh_argmax_scratch_bytes(int n_vocab);
+
+/* Embedding row lookup for the token at state->pos (ggml_get_rows on
+ * token_embd, forward.cc:94-95, streaming_forward.cc:58-66): dequantises one
+ * row of `table` ([n_vocab] rows of n_embd) into h_out. */
+int nh_embed_step(const NhDecodeState* state, const int32_t* prompt_ids, const void* table,
+                  int32_t type, int64_t n_embd, int64_t n_vocab, float* h_out, void* stream);
+
+/* RMSNorm(h)*attn_norm followed by the Q, K and V projections
+ * (attention.cc:128-132): q_out[n_embd], k_out[n_embd_kv], v_out[n_embd_kv].
+ * Each weight may be F32, Q4_K or Q6_K independently. */
+int nh_qkv_proj(const float* h, const float* attn_norm, float eps, const void* wq, int32_t tq,
+                const void* wk, int32_t tk, const void* wv, int32_t tv, int64_t n_embd,
+                int64_t n_embd_kv, float* q_out, float* k_out, float* v_out, void* stream);
+
+/* One decode position of cached attention (attention.cc:133-183): QK-norm
+ * over the full width (q_norm over n_embd, k_norm over n_embd_kv), NEOX RoPE
+ * at state->pos, append post-RoPE K and raw V to the f32 caches
+ * ([max_seq][n_embd_kv] per layer, kv_cache.cc:11-22), then causal softmax
+ * attention over positions 0..pos split across CTAs with a deterministic
+ * combine.  rope_cs is a [max_seq][head_dim/2] table of (cos, sin) pairs for
+ * theta_i = pos * base^(-2i/head_dim), theta advanced by repeated f32
+ * multiplication as ggml_rope_ext does (attention.cc:137-142); nh_rope_table
+ * fills it.  kq_scale = 1/sqrtf(head_dim) (attention.cc:175).  `scratch`
+ * holds nh_attention_scratch_bytes() bytes, zeroed once before first use (the
+ * kernel leaves its counters zeroed). */
+int nh_attention_step(const NhDecodeState* state, const float* q, const float* k,
+                      const float* v, const float* q_norm, const float* k_norm, float eps,
+                      int n_head, int n_head_kv, int head_dim, const float* rope_cs,
+                      float kq_scale, float* k_cache, float* v_cache, int max_seq,
+                      void* scratch, float* attn_out, void* stream);
+
+/* Host helper: fills rope_cs_host[max_seq][head_dim/2][2] (see above). */
+void nh_rope_table(float base, int head_dim, int max_seq, float* rope_cs_host);
+
+/* h_io[r] = h_io[r] + (W . x)[r]: output projection plus residual
+ * (attention.cc:183, forward.cc:106-108). */
+int nh_out_proj_residual(const float* x, const void* wo, int32_t to, int64_t n_embd,
+                         float* h_io, void* stream);
+
+/* Router (moe.cc:16-37, streaming_forward.cc:286-301): RMSNorm(h)*ffn_norm,
+ * F32 router GEMV, softmax over n_expert, top-k in descending probability
+ * (equal probabilities: lower expert id first), the selected probabilities
+ * (renormalised when norm_topk, clamped sum 6.103515625e-5).  Writes sel[k],
+ * wts[k]; when trace_sel is not null also trace_sel[pos*n_layers*k + layer*k
+ * + i] and trace_gap[pos*n_layers + layer] (k-th minus (k+1)-th probability). */
+int nh_router_topk(const NhDecodeState* state, const float* h, const float* ffn_norm,
+                   float eps, const float* router, int64_t n_embd, int n_expert, int k,
+                   int norm_topk, int32_t* sel, float* wts, int32_t* trace_sel,
+                   float* trace_gap, int layer, int n_layers, void* scratch, void* stream);
+int64_t nh_router_scratch_bytes(int n_expert);
+
+/* Expert up/gate projections and SwiGLU (moe.cc:41-46): for i < k,
+ * ff[i][r] = silu((gate_e . b)[r]) * (up_e . b)[r] with e = wsel[i] and
+ * b = RMSNorm(h)*ffn_norm.  gate/up are [n_slots][n_ff][n_embd] with
+ * per-expert stride *_nb2 bytes (the resident expert tensors or the slot pool). */
+int nh_moe_gate_up(const float* h, const float* ffn_norm, float eps, const int32_t* wsel, int k,
+                   const void* gate, int32_t tg, uint64_t gate_nb2, const void* up, int32_t tu,
+                   uint64_t up_nb2, int64_t n_embd, int64_t n_ff, float* ff, void* stream);
+
+/* Down projections, routing weights and residual (moe.cc:47-60,
+ * forward.cc:117-119): h_io[r] = h_io[r] + sum_i wts[i]*(down_e . ff[i])[r],
+ * the products rounded before the adds and summed in top-k order.  When
+ * dump is not null and state->pos >= n_prompt-1, h_io is also copied to
+ * dump[(pos-n_prompt+1)*dump_step_stride + dump_offset + r]. */
+int nh_moe_down_combine(const NhDecodeState* state, const float* ff, const int32_t* wsel,
+                        const float* wts, int k, const void* down, int32_t td,
+                        uint64_t down_nb2, int64_t n_ff, int64_t n_embd, float* h_io,
+                        float* dump, int64_t dump_step_stride, int64_t dump_offset,
+                        void* stream);
+
+/* Output norm, lm_head GEMV and greedy argmax (forward.cc:123-125,
+ * generate.cc:93-102): first maximum wins.  Skipped (beyond the state
+ * advance) for positions before the last prompt token.  The last CTA writes
+ * out_tokens[n_out], feeds the id back into state->token, and advances
+ * state->pos (and n_out).  logits_dump, when not null, receives the logits of
+ * each generated step at [(pos-n_prompt+1)*n_vocab]. */
+int nh_lm_head_argmax(NhDecodeState* state, const float* h, const float* out_norm, float eps,
+                      const void* w, int32_t tw, int64_t n_embd, int64_t n_vocab,
+                      int32_t* out_tokens, float* logits_dump, void* scratch, void* stream);
+
+/* ---- standalone forms used by the parity tests ---- */
+
+/* y[r] = (W . x)[r] for r < rows (ggml_mul_mat for one activation row); when
+ * norm_w is not null x is first RMS-normalised and multiplied by norm_w. */
+int nh_gemv(const void* w, int32_t type, int64_t n, int64_t rows, const float* x,
+            const float* norm_w, float eps, float* y, void* stream);
+
+/* Q8_K quantisation of n values (n a multiple of 256) into 292-byte blocks
+ * (f32 d, int8 qs[256], int16 bsums[16]). */
+int nh_quantize_q8k(const float* x, int64_t n, void* out, void* stream);
+
+/* Dequantise `rows` rows of n values (ggml dequantize_row_*). */
+int nh_dequantize(const void* w, int32_t type, int64_t n, int64_t rows, float* y, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NH_KERNELS_H_ */

@@ -1,0 +1,51 @@
+// Greedy generation on one B200 (reference: src/model/generate.h:16-33).
+//
+// Each token runs the per-token forward on the device: embedding, n_layers x
+// (QKV, fused QK-norm/RoPE/KV-append/attention, output projection + residual,
+// router top-k, expert gate/up SwiGLU, expert down + weighted combine +
+// residual), output norm + lm_head + argmax.  The decode cursor lives in
+// device memory, so the whole generation is enqueued without host round
+// trips (one CUDA graph replay per token when graphs are on) and the host
+// reads the generated ids once at the end.
+#ifndef NUTHATCH_B200_GENERATE_H_
+#define NUTHATCH_B200_GENERATE_H_
+
+#include <cstdint>
+#include <vector>
+
+#include "nuthatch/olmoe_model.h"
+#include "nuthatch/routing_trace.h"
+
+namespace nuthatch {
+
+// Optional outputs and switches (no reference counterpart: debugging and
+// parity hooks).
+struct GenerateOptions {
+  bool use_graph = true;          // replay a captured CUDA graph per token
+  RoutingTrace* trace = nullptr;  // routing records, token-major (generate.cc:154-166)
+  std::vector<float>* trace_gap = nullptr;  // per (token, layer): k-th minus (k+1)-th probability
+  std::vector<float>* hidden = nullptr;     // per step, per layer h after the MoE residual [n_predict][L][d]
+  std::vector<float>* logits = nullptr;     // per step logits [n_predict][V]
+  int status = 0;                            // NH_OK or the first error code
+};
+
+// Full recompute of the sequence every step (generate.cc:10-53).
+std::vector<int32_t> GreedyGenerate(const OlmoeModel& model, std::vector<int32_t> ids,
+                                    int n_predict, bool norm_topk);
+
+// KV-cached greedy decode (generate.cc:55-106).  Returns the n_predict new ids.
+std::vector<int32_t> GreedyGenerateCached(const OlmoeModel& model, std::vector<int32_t> ids,
+                                          int n_predict, bool norm_topk);
+
+// Same, with the routing of every processed token appended to *trace
+// (generate.cc:108-181).
+std::vector<int32_t> GreedyGenerateCachedTrace(const OlmoeModel& model, std::vector<int32_t> ids,
+                                               int n_predict, bool norm_topk, RoutingTrace* trace);
+
+// The general form used by the three above.
+std::vector<int32_t> GreedyGenerateCachedEx(const OlmoeModel& model, const std::vector<int32_t>& ids,
+                                            int n_predict, bool norm_topk, GenerateOptions* opt);
+
+}  // namespace nuthatch
+
+#endif  // NUTHATCH_B200_GENERATE_H_

@@ -1,0 +1,110 @@
+"""ctypes bindings of libnuthatch_b200.so (include/nh_api.h, include/nh_kernels.h).
+
+The library is built in-tree by ``python -m nuthatch_b200.build``.  A missing
+library is an error: there is no fallback implementation.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+LIB_DIR = Path(__file__).resolve().parent / "lib"
+LIB_PATH = LIB_DIR / "libnuthatch_b200.so"
+
+i32, i64, u32, u64, f32 = C.c_int32, C.c_int64, C.c_uint32, C.c_uint64, C.c_float
+vp, cp = C.c_void_p, C.c_char_p
+P = C.POINTER
+
+
+class NhConfig(C.Structure):
+    _fields_ = [("n_layers", u32), ("n_embd", u32), ("n_head", u32), ("n_head_kv", u32), ("n_ff", u32),
+                ("n_expert", u32), ("n_expert_used", u32), ("n_vocab", u32), ("n_ctx_train", u32),
+                ("rope_freq_base", f32), ("rms_eps", f32)]
+
+
+class NhDecodeState(C.Structure):
+    _fields_ = [("pos", i32), ("n_prompt", i32), ("n_predict", i32), ("n_out", i32), ("token", i32),
+                ("error", i32), ("pad0", i32), ("pad1", i32)]
+
+
+# name -> (restype, argtypes)
+SIGNATURES = {
+    # nh_api.h
+    "nh_version": (cp, []),
+    "nh_set_device": (C.c_int, [C.c_int]),
+    "nh_last_error": (cp, []),
+    "nh_gguf_probe": (C.c_int, [cp, P(NhConfig)]),
+    "nh_model_load": (vp, [cp]),
+    "nh_model_free": (None, [vp]),
+    "nh_model_config": (C.c_int, [vp, P(NhConfig)]),
+    "nh_model_tensor": (C.c_int, [vp, cp, P(i64), P(i32), P(vp), P(u64)]),
+    "nh_generate": (C.c_int, [vp, C.c_int, P(i32), C.c_int, C.c_int, C.c_int, C.c_int, P(i32), P(i32), P(f32),
+                              P(f32), P(f32)]),
+    "nh_generate_launches": (C.c_int, [vp]),
+    "nh_decode_prepare": (C.c_int, [vp, P(i32), C.c_int, C.c_int]),
+    "nh_decode_run": (C.c_int, [vp, C.c_int]),
+    "nh_decode_result": (C.c_int, [vp, C.c_int, P(i32)]),
+    "nh_model_stream": (vp, [vp]),
+    "nh_decode_kernel_loop": (C.c_int, [vp, C.c_int, C.c_int]),
+    "nh_stream_model_load": (vp, [cp, C.c_int]),
+    "nh_stream_model_free": (None, [vp]),
+    "nh_stream_model_config": (C.c_int, [vp, P(NhConfig)]),
+    "nh_stream_generate": (C.c_int, [vp, P(i32), C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, P(u64),
+                                     P(i32), P(i64), P(i64), P(u64), P(i32)]),
+    "nh_replay": (i64, [C.c_int, u32, u32, i64, P(u32), P(i64), P(u32), u32, u32, P(u64), P(i64)]),
+    "nh_sweep_budgets": (C.c_int, [u32, u32, i64, P(u32), P(i64), P(u32), P(u32), C.c_int, P(C.c_double)]),
+    "nh_sweep_pin_ratio": (C.c_int, [u32, u32, i64, P(u32), P(i64), P(u32), u32, P(C.c_double)]),
+    "nh_trace_write": (C.c_int, [cp, u32, u32, i64, P(u32), P(u32), P(i64), P(u32)]),
+    "nh_trace_read": (i64, [cp, C.c_int, P(u32), P(u32), P(i64), i64, i64, P(u32), P(u32), P(i64), P(u32)]),
+    "nh_expert_reader_open": (vp, [cp]),
+    "nh_expert_reader_free": (None, [vp]),
+    "nh_expert_reader_bytes": (u64, [vp, cp]),
+    "nh_expert_reader_read": (C.c_int, [vp, cp, C.c_int, vp]),
+    "nh_slot_cache_create": (vp, [P(NhConfig), C.c_int, C.c_int, vp, C.c_int, C.c_int, P(u64)]),
+    "nh_slot_cache_free": (None, [vp]),
+    "nh_slot_cache_ensure": (C.c_int, [vp, P(i32), C.c_int, P(i32)]),
+    "nh_slot_cache_hits": (i64, [vp]),
+    "nh_slot_cache_misses": (i64, [vp]),
+    "nh_slot_cache_read_slot": (C.c_int, [vp, C.c_int, C.c_int, vp, u64]),
+    # nh_kernels.h
+    "nh_device_sm_count": (C.c_int, [C.c_int]),
+    "nh_attention_scratch_bytes": (i64, [C.c_int, C.c_int, C.c_int]),
+    "nh_argmax_scratch_bytes": (i64, [C.c_int]),
+    "nh_router_scratch_bytes": (i64, [C.c_int]),
+    "nh_rope_table": (None, [f32, C.c_int, C.c_int, P(f32)]),
+    "nh_embed_step": (C.c_int, [vp, vp, vp, i32, i64, i64, vp, vp]),
+    "nh_qkv_proj": (C.c_int, [vp, vp, f32, vp, i32, vp, i32, vp, i32, i64, i64, vp, vp, vp, vp]),
+    "nh_attention_step": (C.c_int, [vp, vp, vp, vp, vp, vp, f32, C.c_int, C.c_int, C.c_int, vp, f32, vp, vp,
+                                    C.c_int, vp, vp, vp]),
+    "nh_out_proj_residual": (C.c_int, [vp, vp, i32, i64, vp, vp]),
+    "nh_router_topk": (C.c_int, [vp, vp, vp, f32, vp, i64, C.c_int, C.c_int, C.c_int, vp, vp, vp, vp, C.c_int,
+                                 C.c_int, vp, vp]),
+    "nh_moe_gate_up": (C.c_int, [vp, vp, f32, vp, C.c_int, vp, i32, u64, vp, i32, u64, i64, i64, vp, vp]),
+    "nh_moe_down_combine": (C.c_int, [vp, vp, vp, vp, C.c_int, vp, i32, u64, i64, i64, vp, vp, i64, i64, vp]),
+    "nh_lm_head_argmax": (C.c_int, [vp, vp, vp, f32, vp, i32, i64, i64, vp, vp, vp, vp]),
+    "nh_gemv": (C.c_int, [vp, i32, i64, i64, vp, vp, f32, vp, vp]),
+    "nh_quantize_q8k": (C.c_int, [vp, i64, vp, vp]),
+    "nh_dequantize": (C.c_int, [vp, i32, i64, i64, vp, vp]),
+}
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """Loads the native library (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"{LIB_PATH} is missing: run `python -m nuthatch_b200.build` "
+                               "(there is no non-native implementation)")
+        handle = C.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def exported_symbols() -> list[str]:
+    return sorted(SIGNATURES)

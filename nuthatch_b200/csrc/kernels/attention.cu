@@ -1,0 +1,294 @@
+// Decode-step attention over the f32 KV cache, fused with QK-norm, NEOX RoPE
+// and the KV append.
+//
+// Grid (n_head, n_split): CTA (h, s) owns positions [s*kAttnSplit,
+// (s+1)*kAttnSplit) of query head h.  Every CTA re-derives the normalised,
+// rotated query of its head (the QK-norm spans the full width, so each CTA
+// reduces the whole q row; a few KB of L2 reads).  The CTA whose range holds
+// the current position also forms the current K/V row itself, and the first
+// query head of each KV head appends it to the cache, so no CTA reads a cache
+// row that is being written.  Partial (max, sum, weighted V) triples are
+// combined by the last CTA of each head in split order, so the result does
+// not depend on CTA scheduling.
+#include <cmath>
+
+#include "common.cuh"
+
+namespace nh {
+
+constexpr int kAttnThreads = 128;
+constexpr int kAttnSplit = 256;
+
+struct AttnArgs {
+  const NhDecodeState* state;
+  const float* q;
+  const float* k;
+  const float* v;
+  const float* q_norm;
+  const float* k_norm;
+  float eps;
+  int n_head, n_head_kv, hd;
+  const float* rope_cs;
+  float kq_scale;
+  float* k_cache;
+  float* v_cache;
+  int n_split;
+  unsigned* tickets;
+  double* part_l;
+  float* part_m;
+  float* part_acc;
+  float* out;
+};
+
+// Block-wide RMS scale of x[0..n) with ggml_rms_norm semantics.
+__device__ float rms_scale_block(const float* x, int n, float eps, double* red) {
+  double s = 0.0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = x[i];
+    s += static_cast<double>(__fmul_rn(v, v));
+  }
+  s = warp_sum_d(s);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += red[w];
+    red[32] = t;
+  }
+  __syncthreads();
+  const float mean = static_cast<float>(red[32] / static_cast<double>(n));
+  __syncthreads();
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+}
+
+__device__ void rope_inplace(float* x, int hd, const float* cs) {
+  const int half = hd / 2;
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    const float c = cs[2 * i], s = cs[2 * i + 1];
+    const float x0 = x[i], x1 = x[i + half];
+    x[i] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+    x[i + half] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+  }
+}
+
+__global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs p) {
+  const int h = blockIdx.x, sp = blockIdx.y;
+  const int pos = p.state->pos;
+  const int n_kv = pos + 1;
+  const int n_active = (n_kv + kAttnSplit - 1) / kAttnSplit;
+  if (sp >= n_active) return;
+  extern __shared__ __align__(16) float sm[];
+  const int hd = p.hd;
+  float* qh = sm;
+  float* kc = sm + hd;
+  float* vc = sm + 2 * hd;
+  float* sc = sm + 3 * hd;
+  __shared__ double red[40];
+  __shared__ float s_max;
+  __shared__ bool s_last;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
+  const int group = p.n_head / p.n_head_kv;
+  const int kh = h / group;
+  const int dq = p.n_head * hd, dkv = p.n_head_kv * hd;
+  const float* cs = p.rope_cs + static_cast<int64_t>(pos) * hd;
+
+  const float sq = rms_scale_block(p.q, dq, p.eps, red);
+  for (int i = tid; i < hd; i += blockDim.x) {
+    qh[i] = __fmul_rn(__fmul_rn(p.q[h * hd + i], sq), p.q_norm[h * hd + i]);
+  }
+  __syncthreads();
+  rope_inplace(qh, hd, cs);
+
+  const int p0 = sp * kAttnSplit;
+  const int p1 = min(n_kv, p0 + kAttnSplit);
+  const bool covers_cur = (p1 == n_kv);
+  if (covers_cur) {
+    const float sk = rms_scale_block(p.k, dkv, p.eps, red);
+    for (int i = tid; i < hd; i += blockDim.x) {
+      kc[i] = __fmul_rn(__fmul_rn(p.k[kh * hd + i], sk), p.k_norm[kh * hd + i]);
+      vc[i] = p.v[kh * hd + i];
+    }
+    __syncthreads();
+    rope_inplace(kc, hd, cs);
+    __syncthreads();
+    if (h % group == 0) {
+      float* kd = p.k_cache + static_cast<int64_t>(pos) * dkv + kh * hd;
+      float* vd = p.v_cache + static_cast<int64_t>(pos) * dkv + kh * hd;
+      for (int i = tid; i < hd; i += blockDim.x) {
+        kd[i] = kc[i];
+        vd[i] = vc[i];
+      }
+    }
+  }
+  __syncthreads();
+
+  // Scores kq = K.q * kq_scale, one warp per position.
+  for (int j = p0 + warp; j < p1; j += nw) {
+    const float* kr = (j == pos) ? kc : p.k_cache + static_cast<int64_t>(j) * dkv + kh * hd;
+    float d = 0.f;
+    for (int i = lane; i < hd; i += 32) d = __fadd_rn(d, __fmul_rn(kr[i], qh[i]));
+    d = warp_sum(d);
+    if (lane == 0) sc[j - p0] = __fmul_rn(d, p.kq_scale);
+  }
+  __syncthreads();
+  const int n = p1 - p0;
+  float m = -INFINITY;
+  for (int j = tid; j < n; j += blockDim.x) m = fmaxf(m, sc[j]);
+  m = warp_max(m);
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  if (tid == 0) {
+    float t = -INFINITY;
+    for (int w = 0; w < nw; ++w) t = fmaxf(t, static_cast<float>(red[w]));
+    s_max = t;
+  }
+  __syncthreads();
+  m = s_max;
+  double l = 0.0;
+  for (int j = tid; j < n; j += blockDim.x) {
+    const float e = expf(__fsub_rn(sc[j], m));
+    sc[j] = e;
+    l += static_cast<double>(e);
+  }
+  l = warp_sum_d(l);
+  __syncthreads();
+  if (lane == 0) red[warp] = l;
+  __syncthreads();
+  if (tid == 0) {
+    double t = 0.0;
+    for (int w = 0; w < nw; ++w) t += red[w];
+    red[32] = t;
+  }
+  __syncthreads();
+  l = red[32];
+
+  float* out = p.out + h * hd;
+  if (n_active == 1) {
+    // ggml_soft_max scales the exponentials by 1/sum before the V product.
+    const float inv = static_cast<float>(1.0 / l);
+    for (int j = tid; j < n; j += blockDim.x) sc[j] = __fmul_rn(sc[j], inv);
+    __syncthreads();
+    for (int i = tid; i < hd; i += blockDim.x) {
+      float acc = 0.f;
+      for (int j = 0; j < n; ++j) {
+        const float vv = (p0 + j == pos) ? vc[i] : p.v_cache[static_cast<int64_t>(p0 + j) * dkv + kh * hd + i];
+        acc = __fadd_rn(acc, __fmul_rn(vv, sc[j]));
+      }
+      out[i] = acc;
+    }
+    return;
+  }
+  const int slot = h * p.n_split + sp;
+  for (int i = tid; i < hd; i += blockDim.x) {
+    float acc = 0.f;
+    for (int j = 0; j < n; ++j) {
+      const float vv = (p0 + j == pos) ? vc[i] : p.v_cache[static_cast<int64_t>(p0 + j) * dkv + kh * hd + i];
+      acc = __fadd_rn(acc, __fmul_rn(vv, sc[j]));
+    }
+    p.part_acc[static_cast<int64_t>(slot) * hd + i] = acc;
+  }
+  if (tid == 0) {
+    p.part_m[slot] = m;
+    p.part_l[slot] = l;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    const unsigned t = atomicAdd(&p.tickets[h], 1u);
+    s_last = (t == static_cast<unsigned>(n_active - 1));
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  volatile float* pm = p.part_m;
+  volatile double* pl = p.part_l;
+  volatile float* pa = p.part_acc;
+  float M = -INFINITY;
+  for (int s = 0; s < n_active; ++s) M = fmaxf(M, pm[h * p.n_split + s]);
+  double L = 0.0;
+  for (int s = 0; s < n_active; ++s) {
+    L += pl[h * p.n_split + s] * static_cast<double>(expf(__fsub_rn(pm[h * p.n_split + s], M)));
+  }
+  const float inv = static_cast<float>(1.0 / L);
+  for (int i = tid; i < hd; i += blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < n_active; ++s) {
+      const float w = expf(__fsub_rn(pm[h * p.n_split + s], M));
+      acc = __fadd_rn(acc, __fmul_rn(pa[static_cast<int64_t>(h * p.n_split + s) * hd + i], w));
+    }
+    out[i] = __fmul_rn(acc, inv);
+  }
+  if (tid == 0) p.tickets[h] = 0u;
+}
+
+int attn_splits(int max_seq) { return (max_seq + kAttnSplit - 1) / kAttnSplit; }
+
+}  // namespace nh
+
+using namespace nh;
+
+extern "C" int64_t nh_attention_scratch_bytes(int n_head, int head_dim, int max_seq) {
+  const int64_t S = attn_splits(max_seq);
+  return 256 + n_head * S * (8 + 4 + 4 * static_cast<int64_t>(head_dim)) + 512;
+}
+
+extern "C" void nh_rope_table(float base, int head_dim, int max_seq, float* cs) {
+  const int half = head_dim / 2;
+  const float theta_scale = std::pow(base, -2.0f / static_cast<float>(head_dim));
+  for (int p = 0; p < max_seq; ++p) {
+    float theta = static_cast<float>(p);
+    for (int i = 0; i < half; ++i) {
+      cs[(static_cast<int64_t>(p) * half + i) * 2 + 0] = std::cos(theta);
+      cs[(static_cast<int64_t>(p) * half + i) * 2 + 1] = std::sin(theta);
+      theta *= theta_scale;
+    }
+  }
+}
+
+extern "C" int nh_attention_step(const NhDecodeState* state, const float* q, const float* k,
+                                 const float* v, const float* q_norm, const float* k_norm,
+                                 float eps, int n_head, int n_head_kv, int head_dim,
+                                 const float* rope_cs, float kq_scale, float* k_cache,
+                                 float* v_cache, int max_seq, void* scratch, float* attn_out,
+                                 void* stream) {
+  if (state == nullptr || q == nullptr || k == nullptr || v == nullptr || q_norm == nullptr ||
+      k_norm == nullptr || rope_cs == nullptr || k_cache == nullptr || v_cache == nullptr ||
+      scratch == nullptr || attn_out == nullptr) {
+    return NH_E_ARG;
+  }
+  if (n_head <= 0 || n_head_kv <= 0 || n_head % n_head_kv != 0 || head_dim <= 0 ||
+      head_dim % 2 != 0 || head_dim > 1024 || max_seq <= 0) {
+    return NH_E_ARG;
+  }
+  AttnArgs p;
+  p.state = state;
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  p.q_norm = q_norm;
+  p.k_norm = k_norm;
+  p.eps = eps;
+  p.n_head = n_head;
+  p.n_head_kv = n_head_kv;
+  p.hd = head_dim;
+  p.rope_cs = rope_cs;
+  p.kq_scale = kq_scale;
+  p.k_cache = k_cache;
+  p.v_cache = v_cache;
+  p.n_split = attn_splits(max_seq);
+  uint8_t* sc = static_cast<uint8_t*>(scratch);
+  p.tickets = reinterpret_cast<unsigned*>(sc);
+  const int64_t slots = static_cast<int64_t>(n_head) * p.n_split;
+  int64_t off = 256;
+  p.part_l = reinterpret_cast<double*>(sc + off);
+  off += slots * 8;
+  p.part_m = reinterpret_cast<float*>(sc + off);
+  off += slots * 4;
+  off = (off + 15) & ~15ll;
+  p.part_acc = reinterpret_cast<float*>(sc + off);
+  p.out = attn_out;
+  const size_t smem = static_cast<size_t>(3 * head_dim + kAttnSplit) * sizeof(float);
+  dim3 grid(n_head, p.n_split);
+  attention_kernel<<<grid, kAttnThreads, smem, static_cast<cudaStream_t>(stream)>>>(p);
+  return cudaGetLastError() == cudaSuccess ? NH_OK : NH_E_CUDA;
+}

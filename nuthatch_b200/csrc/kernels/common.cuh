@@ -1,0 +1,331 @@
+// Shared device helpers for the sm_100a kernels: GGUF block formats, the Q8_K
+// activation (the arithmetic ggml's CPU mul_mat applies to activations that
+// meet a Q4_K/Q6_K weight), cp.async row staging and warp reductions.
+//
+// Rounding: every f32 product/sum that the reference rounds separately is
+// written with __fmul_rn/__fadd_rn/__fsub_rn so nvcc cannot contract it into
+// an FMA; integer sub-block sums are exact.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../../include/nh_kernels.h"
+
+namespace nh {
+
+constexpr int QK = 256;
+constexpr int kQ4KBytes = 144;
+constexpr int kQ6KBytes = 210;
+constexpr int kMaxK = 4096;  // longest activation row the kernels stage in shared memory
+
+__host__ __device__ inline size_t row_bytes(int type, int64_t n) {
+  return type == NH_TYPE_Q4_K   ? static_cast<size_t>(n / QK) * kQ4KBytes
+         : type == NH_TYPE_Q6_K ? static_cast<size_t>(n / QK) * kQ6KBytes
+                                : static_cast<size_t>(n) * 4;
+}
+
+__device__ __forceinline__ float half_bits_to_float(uint32_t bits16) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16 & 0xFFFF)));
+}
+
+// ------------------------------------------------------------ warp helpers
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// ------------------------------------------------------------ cp.async staging
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+// Stages `bytes` bytes starting at `src` into `dst` (16-byte aligned shared
+// buffer of at least bytes + 32).  The copy starts at src rounded down to 16
+// bytes; the staged data begins at dst + (src & 15), which is returned.
+// Callers guarantee the 16-byte-rounded range stays inside the allocation
+// (device weight regions carry 256 bytes of tail padding).
+__device__ __forceinline__ const uint8_t* stage_bytes_warp(uint8_t* dst, const uint8_t* src,
+                                                           size_t bytes, int lane) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(src);
+  const uintptr_t al = a & ~static_cast<uintptr_t>(15);
+  const int off = static_cast<int>(a - al);
+  const int n16 = static_cast<int>((off + bytes + 15) >> 4);
+  const uint8_t* g = reinterpret_cast<const uint8_t*>(al);
+  for (int k = lane; k < n16; k += 32) cp_async16(dst + 16 * k, g + 16 * k);
+  return dst + off;
+}
+
+// ------------------------------------------------------------ activation (smem)
+// One activation row in shared memory: f32 values, and when the consumer
+// weights are quantised, its Q8_K form (int8 quants, per-256 scale, per-16 sums).
+struct ActSmem {
+  float* xf;       // [K]
+  int8_t* qs;      // [K]
+  float* d;        // [K/256]
+  int16_t* bsums;  // [K/16]
+  int K;
+};
+
+__host__ __device__ inline size_t act_smem_bytes(int K) {
+  return static_cast<size_t>(K) * 4 + K + (K / QK + 1) * 4 + (K / 16 + 1) * 2 + 64;
+}
+
+__device__ inline ActSmem carve_act(uint8_t* base, int K) {
+  ActSmem a;
+  a.K = K;
+  a.xf = reinterpret_cast<float*>(base);
+  a.qs = reinterpret_cast<int8_t*>(base + static_cast<size_t>(K) * 4);
+  uintptr_t p = reinterpret_cast<uintptr_t>(a.qs + K);
+  p = (p + 15) & ~static_cast<uintptr_t>(15);
+  a.d = reinterpret_cast<float*>(p);
+  p += (K / QK + 1) * 4;
+  p = (p + 15) & ~static_cast<uintptr_t>(15);
+  a.bsums = reinterpret_cast<int16_t*>(p);
+  return a;
+}
+
+// Block-wide: xf = src (optionally RMS-normalised and multiplied by norm_w with
+// ggml_rms_norm + ggml_mul semantics: sum of squares in double, scale =
+// 1/sqrtf(mean + eps), y = (x*scale)*w), then Q8_K-quantised if `quant`.
+// `red` is >= 33 doubles of shared scratch.  Ends with __syncthreads().
+__device__ inline void prep_act(ActSmem& a, const float* __restrict__ src,
+                                const float* __restrict__ norm_w, bool do_norm, float eps,
+                                bool quant, double* red) {
+  const int K = a.K;
+  const int tid = threadIdx.x, nt = blockDim.x;
+  float scale = 1.f;
+  if (do_norm) {
+    double s = 0.0;
+    for (int i = tid; i < K; i += nt) {
+      const float v = src[i];
+      s += static_cast<double>(__fmul_rn(v, v));
+    }
+    s = warp_sum_d(s);
+    if ((tid & 31) == 0) red[tid >> 5] = s;
+    __syncthreads();
+    if (tid < 32) {
+      double t = tid < (nt >> 5) ? red[tid] : 0.0;
+      t = warp_sum_d(t);
+      if (tid == 0) red[32] = t;
+    }
+    __syncthreads();
+    const float mean = static_cast<float>(red[32] / static_cast<double>(K));
+    scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+  }
+  for (int i = tid; i < K; i += nt) {
+    float v = src[i];
+    if (do_norm) {
+      v = __fmul_rn(v, scale);
+      if (norm_w != nullptr) v = __fmul_rn(v, norm_w[i]);
+    }
+    a.xf[i] = v;
+  }
+  __syncthreads();
+  if (!quant) return;
+  // quantize_row_q8_K semantics, one warp per 256-block: the first element of
+  // largest magnitude maps to -127 (iscale = -127/max, d = 1/iscale), round
+  // half to even, clamp at +127, 16 partial sums.
+  const int warp = tid >> 5, lane = tid & 31, nw = nt >> 5;
+  for (int b = warp; b < K / QK; b += nw) {
+    const float* x = a.xf + b * QK;
+    float amax = 0.f, mx = 0.f;
+    int idx = 1 << 30;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int i = lane * 8 + k;
+      const float ax = fabsf(x[i]);
+      if (ax > amax) {
+        amax = ax;
+        mx = x[i];
+        idx = i;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float oa = __shfl_xor_sync(0xffffffffu, amax, o);
+      const float om = __shfl_xor_sync(0xffffffffu, mx, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+      if (oa > amax || (oa == amax && oi < idx)) {
+        amax = oa;
+        mx = om;
+        idx = oi;
+      }
+    }
+    int8_t* q = a.qs + b * QK;
+    if (amax == 0.f) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) q[lane * 8 + k] = 0;
+      if (lane < 16) a.bsums[b * 16 + lane] = 0;
+      if (lane == 0) a.d[b] = 0.f;
+      continue;
+    }
+    const float iscale = __fdiv_rn(-127.f, mx);
+    int part = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      int v = __float2int_rn(__fmul_rn(iscale, x[lane * 8 + k]));
+      v = min(127, v);
+      q[lane * 8 + k] = static_cast<int8_t>(v);
+      part += v;
+    }
+    part += __shfl_xor_sync(0xffffffffu, part, 1);
+    if ((lane & 1) == 0) a.bsums[b * 16 + (lane >> 1)] = static_cast<int16_t>(part);
+    if (lane == 0) a.d[b] = __fdiv_rn(1.f, iscale);
+  }
+  __syncthreads();
+}
+
+// ------------------------------------------------------------ super-block dots
+// One lane computes one whole super-block's contribution.  `blk` points into
+// shared memory; `q8`/`bs` are the activation's quants and 16-sums for the
+// same 256 elements; `yd` its scale.  Result as the oracle forms it per
+// super-block: (d*yd)*sumi - (dmin*yd)*summ.
+__device__ __forceinline__ void q4k_scale_min(const uint8_t* s, int j, int& sc, int& m) {
+  if (j < 4) {
+    sc = s[j] & 63;
+    m = s[4 + j] & 63;
+  } else {
+    sc = (s[j + 4] & 15) | ((s[j - 4] >> 6) << 4);
+    m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+  }
+}
+
+__device__ __forceinline__ float sb_dot_q4k(const uint8_t* blk, const int8_t* q8,
+                                            const int16_t* bs, float yd) {
+  const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
+  const float d = half_bits_to_float(hdr.x);
+  const float dmin = half_bits_to_float(hdr.x >> 16);
+  uint8_t s[12];
+  *reinterpret_cast<uint32_t*>(s + 0) = hdr.y;
+  *reinterpret_cast<uint32_t*>(s + 4) = hdr.z;
+  *reinterpret_cast<uint32_t*>(s + 8) = hdr.w;
+  int sumi = 0, summ = 0;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const uint4 w0 = *reinterpret_cast<const uint4*>(blk + 16 + 32 * c);
+    const uint4 w1 = *reinterpret_cast<const uint4*>(blk + 32 + 32 * c);
+    const int4 xa = *reinterpret_cast<const int4*>(q8 + 64 * c);
+    const int4 xb = *reinterpret_cast<const int4*>(q8 + 64 * c + 16);
+    const int4 xc = *reinterpret_cast<const int4*>(q8 + 64 * c + 32);
+    const int4 xd = *reinterpret_cast<const int4*>(q8 + 64 * c + 48);
+    const uint32_t m4 = 0x0F0F0F0Fu;
+    int lo = 0, hi = 0;
+    lo = __dp4a(static_cast<int>(w0.x & m4), xa.x, lo);
+    lo = __dp4a(static_cast<int>(w0.y & m4), xa.y, lo);
+    lo = __dp4a(static_cast<int>(w0.z & m4), xa.z, lo);
+    lo = __dp4a(static_cast<int>(w0.w & m4), xa.w, lo);
+    lo = __dp4a(static_cast<int>(w1.x & m4), xb.x, lo);
+    lo = __dp4a(static_cast<int>(w1.y & m4), xb.y, lo);
+    lo = __dp4a(static_cast<int>(w1.z & m4), xb.z, lo);
+    lo = __dp4a(static_cast<int>(w1.w & m4), xb.w, lo);
+    hi = __dp4a(static_cast<int>((w0.x >> 4) & m4), xc.x, hi);
+    hi = __dp4a(static_cast<int>((w0.y >> 4) & m4), xc.y, hi);
+    hi = __dp4a(static_cast<int>((w0.z >> 4) & m4), xc.z, hi);
+    hi = __dp4a(static_cast<int>((w0.w >> 4) & m4), xc.w, hi);
+    hi = __dp4a(static_cast<int>((w1.x >> 4) & m4), xd.x, hi);
+    hi = __dp4a(static_cast<int>((w1.y >> 4) & m4), xd.y, hi);
+    hi = __dp4a(static_cast<int>((w1.z >> 4) & m4), xd.z, hi);
+    hi = __dp4a(static_cast<int>((w1.w >> 4) & m4), xd.w, hi);
+    int sc0, m0, sc1, m1;
+    q4k_scale_min(s, 2 * c, sc0, m0);
+    q4k_scale_min(s, 2 * c + 1, sc1, m1);
+    sumi += sc0 * lo + sc1 * hi;
+    summ += m0 * (bs[4 * c] + bs[4 * c + 1]) + m1 * (bs[4 * c + 2] + bs[4 * c + 3]);
+  }
+  const float dd = __fmul_rn(d, yd), dm = __fmul_rn(dmin, yd);
+  return __fsub_rn(__fmul_rn(dd, static_cast<float>(sumi)), __fmul_rn(dm, static_cast<float>(summ)));
+}
+
+// Unaligned 32-bit read from shared memory (the address is at least 2-byte aligned).
+__device__ __forceinline__ uint32_t ld32u(const uint8_t* p) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~static_cast<uintptr_t>(3));
+  return __funnelshift_r(w[0], w[1], static_cast<uint32_t>((a & 3) * 8));
+}
+
+__device__ __forceinline__ float sb_dot_q6k(const uint8_t* blk, const int8_t* q8,
+                                            const int16_t* bs, float yd) {
+  const uint8_t* ql = blk;
+  const uint8_t* qh = blk + 128;
+  int grp[16];
+#pragma unroll
+  for (int g = 0; g < 16; ++g) grp[g] = 0;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+#pragma unroll
+    for (int l4 = 0; l4 < 8; ++l4) {
+      const uint32_t A = ld32u(ql + 64 * h + 4 * l4);
+      const uint32_t B = ld32u(ql + 64 * h + 32 + 4 * l4);
+      const uint32_t H = ld32u(qh + 32 * h + 4 * l4);
+      const uint32_t m4 = 0x0F0F0F0Fu, m2 = 0x30303030u;
+      const uint32_t q0 = (A & m4) | ((H << 4) & m2);
+      const uint32_t q1 = (B & m4) | ((H << 2) & m2);
+      const uint32_t q2 = ((A >> 4) & m4) | (H & m2);
+      const uint32_t q3 = ((B >> 4) & m4) | ((H >> 2) & m2);
+      const int base = 128 * h + 4 * l4;
+      const int g = 8 * h + (l4 >> 2);
+      grp[g + 0] = __dp4a(static_cast<int>(q0), *reinterpret_cast<const int*>(q8 + base), grp[g + 0]);
+      grp[g + 2] = __dp4a(static_cast<int>(q1), *reinterpret_cast<const int*>(q8 + base + 32), grp[g + 2]);
+      grp[g + 4] = __dp4a(static_cast<int>(q2), *reinterpret_cast<const int*>(q8 + base + 64), grp[g + 4]);
+      grp[g + 6] = __dp4a(static_cast<int>(q3), *reinterpret_cast<const int*>(q8 + base + 96), grp[g + 6]);
+    }
+  }
+  const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192);
+  int sumi = 0;
+#pragma unroll
+  for (int g = 0; g < 16; ++g) sumi += static_cast<int>(sc[g]) * (grp[g] - 32 * bs[g]);
+  const uint32_t dbits = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(blk + 208));
+  return __fmul_rn(__fmul_rn(half_bits_to_float(dbits), yd), static_cast<float>(sumi));
+}
+
+// Lanes per row for a row of `nsb` super-blocks: the next power of two, capped at 32.
+__host__ __device__ inline int lanes_per_row(int nsb) {
+  int l = 1;
+  while (l < nsb && l < 32) l <<= 1;
+  return l;
+}
+
+// Dot of one staged quantised row with the activation: lane `sub` of `lpr`
+// lanes handles super-blocks sub, sub+lpr, ...; result reduced over the lpr
+// lanes (valid in every one of them).  Super-blocks are summed as a tree.
+__device__ __forceinline__ float row_dot_q(const uint8_t* row, int type, int nsb, int sub,
+                                           int lpr, const ActSmem& a) {
+  float acc = 0.f;
+  for (int s = sub; s < nsb; s += lpr) {
+    const float v = type == NH_TYPE_Q4_K
+                        ? sb_dot_q4k(row + s * kQ4KBytes, a.qs + s * QK, a.bsums + s * 16, a.d[s])
+                        : sb_dot_q6k(row + s * kQ6KBytes, a.qs + s * QK, a.bsums + s * 16, a.d[s]);
+    acc = __fadd_rn(acc, v);
+  }
+  for (int o = 1; o < lpr; o <<= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+  return acc;
+}
+
+// f32 row (global memory) dot the f32 activation; whole warp, result in every lane.
+__device__ __forceinline__ float row_dot_f32(const float* __restrict__ w, const float* x, int K,
+                                             int lane) {
+  float s = 0.f;
+  for (int i = lane; i < K; i += 32) s = __fadd_rn(s, __fmul_rn(w[i], x[i]));
+  return warp_sum(s);
+}
+
+}  // namespace nh

@@ -1,0 +1,1058 @@
+// ORACLE — test infrastructure only.  Never linked, imported or called by the
+// product path (nuthatch_b200/); only tests/, __graft_entry__.smoke() and the
+// CPU-baseline leg of bench.py load it, as the checker.
+//
+// A plain C++ CPU restatement of nuthatch's per-token OLMoE forward:
+//   * graph structure from the reference sources (cited per function below:
+//     attention.cc:65-135, moe.cc:7-63, forward.cc:45-85, generate.cc:10-181,
+//     streaming_forward.cc:75-253, expert_slot_cache.cc:59-104,
+//     kv_cache.cc:5-23, olmoe_model.cc:31-54);
+//   * op arithmetic from ggml's published CPU semantics (ggml 0.11.1, pinned by
+//     the reference's vcpkg baseline, BLADE_ROOT:35-41; ggml itself is not in
+//     the reference tree): rms_norm sums squares in double, soft_max sums in
+//     double, mul_mat with a Q4_K/Q6_K weight first quantises the activation
+//     row to Q8_K (one f32 scale, 256 int8, 16 int16 partial sums per block)
+//     and forms integer sub-block dot products that are scaled in f32, NEOX
+//     RoPE advances theta by repeated multiplication by base^(-2/n_dims).
+//
+// Pinning: Q4_K/Q6_K bit layouts are checked against gguf-py's dequantisers;
+// the structural properties of the reference tests (cached == uncached,
+// streaming == resident, causality, trace well-formedness) are checked on the
+// reference's own LCG fixture; cache policies are checked against the
+// reference's own compiled src/cache code (oracle/_ref).  The quantised dot
+// arithmetic itself has no golden vector in the reference: parity unpinned
+// there beyond those checks.
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <condition_variable>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <fcntl.h>
+#include <functional>
+#include <list>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <thread>
+#include <unistd.h>
+#include <unordered_map>
+#include <unordered_set>
+#include <vector>
+
+namespace oracle {
+
+constexpr int QK = 256;
+constexpr int T_F32 = 0, T_Q4K = 12, T_Q6K = 14;
+
+// ---------------------------------------------------------------- thread pool
+class Pool {
+ public:
+  static Pool& Get() {
+    static Pool p;
+    return p;
+  }
+  void SetThreads(int n) {
+    Stop();
+    n_ = std::max(1, n);
+    for (int i = 1; i < n_; ++i) workers_.emplace_back([this, i] { Loop(i); });
+  }
+  int threads() const { return n_; }
+  // fn(begin, end) over [0, n) split into contiguous ranges, one per thread.
+  void For(int64_t n, const std::function<void(int64_t, int64_t)>& fn) {
+    if (n_ <= 1 || n < 2) {
+      fn(0, n);
+      return;
+    }
+    {
+      std::unique_lock<std::mutex> lk(mu_);
+      job_ = &fn;
+      job_n_ = n;
+      pending_ = n_ - 1;
+      ++gen_;
+    }
+    cv_.notify_all();
+    Run(0, fn, n);
+    std::unique_lock<std::mutex> lk(mu_);
+    done_cv_.wait(lk, [this] { return pending_ == 0; });
+    job_ = nullptr;
+  }
+  ~Pool() { Stop(); }
+
+ private:
+  Pool() { SetThreads(1); }
+  void Run(int tid, const std::function<void(int64_t, int64_t)>& fn, int64_t n) {
+    const int64_t per = (n + n_ - 1) / n_;
+    const int64_t b = std::min<int64_t>(n, per * tid), e = std::min<int64_t>(n, b + per);
+    if (b < e) fn(b, e);
+  }
+  void Loop(int tid) {
+    uint64_t seen = 0;
+    for (;;) {
+      const std::function<void(int64_t, int64_t)>* job;
+      int64_t n;
+      {
+        std::unique_lock<std::mutex> lk(mu_);
+        cv_.wait(lk, [&] { return stop_ || gen_ != seen; });
+        if (stop_) return;
+        seen = gen_;
+        job = job_;
+        n = job_n_;
+      }
+      Run(tid, *job, n);
+      {
+        std::unique_lock<std::mutex> lk(mu_);
+        if (--pending_ == 0) done_cv_.notify_all();
+      }
+    }
+  }
+  void Stop() {
+    {
+      std::unique_lock<std::mutex> lk(mu_);
+      stop_ = true;
+    }
+    cv_.notify_all();
+    for (auto& t : workers_) t.join();
+    workers_.clear();
+    stop_ = false;
+  }
+  int n_ = 1;
+  std::vector<std::thread> workers_;
+  std::mutex mu_;
+  std::condition_variable cv_, done_cv_;
+  const std::function<void(int64_t, int64_t)>* job_ = nullptr;
+  int64_t job_n_ = 0;
+  int pending_ = 0;
+  uint64_t gen_ = 0;
+  bool stop_ = false;
+};
+
+// ---------------------------------------------------------------- formats
+inline float Half(uint16_t u) {
+  _Float16 h;
+  std::memcpy(&h, &u, 2);
+  return static_cast<float>(h);
+}
+
+size_t RowBytes(int type, int64_t n) {
+  if (type == T_Q4K) return static_cast<size_t>(n / QK) * 144;
+  if (type == T_Q6K) return static_cast<size_t>(n / QK) * 210;
+  return static_cast<size_t>(n) * 4;
+}
+
+// Q4_K 6-bit scale/min unpacking (layout as in gguf-py quants.py Q4_K.get_scale_min).
+inline void Q4KScaleMin(const uint8_t* s, int j, int* sc, int* m) {
+  if (j < 4) {
+    *sc = s[j] & 63;
+    *m = s[4 + j] & 63;
+  } else {
+    *sc = (s[8 + j - 4] & 15) | ((s[j - 4] >> 6) << 4);
+    *m = (s[8 + j - 4] >> 4) | ((s[4 + j - 4] >> 6) << 4);
+  }
+}
+
+// dequantize_row_q4_K semantics: y = (d*sc)*q - (dmin*m), both products in f32.
+void DequantQ4K(const uint8_t* b, float* y) {
+  uint16_t dh, mh;
+  std::memcpy(&dh, b, 2);
+  std::memcpy(&mh, b + 2, 2);
+  const float d = Half(dh), dmin = Half(mh);
+  const uint8_t* sc = b + 4;
+  const uint8_t* qs = b + 16;
+  for (int c = 0; c < 4; ++c) {
+    int s0, m0, s1, m1;
+    Q4KScaleMin(sc, 2 * c, &s0, &m0);
+    Q4KScaleMin(sc, 2 * c + 1, &s1, &m1);
+    const float d0 = d * s0, n0 = dmin * m0, d1 = d * s1, n1 = dmin * m1;
+    for (int l = 0; l < 32; ++l) {
+      const float a = d0 * static_cast<float>(qs[32 * c + l] & 15);
+      const float bb = d1 * static_cast<float>(qs[32 * c + l] >> 4);
+      y[64 * c + l] = a - n0;
+      y[64 * c + 32 + l] = bb - n1;
+    }
+  }
+}
+
+inline int Q6KValue(const uint8_t* b, int i) {
+  const int h = i / 128, e = i % 128;
+  const uint8_t* ql = b;
+  const uint8_t* qh = b + 128;
+  const int lo = e < 64 ? (ql[64 * h + e] & 15) : (ql[64 * h + e - 64] >> 4);
+  const int hi = (qh[32 * h + e % 32] >> (2 * (e / 32))) & 3;
+  return (lo | (hi << 4)) - 32;
+}
+
+// dequantize_row_q6_K semantics: y = (d*sc)*(q-32).
+void DequantQ6K(const uint8_t* b, float* y) {
+  uint16_t dh;
+  std::memcpy(&dh, b + 208, 2);
+  const float d = Half(dh);
+  const int8_t* sc = reinterpret_cast<const int8_t*>(b + 192);
+  for (int i = 0; i < QK; ++i) y[i] = (d * sc[i / 16]) * static_cast<float>(Q6KValue(b, i));
+}
+
+void DequantRow(int type, const void* src, int64_t n, float* y) {
+  const uint8_t* b = static_cast<const uint8_t*>(src);
+  if (type == T_F32) {
+    std::memcpy(y, src, n * 4);
+  } else if (type == T_Q4K) {
+    for (int64_t i = 0; i < n / QK; ++i) DequantQ4K(b + 144 * i, y + QK * i);
+  } else if (type == T_Q6K) {
+    for (int64_t i = 0; i < n / QK; ++i) DequantQ6K(b + 210 * i, y + QK * i);
+  }
+}
+
+struct Q8K {
+  float d;
+  int8_t qs[QK];
+  int16_t bsums[QK / 16];
+};
+static_assert(sizeof(Q8K) == 292, "Q8_K block is 292 bytes");
+
+// quantize_row_q8_K semantics: the element of largest magnitude maps to -127
+// (iscale = -127/max, d = 1/iscale), round half to even, clamp at 127, and 16
+// partial sums of 16 quants.  An all-zero block gets d = 0.
+void QuantizeQ8K(const float* x, int64_t n, Q8K* y) {
+  for (int64_t b = 0; b < n / QK; ++b) {
+    const float* xb = x + QK * b;
+    float amax = 0.f, max = 0.f;
+    for (int j = 0; j < QK; ++j) {
+      const float ax = std::fabs(xb[j]);
+      if (ax > amax) {
+        amax = ax;
+        max = xb[j];
+      }
+    }
+    if (amax == 0.f) {
+      std::memset(&y[b], 0, sizeof(Q8K));
+      continue;
+    }
+    const float iscale = -127.f / max;
+    for (int j = 0; j < QK; ++j) {
+      const int v = static_cast<int>(std::nearbyint(iscale * xb[j]));
+      y[b].qs[j] = static_cast<int8_t>(std::min(127, v));
+    }
+    for (int j = 0; j < QK / 16; ++j) {
+      int s = 0;
+      for (int i = 0; i < 16; ++i) s += y[b].qs[16 * j + i];
+      y[b].bsums[j] = static_cast<int16_t>(s);
+    }
+    y[b].d = 1.f / iscale;
+  }
+}
+
+// Q4_K x Q8_K: per super-block, integer sums sum_j sc_j*<q4,q8>_j and
+// sum_j m_j*bsum_j, scaled by (d*yd) and (dmin*yd) in f32.
+float DotQ4K(const uint8_t* w, const Q8K* y, int64_t n) {
+  float sumf = 0.f;
+  for (int64_t b = 0; b < n / QK; ++b) {
+    const uint8_t* blk = w + 144 * b;
+    uint16_t dh, mh;
+    std::memcpy(&dh, blk, 2);
+    std::memcpy(&mh, blk + 2, 2);
+    const uint8_t* qs = blk + 16;
+    int32_t sumi = 0, summ = 0;
+    for (int j = 0; j < 8; ++j) {
+      int sc, m;
+      Q4KScaleMin(blk + 4, j, &sc, &m);
+      const int c = j / 2, hi = j % 2;
+      int32_t s = 0;
+      for (int l = 0; l < 32; ++l) {
+        const int q = hi ? (qs[32 * c + l] >> 4) : (qs[32 * c + l] & 15);
+        s += q * y[b].qs[32 * j + l];
+      }
+      sumi += sc * s;
+      summ += m * (y[b].bsums[2 * j] + y[b].bsums[2 * j + 1]);
+    }
+    const float d = Half(dh) * y[b].d;
+    const float dmin = Half(mh) * y[b].d;
+    sumf += d * static_cast<float>(sumi) - dmin * static_cast<float>(summ);
+  }
+  return sumf;
+}
+
+// Q6_K x Q8_K: per super-block, integer sum_j sc_j*<q6-32,q8>_j scaled by d*yd.
+float DotQ6K(const uint8_t* w, const Q8K* y, int64_t n) {
+  float sumf = 0.f;
+  for (int64_t b = 0; b < n / QK; ++b) {
+    const uint8_t* blk = w + 210 * b;
+    uint16_t dh;
+    std::memcpy(&dh, blk + 208, 2);
+    const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192);
+    int32_t sumi = 0;
+    for (int j = 0; j < 16; ++j) {
+      int32_t s = 0;
+      for (int l = 0; l < 16; ++l) s += Q6KValue(blk, 16 * j + l) * y[b].qs[16 * j + l];
+      sumi += sc[j] * s;
+    }
+    sumf += (Half(dh) * y[b].d) * static_cast<float>(sumi);
+  }
+  return sumf;
+}
+
+float DotF32(const float* a, const float* b, int64_t n) {
+  float s = 0.f;
+  for (int64_t i = 0; i < n; ++i) s += a[i] * b[i];
+  return s;
+}
+
+// ---------------------------------------------------------------- GGUF reading
+struct Tensor {
+  std::string name;
+  int type = -1;
+  int64_t ne[4] = {1, 1, 1, 1};
+  size_t nb1 = 0, nb2 = 0;  // row and matrix strides in bytes
+  uint64_t offset = 0;      // absolute file offset
+  const uint8_t* data = nullptr;
+  size_t nbytes = 0;
+};
+
+struct Config {
+  uint32_t n_layers = 0, n_embd = 0, n_head = 0, n_head_kv = 0, n_ff = 0;
+  uint32_t n_expert = 0, n_expert_used = 0, n_vocab = 0, n_ctx_train = 0;
+  float rope_freq_base = 10000.f, rms_eps = 1e-5f;
+  uint32_t head_dim() const { return n_head ? n_embd / n_head : 0; }
+};
+
+class Model {
+ public:
+  static std::unique_ptr<Model> Load(const std::string& path);
+  ~Model() {
+    if (map_ != nullptr) munmap(map_, size_);
+  }
+  const Tensor* T(const std::string& n) const {
+    auto it = tensors_.find(n);
+    return it == tensors_.end() ? nullptr : &it->second;
+  }
+  const Tensor* L(int l, const char* s) const { return T("blk." + std::to_string(l) + "." + s); }
+  Config cfg;
+
+ private:
+  void* map_ = nullptr;
+  size_t size_ = 0;
+  std::unordered_map<std::string, Tensor> tensors_;
+};
+
+struct Cursor {
+  const uint8_t* p;
+  const uint8_t* end;
+  bool ok = true;
+  template <typename V>
+  V Get() {
+    V v{};
+    if (p + sizeof(V) > end) {
+      ok = false;
+      return v;
+    }
+    std::memcpy(&v, p, sizeof(V));
+    p += sizeof(V);
+    return v;
+  }
+  std::string Str() {
+    const uint64_t n = Get<uint64_t>();
+    if (!ok || n > static_cast<uint64_t>(end - p)) {
+      ok = false;
+      return {};
+    }
+    std::string s(reinterpret_cast<const char*>(p), n);
+    p += n;
+    return s;
+  }
+  void Skip(uint32_t type) {
+    static const int sz[13] = {1, 1, 2, 2, 4, 4, 4, 1, 0, 0, 8, 8, 8};
+    if (type == 8) {
+      Str();
+    } else if (type == 9) {
+      const uint32_t et = Get<uint32_t>();
+      const uint64_t n = Get<uint64_t>();
+      for (uint64_t i = 0; i < n && ok; ++i) Skip(et);
+    } else if (type < 13) {
+      if (p + sz[type] > end) ok = false;
+      else p += sz[type];
+    } else {
+      ok = false;
+    }
+  }
+};
+
+std::unique_ptr<Model> Model::Load(const std::string& path) {
+  const int fd = open(path.c_str(), O_RDONLY);
+  if (fd < 0) return nullptr;
+  struct stat st;
+  if (fstat(fd, &st) != 0 || st.st_size < 24) {
+    close(fd);
+    return nullptr;
+  }
+  void* map = mmap(nullptr, st.st_size, PROT_READ, MAP_PRIVATE, fd, 0);
+  close(fd);
+  if (map == MAP_FAILED) return nullptr;
+  std::unique_ptr<Model> m(new Model());
+  m->map_ = map;
+  m->size_ = st.st_size;
+  const uint8_t* base = static_cast<const uint8_t*>(map);
+  Cursor c{base, base + st.st_size};
+  if (std::memcmp(base, "GGUF", 4) != 0) return nullptr;
+  c.p += 4;
+  const uint32_t version = c.Get<uint32_t>();
+  if (version != 2 && version != 3) return nullptr;
+  const uint64_t n_tensors = c.Get<uint64_t>();
+  const uint64_t n_kv = c.Get<uint64_t>();
+  std::unordered_map<std::string, uint32_t> u32;
+  std::unordered_map<std::string, float> f32;
+  std::unordered_map<std::string, std::string> str;
+  uint32_t alignment = 32;
+  for (uint64_t i = 0; i < n_kv && c.ok; ++i) {
+    const std::string key = c.Str();
+    const uint32_t type = c.Get<uint32_t>();
+    if (type == 4) u32[key] = c.Get<uint32_t>();
+    else if (type == 6) f32[key] = c.Get<float>();
+    else if (type == 8) str[key] = c.Str();
+    else c.Skip(type);
+  }
+  if (u32.count("general.alignment")) alignment = u32["general.alignment"];
+  std::vector<Tensor> infos;
+  for (uint64_t i = 0; i < n_tensors && c.ok; ++i) {
+    Tensor t;
+    t.name = c.Str();
+    const uint32_t nd = c.Get<uint32_t>();
+    if (nd > 4) return nullptr;
+    for (uint32_t d = 0; d < nd; ++d) t.ne[d] = static_cast<int64_t>(c.Get<uint64_t>());
+    t.type = static_cast<int>(c.Get<uint32_t>());
+    t.offset = c.Get<uint64_t>();
+    infos.push_back(t);
+  }
+  if (!c.ok) return nullptr;
+  const size_t hdr = static_cast<size_t>(c.p - base);
+  const size_t data_off = (hdr + alignment - 1) / alignment * alignment;
+  for (Tensor& t : infos) {
+    if (t.type != T_F32 && t.type != T_Q4K && t.type != T_Q6K) return nullptr;
+    if (t.type != T_F32 && t.ne[0] % QK != 0) return nullptr;
+    t.nb1 = RowBytes(t.type, t.ne[0]);
+    t.nb2 = t.nb1 * t.ne[1];
+    t.nbytes = t.nb2 * t.ne[2] * t.ne[3];
+    t.offset += data_off;
+    if (t.offset + t.nbytes > static_cast<size_t>(st.st_size)) return nullptr;
+    t.data = base + t.offset;
+    m->tensors_[t.name] = t;
+  }
+  // ParseOlmoeConfig, olmoe_model.cc:31-54: keys prefixed by general.architecture.
+  std::string arch = str.count("general.architecture") ? str["general.architecture"] : "";
+  if (arch.empty()) arch = "olmoe";
+  auto U = [&](const char* k, uint32_t def) {
+    auto it = u32.find(arch + "." + k);
+    return it == u32.end() ? def : it->second;
+  };
+  auto F = [&](const char* k, float def) {
+    auto it = f32.find(arch + "." + k);
+    return it == f32.end() ? def : it->second;
+  };
+  Config& g = m->cfg;
+  g.n_layers = U("block_count", 0);
+  g.n_embd = U("embedding_length", 0);
+  g.n_head = U("attention.head_count", 0);
+  g.n_head_kv = U("attention.head_count_kv", g.n_head);
+  g.n_ff = U("feed_forward_length", 0);
+  g.n_expert = U("expert_count", 0);
+  g.n_expert_used = U("expert_used_count", 0);
+  g.n_ctx_train = U("context_length", 0);
+  g.rope_freq_base = F("rope.freq_base", 10000.f);
+  g.rms_eps = F("attention.layer_norm_rms_epsilon", 1e-5f);
+  const Tensor* out = m->T("output.weight");
+  if (out == nullptr) out = m->T("token_embd.weight");
+  if (out != nullptr) g.n_vocab = static_cast<uint32_t>(out->ne[1]);
+  return m;
+}
+
+// ---------------------------------------------------------------- ops
+// ggml_rms_norm (sum of squares in double) followed by ggml_mul with w.
+void RmsNormMul(const float* x, const float* w, int64_t n, float eps, float* y) {
+  double sum = 0.0;
+  for (int64_t i = 0; i < n; ++i) sum += static_cast<double>(x[i] * x[i]);
+  const float mean = static_cast<float>(sum / static_cast<double>(n));
+  const float scale = 1.0f / std::sqrt(mean + eps);
+  for (int64_t i = 0; i < n; ++i) {
+    const float t = x[i] * scale;
+    y[i] = w != nullptr ? t * w[i] : t;
+  }
+}
+
+// ggml_soft_max over one row: exp(x - max) summed in double, scaled by 1/sum.
+void SoftMax(float* x, int64_t n) {
+  float mx = -INFINITY;
+  for (int64_t i = 0; i < n; ++i) mx = std::max(mx, x[i]);
+  double sum = 0.0;
+  for (int64_t i = 0; i < n; ++i) {
+    const float e = (x[i] == -INFINITY) ? 0.f : std::exp(x[i] - mx);
+    x[i] = e;
+    sum += static_cast<double>(e);
+  }
+  const float inv = static_cast<float>(1.0 / sum);
+  for (int64_t i = 0; i < n; ++i) x[i] *= inv;
+}
+
+// ggml_rope_ext, NEOX mode, ext_factor 0, freq_scale 1, attn_factor 1:
+// pair (i, i + n_dims/2) rotated by theta_i = pos * base^(-2i/n_dims), theta
+// advanced by repeated multiplication (attention.cc:88-93).
+void RopeNeox(float* x, int n_dims, int pos, float base) {
+  const float theta_scale = std::pow(base, -2.0f / static_cast<float>(n_dims));
+  float theta = static_cast<float>(pos);
+  const int half = n_dims / 2;
+  for (int i = 0; i < half; ++i) {
+    const float c = std::cos(theta), s = std::sin(theta);
+    const float x0 = x[i], x1 = x[i + half];
+    x[i] = x0 * c - x1 * s;
+    x[i + half] = x0 * s + x1 * c;
+    theta *= theta_scale;
+  }
+}
+
+inline float Silu(float x) { return x / (1.0f + std::exp(-x)); }
+
+// ggml_mul_mat(W, x) for one activation row over the rows [r0, r1) of a
+// (possibly 3-D expert) weight: quantised weights use the Q8_K activation.
+struct Act {
+  std::vector<float> f;
+  std::vector<Q8K> q;
+  void Set(const float* x, int64_t n, bool quant) {
+    f.assign(x, x + n);
+    if (quant) {
+      q.resize(n / QK);
+      QuantizeQ8K(x, n, q.data());
+    }
+  }
+};
+
+float RowDot(const Tensor& w, const uint8_t* row, const Act& a) {
+  const int64_t n = w.ne[0];
+  if (w.type == T_Q4K) return DotQ4K(row, a.q.data(), n);
+  if (w.type == T_Q6K) return DotQ6K(row, a.q.data(), n);
+  return DotF32(reinterpret_cast<const float*>(row), a.f.data(), n);
+}
+
+void MatVec(const Tensor& w, int64_t expert, const float* x, float* y, bool parallel = true) {
+  Act a;
+  a.Set(x, w.ne[0], w.type != T_F32);
+  const uint8_t* base = w.data + w.nb2 * expert;
+  auto body = [&](int64_t r0, int64_t r1) {
+    for (int64_t r = r0; r < r1; ++r) y[r] = RowDot(w, base + w.nb1 * r, a);
+  };
+  if (parallel) Pool::Get().For(w.ne[1], body);
+  else body(0, w.ne[1]);
+}
+
+// ---------------------------------------------------------------- forward
+struct Kv {
+  int max_seq = 0;
+  int64_t n_embd_kv = 0;
+  std::vector<std::vector<float>> k, v;  // per layer [max_seq][n_embd_kv]
+  int n_past = 0;
+  void Init(const Config& c, int max) {
+    max_seq = max;
+    n_embd_kv = static_cast<int64_t>(c.n_head_kv) * c.head_dim();
+    k.assign(c.n_layers, std::vector<float>(static_cast<size_t>(max) * n_embd_kv, 0.f));
+    v.assign(c.n_layers, std::vector<float>(static_cast<size_t>(max) * n_embd_kv, 0.f));
+    n_past = 0;
+  }
+};
+
+struct Observe {
+  // Per token processed (token-major): selected ids [L][k] and router gap [L].
+  std::vector<int32_t>* sel = nullptr;
+  std::vector<float>* gap = nullptr;
+  // Per layer hidden state after the MoE residual for the last token of the step.
+  std::vector<float>* hidden_last = nullptr;
+  // Called per (token, layer) with the selected ids in top-k order.
+  std::function<void(int layer, const std::vector<int32_t>& ids)> on_route;
+};
+
+// BuildForwardCached (forward.cc:45-85) over T new tokens at positions
+// n_past..n_past+T-1; writes the logits of every position ([T][V]).
+void ForwardCached(const Model& m, Kv* kv, const std::vector<int32_t>& tok, bool norm_topk,
+                   std::vector<float>* logits, Observe* obs) {
+  const Config& c = m.cfg;
+  const int64_t d = c.n_embd, hd = c.head_dim(), H = c.n_head, Hkv = c.n_head_kv;
+  const int64_t dkv = Hkv * hd, E = c.n_expert, K = c.n_expert_used, F = c.n_ff;
+  const int64_t V = c.n_vocab;
+  const int T = static_cast<int>(tok.size());
+  const int n_past = kv->n_past;
+  const int n_kv = n_past + T;
+  const int64_t group = H / Hkv;
+
+  // ggml_get_rows on token_embd (forward.cc:94-95): dequantised rows.
+  std::vector<float> h(static_cast<size_t>(T) * d);
+  const Tensor* emb = m.T("token_embd.weight");
+  for (int t = 0; t < T; ++t) DequantRow(emb->type, emb->data + emb->nb1 * tok[t], d, &h[t * d]);
+
+  if (obs && obs->sel) obs->sel->resize(static_cast<size_t>(T) * c.n_layers * K);
+  if (obs && obs->gap) obs->gap->resize(static_cast<size_t>(T) * c.n_layers);
+  if (obs && obs->hidden_last) obs->hidden_last->resize(static_cast<size_t>(c.n_layers) * d);
+
+  std::vector<float> cur(d), q(static_cast<size_t>(T) * d), k(static_cast<size_t>(T) * dkv),
+      v(static_cast<size_t>(T) * dkv), att(static_cast<size_t>(T) * d), tmp(std::max(d, dkv));
+  const float kq_scale = 1.0f / std::sqrt(static_cast<float>(hd));
+
+  for (int l = 0; l < static_cast<int>(c.n_layers); ++l) {
+    const float* attn_norm = reinterpret_cast<const float*>(m.L(l, "attn_norm.weight")->data);
+    const float* q_norm = reinterpret_cast<const float*>(m.L(l, "attn_q_norm.weight")->data);
+    const float* k_norm = reinterpret_cast<const float*>(m.L(l, "attn_k_norm.weight")->data);
+    // attention.cc:128-142: norm -> QKV -> QK-norm over the full width -> NEOX RoPE.
+    for (int t = 0; t < T; ++t) {
+      RmsNormMul(&h[t * d], attn_norm, d, c.rms_eps, cur.data());
+      MatVec(*m.L(l, "attn_q.weight"), 0, cur.data(), &q[t * d]);
+      MatVec(*m.L(l, "attn_k.weight"), 0, cur.data(), &k[t * dkv]);
+      MatVec(*m.L(l, "attn_v.weight"), 0, cur.data(), &v[t * dkv]);
+      RmsNormMul(&q[t * d], q_norm, d, c.rms_eps, tmp.data());
+      std::copy(tmp.begin(), tmp.begin() + d, q.begin() + t * d);
+      RmsNormMul(&k[t * dkv], k_norm, dkv, c.rms_eps, tmp.data());
+      std::copy(tmp.begin(), tmp.begin() + dkv, k.begin() + t * dkv);
+      for (int64_t hh = 0; hh < H; ++hh) {
+        RopeNeox(&q[t * d + hh * hd], static_cast<int>(hd), n_past + t, c.rope_freq_base);
+      }
+      for (int64_t hh = 0; hh < Hkv; ++hh) {
+        RopeNeox(&k[t * dkv + hh * hd], static_cast<int>(hd), n_past + t, c.rope_freq_base);
+      }
+      // attention.cc:145-153: the cache holds post-RoPE K and raw V at n_past+t.
+      std::copy(&k[t * dkv], &k[t * dkv] + dkv, kv->k[l].begin() + (n_past + t) * dkv);
+      std::copy(&v[t * dkv], &v[t * dkv] + dkv, kv->v[l].begin() + (n_past + t) * dkv);
+    }
+    // attention.cc:174-182: kq = K.q * 1/sqrt(hd), causal mask offset n_past, softmax, V.p.
+    Pool::Get().For(H * T, [&](int64_t b, int64_t e) {
+      std::vector<float> p(n_kv);
+      for (int64_t job = b; job < e; ++job) {
+        const int64_t hh = job / T;
+        const int t = static_cast<int>(job % T);
+        const int64_t kh = hh / group;
+        const float* qv = &q[t * d + hh * hd];
+        for (int j = 0; j < n_kv; ++j) {
+          if (j > n_past + t) {
+            p[j] = -INFINITY;
+          } else {
+            const float* kr = &kv->k[l][j * dkv + kh * hd];
+            p[j] = DotF32(kr, qv, hd) * kq_scale;
+          }
+        }
+        SoftMax(p.data(), n_kv);
+        for (int64_t i = 0; i < hd; ++i) {
+          float s = 0.f;
+          for (int j = 0; j < n_kv; ++j) s += kv->v[l][j * dkv + kh * hd + i] * p[j];
+          att[t * d + hh * hd + i] = s;
+        }
+      }
+    });
+    // Output projection and residual (forward.cc:106-108).
+    std::vector<float> o(d);
+    for (int t = 0; t < T; ++t) {
+      MatVec(*m.L(l, "attn_output.weight"), 0, &att[t * d], o.data());
+      for (int64_t i = 0; i < d; ++i) h[t * d + i] = h[t * d + i] + o[i];
+    }
+    // MoE, moe.cc:7-63.
+    const float* ffn_norm = reinterpret_cast<const float*>(m.L(l, "ffn_norm.weight")->data);
+    const Tensor* router = m.L(l, "ffn_gate_inp.weight");
+    const Tensor* gate = m.L(l, "ffn_gate_exps.weight");
+    const Tensor* up = m.L(l, "ffn_up_exps.weight");
+    const Tensor* down = m.L(l, "ffn_down_exps.weight");
+    std::vector<float> b(d), probs(E);
+    std::vector<float> y(static_cast<size_t>(K) * d), g(static_cast<size_t>(K) * F),
+        u(static_cast<size_t>(K) * F);
+    for (int t = 0; t < T; ++t) {
+      RmsNormMul(&h[t * d], ffn_norm, d, c.rms_eps, b.data());
+      MatVec(*router, 0, b.data(), probs.data(), false);
+      SoftMax(probs.data(), E);
+      // ggml_argsort_top_k: descending probability, ties by lower expert id.
+      std::vector<int32_t> order(E);
+      for (int64_t e = 0; e < E; ++e) order[e] = static_cast<int32_t>(e);
+      std::stable_sort(order.begin(), order.end(),
+                       [&](int32_t a, int32_t bb) { return probs[a] > probs[bb]; });
+      std::vector<int32_t> sel(order.begin(), order.begin() + K);
+      std::vector<float> wts(K);
+      for (int64_t i = 0; i < K; ++i) wts[i] = probs[sel[i]];
+      if (norm_topk) {
+        double s = 0.0;
+        for (int64_t i = 0; i < K; ++i) s += static_cast<double>(wts[i]);
+        const float ws = std::max(static_cast<float>(s), 6.103515625e-5f);
+        for (int64_t i = 0; i < K; ++i) wts[i] = wts[i] / ws;
+      }
+      if (obs && obs->sel) {
+        std::copy(sel.begin(), sel.end(), obs->sel->begin() + (static_cast<int64_t>(t) * c.n_layers + l) * K);
+      }
+      if (obs && obs->gap) {
+        (*obs->gap)[t * c.n_layers + l] = K < E ? probs[order[K - 1]] - probs[order[K]] : 1.f;
+      }
+      if (obs && obs->on_route) obs->on_route(l, sel);
+      // up, gate, silu(gate)*up, down for each selected expert.
+      Pool::Get().For(K * F * 2, [&](int64_t r0, int64_t r1) {
+        Act a;
+        a.Set(b.data(), d, gate->type != T_F32 || up->type != T_F32);
+        for (int64_t r = r0; r < r1; ++r) {
+          const int64_t i = r / (2 * F), rr = r % (2 * F);
+          const Tensor* w = rr < F ? up : gate;
+          const int64_t row = rr % F;
+          const float val = RowDot(*w, w->data + w->nb2 * sel[i] + w->nb1 * row, a);
+          (rr < F ? u : g)[i * F + row] = val;
+        }
+      });
+      std::vector<float> ff(static_cast<size_t>(K) * F);
+      for (int64_t i = 0; i < K * F; ++i) ff[i] = Silu(g[i]) * u[i];
+      Pool::Get().For(K * d, [&](int64_t r0, int64_t r1) {
+        Act a;
+        int64_t cur_i = -1;
+        for (int64_t r = r0; r < r1; ++r) {
+          const int64_t i = r / d, row = r % d;
+          if (i != cur_i) {
+            a.Set(&ff[i * F], F, down->type != T_F32);
+            cur_i = i;
+          }
+          y[i * d + row] = RowDot(*down, down->data + down->nb2 * sel[i] + down->nb1 * row, a);
+        }
+      });
+      // ggml_mul by the weights, then the chained adds in top-k order, then residual.
+      for (int64_t j = 0; j < d; ++j) {
+        float acc = y[j] * wts[0];
+        for (int64_t i = 1; i < K; ++i) {
+          const float term = y[i * d + j] * wts[i];
+          acc = acc + term;
+        }
+        h[t * d + j] = h[t * d + j] + acc;
+      }
+    }
+    if (obs && obs->hidden_last) {
+      std::copy(&h[(T - 1) * d], &h[(T - 1) * d] + d, obs->hidden_last->begin() + l * d);
+    }
+  }
+  // Output norm and lm_head (forward.cc:123-125), every position.
+  logits->resize(static_cast<size_t>(T) * V);
+  const float* onorm = reinterpret_cast<const float*>(m.T("output_norm.weight")->data);
+  for (int t = 0; t < T; ++t) {
+    RmsNormMul(&h[t * d], onorm, d, c.rms_eps, cur.data());
+    MatVec(*m.T("output.weight"), 0, cur.data(), &(*logits)[t * V]);
+  }
+}
+
+// Host argmax of generate.cc:93-98: first maximum wins (strict >).
+int Argmax(const float* v, int64_t n, float* gap) {
+  int best = 0;
+  for (int64_t i = 1; i < n; ++i)
+    if (v[i] > v[best]) best = static_cast<int>(i);
+  if (gap) {
+    float second = -INFINITY;
+    for (int64_t i = 0; i < n; ++i)
+      if (i != best) second = std::max(second, v[i]);
+    *gap = v[best] - second;
+  }
+  return best;
+}
+
+// ---------------------------------------------------------------- policies
+// Restated from the reference src/cache: LRU per layer (lru_policy.cc:8-30),
+// global LRU "OS page cache" (os_page_cache_policy.cc:7-25), learned pin
+// (learned_pin_policy.cc:8-59; equal usage counts break toward the lower id).
+class Policy {
+ public:
+  virtual ~Policy() = default;
+  virtual bool Access(uint32_t layer, uint32_t expert) = 0;
+};
+
+class LruList {
+ public:
+  explicit LruList(uint32_t cap) : cap_(cap) {}
+  bool Access(uint64_t key) {
+    auto it = pos_.find(key);
+    if (it != pos_.end()) {
+      order_.splice(order_.begin(), order_, it->second);
+      return true;
+    }
+    if (cap_ == 0) return false;
+    order_.push_front(key);
+    pos_[key] = order_.begin();
+    if (order_.size() > cap_) {
+      pos_.erase(order_.back());
+      order_.pop_back();
+    }
+    return false;
+  }
+
+ private:
+  uint64_t cap_;
+  std::list<uint64_t> order_;
+  std::unordered_map<uint64_t, std::list<uint64_t>::iterator> pos_;
+};
+
+class LruPolicy : public Policy {
+ public:
+  LruPolicy(uint32_t n_layers, uint32_t slots) : layers_(n_layers, LruList(slots)) {}
+  bool Access(uint32_t l, uint32_t e) override { return l < layers_.size() && layers_[l].Access(e); }
+
+ private:
+  std::vector<LruList> layers_;
+};
+
+class OsPolicy : public Policy {
+ public:
+  explicit OsPolicy(uint64_t cap) : lru_(static_cast<uint32_t>(cap)) {}
+  bool Access(uint32_t l, uint32_t e) override {
+    return lru_.Access((static_cast<uint64_t>(l) << 32) | e);
+  }
+
+ private:
+  LruList lru_;
+};
+
+// usage[l] is a list of (expert, count); pinned = top `pin` by count, ties by lower id.
+class LearnedPinPolicy : public Policy {
+ public:
+  LearnedPinPolicy(uint32_t n_layers, uint32_t pin, uint32_t lru,
+                   const std::vector<std::vector<uint64_t>>& usage)
+      : pinned_(n_layers), lru_(n_layers, LruList(lru)) {
+    for (uint32_t l = 0; l < n_layers && l < usage.size(); ++l) {
+      std::vector<std::pair<uint32_t, uint64_t>> v;
+      for (uint32_t e = 0; e < usage[l].size(); ++e)
+        if (usage[l][e] > 0) v.push_back({e, usage[l][e]});
+      std::stable_sort(v.begin(), v.end(), [](auto& a, auto& b) { return a.second > b.second; });
+      for (size_t i = 0; i < std::min<size_t>(pin, v.size()); ++i) pinned_[l].insert(v[i].first);
+    }
+  }
+  bool Access(uint32_t l, uint32_t e) override {
+    if (l >= pinned_.size()) return false;
+    if (pinned_[l].count(e)) return true;
+    return lru_[l].Access(e);
+  }
+
+ private:
+  std::vector<std::unordered_set<uint32_t>> pinned_;
+  std::vector<LruList> lru_;
+};
+
+}  // namespace oracle
+
+// ============================================================== C ABI (ctypes)
+using namespace oracle;
+
+extern "C" {
+
+struct OracleConfig {
+  uint32_t n_layers, n_embd, n_head, n_head_kv, n_ff, n_expert, n_expert_used, n_vocab,
+      n_ctx_train;
+  float rope_freq_base, rms_eps;
+};
+
+void oracle_set_threads(int n) { Pool::Get().SetThreads(n); }
+int oracle_threads() { return Pool::Get().threads(); }
+
+void* oracle_model_load(const char* path) { return Model::Load(path).release(); }
+void oracle_model_free(void* m) { delete static_cast<Model*>(m); }
+
+int oracle_model_config(void* mp, OracleConfig* out) {
+  const Config& c = static_cast<Model*>(mp)->cfg;
+  *out = {c.n_layers, c.n_embd, c.n_head, c.n_head_kv, c.n_ff, c.n_expert, c.n_expert_used,
+          c.n_vocab, c.n_ctx_train, c.rope_freq_base, c.rms_eps};
+  return 0;
+}
+
+// Byte view of one tensor (for tests comparing uploaded bytes).
+int oracle_tensor_info(void* mp, const char* name, int64_t* ne4, int* type, uint64_t* file_offset,
+                       uint64_t* nbytes) {
+  const Tensor* t = static_cast<Model*>(mp)->T(name);
+  if (t == nullptr) return -1;
+  for (int i = 0; i < 4; ++i) ne4[i] = t->ne[i];
+  *type = t->type;
+  *file_offset = t->offset;
+  *nbytes = t->nbytes;
+  return 0;
+}
+
+// Greedy generation.  mode 0: GreedyGenerateCached (one-shot prompt prefill,
+// generate.cc:55-106); 1: GreedyGenerate (full recompute per step,
+// generate.cc:10-53); 2: token-by-token prefill as StreamingGenerate does
+// (streaming_forward.cc:228-253).  Optional outputs, token-major over the
+// processed tokens (n_prompt + n_predict - 1 of them; for mode 1 the routing
+// of the final recompute):
+//   sel [n_tok][L][k], gap [n_tok][L]; per step: hidden [n_predict][L][d]
+//   (last position), logits [n_predict][V], logit_gap [n_predict].
+int oracle_generate(void* mp, int mode, const int32_t* prompt, int n_prompt, int n_predict,
+                    int norm_topk, int32_t* out_tokens, int32_t* sel_out, float* gap_out,
+                    float* hidden_out, float* logits_out, float* logit_gap_out) {
+  Model& m = *static_cast<Model*>(mp);
+  const Config& c = m.cfg;
+  if (n_prompt <= 0 || n_predict <= 0) return 0;
+  const int64_t L = c.n_layers, K = c.n_expert_used, V = c.n_vocab, d = c.n_embd;
+  std::vector<int32_t> ids(prompt, prompt + n_prompt);
+  Kv kv;
+  kv.Init(c, n_prompt + n_predict + 1);
+  std::vector<float> logits;
+  std::vector<int32_t> sel;
+  std::vector<float> gap, hid;
+  int64_t tok_done = 0;
+  auto record = [&](int T) {
+    if (sel_out) std::copy(sel.begin(), sel.begin() + T * L * K, sel_out + tok_done * L * K);
+    if (gap_out) std::copy(gap.begin(), gap.begin() + T * L, gap_out + tok_done * L);
+    tok_done += T;
+  };
+  std::vector<int32_t> cur = ids;
+  for (int step = 0; step < n_predict; ++step) {
+    Observe obs;
+    obs.sel = &sel;
+    obs.gap = &gap;
+    obs.hidden_last = &hid;
+    if (mode == 1) {
+      // Full recompute of the whole sequence from an empty cache; the routing
+      // recorded for this step is that of the tokens new at this step (the
+      // tail of the pass).
+      kv.Init(c, static_cast<int>(ids.size()) + 1);
+      ForwardCached(m, &kv, ids, norm_topk != 0, &logits, &obs);
+      const int newT = step == 0 ? static_cast<int>(ids.size()) : 1;
+      sel.erase(sel.begin(), sel.end() - static_cast<int64_t>(newT) * L * K);
+      gap.erase(gap.begin(), gap.end() - static_cast<int64_t>(newT) * L);
+      record(newT);
+    } else if (mode == 0) {
+      ForwardCached(m, &kv, cur, norm_topk != 0, &logits, &obs);
+      kv.n_past += static_cast<int>(cur.size());
+      record(static_cast<int>(cur.size()));
+    } else {
+      for (size_t i = 0; i < cur.size(); ++i) {
+        ForwardCached(m, &kv, {cur[i]}, norm_topk != 0, &logits, &obs);
+        kv.n_past += 1;
+        record(1);
+      }
+    }
+    const int T = static_cast<int>(logits.size() / V);
+    const float* last = &logits[static_cast<size_t>(T - 1) * V];
+    float lg = 0.f;
+    const int best = Argmax(last, V, &lg);
+    out_tokens[step] = best;
+    if (hidden_out) std::copy(hid.begin(), hid.end(), hidden_out + step * L * d);
+    if (logits_out) std::copy(last, last + V, logits_out + step * V);
+    if (logit_gap_out) logit_gap_out[step] = lg;
+    ids.push_back(best);
+    cur = {best};
+  }
+  return static_cast<int>(tok_done);
+}
+
+// BuildForward over T tokens from an empty cache (forward.cc:8-43): logits of
+// every position, [T][V].
+int oracle_forward(void* mp, const int32_t* tokens, int T, int norm_topk, float* logits_out) {
+  Model& m = *static_cast<Model*>(mp);
+  if (T <= 0) return -1;
+  Kv kv;
+  kv.Init(m.cfg, T + 1);
+  std::vector<float> logits;
+  ForwardCached(m, &kv, std::vector<int32_t>(tokens, tokens + T), norm_topk != 0, &logits, nullptr);
+  std::copy(logits.begin(), logits.end(), logits_out);
+  return 0;
+}
+
+// StreamingGenerate with a slot policy (streaming_forward.cc:228-253 and
+// expert_slot_cache.cc:83-104).  policy 0: per-layer LRU of `capacity` slots
+// (the reference ExpertSlotCache); 1: learned pin with pin_slots pinned and
+// capacity - pin_slots LRU slots, pinned set from usage [L][E].
+// Per layer hits/misses are written to hits_out/misses_out [L].
+int oracle_stream_generate(void* mp, const int32_t* prompt, int n_prompt, int n_predict,
+                           int norm_topk, int capacity, int policy, int pin_slots,
+                           const uint64_t* usage, int32_t* out_tokens, int64_t* hits_out,
+                           int64_t* misses_out) {
+  Model& m = *static_cast<Model*>(mp);
+  const Config& c = m.cfg;
+  if (n_prompt <= 0 || n_predict <= 0) return 0;
+  if (capacity <= 0) return -1;
+  std::unique_ptr<Policy> pol;
+  if (policy == 0) {
+    pol.reset(new LruPolicy(c.n_layers, capacity));
+  } else {
+    std::vector<std::vector<uint64_t>> u(c.n_layers, std::vector<uint64_t>(c.n_expert, 0));
+    for (uint32_t l = 0; l < c.n_layers; ++l)
+      for (uint32_t e = 0; e < c.n_expert; ++e) u[l][e] = usage[l * c.n_expert + e];
+    pol.reset(new LearnedPinPolicy(c.n_layers, pin_slots, capacity - pin_slots, u));
+  }
+  for (uint32_t l = 0; l < c.n_layers; ++l) hits_out[l] = misses_out[l] = 0;
+  Observe obs;
+  obs.on_route = [&](int layer, const std::vector<int32_t>& ids) {
+    std::unordered_set<int32_t> seen;
+    for (int32_t e : ids) {
+      if (!seen.insert(e).second) continue;  // in-batch dedup, expert_slot_cache.cc:87
+      if (pol->Access(layer, static_cast<uint32_t>(e))) ++hits_out[layer];
+      else ++misses_out[layer];
+    }
+  };
+  Kv kv;
+  kv.Init(c, n_prompt + n_predict + 1);
+  std::vector<float> logits;
+  for (int i = 0; i < n_prompt; ++i) {
+    ForwardCached(m, &kv, {prompt[i]}, norm_topk != 0, &logits, &obs);
+    kv.n_past += 1;
+  }
+  for (int step = 0; step < n_predict; ++step) {
+    const int next = Argmax(logits.data(), c.n_vocab, nullptr);
+    out_tokens[step] = next;
+    if (step + 1 < n_predict) {
+      ForwardCached(m, &kv, {next}, norm_topk != 0, &logits, &obs);
+      kv.n_past += 1;
+    }
+  }
+  return 0;
+}
+
+// ---- primitives for unit tests
+int oracle_dequant(int type, const void* src, int64_t n, float* dst) {
+  if (type != T_F32 && n % QK != 0) return -1;
+  DequantRow(type, src, n, dst);
+  return 0;
+}
+int oracle_quantize_q8k(const float* x, int64_t n, void* out) {
+  if (n % QK != 0) return -1;
+  QuantizeQ8K(x, n, static_cast<Q8K*>(out));
+  return 0;
+}
+// y[r] = W[r] . x for a 2-D weight of `rows` rows of n elements, ggml mul_mat semantics.
+int oracle_matvec(int type, const void* w, int64_t n, int64_t rows, const float* x, float* y) {
+  Tensor t;
+  t.type = type;
+  t.ne[0] = n;
+  t.ne[1] = rows;
+  t.nb1 = RowBytes(type, n);
+  t.nb2 = t.nb1 * rows;
+  t.data = static_cast<const uint8_t*>(w);
+  MatVec(t, 0, x, y);
+  return 0;
+}
+void oracle_rms_norm_mul(const float* x, const float* w, int64_t n, float eps, float* y) {
+  RmsNormMul(x, w, n, eps, y);
+}
+void oracle_rope_neox(float* x, int n_dims, int pos, float base) { RopeNeox(x, n_dims, pos, base); }
+void oracle_softmax(float* x, int64_t n) { SoftMax(x, n); }
+
+// ---- policies over a flat trace: records of (layer, n, experts...) given as
+// arrays layer[R], offsets[R+1] into experts[].  kind 0 LRU(slots), 1 OS(slots
+// total), 2 learned pin (pin, lru) with the usage histogram built from the
+// same trace (learned_pin_policy.cc:8-17).  Returns hits; *accesses set.
+int64_t oracle_replay(int kind, uint32_t n_layers, uint32_t n_expert, int64_t n_records,
+                      const uint32_t* layer, const int64_t* offsets, const uint32_t* experts,
+                      uint32_t a, uint32_t b, int64_t* accesses) {
+  std::unique_ptr<Policy> p;
+  if (kind == 0) {
+    p.reset(new LruPolicy(n_layers, a));
+  } else if (kind == 1) {
+    p.reset(new OsPolicy(a));
+  } else {
+    std::vector<std::vector<uint64_t>> u(n_layers, std::vector<uint64_t>(n_expert, 0));
+    for (int64_t r = 0; r < n_records; ++r) {
+      if (layer[r] >= n_layers) continue;
+      for (int64_t i = offsets[r]; i < offsets[r + 1]; ++i)
+        if (experts[i] < n_expert) ++u[layer[r]][experts[i]];
+    }
+    p.reset(new LearnedPinPolicy(n_layers, a, b, u));
+  }
+  int64_t hits = 0, acc = 0;
+  for (int64_t r = 0; r < n_records; ++r) {
+    for (int64_t i = offsets[r]; i < offsets[r + 1]; ++i) {
+      ++acc;
+      if (p->Access(layer[r], experts[i])) ++hits;
+    }
+  }
+  *accesses = acc;
+  return hits;
+}
+
+}  // extern "C"
