@@ -171,6 +171,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="prefill, warm-up, then exactly one timed-step's decode and exit (for ncu launch lists)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":
@@ -223,6 +225,13 @@ def main() -> None:
         assert L.nh_decode_run(m._h, N_PREDICT) == 0
     assert L.nh_decode_result(m._h, N_PREDICT, op) == 0
     ref_tokens = out.tolist()
+    if args.profile:
+        # Launches after the warm-up: exactly one step = N_PREDICT x launches_per_token kernels.
+        assert L.nh_decode_run(m._h, N_PREDICT) == 0
+        assert L.nh_decode_result(m._h, N_PREDICT, op) == 0
+        print(json.dumps({"profile_step_launches": N_PREDICT * L.nh_generate_launches(m._h),
+                          "launches_before": (N_PROMPT - 1 + args.warmup * N_PREDICT) * L.nh_generate_launches(m._h)}))
+        return
 
     # ---- timed region: K decode steps, inputs resident in HBM (weights 4.2 GB > L2)
     clocks = ClockSampler(local_rank)

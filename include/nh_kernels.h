@@ -13,6 +13,10 @@
  * hold weights must carry at least 32 bytes of readable tail padding: rows are
  * staged with 16-byte copies rounded outwards.
  *
+ * Kernels taking an NhDecodeState* record a failed bounded device-side wait
+ * as NH_E_TIMEOUT in state->error (the state may be NULL for the standalone
+ * forms, which then only stop early).
+ *
  * Activations that meet a quantised weight are quantised to Q8_K inside the
  * kernel exactly as ggml's CPU mul_mat does (per 256 values: the element of
  * largest magnitude maps to -127, round half to even), and each 256-value
@@ -39,6 +43,7 @@ extern "C" {
 #define NH_E_STATE (-5)       /* object in the wrong state (host API) */
 #define NH_E_NOMEM (-6)       /* device or host allocation failed (host API) */
 #define NH_E_CAPACITY (-7)    /* request beyond a stated capacity */
+#define NH_E_TIMEOUT (-8)     /* a bounded device-side wait expired (recorded in NhDecodeState.error) */
 
 /* Per-sequence decode cursor, resident in device memory.  The kernels read
  * `pos` (tokens already in the KV cache); nh_lm_head_argmax advances it, so a
@@ -72,8 +77,8 @@ int nh_embed_step(const NhDecodeState* state, const int32_t* prompt_ids, const v
 /* RMSNorm(h)*attn_norm followed by the Q, K and V projections
  * (attention.cc:128-132): q_out[n_embd], k_out[n_embd_kv], v_out[n_embd_kv].
  * Each weight may be F32, Q4_K or Q6_K independently. */
-int nh_qkv_proj(const float* h, const float* attn_norm, float eps, const void* wq, int32_t tq,
-                const void* wk, int32_t tk, const void* wv, int32_t tv, int64_t n_embd,
+int nh_qkv_proj(NhDecodeState* state, const float* h, const float* attn_norm, float eps, const void* wq,
+                int32_t tq, const void* wk, int32_t tk, const void* wv, int32_t tv, int64_t n_embd,
                 int64_t n_embd_kv, float* q_out, float* k_out, float* v_out, void* stream);
 
 /* One decode position of cached attention (attention.cc:133-183): QK-norm
@@ -98,15 +103,16 @@ void nh_rope_table(float base, int head_dim, int max_seq, float* rope_cs_host);
 
 /* h_io[r] = h_io[r] + (W . x)[r]: output projection plus residual
  * (attention.cc:183, forward.cc:106-108). */
-int nh_out_proj_residual(const float* x, const void* wo, int32_t to, int64_t n_embd,
-                         float* h_io, void* stream);
+int nh_out_proj_residual(NhDecodeState* state, const float* x, const void* wo, int32_t to,
+                         int64_t n_embd, float* h_io, void* stream);
 
 /* Router (moe.cc:16-37, streaming_forward.cc:286-301): RMSNorm(h)*ffn_norm,
  * F32 router GEMV, softmax over n_expert, top-k in descending probability
  * (equal probabilities: lower expert id first), the selected probabilities
  * (renormalised when norm_topk, clamped sum 6.103515625e-5).  Writes sel[k],
  * wts[k]; when trace_sel is not null also trace_sel[pos*n_layers*k + layer*k
- * + i] and trace_gap[pos*n_layers + layer] (k-th minus (k+1)-th probability). */
+ * + i] and trace_gap[pos*n_layers + layer] (the smallest difference between
+ * adjacent probabilities of the descending top-(k+1): the near-tie measure). */
 int nh_router_topk(const NhDecodeState* state, const float* h, const float* ffn_norm,
                    float eps, const float* router, int64_t n_embd, int n_expert, int k,
                    int norm_topk, int32_t* sel, float* wts, int32_t* trace_sel,
@@ -117,7 +123,8 @@ int64_t nh_router_scratch_bytes(int n_expert);
  * ff[i][r] = silu((gate_e . b)[r]) * (up_e . b)[r] with e = wsel[i] and
  * b = RMSNorm(h)*ffn_norm.  gate/up are [n_slots][n_ff][n_embd] with
  * per-expert stride *_nb2 bytes (the resident expert tensors or the slot pool). */
-int nh_moe_gate_up(const float* h, const float* ffn_norm, float eps, const int32_t* wsel, int k,
+int nh_moe_gate_up(NhDecodeState* state, const float* h, const float* ffn_norm, float eps,
+                   const int32_t* wsel, int k,
                    const void* gate, int32_t tg, uint64_t gate_nb2, const void* up, int32_t tu,
                    uint64_t up_nb2, int64_t n_embd, int64_t n_ff, float* ff, void* stream);
 
@@ -146,12 +153,16 @@ int nh_lm_head_argmax(NhDecodeState* state, const float* h, const float* out_nor
 
 /* y[r] = (W . x)[r] for r < rows (ggml_mul_mat for one activation row); when
  * norm_w is not null x is first RMS-normalised and multiplied by norm_w. */
-int nh_gemv(const void* w, int32_t type, int64_t n, int64_t rows, const float* x,
-            const float* norm_w, float eps, float* y, void* stream);
+int nh_gemv(NhDecodeState* state, const void* w, int32_t type, int64_t n, int64_t rows,
+            const float* x, const float* norm_w, float eps, float* y, void* stream);
 
 /* Q8_K quantisation of n values (n a multiple of 256) into 292-byte blocks
  * (f32 d, int8 qs[256], int16 bsums[16]). */
 int nh_quantize_q8k(const float* x, int64_t n, void* out, void* stream);
+
+/* y[i] = exp(x[i]) as the kernels compute it (Cody-Waite reduction, degree-7
+ * Taylor polynomial, IEEE f32 steps); used by softmax and SiLU. */
+int nh_exp_cw(const float* x, int64_t n, float* y, void* stream);
 
 /* Dequantise `rows` rows of n values (ggml dequantize_row_*). */
 int nh_dequantize(const void* w, int32_t type, int64_t n, int64_t rows, float* y, void* stream);

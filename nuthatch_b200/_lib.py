@@ -73,18 +73,19 @@ SIGNATURES = {
     "nh_router_scratch_bytes": (i64, [C.c_int]),
     "nh_rope_table": (None, [f32, C.c_int, C.c_int, P(f32)]),
     "nh_embed_step": (C.c_int, [vp, vp, vp, i32, i64, i64, vp, vp]),
-    "nh_qkv_proj": (C.c_int, [vp, vp, f32, vp, i32, vp, i32, vp, i32, i64, i64, vp, vp, vp, vp]),
+    "nh_qkv_proj": (C.c_int, [vp, vp, vp, f32, vp, i32, vp, i32, vp, i32, i64, i64, vp, vp, vp, vp]),
     "nh_attention_step": (C.c_int, [vp, vp, vp, vp, vp, vp, f32, C.c_int, C.c_int, C.c_int, vp, f32, vp, vp,
                                     C.c_int, vp, vp, vp]),
-    "nh_out_proj_residual": (C.c_int, [vp, vp, i32, i64, vp, vp]),
+    "nh_out_proj_residual": (C.c_int, [vp, vp, vp, i32, i64, vp, vp]),
     "nh_router_topk": (C.c_int, [vp, vp, vp, f32, vp, i64, C.c_int, C.c_int, C.c_int, vp, vp, vp, vp, C.c_int,
                                  C.c_int, vp, vp]),
-    "nh_moe_gate_up": (C.c_int, [vp, vp, f32, vp, C.c_int, vp, i32, u64, vp, i32, u64, i64, i64, vp, vp]),
+    "nh_moe_gate_up": (C.c_int, [vp, vp, vp, f32, vp, C.c_int, vp, i32, u64, vp, i32, u64, i64, i64, vp, vp]),
     "nh_moe_down_combine": (C.c_int, [vp, vp, vp, vp, C.c_int, vp, i32, u64, i64, i64, vp, vp, i64, i64, vp]),
     "nh_lm_head_argmax": (C.c_int, [vp, vp, vp, f32, vp, i32, i64, i64, vp, vp, vp, vp]),
-    "nh_gemv": (C.c_int, [vp, i32, i64, i64, vp, vp, f32, vp, vp]),
+    "nh_gemv": (C.c_int, [vp, vp, i32, i64, i64, vp, vp, f32, vp, vp]),
     "nh_quantize_q8k": (C.c_int, [vp, i64, vp, vp]),
     "nh_dequantize": (C.c_int, [vp, i32, i64, i64, vp, vp]),
+    "nh_exp_cw": (C.c_int, [vp, i64, vp, vp]),
 }
 
 _lib = None

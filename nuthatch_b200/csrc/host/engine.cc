@@ -244,11 +244,11 @@ int Engine::EnqueueAttnPhase(const ModelView& m, int l, bool norm_topk, bool tra
   const int64_t dkv = static_cast<int64_t>(c.n_head_kv) * c.head_dim();
   const int hd = static_cast<int>(c.head_dim());
   const float kq_scale = 1.0f / std::sqrt(static_cast<float>(hd));
-  NH_TRY(nh_qkv_proj(h_, L.attn_norm, c.rms_eps, L.wq, L.tq, L.wk, L.tk, L.wv, L.tv, c.n_embd, dkv, q_, k_, v_,
+  NH_TRY(nh_qkv_proj(state_, h_,L.attn_norm, c.rms_eps, L.wq, L.tq, L.wk, L.tk, L.wv, L.tv, c.n_embd, dkv, q_, k_, v_,
                      stream_));
   NH_TRY(nh_attention_step(state_, q_, k_, v_, L.q_norm, L.k_norm, c.rms_eps, c.n_head, c.n_head_kv, hd, rope_cs_,
                            kq_scale, kv_->k(l), kv_->v(l), max_seq_, attn_scratch_, attn_, stream_));
-  NH_TRY(nh_out_proj_residual(attn_, L.wo, L.to, c.n_embd, h_, stream_));
+  NH_TRY(nh_out_proj_residual(state_, attn_, L.wo, L.to, c.n_embd, h_, stream_));
   return nh_router_topk(state_, h_, L.ffn_norm, c.rms_eps, L.router, c.n_embd, c.n_expert, c.n_expert_used,
                         norm_topk ? 1 : 0, sel_, wts_, trace ? trace_sel_ : nullptr, trace ? trace_gap_ : nullptr, l,
                         c.n_layers, router_scratch_, stream_);
@@ -259,7 +259,7 @@ int Engine::EnqueueMoePhase(const ModelView& m, int l, const void* gate, int32_t
                             const int32_t* wsel, bool dumps) {
   const OlmoeConfig& c = cfg_;
   const LayerView& L = m.layers[l];
-  NH_TRY(nh_moe_gate_up(h_, L.ffn_norm, c.rms_eps, wsel, c.n_expert_used, gate, tg, gnb2, up, tu, unb2, c.n_embd,
+  NH_TRY(nh_moe_gate_up(state_, h_,L.ffn_norm, c.rms_eps, wsel, c.n_expert_used, gate, tg, gnb2, up, tu, unb2, c.n_embd,
                         c.n_ff, ff_, stream_));
   const int64_t d = c.n_embd;
   return nh_moe_down_combine(state_, ff_, wsel, wts_, c.n_expert_used, down, td, dnb2, c.n_ff, d, h_,
@@ -343,14 +343,14 @@ int Engine::KernelLoop(const ModelView& m, int which, int reps) {
       const LayerView& L = m.layers[l];
       int rc;
       if (which == 0) {
-        rc = nh_moe_gate_up(h_, L.ffn_norm, c.rms_eps, sel_, c.n_expert_used, L.gate, L.tg, L.gate_nb2, L.up, L.tu,
+        rc = nh_moe_gate_up(state_, h_,L.ffn_norm, c.rms_eps, sel_, c.n_expert_used, L.gate, L.tg, L.gate_nb2, L.up, L.tu,
                             L.up_nb2, c.n_embd, c.n_ff, ff_, stream_);
       } else if (which == 1) {
         rc = nh_moe_down_combine(state_, ff_, sel_, wts_, c.n_expert_used, L.down, L.td, L.down_nb2, c.n_ff,
                                  c.n_embd, h_, nullptr, 0, 0, stream_);
       } else {
         const int64_t dkv = static_cast<int64_t>(c.n_head_kv) * c.head_dim();
-        rc = nh_qkv_proj(h_, L.attn_norm, c.rms_eps, L.wq, L.tq, L.wk, L.tk, L.wv, L.tv, c.n_embd, dkv, q_, k_, v_,
+        rc = nh_qkv_proj(state_, h_,L.attn_norm, c.rms_eps, L.wq, L.tq, L.wk, L.tk, L.wv, L.tv, c.n_embd, dkv, q_, k_, v_,
                          stream_);
       }
       if (rc != NH_OK) return rc;

@@ -2,25 +2,28 @@
 // and the KV append.
 //
 // Grid (n_head, n_split): CTA (h, s) owns positions [s*kAttnSplit,
-// (s+1)*kAttnSplit) of query head h.  Every CTA re-derives the normalised,
-// rotated query of its head (the QK-norm spans the full width, so each CTA
-// reduces the whole q row; a few KB of L2 reads).  The CTA whose range holds
-// the current position also forms the current K/V row itself, and the first
-// query head of each KV head appends it to the cache, so no CTA reads a cache
-// row that is being written.  Partial (max, sum, weighted V) triples are
-// combined by the last CTA of each head in split order, so the result does
-// not depend on CTA scheduling.
+// (s+1)*kAttnSplit) of query head h.  The cached K/V rows of its range were
+// written by earlier tokens, so the CTA starts their cp.async.bulk copies into
+// shared memory before griddepcontrol.wait.  Every CTA re-derives the
+// normalised, rotated query of its head (the QK-norm spans the full width, so
+// each CTA reduces the whole q row; a few KB of L2 reads).  The CTA whose
+// range holds the current position also forms the current K/V row itself, and
+// the first query head of each KV head appends it to the cache, so no CTA
+// reads a cache row that is being written.  Partial (max, sum, weighted V)
+// triples are combined by the last CTA of each head in split order, so the
+// result does not depend on CTA scheduling.
 #include <cmath>
 
-#include "common.cuh"
+#include "launch.cuh"
+#include "rowdot.cuh"
 
 namespace nh {
 
 constexpr int kAttnThreads = 128;
-constexpr int kAttnSplit = 256;
+constexpr int kAttnSplit = 64;
 
 struct AttnArgs {
-  const NhDecodeState* state;
+  NhDecodeState* state;
   const float* q;
   const float* k;
   const float* v;
@@ -40,27 +43,6 @@ struct AttnArgs {
   float* out;
 };
 
-// Block-wide RMS scale of x[0..n) with ggml_rms_norm semantics.
-__device__ float rms_scale_block(const float* x, int n, float eps, double* red) {
-  double s = 0.0;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float v = x[i];
-    s += static_cast<double>(__fmul_rn(v, v));
-  }
-  s = warp_sum_d(s);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    double t = 0.0;
-    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += red[w];
-    red[32] = t;
-  }
-  __syncthreads();
-  const float mean = static_cast<float>(red[32] / static_cast<double>(n));
-  __syncthreads();
-  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
-}
-
 __device__ void rope_inplace(float* x, int hd, const float* cs) {
   const int half = hd / 2;
   for (int i = threadIdx.x; i < half; i += blockDim.x) {
@@ -73,16 +55,21 @@ __device__ void rope_inplace(float* x, int hd, const float* cs) {
 
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs p) {
   const int h = blockIdx.x, sp = blockIdx.y;
-  const int pos = p.state->pos;
+  // The cursor was last written by the previous token's argmax, completed
+  // before this kernel could launch.
+  const int pos = *reinterpret_cast<volatile const int*>(&p.state->pos);
   const int n_kv = pos + 1;
   const int n_active = (n_kv + kAttnSplit - 1) / kAttnSplit;
   if (sp >= n_active) return;
-  extern __shared__ __align__(16) float sm[];
+  extern __shared__ __align__(128) float sm[];
   const int hd = p.hd;
-  float* qh = sm;
-  float* kc = sm + hd;
-  float* vc = sm + 2 * hd;
-  float* sc = sm + 3 * hd;
+  float* Ks = sm;                      // [kAttnSplit][hd]
+  float* Vs = sm + kAttnSplit * hd;    // [kAttnSplit][hd]
+  float* qh = Vs + kAttnSplit * hd;
+  float* kc = qh + hd;
+  float* vc = kc + hd;
+  float* sc = vc + hd;                 // [kAttnSplit]
+  __shared__ __align__(8) uint64_t bar;
   __shared__ double red[40];
   __shared__ float s_max;
   __shared__ bool s_last;
@@ -90,20 +77,34 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
   const int group = p.n_head / p.n_head_kv;
   const int kh = h / group;
   const int dq = p.n_head * hd, dkv = p.n_head_kv * hd;
-  const float* cs = p.rope_cs + static_cast<int64_t>(pos) * hd;
-
-  const float sq = rms_scale_block(p.q, dq, p.eps, red);
-  for (int i = tid; i < hd; i += blockDim.x) {
-    qh[i] = __fmul_rn(__fmul_rn(p.q[h * hd + i], sq), p.q_norm[h * hd + i]);
-  }
-  __syncthreads();
-  rope_inplace(qh, hd, cs);
-
   const int p0 = sp * kAttnSplit;
   const int p1 = min(n_kv, p0 + kAttnSplit);
+  const int n = p1 - p0;
+  const int n_cached = max(0, min(p1, pos) - p0);
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+    const uint32_t row = static_cast<uint32_t>(hd) * 4;
+    mbar_expect_tx(&bar, 2u * row * static_cast<uint32_t>(n_cached));
+    for (int j = 0; j < n_cached; ++j) {
+      const int64_t g = static_cast<int64_t>(p0 + j) * dkv + kh * hd;
+      bulk_g2s(Ks + j * hd, p.k_cache + g, row, &bar);
+      bulk_g2s(Vs + j * hd, p.v_cache + g, row, &bar);
+    }
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_trigger();
+
+  const float* cs = p.rope_cs + static_cast<int64_t>(pos) * hd;
+  const float sq = block_rms_scale(p.q, dq, p.eps, red);
+  for (int i = tid; i < hd; i += blockDim.x) qh[i] = __fmul_rn(__fmul_rn(p.q[h * hd + i], sq), p.q_norm[h * hd + i]);
+  __syncthreads();
+  rope_inplace(qh, hd, cs);
   const bool covers_cur = (p1 == n_kv);
   if (covers_cur) {
-    const float sk = rms_scale_block(p.k, dkv, p.eps, red);
+    __syncthreads();
+    const float sk = block_rms_scale(p.k, dkv, p.eps, red);
     for (int i = tid; i < hd; i += blockDim.x) {
       kc[i] = __fmul_rn(__fmul_rn(p.k[kh * hd + i], sk), p.k_norm[kh * hd + i]);
       vc[i] = p.v[kh * hd + i];
@@ -120,18 +121,19 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
       }
     }
   }
+  const bool ok = mbar_wait(&bar, 0);
+  if (!ok && tid == 0) atomicCAS(&p.state->error, 0, NH_E_TIMEOUT);
   __syncthreads();
 
   // Scores kq = K.q * kq_scale, one warp per position.
-  for (int j = p0 + warp; j < p1; j += nw) {
-    const float* kr = (j == pos) ? kc : p.k_cache + static_cast<int64_t>(j) * dkv + kh * hd;
+  for (int j = warp; j < n; j += nw) {
+    const float* kr = (p0 + j == pos) ? kc : Ks + j * hd;
     float d = 0.f;
     for (int i = lane; i < hd; i += 32) d = __fadd_rn(d, __fmul_rn(kr[i], qh[i]));
     d = warp_sum(d);
-    if (lane == 0) sc[j - p0] = __fmul_rn(d, p.kq_scale);
+    if (lane == 0) sc[j] = ok ? __fmul_rn(d, p.kq_scale) : 0.f;
   }
   __syncthreads();
-  const int n = p1 - p0;
   float m = -INFINITY;
   for (int j = tid; j < n; j += blockDim.x) m = fmaxf(m, sc[j]);
   m = warp_max(m);
@@ -146,7 +148,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
   m = s_max;
   double l = 0.0;
   for (int j = tid; j < n; j += blockDim.x) {
-    const float e = expf(__fsub_rn(sc[j], m));
+    const float e = exp_cw(__fsub_rn(sc[j], m));
     sc[j] = e;
     l += static_cast<double>(e);
   }
@@ -171,7 +173,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
     for (int i = tid; i < hd; i += blockDim.x) {
       float acc = 0.f;
       for (int j = 0; j < n; ++j) {
-        const float vv = (p0 + j == pos) ? vc[i] : p.v_cache[static_cast<int64_t>(p0 + j) * dkv + kh * hd + i];
+        const float vv = (p0 + j == pos) ? vc[i] : Vs[j * hd + i];
         acc = __fadd_rn(acc, __fmul_rn(vv, sc[j]));
       }
       out[i] = acc;
@@ -182,7 +184,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
   for (int i = tid; i < hd; i += blockDim.x) {
     float acc = 0.f;
     for (int j = 0; j < n; ++j) {
-      const float vv = (p0 + j == pos) ? vc[i] : p.v_cache[static_cast<int64_t>(p0 + j) * dkv + kh * hd + i];
+      const float vv = (p0 + j == pos) ? vc[i] : Vs[j * hd + i];
       acc = __fadd_rn(acc, __fmul_rn(vv, sc[j]));
     }
     p.part_acc[static_cast<int64_t>(slot) * hd + i] = acc;
@@ -200,21 +202,29 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  volatile float* pm = p.part_m;
-  volatile double* pl = p.part_l;
-  volatile float* pa = p.part_acc;
+  // Combine the splits in order: weights exp(m_s - M) staged in shared memory.
+  const volatile float* pm = p.part_m;
+  const volatile double* pl = p.part_l;
   float M = -INFINITY;
   for (int s = 0; s < n_active; ++s) M = fmaxf(M, pm[h * p.n_split + s]);
+  float* wsplit = sc;  // reuse: n_active <= n_split; sized kAttnSplit, so combine in chunks
   double L = 0.0;
-  for (int s = 0; s < n_active; ++s) {
-    L += pl[h * p.n_split + s] * static_cast<double>(expf(__fsub_rn(pm[h * p.n_split + s], M)));
+  for (int s0 = 0; s0 < n_active; s0 += kAttnSplit) {
+    const int cnt = min(kAttnSplit, n_active - s0);
+    __syncthreads();
+    for (int s = tid; s < cnt; s += blockDim.x) wsplit[s] = exp_cw(__fsub_rn(pm[h * p.n_split + s0 + s], M));
+    __syncthreads();
+    for (int s = 0; s < cnt; ++s) L += pl[h * p.n_split + s0 + s] * static_cast<double>(wsplit[s]);
   }
   const float inv = static_cast<float>(1.0 / L);
   for (int i = tid; i < hd; i += blockDim.x) {
     float acc = 0.f;
-    for (int s = 0; s < n_active; ++s) {
-      const float w = expf(__fsub_rn(pm[h * p.n_split + s], M));
-      acc = __fadd_rn(acc, __fmul_rn(pa[static_cast<int64_t>(h * p.n_split + s) * hd + i], w));
+    for (int s0 = 0; s0 < n_active; s0 += kAttnSplit) {
+      const int cnt = min(kAttnSplit, n_active - s0);
+      for (int s = 0; s < cnt; ++s) {
+        const float w = exp_cw(__fsub_rn(pm[h * p.n_split + s0 + s], M));
+        acc = __fadd_rn(acc, __fmul_rn(__ldcg(&p.part_acc[static_cast<int64_t>(h * p.n_split + s0 + s) * hd + i]), w));
+      }
     }
     out[i] = __fmul_rn(acc, inv);
   }
@@ -245,23 +255,23 @@ extern "C" void nh_rope_table(float base, int head_dim, int max_seq, float* cs) 
   }
 }
 
-extern "C" int nh_attention_step(const NhDecodeState* state, const float* q, const float* k,
-                                 const float* v, const float* q_norm, const float* k_norm,
-                                 float eps, int n_head, int n_head_kv, int head_dim,
-                                 const float* rope_cs, float kq_scale, float* k_cache,
-                                 float* v_cache, int max_seq, void* scratch, float* attn_out,
-                                 void* stream) {
-  if (state == nullptr || q == nullptr || k == nullptr || v == nullptr || q_norm == nullptr ||
-      k_norm == nullptr || rope_cs == nullptr || k_cache == nullptr || v_cache == nullptr ||
-      scratch == nullptr || attn_out == nullptr) {
+extern "C" int nh_attention_step(const NhDecodeState* state, const float* q, const float* k, const float* v,
+                                 const float* q_norm, const float* k_norm, float eps, int n_head, int n_head_kv,
+                                 int head_dim, const float* rope_cs, float kq_scale, float* k_cache, float* v_cache,
+                                 int max_seq, void* scratch, float* attn_out, void* stream) {
+  if (state == nullptr || q == nullptr || k == nullptr || v == nullptr || q_norm == nullptr || k_norm == nullptr ||
+      rope_cs == nullptr || k_cache == nullptr || v_cache == nullptr || scratch == nullptr || attn_out == nullptr) {
     return NH_E_ARG;
   }
-  if (n_head <= 0 || n_head_kv <= 0 || n_head % n_head_kv != 0 || head_dim <= 0 ||
-      head_dim % 2 != 0 || head_dim > 1024 || max_seq <= 0) {
+  // Cache rows are copied whole with 16-byte bulk copies: head_dim*4 must be
+  // a multiple of 16 and the cache 16-byte aligned.
+  if (n_head <= 0 || n_head_kv <= 0 || n_head % n_head_kv != 0 || head_dim <= 0 || head_dim % 4 != 0 ||
+      head_dim > 256 || max_seq <= 0 || (reinterpret_cast<uintptr_t>(k_cache) & 15) != 0 ||
+      (reinterpret_cast<uintptr_t>(v_cache) & 15) != 0) {
     return NH_E_ARG;
   }
   AttnArgs p;
-  p.state = state;
+  p.state = const_cast<NhDecodeState*>(state);
   p.q = q;
   p.k = k;
   p.v = v;
@@ -287,8 +297,9 @@ extern "C" int nh_attention_step(const NhDecodeState* state, const float* q, con
   off = (off + 15) & ~15ll;
   p.part_acc = reinterpret_cast<float*>(sc + off);
   p.out = attn_out;
-  const size_t smem = static_cast<size_t>(3 * head_dim + kAttnSplit) * sizeof(float);
-  dim3 grid(n_head, p.n_split);
-  attention_kernel<<<grid, kAttnThreads, smem, static_cast<cudaStream_t>(stream)>>>(p);
-  return cudaGetLastError() == cudaSuccess ? NH_OK : NH_E_CUDA;
+  const size_t smem = static_cast<size_t>(2 * kAttnSplit * head_dim + 3 * head_dim + kAttnSplit) * sizeof(float);
+  static size_t configured = 48 * 1024;
+  if (!ensure_smem(attention_kernel, smem, configured)) return NH_E_CUDA;
+  return launch_pdl(attention_kernel, dim3(n_head, p.n_split), dim3(kAttnThreads), smem,
+                    static_cast<cudaStream_t>(stream), p);
 }

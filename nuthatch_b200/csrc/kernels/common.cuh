@@ -5,6 +5,12 @@
 // Rounding: every f32 product/sum that the reference rounds separately is
 // written with __fmul_rn/__fadd_rn/__fsub_rn so nvcc cannot contract it into
 // an FMA; integer sub-block sums are exact.
+//
+// Shared-memory layout of the Q8_K activation: block b's 256 quants are stored
+// rotated by 16*(b mod 16) bytes (logical byte L of block b lives at
+// b*256 + ((L + 16*(b & 15)) & 255)).  One lane owns one super-block of a
+// weight row, so the lanes of a quarter-warp read the same logical offset of
+// eight consecutive blocks; the rotation puts those reads in distinct banks.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -28,6 +34,29 @@ __host__ __device__ inline size_t row_bytes(int type, int64_t n) {
 
 __device__ __forceinline__ float half_bits_to_float(uint32_t bits16) {
   return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16 & 0xFFFF)));
+}
+
+__device__ __forceinline__ int q8_rot(int b) { return (b & 15) * 16; }
+__device__ __forceinline__ int q8_off(int b, int L) { return b * QK + ((L + q8_rot(b)) & (QK - 1)); }
+
+// exp_cw: exp(x) = 2^k * e^r with k = nearest(x / ln 2) and r = x - k*ln 2
+// reduced in two steps (Cody & Waite, ln 2 = 355/512 - 2.1219444e-4), e^r
+// from its degree-7 Taylor polynomial in Horner form; every step is an IEEE
+// f32 operation, so the host restatement produces the same bits.
+__device__ __forceinline__ float exp_cw(float x) {
+  if (x > 88.72283935546875f) return INFINITY;
+  if (x < -103.97208404541015625f) return 0.f;
+  const float kf = rintf(__fmul_rn(x, 1.44269502162933349609375f));
+  const float r = __fsub_rn(__fsub_rn(x, __fmul_rn(kf, 0.693359375f)), __fmul_rn(kf, -2.12194440e-4f));
+  float p = 1.98412698e-4f;
+  p = __fadd_rn(__fmul_rn(p, r), 1.38888889e-3f);
+  p = __fadd_rn(__fmul_rn(p, r), 8.33333333e-3f);
+  p = __fadd_rn(__fmul_rn(p, r), 4.16666667e-2f);
+  p = __fadd_rn(__fmul_rn(p, r), 1.66666667e-1f);
+  p = __fadd_rn(__fmul_rn(p, r), 0.5f);
+  p = __fadd_rn(__fmul_rn(p, r), 1.0f);
+  p = __fadd_rn(__fmul_rn(p, r), 1.0f);
+  return ldexpf(p, static_cast<int>(kf));
 }
 
 // ------------------------------------------------------------ warp helpers
@@ -75,26 +104,29 @@ __device__ __forceinline__ const uint8_t* stage_bytes_warp(uint8_t* dst, const u
 }
 
 // ------------------------------------------------------------ activation (smem)
-// One activation row in shared memory: f32 values, and when the consumer
-// weights are quantised, its Q8_K form (int8 quants, per-256 scale, per-16 sums).
+// One activation row in shared memory: optional f32 values (for F32 weights)
+// and, for quantised weights, its Q8_K form (rotated int8 quants, per-256
+// scale, per-16 sums).
 struct ActSmem {
-  float* xf;       // [K]
-  int8_t* qs;      // [K]
+  float* xf;       // [K] or nullptr
+  int8_t* qs;      // [K] rotated
   float* d;        // [K/256]
   int16_t* bsums;  // [K/16]
   int K;
 };
 
-__host__ __device__ inline size_t act_smem_bytes(int K) {
-  return static_cast<size_t>(K) * 4 + K + (K / QK + 1) * 4 + (K / 16 + 1) * 2 + 64;
+__host__ __device__ inline size_t act_smem_bytes(int K, bool need_xf) {
+  return (need_xf ? static_cast<size_t>(K) * 4 : 0) + K + (K / QK + 1) * 4 + (K / 16 + 1) * 2 + 64;
 }
 
-__device__ inline ActSmem carve_act(uint8_t* base, int K) {
+__device__ inline ActSmem carve_act(uint8_t* base, int K, bool need_xf) {
   ActSmem a;
   a.K = K;
-  a.xf = reinterpret_cast<float*>(base);
-  a.qs = reinterpret_cast<int8_t*>(base + static_cast<size_t>(K) * 4);
-  uintptr_t p = reinterpret_cast<uintptr_t>(a.qs + K);
+  uintptr_t p = reinterpret_cast<uintptr_t>(base);
+  a.xf = need_xf ? reinterpret_cast<float*>(p) : nullptr;
+  if (need_xf) p += static_cast<size_t>(K) * 4;
+  a.qs = reinterpret_cast<int8_t*>(p);
+  p += K;
   p = (p + 15) & ~static_cast<uintptr_t>(15);
   a.d = reinterpret_cast<float*>(p);
   p += (K / QK + 1) * 4;
@@ -103,102 +135,114 @@ __device__ inline ActSmem carve_act(uint8_t* base, int K) {
   return a;
 }
 
-// Block-wide: xf = src (optionally RMS-normalised and multiplied by norm_w with
-// ggml_rms_norm + ggml_mul semantics: sum of squares in double, scale =
-// 1/sqrtf(mean + eps), y = (x*scale)*w), then Q8_K-quantised if `quant`.
-// `red` is >= 33 doubles of shared scratch.  Ends with __syncthreads().
-__device__ inline void prep_act(ActSmem& a, const float* __restrict__ src,
-                                const float* __restrict__ norm_w, bool do_norm, float eps,
-                                bool quant, double* red) {
-  const int K = a.K;
+// Block-wide RMS scale of src[0..K) with ggml_rms_norm semantics (sum of
+// squares in double, mean rounded to f32, 1/sqrtf(mean + eps)).  `red` holds
+// >= 33 doubles.  Ends synchronised.
+__device__ inline float block_rms_scale(const float* __restrict__ src, int K, float eps, double* red) {
   const int tid = threadIdx.x, nt = blockDim.x;
-  float scale = 1.f;
-  if (do_norm) {
-    double s = 0.0;
-    for (int i = tid; i < K; i += nt) {
-      const float v = src[i];
-      s += static_cast<double>(__fmul_rn(v, v));
-    }
-    s = warp_sum_d(s);
-    if ((tid & 31) == 0) red[tid >> 5] = s;
-    __syncthreads();
-    if (tid < 32) {
-      double t = tid < (nt >> 5) ? red[tid] : 0.0;
-      t = warp_sum_d(t);
-      if (tid == 0) red[32] = t;
-    }
-    __syncthreads();
-    const float mean = static_cast<float>(red[32] / static_cast<double>(K));
-    scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
-  }
+  double s = 0.0;
   for (int i = tid; i < K; i += nt) {
+    const float v = src[i];
+    s += static_cast<double>(__fmul_rn(v, v));
+  }
+  s = warp_sum_d(s);
+  if ((tid & 31) == 0) red[tid >> 5] = s;
+  __syncthreads();
+  if (tid < 32) {
+    double t = tid < (nt >> 5) ? red[tid] : 0.0;
+    t = warp_sum_d(t);
+    if (tid == 0) red[32] = t;
+  }
+  __syncthreads();
+  const float mean = static_cast<float>(red[32] / static_cast<double>(K));
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+}
+
+// quantize_row_q8_K semantics for one 256-value block held 8 per lane
+// (v[k] = element lane*8 + k): the first element of largest magnitude maps to
+// -127 (iscale = -127/max, d = 1/iscale), round half to even, clamp at +127,
+// 16 partial sums.  Writes block b of the activation (rotated layout).
+__device__ __forceinline__ void quantize_block_warp(const float (&v)[8], int b, ActSmem& a, int lane) {
+  float amax = 0.f, mx = 0.f;
+  int idx = 1 << 30;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const float ax = fabsf(v[k]);
+    if (ax > amax) {
+      amax = ax;
+      mx = v[k];
+      idx = lane * 8 + k;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float oa = __shfl_xor_sync(0xffffffffu, amax, o);
+    const float om = __shfl_xor_sync(0xffffffffu, mx, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (oa > amax || (oa == amax && oi < idx)) {
+      amax = oa;
+      mx = om;
+      idx = oi;
+    }
+  }
+  uint32_t w0 = 0, w1 = 0;
+  int part = 0;
+  float dq = 0.f;
+  if (amax != 0.f) {
+    const float iscale = __fdiv_rn(-127.f, mx);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int q = min(127, __float2int_rn(__fmul_rn(iscale, v[k])));
+      part += q;
+      const uint32_t byte = static_cast<uint32_t>(q & 0xFF);
+      if (k < 4) w0 |= byte << (8 * k);
+      else w1 |= byte << (8 * (k - 4));
+    }
+    dq = __fdiv_rn(1.f, iscale);
+  }
+  *reinterpret_cast<uint2*>(a.qs + q8_off(b, lane * 8)) = make_uint2(w0, w1);
+  part += __shfl_xor_sync(0xffffffffu, part, 1);
+  if ((lane & 1) == 0) a.bsums[b * 16 + (lane >> 1)] = static_cast<int16_t>(part);
+  if (lane == 0) a.d[b] = dq;
+}
+
+// Block-wide: the activation x = src (optionally RMS-normalised and
+// multiplied by norm_w, ggml_rms_norm + ggml_mul: y = (x*scale)*w), written as
+// f32 into xf (when allocated) and Q8_K-quantised when `quant`.  Ends
+// synchronised.
+__device__ inline void prep_act(ActSmem& a, const float* __restrict__ src, const float* __restrict__ norm_w,
+                                bool do_norm, float eps, bool quant, double* red) {
+  const int K = a.K;
+  const float scale = do_norm ? block_rms_scale(src, K, eps, red) : 1.f;
+  auto val = [&](int i) {
     float v = src[i];
     if (do_norm) {
       v = __fmul_rn(v, scale);
       if (norm_w != nullptr) v = __fmul_rn(v, norm_w[i]);
     }
-    a.xf[i] = v;
+    return v;
+  };
+  if (a.xf != nullptr) {
+    for (int i = threadIdx.x; i < K; i += blockDim.x) a.xf[i] = val(i);
   }
-  __syncthreads();
-  if (!quant) return;
-  // quantize_row_q8_K semantics, one warp per 256-block: the first element of
-  // largest magnitude maps to -127 (iscale = -127/max, d = 1/iscale), round
-  // half to even, clamp at +127, 16 partial sums.
-  const int warp = tid >> 5, lane = tid & 31, nw = nt >> 5;
-  for (int b = warp; b < K / QK; b += nw) {
-    const float* x = a.xf + b * QK;
-    float amax = 0.f, mx = 0.f;
-    int idx = 1 << 30;
+  if (quant) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int b = warp; b < K / QK; b += nw) {
+      float v[8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int i = lane * 8 + k;
-      const float ax = fabsf(x[i]);
-      if (ax > amax) {
-        amax = ax;
-        mx = x[i];
-        idx = i;
-      }
+      for (int k = 0; k < 8; ++k) v[k] = val(b * QK + lane * 8 + k);
+      quantize_block_warp(v, b, a, lane);
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float oa = __shfl_xor_sync(0xffffffffu, amax, o);
-      const float om = __shfl_xor_sync(0xffffffffu, mx, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-      if (oa > amax || (oa == amax && oi < idx)) {
-        amax = oa;
-        mx = om;
-        idx = oi;
-      }
-    }
-    int8_t* q = a.qs + b * QK;
-    if (amax == 0.f) {
-#pragma unroll
-      for (int k = 0; k < 8; ++k) q[lane * 8 + k] = 0;
-      if (lane < 16) a.bsums[b * 16 + lane] = 0;
-      if (lane == 0) a.d[b] = 0.f;
-      continue;
-    }
-    const float iscale = __fdiv_rn(-127.f, mx);
-    int part = 0;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      int v = __float2int_rn(__fmul_rn(iscale, x[lane * 8 + k]));
-      v = min(127, v);
-      q[lane * 8 + k] = static_cast<int8_t>(v);
-      part += v;
-    }
-    part += __shfl_xor_sync(0xffffffffu, part, 1);
-    if ((lane & 1) == 0) a.bsums[b * 16 + (lane >> 1)] = static_cast<int16_t>(part);
-    if (lane == 0) a.d[b] = __fdiv_rn(1.f, iscale);
   }
   __syncthreads();
 }
 
 // ------------------------------------------------------------ super-block dots
 // One lane computes one whole super-block's contribution.  `blk` points into
-// shared memory; `q8`/`bs` are the activation's quants and 16-sums for the
-// same 256 elements; `yd` its scale.  Result as the oracle forms it per
-// super-block: (d*yd)*sumi - (dmin*yd)*summ.
+// shared memory; `q8` is the base of the activation's quants, `b` the
+// activation block index (for the rotation), `bs` its 16-sums, `yd` its
+// scale.  Result as the oracle forms it per super-block:
+// (d*yd)*sumi - (dmin*yd)*summ.
 __device__ __forceinline__ void q4k_scale_min(const uint8_t* s, int j, int& sc, int& m) {
   if (j < 4) {
     sc = s[j] & 63;
@@ -209,8 +253,12 @@ __device__ __forceinline__ void q4k_scale_min(const uint8_t* s, int j, int& sc, 
   }
 }
 
-__device__ __forceinline__ float sb_dot_q4k(const uint8_t* blk, const int8_t* q8,
-                                            const int16_t* bs, float yd) {
+__device__ __forceinline__ int4 ld_q8_16(const int8_t* q8, int b, int L) {
+  return *reinterpret_cast<const int4*>(q8 + q8_off(b, L));
+}
+
+__device__ __forceinline__ float sb_dot_q4k(const uint8_t* blk, const int8_t* q8, int b, const int16_t* bs,
+                                            float yd) {
   const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
   const float d = half_bits_to_float(hdr.x);
   const float dmin = half_bits_to_float(hdr.x >> 16);
@@ -223,10 +271,10 @@ __device__ __forceinline__ float sb_dot_q4k(const uint8_t* blk, const int8_t* q8
   for (int c = 0; c < 4; ++c) {
     const uint4 w0 = *reinterpret_cast<const uint4*>(blk + 16 + 32 * c);
     const uint4 w1 = *reinterpret_cast<const uint4*>(blk + 32 + 32 * c);
-    const int4 xa = *reinterpret_cast<const int4*>(q8 + 64 * c);
-    const int4 xb = *reinterpret_cast<const int4*>(q8 + 64 * c + 16);
-    const int4 xc = *reinterpret_cast<const int4*>(q8 + 64 * c + 32);
-    const int4 xd = *reinterpret_cast<const int4*>(q8 + 64 * c + 48);
+    const int4 xa = ld_q8_16(q8, b, 64 * c);
+    const int4 xb = ld_q8_16(q8, b, 64 * c + 16);
+    const int4 xc = ld_q8_16(q8, b, 64 * c + 32);
+    const int4 xd = ld_q8_16(q8, b, 64 * c + 48);
     const uint32_t m4 = 0x0F0F0F0Fu;
     int lo = 0, hi = 0;
     lo = __dp4a(static_cast<int>(w0.x & m4), xa.x, lo);
@@ -262,8 +310,8 @@ __device__ __forceinline__ uint32_t ld32u(const uint8_t* p) {
   return __funnelshift_r(w[0], w[1], static_cast<uint32_t>((a & 3) * 8));
 }
 
-__device__ __forceinline__ float sb_dot_q6k(const uint8_t* blk, const int8_t* q8,
-                                            const int16_t* bs, float yd) {
+__device__ __forceinline__ float sb_dot_q6k(const uint8_t* blk, const int8_t* q8, int b, const int16_t* bs,
+                                            float yd) {
   const uint8_t* ql = blk;
   const uint8_t* qh = blk + 128;
   int grp[16];
@@ -283,10 +331,10 @@ __device__ __forceinline__ float sb_dot_q6k(const uint8_t* blk, const int8_t* q8
       const uint32_t q3 = ((B >> 4) & m4) | ((H >> 2) & m2);
       const int base = 128 * h + 4 * l4;
       const int g = 8 * h + (l4 >> 2);
-      grp[g + 0] = __dp4a(static_cast<int>(q0), *reinterpret_cast<const int*>(q8 + base), grp[g + 0]);
-      grp[g + 2] = __dp4a(static_cast<int>(q1), *reinterpret_cast<const int*>(q8 + base + 32), grp[g + 2]);
-      grp[g + 4] = __dp4a(static_cast<int>(q2), *reinterpret_cast<const int*>(q8 + base + 64), grp[g + 4]);
-      grp[g + 6] = __dp4a(static_cast<int>(q3), *reinterpret_cast<const int*>(q8 + base + 96), grp[g + 6]);
+      grp[g + 0] = __dp4a(static_cast<int>(q0), *reinterpret_cast<const int*>(q8 + q8_off(b, base)), grp[g + 0]);
+      grp[g + 2] = __dp4a(static_cast<int>(q1), *reinterpret_cast<const int*>(q8 + q8_off(b, base + 32)), grp[g + 2]);
+      grp[g + 4] = __dp4a(static_cast<int>(q2), *reinterpret_cast<const int*>(q8 + q8_off(b, base + 64)), grp[g + 4]);
+      grp[g + 6] = __dp4a(static_cast<int>(q3), *reinterpret_cast<const int*>(q8 + q8_off(b, base + 96)), grp[g + 6]);
     }
   }
   const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192);
@@ -304,16 +352,16 @@ __host__ __device__ inline int lanes_per_row(int nsb) {
   return l;
 }
 
-// Dot of one staged quantised row with the activation: lane `sub` of `lpr`
-// lanes handles super-blocks sub, sub+lpr, ...; result reduced over the lpr
-// lanes (valid in every one of them).  Super-blocks are summed as a tree.
-__device__ __forceinline__ float row_dot_q(const uint8_t* row, int type, int nsb, int sub,
-                                           int lpr, const ActSmem& a) {
+// Dot of one staged quantised row with the activation blocks b0 .. b0+nsb-1:
+// lane `sub` of `lpr` lanes handles super-blocks sub, sub+lpr, ...; result
+// reduced over the lpr lanes (valid in every one of them).
+__device__ __forceinline__ float row_dot_q(const uint8_t* row, int type, int nsb, int sub, int lpr,
+                                           const ActSmem& a, int b0) {
   float acc = 0.f;
   for (int s = sub; s < nsb; s += lpr) {
-    const float v = type == NH_TYPE_Q4_K
-                        ? sb_dot_q4k(row + s * kQ4KBytes, a.qs + s * QK, a.bsums + s * 16, a.d[s])
-                        : sb_dot_q6k(row + s * kQ6KBytes, a.qs + s * QK, a.bsums + s * 16, a.d[s]);
+    const int b = b0 + s;
+    const float v = type == NH_TYPE_Q4_K ? sb_dot_q4k(row + s * kQ4KBytes, a.qs, b, a.bsums + b * 16, a.d[b])
+                                         : sb_dot_q6k(row + s * kQ6KBytes, a.qs, b, a.bsums + b * 16, a.d[b]);
     acc = __fadd_rn(acc, v);
   }
   for (int o = 1; o < lpr; o <<= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
@@ -321,11 +369,42 @@ __device__ __forceinline__ float row_dot_q(const uint8_t* row, int type, int nsb
 }
 
 // f32 row (global memory) dot the f32 activation; whole warp, result in every lane.
-__device__ __forceinline__ float row_dot_f32(const float* __restrict__ w, const float* x, int K,
-                                             int lane) {
+__device__ __forceinline__ float row_dot_f32(const float* __restrict__ w, const float* x, int K, int lane) {
   float s = 0.f;
   for (int i = lane; i < K; i += 32) s = __fadd_rn(s, __fmul_rn(w[i], x[i]));
   return warp_sum(s);
+}
+
+// Block-wide argmax of (value, index) pairs with the first-maximum rule
+// (greater value wins, equal values keep the lower index); result valid in
+// thread 0.  `sv`/`si` hold >= 32 entries.
+__device__ __forceinline__ bool argmax_better(float v, int i, float bv, int bi) {
+  return v > bv || (v == bv && i < bi);
+}
+__device__ inline void block_argmax(float& v, int& i, float* sv, int* si) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+    if (argmax_better(ov, oi, v, i)) {
+      v = ov;
+      i = oi;
+    }
+  }
+  __syncthreads();
+  if (lane == 0) {
+    sv[warp] = v;
+    si[warp] = i;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < nw; ++w)
+      if (argmax_better(sv[w], si[w], v, i)) {
+        v = sv[w];
+        i = si[w];
+      }
+  }
 }
 
 }  // namespace nh

@@ -1,20 +1,22 @@
-// Batch-1 GEMV kernels over native GGUF Q4_K / Q6_K / F32 rows.
+// Batch-1 GEMV kernels over native GGUF Q4_K / Q6_K / F32 rows: QKV,
+// output projection + residual, lm_head + argmax, and the standalone form.
 //
-// Layout of the work: the activation row is prepared once per CTA in shared
-// memory (optional RMSNorm, Q8_K quantisation).  Each warp owns a sequence of
-// jobs; a job is a group of consecutive weight rows (32/lanes_per_row rows)
-// staged into the warp's shared buffer with 16-byte cp.async copies,
-// kernels_stages deep, so several KB per warp are in flight while the previous
-// group is reduced.  Within a group one lane handles one super-block of one
-// row; the lanes of a row reduce with shuffles.
+// Each warp owns a sequence of jobs (a job = 32/LPR consecutive rows of one
+// weight), staged by its own cp.async.bulk ring (rowdot.cuh).  The weights do
+// not depend on the preceding kernel, so the first kStages jobs are issued
+// before griddepcontrol.wait: the HBM stream of this kernel overlaps the tail
+// of the previous one.  The activation (optional RMSNorm, Q8_K) is prepared
+// once per CTA in shared memory and then held in registers.
 #include <climits>
+#include <cstring>
 
-#include "common.cuh"
+#include "launch.cuh"
+#include "rowdot.cuh"
 
 namespace nh {
 
-constexpr int kGemvWarps = 4;
-constexpr int kGemvStages = 3;
+constexpr int kGemvWarps = 8;
+constexpr int kGemvMaxStages = 4;
 constexpr int kMaxArgmaxBlocks = 2048;
 
 struct GemvSeg {
@@ -35,11 +37,13 @@ struct GemvArgs {
   int jobs_start[4];
   int jobs_total;
   uint32_t stage_bytes;
+  int S;  // ring depth (<= kGemvMaxStages)
   const float* x;
   const float* norm_w;
   float eps;
   int do_norm;
   int quant;
+  int need_xf;
   // lm_head argmax mode
   int argmax;
   NhDecodeState* state;
@@ -58,57 +62,71 @@ __device__ __forceinline__ void gemv_job(const GemvArgs& p, int j, int& s, int& 
   nrows = min(rpp, p.seg[s].rows - row0);
 }
 
-__device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
-  return v > bv || (v == bv && i < bi);
-}
-
+template <int CPL>
 __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const GemvArgs p) {
-  extern __shared__ __align__(16) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  ActSmem a = carve_act(smem, p.K);
-  const size_t act_bytes = (act_smem_bytes(p.K) + 15) & ~static_cast<size_t>(15);
+  ActSmem a = carve_act(smem, p.K, p.need_xf != 0);
+  const size_t act_bytes = (act_smem_bytes(p.K, p.need_xf != 0) + 15) & ~static_cast<size_t>(15);
   double* red = reinterpret_cast<double*>(smem + act_bytes);
-  uint8_t* stage = smem + act_bytes + 48 * sizeof(double);
-  __shared__ float s_bv[kGemvWarps];
-  __shared__ int s_bi[kGemvWarps];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + act_bytes + 48 * sizeof(double));
+  uint8_t* stage = smem + act_bytes + 48 * sizeof(double) + kGemvWarps * p.S * sizeof(uint64_t);
+  __shared__ float s_bv[32];
+  __shared__ int s_bi[32];
   __shared__ bool s_last;
 
   int pos = 0, n_prompt = 0;
   bool skip = false;
   if (p.argmax) {
-    pos = p.state->pos;
-    n_prompt = p.state->n_prompt;
+    // The cursor was last written by the previous token's argmax, which has
+    // completed before this kernel could launch.
+    pos = *reinterpret_cast<volatile const int*>(&p.state->pos);
+    n_prompt = *reinterpret_cast<volatile const int*>(&p.state->n_prompt);
     skip = pos < n_prompt - 1;
   }
+  const int gw = blockIdx.x * kGemvWarps + warp;
+  const int tw = gridDim.x * kGemvWarps;
+  uint64_t* wbar = bars + warp * p.S;
+  uint8_t* wb = stage + static_cast<size_t>(warp) * p.S * p.stage_bytes;
+  if (lane == 0) {
+    for (int s = 0; s < p.S; ++s) mbar_init(&wbar[s], 1);
+    fence_barrier_init();
+  }
+  __syncwarp();
+  auto issue = [&](int j, int st) {
+    int s, row0, nrows;
+    gemv_job(p, j, s, row0, nrows);
+    if (p.seg[s].type == NH_TYPE_F32) return;
+    if (lane == 0) {
+      uint32_t len, off;
+      const uint8_t* src = span16(p.seg[s].w + static_cast<uint64_t>(row0) * p.seg[s].rb,
+                                  static_cast<size_t>(nrows) * p.seg[s].rb, &len, &off);
+      mbar_expect_tx(&wbar[st], len);
+      bulk_g2s(wb + static_cast<size_t>(st) * p.stage_bytes, src, len, &wbar[st]);
+    }
+  };
+  if (!skip) {
+#pragma unroll
+    for (int st = 0; st < p.S; ++st) {
+      const int j = gw + st * tw;
+      if (j < p.jobs_total) issue(j, st);
+    }
+  }
+  pdl_wait();
+  pdl_trigger();
+
   float best_v = -INFINITY;
   int best_i = INT_MAX;
+  bool failed = false;
   if (!skip) {
     prep_act(a, p.x, p.norm_w, p.do_norm != 0, p.eps, p.quant != 0, red);
-    const int gw = blockIdx.x * kGemvWarps + warp;
-    const int tw = gridDim.x * kGemvWarps;
-    uint8_t* wb = stage + static_cast<size_t>(warp) * kGemvStages * p.stage_bytes;
-    const int nsb = p.K / QK;
-    const int sub = lane % p.lpr, kr = lane / p.lpr;
-
-    auto issue = [&](int j, uint8_t* buf) {
-      int s, row0, nrows;
-      gemv_job(p, j, s, row0, nrows);
-      if (p.seg[s].type == NH_TYPE_F32) return;
-      stage_bytes_warp(buf, p.seg[s].w + static_cast<uint64_t>(row0) * p.seg[s].rb,
-                       static_cast<size_t>(nrows) * p.seg[s].rb, lane);
-    };
-#pragma unroll
-    for (int st = 0; st < kGemvStages; ++st) {
-      const int j = gw + st * tw;
-      if (j < p.jobs_total) issue(j, wb + st * p.stage_bytes);
-      cp_async_commit();
-    }
+    const int jl = lane % p.lpr, kr = lane / p.lpr;
+    ActReg<CPL> ar;
+    if (p.quant) load_act<CPL>(ar, a, 0, jl, p.lpr);
     for (int it = 0;; ++it) {
       const int j = gw + it * tw;
       if (j >= p.jobs_total) break;
-      cp_async_wait<kGemvStages - 1>();
-      __syncwarp();
-      uint8_t* buf = wb + (it % kGemvStages) * p.stage_bytes;
+      const int st = it % p.S;
       int s, row0, nrows;
       gemv_job(p, j, s, row0, nrows);
       const GemvSeg& sg = p.seg[s];
@@ -117,81 +135,69 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const GemvArgs p)
       bool writer;
       if (sg.type == NH_TYPE_F32) {
         r = row0;
-        v = row_dot_f32(reinterpret_cast<const float*>(sg.w + static_cast<uint64_t>(r) * sg.rb),
-                        a.xf, p.K, lane);
+        v = row_dot_f32(reinterpret_cast<const float*>(sg.w + static_cast<uint64_t>(r) * sg.rb), a.xf, p.K, lane);
         writer = lane == 0;
       } else {
-        const uintptr_t off = reinterpret_cast<uintptr_t>(sg.w + static_cast<uint64_t>(row0) * sg.rb) & 15;
-        const uint8_t* rowp = buf + off + static_cast<size_t>(kr) * sg.rb;
-        v = row_dot_q(rowp, sg.type, nsb, sub, p.lpr, a);
+        if (!mbar_wait(&wbar[st], (it / p.S) & 1)) {
+          failed = true;
+          break;
+        }
+        const uint32_t off =
+            static_cast<uint32_t>(reinterpret_cast<uintptr_t>(sg.w + static_cast<uint64_t>(row0) * sg.rb) & 15);
+        const uint8_t* rowp = wb + static_cast<size_t>(st) * p.stage_bytes + off + static_cast<size_t>(kr) * sg.rb;
+        v = row_dot_reg<CPL>(rowp, sg.type, jl, p.lpr, ar);
         r = row0 + kr;
-        writer = sub == 0 && kr < nrows;
+        writer = jl == 0 && kr < nrows;
       }
       if (writer) {
         if (sg.resid != nullptr) v = __fadd_rn(sg.resid[r], v);
         if (sg.out != nullptr) sg.out[r] = v;
         if (p.argmax) {
-          if (p.logits_dump != nullptr) {
-            p.logits_dump[static_cast<int64_t>(pos - n_prompt + 1) * sg.rows + r] = v;
-          }
-          if (better(v, r, best_v, best_i)) {
+          if (p.logits_dump != nullptr) p.logits_dump[static_cast<int64_t>(pos - n_prompt + 1) * sg.rows + r] = v;
+          if (argmax_better(v, r, best_v, best_i)) {
             best_v = v;
             best_i = r;
           }
         }
       }
       __syncwarp();
-      const int jn = gw + (it + kGemvStages) * tw;
-      if (jn < p.jobs_total) issue(jn, buf);
-      cp_async_commit();
+      const int jn = gw + (it + p.S) * tw;
+      if (jn < p.jobs_total) issue(jn, st);
     }
-    cp_async_wait<0>();
   }
+  if (failed && lane == 0 && p.state != nullptr) atomicCAS(&p.state->error, 0, NH_E_TIMEOUT);
   if (!p.argmax) return;
 
-  // Block argmax, then the last CTA (by ticket) reduces the per-CTA partials
-  // and advances the decode cursor.
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
-    if (better(ov, oi, best_v, best_i)) {
-      best_v = ov;
-      best_i = oi;
-    }
-  }
-  if (lane == 0) {
-    s_bv[warp] = best_v;
-    s_bi[warp] = best_i;
-  }
-  __syncthreads();
+  // Per-CTA argmax, then the last CTA (by ticket) reduces the partials with
+  // all its threads and advances the decode cursor.
+  block_argmax(best_v, best_i, s_bv, s_bi);
   if (threadIdx.x == 0) {
-    float bv = s_bv[0];
-    int bi = s_bi[0];
-    for (int w = 1; w < kGemvWarps; ++w)
-      if (better(s_bv[w], s_bi[w], bv, bi)) {
-        bv = s_bv[w];
-        bi = s_bi[w];
-      }
-    p.part_val[blockIdx.x] = bv;
-    p.part_idx[blockIdx.x] = bi;
+    p.part_val[blockIdx.x] = best_v;
+    p.part_idx[blockIdx.x] = best_i;
     __threadfence();
     const unsigned t = atomicAdd(p.ticket, 1u);
     s_last = (t == gridDim.x - 1);
   }
   __syncthreads();
-  if (!s_last || threadIdx.x != 0) return;
+  if (!s_last) return;
   __threadfence();
+  float bv = -INFINITY;
+  int bi = INT_MAX;
   if (!skip) {
-    volatile float* pv = p.part_val;
-    volatile int32_t* pi = p.part_idx;
-    float bv = pv[0];
-    int bi = pi[0];
-    for (unsigned b = 1; b < gridDim.x; ++b)
-      if (better(pv[b], pi[b], bv, bi)) {
-        bv = pv[b];
-        bi = pi[b];
+    const volatile float* pv = p.part_val;
+    const volatile int32_t* pi = p.part_idx;
+    for (unsigned b = threadIdx.x; b < gridDim.x; b += blockDim.x) {
+      const float v = pv[b];
+      const int i = pi[b];
+      if (argmax_better(v, i, bv, bi)) {
+        bv = v;
+        bi = i;
       }
+    }
+  }
+  block_argmax(bv, bi, s_bv, s_bi);
+  if (threadIdx.x != 0) return;
+  if (!skip) {
     if (bi == INT_MAX) bi = 0;
     const int n = p.state->n_out;
     if (n < p.state->n_predict) p.out_tokens[n] = bi;
@@ -204,38 +210,34 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const GemvArgs p)
 
 namespace {
 
-int g_sm_count[16] = {0};
-
-int sm_count() {
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 16) dev = 0;
-  if (g_sm_count[dev] == 0) {
-    int n = 0;
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    g_sm_count[dev] = n > 0 ? n : 148;
-  }
-  return g_sm_count[dev];
-}
-
 bool valid_type(int t) { return t == NH_TYPE_F32 || t == NH_TYPE_Q4_K || t == NH_TYPE_Q6_K; }
+
+template <int CPL>
+int gemv_launch_t(GemvArgs& p, size_t smem, int grid, cudaStream_t stream) {
+  static size_t configured = 48 * 1024;
+  if (!ensure_smem(gemv_kernel<CPL>, smem, configured)) return NH_E_CUDA;
+  return launch_pdl(gemv_kernel<CPL>, dim3(grid), dim3(kGemvWarps * 32), smem, stream, p);
+}
 
 // Fills the work split of a GemvArgs whose segments, K and activation source are set.
 int gemv_launch(GemvArgs& p, cudaStream_t stream) {
   if (p.K <= 0 || p.K > kMaxK) return NH_E_ARG;
-  bool any_q = false;
+  bool any_q = false, any_f = false;
   uint64_t rb_max = 0;
   for (int s = 0; s < p.nseg; ++s) {
     if (!valid_type(p.seg[s].type) || p.seg[s].w == nullptr || p.seg[s].rows < 0) return NH_E_ARG;
     if (p.seg[s].type != NH_TYPE_F32) {
-      if (p.K % QK != 0) return NH_E_ARG;
+      if (!rowdot_k_ok(p.K)) return NH_E_ARG;
       any_q = true;
+    } else {
+      any_f = true;
     }
     p.seg[s].rb = row_bytes(p.seg[s].type, p.K);
     rb_max = rb_max > p.seg[s].rb ? rb_max : p.seg[s].rb;
   }
   p.quant = any_q ? 1 : 0;
-  p.lpr = any_q ? lanes_per_row(p.K / QK) : 32;
+  p.need_xf = any_f ? 1 : 0;
+  p.lpr = any_q ? rowdot_lpr(p.K) : 32;
   p.rpp = 32 / p.lpr;
   int total = 0;
   for (int s = 0; s < p.nseg; ++s) {
@@ -245,25 +247,21 @@ int gemv_launch(GemvArgs& p, cudaStream_t stream) {
   }
   for (int s = p.nseg; s < 4; ++s) p.jobs_start[s] = total;
   p.jobs_total = total;
-  p.stage_bytes = any_q ? static_cast<uint32_t>((rb_max * p.rpp + 32 + 15) & ~15ull) : 16u;
-  const size_t smem = ((act_smem_bytes(p.K) + 15) & ~static_cast<size_t>(15)) + 48 * sizeof(double) +
-                      static_cast<size_t>(kGemvWarps) * kGemvStages * p.stage_bytes;
-  static size_t configured = 0;
-  if (smem > configured) {
-    if (cudaFuncSetAttribute(gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem)) != cudaSuccess) {
-      return NH_E_CUDA;
-    }
-    configured = smem;
-  }
-  const int per_sm = smem > 110 * 1024 ? 1 : 2;
+  p.stage_bytes = any_q ? static_cast<uint32_t>((rb_max * p.rpp + 32 + 127) & ~127ull) : 128u;
+  p.S = kGemvMaxStages;
+  while (p.S > 2 && static_cast<size_t>(kGemvWarps) * p.S * p.stage_bytes > 96 * 1024) --p.S;
+  const size_t smem = ((act_smem_bytes(p.K, any_f) + 15) & ~static_cast<size_t>(15)) + 48 * sizeof(double) +
+                      kGemvWarps * p.S * sizeof(uint64_t) +
+                      static_cast<size_t>(kGemvWarps) * p.S * p.stage_bytes;
+  const int per_sm = static_cast<int>(std::min<size_t>(4, (220 * 1024) / (smem + 1024)));
   int grid = (total + kGemvWarps - 1) / kGemvWarps;
-  const int cap = sm_count() * per_sm;
+  const int cap = device_sm_count() * (per_sm < 1 ? 1 : per_sm);
   if (grid > cap) grid = cap;
   if (p.argmax && grid > kMaxArgmaxBlocks) grid = kMaxArgmaxBlocks;
   if (grid < 1) grid = 1;
-  gemv_kernel<<<grid, kGemvWarps * 32, smem, stream>>>(p);
-  return cudaGetLastError() == cudaSuccess ? NH_OK : NH_E_CUDA;
+  const int cpl = any_q ? (p.K / 64 + 31) / 32 : 1;
+  if (cpl <= 1) return gemv_launch_t<1>(p, smem, grid, stream);
+  return gemv_launch_t<2>(p, smem, grid, stream);
 }
 
 GemvArgs blank_args() {
@@ -283,14 +281,11 @@ extern "C" int nh_device_sm_count(int device) {
   return n;
 }
 
-extern "C" int64_t nh_argmax_scratch_bytes(int /*n_vocab*/) {
-  return static_cast<int64_t>(kMaxArgmaxBlocks) * 8 + 64;
-}
+extern "C" int64_t nh_argmax_scratch_bytes(int /*n_vocab*/) { return static_cast<int64_t>(kMaxArgmaxBlocks) * 8 + 64; }
 
-extern "C" int nh_qkv_proj(const float* h, const float* attn_norm, float eps, const void* wq,
-                           int32_t tq, const void* wk, int32_t tk, const void* wv, int32_t tv,
-                           int64_t n_embd, int64_t n_embd_kv, float* q_out, float* k_out,
-                           float* v_out, void* stream) {
+extern "C" int nh_qkv_proj(NhDecodeState* state, const float* h, const float* attn_norm, float eps, const void* wq, int32_t tq,
+                           const void* wk, int32_t tk, const void* wv, int32_t tv, int64_t n_embd, int64_t n_embd_kv,
+                           float* q_out, float* k_out, float* v_out, void* stream) {
   if (h == nullptr || q_out == nullptr || k_out == nullptr || v_out == nullptr) return NH_E_ARG;
   GemvArgs p = blank_args();
   p.nseg = 3;
@@ -298,6 +293,7 @@ extern "C" int nh_qkv_proj(const float* h, const float* attn_norm, float eps, co
   p.seg[0] = {static_cast<const uint8_t*>(wq), q_out, nullptr, static_cast<int32_t>(n_embd), tq, 0};
   p.seg[1] = {static_cast<const uint8_t*>(wk), k_out, nullptr, static_cast<int32_t>(n_embd_kv), tk, 0};
   p.seg[2] = {static_cast<const uint8_t*>(wv), v_out, nullptr, static_cast<int32_t>(n_embd_kv), tv, 0};
+  p.state = state;
   p.x = h;
   p.norm_w = attn_norm;
   p.eps = eps;
@@ -305,20 +301,20 @@ extern "C" int nh_qkv_proj(const float* h, const float* attn_norm, float eps, co
   return gemv_launch(p, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int nh_out_proj_residual(const float* x, const void* wo, int32_t to, int64_t n_embd,
-                                    float* h_io, void* stream) {
+extern "C" int nh_out_proj_residual(NhDecodeState* state, const float* x, const void* wo, int32_t to, int64_t n_embd, float* h_io,
+                                    void* stream) {
   if (x == nullptr || h_io == nullptr) return NH_E_ARG;
   GemvArgs p = blank_args();
   p.nseg = 1;
   p.K = static_cast<int>(n_embd);
   p.seg[0] = {static_cast<const uint8_t*>(wo), h_io, h_io, static_cast<int32_t>(n_embd), to, 0};
+  p.state = state;
   p.x = x;
   return gemv_launch(p, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int nh_lm_head_argmax(NhDecodeState* state, const float* h, const float* out_norm,
-                                 float eps, const void* w, int32_t tw, int64_t n_embd,
-                                 int64_t n_vocab, int32_t* out_tokens, float* logits_dump,
+extern "C" int nh_lm_head_argmax(NhDecodeState* state, const float* h, const float* out_norm, float eps, const void* w,
+                                 int32_t tw, int64_t n_embd, int64_t n_vocab, int32_t* out_tokens, float* logits_dump,
                                  void* scratch, void* stream) {
   if (state == nullptr || h == nullptr || out_tokens == nullptr || scratch == nullptr) return NH_E_ARG;
   GemvArgs p = blank_args();
@@ -340,13 +336,14 @@ extern "C" int nh_lm_head_argmax(NhDecodeState* state, const float* h, const flo
   return gemv_launch(p, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int nh_gemv(const void* w, int32_t type, int64_t n, int64_t rows, const float* x,
-                       const float* norm_w, float eps, float* y, void* stream) {
+extern "C" int nh_gemv(NhDecodeState* state, const void* w, int32_t type, int64_t n, int64_t rows, const float* x, const float* norm_w,
+                       float eps, float* y, void* stream) {
   if (w == nullptr || x == nullptr || y == nullptr || rows <= 0) return NH_E_ARG;
   GemvArgs p = blank_args();
   p.nseg = 1;
   p.K = static_cast<int>(n);
   p.seg[0] = {static_cast<const uint8_t*>(w), y, nullptr, static_cast<int32_t>(rows), type, 0};
+  p.state = state;
   p.x = x;
   p.norm_w = norm_w;
   p.eps = eps;

@@ -1,0 +1,66 @@
+// Host-side launch helpers shared by the kernel files.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdlib>
+#include <utility>
+
+#include "../../../include/nh_kernels.h"
+
+namespace nh {
+
+// SM count of the current device (cached per device).
+inline int device_sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (cached[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
+// Programmatic dependent launch is on unless NH_PDL=0 is set in the
+// environment (read once).
+inline int pdl_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("NH_PDL");
+    v = (e != nullptr && e[0] == '0') ? 0 : 1;
+  }
+  return v;
+}
+
+template <typename Kern>
+bool ensure_smem(Kern k, size_t bytes, size_t& configured) {
+  if (bytes <= configured) return true;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)) != cudaSuccess)
+    return false;
+  configured = bytes;
+  return true;
+}
+
+// Launches with the programmatic-stream-serialisation attribute, so the
+// kernel may begin while its predecessor in the stream finishes; kernels
+// launched this way call griddepcontrol.wait before reading any result of
+// the preceding kernel.
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = pdl_enabled();
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...) == cudaSuccess ? NH_OK : NH_E_CUDA;
+}
+
+}  // namespace nh

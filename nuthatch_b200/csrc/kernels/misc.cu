@@ -1,6 +1,7 @@
 // Embedding lookup for the decode cursor, and the standalone Q8_K
 // quantisation / K-quant dequantisation entry points the parity tests use.
 #include "common.cuh"
+#include "launch.cuh"
 
 namespace nh {
 
@@ -35,6 +36,9 @@ __device__ __forceinline__ float dequant_elem(const uint8_t* row, int type, int6
 __global__ void embed_kernel(const NhDecodeState* state, const int32_t* prompt, const uint8_t* table,
                              int type, int64_t n_embd, int64_t n_vocab, uint64_t rb, float* h) {
   __shared__ int s_tok;
+  // The fed-back id comes from the preceding argmax.
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
   if (threadIdx.x == 0) {
     const int pos = state->pos;
     int tok = pos < state->n_prompt ? prompt[pos] : state->token;
@@ -62,11 +66,11 @@ __global__ void dequant_kernel(const uint8_t* w, int type, int64_t n, int64_t ro
 __global__ void quantize_kernel(const float* x, int64_t n, uint8_t* out) {
   __shared__ __align__(16) uint8_t smem[2048];
   __shared__ double red[48];
-  ActSmem a = carve_act(smem, QK);
+  ActSmem a = carve_act(smem, QK, false);
   prep_act(a, x + static_cast<int64_t>(blockIdx.x) * QK, nullptr, false, 0.f, true, red);
   uint8_t* blk = out + static_cast<int64_t>(blockIdx.x) * 292;
   if (threadIdx.x == 0) *reinterpret_cast<float*>(blk) = a.d[0];
-  for (int i = threadIdx.x; i < QK; i += blockDim.x) blk[4 + i] = static_cast<uint8_t>(a.qs[i]);
+  for (int i = threadIdx.x; i < QK; i += blockDim.x) blk[4 + i] = static_cast<uint8_t>(a.qs[q8_off(0, i)]);
   for (int i = threadIdx.x; i < 16; i += blockDim.x) {
     const int16_t v = a.bsums[i];
     blk[260 + 2 * i] = static_cast<uint8_t>(v & 0xFF);
@@ -74,18 +78,31 @@ __global__ void quantize_kernel(const float* x, int64_t n, uint8_t* out) {
   }
 }
 
+__global__ void exp_cw_kernel(const float* x, int64_t n, float* y) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    y[i] = exp_cw(x[i]);
+}
+
 }  // namespace nh
 
 using namespace nh;
+
+extern "C" int nh_exp_cw(const float* x, int64_t n, float* y, void* stream) {
+  if (x == nullptr || y == nullptr || n <= 0) return NH_E_ARG;
+  const int grid = static_cast<int>(std::min<int64_t>(1024, (n + 255) / 256));
+  exp_cw_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, n, y);
+  return cudaGetLastError() == cudaSuccess ? NH_OK : NH_E_CUDA;
+}
 
 extern "C" int nh_embed_step(const NhDecodeState* state, const int32_t* prompt_ids, const void* table,
                              int32_t type, int64_t n_embd, int64_t n_vocab, float* h_out, void* stream) {
   if (state == nullptr || prompt_ids == nullptr || table == nullptr || h_out == nullptr) return NH_E_ARG;
   if (type != NH_TYPE_F32 && type != NH_TYPE_Q4_K && type != NH_TYPE_Q6_K) return NH_E_TYPE;
   if (type != NH_TYPE_F32 && n_embd % QK != 0) return NH_E_ARG;
-  embed_kernel<<<1, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      state, prompt_ids, static_cast<const uint8_t*>(table), type, n_embd, n_vocab, row_bytes(type, n_embd), h_out);
-  return cudaGetLastError() == cudaSuccess ? NH_OK : NH_E_CUDA;
+  return launch_pdl(embed_kernel, dim3(1), dim3(256), 0, static_cast<cudaStream_t>(stream), state, prompt_ids,
+                    static_cast<const uint8_t*>(table), static_cast<int>(type), n_embd, n_vocab,
+                    static_cast<uint64_t>(row_bytes(type, n_embd)), h_out);
 }
 
 extern "C" int nh_dequantize(const void* w, int32_t type, int64_t n, int64_t rows, float* y, void* stream) {

@@ -60,6 +60,8 @@ def olib() -> C.CDLL:
         L.oracle_rms_norm_mul.argtypes = [P(C.c_float), P(C.c_float), C.c_int64, C.c_float, P(C.c_float)]
         L.oracle_rope_neox.argtypes = [P(C.c_float), C.c_int, C.c_int, C.c_float]
         L.oracle_softmax.argtypes = [P(C.c_float), C.c_int64]
+        L.oracle_exp.restype = C.c_float
+        L.oracle_exp.argtypes = [C.c_float]
         L.oracle_replay.restype = C.c_int64
         L.oracle_replay.argtypes = [C.c_int, C.c_uint32, C.c_uint32, C.c_int64, P(C.c_uint32), P(C.c_int64),
                                     P(C.c_uint32), C.c_uint32, C.c_uint32, P(C.c_int64)]

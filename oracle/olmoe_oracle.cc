@@ -15,6 +15,21 @@
 //     and forms integer sub-block dot products that are scaled in f32, NEOX
 //     RoPE advances theta by repeated multiplication by base^(-2/n_dims).
 //
+// Summation order and exp.  ggml leaves the order of f32 accumulation to each
+// CPU's SIMD code, so any fixed order restates it equally well.  Because a
+// Q8_K activation quantiser is discontinuous (a last-bit difference in its
+// input can move one quant by 1, which moves a whole GEMV output by ~1e-3),
+// this restatement fixes one canonical order, shared with the device kernels
+// so their results can be compared bit for bit:
+//   * a quantised row's super-block values are summed as a pairwise tree
+//     (RowSum below);
+//   * f32 dot products are lane-strided partial sums over 32 lanes combined
+//     by a butterfly (DotF32Lanes), with the 128-element vector variant for
+//     the router when the row length allows it;
+//   * exp is ExpCW: Cody & Waite range reduction (ln 2 = 355/512 + c2) and a
+//     degree-7 Taylor polynomial in Horner form, every step an IEEE f32 op;
+//   * attention runs in 64-position splits combined by their maxima.
+//
 // Pinning: Q4_K/Q6_K bit layouts are checked against gguf-py's dequantisers;
 // the structural properties of the reference tests (cached == uncached,
 // streaming == resident, causality, trace well-formedness) are checked on the
@@ -58,7 +73,10 @@ class Pool {
   void SetThreads(int n) {
     Stop();
     n_ = std::max(1, n);
-    for (int i = 1; i < n_; ++i) workers_.emplace_back([this, i] { Loop(i); });
+    // New workers start from the current job generation, so they wait for the
+    // next job instead of running the last one again.
+    const uint64_t start = gen_;
+    for (int i = 1; i < n_; ++i) workers_.emplace_back([this, i, start] { Loop(i, start); });
   }
   int threads() const { return n_; }
   // fn(begin, end) over [0, n) split into contiguous ranges, one per thread.
@@ -89,8 +107,7 @@ class Pool {
     const int64_t b = std::min<int64_t>(n, per * tid), e = std::min<int64_t>(n, b + per);
     if (b < e) fn(b, e);
   }
-  void Loop(int tid) {
-    uint64_t seen = 0;
+  void Loop(int tid, uint64_t seen) {
     for (;;) {
       const std::function<void(int64_t, int64_t)>* job;
       int64_t n;
@@ -244,10 +261,104 @@ void QuantizeQ8K(const float* x, int64_t n, Q8K* y) {
   }
 }
 
+// ExpCW: exp(x) = 2^k * e^r with k = nearest(x / ln 2) and r = x - k*ln 2
+// reduced in two steps (Cody & Waite, ln 2 = 355/512 - 2.1219444e-4), e^r
+// from its degree-7 Taylor polynomial in Horner form.
+float ExpCW(float x) {
+  if (x > 88.72283935546875f) return INFINITY;
+  if (x < -103.97208404541015625f) return 0.f;
+  const float kf = std::nearbyint(x * 1.44269502162933349609375f);
+  const float r = (x - kf * 0.693359375f) - kf * -2.12194440e-4f;
+  float p = 1.98412698e-4f;
+  p = p * r + 1.38888889e-3f;
+  p = p * r + 8.33333333e-3f;
+  p = p * r + 4.16666667e-2f;
+  p = p * r + 1.66666667e-1f;
+  p = p * r + 0.5f;
+  p = p * r + 1.0f;
+  p = p * r + 1.0f;
+  return std::ldexp(p, static_cast<int>(kf));
+}
+
+// 32-lane butterfly of per-lane partial sums (lane l adds lane l^o for
+// o = 16, 8, 4, 2, 1); the value every lane ends with.
+float Butterfly32(float (&a)[32]) {
+  for (int o = 16; o > 0; o >>= 1) {
+    float b[32];
+    for (int l = 0; l < 32; ++l) b[l] = a[l] + a[l ^ o];
+    std::copy(b, b + 32, a);
+  }
+  return a[0];
+}
+double Butterfly32d(double (&a)[32]) {
+  for (int o = 16; o > 0; o >>= 1) {
+    double b[32];
+    for (int l = 0; l < 32; ++l) b[l] = a[l] + a[l ^ o];
+    std::copy(b, b + 32, a);
+  }
+  return a[0];
+}
+
+// f32 dot: lane l sums elements l, l+32, ... in order, lanes combined by the butterfly.
+float DotF32Lanes(const float* a, const float* b, int64_t n) {
+  float s[32];
+  for (int l = 0; l < 32; ++l) {
+    float acc = 0.f;
+    for (int64_t i = l; i < n; i += 32) acc = acc + a[i] * b[i];
+    s[l] = acc;
+  }
+  return Butterfly32(s);
+}
+
+// f32 dot for rows of a multiple of 128: lane l sums the 4-element groups
+// 4l + 128t (t ascending, elements in order), lanes combined by the butterfly.
+float DotF32Vec128(const float* a, const float* b, int64_t n) {
+  float s[32];
+  for (int l = 0; l < 32; ++l) {
+    float acc = 0.f;
+    for (int64_t t = 0; t < n / 128; ++t)
+      for (int c = 0; c < 4; ++c) {
+        const int64_t i = 4 * l + 128 * t + c;
+        acc = acc + a[i] * b[i];
+      }
+    s[l] = acc;
+  }
+  return Butterfly32(s);
+}
+
+// Sum of a quantised row's super-block values.  The row of n values is n/64
+// chunks over LPR = min(32, n/64) lanes; lane j (a multiple of 4) holds the
+// running sum of super-blocks j/4, j/4 + LPR/4, ...; lanes are combined by a
+// butterfly over strides 4 .. LPR/2.  For 8 super-blocks this is
+// ((v0+v1)+(v2+v3))+((v4+v5)+(v6+v7)).  Other row lengths sum in order.
+float RowSum(const float* v, int64_t n) {
+  const int64_t chunks = n / 64;
+  if (n % QK != 0 || n > 4096 || (chunks & (chunks - 1)) != 0) {
+    float s = 0.f;
+    for (int64_t b = 0; b < n / QK; ++b) s = s + v[b];
+    return s;
+  }
+  const int lpr = static_cast<int>(std::min<int64_t>(32, chunks));
+  const int cpl = static_cast<int>(chunks / lpr);
+  float a[32] = {0};
+  for (int j = 0; j < lpr; j += 4) {
+    float acc = 0.f;
+    for (int t = 0; t < cpl; ++t) acc = acc + v[(j + lpr * t) / 4];
+    a[j] = acc;
+  }
+  for (int o = 4; o < lpr; o <<= 1) {
+    float b[32];
+    for (int j = 0; j < lpr; ++j) b[j] = a[j] + a[j ^ o];
+    std::copy(b, b + lpr, a);
+  }
+  return a[0];
+}
+
 // Q4_K x Q8_K: per super-block, integer sums sum_j sc_j*<q4,q8>_j and
-// sum_j m_j*bsum_j, scaled by (d*yd) and (dmin*yd) in f32.
+// sum_j m_j*bsum_j, scaled by (d*yd) and (dmin*yd) in f32; super-blocks
+// combined by RowSum.
 float DotQ4K(const uint8_t* w, const Q8K* y, int64_t n) {
-  float sumf = 0.f;
+  float vals[QK];
   for (int64_t b = 0; b < n / QK; ++b) {
     const uint8_t* blk = w + 144 * b;
     uint16_t dh, mh;
@@ -269,14 +380,15 @@ float DotQ4K(const uint8_t* w, const Q8K* y, int64_t n) {
     }
     const float d = Half(dh) * y[b].d;
     const float dmin = Half(mh) * y[b].d;
-    sumf += d * static_cast<float>(sumi) - dmin * static_cast<float>(summ);
+    vals[b] = d * static_cast<float>(sumi) - dmin * static_cast<float>(summ);
   }
-  return sumf;
+  return RowSum(vals, n);
 }
 
-// Q6_K x Q8_K: per super-block, integer sum_j sc_j*<q6-32,q8>_j scaled by d*yd.
+// Q6_K x Q8_K: per super-block, integer sum_j sc_j*<q6-32,q8>_j scaled by
+// d*yd; super-blocks combined by RowSum.
 float DotQ6K(const uint8_t* w, const Q8K* y, int64_t n) {
-  float sumf = 0.f;
+  float vals[QK];
   for (int64_t b = 0; b < n / QK; ++b) {
     const uint8_t* blk = w + 210 * b;
     uint16_t dh;
@@ -288,15 +400,9 @@ float DotQ6K(const uint8_t* w, const Q8K* y, int64_t n) {
       for (int l = 0; l < 16; ++l) s += Q6KValue(blk, 16 * j + l) * y[b].qs[16 * j + l];
       sumi += sc[j] * s;
     }
-    sumf += (Half(dh) * y[b].d) * static_cast<float>(sumi);
+    vals[b] = (Half(dh) * y[b].d) * static_cast<float>(sumi);
   }
-  return sumf;
-}
-
-float DotF32(const float* a, const float* b, int64_t n) {
-  float s = 0.f;
-  for (int64_t i = 0; i < n; ++i) s += a[i] * b[i];
-  return s;
+  return RowSum(vals, n);
 }
 
 // ---------------------------------------------------------------- GGUF reading
@@ -479,18 +585,86 @@ void RmsNormMul(const float* x, const float* w, int64_t n, float eps, float* y) 
   }
 }
 
-// ggml_soft_max over one row: exp(x - max) summed in double, scaled by 1/sum.
-void SoftMax(float* x, int64_t n) {
+// ggml_soft_max over the router logits (moe.cc:20): exp(x - max) in f32,
+// summed in double, scaled by 1/sum.  The double sum is formed per lane
+// (experts l, l+32, ...) and combined by the butterfly.
+void RouterSoftMax(float* x, int64_t n) {
   float mx = -INFINITY;
   for (int64_t i = 0; i < n; ++i) mx = std::max(mx, x[i]);
-  double sum = 0.0;
-  for (int64_t i = 0; i < n; ++i) {
-    const float e = (x[i] == -INFINITY) ? 0.f : std::exp(x[i] - mx);
-    x[i] = e;
-    sum += static_cast<double>(e);
+  double lanes[32];
+  for (int l = 0; l < 32; ++l) {
+    double s = 0.0;
+    for (int64_t i = l; i < n; i += 32) {
+      x[i] = ExpCW(x[i] - mx);
+      s += static_cast<double>(x[i]);
+    }
+    lanes[l] = s;
   }
-  const float inv = static_cast<float>(1.0 / sum);
+  const float inv = static_cast<float>(1.0 / Butterfly32d(lanes));
   for (int64_t i = 0; i < n; ++i) x[i] *= inv;
+}
+
+// Attention of one query over keys 0..n_kv-1 (attention.cc:174-182): scores
+// K.q * kq_scale, causal softmax, V.p.  Restated in 64-key splits: a split's
+// exponentials are taken against its own maximum and the splits combined by
+// their maxima, which is the same softmax; one split reduces to ggml's
+// scale-by-1/sum before the V product.  Double sums: per thread t of 128
+// (keys t, t+128, ...), butterfly within each 32-thread group, groups in order.
+constexpr int kSplit = 64;
+
+double SplitSum(const float* e, int n) {
+  double total = 0.0;
+  for (int w = 0; w < 4; ++w) {
+    double lanes[32];
+    for (int l = 0; l < 32; ++l) {
+      double s = 0.0;
+      for (int j = 32 * w + l; j < n; j += 128) s += static_cast<double>(e[j]);
+      lanes[l] = s;
+    }
+    total += Butterfly32d(lanes);
+  }
+  return total;
+}
+
+void AttendOne(const float* qv, const float* kbase, const float* vbase, int64_t stride, int n_kv, int hd,
+               float kq_scale, float* out) {
+  const int n_split = (n_kv + kSplit - 1) / kSplit;
+  std::vector<float> m(n_split), acc(static_cast<size_t>(n_split) * hd), e(kSplit);
+  std::vector<double> l(n_split);
+  for (int s = 0; s < n_split; ++s) {
+    const int p0 = s * kSplit, n = std::min(kSplit, n_kv - p0);
+    float mx = -INFINITY;
+    for (int j = 0; j < n; ++j) {
+      e[j] = DotF32Lanes(kbase + (p0 + j) * stride, qv, hd) * kq_scale;
+      mx = std::max(mx, e[j]);
+    }
+    for (int j = 0; j < n; ++j) e[j] = ExpCW(e[j] - mx);
+    m[s] = mx;
+    l[s] = SplitSum(e.data(), n);
+    if (n_split == 1) {
+      const float inv = static_cast<float>(1.0 / l[s]);
+      for (int j = 0; j < n; ++j) e[j] = e[j] * inv;
+    }
+    for (int i = 0; i < hd; ++i) {
+      float a = 0.f;
+      for (int j = 0; j < n; ++j) a = a + vbase[(p0 + j) * stride + i] * e[j];
+      acc[static_cast<size_t>(s) * hd + i] = a;
+    }
+  }
+  if (n_split == 1) {
+    std::copy(acc.begin(), acc.begin() + hd, out);
+    return;
+  }
+  float M = -INFINITY;
+  for (int s = 0; s < n_split; ++s) M = std::max(M, m[s]);
+  double L = 0.0;
+  for (int s = 0; s < n_split; ++s) L += l[s] * static_cast<double>(ExpCW(m[s] - M));
+  const float inv = static_cast<float>(1.0 / L);
+  for (int i = 0; i < hd; ++i) {
+    float a = 0.f;
+    for (int s = 0; s < n_split; ++s) a = a + acc[static_cast<size_t>(s) * hd + i] * ExpCW(m[s] - M);
+    out[i] = a * inv;
+  }
 }
 
 // ggml_rope_ext, NEOX mode, ext_factor 0, freq_scale 1, attn_factor 1:
@@ -509,7 +683,7 @@ void RopeNeox(float* x, int n_dims, int pos, float base) {
   }
 }
 
-inline float Silu(float x) { return x / (1.0f + std::exp(-x)); }
+inline float Silu(float x) { return x / (1.0f + ExpCW(-x)); }
 
 // ggml_mul_mat(W, x) for one activation row over the rows [r0, r1) of a
 // (possibly 3-D expert) weight: quantised weights use the Q8_K activation.
@@ -525,19 +699,24 @@ struct Act {
   }
 };
 
-float RowDot(const Tensor& w, const uint8_t* row, const Act& a) {
+// `router`: the F32 router rows use the 128-element lane layout when their
+// length allows it.
+float RowDot(const Tensor& w, const uint8_t* row, const Act& a, bool router = false) {
   const int64_t n = w.ne[0];
   if (w.type == T_Q4K) return DotQ4K(row, a.q.data(), n);
   if (w.type == T_Q6K) return DotQ6K(row, a.q.data(), n);
-  return DotF32(reinterpret_cast<const float*>(row), a.f.data(), n);
+  const float* r = reinterpret_cast<const float*>(row);
+  if (router && n % 128 == 0) return DotF32Vec128(r, a.f.data(), n);
+  return DotF32Lanes(r, a.f.data(), n);
 }
 
-void MatVec(const Tensor& w, int64_t expert, const float* x, float* y, bool parallel = true) {
+void MatVec(const Tensor& w, int64_t expert, const float* x, float* y, bool parallel = true,
+            bool router = false) {
   Act a;
   a.Set(x, w.ne[0], w.type != T_F32);
   const uint8_t* base = w.data + w.nb2 * expert;
   auto body = [&](int64_t r0, int64_t r1) {
-    for (int64_t r = r0; r < r1; ++r) y[r] = RowDot(w, base + w.nb1 * r, a);
+    for (int64_t r = r0; r < r1; ++r) y[r] = RowDot(w, base + w.nb1 * r, a, router);
   };
   if (parallel) Pool::Get().For(w.ne[1], body);
   else body(0, w.ne[1]);
@@ -578,7 +757,6 @@ void ForwardCached(const Model& m, Kv* kv, const std::vector<int32_t>& tok, bool
   const int64_t V = c.n_vocab;
   const int T = static_cast<int>(tok.size());
   const int n_past = kv->n_past;
-  const int n_kv = n_past + T;
   const int64_t group = H / Hkv;
 
   // ggml_get_rows on token_embd (forward.cc:94-95): dequantised rows.
@@ -619,27 +797,14 @@ void ForwardCached(const Model& m, Kv* kv, const std::vector<int32_t>& tok, bool
       std::copy(&v[t * dkv], &v[t * dkv] + dkv, kv->v[l].begin() + (n_past + t) * dkv);
     }
     // attention.cc:174-182: kq = K.q * 1/sqrt(hd), causal mask offset n_past, softmax, V.p.
+    // Query t sees keys 0..n_past+t (the causal mask of ggml_diag_mask_inf).
     Pool::Get().For(H * T, [&](int64_t b, int64_t e) {
-      std::vector<float> p(n_kv);
       for (int64_t job = b; job < e; ++job) {
         const int64_t hh = job / T;
         const int t = static_cast<int>(job % T);
         const int64_t kh = hh / group;
-        const float* qv = &q[t * d + hh * hd];
-        for (int j = 0; j < n_kv; ++j) {
-          if (j > n_past + t) {
-            p[j] = -INFINITY;
-          } else {
-            const float* kr = &kv->k[l][j * dkv + kh * hd];
-            p[j] = DotF32(kr, qv, hd) * kq_scale;
-          }
-        }
-        SoftMax(p.data(), n_kv);
-        for (int64_t i = 0; i < hd; ++i) {
-          float s = 0.f;
-          for (int j = 0; j < n_kv; ++j) s += kv->v[l][j * dkv + kh * hd + i] * p[j];
-          att[t * d + hh * hd + i] = s;
-        }
+        AttendOne(&q[t * d + hh * hd], &kv->k[l][kh * hd], &kv->v[l][kh * hd], dkv, n_past + t + 1,
+                  static_cast<int>(hd), kq_scale, &att[t * d + hh * hd]);
       }
     });
     // Output projection and residual (forward.cc:106-108).
@@ -659,8 +824,8 @@ void ForwardCached(const Model& m, Kv* kv, const std::vector<int32_t>& tok, bool
         u(static_cast<size_t>(K) * F);
     for (int t = 0; t < T; ++t) {
       RmsNormMul(&h[t * d], ffn_norm, d, c.rms_eps, b.data());
-      MatVec(*router, 0, b.data(), probs.data(), false);
-      SoftMax(probs.data(), E);
+      MatVec(*router, 0, b.data(), probs.data(), false, true);
+      RouterSoftMax(probs.data(), E);
       // ggml_argsort_top_k: descending probability, ties by lower expert id.
       std::vector<int32_t> order(E);
       for (int64_t e = 0; e < E; ++e) order[e] = static_cast<int32_t>(e);
@@ -679,7 +844,12 @@ void ForwardCached(const Model& m, Kv* kv, const std::vector<int32_t>& tok, bool
         std::copy(sel.begin(), sel.end(), obs->sel->begin() + (static_cast<int64_t>(t) * c.n_layers + l) * K);
       }
       if (obs && obs->gap) {
-        (*obs->gap)[t * c.n_layers + l] = K < E ? probs[order[K - 1]] - probs[order[K]] : 1.f;
+        // Smallest gap between adjacent probabilities of the descending top-(k+1):
+        // a near-tie there can swap ids inside the trace or across the cut.
+        float g = 1.f;
+        for (int64_t i = 0; i + 1 < std::min<int64_t>(K + 1, E); ++i)
+          g = std::min(g, probs[order[i]] - probs[order[i + 1]]);
+        (*obs->gap)[t * c.n_layers + l] = g;
       }
       if (obs && obs->on_route) obs->on_route(l, sel);
       // up, gate, silu(gate)*up, down for each selected expert.
@@ -1021,7 +1191,8 @@ void oracle_rms_norm_mul(const float* x, const float* w, int64_t n, float eps, f
   RmsNormMul(x, w, n, eps, y);
 }
 void oracle_rope_neox(float* x, int n_dims, int pos, float base) { RopeNeox(x, n_dims, pos, base); }
-void oracle_softmax(float* x, int64_t n) { SoftMax(x, n); }
+void oracle_softmax(float* x, int64_t n) { RouterSoftMax(x, n); }
+float oracle_exp(float x) { return ExpCW(x); }
 
 // ---- policies over a flat trace: records of (layer, n, experts...) given as
 // arrays layer[R], offsets[R+1] into experts[].  kind 0 LRU(slots), 1 OS(slots

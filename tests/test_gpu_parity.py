@@ -1,14 +1,18 @@
 """GPU parity: the sm_100a path through the C ABI against the CPU oracle.
 
-Tolerances (written here, from the hot path's stated bar):
+The kernels and the oracle share one arithmetic contract (the order in which
+super-block values and f32 products are summed, and the exp used by softmax
+and SiLU; see the oracle's header), so the whole-token path is expected to be
+bit-identical:
   * integer/byte work is bit-exact: Q8_K activation quantisation, K-quant
-    dequantisation, routing ids (where no top-k near-tie < 1e-4 occurs),
-    greedy ids, slot-cache hit/miss counts;
-  * per-layer hidden states and logits: max |gpu - oracle| / max |oracle|
-    <= 2e-2 (REL_TOL).  The only intended differences are f32 summation
-    order, so the observed error is far smaller;
-  * single GEMV rows: <= GEMV_TOL relative (super-block partial sums are
-    added in a different order, nothing else differs).
+    dequantisation, routing ids, greedy ids, slot-cache hit/miss counts;
+  * per-layer hidden states and logits are compared for exact equality
+    (EXACT); the hot path's stated bound, max |gpu - oracle| / max |oracle|
+    <= 2e-2 (REL_TOL), is checked as well and is what a divergence would be
+    judged against;
+  * a greedy id or routing record may differ only where the oracle shows a
+    near-tie below NEAR_TIE (1e-4) at that point;
+  * standalone GEMV rows on random activations: <= GEMV_TOL relative.
 """
 from __future__ import annotations
 
@@ -34,6 +38,16 @@ def rel_err(a, b) -> float:
     a = np.asarray(a, dtype=np.float64)
     b = np.asarray(b, dtype=np.float64)
     return float(np.max(np.abs(a - b)) / max(float(np.max(np.abs(b))), 1e-30))
+
+
+EXACT = True
+
+
+def assert_matches(got, want, what=""):
+    err = rel_err(got, want)
+    assert err <= REL_TOL, f"{what} relative error {err:.3g} above the stated bound"
+    if EXACT:
+        assert np.array_equal(np.asarray(got), np.asarray(want)), f"{what} not bit-identical (rel err {err:.3g})"
 
 
 def torch_dev():
@@ -69,6 +83,15 @@ def assert_token_parity(gpu_tokens, ora: dict, n_prompt: int):
     assert gaps and min(gaps) < NEAR_TIE, f"greedy ids diverge at step {s} without a near-tie: {g} vs {o} {gaps}"
 
 
+def assert_trace_parity(g_sel, o_sel, o_gap):
+    """Routing records (ids in descending probability) are bit-exact wherever the
+    oracle's top-(k+1) has no adjacent gap below NEAR_TIE."""
+    ok = o_gap >= NEAR_TIE
+    bad = np.any(g_sel != o_sel, axis=-1) & ok
+    assert not bad.any(), (f"{int(bad.sum())} routing records differ away from near-ties; "
+                           f"smallest oracle gap among them {float(o_gap[bad].min()):.3g}")
+
+
 # ------------------------------------------------------------------ primitives
 def test_quantize_q8k_bit_exact(gpu):
     rng = np.random.default_rng(11)
@@ -82,6 +105,18 @@ def test_quantize_q8k_bit_exact(gpu):
     assert lib().nh_quantize_q8k(C.c_void_p(xd.data_ptr()), x.size, C.c_void_p(out.data_ptr()), stream_ptr()) == 0
     torch_dev().cuda.synchronize()
     assert out.cpu().numpy().tobytes() == oracle.quantize_q8k(x)
+
+
+def test_exp_bit_exact(gpu):
+    from tests.test_formats_oracle import exp_inputs
+
+    x = exp_inputs()
+    xd = to_dev(x)
+    y = torch_dev().zeros(x.size, dtype=torch_dev().float32, device="cuda")
+    assert lib().nh_exp_cw(C.c_void_p(xd.data_ptr()), x.size, C.c_void_p(y.data_ptr()), stream_ptr()) == 0
+    torch_dev().cuda.synchronize()
+    ref = np.array([oracle.olib().oracle_exp(float(v)) for v in x], dtype=np.float32)
+    assert np.array_equal(y.cpu().numpy().view(np.uint32), ref.view(np.uint32))
 
 
 @pytest.fixture(scope="module")
@@ -125,7 +160,7 @@ def test_gemv_matches_oracle(gpu, K, qtype, tmp_path):
     wd = to_dev(np.concatenate([raw, np.zeros(256, np.uint8)]))
     xd = to_dev(x)
     y = torch_dev().zeros(rows, dtype=torch_dev().float32, device="cuda")
-    assert lib().nh_gemv(C.c_void_p(wd.data_ptr()), qtype, K, rows, C.c_void_p(xd.data_ptr()), None, 0.0,
+    assert lib().nh_gemv(None, C.c_void_p(wd.data_ptr()), qtype, K, rows, C.c_void_p(xd.data_ptr()), None, 0.0,
                          C.c_void_p(y.data_ptr()), stream_ptr()) == 0
     torch_dev().cuda.synchronize()
     assert rel_err(y.cpu().numpy(), ref) <= GEMV_TOL
@@ -149,10 +184,9 @@ def test_mini_generate_matches_oracle(gpu, mini_models, norm_topk):
     g = nh.generate_ex(m, prompt, n, norm_topk, trace=True, hidden=True, logits=True)
     assert_token_parity(g["tokens"], ora, len(prompt))
     if g["tokens"] == ora["tokens"]:
-        assert rel_err(g["hidden"], ora["hidden"]) <= REL_TOL
-        assert rel_err(g["logits"], ora["logits"]) <= REL_TOL
-        ok = ora["gap"] >= NEAR_TIE
-        assert np.array_equal(g["sel"][ok], ora["sel"][ok])
+        assert_matches(g["hidden"], ora["hidden"])
+        assert_matches(g["logits"], ora["logits"])
+        assert_trace_parity(g["sel"], ora["sel"], ora["gap"])
     # Graph replay and eager launches run the same kernels: identical bits.
     e = nh.generate_ex(m, prompt, n, norm_topk, use_graph=False, hidden=True)
     assert e["tokens"] == g["tokens"]
@@ -167,7 +201,7 @@ def test_mini_gqa_and_all_experts(gpu, synth_dir):
     ora = om.generate(prompt, 8, mode=0, trace=True, hidden=True)
     g = nh.generate_ex(m, prompt, 8, False, hidden=True)
     assert_token_parity(g["tokens"], ora, len(prompt))
-    assert rel_err(g["hidden"], ora["hidden"]) <= REL_TOL
+    assert_matches(g["hidden"], ora["hidden"])
 
 
 def test_long_context_split_attention(gpu, mini_models):
@@ -178,8 +212,8 @@ def test_long_context_split_attention(gpu, mini_models):
     ora = om.generate(prompt, 6, mode=0, trace=True, hidden=True, logits=True)
     g = nh.generate_ex(m, prompt, 6, False, hidden=True, logits=True)
     assert_token_parity(g["tokens"], ora, len(prompt))
-    assert rel_err(g["hidden"], ora["hidden"]) <= REL_TOL
-    assert rel_err(g["logits"], ora["logits"]) <= REL_TOL
+    assert_matches(g["hidden"], ora["hidden"])
+    assert_matches(g["logits"], ora["logits"])
 
 
 # ------------------------------------------------------------------ the reference's own anchors
@@ -324,7 +358,6 @@ def test_olmoe_1b7b_resident_decode_matches_oracle(gpu, olmoe_path):
     assert_token_parity(g["tokens"], ora, len(prompt))
     if g["tokens"] == ora["tokens"]:
         for l in range(cfg.n_layers):
-            assert rel_err(g["hidden"][:, l], ora["hidden"][:, l]) <= REL_TOL, l
-        assert rel_err(g["logits"], ora["logits"]) <= REL_TOL
-        ok = ora["gap"] >= NEAR_TIE
-        assert np.array_equal(g["sel"][ok], ora["sel"][ok])
+            assert_matches(g["hidden"][:, l], ora["hidden"][:, l], f"layer {l}")
+        assert_matches(g["logits"], ora["logits"])
+        assert_trace_parity(g["sel"], ora["sel"], ora["gap"])
