@@ -173,6 +173,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="prefill, warm-up, then exactly one timed-step's decode and exit (for ncu launch lists)")
+    ap.add_argument("--profile-layers", type=int, default=0,
+                    help="with --profile: the same OLMoE-1B-7B width cut to this many layers (small ncu captures)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":
@@ -206,10 +208,13 @@ def main() -> None:
 
     L = lib()
     assert L.nh_set_device(local_rank) == 0
+    spec = synth.OLMOE_1B7B
+    if args.profile and args.profile_layers > 0:
+        spec = synth.replace(spec, n_layers=args.profile_layers)
     if rank == 0:
-        path = str(synth.cached(synth.OLMOE_1B7B))
+        path = str(synth.cached(spec))
     barrier()
-    path = str(synth.cached(synth.OLMOE_1B7B))
+    path = str(synth.cached(spec))
     m = nh.OlmoeModel.Load(path)
     if m is None:
         raise SystemExit("model load failed")

@@ -68,7 +68,11 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
   float* qh = Vs + kAttnSplit * hd;
   float* kc = qh + hd;
   float* vc = kc + hd;
-  float* sc = vc + hd;                 // [kAttnSplit]
+  float* qn = vc + hd;                 // this head's q_norm slice
+  float* kn = qn + hd;                 // this KV head's k_norm slice
+  float* sc = kn + hd;                 // [kAttnSplit]
+  float* qfull = sc + kAttnSplit;      // [n_head*hd]
+  float* kfull = qfull + p.n_head * hd;  // [n_head_kv*hd]
   __shared__ __align__(8) uint64_t bar;
   __shared__ double red[40];
   __shared__ float s_max;
@@ -92,23 +96,31 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
       bulk_g2s(Vs + j * hd, p.v_cache + g, row, &bar);
     }
   }
+  const bool covers_cur = (p1 == n_kv);
+  // Norm weights are static: stage them before waiting.
+  copy_to_smem(qn, p.q_norm + h * hd, hd);
+  if (covers_cur) copy_to_smem(kn, p.k_norm + kh * hd, hd);
   __syncthreads();
   pdl_wait();
   pdl_trigger();
 
+  // q (and, for the CTA holding the current position, k and v) as one batch
+  // of vector loads into shared memory.
+  copy_to_smem(qfull, p.q, dq);
+  if (covers_cur) {
+    copy_to_smem(kfull, p.k, dkv);
+    copy_to_smem(vc, p.v + kh * hd, hd);
+  }
+  __syncthreads();
   const float* cs = p.rope_cs + static_cast<int64_t>(pos) * hd;
-  const float sq = block_rms_scale(p.q, dq, p.eps, red);
-  for (int i = tid; i < hd; i += blockDim.x) qh[i] = __fmul_rn(__fmul_rn(p.q[h * hd + i], sq), p.q_norm[h * hd + i]);
+  const float sq = block_rms_scale(qfull, dq, p.eps, red);
+  for (int i = tid; i < hd; i += blockDim.x) qh[i] = __fmul_rn(__fmul_rn(qfull[h * hd + i], sq), qn[i]);
   __syncthreads();
   rope_inplace(qh, hd, cs);
-  const bool covers_cur = (p1 == n_kv);
   if (covers_cur) {
     __syncthreads();
-    const float sk = block_rms_scale(p.k, dkv, p.eps, red);
-    for (int i = tid; i < hd; i += blockDim.x) {
-      kc[i] = __fmul_rn(__fmul_rn(p.k[kh * hd + i], sk), p.k_norm[kh * hd + i]);
-      vc[i] = p.v[kh * hd + i];
-    }
+    const float sk = block_rms_scale(kfull, dkv, p.eps, red);
+    for (int i = tid; i < hd; i += blockDim.x) kc[i] = __fmul_rn(__fmul_rn(kfull[kh * hd + i], sk), kn[i]);
     __syncthreads();
     rope_inplace(kc, hd, cs);
     __syncthreads();
@@ -297,7 +309,10 @@ extern "C" int nh_attention_step(const NhDecodeState* state, const float* q, con
   off = (off + 15) & ~15ll;
   p.part_acc = reinterpret_cast<float*>(sc + off);
   p.out = attn_out;
-  const size_t smem = static_cast<size_t>(2 * kAttnSplit * head_dim + 3 * head_dim + kAttnSplit) * sizeof(float);
+  const size_t smem =
+      static_cast<size_t>(2 * kAttnSplit * head_dim + 5 * head_dim + kAttnSplit + (n_head + n_head_kv) * head_dim) *
+      sizeof(float);
+  if (smem > 220 * 1024) return NH_E_ARG;
   static size_t configured = 48 * 1024;
   if (!ensure_smem(attention_kernel, smem, configured)) return NH_E_CUDA;
   return launch_pdl(attention_kernel, dim3(n_head, p.n_split), dim3(kAttnThreads), smem,

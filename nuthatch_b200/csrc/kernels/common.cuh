@@ -104,27 +104,31 @@ __device__ __forceinline__ const uint8_t* stage_bytes_warp(uint8_t* dst, const u
 }
 
 // ------------------------------------------------------------ activation (smem)
-// One activation row in shared memory: optional f32 values (for F32 weights)
-// and, for quantised weights, its Q8_K form (rotated int8 quants, per-256
-// scale, per-16 sums).
+// One activation row in shared memory: its f32 values (the staged input, then
+// the normalised row), the staged RMSNorm weight, and, for quantised weights,
+// its Q8_K form (rotated int8 quants, per-256 scale, per-16 sums).
 struct ActSmem {
   float* xf;       // [K] or nullptr
+  float* wf;       // [K] or nullptr
   int8_t* qs;      // [K] rotated
   float* d;        // [K/256]
   int16_t* bsums;  // [K/16]
   int K;
 };
 
-__host__ __device__ inline size_t act_smem_bytes(int K, bool need_xf) {
-  return (need_xf ? static_cast<size_t>(K) * 4 : 0) + K + (K / QK + 1) * 4 + (K / 16 + 1) * 2 + 64;
+__host__ __device__ inline size_t act_smem_bytes(int K, bool need_xf, bool need_wf = false) {
+  return (need_xf ? static_cast<size_t>(K) * 4 + 16 : 0) + (need_wf ? static_cast<size_t>(K) * 4 + 16 : 0) + K +
+         (K / QK + 1) * 4 + (K / 16 + 1) * 2 + 64;
 }
 
-__device__ inline ActSmem carve_act(uint8_t* base, int K, bool need_xf) {
+__device__ inline ActSmem carve_act(uint8_t* base, int K, bool need_xf, bool need_wf = false) {
   ActSmem a;
   a.K = K;
   uintptr_t p = reinterpret_cast<uintptr_t>(base);
   a.xf = need_xf ? reinterpret_cast<float*>(p) : nullptr;
-  if (need_xf) p += static_cast<size_t>(K) * 4;
+  if (need_xf) p = (p + static_cast<size_t>(K) * 4 + 15) & ~static_cast<uintptr_t>(15);
+  a.wf = need_wf ? reinterpret_cast<float*>(p) : nullptr;
+  if (need_wf) p = (p + static_cast<size_t>(K) * 4 + 15) & ~static_cast<uintptr_t>(15);
   a.qs = reinterpret_cast<int8_t*>(p);
   p += K;
   p = (p + 15) & ~static_cast<uintptr_t>(15);
@@ -135,14 +139,44 @@ __device__ inline ActSmem carve_act(uint8_t* base, int K, bool need_xf) {
   return a;
 }
 
-// Block-wide RMS scale of src[0..K) with ggml_rms_norm semantics (sum of
-// squares in double, mean rounded to f32, 1/sqrtf(mean + eps)).  `red` holds
-// >= 33 doubles.  Ends synchronised.
-__device__ inline float block_rms_scale(const float* __restrict__ src, int K, float eps, double* red) {
+// Block-wide copy of n floats from global to shared memory.  Each thread
+// issues all its (up to 8) 16-byte loads before its first store, so the row
+// arrives in one memory latency instead of one per loop trip.  Falls back to
+// scalar loads when src or dst is not 16-byte aligned or n is not a multiple
+// of 4.  Does not synchronise.
+__device__ inline void copy_to_smem(float* dst, const float* __restrict__ src, int n) {
+  const int tid = threadIdx.x, nt = blockDim.x;
+  if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) != 0 || (n & 3) != 0) {
+    for (int i = tid; i < n; i += nt) dst[i] = src[i];
+    return;
+  }
+  constexpr int U = 8;
+  const float4* s4 = reinterpret_cast<const float4*>(src);
+  float4* d4 = reinterpret_cast<float4*>(dst);
+  const int n4 = n >> 2;
+  for (int base = tid; base < n4; base += U * nt) {
+    float4 buf[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = base + u * nt;
+      if (i < n4) buf[u] = s4[i];
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = base + u * nt;
+      if (i < n4) d4[i] = buf[u];
+    }
+  }
+}
+
+// Block-wide RMS scale of the shared row x[0..K) with ggml_rms_norm semantics
+// (sum of squares in double, mean rounded to f32, 1/sqrtf(mean + eps)).
+// `red` holds >= 33 doubles.  Ends synchronised.
+__device__ inline float block_rms_scale(const float* x, int K, float eps, double* red) {
   const int tid = threadIdx.x, nt = blockDim.x;
   double s = 0.0;
   for (int i = tid; i < K; i += nt) {
-    const float v = src[i];
+    const float v = x[i];
     s += static_cast<double>(__fmul_rn(v, v));
   }
   s = warp_sum_d(s);
@@ -206,31 +240,38 @@ __device__ __forceinline__ void quantize_block_warp(const float (&v)[8], int b, 
   if (lane == 0) a.d[b] = dq;
 }
 
-// Block-wide: the activation x = src (optionally RMS-normalised and
-// multiplied by norm_w, ggml_rms_norm + ggml_mul: y = (x*scale)*w), written as
-// f32 into xf (when allocated) and Q8_K-quantised when `quant`.  Ends
-// synchronised.
-__device__ inline void prep_act(ActSmem& a, const float* __restrict__ src, const float* __restrict__ norm_w,
-                                bool do_norm, float eps, bool quant, double* red) {
+// Stages the RMSNorm weight of an activation (static model data, so callers
+// issue it before griddepcontrol.wait).  Does not synchronise; prep_act's
+// first barrier orders it before use.
+__device__ inline void act_load_norm(ActSmem& a, const float* __restrict__ norm_w) {
+  if (a.wf != nullptr && norm_w != nullptr) copy_to_smem(a.wf, norm_w, a.K);
+}
+
+// Block-wide: the activation x = src (optionally RMS-normalised and, when
+// has_norm_w, multiplied by the weight staged by act_load_norm: ggml_rms_norm
+// + ggml_mul, y = (x*scale)*w), left as f32 in xf and Q8_K-quantised when
+// `quant`.  Needs xf.  Ends synchronised.
+__device__ inline void prep_act(ActSmem& a, const float* __restrict__ src, bool has_norm_w, bool do_norm,
+                                float eps, bool quant, double* red) {
   const int K = a.K;
-  const float scale = do_norm ? block_rms_scale(src, K, eps, red) : 1.f;
-  auto val = [&](int i) {
-    float v = src[i];
-    if (do_norm) {
-      v = __fmul_rn(v, scale);
-      if (norm_w != nullptr) v = __fmul_rn(v, norm_w[i]);
+  copy_to_smem(a.xf, src, K);
+  __syncthreads();
+  if (do_norm) {
+    const float scale = block_rms_scale(a.xf, K, eps, red);
+    const bool w = has_norm_w && a.wf != nullptr;
+    for (int i = threadIdx.x; i < K; i += blockDim.x) {
+      float v = __fmul_rn(a.xf[i], scale);
+      if (w) v = __fmul_rn(v, a.wf[i]);
+      a.xf[i] = v;
     }
-    return v;
-  };
-  if (a.xf != nullptr) {
-    for (int i = threadIdx.x; i < K; i += blockDim.x) a.xf[i] = val(i);
+    __syncthreads();
   }
   if (quant) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     for (int b = warp; b < K / QK; b += nw) {
-      float v[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) v[k] = val(b * QK + lane * 8 + k);
+      const float4 v0 = *reinterpret_cast<const float4*>(a.xf + b * QK + lane * 8);
+      const float4 v1 = *reinterpret_cast<const float4*>(a.xf + b * QK + lane * 8 + 4);
+      const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
       quantize_block_warp(v, b, a, lane);
     }
   }

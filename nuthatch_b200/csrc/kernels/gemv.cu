@@ -43,7 +43,7 @@ struct GemvArgs {
   float eps;
   int do_norm;
   int quant;
-  int need_xf;
+  int need_wf;  // stage norm_w in shared memory
   // lm_head argmax mode
   int argmax;
   NhDecodeState* state;
@@ -66,8 +66,8 @@ template <int CPL>
 __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const GemvArgs p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  ActSmem a = carve_act(smem, p.K, p.need_xf != 0);
-  const size_t act_bytes = (act_smem_bytes(p.K, p.need_xf != 0) + 15) & ~static_cast<size_t>(15);
+  ActSmem a = carve_act(smem, p.K, true, p.need_wf != 0);
+  const size_t act_bytes = (act_smem_bytes(p.K, true, p.need_wf != 0) + 15) & ~static_cast<size_t>(15);
   double* red = reinterpret_cast<double*>(smem + act_bytes);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + act_bytes + 48 * sizeof(double));
   uint8_t* stage = smem + act_bytes + 48 * sizeof(double) + kGemvWarps * p.S * sizeof(uint64_t);
@@ -111,6 +111,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const GemvArgs p)
       const int j = gw + st * tw;
       if (j < p.jobs_total) issue(j, st);
     }
+    act_load_norm(a, p.norm_w);
   }
   pdl_wait();
   pdl_trigger();
@@ -119,7 +120,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const GemvArgs p)
   int best_i = INT_MAX;
   bool failed = false;
   if (!skip) {
-    prep_act(a, p.x, p.norm_w, p.do_norm != 0, p.eps, p.quant != 0, red);
+    prep_act(a, p.x, p.norm_w != nullptr, p.do_norm != 0, p.eps, p.quant != 0, red);
     const int jl = lane % p.lpr, kr = lane / p.lpr;
     ActReg<CPL> ar;
     if (p.quant) load_act<CPL>(ar, a, 0, jl, p.lpr);
@@ -222,21 +223,19 @@ int gemv_launch_t(GemvArgs& p, size_t smem, int grid, cudaStream_t stream) {
 // Fills the work split of a GemvArgs whose segments, K and activation source are set.
 int gemv_launch(GemvArgs& p, cudaStream_t stream) {
   if (p.K <= 0 || p.K > kMaxK) return NH_E_ARG;
-  bool any_q = false, any_f = false;
+  bool any_q = false;
   uint64_t rb_max = 0;
   for (int s = 0; s < p.nseg; ++s) {
     if (!valid_type(p.seg[s].type) || p.seg[s].w == nullptr || p.seg[s].rows < 0) return NH_E_ARG;
     if (p.seg[s].type != NH_TYPE_F32) {
       if (!rowdot_k_ok(p.K)) return NH_E_ARG;
       any_q = true;
-    } else {
-      any_f = true;
     }
     p.seg[s].rb = row_bytes(p.seg[s].type, p.K);
     rb_max = rb_max > p.seg[s].rb ? rb_max : p.seg[s].rb;
   }
   p.quant = any_q ? 1 : 0;
-  p.need_xf = any_f ? 1 : 0;
+  p.need_wf = (p.do_norm != 0 && p.norm_w != nullptr) ? 1 : 0;
   p.lpr = any_q ? rowdot_lpr(p.K) : 32;
   p.rpp = 32 / p.lpr;
   int total = 0;
@@ -250,7 +249,7 @@ int gemv_launch(GemvArgs& p, cudaStream_t stream) {
   p.stage_bytes = any_q ? static_cast<uint32_t>((rb_max * p.rpp + 32 + 127) & ~127ull) : 128u;
   p.S = kGemvMaxStages;
   while (p.S > 2 && static_cast<size_t>(kGemvWarps) * p.S * p.stage_bytes > 96 * 1024) --p.S;
-  const size_t smem = ((act_smem_bytes(p.K, any_f) + 15) & ~static_cast<size_t>(15)) + 48 * sizeof(double) +
+  const size_t smem = ((act_smem_bytes(p.K, true, p.need_wf != 0) + 15) & ~static_cast<size_t>(15)) + 48 * sizeof(double) +
                       kGemvWarps * p.S * sizeof(uint64_t) +
                       static_cast<size_t>(kGemvWarps) * p.S * p.stage_bytes;
   const int per_sm = static_cast<int>(std::min<size_t>(4, (220 * 1024) / (smem + 1024)));

@@ -49,7 +49,17 @@ __global__ void embed_kernel(const NhDecodeState* state, const int32_t* prompt, 
     s_tok = tok;
   }
   __syncthreads();
-  const uint8_t* row = table + static_cast<uint64_t>(s_tok) * rb;
+  // Stage the row with 16-byte loads from its 16-byte-rounded start (weight
+  // regions carry tail padding), then dequantise from shared memory.
+  extern __shared__ __align__(16) uint8_t row_s[];
+  const uintptr_t a = reinterpret_cast<uintptr_t>(table + static_cast<uint64_t>(s_tok) * rb);
+  const uintptr_t al = a & ~static_cast<uintptr_t>(15);
+  const int off = static_cast<int>(a - al);
+  const int n16 = static_cast<int>((off + rb + 15) >> 4);
+  const uint4* g = reinterpret_cast<const uint4*>(al);
+  for (int k = threadIdx.x; k < n16; k += blockDim.x) reinterpret_cast<uint4*>(row_s)[k] = g[k];
+  __syncthreads();
+  const uint8_t* row = row_s + off;
   for (int64_t i = threadIdx.x; i < n_embd; i += blockDim.x) h[i] = dequant_elem(row, type, i);
 }
 
@@ -64,10 +74,10 @@ __global__ void dequant_kernel(const uint8_t* w, int type, int64_t n, int64_t ro
 
 // One CTA per 256-value block: prep_act's quantiser over a one-block row.
 __global__ void quantize_kernel(const float* x, int64_t n, uint8_t* out) {
-  __shared__ __align__(16) uint8_t smem[2048];
+  __shared__ __align__(16) uint8_t smem[4096];
   __shared__ double red[48];
-  ActSmem a = carve_act(smem, QK, false);
-  prep_act(a, x + static_cast<int64_t>(blockIdx.x) * QK, nullptr, false, 0.f, true, red);
+  ActSmem a = carve_act(smem, QK, true);
+  prep_act(a, x + static_cast<int64_t>(blockIdx.x) * QK, false, false, 0.f, true, red);
   uint8_t* blk = out + static_cast<int64_t>(blockIdx.x) * 292;
   if (threadIdx.x == 0) *reinterpret_cast<float*>(blk) = a.d[0];
   for (int i = threadIdx.x; i < QK; i += blockDim.x) blk[4 + i] = static_cast<uint8_t>(a.qs[q8_off(0, i)]);
@@ -100,7 +110,10 @@ extern "C" int nh_embed_step(const NhDecodeState* state, const int32_t* prompt_i
   if (state == nullptr || prompt_ids == nullptr || table == nullptr || h_out == nullptr) return NH_E_ARG;
   if (type != NH_TYPE_F32 && type != NH_TYPE_Q4_K && type != NH_TYPE_Q6_K) return NH_E_TYPE;
   if (type != NH_TYPE_F32 && n_embd % QK != 0) return NH_E_ARG;
-  return launch_pdl(embed_kernel, dim3(1), dim3(256), 0, static_cast<cudaStream_t>(stream), state, prompt_ids,
+  const size_t smem = row_bytes(type, n_embd) + 32;
+  static size_t configured = 48 * 1024;
+  if (smem > 220 * 1024 || !ensure_smem(embed_kernel, smem, configured)) return NH_E_ARG;
+  return launch_pdl(embed_kernel, dim3(1), dim3(256), smem, static_cast<cudaStream_t>(stream), state, prompt_ids,
                     static_cast<const uint8_t*>(table), static_cast<int>(type), n_embd, n_vocab,
                     static_cast<uint64_t>(row_bytes(type, n_embd)), h_out);
 }

@@ -42,7 +42,7 @@ constexpr int kRouterMaxVec = kMaxK / 128;
 
 __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(const RouterArgs p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  ActSmem a = carve_act(smem, p.K, true);
+  ActSmem a = carve_act(smem, p.K, true, true);
   __shared__ double red[48];
   __shared__ bool s_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -57,9 +57,10 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(const RouterA
     for (int t = 0; t < kRouterMaxVec; ++t)
       if (t < p.K / 128) wv[t] = w4[lane + 32 * t];
   }
+  act_load_norm(a, p.norm);
   pdl_wait();
   pdl_trigger();
-  prep_act(a, p.h, p.norm, true, p.eps, false, red);
+  prep_act(a, p.h, p.norm != nullptr, true, p.eps, false, red);
   if (e < p.E) {
     float v;
     if (vec) {
@@ -202,8 +203,8 @@ __global__ void __launch_bounds__(kMoeWarps * 32) gate_up_kernel(const GateUpArg
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool quant = p.tg != NH_TYPE_F32;
-  ActSmem a = carve_act(smem, p.K, !quant);
-  const size_t act_bytes = (act_smem_bytes(p.K, !quant) + 15) & ~static_cast<size_t>(15);
+  ActSmem a = carve_act(smem, p.K, true, true);
+  const size_t act_bytes = (act_smem_bytes(p.K, true, true) + 15) & ~static_cast<size_t>(15);
   double* red = reinterpret_cast<double*>(smem + act_bytes);
   float* ybuf = reinterpret_cast<float*>(smem + act_bytes + 48 * sizeof(double));  // [warps][64]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + act_bytes + 48 * sizeof(double) + kMoeWarps * 64 * sizeof(float));
@@ -217,6 +218,7 @@ __global__ void __launch_bounds__(kMoeWarps * 32) gate_up_kernel(const GateUpArg
     fence_barrier_init();
   }
   __syncwarp();
+  act_load_norm(a, p.norm);
   pdl_wait();
   pdl_trigger();
 
@@ -251,7 +253,7 @@ __global__ void __launch_bounds__(kMoeWarps * 32) gate_up_kernel(const GateUpArg
     const uint64_t end = blockIdx.x + 1 == gridDim.x ? p.down_nb2 : ((per * (blockIdx.x + 1)) & ~static_cast<uint64_t>(15));
     if (end > beg) prefetch_l2(p.down + e * p.down_nb2 + beg, static_cast<uint32_t>(end - beg));
   }
-  prep_act(a, p.h, p.norm, true, p.eps, quant, red);
+  prep_act(a, p.h, p.norm != nullptr, true, p.eps, quant, red);
   const int jl = lane % p.lpr, kr = lane / p.lpr;
   ActReg<CPL> ar;
   if (quant) load_act<CPL>(ar, a, 0, jl, p.lpr);
@@ -362,13 +364,37 @@ __global__ void __launch_bounds__(kMoeWarps * 32) down_kernel(const DownArgs p) 
     const int j = gw + st * tw;
     if (j < p.jobs_total) issue(j, st);
   }
-  // The activation: each expert's ff row, Q8_K-quantised per 256-block.
+  // The activation: each expert's ff row, Q8_K-quantised per 256-block.  A
+  // warp issues the loads of up to kU blocks before quantising any of them.
   if (quant) {
-    for (int b = warp; b < KF / QK; b += kMoeWarps) {
-      float v[8];
+    constexpr int kU = 8;
+    const int nb = KF / QK;
+    const bool al = (reinterpret_cast<uintptr_t>(p.ff) & 15) == 0;
+    for (int b0 = warp; b0 < nb; b0 += kU * kMoeWarps) {
+      float4 buf[kU][2];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) v[k] = p.ff[b * QK + lane * 8 + k];
-      quantize_block_warp(v, b, a, lane);
+      for (int u = 0; u < kU; ++u) {
+        const int b = b0 + u * kMoeWarps;
+        if (b < nb) {
+          const float* src = p.ff + b * QK + lane * 8;
+          if (al) {
+            buf[u][0] = *reinterpret_cast<const float4*>(src);
+            buf[u][1] = *reinterpret_cast<const float4*>(src + 4);
+          } else {
+            buf[u][0] = make_float4(src[0], src[1], src[2], src[3]);
+            buf[u][1] = make_float4(src[4], src[5], src[6], src[7]);
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int b = b0 + u * kMoeWarps;
+        if (b < nb) {
+          const float v[8] = {buf[u][0].x, buf[u][0].y, buf[u][0].z, buf[u][0].w,
+                              buf[u][1].x, buf[u][1].y, buf[u][1].z, buf[u][1].w};
+          quantize_block_warp(v, b, a, lane);
+        }
+      }
     }
   } else {
     for (int i = threadIdx.x; i < KF; i += blockDim.x) a.xf[i] = p.ff[i];
@@ -459,7 +485,7 @@ extern "C" int nh_router_topk(const NhDecodeState* state, const float* h, const 
   p.trace_gap = trace_gap;
   p.ticket = static_cast<unsigned*>(scratch);
   p.logits = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + 64);
-  const size_t smem = act_smem_bytes(p.K, true);
+  const size_t smem = act_smem_bytes(p.K, true, true);
   static size_t configured = 48 * 1024;
   if (!ensure_smem(router_kernel, smem, configured)) return NH_E_CUDA;
   const int grid = (n_expert + kRouterWarps - 1) / kRouterWarps;
@@ -549,10 +575,10 @@ extern "C" int nh_moe_gate_up(NhDecodeState* state, const float* h, const float*
   p.jobs_per_expert = (p.F + p.R - 1) / p.R;
   p.jobs_total = p.jobs_per_expert * k;
   p.ff = ff;
-  p.S = pick_stages(((act_smem_bytes(p.K, !quant) + 15) & ~static_cast<size_t>(15)) + 48 * sizeof(double) +
+  p.S = pick_stages(((act_smem_bytes(p.K, true, true) + 15) & ~static_cast<size_t>(15)) + 48 * sizeof(double) +
                         kMoeWarps * 64 * sizeof(float),
                     p.stage_bytes);
-  const size_t smem = ((act_smem_bytes(p.K, !quant) + 15) & ~static_cast<size_t>(15)) + 48 * sizeof(double) +
+  const size_t smem = ((act_smem_bytes(p.K, true, true) + 15) & ~static_cast<size_t>(15)) + 48 * sizeof(double) +
                       kMoeWarps * 64 * sizeof(float) + kMoeWarps * p.S * sizeof(uint64_t) +
                       static_cast<size_t>(kMoeWarps) * p.S * p.stage_bytes;
   const int grid = grid_for(p.jobs_total, smem);
