@@ -98,6 +98,33 @@ int nh_attention_step(const NhDecodeState* state, const float* q, const float* k
                       float kq_scale, float* k_cache, float* v_cache, int max_seq,
                       void* scratch, float* attn_out, void* stream);
 
+/* No counterpart in the reference.  nh_attention_step without the caller's
+ * scratch buffer, for callers that cannot allocate device memory: code that
+ * runs inside an allocator hook or memory-pool callback (calling the
+ * allocator there would re-enter it), plugin hosts that own every device
+ * allocation, and processes whose allocator is already at its limit.  The
+ * split-combine scratch is a static device array of
+ * NH_ATTN_STATIC_SCRATCH_BYTES that each GPU loading the library holds until
+ * the process exits; nothing is allocated per call.  Same arguments and
+ * results as nh_attention_step minus `scratch`.
+ *   - Returns NH_E_CAPACITY, launching nothing, when
+ *     nh_attention_scratch_bytes(n_head, head_dim, max_seq) exceeds
+ *     NH_ATTN_STATIC_SCRATCH_BYTES or n_head > 64 (for head_dim 128 and 16
+ *     heads that allows max_seq up to 7,936).
+ *   - The first call on a device looks up the array's device address (with
+ *     that device current); make that first call before any stream capture.
+ *   - Every call clears the array's split counters on `stream`, then runs the
+ *     step there.  All calls on a device share its one array and it keeps the
+ *     last call's contents: calls that can overlap on the GPU (issued to
+ *     streams with no ordering between them) race on it, so the caller must
+ *     serialise them. */
+#define NH_ATTN_STATIC_SCRATCH_BYTES (1 << 20)
+int nh_attention_step_static(const NhDecodeState* state, const float* q, const float* k,
+                             const float* v, const float* q_norm, const float* k_norm, float eps,
+                             int n_head, int n_head_kv, int head_dim, const float* rope_cs,
+                             float kq_scale, float* k_cache, float* v_cache, int max_seq,
+                             float* attn_out, void* stream);
+
 /* Host helper: fills rope_cs_host[max_seq][head_dim/2][2] (see above). */
 void nh_rope_table(float base, int head_dim, int max_seq, float* rope_cs_host);
 

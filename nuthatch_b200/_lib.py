@@ -76,6 +76,8 @@ SIGNATURES = {
     "nh_qkv_proj": (C.c_int, [vp, vp, vp, f32, vp, i32, vp, i32, vp, i32, i64, i64, vp, vp, vp, vp]),
     "nh_attention_step": (C.c_int, [vp, vp, vp, vp, vp, vp, f32, C.c_int, C.c_int, C.c_int, vp, f32, vp, vp,
                                     C.c_int, vp, vp, vp]),
+    "nh_attention_step_static": (C.c_int, [vp, vp, vp, vp, vp, vp, f32, C.c_int, C.c_int, C.c_int, vp, f32, vp,
+                                           vp, C.c_int, vp, vp]),
     "nh_out_proj_residual": (C.c_int, [vp, vp, vp, i32, i64, vp, vp]),
     "nh_router_topk": (C.c_int, [vp, vp, vp, f32, vp, i64, C.c_int, C.c_int, C.c_int, vp, vp, vp, vp, C.c_int,
                                  C.c_int, vp, vp]),

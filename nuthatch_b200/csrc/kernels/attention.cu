@@ -13,6 +13,7 @@
 // triples are combined by the last CTA of each head in split order, so the
 // result does not depend on CTA scheduling.
 #include <cmath>
+#include <mutex>
 
 #include "launch.cuh"
 #include "rowdot.cuh"
@@ -317,4 +318,57 @@ extern "C" int nh_attention_step(const NhDecodeState* state, const float* q, con
   if (!ensure_smem(attention_kernel, smem, configured)) return NH_E_CUDA;
   return launch_pdl(attention_kernel, dim3(n_head, p.n_split), dim3(kAttnThreads), smem,
                     static_cast<cudaStream_t>(stream), p);
+}
+
+// ---------------------------------------------------------------- no-alloc form
+// nh_attention_step_static: the same attention step for callers that cannot
+// allocate device memory themselves (code running inside a host-side
+// allocator hook or a memory-pool callback, plugin hosts that own all device
+// allocations, or a process whose allocator is already at its limit), so they
+// cannot provide the split-combine scratch.  Its scratch is a file-scope
+// device array of NH_ATTN_STATIC_SCRATCH_BYTES, which every GPU that loads
+// this library holds until the process exits.
+//
+// In host code `g_attn_static_scratch` names a host-side stand-in, not device
+// memory; the device address comes from cudaGetSymbolAddress, looked up once
+// per device (with that device current) on the first call made there and kept.
+namespace {
+
+__device__ __align__(256) uint8_t g_attn_static_scratch[NH_ATTN_STATIC_SCRATCH_BYTES];
+
+constexpr int kStaticMaxDevices = 64;
+std::mutex g_static_mu;
+void* g_static_addr[kStaticMaxDevices] = {};
+
+// Device address of the array on the current device, or nullptr.
+void* static_scratch_address() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kStaticMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (g_static_addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_attn_static_scratch) != cudaSuccess) return nullptr;
+    g_static_addr[dev] = p;
+  }
+  return g_static_addr[dev];
+}
+
+}  // namespace
+
+extern "C" int nh_attention_step_static(const NhDecodeState* state, const float* q, const float* k, const float* v,
+                                        const float* q_norm, const float* k_norm, float eps, int n_head,
+                                        int n_head_kv, int head_dim, const float* rope_cs, float kq_scale,
+                                        float* k_cache, float* v_cache, int max_seq, float* attn_out,
+                                        void* stream) {
+  if (n_head <= 0 || n_head_kv <= 0 || head_dim <= 0 || max_seq <= 0) return NH_E_ARG;
+  // The per-head split counters occupy the first 256 bytes: 4 bytes per head.
+  if (n_head > 64) return NH_E_CAPACITY;
+  if (nh_attention_scratch_bytes(n_head, head_dim, max_seq) > NH_ATTN_STATIC_SCRATCH_BYTES) return NH_E_CAPACITY;
+  void* scratch = static_scratch_address();
+  if (scratch == nullptr) return NH_E_CUDA;
+  // The array keeps whatever the previous call left; the counters must start
+  // at zero (the split partials are always written before they are read).
+  if (cudaMemsetAsync(scratch, 0, 256, static_cast<cudaStream_t>(stream)) != cudaSuccess) return NH_E_CUDA;
+  return nh_attention_step(state, q, k, v, q_norm, k_norm, eps, n_head, n_head_kv, head_dim, rope_cs, kq_scale,
+                           k_cache, v_cache, max_seq, scratch, attn_out, stream);
 }
