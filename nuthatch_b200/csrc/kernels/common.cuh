@@ -197,28 +197,24 @@ __device__ inline float block_rms_scale(const float* x, int K, float eps, double
 // -127 (iscale = -127/max, d = 1/iscale), round half to even, clamp at +127,
 // 16 partial sums.  Writes block b of the activation (rotated layout).
 __device__ __forceinline__ void quantize_block_warp(const float (&v)[8], int b, ActSmem& a, int lane) {
-  float amax = 0.f, mx = 0.f;
-  int idx = 1 << 30;
+  // Largest magnitude over the block, then the first element (lowest index:
+  // lowest lane, then lowest k) that has it; mx is that element's value.
+  float amax = 0.f;
 #pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const float ax = fabsf(v[k]);
-    if (ax > amax) {
-      amax = ax;
-      mx = v[k];
-      idx = lane * 8 + k;
+  for (int k = 0; k < 8; ++k) amax = fmaxf(amax, fabsf(v[k]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  float cand = 0.f;
+  bool has = false;
+#pragma unroll
+  for (int k = 7; k >= 0; --k) {
+    if (fabsf(v[k]) == amax) {
+      cand = v[k];
+      has = true;
     }
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float oa = __shfl_xor_sync(0xffffffffu, amax, o);
-    const float om = __shfl_xor_sync(0xffffffffu, mx, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-    if (oa > amax || (oa == amax && oi < idx)) {
-      amax = oa;
-      mx = om;
-      idx = oi;
-    }
-  }
+  const unsigned who = __ballot_sync(0xffffffffu, has);
+  const float mx = __shfl_sync(0xffffffffu, cand, who != 0u ? __ffs(who) - 1 : 0);
   uint32_t w0 = 0, w1 = 0;
   int part = 0;
   float dq = 0.f;
@@ -254,25 +250,50 @@ __device__ inline void act_load_norm(ActSmem& a, const float* __restrict__ norm_
 __device__ inline void prep_act(ActSmem& a, const float* __restrict__ src, bool has_norm_w, bool do_norm,
                                 float eps, bool quant, double* red) {
   const int K = a.K;
+  const int tid = threadIdx.x, nt = blockDim.x, warp = tid >> 5, lane = tid & 31, nw = nt >> 5;
   copy_to_smem(a.xf, src, K);
   __syncthreads();
+  float scale = 1.f;
   if (do_norm) {
-    const float scale = block_rms_scale(a.xf, K, eps, red);
-    const bool w = has_norm_w && a.wf != nullptr;
-    for (int i = threadIdx.x; i < K; i += blockDim.x) {
+    // Sum of squares in double: per thread, per warp (butterfly), then the
+    // warp partials in warp order by every thread.
+    double s = 0.0;
+    for (int i = tid; i < K; i += nt) {
+      const float v = a.xf[i];
+      s += static_cast<double>(__fmul_rn(v, v));
+    }
+    s = warp_sum_d(s);
+    if (lane == 0) red[warp] = s;
+    __syncthreads();
+    double t = 0.0;
+    for (int w = 0; w < nw; ++w) t += red[w];
+    const float mean = static_cast<float>(t / static_cast<double>(K));
+    scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+  }
+  const bool w = do_norm && has_norm_w && a.wf != nullptr;
+  if (quant) {
+    // Each warp normalises its own 256-value blocks and quantises them.
+    for (int b = warp; b < K / QK; b += nw) {
+      float* xb = a.xf + b * QK + lane * 8;
+      const float4 v0 = *reinterpret_cast<const float4*>(xb);
+      const float4 v1 = *reinterpret_cast<const float4*>(xb + 4);
+      float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+      if (do_norm) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          v[k] = __fmul_rn(v[k], scale);
+          if (w) v[k] = __fmul_rn(v[k], a.wf[b * QK + lane * 8 + k]);
+        }
+        *reinterpret_cast<float4*>(xb) = make_float4(v[0], v[1], v[2], v[3]);
+        *reinterpret_cast<float4*>(xb + 4) = make_float4(v[4], v[5], v[6], v[7]);
+      }
+      quantize_block_warp(v, b, a, lane);
+    }
+  } else if (do_norm) {
+    for (int i = tid; i < K; i += nt) {
       float v = __fmul_rn(a.xf[i], scale);
       if (w) v = __fmul_rn(v, a.wf[i]);
       a.xf[i] = v;
-    }
-    __syncthreads();
-  }
-  if (quant) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    for (int b = warp; b < K / QK; b += nw) {
-      const float4 v0 = *reinterpret_cast<const float4*>(a.xf + b * QK + lane * 8);
-      const float4 v1 = *reinterpret_cast<const float4*>(a.xf + b * QK + lane * 8 + 4);
-      const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-      quantize_block_warp(v, b, a, lane);
     }
   }
   __syncthreads();

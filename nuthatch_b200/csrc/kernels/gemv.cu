@@ -11,7 +11,7 @@
 #include <cstring>
 
 #include "launch.cuh"
-#include "rowdot.cuh"
+#include "rowdot3.cuh"
 
 namespace nh {
 
@@ -209,6 +209,144 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const GemvArgs p)
   *p.ticket = 0u;
 }
 
+// Lane-per-super-block form (K <= 2048, every segment quantised): a job is
+// P = 32/G rows of one segment, all computed in one warp pass.
+__global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv3_kernel(const GemvArgs p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  ActSmem a = carve_act(smem, p.K, true, p.need_wf != 0);
+  const size_t act_bytes = (act_smem_bytes(p.K, true, p.need_wf != 0) + 15) & ~static_cast<size_t>(15);
+  double* red = reinterpret_cast<double*>(smem + act_bytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + act_bytes + 48 * sizeof(double));
+  uint8_t* stage = smem + act_bytes + 48 * sizeof(double) + kGemvWarps * p.S * sizeof(uint64_t);
+  __shared__ float s_bv[32];
+  __shared__ int s_bi[32];
+  __shared__ bool s_last;
+
+  int pos = 0, n_prompt = 0;
+  bool skip = false;
+  if (p.argmax) {
+    pos = *reinterpret_cast<volatile const int*>(&p.state->pos);
+    n_prompt = *reinterpret_cast<volatile const int*>(&p.state->n_prompt);
+    skip = pos < n_prompt - 1;
+  }
+  const int gw = blockIdx.x * kGemvWarps + warp;
+  const int tw = gridDim.x * kGemvWarps;
+  const int G = p.lpr, P = p.rpp;
+  uint64_t* wbar = bars + warp * p.S;
+  uint8_t* wb = stage + static_cast<size_t>(warp) * p.S * p.stage_bytes;
+  if (lane == 0) {
+    for (int s = 0; s < p.S; ++s) mbar_init(&wbar[s], 1);
+    fence_barrier_init();
+  }
+  __syncwarp();
+  auto job = [&](int j, int& s, int& row0, int& nrows) {
+    s = 0;
+    while (s + 1 < p.nseg && j >= p.jobs_start[s + 1]) ++s;
+    row0 = (j - p.jobs_start[s]) * P;
+    nrows = min(P, p.seg[s].rows - row0);
+  };
+  auto issue = [&](int j, int st) {
+    if (lane != 0) return;
+    int s, row0, nrows;
+    job(j, s, row0, nrows);
+    uint32_t len, off;
+    const uint8_t* src = span16(p.seg[s].w + static_cast<uint64_t>(row0) * p.seg[s].rb,
+                                static_cast<size_t>(nrows) * p.seg[s].rb, &len, &off);
+    mbar_expect_tx(&wbar[st], len);
+    bulk_g2s(wb + static_cast<size_t>(st) * p.stage_bytes, src, len, &wbar[st]);
+  };
+  if (!skip) {
+    for (int st = 0; st < p.S; ++st) {
+      const int j = gw + st * tw;
+      if (j < p.jobs_total) issue(j, st);
+    }
+    act_load_norm(a, p.norm_w);
+  }
+  pdl_wait();
+  pdl_trigger();
+
+  float best_v = -INFINITY;
+  int best_i = INT_MAX;
+  bool failed = false;
+  if (!skip) {
+    prep_act(a, p.x, p.norm_w != nullptr, p.do_norm != 0, p.eps, true, red);
+    const int g = lane % G, r = lane / G;
+    Act3 act;
+    load_act3(act, a, g);
+    for (int it = 0;; ++it) {
+      const int j = gw + it * tw;
+      if (j >= p.jobs_total) break;
+      const int st = it % p.S;
+      int s, row0, nrows;
+      job(j, s, row0, nrows);
+      const GemvSeg& sg = p.seg[s];
+      if (!mbar_wait(&wbar[st], (it / p.S) & 1)) {
+        failed = true;
+        break;
+      }
+      const uint32_t off =
+          static_cast<uint32_t>(reinterpret_cast<uintptr_t>(sg.w + static_cast<uint64_t>(row0) * sg.rb) & 15);
+      const uint8_t* rowp = wb + static_cast<size_t>(st) * p.stage_bytes + off + static_cast<size_t>(r) * sg.rb;
+      float v = row_dot3(rowp, sg.type, g, G, act);
+      const int row = row0 + r;
+      if (g == 0 && r < nrows) {
+        if (sg.resid != nullptr) v = __fadd_rn(sg.resid[row], v);
+        if (sg.out != nullptr) sg.out[row] = v;
+        if (p.argmax) {
+          if (p.logits_dump != nullptr) p.logits_dump[static_cast<int64_t>(pos - n_prompt + 1) * sg.rows + row] = v;
+          if (argmax_better(v, row, best_v, best_i)) {
+            best_v = v;
+            best_i = row;
+          }
+        }
+      }
+      __syncwarp();
+      const int jn = gw + (it + p.S) * tw;
+      if (jn < p.jobs_total) issue(jn, st);
+    }
+  }
+  if (failed && lane == 0 && p.state != nullptr) atomicCAS(&p.state->error, 0, NH_E_TIMEOUT);
+  if (!p.argmax) return;
+
+  block_argmax(best_v, best_i, s_bv, s_bi);
+  if (threadIdx.x == 0) {
+    p.part_val[blockIdx.x] = best_v;
+    p.part_idx[blockIdx.x] = best_i;
+    __threadfence();
+    const unsigned t = atomicAdd(p.ticket, 1u);
+    s_last = (t == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  float bv = -INFINITY;
+  int bi = INT_MAX;
+  if (!skip) {
+    const volatile float* pv = p.part_val;
+    const volatile int32_t* pi = p.part_idx;
+    for (unsigned b = threadIdx.x; b < gridDim.x; b += blockDim.x) {
+      const float v = pv[b];
+      const int i = pi[b];
+      if (argmax_better(v, i, bv, bi)) {
+        bv = v;
+        bi = i;
+      }
+    }
+  }
+  block_argmax(bv, bi, s_bv, s_bi);
+  if (threadIdx.x != 0) return;
+  if (!skip) {
+    if (bi == INT_MAX) bi = 0;
+    const int n = p.state->n_out;
+    if (n < p.state->n_predict) p.out_tokens[n] = bi;
+    p.state->token = bi;
+    p.state->n_out = n + 1;
+  }
+  p.state->pos = pos + 1;
+  *p.ticket = 0u;
+}
+
 namespace {
 
 bool valid_type(int t) { return t == NH_TYPE_F32 || t == NH_TYPE_Q4_K || t == NH_TYPE_Q6_K; }
@@ -221,8 +359,60 @@ int gemv_launch_t(GemvArgs& p, size_t smem, int grid, cudaStream_t stream) {
 }
 
 // Fills the work split of a GemvArgs whose segments, K and activation source are set.
+// Resident CTAs per SM for a kernel at a dynamic shared-memory size (at most 4).
+template <typename Kern>
+int resident_ctas(Kern k, int threads, size_t smem) {
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, threads, smem) != cudaSuccess || n < 1) n = 1;
+  return n > 4 ? 4 : n;
+}
+
+// The lane-per-super-block path: every segment quantised and K <= 2048.
+int gemv3_launch(GemvArgs& p, cudaStream_t stream) {
+  uint64_t rb_max = 0;
+  for (int s = 0; s < p.nseg; ++s) {
+    p.seg[s].rb = row_bytes(p.seg[s].type, p.K);
+    rb_max = rb_max > p.seg[s].rb ? rb_max : p.seg[s].rb;
+  }
+  p.quant = 1;
+  p.need_wf = (p.do_norm != 0 && p.norm_w != nullptr) ? 1 : 0;
+  p.lpr = p.K / QK;      // G: lanes per row
+  p.rpp = 32 / p.lpr;    // P: rows per job (one warp pass)
+  int total = 0;
+  for (int s = 0; s < p.nseg; ++s) {
+    p.jobs_start[s] = total;
+    total += (p.seg[s].rows + p.rpp - 1) / p.rpp;
+  }
+  for (int s = p.nseg; s < 4; ++s) p.jobs_start[s] = total;
+  p.jobs_total = total;
+  p.stage_bytes = static_cast<uint32_t>((rb_max * p.rpp + 32 + 127) & ~127ull);
+  const size_t fixed = ((act_smem_bytes(p.K, true, p.need_wf != 0) + 15) & ~static_cast<size_t>(15)) +
+                       48 * sizeof(double);
+  p.S = kGemvMaxStages;
+  while (p.S > 1 && fixed + static_cast<size_t>(kGemvWarps) * p.S * (p.stage_bytes + 8) > 110 * 1024) --p.S;
+  const size_t smem = fixed + kGemvWarps * p.S * sizeof(uint64_t) + static_cast<size_t>(kGemvWarps) * p.S * p.stage_bytes;
+  static size_t configured = 48 * 1024;
+  if (!ensure_smem(gemv3_kernel, smem, configured)) return NH_E_CUDA;
+  const int per_sm = resident_ctas(gemv3_kernel, kGemvWarps * 32, smem);
+  int grid = (total + kGemvWarps - 1) / kGemvWarps;
+  const int cap = device_sm_count() * per_sm;
+  if (grid > cap) grid = cap;
+  if (p.argmax && grid > kMaxArgmaxBlocks) grid = kMaxArgmaxBlocks;
+  if (grid < 1) grid = 1;
+  return launch_pdl(gemv3_kernel, dim3(grid), dim3(kGemvWarps * 32), smem, stream, p);
+}
+
 int gemv_launch(GemvArgs& p, cudaStream_t stream) {
   if (p.K <= 0 || p.K > kMaxK) return NH_E_ARG;
+  {
+    bool v3 = rowdot3_k_ok(p.K) && engine_v3();
+    for (int s = 0; s < p.nseg; ++s) {
+      if (!valid_type(p.seg[s].type) || p.seg[s].w == nullptr || p.seg[s].rows < 0) return NH_E_ARG;
+      if (p.seg[s].type == NH_TYPE_F32) v3 = false;
+      if (p.seg[s].type == NH_TYPE_Q4_K && (reinterpret_cast<uintptr_t>(p.seg[s].w) & 15) != 0) return NH_E_ARG;
+    }
+    if (v3) return gemv3_launch(p, stream);
+  }
   bool any_q = false;
   uint64_t rb_max = 0;
   for (int s = 0; s < p.nseg; ++s) {

@@ -35,6 +35,18 @@ inline int pdl_enabled() {
   return v;
 }
 
+// The lane-per-super-block row-dot engine is used where it covers the shape
+// unless NH_ROWDOT=2 selects the lane-per-chunk engine everywhere (read once;
+// both give identical results).
+inline bool engine_v3() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("NH_ROWDOT");
+    v = (e != nullptr && e[0] == '2') ? 0 : 1;
+  }
+  return v != 0;
+}
+
 template <typename Kern>
 bool ensure_smem(Kern k, size_t bytes, size_t& configured) {
   if (bytes <= configured) return true;

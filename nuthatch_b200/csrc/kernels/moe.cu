@@ -11,7 +11,7 @@
 #include <climits>
 
 #include "launch.cuh"
-#include "rowdot.cuh"
+#include "rowdot3.cuh"
 
 namespace nh {
 
@@ -452,6 +452,206 @@ __global__ void __launch_bounds__(kMoeWarps * 32) down_kernel(const DownArgs p) 
   if (failed && lane == 0) atomicCAS(&p.state->error, 0, NH_E_TIMEOUT);
 }
 
+// ------------------------------------------------------------------ lane-per-super-block forms
+// gate/up: a job is P = 32/G rows of one expert; pass 1 computes the P gate
+// rows, pass 2 the P up rows, so the lane that holds a gate row's value also
+// holds the matching up row's value and writes silu(gate)*up itself.
+__global__ void __launch_bounds__(kMoeWarps * 32, 2) gate_up3_kernel(const GateUpArgs p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  ActSmem a = carve_act(smem, p.K, true, true);
+  const size_t act_bytes = (act_smem_bytes(p.K, true, true) + 15) & ~static_cast<size_t>(15);
+  double* red = reinterpret_cast<double*>(smem + act_bytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + act_bytes + 48 * sizeof(double));
+  uint8_t* stage = reinterpret_cast<uint8_t*>(bars + kMoeWarps * p.S);
+  __shared__ int s_sel[kMaxTopK];
+  const int gw = blockIdx.x * kMoeWarps + warp, tw = gridDim.x * kMoeWarps;
+  const int G = p.lpr, P = p.rpp;
+  uint64_t* wbar = bars + warp * p.S;
+  uint8_t* wb = stage + static_cast<size_t>(warp) * p.S * p.stage_bytes;
+  if (lane == 0) {
+    for (int s = 0; s < p.S; ++s) mbar_init(&wbar[s], 1);
+    fence_barrier_init();
+  }
+  act_load_norm(a, p.norm);
+  pdl_wait();
+  pdl_trigger();
+  // The selection is read once; every job then finds its expert in shared memory.
+  if (threadIdx.x < p.topk) s_sel[threadIdx.x] = p.wsel[threadIdx.x];
+  __syncthreads();
+
+  auto job_rows = [&](int j, int& i, int& e, int& r0, int& n) {
+    i = j / p.jobs_per_expert;
+    r0 = (j - i * p.jobs_per_expert) * P;
+    n = min(P, p.F - r0);
+    e = s_sel[i];
+  };
+  auto issue = [&](int j, int st) {
+    if (lane != 0) return;
+    int i, e, r0, n;
+    job_rows(j, i, e, r0, n);
+    uint32_t lg, og, lu, ou;
+    const uint8_t* sg = span16(p.gate + e * p.gate_nb2 + r0 * p.rb_g, n * p.rb_g, &lg, &og);
+    const uint8_t* su = span16(p.up + e * p.up_nb2 + r0 * p.rb_u, n * p.rb_u, &lu, &ou);
+    mbar_expect_tx(&wbar[st], lg + lu);
+    uint8_t* buf = wb + static_cast<size_t>(st) * p.stage_bytes;
+    bulk_g2s(buf, sg, lg, &wbar[st]);
+    bulk_g2s(buf + p.up_off, su, lu, &wbar[st]);
+  };
+  for (int st = 0; st < p.S; ++st) {
+    const int j = gw + st * tw;
+    if (j < p.jobs_total) issue(j, st);
+  }
+  prep_act(a, p.h, p.norm != nullptr, true, p.eps, true, red);
+  const int g = lane % G, r = lane / G;
+  Act3 act;
+  load_act3(act, a, g);
+  bool failed = false;
+  for (int it = 0;; ++it) {
+    const int j = gw + it * tw;
+    if (j >= p.jobs_total) break;
+    const int st = it % p.S;
+    int i, e, r0, n;
+    job_rows(j, i, e, r0, n);
+    if (!mbar_wait(&wbar[st], (it / p.S) & 1)) {
+      failed = true;
+      break;
+    }
+    const uint8_t* buf = wb + static_cast<size_t>(st) * p.stage_bytes;
+    const uint32_t og = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p.gate + e * p.gate_nb2 + r0 * p.rb_g) & 15);
+    const uint32_t ou = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p.up + e * p.up_nb2 + r0 * p.rb_u) & 15);
+    const float vg = row_dot3(buf + og + r * p.rb_g, p.tg, g, G, act);
+    const float vu = row_dot3(buf + p.up_off + ou + r * p.rb_u, p.tu, g, G, act);
+    if (g == 0 && r < n) p.ff[static_cast<int64_t>(i) * p.F + r0 + r] = silu_mul(vg, vu);
+    __syncwarp();
+    const int jn = gw + (it + p.S) * tw;
+    if (jn < p.jobs_total) issue(jn, st);
+  }
+  if (failed && lane == 0 && p.state != nullptr) atomicCAS(&p.state->error, 0, NH_E_TIMEOUT);
+}
+
+// down + combine: G = F/256 lanes per row and P = 32/G row groups per pass;
+// group q takes expert q % k and row q / k of the job's Rp = P/k rows, so a
+// lane's activation (its expert's super-block g of ff) never changes.  The k
+// values of a row are gathered by shuffles and summed in top-k order.
+__global__ void __launch_bounds__(kMoeWarps * 32, 2) down3_kernel(const DownArgs p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int KF = p.topk * p.F;
+  ActSmem a = carve_act(smem, KF, false);
+  const size_t act_bytes = (act_smem_bytes(KF, false) + 15) & ~static_cast<size_t>(15);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + act_bytes);
+  uint8_t* stage = reinterpret_cast<uint8_t*>(bars + kMoeWarps * p.S);
+  __shared__ int s_sel[kMaxTopK];
+  __shared__ float s_wts[kMaxTopK];
+  const int gw = blockIdx.x * kMoeWarps + warp, tw = gridDim.x * kMoeWarps;
+  const int G = p.lpr, k = p.topk, Rp = p.R;
+  uint64_t* wbar = bars + warp * p.S;
+  uint8_t* wb = stage + static_cast<size_t>(warp) * p.S * p.stage_bytes;
+  if (lane == 0) {
+    for (int s = 0; s < p.S; ++s) mbar_init(&wbar[s], 1);
+    fence_barrier_init();
+  }
+  pdl_wait();
+  pdl_trigger();
+  if (threadIdx.x < k) {
+    s_sel[threadIdx.x] = p.wsel[threadIdx.x];
+    s_wts[threadIdx.x] = p.wts[threadIdx.x];
+  }
+  __syncthreads();
+
+  auto issue = [&](int j, int st) {
+    if (lane != 0) return;
+    const int r0 = j * Rp;
+    const int n = min(Rp, p.D - r0);
+    uint32_t total = 0, len, off;
+    for (int i = 0; i < k; ++i) {
+      span16(p.down + s_sel[i] * p.nb2 + r0 * p.rb, n * p.rb, &len, &off);
+      total += len;
+    }
+    mbar_expect_tx(&wbar[st], total);
+    uint8_t* buf = wb + static_cast<size_t>(st) * p.stage_bytes;
+    for (int i = 0; i < k; ++i) {
+      const uint8_t* src = span16(p.down + s_sel[i] * p.nb2 + r0 * p.rb, n * p.rb, &len, &off);
+      bulk_g2s(buf + i * p.slot_bytes, src, len, &wbar[st]);
+    }
+  };
+  for (int st = 0; st < p.S; ++st) {
+    const int j = gw + st * tw;
+    if (j < p.jobs_total) issue(j, st);
+  }
+  // The activation: each expert's ff row, Q8_K-quantised per 256-block; a
+  // warp issues the loads of up to kU blocks before quantising any of them.
+  {
+    constexpr int kU = 8;
+    const int nb = KF / QK;
+    const bool al = (reinterpret_cast<uintptr_t>(p.ff) & 15) == 0;
+    for (int b0 = warp; b0 < nb; b0 += kU * kMoeWarps) {
+      float4 buf[kU][2];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int b = b0 + u * kMoeWarps;
+        if (b < nb) {
+          const float* src = p.ff + b * QK + lane * 8;
+          if (al) {
+            buf[u][0] = *reinterpret_cast<const float4*>(src);
+            buf[u][1] = *reinterpret_cast<const float4*>(src + 4);
+          } else {
+            buf[u][0] = make_float4(src[0], src[1], src[2], src[3]);
+            buf[u][1] = make_float4(src[4], src[5], src[6], src[7]);
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int b = b0 + u * kMoeWarps;
+        if (b < nb) {
+          const float v[8] = {buf[u][0].x, buf[u][0].y, buf[u][0].z, buf[u][0].w,
+                              buf[u][1].x, buf[u][1].y, buf[u][1].z, buf[u][1].w};
+          quantize_block_warp(v, b, a, lane);
+        }
+      }
+    }
+  }
+  __syncthreads();
+  const int g = lane % G, q = lane / G;
+  const int ie = q % k, rr = q / k;  // this lane's expert and row within the job
+  Act3 act;
+  load_act3(act, a, ie * G + g);
+  const int pos = p.state->pos, n_prompt = p.state->n_prompt;
+  const bool dump = p.dump != nullptr && pos >= n_prompt - 1;
+  const int rl = lane % Rp;  // the row this lane combines (lanes < n write it)
+  bool failed = false;
+  for (int it = 0;; ++it) {
+    const int j = gw + it * tw;
+    if (j >= p.jobs_total) break;
+    const int st = it % p.S;
+    const int r0 = j * Rp;
+    const int n = min(Rp, p.D - r0);
+    if (!mbar_wait(&wbar[st], (it / p.S) & 1)) {
+      failed = true;
+      break;
+    }
+    const uint8_t* buf = wb + static_cast<size_t>(st) * p.stage_bytes;
+    const uint32_t off =
+        static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p.down + s_sel[ie] * p.nb2 + r0 * p.rb) & 15);
+    const float v = row_dot3(buf + ie * p.slot_bytes + off + rr * p.rb, p.td, g, G, act);
+    // ggml_mul by the routing weights, then the chained adds in top-k order.
+    float acc = __fmul_rn(__shfl_sync(0xffffffffu, v, (rl * k) * G), s_wts[0]);
+    for (int i = 1; i < k; ++i) acc = __fadd_rn(acc, __fmul_rn(__shfl_sync(0xffffffffu, v, (rl * k + i) * G), s_wts[i]));
+    if (lane < n) {
+      const int row = r0 + lane;
+      const float hv = __fadd_rn(p.h[row], acc);
+      p.h[row] = hv;
+      if (dump) p.dump[static_cast<int64_t>(pos - n_prompt + 1) * p.dump_stride + p.dump_off + row] = hv;
+    }
+    __syncwarp();
+    const int jn = gw + (it + p.S) * tw;
+    if (jn < p.jobs_total) issue(jn, st);
+  }
+  if (failed && lane == 0) atomicCAS(&p.state->error, 0, NH_E_TIMEOUT);
+}
+
 }  // namespace nh
 
 using namespace nh;
@@ -524,6 +724,33 @@ int grid_for(int jobs, size_t smem) {
   return grid > cap ? cap : (grid < 1 ? 1 : grid);
 }
 
+// Grid for a kernel at a dynamic shared-memory size: one warp per job, at
+// most the CTAs that can be resident at once.
+template <typename Kern>
+int grid_resident(Kern k, int jobs, size_t smem) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kMoeWarps * 32, smem) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  int grid = (jobs + kMoeWarps - 1) / kMoeWarps;
+  const int cap = device_sm_count() * per_sm;
+  return grid > cap ? cap : (grid < 1 ? 1 : grid);
+}
+
+// Ring depth for the lane-per-super-block kernels: enough stages that the
+// resident warps cover every job (two CTAs per SM), within ~110 KB.
+int pick_stages3(size_t fixed, uint32_t stage_bytes, int jobs) {
+  const int warps = device_sm_count() * 2 * kMoeWarps;
+  int s = (jobs + warps - 1) / warps;
+  if (s < 1) s = 1;
+  if (s > kMoeMaxStages) s = kMoeMaxStages;
+  while (s > 1 && fixed + static_cast<size_t>(kMoeWarps) * s * (stage_bytes + 8) > 110 * 1024) --s;
+  return s;
+}
+
+bool aligned16(const void* p, uint64_t stride) {
+  return (reinterpret_cast<uintptr_t>(p) & 15) == 0 && (stride & 15) == 0;
+}
+
 }  // namespace
 
 extern "C" int nh_moe_gate_up(NhDecodeState* state, const float* h, const float* ffn_norm, float eps,
@@ -537,6 +764,8 @@ extern "C" int nh_moe_gate_up(NhDecodeState* state, const float* h, const float*
   for (int t : {tg, tu})
     if (t != NH_TYPE_F32 && t != NH_TYPE_Q4_K && t != NH_TYPE_Q6_K) return NH_E_TYPE;
   if (quant && !rowdot_k_ok(static_cast<int>(n_embd))) return NH_E_ARG;
+  if ((tg == NH_TYPE_Q4_K && !aligned16(gate, gate_nb2)) || (tu == NH_TYPE_Q4_K && !aligned16(up, up_nb2)))
+    return NH_E_ARG;
   GateUpArgs p;
   p.state = state;
   p.h = h;
@@ -556,6 +785,25 @@ extern "C" int nh_moe_gate_up(NhDecodeState* state, const float* h, const float*
   p.rb_u = row_bytes(tu, n_embd);
   p.down = nullptr;
   p.down_nb2 = 0;
+  if (quant && rowdot3_k_ok(p.K) && engine_v3()) {
+    p.lpr = p.K / QK;  // G
+    p.rpp = 32 / p.lpr;  // P rows of gate and of up per job
+    p.R = p.rpp;
+    const uint64_t gb = (p.rb_g * p.rpp + 32 + 127) & ~127ull;
+    const uint64_t ub = (p.rb_u * p.rpp + 32 + 127) & ~127ull;
+    p.up_off = static_cast<uint32_t>(gb);
+    p.stage_bytes = static_cast<uint32_t>(gb + ub);
+    p.jobs_per_expert = (p.F + p.rpp - 1) / p.rpp;
+    p.jobs_total = p.jobs_per_expert * k;
+    p.ff = ff;
+    const size_t fixed = ((act_smem_bytes(p.K, true, true) + 15) & ~static_cast<size_t>(15)) + 48 * sizeof(double);
+    p.S = pick_stages3(fixed, p.stage_bytes, p.jobs_total);
+    const size_t smem = fixed + kMoeWarps * p.S * sizeof(uint64_t) + static_cast<size_t>(kMoeWarps) * p.S * p.stage_bytes;
+    static size_t configured = 48 * 1024;
+    if (!ensure_smem(gate_up3_kernel, smem, configured)) return NH_E_CUDA;
+    const int grid = grid_resident(gate_up3_kernel, p.jobs_total, smem);
+    return launch_pdl(gate_up3_kernel, dim3(grid), dim3(kMoeWarps * 32), smem, static_cast<cudaStream_t>(stream), p);
+  }
   if (quant) {
     p.lpr = rowdot_lpr(p.K);
     p.rpp = 32 / p.lpr;
@@ -598,6 +846,7 @@ extern "C" int nh_moe_down_combine(const NhDecodeState* state, const float* ff, 
   const bool quant = td != NH_TYPE_F32;
   if (quant && !rowdot_k_ok(static_cast<int>(n_ff))) return NH_E_ARG;
   if (static_cast<int64_t>(k) * n_ff > 4 * kMaxK) return NH_E_ARG;
+  if (td == NH_TYPE_Q4_K && !aligned16(down, down_nb2)) return NH_E_ARG;
   DownArgs p;
   p.state = const_cast<NhDecodeState*>(state);
   p.ff = ff;
@@ -610,6 +859,27 @@ extern "C" int nh_moe_down_combine(const NhDecodeState* state, const float* ff, 
   p.rb = row_bytes(td, n_ff);
   p.F = static_cast<int>(n_ff);
   p.D = static_cast<int>(n_embd);
+  if (quant && rowdot3_k_ok(p.F) && (32 / (p.F / QK)) % k == 0 && engine_v3()) {
+    p.lpr = p.F / QK;            // G
+    p.rpp = 32 / p.lpr;          // row groups per pass
+    p.R = p.rpp / k;             // rows per job
+    p.slot_bytes = static_cast<uint32_t>((p.rb * p.R + 32 + 127) & ~127ull);
+    p.stage_bytes = p.slot_bytes * k;
+    p.jobs_total = (p.D + p.R - 1) / p.R;
+    p.ystride = 0;
+    p.h = h_io;
+    p.dump = dump;
+    p.dump_stride = dump_step_stride;
+    p.dump_off = dump_offset;
+    const size_t fixed = (act_smem_bytes(k * p.F, false) + 15) & ~static_cast<size_t>(15);
+    p.S = pick_stages3(fixed, p.stage_bytes, p.jobs_total);
+    const size_t smem = fixed + kMoeWarps * p.S * sizeof(uint64_t) + static_cast<size_t>(kMoeWarps) * p.S * p.stage_bytes;
+    if (smem > 220 * 1024) return NH_E_ARG;
+    static size_t configured = 48 * 1024;
+    if (!ensure_smem(down3_kernel, smem, configured)) return NH_E_CUDA;
+    const int grid = grid_resident(down3_kernel, p.jobs_total, smem);
+    return launch_pdl(down3_kernel, dim3(grid), dim3(kMoeWarps * 32), smem, static_cast<cudaStream_t>(stream), p);
+  }
   if (quant) {
     p.lpr = rowdot_lpr(p.F);
     p.rpp = 32 / p.lpr;
