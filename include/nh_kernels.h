@@ -146,6 +146,7 @@ int nh_router_topk(const NhDecodeState* state, const float* h, const float* ffn_
                    float* trace_gap, int layer, int n_layers, void* scratch, void* stream);
 int64_t nh_router_scratch_bytes(int n_expert);
 
+
 /* Expert up/gate projections and SwiGLU (moe.cc:41-46): for i < k,
  * ff[i][r] = silu((gate_e . b)[r]) * (up_e . b)[r] with e = wsel[i] and
  * b = RMSNorm(h)*ffn_norm.  gate/up are [n_slots][n_ff][n_embd] with
@@ -154,6 +155,14 @@ int nh_moe_gate_up(NhDecodeState* state, const float* h, const float* ffn_norm, 
                    const int32_t* wsel, int k,
                    const void* gate, int32_t tg, uint64_t gate_nb2, const void* up, int32_t tu,
                    uint64_t up_nb2, int64_t n_embd, int64_t n_ff, float* ff, void* stream);
+/* nh_moe_gate_up that also starts the selected experts' down slices
+ * (down + wsel[i] * down_nb2, down_nb2 bytes each) towards L2, each CTA a
+ * share, so nh_moe_down_combine reads them from L2.  A performance hint only:
+ * results are those of nh_moe_gate_up; down may be null. */
+int nh_moe_gate_up_prefetch(NhDecodeState* state, const float* h, const float* ffn_norm, float eps,
+                            const int32_t* wsel, int k, const void* gate, int32_t tg, uint64_t gate_nb2,
+                            const void* up, int32_t tu, uint64_t up_nb2, int64_t n_embd, int64_t n_ff,
+                            float* ff, const void* down, uint64_t down_nb2, void* stream);
 
 /* Down projections, routing weights and residual (moe.cc:47-60,
  * forward.cc:117-119): h_io[r] = h_io[r] + sum_i wts[i]*(down_e . ff[i])[r],

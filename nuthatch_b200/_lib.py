@@ -82,6 +82,8 @@ SIGNATURES = {
     "nh_router_topk": (C.c_int, [vp, vp, vp, f32, vp, i64, C.c_int, C.c_int, C.c_int, vp, vp, vp, vp, C.c_int,
                                  C.c_int, vp, vp]),
     "nh_moe_gate_up": (C.c_int, [vp, vp, vp, f32, vp, C.c_int, vp, i32, u64, vp, i32, u64, i64, i64, vp, vp]),
+    "nh_moe_gate_up_prefetch": (C.c_int, [vp, vp, vp, f32, vp, C.c_int, vp, i32, u64, vp, i32, u64, i64, i64, vp,
+                                          vp, u64, vp]),
     "nh_moe_down_combine": (C.c_int, [vp, vp, vp, vp, C.c_int, vp, i32, u64, i64, i64, vp, vp, i64, i64, vp]),
     "nh_lm_head_argmax": (C.c_int, [vp, vp, vp, f32, vp, i32, i64, i64, vp, vp, vp, vp]),
     "nh_gemv": (C.c_int, [vp, vp, i32, i64, i64, vp, vp, f32, vp, vp]),

@@ -259,8 +259,9 @@ int Engine::EnqueueMoePhase(const ModelView& m, int l, const void* gate, int32_t
                             const int32_t* wsel, bool dumps) {
   const OlmoeConfig& c = cfg_;
   const LayerView& L = m.layers[l];
-  NH_TRY(nh_moe_gate_up(state_, h_,L.ffn_norm, c.rms_eps, wsel, c.n_expert_used, gate, tg, gnb2, up, tu, unb2, c.n_embd,
-                        c.n_ff, ff_, stream_));
+  // gate/up also starts this layer's selected down slices towards L2.
+  NH_TRY(nh_moe_gate_up_prefetch(state_, h_, L.ffn_norm, c.rms_eps, wsel, c.n_expert_used, gate, tg, gnb2, up, tu,
+                                 unb2, c.n_embd, c.n_ff, ff_, down, dnb2, stream_));
   const int64_t d = c.n_embd;
   return nh_moe_down_combine(state_, ff_, wsel, wts_, c.n_expert_used, down, td, dnb2, c.n_ff, d, h_,
                              dumps ? dump_hidden_ : nullptr, static_cast<int64_t>(c.n_layers) * d, l * d, stream_);

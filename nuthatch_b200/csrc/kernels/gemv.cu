@@ -393,7 +393,7 @@ int gemv3_launch(GemvArgs& p, cudaStream_t stream) {
   const size_t smem = fixed + kGemvWarps * p.S * sizeof(uint64_t) + static_cast<size_t>(kGemvWarps) * p.S * p.stage_bytes;
   static size_t configured = 48 * 1024;
   if (!ensure_smem(gemv3_kernel, smem, configured)) return NH_E_CUDA;
-  const int per_sm = resident_ctas(gemv3_kernel, kGemvWarps * 32, smem);
+  const int per_sm = std::min(resident_ctas(gemv3_kernel, kGemvWarps * 32, smem), ctas_per_sm_cap());
   int grid = (total + kGemvWarps - 1) / kGemvWarps;
   const int cap = device_sm_count() * per_sm;
   if (grid > cap) grid = cap;

@@ -47,6 +47,18 @@ inline bool engine_v3() {
   return v != 0;
 }
 
+// Upper bound on resident CTAs per SM for the row-dot kernels (NH_CTAS_PER_SM,
+// default 2, read once).  One CTA per SM leaves room for the next kernel's
+// CTAs to become resident early under programmatic dependent launch.
+inline int ctas_per_sm_cap() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("NH_CTAS_PER_SM");
+    v = (e != nullptr && e[0] >= '1' && e[0] <= '4') ? e[0] - '0' : 2;
+  }
+  return v;
+}
+
 template <typename Kern>
 bool ensure_smem(Kern k, size_t bytes, size_t& configured) {
   if (bytes <= configured) return true;

@@ -40,6 +40,8 @@ struct RouterArgs {
 // f32 router row in registers: lane l holds elements 4l + 128t (t < K/128).
 constexpr int kRouterMaxVec = kMaxK / 128;
 
+// KP = experts per lane of the softmax / top-k warp (n_expert <= 32*KP).
+template <int KP>
 __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(const RouterArgs p) {
   extern __shared__ __align__(128) uint8_t smem[];
   ActSmem a = carve_act(smem, p.K, true, true);
@@ -92,7 +94,7 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(const RouterA
   // ggml_soft_max over the E logits: exp(x - max) in f32, summed in double,
   // scaled by 1/sum.  Lane l holds experts l, l+32, ...
   const volatile float* lg = p.logits;
-  constexpr int kPer = kMaxExperts / 32;
+  constexpr int kPer = KP;
   float pr[kPer];
   float mx = -INFINITY;
 #pragma unroll
@@ -111,61 +113,63 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(const RouterA
   }
   sum = warp_sum_d(sum);
   const float inv = static_cast<float>(1.0 / sum);
-  uint32_t taken = 0;
 #pragma unroll
   for (int k = 0; k < kPer; ++k) pr[k] = __fmul_rn(pr[k], inv);
-  // Top-(k+1) by repeated warp argmax: descending probability, equal
-  // probabilities keep the lower expert id first.
-  int ids[kMaxTopK + 1];
-  float vals[kMaxTopK + 1];
+  // Top-(k+1) by rank: descending probability, equal probabilities keep the
+  // lower expert id first (the order repeated argmax would produce).  Every
+  // lane ranks its own experts against all others, read by shuffles.
+  __shared__ int s_ids[kMaxTopK + 1];
+  __shared__ float s_vals[kMaxTopK + 1];
   const int kk = min(p.topk + 1, p.E);
-  for (int t = 0; t < kk; ++t) {
-    float bv = -INFINITY;
-    int bi = INT_MAX;
+  int rank[kPer];
 #pragma unroll
-    for (int k = 0; k < kPer; ++k) {
-      const int i = lane + 32 * k;
-      if (i < p.E && !(taken & (1u << k)) && (bi == INT_MAX || argmax_better(pr[k], i, bv, bi))) {
-        bv = pr[k];
-        bi = i;
+  for (int k = 0; k < kPer; ++k) rank[k] = 0;
+#pragma unroll
+  for (int kj = 0; kj < kPer; ++kj) {
+#pragma unroll 8
+    for (int src = 0; src < 32; ++src) {
+      const float pj = __shfl_sync(0xffffffffu, pr[kj], src);
+      const int j = src + 32 * kj;
+#pragma unroll
+      for (int ki = 0; ki < kPer; ++ki) {
+        const int i = lane + 32 * ki;
+        rank[ki] += (j < p.E && (pj > pr[ki] || (pj == pr[ki] && j < i))) ? 1 : 0;
       }
     }
+  }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (oi != INT_MAX && (bi == INT_MAX || argmax_better(ov, oi, bv, bi))) {
-        bv = ov;
-        bi = oi;
-      }
+  for (int k = 0; k < kPer; ++k) {
+    const int i = lane + 32 * k;
+    if (i < p.E && rank[k] < kk) {
+      s_ids[rank[k]] = i;
+      s_vals[rank[k]] = pr[k];
     }
-    ids[t] = bi;
-    vals[t] = bv;
-    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+  }
+  __syncwarp();
+  // Lane t writes output t.
+  float ws = 1.f;
+  if (p.norm_topk) {
+    double sw = 0.0;
+    for (int t = 0; t < p.topk; ++t) sw += static_cast<double>(s_vals[t]);
+    ws = fmaxf(static_cast<float>(sw), 6.103515625e-5f);
+  }
+  const int64_t pos = p.state->pos;
+  for (int t = lane; t < p.topk; t += 32) {
+    const int id = s_ids[t];
+    const float v = s_vals[t];
+    p.sel[t] = id;
+    p.wts[t] = p.norm_topk ? __fdiv_rn(v, ws) : v;
+    if (p.trace_sel != nullptr) p.trace_sel[(pos * p.n_layers + p.layer) * p.topk + t] = id;
+  }
+  if (p.trace_sel != nullptr && p.trace_gap != nullptr) {
+    // Smallest gap between adjacent probabilities of the descending top-(k+1).
+    float g = 1.f;
+    for (int t = lane; t + 1 < kk; t += 32) g = fminf(g, __fsub_rn(s_vals[t], s_vals[t + 1]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) g = fminf(g, __shfl_xor_sync(0xffffffffu, g, o));
+    if (lane == 0) p.trace_gap[pos * p.n_layers + p.layer] = g;
   }
   if (lane != 0) return;
-  float w[kMaxTopK];
-  for (int t = 0; t < p.topk; ++t) w[t] = vals[t];
-  if (p.norm_topk) {
-    double s = 0.0;
-    for (int t = 0; t < p.topk; ++t) s += static_cast<double>(w[t]);
-    const float ws = fmaxf(static_cast<float>(s), 6.103515625e-5f);
-    for (int t = 0; t < p.topk; ++t) w[t] = __fdiv_rn(w[t], ws);
-  }
-  for (int t = 0; t < p.topk; ++t) {
-    p.sel[t] = ids[t];
-    p.wts[t] = w[t];
-  }
-  if (p.trace_sel != nullptr) {
-    const int64_t pos = p.state->pos;
-    for (int t = 0; t < p.topk; ++t) p.trace_sel[(pos * p.n_layers + p.layer) * p.topk + t] = ids[t];
-    if (p.trace_gap != nullptr) {
-      // Smallest gap between adjacent probabilities of the descending top-(k+1).
-      float g = 1.f;
-      for (int t = 0; t + 1 < kk; ++t) g = fminf(g, __fsub_rn(vals[t], vals[t + 1]));
-      p.trace_gap[pos * p.n_layers + p.layer] = g;
-    }
-  }
   *p.ticket = 0u;
 }
 
@@ -502,6 +506,22 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) gate_up3_kernel(const GateU
     const int j = gw + st * tw;
     if (j < p.jobs_total) issue(j, st);
   }
+  // Start the selected experts' down weights towards L2 for the kernel that
+  // follows: this CTA's share, in pieces of at most 64 KB over warp 0's lanes.
+  if (p.down != nullptr && warp == 0) {
+    constexpr uint64_t kPiece = 64 * 1024;
+    const uint64_t total = p.down_nb2 * static_cast<uint64_t>(p.topk);
+    const uint64_t share = ((total / gridDim.x) + 15) & ~static_cast<uint64_t>(15);
+    const uint64_t beg = share * blockIdx.x;
+    const uint64_t end = beg + share < total ? beg + share : total;
+    for (uint64_t o = beg + static_cast<uint64_t>(lane) * kPiece; o < end; o += 32 * kPiece) {
+      // Pieces never straddle two experts: clip at the expert boundary.
+      const uint64_t i = o / p.down_nb2, in = o - i * p.down_nb2;
+      uint64_t len = end - o < kPiece ? end - o : kPiece;
+      if (in + len > p.down_nb2) len = p.down_nb2 - in;
+      prefetch_l2(p.down + static_cast<uint64_t>(s_sel[i]) * p.down_nb2 + in, static_cast<uint32_t>(len));
+    }
+  }
   prep_act(a, p.h, p.norm != nullptr, true, p.eps, true, red);
   const int g = lane % G, r = lane / G;
   Act3 act;
@@ -656,6 +676,15 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) down3_kernel(const DownArgs
 
 using namespace nh;
 
+namespace {
+template <int KP>
+int launch_router(const RouterArgs& p, size_t smem, int grid, cudaStream_t st) {
+  static size_t configured = 48 * 1024;
+  if (!ensure_smem(router_kernel<KP>, smem, configured)) return NH_E_CUDA;
+  return launch_pdl(router_kernel<KP>, dim3(grid), dim3(kRouterWarps * 32), smem, st, p);
+}
+}  // namespace
+
 extern "C" int64_t nh_router_scratch_bytes(int n_expert) { return 64 + 4 * static_cast<int64_t>(n_expert) + 64; }
 
 extern "C" int nh_router_topk(const NhDecodeState* state, const float* h, const float* ffn_norm, float eps,
@@ -686,10 +715,12 @@ extern "C" int nh_router_topk(const NhDecodeState* state, const float* h, const 
   p.ticket = static_cast<unsigned*>(scratch);
   p.logits = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + 64);
   const size_t smem = act_smem_bytes(p.K, true, true);
-  static size_t configured = 48 * 1024;
-  if (!ensure_smem(router_kernel, smem, configured)) return NH_E_CUDA;
   const int grid = (n_expert + kRouterWarps - 1) / kRouterWarps;
-  return launch_pdl(router_kernel, dim3(grid), dim3(kRouterWarps * 32), smem, static_cast<cudaStream_t>(stream), p);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (n_expert <= 32) return launch_router<1>(p, smem, grid, st);
+  if (n_expert <= 64) return launch_router<2>(p, smem, grid, st);
+  if (n_expert <= 128) return launch_router<4>(p, smem, grid, st);
+  return launch_router<8>(p, smem, grid, st);
 }
 
 namespace {
@@ -731,6 +762,7 @@ int grid_resident(Kern k, int jobs, size_t smem) {
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kMoeWarps * 32, smem) != cudaSuccess || per_sm < 1)
     per_sm = 1;
+  if (per_sm > ctas_per_sm_cap()) per_sm = ctas_per_sm_cap();
   int grid = (jobs + kMoeWarps - 1) / kMoeWarps;
   const int cap = device_sm_count() * per_sm;
   return grid > cap ? cap : (grid < 1 ? 1 : grid);
@@ -739,7 +771,7 @@ int grid_resident(Kern k, int jobs, size_t smem) {
 // Ring depth for the lane-per-super-block kernels: enough stages that the
 // resident warps cover every job (two CTAs per SM), within ~110 KB.
 int pick_stages3(size_t fixed, uint32_t stage_bytes, int jobs) {
-  const int warps = device_sm_count() * 2 * kMoeWarps;
+  const int warps = device_sm_count() * ctas_per_sm_cap() * kMoeWarps;
   int s = (jobs + warps - 1) / warps;
   if (s < 1) s = 1;
   if (s > kMoeMaxStages) s = kMoeMaxStages;
@@ -753,10 +785,10 @@ bool aligned16(const void* p, uint64_t stride) {
 
 }  // namespace
 
-extern "C" int nh_moe_gate_up(NhDecodeState* state, const float* h, const float* ffn_norm, float eps,
-                              const int32_t* wsel, int k, const void* gate, int32_t tg, uint64_t gate_nb2,
-                              const void* up, int32_t tu, uint64_t up_nb2, int64_t n_embd, int64_t n_ff, float* ff,
-                              void* stream) {
+extern "C" int nh_moe_gate_up_prefetch(NhDecodeState* state, const float* h, const float* ffn_norm, float eps,
+                                       const int32_t* wsel, int k, const void* gate, int32_t tg, uint64_t gate_nb2,
+                                       const void* up, int32_t tu, uint64_t up_nb2, int64_t n_embd, int64_t n_ff,
+                                       float* ff, const void* down, uint64_t down_nb2, void* stream) {
   if (h == nullptr || wsel == nullptr || gate == nullptr || up == nullptr || ff == nullptr) return NH_E_ARG;
   if (k <= 0 || k > kMaxTopK || n_embd <= 0 || n_embd > kMaxK || n_ff <= 0) return NH_E_ARG;
   const bool quant = tg != NH_TYPE_F32;
@@ -783,8 +815,10 @@ extern "C" int nh_moe_gate_up(NhDecodeState* state, const float* h, const float*
   p.F = static_cast<int>(n_ff);
   p.rb_g = row_bytes(tg, n_embd);
   p.rb_u = row_bytes(tu, n_embd);
-  p.down = nullptr;
-  p.down_nb2 = 0;
+  // Prefetch ranges start 16-byte aligned and have 16-byte multiple lengths.
+  const bool pf = down != nullptr && down_nb2 > 0 && (reinterpret_cast<uintptr_t>(down) & 15) == 0 && (down_nb2 & 15) == 0;
+  p.down = pf ? static_cast<const uint8_t*>(down) : nullptr;
+  p.down_nb2 = pf ? down_nb2 : 0;
   if (quant && rowdot3_k_ok(p.K) && engine_v3()) {
     p.lpr = p.K / QK;  // G
     p.rpp = 32 / p.lpr;  // P rows of gate and of up per job
@@ -833,6 +867,14 @@ extern "C" int nh_moe_gate_up(NhDecodeState* state, const float* h, const float*
   const int cpl = quant ? (p.K / 64 + 31) / 32 : 1;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return cpl <= 1 ? launch_gate_up<1>(p, smem, grid, s) : launch_gate_up<2>(p, smem, grid, s);
+}
+
+extern "C" int nh_moe_gate_up(NhDecodeState* state, const float* h, const float* ffn_norm, float eps,
+                              const int32_t* wsel, int k, const void* gate, int32_t tg, uint64_t gate_nb2,
+                              const void* up, int32_t tu, uint64_t up_nb2, int64_t n_embd, int64_t n_ff, float* ff,
+                              void* stream) {
+  return nh_moe_gate_up_prefetch(state, h, ffn_norm, eps, wsel, k, gate, tg, gate_nb2, up, tu, up_nb2, n_embd, n_ff,
+                                 ff, nullptr, 0, stream);
 }
 
 extern "C" int nh_moe_down_combine(const NhDecodeState* state, const float* ff, const int32_t* wsel, const float* wts,
