@@ -11,6 +11,7 @@
 #include <cstring>
 
 #include "launch.cuh"
+#include "cluster_prep.cuh"
 #include "rowdot3.cuh"
 
 namespace nh {
@@ -222,6 +223,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv3_kernel(const GemvArg
   __shared__ float s_bv[32];
   __shared__ int s_bi[32];
   __shared__ bool s_last;
+  __shared__ double s_part[8];
+  cluster_arrive_relaxed();
 
   int pos = 0, n_prompt = 0;
   bool skip = false;
@@ -261,16 +264,17 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv3_kernel(const GemvArg
       const int j = gw + st * tw;
       if (j < p.jobs_total) issue(j, st);
     }
-    act_load_norm(a, p.norm_w);
+    cluster_load_norm(a, p.norm_w);
   }
   pdl_wait();
   pdl_trigger();
+  cluster_wait();
 
   float best_v = -INFINITY;
   int best_i = INT_MAX;
   bool failed = false;
   if (!skip) {
-    prep_act(a, p.x, p.norm_w != nullptr, p.do_norm != 0, p.eps, true, red);
+    cluster_prep_act(a, p.x, p.norm_w != nullptr, p.do_norm != 0, p.eps, true, false, red, s_part);
     const int g = lane % G, r = lane / G;
     Act3 act;
     load_act3(act, a, g);
@@ -399,7 +403,10 @@ int gemv3_launch(GemvArgs& p, cudaStream_t stream) {
   if (grid > cap) grid = cap;
   if (p.argmax && grid > kMaxArgmaxBlocks) grid = kMaxArgmaxBlocks;
   if (grid < 1) grid = 1;
-  return launch_pdl(gemv3_kernel, dim3(grid), dim3(kGemvWarps * 32), smem, stream, p);
+  int cluster = prep_cluster_size(p.K, true);
+  while (cluster > grid) cluster >>= 1;
+  grid = round_grid(grid, cluster);
+  return launch_pdl_cluster(gemv3_kernel, dim3(grid), dim3(kGemvWarps * 32), smem, stream, cluster, p);
 }
 
 int gemv_launch(GemvArgs& p, cudaStream_t stream) {

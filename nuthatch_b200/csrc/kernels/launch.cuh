@@ -59,6 +59,28 @@ inline int ctas_per_sm_cap() {
   return v;
 }
 
+// Thread-block clusters that share the activation preparation are used only
+// when NH_CLUSTER=1 (read once).  Measured on B200 they cost more in cluster
+// barriers and scheduling than the shared preparation saves, so the default
+// is one CTA per cluster.
+inline bool clusters_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("NH_CLUSTER");
+    v = (e != nullptr && e[0] == '1') ? 1 : 0;
+  }
+  return v != 0;
+}
+
+// Largest cluster size C <= 8 (a power of two) with K % (4*C) == 0 and, when
+// the activation is quantised, (K/256) % C == 0; 1 when clusters are off.
+inline int prep_cluster_size(int K, bool quant) {
+  if (!clusters_enabled()) return 1;
+  int c = 8;
+  while (c > 1 && (K % (4 * c) != 0 || (quant && (K / 256) % c != 0))) c >>= 1;
+  return c;
+}
+
 template <typename Kern>
 bool ensure_smem(Kern k, size_t bytes, size_t& configured) {
   if (bytes <= configured) return true;
@@ -85,6 +107,36 @@ int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaS
   cfg.attrs = at;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...) == cudaSuccess ? NH_OK : NH_E_CUDA;
+}
+
+// launch_pdl with a 1-D thread-block cluster of `cluster` CTAs (grid.x must
+// be a multiple of it).
+template <typename... KArgs, typename... Args>
+int launch_pdl_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, int cluster,
+                       Args&&... args) {
+  if (cluster <= 1) return launch_pdl(kern, grid, block, smem, s, std::forward<Args>(args)...);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = pdl_enabled();
+  at[1].id = cudaLaunchAttributeClusterDimension;
+  at[1].val.clusterDim.x = static_cast<unsigned>(cluster);
+  at[1].val.clusterDim.y = 1;
+  at[1].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...) == cudaSuccess ? NH_OK : NH_E_CUDA;
+}
+
+// Rounds a grid down to a multiple of the cluster size (at least one cluster).
+inline int round_grid(int grid, int cluster) {
+  if (cluster <= 1) return grid;
+  const int g = grid / cluster * cluster;
+  return g < cluster ? cluster : g;
 }
 
 }  // namespace nh

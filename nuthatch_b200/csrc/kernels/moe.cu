@@ -11,6 +11,7 @@
 #include <climits>
 
 #include "launch.cuh"
+#include "cluster_prep.cuh"
 #include "rowdot3.cuh"
 
 namespace nh {
@@ -46,7 +47,9 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(const RouterA
   extern __shared__ __align__(128) uint8_t smem[];
   ActSmem a = carve_act(smem, p.K, true, true);
   __shared__ double red[48];
+  __shared__ double s_part[8];
   __shared__ bool s_last;
+  cluster_arrive_relaxed();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e = blockIdx.x * kRouterWarps + warp;
   // The router weights do not depend on the preceding kernel: load the row
@@ -59,10 +62,11 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(const RouterA
     for (int t = 0; t < kRouterMaxVec; ++t)
       if (t < p.K / 128) wv[t] = w4[lane + 32 * t];
   }
-  act_load_norm(a, p.norm);
+  cluster_load_norm(a, p.norm);
   pdl_wait();
   pdl_trigger();
-  prep_act(a, p.h, p.norm != nullptr, true, p.eps, false, red);
+  cluster_wait();
+  cluster_prep_act(a, p.h, p.norm != nullptr, true, p.eps, false, true, red, s_part);
   if (e < p.E) {
     float v;
     if (vec) {
@@ -469,6 +473,8 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) gate_up3_kernel(const GateU
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + act_bytes + 48 * sizeof(double));
   uint8_t* stage = reinterpret_cast<uint8_t*>(bars + kMoeWarps * p.S);
   __shared__ int s_sel[kMaxTopK];
+  __shared__ double s_part[8];
+  cluster_arrive_relaxed();
   const int gw = blockIdx.x * kMoeWarps + warp, tw = gridDim.x * kMoeWarps;
   const int G = p.lpr, P = p.rpp;
   uint64_t* wbar = bars + warp * p.S;
@@ -477,7 +483,7 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) gate_up3_kernel(const GateU
     for (int s = 0; s < p.S; ++s) mbar_init(&wbar[s], 1);
     fence_barrier_init();
   }
-  act_load_norm(a, p.norm);
+  cluster_load_norm(a, p.norm);
   pdl_wait();
   pdl_trigger();
   // The selection is read once; every job then finds its expert in shared memory.
@@ -522,7 +528,8 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) gate_up3_kernel(const GateU
       prefetch_l2(p.down + static_cast<uint64_t>(s_sel[i]) * p.down_nb2 + in, static_cast<uint32_t>(len));
     }
   }
-  prep_act(a, p.h, p.norm != nullptr, true, p.eps, true, red);
+  cluster_wait();
+  cluster_prep_act(a, p.h, p.norm != nullptr, true, p.eps, true, false, red, s_part);
   const int g = lane % G, r = lane / G;
   Act3 act;
   load_act3(act, a, g);
@@ -558,12 +565,15 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) down3_kernel(const DownArgs
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int KF = p.topk * p.F;
-  ActSmem a = carve_act(smem, KF, false);
-  const size_t act_bytes = (act_smem_bytes(KF, false) + 15) & ~static_cast<size_t>(15);
+  ActSmem a = carve_act(smem, KF, true);
+  const size_t act_bytes = (act_smem_bytes(KF, true) + 15) & ~static_cast<size_t>(15);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + act_bytes);
   uint8_t* stage = reinterpret_cast<uint8_t*>(bars + kMoeWarps * p.S);
   __shared__ int s_sel[kMaxTopK];
   __shared__ float s_wts[kMaxTopK];
+  __shared__ double red[40];
+  __shared__ double s_part[8];
+  cluster_arrive_relaxed();
   const int gw = blockIdx.x * kMoeWarps + warp, tw = gridDim.x * kMoeWarps;
   const int G = p.lpr, k = p.topk, Rp = p.R;
   uint64_t* wbar = bars + warp * p.S;
@@ -580,60 +590,29 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) down3_kernel(const DownArgs
   }
   __syncthreads();
 
+  // Lane i < k copies expert i's rows; lane 0 registers the total bytes on
+  // the stage's barrier before any copy is issued.
   auto issue = [&](int j, int st) {
-    if (lane != 0) return;
     const int r0 = j * Rp;
     const int n = min(Rp, p.D - r0);
-    uint32_t total = 0, len, off;
-    for (int i = 0; i < k; ++i) {
-      span16(p.down + s_sel[i] * p.nb2 + r0 * p.rb, n * p.rb, &len, &off);
-      total += len;
-    }
-    mbar_expect_tx(&wbar[st], total);
-    uint8_t* buf = wb + static_cast<size_t>(st) * p.stage_bytes;
-    for (int i = 0; i < k; ++i) {
-      const uint8_t* src = span16(p.down + s_sel[i] * p.nb2 + r0 * p.rb, n * p.rb, &len, &off);
-      bulk_g2s(buf + i * p.slot_bytes, src, len, &wbar[st]);
-    }
+    uint32_t len = 0, off;
+    const uint8_t* src = nullptr;
+    if (lane < k) src = span16(p.down + s_sel[lane] * p.nb2 + r0 * p.rb, n * p.rb, &len, &off);
+    uint32_t total = len;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+    if (lane == 0) mbar_expect_tx(&wbar[st], total);
+    __syncwarp();
+    if (lane < k) bulk_g2s(wb + static_cast<size_t>(st) * p.stage_bytes + lane * p.slot_bytes, src, len, &wbar[st]);
   };
   for (int st = 0; st < p.S; ++st) {
     const int j = gw + st * tw;
     if (j < p.jobs_total) issue(j, st);
   }
-  // The activation: each expert's ff row, Q8_K-quantised per 256-block; a
-  // warp issues the loads of up to kU blocks before quantising any of them.
-  {
-    constexpr int kU = 8;
-    const int nb = KF / QK;
-    const bool al = (reinterpret_cast<uintptr_t>(p.ff) & 15) == 0;
-    for (int b0 = warp; b0 < nb; b0 += kU * kMoeWarps) {
-      float4 buf[kU][2];
-#pragma unroll
-      for (int u = 0; u < kU; ++u) {
-        const int b = b0 + u * kMoeWarps;
-        if (b < nb) {
-          const float* src = p.ff + b * QK + lane * 8;
-          if (al) {
-            buf[u][0] = *reinterpret_cast<const float4*>(src);
-            buf[u][1] = *reinterpret_cast<const float4*>(src + 4);
-          } else {
-            buf[u][0] = make_float4(src[0], src[1], src[2], src[3]);
-            buf[u][1] = make_float4(src[4], src[5], src[6], src[7]);
-          }
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < kU; ++u) {
-        const int b = b0 + u * kMoeWarps;
-        if (b < nb) {
-          const float v[8] = {buf[u][0].x, buf[u][0].y, buf[u][0].z, buf[u][0].w,
-                              buf[u][1].x, buf[u][1].y, buf[u][1].z, buf[u][1].w};
-          quantize_block_warp(v, b, a, lane);
-        }
-      }
-    }
-  }
-  __syncthreads();
+  // The activation: the k experts' ff rows, Q8_K-quantised per 256-block,
+  // each CTA of the cluster quantising its share.
+  cluster_wait();
+  cluster_prep_act(a, p.ff, false, false, 0.f, true, false, red, s_part);
   const int g = lane % G, q = lane / G;
   const int ie = q % k, rr = q / k;  // this lane's expert and row within the job
   Act3 act;
@@ -681,7 +660,10 @@ template <int KP>
 int launch_router(const RouterArgs& p, size_t smem, int grid, cudaStream_t st) {
   static size_t configured = 48 * 1024;
   if (!ensure_smem(router_kernel<KP>, smem, configured)) return NH_E_CUDA;
-  return launch_pdl(router_kernel<KP>, dim3(grid), dim3(kRouterWarps * 32), smem, st, p);
+  // One cluster shares the preparation when the grid is a power of two <= 8.
+  int cluster = prep_cluster_size(p.K, false);
+  while (cluster > 1 && grid % cluster != 0) cluster >>= 1;
+  return launch_pdl_cluster(router_kernel<KP>, dim3(grid), dim3(kRouterWarps * 32), smem, st, cluster, p);
 }
 }  // namespace
 
@@ -835,8 +817,12 @@ extern "C" int nh_moe_gate_up_prefetch(NhDecodeState* state, const float* h, con
     const size_t smem = fixed + kMoeWarps * p.S * sizeof(uint64_t) + static_cast<size_t>(kMoeWarps) * p.S * p.stage_bytes;
     static size_t configured = 48 * 1024;
     if (!ensure_smem(gate_up3_kernel, smem, configured)) return NH_E_CUDA;
-    const int grid = grid_resident(gate_up3_kernel, p.jobs_total, smem);
-    return launch_pdl(gate_up3_kernel, dim3(grid), dim3(kMoeWarps * 32), smem, static_cast<cudaStream_t>(stream), p);
+    int grid = grid_resident(gate_up3_kernel, p.jobs_total, smem);
+    int cluster = prep_cluster_size(p.K, true);
+    while (cluster > grid) cluster >>= 1;
+    grid = round_grid(grid, cluster);
+    return launch_pdl_cluster(gate_up3_kernel, dim3(grid), dim3(kMoeWarps * 32), smem,
+                              static_cast<cudaStream_t>(stream), cluster, p);
   }
   if (quant) {
     p.lpr = rowdot_lpr(p.K);
@@ -905,7 +891,11 @@ extern "C" int nh_moe_down_combine(const NhDecodeState* state, const float* ff, 
     p.lpr = p.F / QK;            // G
     p.rpp = 32 / p.lpr;          // row groups per pass
     p.R = p.rpp / k;             // rows per job
-    p.slot_bytes = static_cast<uint32_t>((p.rb * p.R + 32 + 127) & ~127ull);
+    // Expert slots are offset from 128-byte multiples so the lanes that read
+    // the same super-block of different experts hit different banks: 64 mod
+    // 128 for Q4_K (16-byte loads, two experts per quarter warp), 16 mod 128
+    // for Q6_K (32-bit loads across the warp).
+    p.slot_bytes = static_cast<uint32_t>(((p.rb * p.R + 32 + 127) & ~127ull) + (td == NH_TYPE_Q4_K ? 64 : 16));
     p.stage_bytes = p.slot_bytes * k;
     p.jobs_total = (p.D + p.R - 1) / p.R;
     p.ystride = 0;
@@ -913,14 +903,18 @@ extern "C" int nh_moe_down_combine(const NhDecodeState* state, const float* ff, 
     p.dump = dump;
     p.dump_stride = dump_step_stride;
     p.dump_off = dump_offset;
-    const size_t fixed = (act_smem_bytes(k * p.F, false) + 15) & ~static_cast<size_t>(15);
+    const size_t fixed = (act_smem_bytes(k * p.F, true) + 15) & ~static_cast<size_t>(15);
     p.S = pick_stages3(fixed, p.stage_bytes, p.jobs_total);
     const size_t smem = fixed + kMoeWarps * p.S * sizeof(uint64_t) + static_cast<size_t>(kMoeWarps) * p.S * p.stage_bytes;
     if (smem > 220 * 1024) return NH_E_ARG;
     static size_t configured = 48 * 1024;
     if (!ensure_smem(down3_kernel, smem, configured)) return NH_E_CUDA;
-    const int grid = grid_resident(down3_kernel, p.jobs_total, smem);
-    return launch_pdl(down3_kernel, dim3(grid), dim3(kMoeWarps * 32), smem, static_cast<cudaStream_t>(stream), p);
+    int grid = grid_resident(down3_kernel, p.jobs_total, smem);
+    int cluster = prep_cluster_size(k * p.F, true);
+    while (cluster > grid) cluster >>= 1;
+    grid = round_grid(grid, cluster);
+    return launch_pdl_cluster(down3_kernel, dim3(grid), dim3(kMoeWarps * 32), smem,
+                              static_cast<cudaStream_t>(stream), cluster, p);
   }
   if (quant) {
     p.lpr = rowdot_lpr(p.F);
