@@ -164,6 +164,69 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_streaming(args) -> None:
+    """Streaming decode (two-phase, HBM expert slot pool) on the skewed
+    OLMoE-1B-7B-shaped GGUF: prompt 64, 256 greedy ids, budget B experts per
+    layer, learned-pin (pin = ceil(0.75 B)) calibrated on a resident routing
+    trace of a different seeded prompt, and LRU at the same budget.  Timed end
+    to end through StreamingGenerate (host ids in and out, token-by-token
+    prefill included); one JSON line per (policy, budget)."""
+    import math
+
+    import torch
+
+    import nuthatch_b200 as nh
+    from nuthatch_b200 import build, synth
+
+    build.build_product()
+    torch.cuda.set_device(0)
+    path = str(synth.cached(synth.OLMOE_1B7B_SKEW))
+    n_prompt, n_pred = 64, args.stream_tokens
+    rng = np.random.default_rng(7)
+    resident = nh.OlmoeModel.Load(path)
+    cfg = resident.config()
+    calib_prompt = rng.integers(0, cfg.n_vocab, n_prompt).tolist()
+    prompt = np.random.default_rng(8).integers(0, cfg.n_vocab, n_prompt).tolist()
+    trace = nh.RoutingTrace()
+    nh.GreedyGenerateCachedTrace(resident, calib_prompt, n_pred, False, trace)
+    usage = nh.BuildUsage(trace, cfg.n_expert).counts
+    ref = nh.GreedyGenerateCached(resident, prompt, n_pred, False)
+    # Realised expert-frequency skew of the calibration trace (share of the top quarter of experts).
+    per = np.sort(usage.astype(np.float64), axis=1)[:, ::-1]
+    skew = float(np.mean(per[:, : cfg.n_expert // 4].sum(1) / per.sum(1)))
+    del resident
+    torch.cuda.empty_cache()
+    sm = nh.StreamingModel.Load(path)
+    for budget in args.budgets:
+        for policy in ("learned_pin", "lru"):
+            pin = int(math.ceil(0.75 * budget)) if policy == "learned_pin" else 0
+            kw = dict(policy=policy, pin_slots=pin, usage=usage if policy == "learned_pin" else None)
+            for _ in range(args.warmup):
+                nh.streaming_generate_ex(sm, prompt, 8, False, budget, **kw)
+            times, out = [], None
+            for _ in range(args.steps):
+                t0 = time.perf_counter()
+                out = nh.streaming_generate_ex(sm, prompt, n_pred, False, budget, **kw)
+                times.append(time.perf_counter() - t0)
+            hits, misses = int(out["hits"].sum()), int(out["misses"].sum())
+            dt = float(np.median(times))
+            line = {"metric": f"OLMoE streaming decode tok/s (bs1, budget {budget}, {policy})",
+                    "value": n_pred / dt, "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                    "ms_per_step": 1000 * dt, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                    "dtype": "q4k/q6k x q8k int dot, f32 accumulate",
+                    "data": "synthetic (seeded random-init GGUF of the OLMoE-1B-7B shape, log-Zipf router skew)",
+                    "config": {"workload": f"olmoe-1b7b-q4km-skew-streaming-bs1 (prompt {n_prompt}, {n_pred} greedy "
+                                           f"tokens, budget {budget} of {cfg.n_expert} per layer)",
+                               "policy": policy, "pin_slots": pin, "calibration": "resident trace, different prompt",
+                               "top_quarter_expert_share": skew},
+                    "hits": hits, "misses": misses, "hit_rate": hits / max(1, hits + misses),
+                    "h2d_bytes_per_token": out["h2d_bytes"] / (n_prompt + n_pred - 1),
+                    "tokens_match_resident": out["tokens"] == ref,
+                    "step": "one StreamingGenerate call (prefill token by token + decode), host ids in/out"}
+            print(json.dumps(line), flush=True)
+    sm.close()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -175,8 +238,15 @@ def main() -> None:
                     help="prefill, warm-up, then exactly one timed-step's decode and exit (for ncu launch lists)")
     ap.add_argument("--profile-layers", type=int, default=0,
                     help="with --profile: the same OLMoE-1B-7B width cut to this many layers (small ncu captures)")
+    ap.add_argument("--workload", default="resident", choices=["resident", "streaming"])
+    ap.add_argument("--budgets", type=int, nargs="*", default=[4, 8, 16, 32])
+    ap.add_argument("--stream-tokens", type=int, default=256)
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    if args.workload == "streaming":
+        args.steps = min(args.steps, 3)
+        run_streaming(args)
+        return
     if args.impl == "reference":
         run_reference(args)
         return

@@ -76,6 +76,10 @@ class ExpertSlotCache {
   std::unordered_map<int, int> Ensure(const std::vector<int>& expert_ids);
   // Enqueues the deferred staging -> LRU slot copies on `stream` after the compute.
   int Commit(void* stream);
+  // Starts a new generation with the same slots: empties the LRU part, keeps
+  // the pinned experts (their slots still hold them) and zeroes the counters.
+  // Waits for this cache's copies in flight first.
+  void Restart();
   // Event recorded after the last fill of the latest Ensure (cudaEvent_t).
   void* fills_done_event() const { return fill_event_; }
   // false once a fill failed; the slot involved is left empty.

@@ -35,6 +35,15 @@ class StreamingModel {
   const ExpertHostStore* host_store(int layer) const;
   size_t resident_bytes() const { return bytes_; }
 
+  // Per-layer slot pools of the last StreamingGenerate call and what they
+  // were built for.
+  struct SlotSet {
+    int capacity = 0;
+    SlotPolicy policy = SlotPolicy::kLru;
+    uint32_t pin_slots = 0;
+    std::vector<std::vector<uint32_t>> pinned;
+    std::vector<std::unique_ptr<ExpertSlotCache>> caches;
+  };
   struct Workspace;
   Workspace* workspace() const { return ws_.get(); }
 

@@ -113,7 +113,12 @@ bool UploadTensors(const std::string& path, const GgufFile& g, bool skip_experts
   total += kTailPad;
   void* dev = nullptr;
   if (cudaMalloc(&dev, total) != cudaSuccess) return false;
-  cudaMemset(dev, 0, total);
+  // The uploads below run on a non-blocking stream, which does not order
+  // itself after the legacy stream: finish the zeroing first.
+  if (cudaMemset(dev, 0, total) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+    cudaFree(dev);
+    return false;
+  }
   auto src = TensorSource::Open(path);
   Uploader up;
   bool ok = src != nullptr && up.ok();
@@ -285,6 +290,8 @@ std::unique_ptr<StreamingModel> StreamingModel::Load(const std::string& path, bo
 }
 
 StreamingModel::~StreamingModel() {
+  // The slot pools synchronise on the copy stream when released: free them first.
+  if (ws_ != nullptr) ws_->slots.caches.clear();
   if (ws_ != nullptr && ws_->copy_stream != nullptr) cudaStreamDestroy(ws_->copy_stream);
   ws_.reset();
   if (base_ != nullptr) cudaFree(base_);

@@ -68,7 +68,9 @@ std::unique_ptr<ExpertSlotCache> ExpertSlotCache::Create(const OlmoeConfig& cfg,
     c->base_ = nullptr;
     return nullptr;
   }
-  cudaMemset(c->base_, 0, total);
+  // Zero the pool on the copy stream so that the preload fills below are
+  // ordered after it (the copy stream does not wait for the legacy stream).
+  if (cudaMemsetAsync(c->base_, 0, total, static_cast<cudaStream_t>(c->copy_stream_)) != cudaSuccess) return nullptr;
   uint8_t* p = static_cast<uint8_t*>(c->base_);
   auto init = [&](DTensor& t, const std::string& name, int32_t type, size_t stride, int64_t ne0, int64_t ne1,
                   uint8_t* data) {
@@ -114,6 +116,21 @@ ExpertSlotCache::~ExpertSlotCache() {
   if (fill_event_ != nullptr) cudaEventDestroy(static_cast<cudaEvent_t>(fill_event_));
   if (base_ != nullptr) cudaFree(base_);
   if (bounce_ != nullptr) cudaFreeHost(bounce_);
+}
+
+void ExpertSlotCache::Restart() {
+  if (copy_stream_ != nullptr) cudaStreamSynchronize(static_cast<cudaStream_t>(copy_stream_));
+  else cudaDeviceSynchronize();
+  id_to_slot_.clear();
+  for (size_t s = 0; s < slot_to_id_.size(); ++s) {
+    if (static_cast<int>(s) >= pin_count_) slot_to_id_[s] = -1;
+    slot_tick_[s] = 0;
+  }
+  tick_ = 0;
+  pending_.clear();
+  hits_ = misses_ = 0;
+  h2d_bytes_ = 0;
+  ok_ = true;
 }
 
 // Enqueues the three copies of `expert` into `slot` on the copy stream.
@@ -267,20 +284,42 @@ std::vector<int32_t> StreamingGenerateEx(const StreamingModel& model, const std:
     }
   }
   const int L = static_cast<int>(c.n_layers), K = static_cast<int>(c.n_expert_used);
-  std::vector<std::unique_ptr<ExpertSlotCache>> caches(L);
-  for (int l = 0; l < L; ++l) {
-    SlotCacheOptions so;
-    so.policy = opt.policy;
-    so.usage = opt.usage;
-    so.pin_slots = opt.pin_slots > 0 ? opt.pin_slots : LearnedPinSlots(static_cast<uint32_t>(capacity));
-    so.staging = K;
-    so.copy_stream = ws->copy_stream;
-    caches[l] = ExpertSlotCache::Create(c, l, capacity, model.reader(), model.host_store(l), so);
-    if (caches[l] == nullptr) {
-      stats.status = NH_E_NOMEM;
-      return out;
+  // The slot pools of the previous call are reused when capacity, policy and
+  // pinned set are unchanged: the LRU part restarts empty, the pinned experts
+  // stay loaded.  Otherwise they are released and created anew.
+  const uint32_t pin_slots = opt.pin_slots > 0 ? opt.pin_slots : LearnedPinSlots(static_cast<uint32_t>(capacity));
+  std::vector<std::vector<uint32_t>> pinned;
+  if (opt.policy == SlotPolicy::kLearnedPin && opt.usage != nullptr) {
+    for (int l = 0; l < L; ++l)
+      pinned.push_back(PinnedExperts(*opt.usage, static_cast<uint32_t>(l), std::min<uint32_t>(pin_slots, capacity)));
+  }
+  StreamingModel::SlotSet& set = ws->slots;
+  const bool reuse = set.caches.size() == static_cast<size_t>(L) && set.capacity == capacity &&
+                     set.policy == opt.policy && set.pin_slots == pin_slots && set.pinned == pinned;
+  if (reuse) {
+    for (auto& cache : set.caches) cache->Restart();
+  } else {
+    set.caches.clear();
+    set.capacity = capacity;
+    set.policy = opt.policy;
+    set.pin_slots = pin_slots;
+    set.pinned = pinned;
+    for (int l = 0; l < L; ++l) {
+      SlotCacheOptions so;
+      so.policy = opt.policy;
+      so.usage = opt.usage;
+      so.pin_slots = pin_slots;
+      so.staging = K;
+      so.copy_stream = ws->copy_stream;
+      set.caches.push_back(ExpertSlotCache::Create(c, l, capacity, model.reader(), model.host_store(l), so));
+      if (set.caches.back() == nullptr) {
+        set.caches.clear();
+        stats.status = NH_E_NOMEM;
+        return out;
+      }
     }
   }
+  std::vector<std::unique_ptr<ExpertSlotCache>>& caches = set.caches;
   Engine& e = ws->engine;
   const int P = static_cast<int>(ids.size());
   int rc = e.Reserve(P + n_predict + 1, P, n_predict, false);

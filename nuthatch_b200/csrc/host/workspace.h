@@ -20,6 +20,7 @@ struct StreamingModel::Workspace {
   ModelView view;
   bool view_ok = false;
   cudaStream_t copy_stream = nullptr;
+  SlotSet slots;  // slot pools kept between StreamingGenerate calls
 };
 
 }  // namespace nuthatch

@@ -6,9 +6,12 @@ Named workloads (sizes as stated by the benchmark configurations):
     attn_v/ffn_down Q6_K on odd layers, output Q6_K), weights ~N(0, 0.02),
     norms 1.0, router F32.
   * ``olmoe_1b7b_skew``: the same plus a log-Zipf(s=1.1) router bias baked
-    into the weights (column 0 of every token embedding row is a constant
-    whose normalised value feeds column 0 of the router), for the streaming
-    cache-policy workloads.
+    into the weights (column 0 of every token embedding row is the constant
+    0.3, whose normalised value feeds column 0 of the router with gain 0.03),
+    for the streaming cache-policy workloads.  Random-init weights already
+    route in a strongly token-independent way (without any bias the top
+    quarter of experts takes ~95% of a 48-token trace's selections), so the
+    bias is kept mild; the bench reports the realised skew.
   * ``granite_moe``: 24 layers, n_embd 1024, 16 query heads x 64, 8 KV heads,
     32 experts top-8, expert FFN 512, vocab 49155.
   * ``mini`` / ``mini_f32``: small shapes for parity tests.
@@ -59,7 +62,7 @@ class SynthSpec:
 
 OLMOE_1B7B = SynthSpec(n_layers=16, n_embd=2048, n_head=16, n_head_kv=16, n_ff=1024, n_expert=64,
                        n_expert_used=8, n_vocab=50304, seed=1)
-OLMOE_1B7B_SKEW = replace(OLMOE_1B7B, seed=2, skew_embd=64.0, skew_router=0.25, skew_zipf_s=1.1)
+OLMOE_1B7B_SKEW = replace(OLMOE_1B7B, seed=2, skew_embd=0.3, skew_router=0.03, skew_zipf_s=1.1)
 GRANITE_MOE = SynthSpec(n_layers=24, n_embd=1024, n_head=16, n_head_kv=8, n_ff=512, n_expert=32,
                         n_expert_used=8, n_vocab=49155, seed=5)
 MINI = SynthSpec(n_layers=2, n_embd=512, n_head=4, n_head_kv=4, n_ff=256, n_expert=16, n_expert_used=4,

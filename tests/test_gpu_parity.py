@@ -361,3 +361,31 @@ def test_olmoe_1b7b_resident_decode_matches_oracle(gpu, olmoe_path):
             assert_matches(g["hidden"][:, l], ora["hidden"][:, l], f"layer {l}")
         assert_matches(g["logits"], ora["logits"])
         assert_trace_parity(g["sel"], ora["sel"], ora["gap"])
+
+
+def test_olmoe_streaming_fresh_learned_pin_pools_match_resident(gpu, synth_dir):
+    """Full-width streaming with freshly created learned-pin slot pools (pinned
+    experts preloaded at creation) and with reused pools: tokens equal the
+    resident decode and hit counts are identical across repeats.  Guards the
+    ordering of the pool zeroing before the preload copies."""
+    path = synth.cached(synth.OLMOE_1B7B_SKEW, synth_dir)
+    m = nh.OlmoeModel.Load(str(path))
+    cfg = m.config()
+    cal = nh.RoutingTrace()
+    nh.GreedyGenerateCachedTrace(m, np.random.default_rng(7).integers(0, cfg.n_vocab, 16).tolist(), 16, False, cal)
+    usage = nh.BuildUsage(cal, cfg.n_expert).counts
+    prompt = np.random.default_rng(8).integers(0, cfg.n_vocab, 16).tolist()
+    ref = nh.GreedyGenerateCached(m, prompt, 16, False)
+    del m
+    for cap in (4, 8):
+        pin = (cap * 3 + 3) // 4
+        hits = set()
+        for trial in range(2):  # two freshly loaded models
+            sm = nh.StreamingModel.Load(str(path))
+            for call in range(2):  # the first call creates the pools, the second reuses them
+                r = nh.streaming_generate_ex(sm, prompt, 16, False, cap, policy="learned_pin", pin_slots=pin,
+                                             usage=usage)
+                assert r["tokens"] == ref, (cap, trial, call)
+                hits.add(int(r["hits"].sum()))
+            sm.close()
+        assert len(hits) == 1, (cap, hits)
