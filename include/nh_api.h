@@ -59,6 +59,13 @@ int nh_generate(void* model, int mode, const int32_t* prompt, int n_prompt, int 
 /* Kernel launches per decode step of this model. */
 int nh_generate_launches(const void* model);
 
+/* Batched greedy decode (GreedyGenerateCachedBatch): n_seq prompts of
+ * n_prompt ids each (prompts [n_seq][n_prompt]); writes out_tokens
+ * [n_seq][n_predict] and, when decode_ms is not null, the device time of the
+ * decode part (last prompt position onwards). */
+int nh_generate_batch(void* model, const int32_t* prompts, int n_seq, int n_prompt, int n_predict, int norm_topk,
+                      int use_graph, int32_t* out_tokens, double* decode_ms);
+
 /* Decode replay for timing (no reference counterpart; the reference times
  * whole generate calls).  prepare: runs the prompt's first n_prompt-1
  * positions and saves the cursor (synchronises).  run: restores the cursor

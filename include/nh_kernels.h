@@ -185,6 +185,92 @@ int nh_lm_head_argmax(NhDecodeState* state, const float* h, const float* out_nor
                       const void* w, int32_t tw, int64_t n_embd, int64_t n_vocab,
                       int32_t* out_tokens, float* logits_dump, void* scratch, void* stream);
 
+/* ---- batched decode: B sequences advanced one position per step in lockstep
+ * (the batched form of GreedyGenerateCached, generate.cc:55-106, for
+ * independent sequences of equal prompt length).  The shared cursor
+ * NhDecodeState.pos is the position every sequence is at.  Per token the
+ * arithmetic equals the batch-1 kernels', so each sequence's ids equal a
+ * batch-1 decode of it.  Q8 activation rows are K/256 blocks of 304 bytes
+ * (int8 quants[256] in element order, int16 sums[16], f32 scale, padding). */
+
+/* Bytes of a Q8 activation buffer of `rows` rows of n values. */
+int64_t nh_batch_q8_bytes(int64_t rows, int64_t n);
+
+/* h[b] = embedding row of sequence b's token at state->pos (prompts
+ * [n_seq][n_prompt], later the fed-back id fed[b]). */
+int nh_batch_embed(const NhDecodeState* state, const int32_t* prompts, int n_prompt, const int32_t* fed,
+                   int n_seq, const void* table, int32_t type, int64_t n_embd, int64_t n_vocab, float* h,
+                   void* stream);
+
+/* Per row r < rows of x (row stride x_stride floats): optional RMSNorm * norm_w
+ * (do_norm), then Q8_K into q8 (may be null) and the normalised f32 row into
+ * xn (may be null; [rows][n]). */
+int nh_batch_prep(const float* x, int64_t x_stride, int64_t rows, const float* norm_w, float eps, int do_norm,
+                  int64_t n, void* q8, float* xn, void* stream);
+
+#define NH_ROWDOT_STORE 0    /* out[o][row] = W.x */
+#define NH_ROWDOT_RESIDUAL 1 /* out[o][row] += W.x */
+#define NH_ROWDOT_SWIGLU 2   /* out[o][row] = silu(W.x) * (W2.x) */
+
+/* Grouped row dots over Q4_K/Q6_K matrices of n <= 2048 columns (ggml_mul_mat
+ * and, with groups, mul_mat_id, moe.cc:41-50).  Group e multiplies matrix
+ * w + e*mstride (rows x n) with tokens j in [off[e], off[e]+cnt[e]): token j
+ * reads Q8 row act_idx[j] and writes output row out_idx[j].  With off null
+ * there is one group over tokens 0..n_tok-1 (identity indices).  max_tokens
+ * bounds any group's token count. */
+typedef struct NhGroupedRowDot {
+  const void* w;
+  const void* w2;
+  uint64_t mstride, mstride2;
+  int32_t type, type2;
+  int64_t n, rows;
+  int32_t n_groups;
+  const int32_t* off;
+  const int32_t* cnt;
+  const int32_t* act_idx;
+  const int32_t* out_idx;
+  int32_t n_tok, max_tokens;
+  const void* q8;
+  float* out;
+  int64_t out_stride;
+  int32_t mode;
+} NhGroupedRowDot;
+int nh_batch_rowdot(const NhGroupedRowDot* g, void* stream);
+
+/* Per sequence: QK-norm over the full q/k width, NEOX RoPE at state->pos,
+ * rotated q into qr [n_seq][n_head*head_dim], and the new K/V rows appended to
+ * the caches ([n_seq][max_seq][n_head_kv*head_dim] per layer). */
+int nh_batch_qk(const NhDecodeState* state, const float* q, const float* k, const float* v, const float* q_norm,
+                const float* k_norm, float eps, int n_seq, int n_head, int n_head_kv, int head_dim,
+                const float* rope_cs, float* k_cache, float* v_cache, int max_seq, float* qr, void* stream);
+
+/* Attention of every sequence over positions 0..state->pos in 64-position
+ * splits combined in order (the batch-1 kernel's arithmetic).  `scratch`:
+ * nh_batch_attention_scratch_bytes() bytes, zeroed once. */
+int64_t nh_batch_attention_scratch_bytes(int n_seq, int n_head, int head_dim, int max_seq);
+int nh_batch_attention(const NhDecodeState* state, const float* qr, int n_seq, int n_head, int n_head_kv,
+                       int head_dim, float kq_scale, const float* k_cache, const float* v_cache, int max_seq,
+                       void* scratch, float* out, void* stream);
+
+/* Router per token from the normalised rows xn [n_seq][n_embd]: sel/wts
+ * [n_seq][k] as nh_router_topk. */
+int nh_batch_router(const float* xn, const float* router, int n_seq, int64_t n_embd, int n_expert, int k,
+                    int norm_topk, int32_t* sel, float* wts, void* stream);
+
+/* Per-expert token lists of sel [n_seq][k] in (token, slot) order: off/cnt
+ * [n_expert], act_idx[j] = token, out_idx[j] = token*k + slot. */
+int nh_batch_moe_plan(const int32_t* sel, int n_seq, int k, int n_expert, int32_t* off, int32_t* cnt,
+                      int32_t* act_idx, int32_t* out_idx, void* stream);
+
+/* h[b] += sum_i wts[b][i] * y[b*k+i] (products rounded, top-k order). */
+int nh_batch_combine(const float* y, const float* wts, int n_seq, int k, int64_t n_embd, float* h, void* stream);
+
+/* Greedy ids from logits [n_seq][n_vocab] (first maximum); from the last
+ * prompt position on writes out_tokens[b][pos-n_prompt+1] and fed[b]; the
+ * last CTA advances state->pos.  scratch: 64 zeroed bytes. */
+int nh_batch_argmax(NhDecodeState* state, const float* logits, int n_seq, int64_t n_vocab, int32_t* fed,
+                    int32_t* out_tokens, int n_predict, void* scratch, void* stream);
+
 /* ---- standalone forms used by the parity tests ---- */
 
 /* y[r] = (W . x)[r] for r < rows (ggml_mul_mat for one activation row); when

@@ -46,6 +46,20 @@ std::vector<int32_t> GreedyGenerateCachedTrace(const OlmoeModel& model, std::vec
 std::vector<int32_t> GreedyGenerateCachedEx(const OlmoeModel& model, const std::vector<int32_t>& ids,
                                             int n_predict, bool norm_topk, GenerateOptions* opt);
 
+// Batched greedy decode (no reference counterpart: the batched overload the
+// boundary needs for many independent sequences).  All prompts must have the
+// same length; each sequence advances one position per step in lockstep with
+// its own KV cache, and its ids equal GreedyGenerateCached on it alone.
+struct BatchOptions {
+  bool use_graph = true;  // replay a captured CUDA graph per step
+  double decode_ms = 0;   // out: device time from the last prompt position to the end
+  int status = 0;         // out: NH_OK or the first error code
+};
+std::vector<std::vector<int32_t>> GreedyGenerateCachedBatch(const OlmoeModel& model,
+                                                            const std::vector<std::vector<int32_t>>& prompts,
+                                                            int n_predict, bool norm_topk,
+                                                            BatchOptions* opt = nullptr);
+
 }  // namespace nuthatch
 
 #endif  // NUTHATCH_B200_GENERATE_H_

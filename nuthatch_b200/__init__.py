@@ -196,6 +196,27 @@ def GreedyGenerateCachedTrace(model: OlmoeModel, ids: Sequence[int], n_predict: 
     return r["tokens"]
 
 
+def generate_batch_ex(model: OlmoeModel, prompts: Sequence[Sequence[int]], n_predict: int, norm_topk: bool,
+                      use_graph: bool = True) -> dict:
+    """Batched greedy decode of equal-length prompts; ids per sequence and the
+    device time of the decode part."""
+    p = np.ascontiguousarray(np.asarray(prompts, dtype=np.int32))
+    if p.ndim != 2:
+        raise ValueError("prompts must all have the same length")
+    n_seq, n_prompt = p.shape
+    out = np.zeros((n_seq, n_predict), dtype=np.int32)
+    ms = C.c_double(0.0)
+    _check(lib().nh_generate_batch(model._h, _ptr(p, C.c_int32), n_seq, n_prompt, n_predict, int(norm_topk),
+                                   int(use_graph), _ptr(out, C.c_int32), C.byref(ms)), "nh_generate_batch")
+    return {"tokens": out.tolist(), "decode_ms": ms.value}
+
+
+def GreedyGenerateCachedBatch(model: OlmoeModel, prompts: Sequence[Sequence[int]], n_predict: int,
+                              norm_topk: bool) -> list[list[int]]:
+    """Each sequence's n_predict greedy ids; equal to GreedyGenerateCached on it alone."""
+    return generate_batch_ex(model, prompts, n_predict, norm_topk)["tokens"]
+
+
 class StreamingModel:
     """Non-expert weights in HBM, experts in pinned host memory (streaming_model.h:17-44)."""
 

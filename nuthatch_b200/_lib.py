@@ -41,6 +41,10 @@ SIGNATURES = {
     "nh_generate": (C.c_int, [vp, C.c_int, P(i32), C.c_int, C.c_int, C.c_int, C.c_int, P(i32), P(i32), P(f32),
                               P(f32), P(f32)]),
     "nh_generate_launches": (C.c_int, [vp]),
+    "nh_generate_batch": (C.c_int, [vp, P(i32), C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, P(i32),
+                                    P(C.c_double)]),
+    "nh_batch_q8_bytes": (i64, [i64, i64]),
+    "nh_batch_attention_scratch_bytes": (i64, [C.c_int, C.c_int, C.c_int, C.c_int]),
     "nh_decode_prepare": (C.c_int, [vp, P(i32), C.c_int, C.c_int]),
     "nh_decode_run": (C.c_int, [vp, C.c_int]),
     "nh_decode_result": (C.c_int, [vp, C.c_int, P(i32)]),

@@ -149,6 +149,29 @@ int nh_generate_launches(const void* model) {
   return 2 + 6 * static_cast<int>(static_cast<const OlmoeModel*>(model)->config().n_layers);
 }
 
+int nh_generate_batch(void* model, const int32_t* prompts, int n_seq, int n_prompt, int n_predict, int norm_topk,
+                      int use_graph, int32_t* out_tokens, double* decode_ms) {
+  if (model == nullptr || prompts == nullptr || out_tokens == nullptr || n_seq <= 0 || n_prompt <= 0 ||
+      n_predict <= 0) {
+    SetErr("nh_generate_batch: bad argument");
+    return NH_E_ARG;
+  }
+  std::vector<std::vector<int32_t>> p(n_seq);
+  for (int b = 0; b < n_seq; ++b)
+    p[b].assign(prompts + static_cast<size_t>(b) * n_prompt, prompts + static_cast<size_t>(b + 1) * n_prompt);
+  BatchOptions o;
+  o.use_graph = use_graph != 0;
+  const auto ids = GreedyGenerateCachedBatch(*static_cast<const OlmoeModel*>(model), p, n_predict, norm_topk != 0, &o);
+  if (o.status != NH_OK) {
+    SetErr("nh_generate_batch: failed with code " + std::to_string(o.status));
+    return o.status;
+  }
+  for (int b = 0; b < n_seq; ++b)
+    std::memcpy(out_tokens + static_cast<size_t>(b) * n_predict, ids[b].data(), static_cast<size_t>(n_predict) * 4);
+  if (decode_ms != nullptr) *decode_ms = o.decode_ms;
+  return NH_OK;
+}
+
 int nh_decode_prepare(void* model, const int32_t* prompt, int n_prompt, int n_predict) {
   if (model == nullptr || prompt == nullptr || n_prompt <= 0 || n_predict <= 0) return NH_E_ARG;
   OlmoeModel::Workspace* ws = static_cast<OlmoeModel*>(model)->workspace();

@@ -1,0 +1,906 @@
+// Batched greedy decode: B independent sequences advanced one position per
+// step in lockstep (configuration 3 of the benchmarks: 64 sequences).
+//
+// Per token the arithmetic is exactly that of the batch-1 kernels (the same
+// Q8_K quantisation, super-block dots and butterfly tree, attention splits,
+// softmax, top-k and top-k-order combine), so every sequence's ids equal
+// those of a batch-1 decode of it.  What changes is the work layout:
+//  * activations are prepared once per token (RMS, norm weight, Q8_K) into a
+//    global Q8 buffer by batch_prep_kernel, instead of once per CTA;
+//  * one grouped row-dot kernel serves QKV, the output projection, the
+//    per-expert gate/up and down projections (each expert over the list of
+//    tokens routed to it) and lm_head: a warp pass covers 32/G rows x one
+//    token, the Q4_K weight super-block stays in registers while the warp
+//    walks the CTA's tokens, and the tokens' Q8_K blocks are staged in
+//    shared memory;
+//  * QK-norm, RoPE and the KV append run once per sequence, then attention
+//    runs over (head, 64-position split, sequence) CTAs.
+//
+// Q8 global block layout (kQ8Stride bytes per 256 values): int8 qs[256] in
+// element order, int16 bsums[16], f32 d, padding.
+#include <climits>
+#include <cstring>
+
+#include "launch.cuh"
+#include "rowdot3.cuh"
+
+namespace nh {
+
+constexpr int kQ8Stride = 304;
+constexpr int kBatchWarps = 8;
+constexpr int kBatchTokTile = 32;  // tokens staged per CTA
+constexpr int kBMaxTopK = 32;
+
+// ---------------------------------------------------------------- embed
+__global__ void batch_embed_kernel(const NhDecodeState* state, const int32_t* prompts, int n_prompt,
+                                   const int32_t* fed, const uint8_t* table, int type, int n_embd, int n_vocab,
+                                   uint64_t rb, float* h) {
+  const int b = blockIdx.x;
+  __shared__ int s_tok;
+  pdl_wait();
+  pdl_trigger();
+  if (threadIdx.x == 0) {
+    const int pos = state->pos;
+    int tok = pos < n_prompt ? prompts[static_cast<int64_t>(b) * n_prompt + pos] : fed[b];
+    if (tok < 0 || tok >= n_vocab) {
+      atomicCAS(const_cast<int32_t*>(&state->error), 0, NH_E_ARG);
+      tok = 0;
+    }
+    s_tok = tok;
+  }
+  __syncthreads();
+  const uint8_t* row = table + static_cast<uint64_t>(s_tok) * rb;
+  float* out = h + static_cast<int64_t>(b) * n_embd;
+  for (int i = threadIdx.x; i < n_embd; i += blockDim.x) {
+    if (type == NH_TYPE_F32) {
+      out[i] = reinterpret_cast<const float*>(row)[i];
+    } else {
+      // Same element formulas as the batch-1 embedding (dequantize_row_*).
+      const int64_t blk = i / QK;
+      const int e = i % QK;
+      if (type == NH_TYPE_Q4_K) {
+        const uint8_t* q = row + blk * kQ4KBytes;
+        const float d = half_bits_to_float(q[0] | (q[1] << 8));
+        const float dmin = half_bits_to_float(q[2] | (q[3] << 8));
+        const int j = e / 32, c = j / 2;
+        int sc, m;
+        q4k_scale_min(q + 4, j, sc, m);
+        const uint8_t byte = q[16 + 32 * c + (e % 32)];
+        const int v = (j & 1) ? (byte >> 4) : (byte & 15);
+        out[i] = __fsub_rn(__fmul_rn(__fmul_rn(d, static_cast<float>(sc)), static_cast<float>(v)),
+                           __fmul_rn(dmin, static_cast<float>(m)));
+      } else {
+        const uint8_t* q = row + blk * kQ6KBytes;
+        const float d = half_bits_to_float(q[208] | (q[209] << 8));
+        const int hh = e / 128, ee = e % 128;
+        const int lo = ee < 64 ? (q[64 * hh + ee] & 15) : (q[64 * hh + ee - 64] >> 4);
+        const int hi = (q[128 + 32 * hh + ee % 32] >> (2 * (ee / 32))) & 3;
+        const int v = (lo | (hi << 4)) - 32;
+        const int8_t sc = static_cast<int8_t>(q[192 + e / 16]);
+        out[i] = __fmul_rn(__fmul_rn(d, static_cast<float>(sc)), static_cast<float>(v));
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- prep
+// One CTA per token row: x (optionally RMS-normalised and multiplied by
+// norm_w) quantised to Q8_K blocks in global memory; xn (optional) receives
+// the normalised f32 row.
+__global__ void __launch_bounds__(256) batch_prep_kernel(const float* x, int64_t x_stride, const float* norm_w,
+                                                         float eps, int do_norm, int K, uint8_t* q8, float* xn) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ double red[48];
+  ActSmem a = carve_act(smem, K, true, norm_w != nullptr && do_norm);
+  act_load_norm(a, do_norm ? norm_w : nullptr);
+  pdl_wait();
+  pdl_trigger();
+  const int r = blockIdx.x;
+  prep_act(a, x + r * x_stride, norm_w != nullptr, do_norm != 0, eps, q8 != nullptr, red);
+  const int nb = K / QK;
+  if (q8 != nullptr) {
+    uint8_t* dst = q8 + static_cast<int64_t>(r) * nb * kQ8Stride;
+    for (int i = threadIdx.x; i < nb * QK; i += blockDim.x) {
+      const int b = i / QK, L = i % QK;
+      dst[b * kQ8Stride + L] = static_cast<uint8_t>(a.qs[q8_off(b, L)]);
+    }
+    for (int i = threadIdx.x; i < nb * 16; i += blockDim.x)
+      reinterpret_cast<int16_t*>(dst + (i / 16) * kQ8Stride + 256)[i % 16] = a.bsums[i];
+    for (int b = threadIdx.x; b < nb; b += blockDim.x) *reinterpret_cast<float*>(dst + b * kQ8Stride + 288) = a.d[b];
+  }
+  if (xn != nullptr)
+    for (int i = threadIdx.x; i < K; i += blockDim.x) xn[static_cast<int64_t>(r) * K + i] = a.xf[i];
+}
+
+// ---------------------------------------------------------------- grouped row dots
+// Super-block dots against a Q8 block in shared memory (element-order quants,
+// 16-byte loads).  Q4_K: the weight super-block is held in registers.
+struct WQ4 {
+  uint4 hdr;
+  uint4 q[8];
+};
+
+__device__ __forceinline__ void load_wq4(WQ4& w, const uint8_t* blk) {
+  const uint4* p = reinterpret_cast<const uint4*>(blk);
+  w.hdr = __ldg(p);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) w.q[i] = __ldg(p + 1 + i);
+}
+
+__device__ __forceinline__ float dot_q4k_w(const WQ4& w, const uint8_t* ab) {
+  const uint32_t sc0 = w.hdr.y & 0x3F3F3F3Fu;
+  const uint32_t m0 = w.hdr.z & 0x3F3F3F3Fu;
+  const uint32_t sc1 = (w.hdr.w & 0x0F0F0F0Fu) | ((w.hdr.y >> 2) & 0x30303030u);
+  const uint32_t m1 = ((w.hdr.w >> 4) & 0x0F0F0F0Fu) | ((w.hdr.z >> 2) & 0x30303030u);
+  const uint32_t m4 = 0x0F0F0F0Fu;
+  int sumi = 0;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const int4 xa = *reinterpret_cast<const int4*>(ab + 64 * c);
+    const int4 xb = *reinterpret_cast<const int4*>(ab + 64 * c + 16);
+    const int4 xc = *reinterpret_cast<const int4*>(ab + 64 * c + 32);
+    const int4 xd = *reinterpret_cast<const int4*>(ab + 64 * c + 48);
+    const uint4 w0 = w.q[2 * c], w1 = w.q[2 * c + 1];
+    int lo = 0, hi = 0;
+    lo = __dp4a(static_cast<int>(w0.x & m4), xa.x, lo);
+    lo = __dp4a(static_cast<int>(w0.y & m4), xa.y, lo);
+    lo = __dp4a(static_cast<int>(w0.z & m4), xa.z, lo);
+    lo = __dp4a(static_cast<int>(w0.w & m4), xa.w, lo);
+    lo = __dp4a(static_cast<int>(w1.x & m4), xb.x, lo);
+    lo = __dp4a(static_cast<int>(w1.y & m4), xb.y, lo);
+    lo = __dp4a(static_cast<int>(w1.z & m4), xb.z, lo);
+    lo = __dp4a(static_cast<int>(w1.w & m4), xb.w, lo);
+    hi = __dp4a(static_cast<int>((w0.x >> 4) & m4), xc.x, hi);
+    hi = __dp4a(static_cast<int>((w0.y >> 4) & m4), xc.y, hi);
+    hi = __dp4a(static_cast<int>((w0.z >> 4) & m4), xc.z, hi);
+    hi = __dp4a(static_cast<int>((w0.w >> 4) & m4), xc.w, hi);
+    hi = __dp4a(static_cast<int>((w1.x >> 4) & m4), xd.x, hi);
+    hi = __dp4a(static_cast<int>((w1.y >> 4) & m4), xd.y, hi);
+    hi = __dp4a(static_cast<int>((w1.z >> 4) & m4), xd.z, hi);
+    hi = __dp4a(static_cast<int>((w1.w >> 4) & m4), xd.w, hi);
+    const uint32_t scw = c < 2 ? sc0 : sc1;
+    sumi += byte_of(scw, (2 * c) & 3) * lo + byte_of(scw, (2 * c + 1) & 3) * hi;
+  }
+  const int4 bs0 = *reinterpret_cast<const int4*>(ab + 256);
+  const int4 bs1 = *reinterpret_cast<const int4*>(ab + 272);
+  const int bsw[8] = {bs0.x, bs0.y, bs0.z, bs0.w, bs1.x, bs1.y, bs1.z, bs1.w};
+  int summ = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) summ += byte_of(j < 4 ? m0 : m1, j & 3) * (lo16(bsw[j]) + hi16(bsw[j]));
+  const float yd = *reinterpret_cast<const float*>(ab + 288);
+  const float d = half_bits_to_float(w.hdr.x), dmin = half_bits_to_float(w.hdr.x >> 16);
+  return __fsub_rn(__fmul_rn(__fmul_rn(d, yd), static_cast<float>(sumi)),
+                   __fmul_rn(__fmul_rn(dmin, yd), static_cast<float>(summ)));
+}
+
+// Q6_K: the weight super-block (2-byte aligned, global memory, L1 cached)
+// against a shared Q8 block.
+__device__ __forceinline__ float dot_q6k_g(const uint8_t* blk, const uint8_t* ab) {
+  const uintptr_t addr = reinterpret_cast<uintptr_t>(blk);
+  const uint32_t* base = reinterpret_cast<const uint32_t*>(addr & ~static_cast<uintptr_t>(3));
+  const uint32_t sh = static_cast<uint32_t>(addr & 3) * 8;
+  auto word = [&](int i) { return __funnelshift_r(__ldg(base + i), __ldg(base + i + 1), sh); };
+  const int* x = reinterpret_cast<const int*>(ab);
+  const uint32_t m4 = 0x0F0F0F0Fu, m2 = 0x30303030u;
+  const uint32_t scw[4] = {word(48), word(49), word(50), word(51)};
+  const int4 bs0 = *reinterpret_cast<const int4*>(ab + 256);
+  const int4 bs1 = *reinterpret_cast<const int4*>(ab + 272);
+  const int bsw[8] = {bs0.x, bs0.y, bs0.z, bs0.w, bs1.x, bs1.y, bs1.z, bs1.w};
+  int sumi = 0;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      int g1 = 0, g2 = 0, g3 = 0, g4 = 0;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const int k = 4 * half + kk;
+        const uint32_t A = word(16 * h + k), B = word(16 * h + 8 + k), H = word(32 + 8 * h + k);
+        g1 = __dp4a(static_cast<int>((A & m4) | ((H << 4) & m2)), x[32 * h + k], g1);
+        g2 = __dp4a(static_cast<int>((B & m4) | ((H << 2) & m2)), x[32 * h + 8 + k], g2);
+        g3 = __dp4a(static_cast<int>(((A >> 4) & m4) | (H & m2)), x[32 * h + 16 + k], g3);
+        g4 = __dp4a(static_cast<int>(((B >> 4) & m4) | ((H >> 2) & m2)), x[32 * h + 24 + k], g4);
+      }
+      const int gs[4] = {g1, g2, g3, g4};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int g = 8 * h + half + 2 * t;
+        const int sc = static_cast<int>(static_cast<int8_t>((scw[g >> 2] >> (8 * (g & 3))) & 0xFF));
+        const int bsum = (g & 1) ? hi16(bsw[g >> 1]) : lo16(bsw[g >> 1]);
+        sumi += sc * (gs[t] - 32 * bsum);
+      }
+    }
+  }
+  const float yd = *reinterpret_cast<const float*>(ab + 288);
+  return __fmul_rn(__fmul_rn(half_bits_to_float(word(52)), yd), static_cast<float>(sumi));
+}
+
+// Epilogues of the grouped row-dot kernel.
+enum GroupMode : int { kStore = 0, kResidual = 1, kSwiGLU = 2 };
+
+// Work: n_groups groups; group e multiplies matrix e (base + e * mstride,
+// `rows` rows of rb bytes; for SwiGLU a second matrix w2 gives the up rows)
+// with the tokens j in [off[e], off[e] + cnt[e]): token j reads Q8 activation
+// row act_idx[j] and writes out[out_idx[j] * out_stride + row].  Without
+// lists (off null) there is one group over tokens 0 .. n_tok-1.
+// blockIdx.x = group * row_blocks + row block; blockIdx.y = token tile.
+struct GroupArgs {
+  const uint8_t* w;
+  const uint8_t* w2;
+  uint64_t mstride, mstride2;
+  int type, type2;
+  int K, rows, rows_per_block;
+  uint64_t rb, rb2;
+  int n_groups, row_blocks;
+  const int32_t* off;
+  const int32_t* cnt;
+  const int32_t* act_idx;
+  const int32_t* out_idx;
+  int n_tok;
+  const uint8_t* q8;  // [activation rows][K/256] blocks of kQ8Stride bytes
+  float* out;
+  int64_t out_stride;
+  int mode;
+};
+
+__global__ void __launch_bounds__(kBatchWarps * 32) batch_rowdot_kernel(const GroupArgs p) {
+  extern __shared__ __align__(128) uint8_t smem[];  // [kBatchTokTile][K/256][kQ8Stride]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nb = p.K / QK, G = nb, P = 32 / G;
+  const int e = blockIdx.x / p.row_blocks, rblk = blockIdx.x % p.row_blocks;
+  pdl_wait();
+  pdl_trigger();
+  const int t_off = p.off != nullptr ? p.off[e] : 0;
+  const int t_cnt = p.off != nullptr ? p.cnt[e] : p.n_tok;
+  const int t0 = blockIdx.y * kBatchTokTile;
+  const int nt = min(kBatchTokTile, t_cnt - t0);
+  if (nt <= 0) return;
+  // Stage this tile's activation rows (16-byte copies).
+  const int blk_bytes = nb * kQ8Stride, n16 = blk_bytes / 16;
+  for (int q = threadIdx.x; q < nt * n16; q += blockDim.x) {
+    const int t = q / n16, part = q % n16;
+    const int a = p.act_idx != nullptr ? p.act_idx[t_off + t0 + t] : t0 + t;
+    reinterpret_cast<uint4*>(smem + t * blk_bytes)[part] =
+        reinterpret_cast<const uint4*>(p.q8 + static_cast<int64_t>(a) * blk_bytes)[part];
+  }
+  __syncthreads();
+  const int g = lane % G, r = lane / G;
+  const uint8_t* W = p.w + static_cast<uint64_t>(e) * p.mstride;
+  const uint8_t* W2 = p.w2 != nullptr ? p.w2 + static_cast<uint64_t>(e) * p.mstride2 : nullptr;
+  const int row_beg = rblk * p.rows_per_block;
+  const int row_end = min(p.rows, row_beg + p.rows_per_block);
+  // Warps take passes of P rows; every pass walks all staged tokens with the
+  // lane's weight super-block held in registers (Q4_K).
+  for (int row0 = row_beg + warp * P; row0 < row_end; row0 += kBatchWarps * P) {
+    const int row = row0 + r;
+    const bool live = row < row_end;
+    const int rr = live ? row : row_end - 1;
+    const uint8_t* sb = W + static_cast<uint64_t>(rr) * p.rb + g * (p.type == NH_TYPE_Q4_K ? kQ4KBytes : kQ6KBytes);
+    const uint8_t* sb2 =
+        W2 != nullptr ? W2 + static_cast<uint64_t>(rr) * p.rb2 + g * (p.type2 == NH_TYPE_Q4_K ? kQ4KBytes : kQ6KBytes)
+                      : nullptr;
+    WQ4 wq, wq2;
+    if (p.type == NH_TYPE_Q4_K) load_wq4(wq, sb);
+    if (sb2 != nullptr && p.type2 == NH_TYPE_Q4_K) load_wq4(wq2, sb2);
+    for (int t = 0; t < nt; ++t) {
+      const uint8_t* ab = smem + t * blk_bytes + g * kQ8Stride;
+      float v = p.type == NH_TYPE_Q4_K ? dot_q4k_w(wq, ab) : dot_q6k_g(sb, ab);
+      for (int o = 1; o < G; o <<= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+      float v2 = 0.f;
+      if (sb2 != nullptr) {
+        v2 = p.type2 == NH_TYPE_Q4_K ? dot_q4k_w(wq2, ab) : dot_q6k_g(sb2, ab);
+        for (int o = 1; o < G; o <<= 1) v2 = __fadd_rn(v2, __shfl_xor_sync(0xffffffffu, v2, o));
+      }
+      if (g == 0 && live) {
+        const int o = p.out_idx != nullptr ? p.out_idx[t_off + t0 + t] : t0 + t;
+        float* dst = p.out + static_cast<int64_t>(o) * p.out_stride + row;
+        if (p.mode == kStore) {
+          *dst = v;
+        } else if (p.mode == kResidual) {
+          *dst = __fadd_rn(*dst, v);
+        } else {
+          // silu(gate) * up, as the batch-1 gate/up kernel forms it.
+          const float s = __fdiv_rn(v, __fadd_rn(1.0f, exp_cw(-v)));
+          *dst = __fmul_rn(s, v2);
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- QK-norm, RoPE, KV append
+// One CTA per sequence: QK-norm over the full q (and k) width, NEOX RoPE at
+// the shared position, the rotated q to qr, and the new K (rotated) and V
+// rows appended to the sequence's cache ([B][max_seq][n_embd_kv] per layer).
+__global__ void __launch_bounds__(128) batch_qk_kernel(const NhDecodeState* state, const float* q, const float* k,
+                                                       const float* v, const float* q_norm, const float* k_norm,
+                                                       float eps, int n_head, int n_head_kv, int hd,
+                                                       const float* rope_cs, float* k_cache, float* v_cache,
+                                                       int max_seq, float* qr) {
+  const int b = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
+  const int dq = n_head * hd, dkv = n_head_kv * hd, half = hd / 2;
+  __shared__ double red[16];
+  pdl_wait();
+  pdl_trigger();
+  const int pos = state->pos;
+  const float* qb = q + static_cast<int64_t>(b) * dq;
+  const float* kb = k + static_cast<int64_t>(b) * dkv;
+  double sq = 0.0, sk = 0.0;
+  for (int i = tid; i < dq; i += blockDim.x) sq += static_cast<double>(__fmul_rn(qb[i], qb[i]));
+  for (int i = tid; i < dkv; i += blockDim.x) sk += static_cast<double>(__fmul_rn(kb[i], kb[i]));
+  sq = warp_sum_d(sq);
+  sk = warp_sum_d(sk);
+  if (lane == 0) {
+    red[warp] = sq;
+    red[8 + warp] = sk;
+  }
+  __syncthreads();
+  double tq = 0.0, tk = 0.0;
+  for (int w = 0; w < nw; ++w) {
+    tq += red[w];
+    tk += red[8 + w];
+  }
+  const float scq = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(tq / static_cast<double>(dq)), eps)));
+  const float sck = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(tk / static_cast<double>(dkv)), eps)));
+  const float* cs = rope_cs + static_cast<int64_t>(pos) * hd;
+  float* qo = qr + static_cast<int64_t>(b) * dq;
+  for (int j = tid; j < n_head * half; j += blockDim.x) {
+    const int h = j / half, i = j % half;
+    const float c = cs[2 * i], s = cs[2 * i + 1];
+    const float x0 = __fmul_rn(__fmul_rn(qb[h * hd + i], scq), q_norm[h * hd + i]);
+    const float x1 = __fmul_rn(__fmul_rn(qb[h * hd + i + half], scq), q_norm[h * hd + i + half]);
+    qo[h * hd + i] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+    qo[h * hd + i + half] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+  }
+  float* kd = k_cache + (static_cast<int64_t>(b) * max_seq + pos) * dkv;
+  float* vd = v_cache + (static_cast<int64_t>(b) * max_seq + pos) * dkv;
+  for (int j = tid; j < n_head_kv * half; j += blockDim.x) {
+    const int h = j / half, i = j % half;
+    const float c = cs[2 * i], s = cs[2 * i + 1];
+    const float x0 = __fmul_rn(__fmul_rn(kb[h * hd + i], sck), k_norm[h * hd + i]);
+    const float x1 = __fmul_rn(__fmul_rn(kb[h * hd + i + half], sck), k_norm[h * hd + i + half]);
+    kd[h * hd + i] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+    kd[h * hd + i + half] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+  }
+  const float* vb = v + static_cast<int64_t>(b) * dkv;
+  for (int i = tid; i < dkv; i += blockDim.x) vd[i] = vb[i];
+}
+
+// ---------------------------------------------------------------- attention
+constexpr int kBAttnThreads = 128;
+constexpr int kBAttnSplit = 64;
+
+// The thread-per-position score of the batch-1 attention kernel (the same
+// lane-strided sums and butterfly tree).
+__device__ __forceinline__ float bscore_thread(const float* kr, const float* q, int hd) {
+  float part[32];
+#pragma unroll
+  for (int l = 0; l < 32; ++l) part[l] = 0.f;
+  for (int base = 0; base < hd; base += 32) {
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      const float4 kv = *reinterpret_cast<const float4*>(kr + base + 4 * t);
+      const float4 qv = *reinterpret_cast<const float4*>(q + base + 4 * t);
+      part[4 * t + 0] = __fadd_rn(part[4 * t + 0], __fmul_rn(kv.x, qv.x));
+      part[4 * t + 1] = __fadd_rn(part[4 * t + 1], __fmul_rn(kv.y, qv.y));
+      part[4 * t + 2] = __fadd_rn(part[4 * t + 2], __fmul_rn(kv.z, qv.z));
+      part[4 * t + 3] = __fadd_rn(part[4 * t + 3], __fmul_rn(kv.w, qv.w));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+    for (int l = 0; l < o; ++l) part[l] = __fadd_rn(part[l], part[l + o]);
+  }
+  return part[0];
+}
+
+struct BAttnArgs {
+  NhDecodeState* state;
+  const float* qr;
+  const float* k_cache;
+  const float* v_cache;
+  int n_head, n_head_kv, hd, max_seq, n_split;
+  float kq_scale;
+  unsigned* tickets;  // [B][n_head]
+  double* part_l;     // [B][n_head][n_split]
+  float* part_m;
+  float* part_acc;    // [B][n_head][n_split][hd]
+  float* out;         // [B][n_head*hd]
+};
+
+__global__ void __launch_bounds__(kBAttnThreads) batch_attention_kernel(const BAttnArgs p) {
+  const int h = blockIdx.x, sp = blockIdx.y, b = blockIdx.z;
+  const int pos = *reinterpret_cast<volatile const int*>(&p.state->pos);
+  const int n_kv = pos + 1;
+  const int n_active = (n_kv + kBAttnSplit - 1) / kBAttnSplit;
+  if (sp >= n_active) return;
+  extern __shared__ __align__(128) float sm[];
+  const int hd = p.hd, kst = hd + 4;
+  float* Ks = sm;
+  float* Vs = Ks + kBAttnSplit * kst;
+  float* qh = Vs + kBAttnSplit * hd;
+  float* sc = qh + hd;
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ double red[8];
+  __shared__ float s_max[4];
+  __shared__ bool s_last;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
+  const int kh = h / (p.n_head / p.n_head_kv);
+  const int dq = p.n_head * hd, dkv = p.n_head_kv * hd;
+  const int p0 = sp * kBAttnSplit;
+  const int n = min(n_kv, p0 + kBAttnSplit) - p0;
+  const uint32_t row = static_cast<uint32_t>(hd) * 4;
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_trigger();
+  // Every row of the range, including the current position, is in the cache.
+  if (tid == 0) mbar_expect_tx(&bar, 2u * row * static_cast<uint32_t>(n));
+  __syncthreads();
+  {
+    const int j = tid & (kBAttnSplit - 1);
+    if (j < n) {
+      const int64_t g = (static_cast<int64_t>(b) * p.max_seq + p0 + j) * dkv + kh * hd;
+      if (tid < kBAttnSplit) bulk_g2s(Ks + j * kst, p.k_cache + g, row, &bar);
+      else bulk_g2s(Vs + j * hd, p.v_cache + g, row, &bar);
+    }
+  }
+  copy_to_smem(qh, p.qr + static_cast<int64_t>(b) * dq + h * hd, hd);
+  const bool ok = mbar_wait(&bar, 0);
+  if (!ok && tid == 0) atomicCAS(&p.state->error, 0, NH_E_TIMEOUT);
+  __syncthreads();
+  float my = -INFINITY;
+  if ((hd & 31) == 0) {
+    if (tid < n) {
+      const float d = bscore_thread(Ks + tid * kst, qh, hd);
+      my = ok ? __fmul_rn(d, p.kq_scale) : 0.f;
+    }
+  } else {
+    for (int j = warp; j < n; j += nw) {
+      float d = 0.f;
+      for (int i = lane; i < hd; i += 32) d = __fadd_rn(d, __fmul_rn(Ks[j * kst + i], qh[i]));
+      d = warp_sum(d);
+      if (lane == 0) sc[j] = ok ? __fmul_rn(d, p.kq_scale) : 0.f;
+    }
+    __syncthreads();
+    if (tid < n) my = sc[tid];
+  }
+  float m = warp_max(my);
+  if (lane == 0) s_max[warp] = m;
+  __syncthreads();
+  m = s_max[0];
+  for (int w = 1; w < nw; ++w) m = fmaxf(m, s_max[w]);
+  const float e = tid < n ? exp_cw(__fsub_rn(my, m)) : 0.f;
+  double l = warp_sum_d(tid < n ? static_cast<double>(e) : 0.0);
+  if (lane == 0) red[warp] = l;
+  __syncthreads();
+  l = 0.0;
+  for (int w = 0; w < nw; ++w) l += red[w];
+  if (tid < n) sc[tid] = n_active == 1 ? __fmul_rn(e, static_cast<float>(1.0 / l)) : e;
+  __syncthreads();
+  float* out = p.out + static_cast<int64_t>(b) * dq + h * hd;
+  if (n_active == 1) {
+    for (int i = tid; i < hd; i += blockDim.x) {
+      float acc = 0.f;
+      for (int j = 0; j < n; ++j) acc = __fadd_rn(acc, __fmul_rn(Vs[j * hd + i], sc[j]));
+      out[i] = acc;
+    }
+    return;
+  }
+  const int64_t bh = static_cast<int64_t>(b) * p.n_head + h;
+  const int64_t slot = bh * p.n_split + sp;
+  for (int i = tid; i < hd; i += blockDim.x) {
+    float acc = 0.f;
+    for (int j = 0; j < n; ++j) acc = __fadd_rn(acc, __fmul_rn(Vs[j * hd + i], sc[j]));
+    p.part_acc[slot * hd + i] = acc;
+  }
+  if (tid == 0) {
+    p.part_m[slot] = m;
+    p.part_l[slot] = l;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    s_last = atomicAdd(&p.tickets[bh], 1u) == static_cast<unsigned>(n_active - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const volatile float* pm = p.part_m + bh * p.n_split;
+  const volatile double* pl = p.part_l + bh * p.n_split;
+  float M = -INFINITY;
+  for (int s = 0; s < n_active; ++s) M = fmaxf(M, pm[s]);
+  double L = 0.0;
+  for (int s0 = 0; s0 < n_active; s0 += kBAttnSplit) {
+    const int cnt = min(kBAttnSplit, n_active - s0);
+    __syncthreads();
+    for (int s = tid; s < cnt; s += blockDim.x) sc[s] = exp_cw(__fsub_rn(pm[s0 + s], M));
+    __syncthreads();
+    for (int s = 0; s < cnt; ++s) L += pl[s0 + s] * static_cast<double>(sc[s]);
+  }
+  const float inv = static_cast<float>(1.0 / L);
+  for (int i = tid; i < hd; i += blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < n_active; ++s) {
+      const float w = exp_cw(__fsub_rn(pm[s], M));
+      acc = __fadd_rn(acc, __fmul_rn(__ldcg(&p.part_acc[(bh * p.n_split + s) * hd + i]), w));
+    }
+    out[i] = __fmul_rn(acc, inv);
+  }
+  if (tid == 0) p.tickets[bh] = 0u;
+}
+
+// ---------------------------------------------------------------- router
+// One CTA per token: the E logits from the normalised f32 row (the batch-1
+// router's dot order), then softmax and top-(k+1) by rank in warp 0.
+template <int KP>
+__global__ void __launch_bounds__(256) batch_router_kernel(const float* xn,
+                                                           const float* router, int K, int E, int topk,
+                                                           int norm_topk, int32_t* sel, float* wts) {
+  const int b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ float lg[32 * KP];
+  __shared__ int s_ids[kBMaxTopK + 1];
+  __shared__ float s_vals[kBMaxTopK + 1];
+  pdl_wait();
+  pdl_trigger();
+  const float* x = xn + static_cast<int64_t>(b) * K;
+  for (int e = warp; e < E; e += 8) {
+    const float* w = router + static_cast<int64_t>(e) * K;
+    float s = 0.f;
+    if (K % 128 == 0) {
+      for (int t = 0; t < K / 128; ++t) {
+        const float4 wv = *reinterpret_cast<const float4*>(w + 4 * lane + 128 * t);
+        const float4 xv = *reinterpret_cast<const float4*>(x + 4 * lane + 128 * t);
+        s = __fadd_rn(s, __fmul_rn(wv.x, xv.x));
+        s = __fadd_rn(s, __fmul_rn(wv.y, xv.y));
+        s = __fadd_rn(s, __fmul_rn(wv.z, xv.z));
+        s = __fadd_rn(s, __fmul_rn(wv.w, xv.w));
+      }
+    } else {
+      for (int i = lane; i < K; i += 32) s = __fadd_rn(s, __fmul_rn(w[i], x[i]));
+    }
+    s = warp_sum(s);
+    if (lane == 0) lg[e] = s;
+  }
+  __syncthreads();
+  if (warp != 0) return;
+  float pr[KP];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int k = 0; k < KP; ++k) {
+    const int i = lane + 32 * k;
+    pr[k] = i < E ? lg[i] : -INFINITY;
+    mx = fmaxf(mx, pr[k]);
+  }
+  mx = warp_max(mx);
+  double sum = 0.0;
+#pragma unroll
+  for (int k = 0; k < KP; ++k) {
+    const int i = lane + 32 * k;
+    pr[k] = i < E ? exp_cw(__fsub_rn(pr[k], mx)) : 0.f;
+    sum += static_cast<double>(pr[k]);
+  }
+  sum = warp_sum_d(sum);
+  const float inv = static_cast<float>(1.0 / sum);
+#pragma unroll
+  for (int k = 0; k < KP; ++k) pr[k] = __fmul_rn(pr[k], inv);
+  const int kk = min(topk + 1, E);
+  int rank[KP];
+#pragma unroll
+  for (int k = 0; k < KP; ++k) rank[k] = 0;
+#pragma unroll
+  for (int kj = 0; kj < KP; ++kj) {
+#pragma unroll 8
+    for (int src = 0; src < 32; ++src) {
+      const float pj = __shfl_sync(0xffffffffu, pr[kj], src);
+      const int j = src + 32 * kj;
+#pragma unroll
+      for (int ki = 0; ki < KP; ++ki) {
+        const int i = lane + 32 * ki;
+        rank[ki] += (j < E && (pj > pr[ki] || (pj == pr[ki] && j < i))) ? 1 : 0;
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < KP; ++k) {
+    const int i = lane + 32 * k;
+    if (i < E && rank[k] < kk) {
+      s_ids[rank[k]] = i;
+      s_vals[rank[k]] = pr[k];
+    }
+  }
+  __syncwarp();
+  float ws = 1.f;
+  if (norm_topk) {
+    double sw = 0.0;
+    for (int t = 0; t < topk; ++t) sw += static_cast<double>(s_vals[t]);
+    ws = fmaxf(static_cast<float>(sw), 6.103515625e-5f);
+  }
+  for (int t = lane; t < topk; t += 32) {
+    sel[b * topk + t] = s_ids[t];
+    wts[b * topk + t] = norm_topk ? __fdiv_rn(s_vals[t], ws) : s_vals[t];
+  }
+}
+
+// ---------------------------------------------------------------- expert plan
+// One CTA: for the B*k (token, slot) pairs, per-expert counts, offsets and
+// the token lists in (token, slot) order: act_idx = token, out_idx = token*k
+// + slot.
+__global__ void __launch_bounds__(512) batch_moe_plan_kernel(const int32_t* sel, int n_pairs, int E, int topk,
+                                                             int32_t* off, int32_t* cnt, int32_t* act_idx,
+                                                             int32_t* out_idx) {
+  extern __shared__ int sh[];  // [E] counts, [E] offsets, [n_pairs] selection
+  int* c = sh;
+  int* o = sh + E;
+  int* s = sh + 2 * E;
+  pdl_wait();
+  pdl_trigger();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) c[e] = 0;
+  for (int j = threadIdx.x; j < n_pairs; j += blockDim.x) s[j] = sel[j];
+  __syncthreads();
+  for (int j = threadIdx.x; j < n_pairs; j += blockDim.x) atomicAdd(&c[s[j]], 1);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int e = 0; e < E; ++e) {
+      o[e] = acc;
+      acc += c[e];
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    off[e] = o[e];
+    cnt[e] = c[e];
+  }
+  for (int j = threadIdx.x; j < n_pairs; j += blockDim.x) {
+    const int e = s[j];
+    int rank = 0;
+    for (int q = 0; q < j; ++q) rank += s[q] == e ? 1 : 0;
+    act_idx[o[e] + rank] = j / topk;
+    out_idx[o[e] + rank] = j;
+  }
+}
+
+// ---------------------------------------------------------------- combine
+// h[b][r] += sum_i wts[b][i] * y[b*k+i][r], products rounded, added in top-k order.
+__global__ void batch_combine_kernel(const float* y, const float* wts, int topk, int D, float* h) {
+  const int b = blockIdx.x;
+  pdl_wait();
+  pdl_trigger();
+  const float* wb = wts + b * topk;
+  for (int r = threadIdx.x; r < D; r += blockDim.x) {
+    const float* yb = y + static_cast<int64_t>(b) * topk * D + r;
+    float acc = __fmul_rn(yb[0], wb[0]);
+    for (int i = 1; i < topk; ++i) acc = __fadd_rn(acc, __fmul_rn(yb[static_cast<int64_t>(i) * D], wb[i]));
+    h[static_cast<int64_t>(b) * D + r] = __fadd_rn(h[static_cast<int64_t>(b) * D + r], acc);
+  }
+}
+
+// ---------------------------------------------------------------- argmax
+// One CTA per sequence over its logits (first maximum wins); the last CTA
+// advances the shared cursor.
+__global__ void batch_argmax_kernel(NhDecodeState* state, const float* logits, int V, int32_t* fed,
+                                    int32_t* out_tokens, int n_predict, unsigned* ticket) {
+  const int b = blockIdx.x;
+  __shared__ float s_bv[32];
+  __shared__ int s_bi[32];
+  __shared__ bool s_last;
+  pdl_wait();
+  pdl_trigger();
+  const int pos = state->pos, n_prompt = state->n_prompt;
+  const bool emit = pos >= n_prompt - 1;
+  float bv = -INFINITY;
+  int bi = INT_MAX;
+  if (emit) {
+    const float* lg = logits + static_cast<int64_t>(b) * V;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+      const float v = lg[i];
+      if (argmax_better(v, i, bv, bi)) {
+        bv = v;
+        bi = i;
+      }
+    }
+  }
+  block_argmax(bv, bi, s_bv, s_bi);
+  if (threadIdx.x == 0) {
+    if (emit) {
+      if (bi == INT_MAX) bi = 0;
+      const int n = pos - (n_prompt - 1);
+      if (n < n_predict) out_tokens[static_cast<int64_t>(b) * n_predict + n] = bi;
+      fed[b] = bi;
+    }
+    __threadfence();
+    s_last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (threadIdx.x != 0 || !s_last) return;
+  if (emit) state->n_out = state->n_out + 1;
+  state->pos = pos + 1;
+  *ticket = 0u;
+}
+
+}  // namespace nh
+
+using namespace nh;
+
+extern "C" int64_t nh_batch_q8_bytes(int64_t rows, int64_t n) { return rows * (n / QK) * kQ8Stride; }
+
+extern "C" int nh_batch_embed(const NhDecodeState* state, const int32_t* prompts, int n_prompt, const int32_t* fed,
+                              int n_seq, const void* table, int32_t type, int64_t n_embd, int64_t n_vocab, float* h,
+                              void* stream) {
+  if (state == nullptr || prompts == nullptr || fed == nullptr || table == nullptr || h == nullptr || n_seq <= 0)
+    return NH_E_ARG;
+  if (type != NH_TYPE_F32 && type != NH_TYPE_Q4_K && type != NH_TYPE_Q6_K) return NH_E_TYPE;
+  if (type != NH_TYPE_F32 && n_embd % QK != 0) return NH_E_ARG;
+  return launch_pdl(batch_embed_kernel, dim3(n_seq), dim3(256), 0, static_cast<cudaStream_t>(stream), state, prompts,
+                    n_prompt, fed, static_cast<const uint8_t*>(table), static_cast<int>(type),
+                    static_cast<int>(n_embd), static_cast<int>(n_vocab), static_cast<uint64_t>(row_bytes(type, n_embd)),
+                    h);
+}
+
+extern "C" int nh_batch_prep(const float* x, int64_t x_stride, int64_t rows, const float* norm_w, float eps,
+                             int do_norm, int64_t n, void* q8, float* xn, void* stream) {
+  if (x == nullptr || rows <= 0 || n <= 0 || n > kMaxK || (q8 == nullptr && xn == nullptr)) return NH_E_ARG;
+  if (q8 != nullptr && n % QK != 0) return NH_E_ARG;
+  const size_t smem = act_smem_bytes(static_cast<int>(n), true, norm_w != nullptr && do_norm);
+  static size_t configured = 48 * 1024;
+  if (!ensure_smem(batch_prep_kernel, smem, configured)) return NH_E_CUDA;
+  return launch_pdl(batch_prep_kernel, dim3(static_cast<unsigned>(rows)), dim3(256), smem,
+                    static_cast<cudaStream_t>(stream), x, x_stride, norm_w, eps, do_norm, static_cast<int>(n),
+                    static_cast<uint8_t*>(q8), xn);
+}
+
+extern "C" int nh_batch_rowdot(const NhGroupedRowDot* g, void* stream) {
+  if (g == nullptr || g->w == nullptr || g->q8 == nullptr || g->out == nullptr || g->rows <= 0 || g->n_groups <= 0)
+    return NH_E_ARG;
+  if (!rowdot3_k_ok(static_cast<int>(g->n))) return NH_E_ARG;
+  for (int32_t t : {g->type, g->type2})
+    if (t != NH_TYPE_Q4_K && t != NH_TYPE_Q6_K) return NH_E_TYPE;
+  if (g->mode == kSwiGLU && g->w2 == nullptr) return NH_E_ARG;
+  if ((g->type == NH_TYPE_Q4_K && (reinterpret_cast<uintptr_t>(g->w) & 15) != 0) ||
+      (g->w2 != nullptr && g->type2 == NH_TYPE_Q4_K && (reinterpret_cast<uintptr_t>(g->w2) & 15) != 0))
+    return NH_E_ARG;
+  GroupArgs p;
+  memset(&p, 0, sizeof(p));
+  p.w = static_cast<const uint8_t*>(g->w);
+  p.w2 = static_cast<const uint8_t*>(g->w2);
+  p.mstride = g->mstride;
+  p.mstride2 = g->mstride2;
+  p.type = g->type;
+  p.type2 = g->w2 != nullptr ? g->type2 : g->type;
+  p.K = static_cast<int>(g->n);
+  p.rows = static_cast<int>(g->rows);
+  p.rb = row_bytes(g->type, g->n);
+  p.rb2 = row_bytes(p.type2, g->n);
+  p.n_groups = g->n_groups;
+  p.off = g->off;
+  p.cnt = g->cnt;
+  p.act_idx = g->act_idx;
+  p.out_idx = g->out_idx;
+  p.n_tok = g->n_tok;
+  p.q8 = static_cast<const uint8_t*>(g->q8);
+  p.out = g->out;
+  p.out_stride = g->out_stride;
+  p.mode = g->mode;
+  // Row blocks: enough CTAs to fill the GPU at least twice over the groups.
+  const int P = 32 / (p.K / QK);
+  const int per_pass = kBatchWarps * P;
+  const int target = std::max(1, 2 * device_sm_count() / std::max(1, g->n_groups));
+  int rpb = (p.rows + target - 1) / target;
+  rpb = (rpb + per_pass - 1) / per_pass * per_pass;
+  p.rows_per_block = rpb;
+  p.row_blocks = (p.rows + rpb - 1) / rpb;
+  const int tiles = (g->max_tokens + kBatchTokTile - 1) / kBatchTokTile;
+  const size_t smem = static_cast<size_t>(kBatchTokTile) * (p.K / QK) * kQ8Stride;
+  static size_t configured = 48 * 1024;
+  if (!ensure_smem(batch_rowdot_kernel, smem, configured)) return NH_E_CUDA;
+  return launch_pdl(batch_rowdot_kernel, dim3(p.n_groups * p.row_blocks, std::max(1, tiles)), dim3(kBatchWarps * 32),
+                    smem, static_cast<cudaStream_t>(stream), p);
+}
+
+extern "C" int nh_batch_qk(const NhDecodeState* state, const float* q, const float* k, const float* v,
+                           const float* q_norm, const float* k_norm, float eps, int n_seq, int n_head, int n_head_kv,
+                           int head_dim, const float* rope_cs, float* k_cache, float* v_cache, int max_seq, float* qr,
+                           void* stream) {
+  if (state == nullptr || q == nullptr || k == nullptr || v == nullptr || q_norm == nullptr || k_norm == nullptr ||
+      rope_cs == nullptr || k_cache == nullptr || v_cache == nullptr || qr == nullptr || n_seq <= 0 ||
+      head_dim % 2 != 0 || n_head % n_head_kv != 0)
+    return NH_E_ARG;
+  return launch_pdl(batch_qk_kernel, dim3(n_seq), dim3(128), 0, static_cast<cudaStream_t>(stream), state, q, k, v,
+                    q_norm, k_norm, eps, n_head, n_head_kv, head_dim, rope_cs, k_cache, v_cache, max_seq, qr);
+}
+
+extern "C" int64_t nh_batch_attention_scratch_bytes(int n_seq, int n_head, int head_dim, int max_seq) {
+  const int64_t S = (max_seq + kBAttnSplit - 1) / kBAttnSplit;
+  const int64_t bh = static_cast<int64_t>(n_seq) * n_head;
+  return ((bh * 4 + 255) / 256) * 256 + bh * S * (8 + 4 + 4 * static_cast<int64_t>(head_dim)) + 512;
+}
+
+extern "C" int nh_batch_attention(const NhDecodeState* state, const float* qr, int n_seq, int n_head, int n_head_kv,
+                                  int head_dim, float kq_scale, const float* k_cache, const float* v_cache, int max_seq,
+                                  void* scratch, float* out, void* stream) {
+  if (state == nullptr || qr == nullptr || k_cache == nullptr || v_cache == nullptr || scratch == nullptr ||
+      out == nullptr || n_seq <= 0 || head_dim % 4 != 0 || head_dim > 256 || n_head % n_head_kv != 0 ||
+      (reinterpret_cast<uintptr_t>(k_cache) & 15) != 0 || (reinterpret_cast<uintptr_t>(v_cache) & 15) != 0)
+    return NH_E_ARG;
+  BAttnArgs p;
+  p.state = const_cast<NhDecodeState*>(state);
+  p.qr = qr;
+  p.k_cache = k_cache;
+  p.v_cache = v_cache;
+  p.n_head = n_head;
+  p.n_head_kv = n_head_kv;
+  p.hd = head_dim;
+  p.max_seq = max_seq;
+  p.n_split = (max_seq + kBAttnSplit - 1) / kBAttnSplit;
+  p.kq_scale = kq_scale;
+  const int64_t bh = static_cast<int64_t>(n_seq) * n_head;
+  uint8_t* sc = static_cast<uint8_t*>(scratch);
+  p.tickets = reinterpret_cast<unsigned*>(sc);
+  int64_t off = ((bh * 4 + 255) / 256) * 256;
+  p.part_l = reinterpret_cast<double*>(sc + off);
+  off += bh * p.n_split * 8;
+  p.part_m = reinterpret_cast<float*>(sc + off);
+  off += bh * p.n_split * 4;
+  off = (off + 15) & ~15ll;
+  p.part_acc = reinterpret_cast<float*>(sc + off);
+  p.out = out;
+  const size_t smem = static_cast<size_t>(kBAttnSplit * (head_dim + 4) + kBAttnSplit * head_dim + head_dim +
+                                          kBAttnSplit) * sizeof(float);
+  static size_t configured = 48 * 1024;
+  if (!ensure_smem(batch_attention_kernel, smem, configured)) return NH_E_CUDA;
+  return launch_pdl(batch_attention_kernel, dim3(n_head, p.n_split, n_seq), dim3(kBAttnThreads), smem,
+                    static_cast<cudaStream_t>(stream), p);
+}
+
+extern "C" int nh_batch_router(const float* xn, const float* router, int n_seq, int64_t n_embd, int n_expert, int k,
+                               int norm_topk, int32_t* sel, float* wts, void* stream) {
+  if (xn == nullptr || router == nullptr || sel == nullptr || wts == nullptr || n_seq <= 0 || n_expert <= 0 ||
+      n_expert > 256 || k <= 0 || k > kBMaxTopK || k > n_expert || n_embd % 4 != 0)
+    return NH_E_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int K = static_cast<int>(n_embd);
+  if (n_expert <= 32)
+    return launch_pdl(batch_router_kernel<1>, dim3(n_seq), dim3(256), 0, st, xn, router, K, n_expert, k, norm_topk,
+                      sel, wts);
+  if (n_expert <= 64)
+    return launch_pdl(batch_router_kernel<2>, dim3(n_seq), dim3(256), 0, st, xn, router, K, n_expert, k, norm_topk,
+                      sel, wts);
+  if (n_expert <= 128)
+    return launch_pdl(batch_router_kernel<4>, dim3(n_seq), dim3(256), 0, st, xn, router, K, n_expert, k, norm_topk,
+                      sel, wts);
+  return launch_pdl(batch_router_kernel<8>, dim3(n_seq), dim3(256), 0, st, xn, router, K, n_expert, k, norm_topk,
+                    sel, wts);
+}
+
+extern "C" int nh_batch_moe_plan(const int32_t* sel, int n_seq, int k, int n_expert, int32_t* off, int32_t* cnt,
+                                 int32_t* act_idx, int32_t* out_idx, void* stream) {
+  if (sel == nullptr || off == nullptr || cnt == nullptr || act_idx == nullptr || out_idx == nullptr || n_seq <= 0 ||
+      k <= 0 || n_expert <= 0)
+    return NH_E_ARG;
+  const int n_pairs = n_seq * k;
+  const size_t smem = static_cast<size_t>(2 * n_expert + n_pairs) * sizeof(int);
+  if (smem > 48 * 1024) return NH_E_CAPACITY;
+  return launch_pdl(batch_moe_plan_kernel, dim3(1), dim3(512), smem, static_cast<cudaStream_t>(stream), sel, n_pairs,
+                    n_expert, k, off, cnt, act_idx, out_idx);
+}
+
+extern "C" int nh_batch_combine(const float* y, const float* wts, int n_seq, int k, int64_t n_embd, float* h,
+                                void* stream) {
+  if (y == nullptr || wts == nullptr || h == nullptr || n_seq <= 0 || k <= 0) return NH_E_ARG;
+  return launch_pdl(batch_combine_kernel, dim3(n_seq), dim3(256), 0, static_cast<cudaStream_t>(stream), y, wts, k,
+                    static_cast<int>(n_embd), h);
+}
+
+extern "C" int nh_batch_argmax(NhDecodeState* state, const float* logits, int n_seq, int64_t n_vocab, int32_t* fed,
+                               int32_t* out_tokens, int n_predict, void* scratch, void* stream) {
+  if (state == nullptr || logits == nullptr || fed == nullptr || out_tokens == nullptr || scratch == nullptr ||
+      n_seq <= 0)
+    return NH_E_ARG;
+  return launch_pdl(batch_argmax_kernel, dim3(n_seq), dim3(256), 0, static_cast<cudaStream_t>(stream), state, logits,
+                    static_cast<int>(n_vocab), fed, out_tokens, n_predict, static_cast<unsigned*>(scratch));
+}
