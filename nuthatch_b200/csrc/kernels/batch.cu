@@ -241,9 +241,10 @@ struct GroupArgs {
   float* out;
   int64_t out_stride;
   int mode;
+  int tok_tile;  // tokens staged per CTA (<= kBatchTokTile)
 };
 
-__global__ void __launch_bounds__(kBatchWarps * 32) batch_rowdot_kernel(const GroupArgs p) {
+__global__ void __launch_bounds__(kBatchWarps * 32, 2) batch_rowdot_kernel(const GroupArgs p) {
   extern __shared__ __align__(128) uint8_t smem[];  // [kBatchTokTile][K/256][kQ8Stride]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nb = p.K / QK, G = nb, P = 32 / G;
@@ -252,8 +253,8 @@ __global__ void __launch_bounds__(kBatchWarps * 32) batch_rowdot_kernel(const Gr
   pdl_trigger();
   const int t_off = p.off != nullptr ? p.off[e] : 0;
   const int t_cnt = p.off != nullptr ? p.cnt[e] : p.n_tok;
-  const int t0 = blockIdx.y * kBatchTokTile;
-  const int nt = min(kBatchTokTile, t_cnt - t0);
+  const int t0 = blockIdx.y * p.tok_tile;
+  const int nt = min(p.tok_tile, t_cnt - t0);
   if (nt <= 0) return;
   // Stage this tile's activation rows (16-byte copies).
   const int blk_bytes = nb * kQ8Stride, n16 = blk_bytes / 16;
@@ -323,8 +324,12 @@ __global__ void __launch_bounds__(128) batch_qk_kernel(const NhDecodeState* stat
   pdl_wait();
   pdl_trigger();
   const int pos = state->pos;
-  const float* qb = q + static_cast<int64_t>(b) * dq;
-  const float* kb = k + static_cast<int64_t>(b) * dkv;
+  extern __shared__ __align__(16) float qk_s[];  // [dq] q row, [dkv] k row
+  copy_to_smem(qk_s, q + static_cast<int64_t>(b) * dq, dq);
+  copy_to_smem(qk_s + dq, k + static_cast<int64_t>(b) * dkv, dkv);
+  __syncthreads();
+  const float* qb = qk_s;
+  const float* kb = qk_s + dq;
   double sq = 0.0, sk = 0.0;
   for (int i = tid; i < dq; i += blockDim.x) sq += static_cast<double>(__fmul_rn(qb[i], qb[i]));
   for (int i = tid; i < dkv; i += blockDim.x) sk += static_cast<double>(__fmul_rn(kb[i], kb[i]));
@@ -548,23 +553,52 @@ __global__ void __launch_bounds__(256) batch_router_kernel(const float* xn,
   pdl_wait();
   pdl_trigger();
   const float* x = xn + static_cast<int64_t>(b) * K;
-  for (int e = warp; e < E; e += 8) {
-    const float* w = router + static_cast<int64_t>(e) * K;
-    float s = 0.f;
-    if (K % 128 == 0) {
-      for (int t = 0; t < K / 128; ++t) {
-        const float4 wv = *reinterpret_cast<const float4*>(w + 4 * lane + 128 * t);
-        const float4 xv = *reinterpret_cast<const float4*>(x + 4 * lane + 128 * t);
-        s = __fadd_rn(s, __fmul_rn(wv.x, xv.x));
-        s = __fadd_rn(s, __fmul_rn(wv.y, xv.y));
-        s = __fadd_rn(s, __fmul_rn(wv.z, xv.z));
-        s = __fadd_rn(s, __fmul_rn(wv.w, xv.w));
+  if (K % 128 == 0 && K <= 2048) {
+    // The lane's slice of x stays in registers; each expert row's slice is
+    // loaded as one batch before its (ordered) sum.
+    constexpr int kV = 2048 / 128;
+    float4 xv[kV];
+#pragma unroll
+    for (int t = 0; t < kV; ++t)
+      if (t < K / 128) xv[t] = *reinterpret_cast<const float4*>(x + 4 * lane + 128 * t);
+    for (int e = warp; e < E; e += 8) {
+      const float4* w4 = reinterpret_cast<const float4*>(router + static_cast<int64_t>(e) * K);
+      float4 wv[kV];
+#pragma unroll
+      for (int t = 0; t < kV; ++t)
+        if (t < K / 128) wv[t] = __ldg(w4 + lane + 32 * t);
+      float s = 0.f;
+#pragma unroll
+      for (int t = 0; t < kV; ++t) {
+        if (t < K / 128) {
+          s = __fadd_rn(s, __fmul_rn(wv[t].x, xv[t].x));
+          s = __fadd_rn(s, __fmul_rn(wv[t].y, xv[t].y));
+          s = __fadd_rn(s, __fmul_rn(wv[t].z, xv[t].z));
+          s = __fadd_rn(s, __fmul_rn(wv[t].w, xv[t].w));
+        }
       }
-    } else {
-      for (int i = lane; i < K; i += 32) s = __fadd_rn(s, __fmul_rn(w[i], x[i]));
+      s = warp_sum(s);
+      if (lane == 0) lg[e] = s;
     }
-    s = warp_sum(s);
-    if (lane == 0) lg[e] = s;
+  } else {
+    for (int e = warp; e < E; e += 8) {
+      const float* w = router + static_cast<int64_t>(e) * K;
+      float s = 0.f;
+      if (K % 128 == 0) {
+        for (int t = 0; t < K / 128; ++t) {
+          const float4 wv = *reinterpret_cast<const float4*>(w + 4 * lane + 128 * t);
+          const float4 xv = *reinterpret_cast<const float4*>(x + 4 * lane + 128 * t);
+          s = __fadd_rn(s, __fmul_rn(wv.x, xv.x));
+          s = __fadd_rn(s, __fmul_rn(wv.y, xv.y));
+          s = __fadd_rn(s, __fmul_rn(wv.z, xv.z));
+          s = __fadd_rn(s, __fmul_rn(wv.w, xv.w));
+        }
+      } else {
+        for (int i = lane; i < K; i += 32) s = __fadd_rn(s, __fmul_rn(w[i], x[i]));
+      }
+      s = warp_sum(s);
+      if (lane == 0) lg[e] = s;
+    }
   }
   __syncthreads();
   if (warp != 0) return;
@@ -672,7 +706,7 @@ __global__ void batch_combine_kernel(const float* y, const float* wts, int topk,
   pdl_wait();
   pdl_trigger();
   const float* wb = wts + b * topk;
-  for (int r = threadIdx.x; r < D; r += blockDim.x) {
+  for (int r = blockIdx.y * blockDim.x + threadIdx.x; r < D; r += gridDim.y * blockDim.x) {
     const float* yb = y + static_cast<int64_t>(b) * topk * D + r;
     float acc = __fmul_rn(yb[0], wb[0]);
     for (int i = 1; i < topk; ++i) acc = __fadd_rn(acc, __fmul_rn(yb[static_cast<int64_t>(i) * D], wb[i]));
@@ -786,16 +820,25 @@ extern "C" int nh_batch_rowdot(const NhGroupedRowDot* g, void* stream) {
   p.out = g->out;
   p.out_stride = g->out_stride;
   p.mode = g->mode;
-  // Row blocks: enough CTAs to fill the GPU at least twice over the groups.
+  // Work split: row blocks of whole warp passes (8 warps x P rows) and token
+  // tiles, aiming at about eight CTAs per SM over all groups so that each
+  // warp has only a few passes; smaller token tiles when the row blocks alone
+  // cannot get there.
   const int P = 32 / (p.K / QK);
   const int per_pass = kBatchWarps * P;
-  const int target = std::max(1, 2 * device_sm_count() / std::max(1, g->n_groups));
+  const int sms = device_sm_count();
+  const int target = std::max(1, 8 * sms / std::max(1, g->n_groups));
   int rpb = (p.rows + target - 1) / target;
   rpb = (rpb + per_pass - 1) / per_pass * per_pass;
   p.rows_per_block = rpb;
   p.row_blocks = (p.rows + rpb - 1) / rpb;
-  const int tiles = (g->max_tokens + kBatchTokTile - 1) / kBatchTokTile;
-  const size_t smem = static_cast<size_t>(kBatchTokTile) * (p.K / QK) * kQ8Stride;
+  const int max_tok = std::max(1, g->max_tokens);
+  p.tok_tile = kBatchTokTile;
+  while (p.tok_tile > 8 && static_cast<int64_t>(p.n_groups) * p.row_blocks * ((max_tok + p.tok_tile - 1) / p.tok_tile) <
+                               4 * sms)
+    p.tok_tile >>= 1;
+  const int tiles = (max_tok + p.tok_tile - 1) / p.tok_tile;
+  const size_t smem = static_cast<size_t>(p.tok_tile) * (p.K / QK) * kQ8Stride;
   static size_t configured = 48 * 1024;
   if (!ensure_smem(batch_rowdot_kernel, smem, configured)) return NH_E_CUDA;
   return launch_pdl(batch_rowdot_kernel, dim3(p.n_groups * p.row_blocks, std::max(1, tiles)), dim3(kBatchWarps * 32),
@@ -810,7 +853,10 @@ extern "C" int nh_batch_qk(const NhDecodeState* state, const float* q, const flo
       rope_cs == nullptr || k_cache == nullptr || v_cache == nullptr || qr == nullptr || n_seq <= 0 ||
       head_dim % 2 != 0 || n_head % n_head_kv != 0)
     return NH_E_ARG;
-  return launch_pdl(batch_qk_kernel, dim3(n_seq), dim3(128), 0, static_cast<cudaStream_t>(stream), state, q, k, v,
+  const size_t smem = static_cast<size_t>(n_head + n_head_kv) * head_dim * sizeof(float);
+  static size_t configured = 48 * 1024;
+  if (smem > 220 * 1024 || !ensure_smem(batch_qk_kernel, smem, configured)) return NH_E_ARG;
+  return launch_pdl(batch_qk_kernel, dim3(n_seq), dim3(128), smem, static_cast<cudaStream_t>(stream), state, q, k, v,
                     q_norm, k_norm, eps, n_head, n_head_kv, head_dim, rope_cs, k_cache, v_cache, max_seq, qr);
 }
 
@@ -892,7 +938,8 @@ extern "C" int nh_batch_moe_plan(const int32_t* sel, int n_seq, int k, int n_exp
 extern "C" int nh_batch_combine(const float* y, const float* wts, int n_seq, int k, int64_t n_embd, float* h,
                                 void* stream) {
   if (y == nullptr || wts == nullptr || h == nullptr || n_seq <= 0 || k <= 0) return NH_E_ARG;
-  return launch_pdl(batch_combine_kernel, dim3(n_seq), dim3(256), 0, static_cast<cudaStream_t>(stream), y, wts, k,
+  return launch_pdl(batch_combine_kernel, dim3(n_seq, static_cast<unsigned>((n_embd + 255) / 256)), dim3(256), 0,
+                    static_cast<cudaStream_t>(stream), y, wts, k,
                     static_cast<int>(n_embd), h);
 }
 
