@@ -93,10 +93,13 @@ def build_synth(verbose: bool = False) -> Path:
 
 def build_checker(verbose: bool = False) -> None:
     """The oracle (always) and oracle/_ref (only where the reference tree exists)."""
-    _run(["make", "-s", "-C", str(ROOT / "oracle")])
+    # The same g++ as the product (libstdc++ linked as a shared library): a
+    # checker with its own static copy misbehaves once the process has also
+    # loaded the shared libstdc++ (numpy and torch do).
+    _run(["make", "-s", "-C", str(ROOT / "oracle"), "CXX=g++"])
     ref = Path(os.environ.get("NUTHATCH_REFERENCE", "/root/reference"))
     if (ref / "src" / "cache" / "cache_policy.cc").exists():
-        _run(["make", "-s", "-C", str(ROOT / "oracle"), "ref", f"REF={ref}"])
+        _run(["make", "-s", "-C", str(ROOT / "oracle"), "ref", f"REF={ref}", "CXX=g++"])
     if verbose:
         print("built oracle")
 
