@@ -131,6 +131,18 @@ def cpu_oracle_run(path: str, n_predict: int, threads: int) -> tuple[float, list
     return dt, out["tokens"]
 
 
+def max_over_ranks(value: float, dist, device: str = "cuda") -> float:
+    """The largest of every rank's value (timings: the job is as slow as its
+    slowest rank); the value itself without a process group."""
+    if dist is None:
+        return value
+    import torch
+
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -381,10 +393,7 @@ def main() -> None:
     clk = clocks.stop()
     assert L.nh_decode_result(m._h, N_PREDICT, op) == 0
     assert out.tolist() == ref_tokens, "replayed decode diverged"
-    if dist is not None:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = max_over_ranks(ms, dist)
     ms_per_step = ms / args.steps
     value = world * N_PREDICT * args.steps / (ms / 1000.0)
     launches_per_token = L.nh_generate_launches(m._h)
@@ -423,10 +432,7 @@ def main() -> None:
     for _ in range(e2e_steps):
         got = nh.GreedyGenerateCached(m, prompt.tolist(), N_PREDICT, False)
     e2e_s = time.perf_counter() - t0
-    if dist is not None:
-        t = torch.tensor([e2e_s], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
+    e2e_s = max_over_ranks(e2e_s, dist)
     assert got == ref_tokens
     e2e = {"value": world * N_PREDICT * e2e_steps / e2e_s, "unit": "tok/s",
            "h2d_bytes_per_step": N_PROMPT * 4 + 32, "d2h_bytes_per_step": N_PREDICT * 4 + 32,
