@@ -309,6 +309,194 @@ __global__ void __launch_bounds__(kBatchWarps * 32, 2) batch_rowdot_kernel(const
   }
 }
 
+// ---------------------------------------------------------------- tensor-core grouped GEMM (Q4_K)
+// The same grouped products on the tensor cores: mma.sync m16n8k32 with int8
+// operands computes, for 16 weight rows x 8 tokens, the integer dot of one
+// 32-value Q4_K sub-block (A = the 4-bit quants, B = the Q8_K activation
+// quants).  Q4_K changes its 6-bit scale every 32 values, so each sub-block's
+// int32 result is scaled in registers (sumi += sc_j * dot_j, summ from the
+// activation's partial sums) before the super-block is formed in f32 exactly
+// as the row-dot kernels form it, and super-blocks are combined by the same
+// pairwise tree.  The results are therefore identical to the dp4a kernels.
+// (A tcgen05 MMA accumulates over all of K in tensor memory; with a new scale
+// every 32 values it would have to be read back after every instruction.)
+//
+// Work: a warp owns one tile of 16 rows of one group and walks that group's
+// tokens 8 at a time (blockIdx.y splits the tokens of ungrouped products).
+__device__ __forceinline__ void mma_s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                       uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%11,%12,%13};\n"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+// Pairwise super-block tree, one value at a time: s-th value v (s from 0).
+struct SbTree {
+  float p, q, o, r;
+  __device__ __forceinline__ void add(int s, float v) {
+    if ((s & 1) == 0) {
+      p = v;
+      r = v;
+      return;
+    }
+    const float pair = __fadd_rn(p, v);
+    r = pair;
+    if ((s & 2) == 0) {
+      q = pair;
+      return;
+    }
+    const float quad = __fadd_rn(q, pair);
+    r = quad;
+    if ((s & 4) == 0) {
+      o = quad;
+      return;
+    }
+    r = __fadd_rn(o, quad);
+  }
+};
+
+// One 16x8 tile of one Q4_K matrix over K (nsb super-blocks): out[r][t] for
+// rows (g, g+8) and tokens (2*tig, 2*tig+1) of the tile.
+__device__ __forceinline__ void tile_q4k_mma(const uint8_t* w_r0, const uint8_t* w_r1, uint64_t rb, int nsb,
+                                             const uint8_t* act_g, const uint8_t* act_t0, const uint8_t* act_t1,
+                                             int tig, float (&out)[2][2]) {
+  (void)rb;
+  SbTree tree[2][2];
+  const uint32_t m4 = 0x0F0F0F0Fu;
+  for (int s = 0; s < nsb; ++s) {
+    const uint8_t* w0 = w_r0 + s * kQ4KBytes;
+    const uint8_t* w1 = w_r1 + s * kQ4KBytes;
+    const uint4 h0 = __ldg(reinterpret_cast<const uint4*>(w0));
+    const uint4 h1 = __ldg(reinterpret_cast<const uint4*>(w1));
+    uint32_t q0[4][2], q1[4][2];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      q0[c][0] = __ldg(reinterpret_cast<const uint32_t*>(w0 + 16 + 32 * c + 4 * tig));
+      q0[c][1] = __ldg(reinterpret_cast<const uint32_t*>(w0 + 16 + 32 * c + 16 + 4 * tig));
+      q1[c][0] = __ldg(reinterpret_cast<const uint32_t*>(w1 + 16 + 32 * c + 4 * tig));
+      q1[c][1] = __ldg(reinterpret_cast<const uint32_t*>(w1 + 16 + 32 * c + 16 + 4 * tig));
+    }
+    const uint8_t* ag = act_g + s * kQ8Stride;
+    const uint8_t* a0p = act_t0 + s * kQ8Stride;
+    const uint8_t* a1p = act_t1 + s * kQ8Stride;
+    // Scales and mins (6 bits, one per byte) of both rows.
+    const uint32_t sc0a = h0.y & 0x3F3F3F3Fu, m0a = h0.z & 0x3F3F3F3Fu;
+    const uint32_t sc0b = (h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u);
+    const uint32_t m0b = ((h0.w >> 4) & 0x0F0F0F0Fu) | ((h0.z >> 2) & 0x30303030u);
+    const uint32_t sc1a = h1.y & 0x3F3F3F3Fu, m1a = h1.z & 0x3F3F3F3Fu;
+    const uint32_t sc1b = (h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u);
+    const uint32_t m1b = ((h1.w >> 4) & 0x0F0F0F0Fu) | ((h1.z >> 2) & 0x30303030u);
+    int sumi[2][2] = {{0, 0}, {0, 0}};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = j >> 1;
+      const bool hi = (j & 1) != 0;
+      const uint32_t a0 = hi ? (q0[c][0] >> 4) & m4 : q0[c][0] & m4;
+      const uint32_t a1 = hi ? (q1[c][0] >> 4) & m4 : q1[c][0] & m4;
+      const uint32_t a2 = hi ? (q0[c][1] >> 4) & m4 : q0[c][1] & m4;
+      const uint32_t a3 = hi ? (q1[c][1] >> 4) & m4 : q1[c][1] & m4;
+      const uint32_t b0 = *reinterpret_cast<const uint32_t*>(ag + 32 * j + 4 * tig);
+      const uint32_t b1 = *reinterpret_cast<const uint32_t*>(ag + 32 * j + 16 + 4 * tig);
+      int d[4];
+      mma_s8(d, a0, a1, a2, a3, b0, b1);
+      const int s0 = byte_of(j < 4 ? sc0a : sc0b, j & 3), s1 = byte_of(j < 4 ? sc1a : sc1b, j & 3);
+      sumi[0][0] += s0 * d[0];
+      sumi[0][1] += s0 * d[1];
+      sumi[1][0] += s1 * d[2];
+      sumi[1][1] += s1 * d[3];
+    }
+    // summ and the f32 super-block values for the thread's two tokens.
+    const uint8_t* at[2] = {a0p, a1p};
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      const int4 bs0 = *reinterpret_cast<const int4*>(at[t] + 256);
+      const int4 bs1 = *reinterpret_cast<const int4*>(at[t] + 272);
+      const int bsw[8] = {bs0.x, bs0.y, bs0.z, bs0.w, bs1.x, bs1.y, bs1.z, bs1.w};
+      const float yd = *reinterpret_cast<const float*>(at[t] + 288);
+      int summ0 = 0, summ1 = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int pair = lo16(bsw[j]) + hi16(bsw[j]);
+        summ0 += byte_of(j < 4 ? m0a : m0b, j & 3) * pair;
+        summ1 += byte_of(j < 4 ? m1a : m1b, j & 3) * pair;
+      }
+      const float d0 = half_bits_to_float(h0.x), dmin0 = half_bits_to_float(h0.x >> 16);
+      const float d1 = half_bits_to_float(h1.x), dmin1 = half_bits_to_float(h1.x >> 16);
+      tree[0][t].add(s, __fsub_rn(__fmul_rn(__fmul_rn(d0, yd), static_cast<float>(sumi[0][t])),
+                                  __fmul_rn(__fmul_rn(dmin0, yd), static_cast<float>(summ0))));
+      tree[1][t].add(s, __fsub_rn(__fmul_rn(__fmul_rn(d1, yd), static_cast<float>(sumi[1][t])),
+                                  __fmul_rn(__fmul_rn(dmin1, yd), static_cast<float>(summ1))));
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 2; ++r)
+#pragma unroll
+    for (int t = 0; t < 2; ++t) out[r][t] = tree[r][t].r;
+}
+
+__global__ void __launch_bounds__(kBatchWarps * 32) batch_mma_kernel(const GroupArgs p) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, tig = lane & 3;
+  const int nsb = p.K / QK;
+  const int tiles_per_group = (p.rows + 15) / 16;
+  const int ctas_per_group = (tiles_per_group + kBatchWarps - 1) / kBatchWarps;
+  const int e = blockIdx.x / ctas_per_group;
+  const int rt = (blockIdx.x % ctas_per_group) * kBatchWarps + warp;
+  pdl_wait();
+  pdl_trigger();
+  if (rt >= tiles_per_group) return;
+  const int t_off = p.off != nullptr ? p.off[e] : 0;
+  const int t_cnt = p.off != nullptr ? p.cnt[e] : p.n_tok;
+  if (t_cnt <= 0) return;
+  const int row0 = rt * 16 + g, row1 = row0 + 8;
+  const int rr0 = min(row0, p.rows - 1), rr1 = min(row1, p.rows - 1);
+  const uint8_t* W = p.w + static_cast<uint64_t>(e) * p.mstride;
+  const uint8_t* W2 = p.w2 != nullptr ? p.w2 + static_cast<uint64_t>(e) * p.mstride2 : nullptr;
+  const int blk_bytes = nsb * kQ8Stride;
+  // Token tiles of 8: ungrouped products split them over blockIdx.y.
+  const int n_tt = (t_cnt + 7) / 8;
+  for (int tt = blockIdx.y; tt < n_tt; tt += gridDim.y) {
+    const int tbase = tt * 8;
+    auto act_row = [&](int t) {
+      const int tc = min(tbase + t, t_cnt - 1);
+      const int a = p.act_idx != nullptr ? p.act_idx[t_off + tc] : tc;
+      return p.q8 + static_cast<int64_t>(a) * blk_bytes;
+    };
+    const uint8_t* act_g = act_row(g);
+    const uint8_t* act_t0 = act_row(2 * tig);
+    const uint8_t* act_t1 = act_row(2 * tig + 1);
+    float v[2][2], v2[2][2];
+    tile_q4k_mma(W + static_cast<uint64_t>(rr0) * p.rb, W + static_cast<uint64_t>(rr1) * p.rb, p.rb, nsb, act_g,
+                 act_t0, act_t1, tig, v);
+    if (W2 != nullptr)
+      tile_q4k_mma(W2 + static_cast<uint64_t>(rr0) * p.rb2, W2 + static_cast<uint64_t>(rr1) * p.rb2, p.rb2, nsb,
+                   act_g, act_t0, act_t1, tig, v2);
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int row = r == 0 ? row0 : row1;
+      if (row >= p.rows) continue;
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int tok = tbase + 2 * tig + t;
+        if (tok >= t_cnt) continue;
+        const int o = p.out_idx != nullptr ? p.out_idx[t_off + tok] : tok;
+        float* dst = p.out + static_cast<int64_t>(o) * p.out_stride + row;
+        if (p.mode == kStore) {
+          *dst = v[r][t];
+        } else if (p.mode == kResidual) {
+          *dst = __fadd_rn(*dst, v[r][t]);
+        } else {
+          const float gv = v[r][t];
+          const float sl = __fdiv_rn(gv, __fadd_rn(1.0f, exp_cw(-gv)));
+          *dst = __fmul_rn(sl, v2[r][t]);
+        }
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------- QK-norm, RoPE, KV append
 // One CTA per sequence: QK-norm over the full q (and k) width, NEOX RoPE at
 // the shared position, the rotated q to qr, and the new K (rotated) and V
@@ -837,6 +1025,18 @@ extern "C" int nh_batch_rowdot(const NhGroupedRowDot* g, void* stream) {
   while (p.tok_tile > 8 && static_cast<int64_t>(p.n_groups) * p.row_blocks * ((max_tok + p.tok_tile - 1) / p.tok_tile) <
                                4 * sms)
     p.tok_tile >>= 1;
+  if (p.type == NH_TYPE_Q4_K && (p.w2 == nullptr || p.type2 == NH_TYPE_Q4_K) && batch_mma_enabled()) {
+    // Tensor-core form: one warp per 16-row tile; ungrouped products also
+    // split their token tiles over grid.y to fill the GPU.
+    const int row_tiles = (p.rows + 15) / 16;
+    const int ctas_per_group = (row_tiles + kBatchWarps - 1) / kBatchWarps;
+    const int tok_tiles = (max_tok + 7) / 8;
+    int gy = 1;
+    if (p.off == nullptr)
+      while (gy < tok_tiles && static_cast<int64_t>(ctas_per_group) * p.n_groups * gy < 4 * sms) ++gy;
+    return launch_pdl(batch_mma_kernel, dim3(p.n_groups * ctas_per_group, gy), dim3(kBatchWarps * 32), 0,
+                      static_cast<cudaStream_t>(stream), p);
+  }
   const int tiles = (max_tok + p.tok_tile - 1) / p.tok_tile;
   const size_t smem = static_cast<size_t>(p.tok_tile) * (p.K / QK) * kQ8Stride;
   static size_t configured = 48 * 1024;

@@ -59,6 +59,17 @@ inline int ctas_per_sm_cap() {
   return v;
 }
 
+// Batched Q4_K products run on the tensor cores unless NH_BATCH_MMA=0 (read
+// once; both forms give identical results).
+inline bool batch_mma_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("NH_BATCH_MMA");
+    v = (e != nullptr && e[0] == '0') ? 0 : 1;
+  }
+  return v != 0;
+}
+
 // Thread-block clusters that share the activation preparation are used only
 // when NH_CLUSTER=1 (read once).  Measured on B200 they cost more in cluster
 // barriers and scheduling than the shared preparation saves, so the default
