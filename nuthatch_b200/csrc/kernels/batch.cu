@@ -436,7 +436,93 @@ __device__ __forceinline__ void tile_q4k_mma(const uint8_t* w_r0, const uint8_t*
     for (int t = 0; t < 2; ++t) out[r][t] = tree[r][t].r;
 }
 
-__global__ void __launch_bounds__(kBatchWarps * 32) batch_mma_kernel(const GroupArgs p) {
+__device__ __forceinline__ void mma_s8_k16(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%8,%9,%10};\n"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(b0), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+// Q6_K: mma m16n8k16 per 16-value group (the format's int8 scale changes
+// every 16 values): sumi += sc_g * (dot_g - 32 * bsum_g), then
+// (d*yd)*sumi per super-block and the pairwise tree, as sb_dot_q6k3 forms it.
+// Super-blocks are 210 bytes, so rows start 2-byte aligned: words are
+// assembled from aligned loads with funnel shifts.
+__device__ __forceinline__ void tile_q6k_mma(const uint8_t* w_r0, const uint8_t* w_r1, int nsb,
+                                             const uint8_t* act_g, const uint8_t* act_t0, const uint8_t* act_t1,
+                                             int tig, float (&out)[2][2]) {
+  SbTree tree[2][2];
+  for (int s = 0; s < nsb; ++s) {
+    const uint8_t* wr[2] = {w_r0 + s * kQ6KBytes, w_r1 + s * kQ6KBytes};
+    const uint32_t* base[2];
+    uint32_t sh[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const uintptr_t addr = reinterpret_cast<uintptr_t>(wr[r]);
+      base[r] = reinterpret_cast<const uint32_t*>(addr & ~static_cast<uintptr_t>(3));
+      sh[r] = static_cast<uint32_t>(addr & 3) * 8;
+    }
+    auto word = [&](int r, int i) { return __funnelshift_r(__ldg(base[r] + i), __ldg(base[r] + i + 1), sh[r]); };
+    uint32_t scw[2][4];
+    float dd[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+#pragma unroll
+      for (int w = 0; w < 4; ++w) scw[r][w] = word(r, 48 + w);
+      dd[r] = half_bits_to_float(word(r, 52));
+    }
+    const uint8_t* ag = act_g + s * kQ8Stride;
+    const uint8_t* at[2] = {act_t0 + s * kQ8Stride, act_t1 + s * kQ8Stride};
+    int bsw[2][8];
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      const int4 v0 = *reinterpret_cast<const int4*>(at[t] + 256);
+      const int4 v1 = *reinterpret_cast<const int4*>(at[t] + 272);
+      bsw[t][0] = v0.x; bsw[t][1] = v0.y; bsw[t][2] = v0.z; bsw[t][3] = v0.w;
+      bsw[t][4] = v1.x; bsw[t][5] = v1.y; bsw[t][6] = v1.z; bsw[t][7] = v1.w;
+    }
+    int sumi[2][2] = {{0, 0}, {0, 0}};
+#pragma unroll
+    for (int gi = 0; gi < 16; ++gi) {
+      // This thread's four values of group gi: elements 16*gi + 4*tig .. +3.
+      const int e0 = 16 * gi + 4 * tig;
+      const int hh = e0 >> 7, ee = e0 & 127;
+      const int ql_word = (64 * hh + (ee & 63)) >> 2, ql_shift = (ee >> 6) * 4;
+      const int qh_word = (128 + 32 * hh + (ee & 31)) >> 2, qh_shift = 2 * (ee >> 5);
+      uint32_t a[2];
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const uint32_t lo = (word(r, ql_word) >> ql_shift) & 0x0F0F0F0Fu;
+        const uint32_t hi = ((word(r, qh_word) >> qh_shift) & 0x03030303u) << 4;
+        a[r] = lo | hi;
+      }
+      const uint32_t b = *reinterpret_cast<const uint32_t*>(ag + 16 * gi + 4 * tig);
+      int d[4];
+      mma_s8_k16(d, a[0], a[1], b);
+      const int sc0 = static_cast<int>(static_cast<int8_t>((scw[0][gi >> 2] >> (8 * (gi & 3))) & 0xFF));
+      const int sc1 = static_cast<int>(static_cast<int8_t>((scw[1][gi >> 2] >> (8 * (gi & 3))) & 0xFF));
+      const int bs0 = (gi & 1) ? hi16(bsw[0][gi >> 1]) : lo16(bsw[0][gi >> 1]);
+      const int bs1 = (gi & 1) ? hi16(bsw[1][gi >> 1]) : lo16(bsw[1][gi >> 1]);
+      sumi[0][0] += sc0 * (d[0] - 32 * bs0);
+      sumi[0][1] += sc0 * (d[1] - 32 * bs1);
+      sumi[1][0] += sc1 * (d[2] - 32 * bs0);
+      sumi[1][1] += sc1 * (d[3] - 32 * bs1);
+    }
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      const float yd = *reinterpret_cast<const float*>(at[t] + 288);
+#pragma unroll
+      for (int r = 0; r < 2; ++r)
+        tree[r][t].add(s, __fmul_rn(__fmul_rn(dd[r], yd), static_cast<float>(sumi[r][t])));
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 2; ++r)
+#pragma unroll
+    for (int t = 0; t < 2; ++t) out[r][t] = tree[r][t].r;
+}
+
+__global__ void __launch_bounds__(kBatchWarps * 32, 2) batch_mma_kernel(const GroupArgs p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, tig = lane & 3;
   const int nsb = p.K / QK;
@@ -468,11 +554,20 @@ __global__ void __launch_bounds__(kBatchWarps * 32) batch_mma_kernel(const Group
     const uint8_t* act_t0 = act_row(2 * tig);
     const uint8_t* act_t1 = act_row(2 * tig + 1);
     float v[2][2], v2[2][2];
-    tile_q4k_mma(W + static_cast<uint64_t>(rr0) * p.rb, W + static_cast<uint64_t>(rr1) * p.rb, p.rb, nsb, act_g,
-                 act_t0, act_t1, tig, v);
-    if (W2 != nullptr)
-      tile_q4k_mma(W2 + static_cast<uint64_t>(rr0) * p.rb2, W2 + static_cast<uint64_t>(rr1) * p.rb2, p.rb2, nsb,
-                   act_g, act_t0, act_t1, tig, v2);
+    if (p.type == NH_TYPE_Q4_K)
+      tile_q4k_mma(W + static_cast<uint64_t>(rr0) * p.rb, W + static_cast<uint64_t>(rr1) * p.rb, p.rb, nsb, act_g,
+                   act_t0, act_t1, tig, v);
+    else
+      tile_q6k_mma(W + static_cast<uint64_t>(rr0) * p.rb, W + static_cast<uint64_t>(rr1) * p.rb, nsb, act_g, act_t0,
+                   act_t1, tig, v);
+    if (W2 != nullptr) {
+      if (p.type2 == NH_TYPE_Q4_K)
+        tile_q4k_mma(W2 + static_cast<uint64_t>(rr0) * p.rb2, W2 + static_cast<uint64_t>(rr1) * p.rb2, p.rb2, nsb,
+                     act_g, act_t0, act_t1, tig, v2);
+      else
+        tile_q6k_mma(W2 + static_cast<uint64_t>(rr0) * p.rb2, W2 + static_cast<uint64_t>(rr1) * p.rb2, nsb, act_g,
+                     act_t0, act_t1, tig, v2);
+    }
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
       const int row = r == 0 ? row0 : row1;
@@ -1025,7 +1120,7 @@ extern "C" int nh_batch_rowdot(const NhGroupedRowDot* g, void* stream) {
   while (p.tok_tile > 8 && static_cast<int64_t>(p.n_groups) * p.row_blocks * ((max_tok + p.tok_tile - 1) / p.tok_tile) <
                                4 * sms)
     p.tok_tile >>= 1;
-  if (p.type == NH_TYPE_Q4_K && (p.w2 == nullptr || p.type2 == NH_TYPE_Q4_K) && batch_mma_enabled()) {
+  if (batch_mma_enabled()) {
     // Tensor-core form: one warp per 16-row tile; ungrouped products also
     // split their token tiles over grid.y to fill the GPU.
     const int row_tiles = (p.rows + 15) / 16;

@@ -59,7 +59,7 @@ inline int ctas_per_sm_cap() {
   return v;
 }
 
-// Batched Q4_K products run on the tensor cores unless NH_BATCH_MMA=0 (read
+// Batched Q4_K/Q6_K products run on the tensor cores unless NH_BATCH_MMA=0 (read
 // once; both forms give identical results).
 inline bool batch_mma_enabled() {
   static int v = -1;
