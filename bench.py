@@ -42,6 +42,10 @@ WORKLOAD = "olmoe-1b7b-q4km-resident-decode-bs1 (prompt 16, 24 greedy tokens)"
 # on Q6_K attn_v layers), router 524,288 B, 8 experts x 3,538,944 B (4,079,616
 # on Q6_K ffn_down layers); lm_head 84,510,720 B.
 GATE_UP_BYTES = 8 * 2 * 1024 * 1152  # one nh_moe_gate_up launch: 8 experts x (gate + up) rows of 1152 B
+# One nh_moe_layer launch (router + gate/up + down), averaged over the 16
+# layers: router 524,288 B + gate/up 18,874,368 B + down 8 x 2048 rows of 576 B
+# (Q4_K layers) or 840 B (Q6_K layers), 8 of each.
+MOE_LAYER_BYTES = 524288 + GATE_UP_BYTES + (8 * 2048 * 576 + 8 * 2048 * 840) // 2
 
 
 def step_bytes_per_token(cfg_layers=16) -> float:
@@ -67,11 +71,12 @@ def measured_peaks() -> dict:
     return {"hbm_gbs": 6650.0, "source": "fallback"}
 
 
-def traffic_summary() -> float | None:
+def traffic_summary(kernel: str) -> float | None:
+    """DRAM bytes per launch of `kernel` from the committed ncu summary."""
     p = ROOT / "profiles" / "traffic.json"
     if p.exists():
         try:
-            return float(json.loads(p.read_text())["moe_gate_up_dram_bytes_per_launch"])
+            return float(json.loads(p.read_text())[f"{kernel}_dram_bytes_per_launch"])
         except Exception:
             return None
     return None
@@ -399,23 +404,29 @@ def main() -> None:
     launches_per_token = L.nh_generate_launches(m._h)
     gpu_launches = args.steps * N_PREDICT * launches_per_token
 
-    # ---- dominant kernel (expert gate/up) timed alone on the same stream,
-    # cycling through all 16 layers so every launch streams its weights from HBM.
+    # ---- dominant kernel timed alone on the same stream, cycling through all
+    # 16 layers so every launch streams its weights from HBM: the fused MoE
+    # block (router + gate/up + down) when the step uses it, else gate/up.
+    fused = launches_per_token == 2 + 4 * 16
+    which, kbytes = (3, MOE_LAYER_BYTES) if fused else (0, GATE_UP_BYTES)
     reps = 20
     k0 = torch.cuda.Event(enable_timing=True)
     k1 = torch.cuda.Event(enable_timing=True)
-    L.nh_decode_kernel_loop(m._h, 0, 2)
+    L.nh_decode_kernel_loop(m._h, which, 2)
     k0.record(stream)
-    n_k = L.nh_decode_kernel_loop(m._h, 0, reps)
+    n_k = L.nh_decode_kernel_loop(m._h, which, reps)
     k1.record(stream)
     torch.cuda.synchronize()
+    assert n_k > 0, f"kernel loop failed ({n_k})"
     k_ms = k0.elapsed_time(k1) / n_k
     peaks = measured_peaks()
-    achieved = GATE_UP_BYTES / (k_ms / 1000.0) / 1e9
-    traffic = traffic_summary()
-    roofline = {"kernel": "nh_moe_gate_up (8 experts x gate+up, Q4_K)", "bound": "hbm", "achieved": achieved,
+    achieved = kbytes / (k_ms / 1000.0) / 1e9
+    traffic = traffic_summary("moe_layer" if fused else "moe_gate_up")
+    kname = ("nh_moe_layer (router + 8 experts gate/up + down, Q4_K/Q6_K)" if fused
+             else "nh_moe_gate_up (8 experts x gate+up, Q4_K)")
+    roofline = {"kernel": kname, "bound": "hbm", "achieved": achieved,
                 "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
-                "algorithmic_bytes_per_launch": GATE_UP_BYTES, "avg_launch_us": k_ms * 1000.0,
+                "algorithmic_bytes_per_launch": kbytes, "avg_launch_us": k_ms * 1000.0,
                 "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs, burst copy)"}
     tok_s_1 = N_PREDICT * args.steps / (ms / 1000.0)
     step_bytes = step_bytes_per_token()

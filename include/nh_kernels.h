@@ -175,6 +175,44 @@ int nh_moe_down_combine(const NhDecodeState* state, const float* ff, const int32
                         float* dump, int64_t dump_step_stride, int64_t dump_offset,
                         void* stream);
 
+/* The whole MoE block of one layer (moe.cc:16-60, forward.cc:111-119) as one
+ * cooperative kernel: nh_router_topk, nh_moe_gate_up and nh_moe_down_combine
+ * in sequence, the same results bit for bit, with the stages separated by
+ * device-side waits instead of kernel boundaries.  Q4_K/Q6_K expert tensors
+ * with n_embd/256 and n_ff/256 in {1,2,4,8} and (32/(n_ff/256)) % k == 0;
+ * outside that range (or when the grid cannot be co-resident) it returns
+ * NH_E_ARG or NH_E_TYPE having launched nothing, and the three kernels above
+ * do the work.  `scratch`: nh_moe_layer_scratch_bytes(n_expert) bytes,
+ * zeroed once (the kernel leaves it zeroed). */
+typedef struct NhMoeLayer {
+  NhDecodeState* state;
+  float* h;                 /* in: the residual stream; out: h + MoE(h) */
+  const float* ffn_norm;
+  float eps;
+  const float* router;      /* [n_expert][n_embd] f32 */
+  int64_t n_embd, n_ff;
+  int n_expert, k, norm_topk, layer, n_layers;
+  const void* gate;
+  int32_t tg;
+  uint64_t gate_nb2;
+  const void* up;
+  int32_t tu;
+  uint64_t up_nb2;
+  const void* down;
+  int32_t td;
+  uint64_t down_nb2;
+  int32_t* sel;             /* [k] selected experts (router output) */
+  float* wts;               /* [k] their weights */
+  int32_t* trace_sel;       /* optional, as nh_router_topk */
+  float* trace_gap;
+  float* ff;                /* [k][n_ff] */
+  float* dump;              /* optional, as nh_moe_down_combine */
+  int64_t dump_step_stride, dump_offset;
+  void* scratch;
+} NhMoeLayer;
+int64_t nh_moe_layer_scratch_bytes(int n_expert);
+int nh_moe_layer(const NhMoeLayer* layer, void* stream);
+
 /* Output norm, lm_head GEMV and greedy argmax (forward.cc:123-125,
  * generate.cc:93-102): first maximum wins.  Skipped (beyond the state
  * advance) for positions before the last prompt token.  The last CTA writes

@@ -27,6 +27,15 @@ class NhDecodeState(C.Structure):
                 ("error", i32), ("pad0", i32), ("pad1", i32)]
 
 
+class NhMoeLayer(C.Structure):
+    _fields_ = [("state", vp), ("h", vp), ("ffn_norm", vp), ("eps", f32), ("router", vp), ("n_embd", i64),
+                ("n_ff", i64), ("n_expert", C.c_int), ("k", C.c_int), ("norm_topk", C.c_int), ("layer", C.c_int),
+                ("n_layers", C.c_int), ("gate", vp), ("tg", i32), ("gate_nb2", u64), ("up", vp), ("tu", i32),
+                ("up_nb2", u64), ("down", vp), ("td", i32), ("down_nb2", u64), ("sel", vp), ("wts", vp),
+                ("trace_sel", vp), ("trace_gap", vp), ("ff", vp), ("dump", vp), ("dump_step_stride", i64),
+                ("dump_offset", i64), ("scratch", vp)]
+
+
 # name -> (restype, argtypes)
 SIGNATURES = {
     # nh_api.h
@@ -89,6 +98,8 @@ SIGNATURES = {
     "nh_moe_gate_up_prefetch": (C.c_int, [vp, vp, vp, f32, vp, C.c_int, vp, i32, u64, vp, i32, u64, i64, i64, vp,
                                           vp, u64, vp]),
     "nh_moe_down_combine": (C.c_int, [vp, vp, vp, vp, C.c_int, vp, i32, u64, i64, i64, vp, vp, i64, i64, vp]),
+    "nh_moe_layer": (C.c_int, [P(NhMoeLayer), vp]),
+    "nh_moe_layer_scratch_bytes": (i64, [C.c_int]),
     "nh_lm_head_argmax": (C.c_int, [vp, vp, vp, f32, vp, i32, i64, i64, vp, vp, vp, vp]),
     "nh_gemv": (C.c_int, [vp, vp, i32, i64, i64, vp, vp, f32, vp, vp]),
     "nh_quantize_q8k": (C.c_int, [vp, i64, vp, vp]),

@@ -146,7 +146,12 @@ int nh_generate(void* model, int mode, const int32_t* prompt, int n_prompt, int 
 
 int nh_generate_launches(const void* model) {
   if (model == nullptr) return NH_E_ARG;
-  return 2 + 6 * static_cast<int>(static_cast<const OlmoeModel*>(model)->config().n_layers);
+  // The count the last resident step enqueued (four or six kernels per
+  // layer, with or without the fused MoE block); before any step, the
+  // six-kernel form's count.
+  const auto* m = static_cast<const OlmoeModel*>(model);
+  const int n = m->workspace() != nullptr ? m->workspace()->engine.step_launches() : 0;
+  return n > 0 ? n : 2 + 6 * static_cast<int>(m->config().n_layers);
 }
 
 int nh_generate_batch(void* model, const int32_t* prompts, int n_seq, int n_prompt, int n_predict, int norm_topk,

@@ -2,6 +2,7 @@
 #include "engine.h"
 
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 
@@ -26,6 +27,17 @@ int HostAlloc(T** p, size_t count) {
              ? NH_OK
              : NH_E_NOMEM;
 }
+// Resident steps run each layer's MoE block as one cooperative kernel unless
+// NH_FUSED_MOE=0 (read once; both forms give identical results).
+bool FusedMoeEnabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("NH_FUSED_MOE");
+    v = (e != nullptr && e[0] == '0') ? 0 : 1;
+  }
+  return v != 0;
+}
+
 template <typename T>
 void DevFree(T*& p) {
   if (p != nullptr) cudaFree(p);
@@ -150,8 +162,9 @@ void Engine::FreeAll() {
   DevFree(rope_cs_);
   if (attn_scratch_) cudaFree(attn_scratch_);
   if (router_scratch_) cudaFree(router_scratch_);
+  if (moe_scratch_) cudaFree(moe_scratch_);
   if (argmax_scratch_) cudaFree(argmax_scratch_);
-  attn_scratch_ = router_scratch_ = argmax_scratch_ = nullptr;
+  attn_scratch_ = router_scratch_ = moe_scratch_ = argmax_scratch_ = nullptr;
   DevFree(trace_sel_);
   DevFree(trace_gap_);
   DevFree(dump_hidden_);
@@ -201,11 +214,13 @@ int Engine::Reserve(int max_seq, int max_prompt, int max_predict, bool dumps) {
   const int64_t ab = nh_attention_scratch_bytes(c.n_head, static_cast<int>(hd), max_seq);
   const int64_t rb = nh_router_scratch_bytes(c.n_expert);
   const int64_t mb = nh_argmax_scratch_bytes(c.n_vocab);
+  const int64_t fb = nh_moe_layer_scratch_bytes(c.n_expert);
   if (cudaMalloc(&attn_scratch_, ab) != cudaSuccess || cudaMalloc(&router_scratch_, rb) != cudaSuccess ||
-      cudaMalloc(&argmax_scratch_, mb) != cudaSuccess)
+      cudaMalloc(&moe_scratch_, fb) != cudaSuccess || cudaMalloc(&argmax_scratch_, mb) != cudaSuccess)
     return NH_E_NOMEM;
   cudaMemset(attn_scratch_, 0, ab);
   cudaMemset(router_scratch_, 0, rb);
+  cudaMemset(moe_scratch_, 0, fb);
   cudaMemset(argmax_scratch_, 0, mb);
   NH_TRY(DevAlloc(&trace_sel_, static_cast<size_t>(max_seq) * L * K));
   NH_TRY(DevAlloc(&trace_gap_, static_cast<size_t>(max_seq) * L));
@@ -238,17 +253,60 @@ int Engine::EnqueueEmbed(const ModelView& m) {
   return nh_embed_step(state_, prompt_, m.embd, m.te, cfg_.n_embd, cfg_.n_vocab, h_, stream_);
 }
 
-int Engine::EnqueueAttnPhase(const ModelView& m, int l, bool norm_topk, bool trace) {
+int Engine::EnqueueAttention(const ModelView& m, int l) {
   const OlmoeConfig& c = cfg_;
   const LayerView& L = m.layers[l];
   const int64_t dkv = static_cast<int64_t>(c.n_head_kv) * c.head_dim();
   const int hd = static_cast<int>(c.head_dim());
   const float kq_scale = 1.0f / std::sqrt(static_cast<float>(hd));
-  NH_TRY(nh_qkv_proj(state_, h_,L.attn_norm, c.rms_eps, L.wq, L.tq, L.wk, L.tk, L.wv, L.tv, c.n_embd, dkv, q_, k_, v_,
-                     stream_));
+  NH_TRY(nh_qkv_proj(state_, h_, L.attn_norm, c.rms_eps, L.wq, L.tq, L.wk, L.tk, L.wv, L.tv, c.n_embd, dkv, q_, k_,
+                     v_, stream_));
   NH_TRY(nh_attention_step(state_, q_, k_, v_, L.q_norm, L.k_norm, c.rms_eps, c.n_head, c.n_head_kv, hd, rope_cs_,
                            kq_scale, kv_->k(l), kv_->v(l), max_seq_, attn_scratch_, attn_, stream_));
-  NH_TRY(nh_out_proj_residual(state_, attn_, L.wo, L.to, c.n_embd, h_, stream_));
+  return nh_out_proj_residual(state_, attn_, L.wo, L.to, c.n_embd, h_, stream_);
+}
+
+int Engine::EnqueueFusedMoe(const ModelView& m, int l, bool norm_topk, bool trace, bool dumps) {
+  const OlmoeConfig& c = cfg_;
+  const LayerView& L = m.layers[l];
+  NhMoeLayer a{};
+  a.state = state_;
+  a.h = h_;
+  a.ffn_norm = L.ffn_norm;
+  a.eps = c.rms_eps;
+  a.router = L.router;
+  a.n_embd = c.n_embd;
+  a.n_ff = c.n_ff;
+  a.n_expert = static_cast<int>(c.n_expert);
+  a.k = static_cast<int>(c.n_expert_used);
+  a.norm_topk = norm_topk ? 1 : 0;
+  a.layer = l;
+  a.n_layers = static_cast<int>(c.n_layers);
+  a.gate = L.gate;
+  a.tg = L.tg;
+  a.gate_nb2 = L.gate_nb2;
+  a.up = L.up;
+  a.tu = L.tu;
+  a.up_nb2 = L.up_nb2;
+  a.down = L.down;
+  a.td = L.td;
+  a.down_nb2 = L.down_nb2;
+  a.sel = sel_;
+  a.wts = wts_;
+  a.trace_sel = trace ? trace_sel_ : nullptr;
+  a.trace_gap = trace ? trace_gap_ : nullptr;
+  a.ff = ff_;
+  a.dump = dumps ? dump_hidden_ : nullptr;
+  a.dump_step_stride = static_cast<int64_t>(c.n_layers) * c.n_embd;
+  a.dump_offset = l * c.n_embd;
+  a.scratch = moe_scratch_;
+  return nh_moe_layer(&a, stream_);
+}
+
+int Engine::EnqueueAttnPhase(const ModelView& m, int l, bool norm_topk, bool trace) {
+  const OlmoeConfig& c = cfg_;
+  const LayerView& L = m.layers[l];
+  NH_TRY(EnqueueAttention(m, l));
   return nh_router_topk(state_, h_, L.ffn_norm, c.rms_eps, L.router, c.n_embd, c.n_expert, c.n_expert_used,
                         norm_topk ? 1 : 0, sel_, wts_, trace ? trace_sel_ : nullptr, trace ? trace_gap_ : nullptr, l,
                         c.n_layers, router_scratch_, stream_);
@@ -274,13 +332,32 @@ int Engine::EnqueueFinal(const ModelView& m, bool dumps) {
 
 int Engine::EnqueueStep(const ModelView& m, bool norm_topk, bool trace, bool dumps) {
   NH_TRY(EnqueueEmbed(m));
+  int launches = 2;  // embed, lm_head
   for (int l = 0; l < static_cast<int>(cfg_.n_layers); ++l) {
     const LayerView& L = m.layers[l];
-    NH_TRY(EnqueueAttnPhase(m, l, norm_topk, trace));
+    launches += 6;
+    if (FusedMoeEnabled()) {
+      NH_TRY(EnqueueAttention(m, l));
+      const int rc = EnqueueFusedMoe(m, l, norm_topk, trace, dumps);
+      if (rc == NH_OK) {
+        launches -= 2;
+        continue;
+      }
+      if (rc != NH_E_ARG && rc != NH_E_TYPE) return rc;
+      // Shapes outside the fused kernel: router, gate/up and down separately.
+      const OlmoeConfig& c = cfg_;
+      NH_TRY(nh_router_topk(state_, h_, L.ffn_norm, c.rms_eps, L.router, c.n_embd, c.n_expert, c.n_expert_used,
+                            norm_topk ? 1 : 0, sel_, wts_, trace ? trace_sel_ : nullptr,
+                            trace ? trace_gap_ : nullptr, l, c.n_layers, router_scratch_, stream_));
+    } else {
+      NH_TRY(EnqueueAttnPhase(m, l, norm_topk, trace));
+    }
     NH_TRY(EnqueueMoePhase(m, l, L.gate, L.tg, L.gate_nb2, L.up, L.tu, L.up_nb2, L.down, L.td, L.down_nb2, sel_,
                            dumps));
   }
-  return EnqueueFinal(m, dumps);
+  NH_TRY(EnqueueFinal(m, dumps));
+  step_launches_ = launches;
+  return NH_OK;
 }
 
 int Engine::RunSteps(const ModelView& m, int steps, bool norm_topk, bool trace, bool dumps, bool use_graph) {
@@ -346,6 +423,8 @@ int Engine::KernelLoop(const ModelView& m, int which, int reps) {
       if (which == 0) {
         rc = nh_moe_gate_up(state_, h_,L.ffn_norm, c.rms_eps, sel_, c.n_expert_used, L.gate, L.tg, L.gate_nb2, L.up, L.tu,
                             L.up_nb2, c.n_embd, c.n_ff, ff_, stream_);
+      } else if (which == 3) {
+        rc = EnqueueFusedMoe(m, l, false, false, false);
       } else if (which == 1) {
         rc = nh_moe_down_combine(state_, ff_, sel_, wts_, c.n_expert_used, L.down, L.td, L.down_nb2, c.n_ff,
                                  c.n_embd, h_, nullptr, 0, 0, stream_);

@@ -61,7 +61,14 @@ class Engine {
   int Begin(const int32_t* prompt, int n_prompt, int n_predict);
 
   int EnqueueEmbed(const ModelView& m);
+  // QKV, attention and the output projection of one layer.
+  int EnqueueAttention(const ModelView& m, int layer);
+  // EnqueueAttention plus the router (phase A of the two-phase form).
   int EnqueueAttnPhase(const ModelView& m, int layer, bool norm_topk, bool trace);
+  // The whole MoE block of a resident layer in one cooperative kernel;
+  // NH_E_ARG / NH_E_TYPE (nothing enqueued) where that kernel does not cover
+  // the shapes.
+  int EnqueueFusedMoe(const ModelView& m, int layer, bool norm_topk, bool trace, bool dumps);
   // Phase B over expert weights at gate/up/down with per-slot selection wsel.
   int EnqueueMoePhase(const ModelView& m, int layer, const void* gate, int32_t tg, uint64_t gnb2,
                       const void* up, int32_t tu, uint64_t unb2, const void* down, int32_t td,
@@ -80,8 +87,11 @@ class Engine {
   int SaveState();
   int RestoreState();
   // Enqueues `reps` passes over all layers of one kernel with the current
-  // activations (0 expert gate/up, 1 expert down, 2 QKV); returns launches.
+  // activations (0 expert gate/up, 1 expert down, 2 QKV, 3 the fused MoE
+  // block, which also updates the residual); returns launches.
   int KernelLoop(const ModelView& m, int which, int reps);
+  // Kernels the last enqueued resident step launched (0 before the first).
+  int step_launches() const { return step_launches_; }
 
   cudaStream_t stream() const { return stream_; }
   int32_t* sel_dev() const { return sel_; }
@@ -123,6 +133,7 @@ class Engine {
   float* rope_cs_ = nullptr;
   void* attn_scratch_ = nullptr;
   void* router_scratch_ = nullptr;
+  void* moe_scratch_ = nullptr;
   void* argmax_scratch_ = nullptr;
   int32_t* trace_sel_ = nullptr;
   float* trace_gap_ = nullptr;
@@ -131,6 +142,7 @@ class Engine {
   cudaGraphExec_t graph_ = nullptr;
   uint64_t graph_key_ = ~0ull;
   uint64_t alloc_gen_ = 0;
+  int step_launches_ = 0;
 };
 
 }  // namespace nuthatch

@@ -143,6 +143,33 @@ int launch_pdl_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
   return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...) == cudaSuccess ? NH_OK : NH_E_CUDA;
 }
 
+// Cooperative launch: the runtime admits the grid only if every CTA can be
+// resident at once, so CTAs may wait for one another.  Programmatic dependent
+// launch is requested too; should the runtime refuse the pair, the launch is
+// repeated without it and the pair is not tried again.
+template <typename... KArgs, typename... Args>
+int launch_coop(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+  static bool pair_ok = true;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeCooperative;
+  at[0].val.cooperative = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = pdl_enabled();
+  cfg.attrs = at;
+  cfg.numAttrs = pair_ok ? 2 : 1;
+  if (cudaLaunchKernelEx(&cfg, kern, args...) == cudaSuccess) return NH_OK;
+  if (!pair_ok) return NH_E_CUDA;
+  (void)cudaGetLastError();
+  pair_ok = false;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...) == cudaSuccess ? NH_OK : NH_E_CUDA;
+}
+
 // Rounds a grid down to a multiple of the cluster size (at least one cluster).
 inline int round_grid(int grid, int cluster) {
   if (cluster <= 1) return grid;

@@ -8,6 +8,7 @@
 // weights depend on the router's choice, so staging starts after
 // griddepcontrol.wait.  The gate/up kernel also prefetches the chosen
 // experts' down rows into L2 for the kernel that follows it.
+#include <algorithm>
 #include <climits>
 
 #include "launch.cuh"
@@ -41,6 +42,133 @@ struct RouterArgs {
 // f32 router row in registers: lane l holds elements 4l + 128t (t < K/128).
 constexpr int kRouterMaxVec = kMaxK / 128;
 
+// The dot of router row e with the normalised activation (xf), the row's
+// lane slice already in registers when K % 128 == 0 (DotF32Vec128 order).
+__device__ __forceinline__ float router_logit(const RouterArgs& p, const float4 (&wv)[kRouterMaxVec],
+                                              const ActSmem& a, int e, int lane) {
+  if ((p.K % 128) == 0) {
+    float s = 0.f;
+#pragma unroll
+    for (int t = 0; t < kRouterMaxVec; ++t) {
+      if (t < p.K / 128) {
+        const float4 x = *reinterpret_cast<const float4*>(a.xf + 4 * lane + 128 * t);
+        s = __fadd_rn(s, __fmul_rn(wv[t].x, x.x));
+        s = __fadd_rn(s, __fmul_rn(wv[t].y, x.y));
+        s = __fadd_rn(s, __fmul_rn(wv[t].z, x.z));
+        s = __fadd_rn(s, __fmul_rn(wv[t].w, x.w));
+      }
+    }
+    return warp_sum(s);
+  }
+  return row_dot_f32(p.router + static_cast<int64_t>(e) * p.K, a.xf, p.K, lane);
+}
+
+__device__ __forceinline__ void router_load_row(const RouterArgs& p, float4 (&wv)[kRouterMaxVec], int e, int lane) {
+  if ((p.K % 128) == 0 && e < p.E) {
+    const float4* w4 = reinterpret_cast<const float4*>(p.router + static_cast<int64_t>(e) * p.K);
+#pragma unroll
+    for (int t = 0; t < kRouterMaxVec; ++t)
+      if (t < p.K / 128) wv[t] = w4[lane + 32 * t];
+  }
+}
+
+// Block-wide expert selection from the E router logits; any CTA that has the
+// logits may run it and all obtain the same result.  Warp 0 forms
+// ggml_soft_max (exp(x - max) in f32, lane l holding experts l, l+32, ...,
+// summed per lane then across lanes in double, scaled by 1/sum); thread i
+// then ranks expert i against all E probabilities (descending, equal
+// probabilities keep the lower expert id first: the order repeated argmax
+// would produce) and the top-(k+1) land in rank order.  Writes the k chosen
+// experts and their weights (renormalised when norm_topk, clamped sum
+// 6.103515625e-5) to o_sel/o_wts (shared) and, when `outputs`, to p.sel,
+// p.wts and the trace.  Needs blockDim.x >= 32 and >= k; ends synchronised.
+template <int KP>
+__device__ __forceinline__ void router_select_block(const RouterArgs& p, const float* logits, bool outputs,
+                                                    int64_t pos, int* o_sel, float* o_wts) {
+  __shared__ __align__(16) float s_prob[kMaxExperts];
+  __shared__ int s_ids[kMaxTopK + 1];
+  __shared__ float s_vals[kMaxTopK + 1];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int E = p.E;
+  const int kk = min(p.topk + 1, E);
+  // Every output slot starts in range: NaN probabilities (a corrupted
+  // activation) have no strict order and their ranks may collide.
+  if (tid < kk) {
+    s_ids[tid] = tid;
+    s_vals[tid] = 0.f;
+  }
+  if (warp == 0) {
+    float pr[KP];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < KP; ++k) {
+      const int i = lane + 32 * k;
+      pr[k] = i < E ? __ldcg(logits + i) : -INFINITY;
+      mx = fmaxf(mx, pr[k]);
+    }
+    mx = warp_max(mx);
+    double sum = 0.0;
+#pragma unroll
+    for (int k = 0; k < KP; ++k) {
+      const int i = lane + 32 * k;
+      pr[k] = i < E ? exp_cw(__fsub_rn(pr[k], mx)) : 0.f;
+      sum += static_cast<double>(pr[k]);
+    }
+    sum = warp_sum_d(sum);
+    const float inv = static_cast<float>(1.0 / sum);
+#pragma unroll
+    for (int k = 0; k < KP; ++k) {
+      const int i = lane + 32 * k;
+      if (i < E) s_prob[i] = __fmul_rn(pr[k], inv);
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < E; i += blockDim.x) {
+    const float pi = s_prob[i];
+    int r = 0;
+    int j = 0;
+    for (; j + 4 <= E; j += 4) {
+      const float4 q = *reinterpret_cast<const float4*>(s_prob + j);
+      r += (q.x > pi || (q.x == pi && j < i)) ? 1 : 0;
+      r += (q.y > pi || (q.y == pi && j + 1 < i)) ? 1 : 0;
+      r += (q.z > pi || (q.z == pi && j + 2 < i)) ? 1 : 0;
+      r += (q.w > pi || (q.w == pi && j + 3 < i)) ? 1 : 0;
+    }
+    for (; j < E; ++j) r += (s_prob[j] > pi || (s_prob[j] == pi && j < i)) ? 1 : 0;
+    if (r < kk) {
+      s_ids[r] = i;
+      s_vals[r] = pi;
+    }
+  }
+  __syncthreads();
+  if (tid < p.topk) {
+    float ws = 1.f;
+    if (p.norm_topk) {
+      double sw = 0.0;
+      for (int t = 0; t < p.topk; ++t) sw += static_cast<double>(s_vals[t]);
+      ws = fmaxf(static_cast<float>(sw), 6.103515625e-5f);
+    }
+    const int id = s_ids[tid];
+    const float w = p.norm_topk ? __fdiv_rn(s_vals[tid], ws) : s_vals[tid];
+    o_sel[tid] = id;
+    o_wts[tid] = w;
+    if (outputs) {
+      p.sel[tid] = id;
+      p.wts[tid] = w;
+      if (p.trace_sel != nullptr) p.trace_sel[(pos * p.n_layers + p.layer) * p.topk + tid] = id;
+    }
+  }
+  if (outputs && p.trace_sel != nullptr && p.trace_gap != nullptr && warp == 0) {
+    // Smallest gap between adjacent probabilities of the descending top-(k+1).
+    float g = 1.f;
+    for (int t = lane; t + 1 < kk; t += 32) g = fminf(g, __fsub_rn(s_vals[t], s_vals[t + 1]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) g = fminf(g, __shfl_xor_sync(0xffffffffu, g, o));
+    if (lane == 0) p.trace_gap[pos * p.n_layers + p.layer] = g;
+  }
+  __syncthreads();
+}
+
 // KP = experts per lane of the softmax / top-k warp (n_expert <= 32*KP).
 template <int KP>
 __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(const RouterArgs p) {
@@ -54,127 +182,31 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(const RouterA
   const int e = blockIdx.x * kRouterWarps + warp;
   // The router weights do not depend on the preceding kernel: load the row
   // before waiting for it.
-  const bool vec = (p.K % 128) == 0;
   float4 wv[kRouterMaxVec];
-  if (vec && e < p.E) {
-    const float4* w4 = reinterpret_cast<const float4*>(p.router + static_cast<int64_t>(e) * p.K);
-#pragma unroll
-    for (int t = 0; t < kRouterMaxVec; ++t)
-      if (t < p.K / 128) wv[t] = w4[lane + 32 * t];
-  }
+  router_load_row(p, wv, e, lane);
   cluster_load_norm(a, p.norm);
   pdl_wait();
   pdl_trigger();
   cluster_wait();
   cluster_prep_act(a, p.h, p.norm != nullptr, true, p.eps, false, true, red, s_part);
   if (e < p.E) {
-    float v;
-    if (vec) {
-      float s = 0.f;
-#pragma unroll
-      for (int t = 0; t < kRouterMaxVec; ++t) {
-        if (t < p.K / 128) {
-          const float4 x = *reinterpret_cast<const float4*>(a.xf + 4 * lane + 128 * t);
-          s = __fadd_rn(s, __fmul_rn(wv[t].x, x.x));
-          s = __fadd_rn(s, __fmul_rn(wv[t].y, x.y));
-          s = __fadd_rn(s, __fmul_rn(wv[t].z, x.z));
-          s = __fadd_rn(s, __fmul_rn(wv[t].w, x.w));
-        }
-      }
-      v = warp_sum(s);
-    } else {
-      v = row_dot_f32(p.router + static_cast<int64_t>(e) * p.K, a.xf, p.K, lane);
-    }
+    const float v = router_logit(p, wv, a, e, lane);
     if (lane == 0) p.logits[e] = v;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
     s_last = atomicAdd(p.ticket, 1u) == gridDim.x - 1;
+    if (s_last) {
+      *p.ticket = 0u;  // every CTA has taken its ticket
+      __threadfence();
+    }
   }
   __syncthreads();
-  if (!s_last || warp != 0) return;
-  __threadfence();
-  // ggml_soft_max over the E logits: exp(x - max) in f32, summed in double,
-  // scaled by 1/sum.  Lane l holds experts l, l+32, ...
-  const volatile float* lg = p.logits;
-  constexpr int kPer = KP;
-  float pr[kPer];
-  float mx = -INFINITY;
-#pragma unroll
-  for (int k = 0; k < kPer; ++k) {
-    const int i = lane + 32 * k;
-    pr[k] = i < p.E ? lg[i] : -INFINITY;
-    mx = fmaxf(mx, pr[k]);
-  }
-  mx = warp_max(mx);
-  double sum = 0.0;
-#pragma unroll
-  for (int k = 0; k < kPer; ++k) {
-    const int i = lane + 32 * k;
-    pr[k] = i < p.E ? exp_cw(__fsub_rn(pr[k], mx)) : 0.f;
-    sum += static_cast<double>(pr[k]);
-  }
-  sum = warp_sum_d(sum);
-  const float inv = static_cast<float>(1.0 / sum);
-#pragma unroll
-  for (int k = 0; k < kPer; ++k) pr[k] = __fmul_rn(pr[k], inv);
-  // Top-(k+1) by rank: descending probability, equal probabilities keep the
-  // lower expert id first (the order repeated argmax would produce).  Every
-  // lane ranks its own experts against all others, read by shuffles.
-  __shared__ int s_ids[kMaxTopK + 1];
-  __shared__ float s_vals[kMaxTopK + 1];
-  const int kk = min(p.topk + 1, p.E);
-  int rank[kPer];
-#pragma unroll
-  for (int k = 0; k < kPer; ++k) rank[k] = 0;
-#pragma unroll
-  for (int kj = 0; kj < kPer; ++kj) {
-#pragma unroll 8
-    for (int src = 0; src < 32; ++src) {
-      const float pj = __shfl_sync(0xffffffffu, pr[kj], src);
-      const int j = src + 32 * kj;
-#pragma unroll
-      for (int ki = 0; ki < kPer; ++ki) {
-        const int i = lane + 32 * ki;
-        rank[ki] += (j < p.E && (pj > pr[ki] || (pj == pr[ki] && j < i))) ? 1 : 0;
-      }
-    }
-  }
-#pragma unroll
-  for (int k = 0; k < kPer; ++k) {
-    const int i = lane + 32 * k;
-    if (i < p.E && rank[k] < kk) {
-      s_ids[rank[k]] = i;
-      s_vals[rank[k]] = pr[k];
-    }
-  }
-  __syncwarp();
-  // Lane t writes output t.
-  float ws = 1.f;
-  if (p.norm_topk) {
-    double sw = 0.0;
-    for (int t = 0; t < p.topk; ++t) sw += static_cast<double>(s_vals[t]);
-    ws = fmaxf(static_cast<float>(sw), 6.103515625e-5f);
-  }
-  const int64_t pos = p.state->pos;
-  for (int t = lane; t < p.topk; t += 32) {
-    const int id = s_ids[t];
-    const float v = s_vals[t];
-    p.sel[t] = id;
-    p.wts[t] = p.norm_topk ? __fdiv_rn(v, ws) : v;
-    if (p.trace_sel != nullptr) p.trace_sel[(pos * p.n_layers + p.layer) * p.topk + t] = id;
-  }
-  if (p.trace_sel != nullptr && p.trace_gap != nullptr) {
-    // Smallest gap between adjacent probabilities of the descending top-(k+1).
-    float g = 1.f;
-    for (int t = lane; t + 1 < kk; t += 32) g = fminf(g, __fsub_rn(s_vals[t], s_vals[t + 1]));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) g = fminf(g, __shfl_xor_sync(0xffffffffu, g, o));
-    if (lane == 0) p.trace_gap[pos * p.n_layers + p.layer] = g;
-  }
-  if (lane != 0) return;
-  *p.ticket = 0u;
+  if (!s_last) return;
+  __shared__ int s_sel[kMaxTopK];
+  __shared__ float s_wts[kMaxTopK];
+  router_select_block<KP>(p, p.logits, true, p.state->pos, s_sel, s_wts);
 }
 
 // ------------------------------------------------------------------ gate/up
@@ -464,6 +496,75 @@ __global__ void __launch_bounds__(kMoeWarps * 32) down_kernel(const DownArgs p) 
 // gate/up: a job is P = 32/G rows of one expert; pass 1 computes the P gate
 // rows, pass 2 the P up rows, so the lane that holds a gate row's value also
 // holds the matching up row's value and writes silu(gate)*up itself.
+// Job j of the gate/up kernels: expert slot i, its expert (or slot) e, the
+// first output row r0 and the row count n.
+__device__ __forceinline__ void gu3_job(const GateUpArgs& p, const int* s_sel, int j, int& i, int& e, int& r0,
+                                        int& n) {
+  i = j / p.jobs_per_expert;
+  r0 = (j - i * p.jobs_per_expert) * p.rpp;
+  n = min(p.rpp, p.F - r0);
+  e = s_sel[i];
+}
+
+// Lane 0 stages job j's gate and up rows into stage st.
+__device__ __forceinline__ void gu3_issue(const GateUpArgs& p, const int* s_sel, uint64_t* wbar, uint8_t* wb, int j,
+                                          int st, int lane) {
+  if (lane != 0) return;
+  int i, e, r0, n;
+  gu3_job(p, s_sel, j, i, e, r0, n);
+  uint32_t lg, og, lu, ou;
+  const uint8_t* sg = span16(p.gate + e * p.gate_nb2 + r0 * p.rb_g, n * p.rb_g, &lg, &og);
+  const uint8_t* su = span16(p.up + e * p.up_nb2 + r0 * p.rb_u, n * p.rb_u, &lu, &ou);
+  mbar_expect_tx(&wbar[st], lg + lu);
+  uint8_t* buf = wb + static_cast<size_t>(st) * p.stage_bytes;
+  bulk_g2s(buf, sg, lg, &wbar[st]);
+  bulk_g2s(buf + p.up_off, su, lu, &wbar[st]);
+}
+
+// Starts the selected experts' down weights towards L2 for the down pass:
+// this CTA's share, in pieces of at most 64 KB over warp 0's lanes.
+__device__ __forceinline__ void gu3_prefetch_down(const GateUpArgs& p, const int* s_sel, int warp, int lane) {
+  if (p.down == nullptr || warp != 0) return;
+  constexpr uint64_t kPiece = 64 * 1024;
+  const uint64_t total = p.down_nb2 * static_cast<uint64_t>(p.topk);
+  const uint64_t share = ((total / gridDim.x) + 15) & ~static_cast<uint64_t>(15);
+  const uint64_t beg = share * blockIdx.x;
+  const uint64_t end = beg + share < total ? beg + share : total;
+  for (uint64_t o = beg + static_cast<uint64_t>(lane) * kPiece; o < end; o += 32 * kPiece) {
+    // Pieces never straddle two experts: clip at the expert boundary.
+    const uint64_t i = o / p.down_nb2, in = o - i * p.down_nb2;
+    uint64_t len = end - o < kPiece ? end - o : kPiece;
+    if (in + len > p.down_nb2) len = p.down_nb2 - in;
+    prefetch_l2(p.down + static_cast<uint64_t>(s_sel[i]) * p.down_nb2 + in, static_cast<uint32_t>(len));
+  }
+}
+
+// The warp's jobs gw, gw+tw, ... (the first S already issued): returns false
+// when a stage wait expired.
+__device__ __forceinline__ bool gu3_run(const GateUpArgs& p, const int* s_sel, uint64_t* wbar, uint8_t* wb,
+                                        const Act3& act, int gw, int tw, int lane) {
+  const int G = p.lpr;
+  const int g = lane % G, r = lane / G;
+  for (int it = 0;; ++it) {
+    const int j = gw + it * tw;
+    if (j >= p.jobs_total) break;
+    const int st = it % p.S;
+    int i, e, r0, n;
+    gu3_job(p, s_sel, j, i, e, r0, n);
+    if (!mbar_wait(&wbar[st], (it / p.S) & 1)) return false;
+    const uint8_t* buf = wb + static_cast<size_t>(st) * p.stage_bytes;
+    const uint32_t og = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p.gate + e * p.gate_nb2 + r0 * p.rb_g) & 15);
+    const uint32_t ou = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p.up + e * p.up_nb2 + r0 * p.rb_u) & 15);
+    const float vg = row_dot3(buf + og + r * p.rb_g, p.tg, g, G, act);
+    const float vu = row_dot3(buf + p.up_off + ou + r * p.rb_u, p.tu, g, G, act);
+    if (g == 0 && r < n) p.ff[static_cast<int64_t>(i) * p.F + r0 + r] = silu_mul(vg, vu);
+    __syncwarp();
+    const int jn = gw + (it + p.S) * tw;
+    if (jn < p.jobs_total) gu3_issue(p, s_sel, wbar, wb, jn, st, lane);
+  }
+  return true;
+}
+
 __global__ void __launch_bounds__(kMoeWarps * 32, 2) gate_up3_kernel(const GateUpArgs p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -476,7 +577,6 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) gate_up3_kernel(const GateU
   __shared__ double s_part[8];
   cluster_arrive_relaxed();
   const int gw = blockIdx.x * kMoeWarps + warp, tw = gridDim.x * kMoeWarps;
-  const int G = p.lpr, P = p.rpp;
   uint64_t* wbar = bars + warp * p.S;
   uint8_t* wb = stage + static_cast<size_t>(warp) * p.S * p.stage_bytes;
   if (lane == 0) {
@@ -489,78 +589,82 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) gate_up3_kernel(const GateU
   // The selection is read once; every job then finds its expert in shared memory.
   if (threadIdx.x < p.topk) s_sel[threadIdx.x] = p.wsel[threadIdx.x];
   __syncthreads();
-
-  auto job_rows = [&](int j, int& i, int& e, int& r0, int& n) {
-    i = j / p.jobs_per_expert;
-    r0 = (j - i * p.jobs_per_expert) * P;
-    n = min(P, p.F - r0);
-    e = s_sel[i];
-  };
-  auto issue = [&](int j, int st) {
-    if (lane != 0) return;
-    int i, e, r0, n;
-    job_rows(j, i, e, r0, n);
-    uint32_t lg, og, lu, ou;
-    const uint8_t* sg = span16(p.gate + e * p.gate_nb2 + r0 * p.rb_g, n * p.rb_g, &lg, &og);
-    const uint8_t* su = span16(p.up + e * p.up_nb2 + r0 * p.rb_u, n * p.rb_u, &lu, &ou);
-    mbar_expect_tx(&wbar[st], lg + lu);
-    uint8_t* buf = wb + static_cast<size_t>(st) * p.stage_bytes;
-    bulk_g2s(buf, sg, lg, &wbar[st]);
-    bulk_g2s(buf + p.up_off, su, lu, &wbar[st]);
-  };
   for (int st = 0; st < p.S; ++st) {
     const int j = gw + st * tw;
-    if (j < p.jobs_total) issue(j, st);
+    if (j < p.jobs_total) gu3_issue(p, s_sel, wbar, wb, j, st, lane);
   }
-  // Start the selected experts' down weights towards L2 for the kernel that
-  // follows: this CTA's share, in pieces of at most 64 KB over warp 0's lanes.
-  if (p.down != nullptr && warp == 0) {
-    constexpr uint64_t kPiece = 64 * 1024;
-    const uint64_t total = p.down_nb2 * static_cast<uint64_t>(p.topk);
-    const uint64_t share = ((total / gridDim.x) + 15) & ~static_cast<uint64_t>(15);
-    const uint64_t beg = share * blockIdx.x;
-    const uint64_t end = beg + share < total ? beg + share : total;
-    for (uint64_t o = beg + static_cast<uint64_t>(lane) * kPiece; o < end; o += 32 * kPiece) {
-      // Pieces never straddle two experts: clip at the expert boundary.
-      const uint64_t i = o / p.down_nb2, in = o - i * p.down_nb2;
-      uint64_t len = end - o < kPiece ? end - o : kPiece;
-      if (in + len > p.down_nb2) len = p.down_nb2 - in;
-      prefetch_l2(p.down + static_cast<uint64_t>(s_sel[i]) * p.down_nb2 + in, static_cast<uint32_t>(len));
-    }
-  }
+  gu3_prefetch_down(p, s_sel, warp, lane);
   cluster_wait();
   cluster_prep_act(a, p.h, p.norm != nullptr, true, p.eps, true, false, red, s_part);
-  const int g = lane % G, r = lane / G;
   Act3 act;
-  load_act3(act, a, g);
-  bool failed = false;
-  for (int it = 0;; ++it) {
-    const int j = gw + it * tw;
-    if (j >= p.jobs_total) break;
-    const int st = it % p.S;
-    int i, e, r0, n;
-    job_rows(j, i, e, r0, n);
-    if (!mbar_wait(&wbar[st], (it / p.S) & 1)) {
-      failed = true;
-      break;
-    }
-    const uint8_t* buf = wb + static_cast<size_t>(st) * p.stage_bytes;
-    const uint32_t og = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p.gate + e * p.gate_nb2 + r0 * p.rb_g) & 15);
-    const uint32_t ou = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p.up + e * p.up_nb2 + r0 * p.rb_u) & 15);
-    const float vg = row_dot3(buf + og + r * p.rb_g, p.tg, g, G, act);
-    const float vu = row_dot3(buf + p.up_off + ou + r * p.rb_u, p.tu, g, G, act);
-    if (g == 0 && r < n) p.ff[static_cast<int64_t>(i) * p.F + r0 + r] = silu_mul(vg, vu);
-    __syncwarp();
-    const int jn = gw + (it + p.S) * tw;
-    if (jn < p.jobs_total) issue(jn, st);
-  }
-  if (failed && lane == 0 && p.state != nullptr) atomicCAS(&p.state->error, 0, NH_E_TIMEOUT);
+  load_act3(act, a, lane % p.lpr);
+  const bool ok = gu3_run(p, s_sel, wbar, wb, act, gw, tw, lane);
+  if (!ok && lane == 0 && p.state != nullptr) atomicCAS(&p.state->error, 0, NH_E_TIMEOUT);
 }
 
 // down + combine: G = F/256 lanes per row and P = 32/G row groups per pass;
 // group q takes expert q % k and row q / k of the job's Rp = P/k rows, so a
 // lane's activation (its expert's super-block g of ff) never changes.  The k
 // values of a row are gathered by shuffles and summed in top-k order.
+// Lane i < k stages expert i's rows of job j; lane 0 registers the total
+// bytes on the stage's barrier before any copy is issued.  Warp-collective.
+__device__ __forceinline__ void dn3_issue(const DownArgs& p, const int* s_sel, uint64_t* wbar, uint8_t* wb, int j,
+                                          int st, int lane) {
+  const int r0 = j * p.R;
+  const int n = min(p.R, p.D - r0);
+  uint32_t len = 0, off;
+  const uint8_t* src = nullptr;
+  if (lane < p.topk) src = span16(p.down + s_sel[lane] * p.nb2 + r0 * p.rb, n * p.rb, &len, &off);
+  uint32_t total = len;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+  if (lane == 0) mbar_expect_tx(&wbar[st], total);
+  __syncwarp();
+  if (lane < p.topk)
+    bulk_g2s(wb + static_cast<size_t>(st) * p.stage_bytes + lane * p.slot_bytes, src, len, &wbar[st]);
+}
+
+// The warp's down jobs (the first S already issued) against the prepared ff
+// activation: returns false when a stage wait expired.
+// pos / n_prompt: the decode cursor (for the dump).  h0: when have_h0, this
+// lane's h value for the warp's first job (read ahead by the caller).
+__device__ __forceinline__ bool dn3_run(const DownArgs& p, const int* s_sel, const float* s_wts, uint64_t* wbar,
+                                        uint8_t* wb, const ActSmem& a, int gw, int tw, int lane, int pos,
+                                        int n_prompt, bool have_h0, float h0) {
+  const int G = p.lpr, k = p.topk, Rp = p.R;
+  const int g = lane % G, q = lane / G;
+  const int ie = q % k, rr = q / k;  // this lane's expert and row within the job
+  Act3 act;
+  load_act3(act, a, ie * G + g);
+  const bool dump = p.dump != nullptr && pos >= n_prompt - 1;
+  const int rl = lane % Rp;  // the row this lane combines (lanes < n write it)
+  for (int it = 0;; ++it) {
+    const int j = gw + it * tw;
+    if (j >= p.jobs_total) break;
+    const int st = it % p.S;
+    const int r0 = j * Rp;
+    const int n = min(Rp, p.D - r0);
+    if (!mbar_wait(&wbar[st], (it / p.S) & 1)) return false;
+    const uint8_t* buf = wb + static_cast<size_t>(st) * p.stage_bytes;
+    const uint32_t off =
+        static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p.down + s_sel[ie] * p.nb2 + r0 * p.rb) & 15);
+    const float v = row_dot3(buf + ie * p.slot_bytes + off + rr * p.rb, p.td, g, G, act);
+    // ggml_mul by the routing weights, then the chained adds in top-k order.
+    float acc = __fmul_rn(__shfl_sync(0xffffffffu, v, (rl * k) * G), s_wts[0]);
+    for (int i = 1; i < k; ++i) acc = __fadd_rn(acc, __fmul_rn(__shfl_sync(0xffffffffu, v, (rl * k + i) * G), s_wts[i]));
+    if (lane < n) {
+      const int row = r0 + lane;
+      const float hv = __fadd_rn(it == 0 && have_h0 ? h0 : p.h[row], acc);
+      p.h[row] = hv;
+      if (dump) p.dump[static_cast<int64_t>(pos - n_prompt + 1) * p.dump_stride + p.dump_off + row] = hv;
+    }
+    __syncwarp();
+    const int jn = gw + (it + p.S) * tw;
+    if (jn < p.jobs_total) dn3_issue(p, s_sel, wbar, wb, jn, st, lane);
+  }
+  return true;
+}
+
 __global__ void __launch_bounds__(kMoeWarps * 32, 2) down3_kernel(const DownArgs p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -575,7 +679,6 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) down3_kernel(const DownArgs
   __shared__ double s_part[8];
   cluster_arrive_relaxed();
   const int gw = blockIdx.x * kMoeWarps + warp, tw = gridDim.x * kMoeWarps;
-  const int G = p.lpr, k = p.topk, Rp = p.R;
   uint64_t* wbar = bars + warp * p.S;
   uint8_t* wb = stage + static_cast<size_t>(warp) * p.S * p.stage_bytes;
   if (lane == 0) {
@@ -584,71 +687,209 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) down3_kernel(const DownArgs
   }
   pdl_wait();
   pdl_trigger();
-  if (threadIdx.x < k) {
+  if (threadIdx.x < p.topk) {
     s_sel[threadIdx.x] = p.wsel[threadIdx.x];
     s_wts[threadIdx.x] = p.wts[threadIdx.x];
   }
   __syncthreads();
-
-  // Lane i < k copies expert i's rows; lane 0 registers the total bytes on
-  // the stage's barrier before any copy is issued.
-  auto issue = [&](int j, int st) {
-    const int r0 = j * Rp;
-    const int n = min(Rp, p.D - r0);
-    uint32_t len = 0, off;
-    const uint8_t* src = nullptr;
-    if (lane < k) src = span16(p.down + s_sel[lane] * p.nb2 + r0 * p.rb, n * p.rb, &len, &off);
-    uint32_t total = len;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
-    if (lane == 0) mbar_expect_tx(&wbar[st], total);
-    __syncwarp();
-    if (lane < k) bulk_g2s(wb + static_cast<size_t>(st) * p.stage_bytes + lane * p.slot_bytes, src, len, &wbar[st]);
-  };
   for (int st = 0; st < p.S; ++st) {
     const int j = gw + st * tw;
-    if (j < p.jobs_total) issue(j, st);
+    if (j < p.jobs_total) dn3_issue(p, s_sel, wbar, wb, j, st, lane);
   }
   // The activation: the k experts' ff rows, Q8_K-quantised per 256-block,
   // each CTA of the cluster quantising its share.
   cluster_wait();
   cluster_prep_act(a, p.ff, false, false, 0.f, true, false, red, s_part);
-  const int g = lane % G, q = lane / G;
-  const int ie = q % k, rr = q / k;  // this lane's expert and row within the job
-  Act3 act;
-  load_act3(act, a, ie * G + g);
-  const int pos = p.state->pos, n_prompt = p.state->n_prompt;
-  const bool dump = p.dump != nullptr && pos >= n_prompt - 1;
-  const int rl = lane % Rp;  // the row this lane combines (lanes < n write it)
-  bool failed = false;
-  for (int it = 0;; ++it) {
-    const int j = gw + it * tw;
-    if (j >= p.jobs_total) break;
-    const int st = it % p.S;
-    const int r0 = j * Rp;
-    const int n = min(Rp, p.D - r0);
-    if (!mbar_wait(&wbar[st], (it / p.S) & 1)) {
-      failed = true;
-      break;
-    }
-    const uint8_t* buf = wb + static_cast<size_t>(st) * p.stage_bytes;
-    const uint32_t off =
-        static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p.down + s_sel[ie] * p.nb2 + r0 * p.rb) & 15);
-    const float v = row_dot3(buf + ie * p.slot_bytes + off + rr * p.rb, p.td, g, G, act);
-    // ggml_mul by the routing weights, then the chained adds in top-k order.
-    float acc = __fmul_rn(__shfl_sync(0xffffffffu, v, (rl * k) * G), s_wts[0]);
-    for (int i = 1; i < k; ++i) acc = __fadd_rn(acc, __fmul_rn(__shfl_sync(0xffffffffu, v, (rl * k + i) * G), s_wts[i]));
-    if (lane < n) {
-      const int row = r0 + lane;
-      const float hv = __fadd_rn(p.h[row], acc);
-      p.h[row] = hv;
-      if (dump) p.dump[static_cast<int64_t>(pos - n_prompt + 1) * p.dump_stride + p.dump_off + row] = hv;
-    }
-    __syncwarp();
-    const int jn = gw + (it + p.S) * tw;
-    if (jn < p.jobs_total) issue(jn, st);
+  const bool ok = dn3_run(p, s_sel, s_wts, wbar, wb, a, gw, tw, lane, p.state->pos, p.state->n_prompt, false, 0.f);
+  if (!ok && lane == 0) atomicCAS(&p.state->error, 0, NH_E_TIMEOUT);
+}
+
+// ------------------------------------------------------------------ fused layer
+// Router, gate/up and down of one layer in one cooperative grid (every CTA
+// resident at once).  The first router_ctas CTAs compute the logits (one warp
+// per expert, the f32 row staged in shared memory before the preceding kernel
+// ends) and count themselves in sync[0]; every CTA then selects the experts
+// itself from the logits (CTA 0 also writes the router outputs), streams its
+// warps' gate/up jobs and, as soon as a warp's last one is consumed, stages
+// the warp's first down jobs in the same shared-memory region, so the down
+// rows load while the grid gathers at sync[1] behind the last ff row.
+// sync[2] counts exits; the last CTA to leave zeroes the three counters for
+// the next launch.  Every wait is bounded and records NH_E_TIMEOUT.
+struct FusedArgs {
+  RouterArgs r;
+  GateUpArgs g;
+  DownArgs d;
+  unsigned* sync;
+  int router_ctas;
+  uint32_t act_bytes;     // the shared activation region (gate/up, then down)
+  uint32_t region_bytes;  // per-warp staging shared by the two rings
+};
+
+constexpr int kGridSpins = 1 << 24;
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Adds to a grid counter with release semantics: this CTA's earlier writes
+// (ordered before the calling thread by a CTA barrier) are visible to any
+// thread that acquires the new count.
+__device__ __forceinline__ void red_release_gpu(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+
+// Bounded wait (one thread) until *p >= target.
+__device__ __forceinline__ bool wait_count(const unsigned* p, unsigned target) {
+  for (int i = 0; i < kGridSpins; ++i) {
+    if (ld_acquire_gpu(p) >= target) return true;
+    __nanosleep(32);
   }
-  if (failed && lane == 0) atomicCAS(&p.state->error, 0, NH_E_TIMEOUT);
+  return false;
+}
+
+// Q8_K quantisation of n_blocks 256-value blocks read from global memory
+// (written by other CTAs of this grid: loaded through L2), each warp its
+// blocks; the same per-block arithmetic as prep_act.
+__device__ __forceinline__ void quant_act_global(ActSmem& a, const float* src, int n_blocks) {
+  constexpr int kAhead = 4;  // blocks per warp whose loads are all in flight at once
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int b0 = warp; b0 < n_blocks; b0 += kAhead * nw) {
+    float4 v4[kAhead][2];
+#pragma unroll
+    for (int i = 0; i < kAhead; ++i) {
+      const int b = b0 + i * nw;
+      if (b < n_blocks) {
+        const float4* s4 = reinterpret_cast<const float4*>(src + b * QK + lane * 8);
+        v4[i][0] = __ldcg(s4);
+        v4[i][1] = __ldcg(s4 + 1);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kAhead; ++i) {
+      const int b = b0 + i * nw;
+      if (b < n_blocks) {
+        float v[8] = {v4[i][0].x, v4[i][0].y, v4[i][0].z, v4[i][0].w,
+                      v4[i][1].x, v4[i][1].y, v4[i][1].z, v4[i][1].w};
+        quantize_block_warp(v, b, a, lane);
+      }
+    }
+  }
+}
+
+template <int KP>
+__global__ void __launch_bounds__(kMoeWarps * 32, 2) moe_fused_kernel(const __grid_constant__ FusedArgs p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const GateUpArgs& g = p.g;
+  const DownArgs& d = p.d;
+  ActSmem a = carve_act(smem, g.K, true, true);
+  double* red = reinterpret_cast<double*>(smem + p.act_bytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.act_bytes + 48 * sizeof(double));
+  uint64_t* gbar = bars + warp * g.S;
+  uint64_t* dbar = bars + kMoeWarps * g.S + warp * d.S;
+  uint64_t* rbar = bars + kMoeWarps * (g.S + d.S) + warp;
+  uint8_t* wb = reinterpret_cast<uint8_t*>(bars + kMoeWarps * (g.S + d.S + 1)) +
+                static_cast<size_t>(warp) * p.region_bytes;
+  __shared__ int s_sel[kMaxTopK];
+  __shared__ float s_wts[kMaxTopK];
+  __shared__ int s_ok, s_pos, s_np;
+  const int gw = blockIdx.x * kMoeWarps + warp, tw = gridDim.x * kMoeWarps;
+  // Router warps stage their expert's f32 row in their staging region (free
+  // until the selection is known) before waiting for the preceding kernel.
+  const bool router_cta = static_cast<int>(blockIdx.x) < p.router_ctas;
+  const int e = blockIdx.x * kMoeWarps + warp;
+  const bool has_row = router_cta && e < p.r.E;
+  if (lane == 0) {
+    for (int s = 0; s < g.S; ++s) mbar_init(&gbar[s], 1);
+    for (int s = 0; s < d.S; ++s) mbar_init(&dbar[s], 1);
+    mbar_init(rbar, 1);
+    fence_barrier_init();
+    if (has_row) {
+      const uint32_t bytes = static_cast<uint32_t>(p.r.K) * 4u;
+      mbar_expect_tx(rbar, bytes);
+      bulk_g2s(wb, p.r.router + static_cast<int64_t>(e) * p.r.K, bytes, rbar);
+    }
+  }
+  act_load_norm(a, g.norm);
+  pdl_wait();
+  pdl_trigger();
+  if (threadIdx.x == 0) {
+    s_pos = d.state->pos;
+    s_np = d.state->n_prompt;
+  }
+  prep_act(a, g.h, g.norm != nullptr, true, g.eps, true, red);
+  bool ok = true;
+  if (router_cta) {
+    if (has_row) {
+      ok = mbar_wait(rbar, 0);
+      // DotF32Vec128 order: lane l sums elements 4l + 128t (t ascending),
+      // then the butterfly across lanes.
+      const float4* w4 = reinterpret_cast<const float4*>(wb);
+      float sdot = 0.f;
+      for (int t = 0; t < p.r.K / 128; ++t) {
+        const float4 w = w4[lane + 32 * t];
+        const float4 x = *reinterpret_cast<const float4*>(a.xf + 4 * lane + 128 * t);
+        sdot = __fadd_rn(sdot, __fmul_rn(w.x, x.x));
+        sdot = __fadd_rn(sdot, __fmul_rn(w.y, x.y));
+        sdot = __fadd_rn(sdot, __fmul_rn(w.z, x.z));
+        sdot = __fadd_rn(sdot, __fmul_rn(w.w, x.w));
+      }
+      sdot = warp_sum(sdot);
+      if (lane == 0) p.r.logits[e] = sdot;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) red_release_gpu(&p.sync[0], 1u);
+  }
+  // This warp's gate/up activation, while the logits gather.
+  Act3 act;
+  load_act3(act, a, lane % g.lpr);
+  if (threadIdx.x == 0) s_ok = wait_count(&p.sync[0], static_cast<unsigned>(p.router_ctas));
+  __syncthreads();
+  const bool sel_ok = s_ok != 0;
+  if (sel_ok) {
+    router_select_block<KP>(p.r, p.r.logits, blockIdx.x == 0, s_pos, s_sel, s_wts);
+    for (int st = 0; st < g.S; ++st) {
+      const int j = gw + st * tw;
+      if (j < g.jobs_total) gu3_issue(g, s_sel, gbar, wb, j, st, lane);
+    }
+    ok = gu3_run(g, s_sel, gbar, wb, act, gw, tw, lane) && ok;
+    if (ok) {
+      for (int st = 0; st < d.S; ++st) {
+        const int j = gw + st * tw;
+        if (j < d.jobs_total) dn3_issue(d, s_sel, dbar, wb, j, st, lane);
+      }
+    }
+  }
+  // The residual rows of this warp's first down job (only this warp writes
+  // them), read ahead of the grid barrier.
+  float h0 = 0.f;
+  if (gw < d.jobs_total && lane < min(d.R, d.D - gw * d.R)) h0 = __ldcg(d.h + gw * d.R + lane);
+  // Grid barrier: every ff row written before any CTA quantises ff.
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    red_release_gpu(&p.sync[1], 1u);
+    s_ok = wait_count(&p.sync[1], gridDim.x);
+  }
+  __syncthreads();
+  bool ok_dn = ok && sel_ok && s_ok != 0;
+  if (s_ok != 0 && sel_ok) {
+    // The gate/up activation is dead (consumed into registers): the ff
+    // activation takes its place.
+    ActSmem af = carve_act(smem, d.topk * d.F, false);
+    quant_act_global(af, d.ff, d.topk * d.F / QK);
+    __syncthreads();
+    if (ok_dn) ok_dn = dn3_run(d, s_sel, s_wts, dbar, wb, af, gw, tw, lane, s_pos, s_np, true, h0);
+  }
+  if (!ok_dn && lane == 0) atomicCAS(&d.state->error, 0, NH_E_TIMEOUT);
+  __syncthreads();
+  if (threadIdx.x == 0 && atomicAdd(&p.sync[2], 1u) == gridDim.x - 1) {
+    p.sync[0] = 0u;
+    p.sync[1] = 0u;
+    p.sync[2] = 0u;
+    __threadfence();
+  }
 }
 
 }  // namespace nh
@@ -765,6 +1006,40 @@ bool aligned16(const void* p, uint64_t stride) {
   return (reinterpret_cast<uintptr_t>(p) & 15) == 0 && (stride & 15) == 0;
 }
 
+// Lane-per-super-block gate/up jobs: G = K/256 lanes per row, P = 32/G gate
+// rows and P up rows per job, staged gate then up (each 128-byte aligned).
+void shape_gate_up3(GateUpArgs& p) {
+  p.lpr = p.K / QK;
+  p.rpp = 32 / p.lpr;
+  p.R = p.rpp;
+  const uint64_t gb = (p.rb_g * p.rpp + 32 + 127) & ~127ull;
+  const uint64_t ub = (p.rb_u * p.rpp + 32 + 127) & ~127ull;
+  p.up_off = static_cast<uint32_t>(gb);
+  p.stage_bytes = static_cast<uint32_t>(gb + ub);
+  p.jobs_per_expert = (p.F + p.rpp - 1) / p.rpp;
+  p.jobs_total = p.jobs_per_expert * p.topk;
+}
+
+// The lane-per-super-block down kernel covers F/256 in {1,2,4,8} with the
+// 32/G row groups of a pass divisible among the k experts.
+bool down3_ok(int F, int k) { return rowdot3_k_ok(F) && (32 / (F / QK)) % k == 0; }
+
+// Lane-per-super-block down jobs: G = F/256 lanes per row, 32/G row groups
+// per pass shared by the k experts, so R = 32/(G*k) output rows per job.
+void shape_down3(DownArgs& p) {
+  p.lpr = p.F / QK;
+  p.rpp = 32 / p.lpr;
+  p.R = p.rpp / p.topk;
+  // Expert slots are offset from 128-byte multiples so the lanes that read
+  // the same super-block of different experts hit different banks: 64 mod
+  // 128 for Q4_K (16-byte loads, two experts per quarter warp), 16 mod 128
+  // for Q6_K (32-bit loads across the warp).
+  p.slot_bytes = static_cast<uint32_t>(((p.rb * p.R + 32 + 127) & ~127ull) + (p.td == NH_TYPE_Q4_K ? 64 : 16));
+  p.stage_bytes = p.slot_bytes * p.topk;
+  p.jobs_total = (p.D + p.R - 1) / p.R;
+  p.ystride = 0;
+}
+
 }  // namespace
 
 extern "C" int nh_moe_gate_up_prefetch(NhDecodeState* state, const float* h, const float* ffn_norm, float eps,
@@ -802,15 +1077,7 @@ extern "C" int nh_moe_gate_up_prefetch(NhDecodeState* state, const float* h, con
   p.down = pf ? static_cast<const uint8_t*>(down) : nullptr;
   p.down_nb2 = pf ? down_nb2 : 0;
   if (quant && rowdot3_k_ok(p.K) && engine_v3()) {
-    p.lpr = p.K / QK;  // G
-    p.rpp = 32 / p.lpr;  // P rows of gate and of up per job
-    p.R = p.rpp;
-    const uint64_t gb = (p.rb_g * p.rpp + 32 + 127) & ~127ull;
-    const uint64_t ub = (p.rb_u * p.rpp + 32 + 127) & ~127ull;
-    p.up_off = static_cast<uint32_t>(gb);
-    p.stage_bytes = static_cast<uint32_t>(gb + ub);
-    p.jobs_per_expert = (p.F + p.rpp - 1) / p.rpp;
-    p.jobs_total = p.jobs_per_expert * k;
+    shape_gate_up3(p);
     p.ff = ff;
     const size_t fixed = ((act_smem_bytes(p.K, true, true) + 15) & ~static_cast<size_t>(15)) + 48 * sizeof(double);
     p.S = pick_stages3(fixed, p.stage_bytes, p.jobs_total);
@@ -887,18 +1154,8 @@ extern "C" int nh_moe_down_combine(const NhDecodeState* state, const float* ff, 
   p.rb = row_bytes(td, n_ff);
   p.F = static_cast<int>(n_ff);
   p.D = static_cast<int>(n_embd);
-  if (quant && rowdot3_k_ok(p.F) && (32 / (p.F / QK)) % k == 0 && engine_v3()) {
-    p.lpr = p.F / QK;            // G
-    p.rpp = 32 / p.lpr;          // row groups per pass
-    p.R = p.rpp / k;             // rows per job
-    // Expert slots are offset from 128-byte multiples so the lanes that read
-    // the same super-block of different experts hit different banks: 64 mod
-    // 128 for Q4_K (16-byte loads, two experts per quarter warp), 16 mod 128
-    // for Q6_K (32-bit loads across the warp).
-    p.slot_bytes = static_cast<uint32_t>(((p.rb * p.R + 32 + 127) & ~127ull) + (td == NH_TYPE_Q4_K ? 64 : 16));
-    p.stage_bytes = p.slot_bytes * k;
-    p.jobs_total = (p.D + p.R - 1) / p.R;
-    p.ystride = 0;
+  if (quant && down3_ok(p.F, k) && engine_v3()) {
+    shape_down3(p);
     p.h = h_io;
     p.dump = dump;
     p.dump_stride = dump_step_stride;
@@ -950,4 +1207,140 @@ extern "C" int nh_moe_down_combine(const NhDecodeState* state, const float* ff, 
   const int cpl = quant ? (p.F / 64 + 31) / 32 : 1;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return cpl <= 1 ? launch_down<1>(p, smem, grid, s) : launch_down<2>(p, smem, grid, s);
+}
+
+extern "C" int64_t nh_moe_layer_scratch_bytes(int n_expert) { return 64 + 4 * static_cast<int64_t>(n_expert) + 64; }
+
+namespace {
+
+template <int KP>
+int launch_fused(FusedArgs& p, cudaStream_t st) {
+  // Grid: enough warps for one job each (at least the router CTAs), at most
+  // two CTAs per SM (the launch bounds); the rings take the remaining jobs.
+  const int need = std::max((std::max(p.g.jobs_total, p.d.jobs_total) + kMoeWarps - 1) / kMoeWarps, p.router_ctas);
+  int grid = std::min(need, 2 * device_sm_count());
+  const size_t fixed = p.act_bytes + 48 * sizeof(double);
+  // Ring depths for that grid, trimmed until two CTAs fit on an SM.
+  const int warps = grid * kMoeWarps;
+  p.g.S = std::min(kMoeMaxStages, std::max(1, (p.g.jobs_total + warps - 1) / warps));
+  p.d.S = std::min(kMoeMaxStages, std::max(1, (p.d.jobs_total + warps - 1) / warps));
+  // Each warp's region also holds one router row (n_embd floats).
+  auto region = [&]() {
+    const uint64_t r = std::max({static_cast<uint64_t>(p.g.S) * p.g.stage_bytes,
+                                 static_cast<uint64_t>(p.d.S) * p.d.stage_bytes, static_cast<uint64_t>(p.r.K) * 4});
+    return static_cast<uint32_t>((r + 127) & ~127ull);
+  };
+  auto total = [&]() {
+    return fixed + kMoeWarps * (p.g.S + p.d.S + 1) * sizeof(uint64_t) + static_cast<size_t>(kMoeWarps) * region();
+  };
+  while ((p.g.S > 1 || p.d.S > 1) && total() > 112 * 1024) {
+    if (static_cast<uint64_t>(p.g.S) * p.g.stage_bytes >= static_cast<uint64_t>(p.d.S) * p.d.stage_bytes && p.g.S > 1)
+      --p.g.S;
+    else if (p.d.S > 1)
+      --p.d.S;
+    else
+      --p.g.S;
+  }
+  p.region_bytes = region();
+  const size_t smem = total();
+  if (smem > 220 * 1024) return NH_E_ARG;
+  static size_t configured = 48 * 1024;
+  if (!ensure_smem(moe_fused_kernel<KP>, smem, configured)) return NH_E_CUDA;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, moe_fused_kernel<KP>, kMoeWarps * 32, smem) !=
+          cudaSuccess ||
+      per_sm < 1)
+    return NH_E_ARG;
+  grid = std::min(grid, per_sm * device_sm_count());
+  if (grid < p.router_ctas) return NH_E_ARG;
+  return launch_coop(moe_fused_kernel<KP>, dim3(grid), dim3(kMoeWarps * 32), smem, st, p);
+}
+
+}  // namespace
+
+extern "C" int nh_moe_layer(const NhMoeLayer* L, void* stream) {
+  if (L == nullptr || L->state == nullptr || L->h == nullptr || L->router == nullptr || L->gate == nullptr ||
+      L->up == nullptr || L->down == nullptr || L->sel == nullptr || L->wts == nullptr || L->ff == nullptr ||
+      L->scratch == nullptr)
+    return NH_E_ARG;
+  const int E = L->n_expert, k = L->k;
+  if (E <= 0 || E > kMaxExperts || k <= 0 || k > kMaxTopK || k > E) return NH_E_ARG;
+  if (L->n_embd <= 0 || L->n_embd > kMaxK || L->n_ff <= 0 || L->n_ff > kMaxK) return NH_E_ARG;
+  for (int t : {L->tg, L->tu, L->td})
+    if (t != NH_TYPE_Q4_K && t != NH_TYPE_Q6_K) return NH_E_TYPE;
+  const int K = static_cast<int>(L->n_embd), F = static_cast<int>(L->n_ff);
+  if (!engine_v3() || !rowdot3_k_ok(K) || !down3_ok(F, k) || static_cast<int64_t>(k) * F > 4 * kMaxK)
+    return NH_E_ARG;
+  // Router rows are staged by bulk copies: 16-byte aligned.
+  if ((reinterpret_cast<uintptr_t>(L->router) & 15) != 0) return NH_E_ARG;
+  if ((L->tg == NH_TYPE_Q4_K && !aligned16(L->gate, L->gate_nb2)) ||
+      (L->tu == NH_TYPE_Q4_K && !aligned16(L->up, L->up_nb2)) ||
+      (L->td == NH_TYPE_Q4_K && !aligned16(L->down, L->down_nb2)))
+    return NH_E_ARG;
+  FusedArgs p;
+  RouterArgs& r = p.r;
+  r.state = L->state;
+  r.h = L->h;
+  r.norm = L->ffn_norm;
+  r.eps = L->eps;
+  r.router = L->router;
+  r.K = K;
+  r.E = E;
+  r.topk = k;
+  r.norm_topk = L->norm_topk;
+  r.layer = L->layer;
+  r.n_layers = L->n_layers;
+  r.sel = L->sel;
+  r.wts = L->wts;
+  r.trace_sel = L->trace_sel;
+  r.trace_gap = L->trace_gap;
+  r.ticket = static_cast<unsigned*>(L->scratch);
+  r.logits = reinterpret_cast<float*>(static_cast<uint8_t*>(L->scratch) + 64);
+  p.sync = static_cast<unsigned*>(L->scratch) + 1;
+  p.router_ctas = (E + kMoeWarps - 1) / kMoeWarps;
+  GateUpArgs& g = p.g;
+  g.state = L->state;
+  g.h = L->h;
+  g.norm = L->ffn_norm;
+  g.eps = L->eps;
+  g.wsel = L->sel;
+  g.topk = k;
+  g.gate = static_cast<const uint8_t*>(L->gate);
+  g.up = static_cast<const uint8_t*>(L->up);
+  g.tg = L->tg;
+  g.tu = L->tu;
+  g.gate_nb2 = L->gate_nb2;
+  g.up_nb2 = L->up_nb2;
+  g.K = K;
+  g.F = F;
+  g.rb_g = row_bytes(g.tg, K);
+  g.rb_u = row_bytes(g.tu, K);
+  g.ff = L->ff;
+  g.down = nullptr;
+  g.down_nb2 = 0;
+  shape_gate_up3(g);
+  DownArgs& d = p.d;
+  d.state = L->state;
+  d.ff = L->ff;
+  d.wsel = L->sel;
+  d.wts = L->wts;
+  d.topk = k;
+  d.down = static_cast<const uint8_t*>(L->down);
+  d.td = L->td;
+  d.nb2 = L->down_nb2;
+  d.rb = row_bytes(d.td, F);
+  d.F = F;
+  d.D = K;
+  d.h = L->h;
+  d.dump = L->dump;
+  d.dump_stride = L->dump_step_stride;
+  d.dump_off = L->dump_offset;
+  shape_down3(d);
+  p.act_bytes = static_cast<uint32_t>(
+      (std::max(act_smem_bytes(K, true, true), act_smem_bytes(k * F, false)) + 15) & ~static_cast<size_t>(15));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (E <= 32) return launch_fused<1>(p, st);
+  if (E <= 64) return launch_fused<2>(p, st);
+  if (E <= 128) return launch_fused<4>(p, st);
+  return launch_fused<8>(p, st);
 }

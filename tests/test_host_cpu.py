@@ -207,3 +207,31 @@ def test_granite_trace_sweep_matches_reference_and_published_rates():
         assert abs(learned - rl) <= 0.002, b
         for got, want in zip((learned, lru, osp), published[b]):
             assert abs(100 * got - want) <= 0.15, (b, 100 * got, want)
+
+
+def test_moe_layer_declines_uncovered_shapes_before_any_launch():
+    """nh_moe_layer validates on the host and returns NH_E_ARG / NH_E_TYPE,
+    launching nothing, where the fused kernel does not cover the layer (the
+    engine then runs the router, gate/up and down kernels); the fake device
+    pointers below are never dereferenced."""
+    from nuthatch_b200._lib import NhMoeLayer
+
+    fake = 1 << 20  # 16-byte aligned, never touched
+    base = dict(state=fake, h=fake, ffn_norm=fake, eps=1e-5, router=fake, n_embd=2048, n_ff=1024, n_expert=64, k=8,
+                n_layers=16, gate=fake, tg=12, gate_nb2=1024 * 8 * 144, up=fake, tu=12, up_nb2=1024 * 8 * 144,
+                down=fake, td=14, down_nb2=2048 * 4 * 210, sel=fake, wts=fake, ff=fake, scratch=fake)
+
+    def rc(**kw):
+        a = NhMoeLayer(**{**base, **kw})
+        return lib().nh_moe_layer(C.byref(a), None)
+
+    assert lib().nh_moe_layer(None, None) == -1
+    assert rc(scratch=None) == -1
+    assert rc(tg=0) == -3 and rc(td=0) == -3               # F32 experts: the separate kernels
+    assert rc(n_embd=2304) == -1                           # n_embd/256 = 9
+    assert rc(n_ff=768) == -1                              # n_ff/256 = 3
+    assert rc(n_ff=2048, k=8) == -1                        # 32/(n_ff/256) = 4 row groups for 8 experts
+    assert rc(k=65) == -1 and rc(n_expert=300) == -1
+    assert rc(router=fake + 4) == -1                       # router rows are bulk-copied
+    assert rc(gate=fake + 8) == -1                         # Q4_K rows are read 16 bytes at a time
+    assert lib().nh_moe_layer_scratch_bytes(64) >= 64 + 4 * 64
