@@ -276,8 +276,9 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv3_kernel(const GemvArg
   if (!skip) {
     cluster_prep_act(a, p.x, p.norm_w != nullptr, p.do_norm != 0, p.eps, true, false, red, s_part);
     const int g = lane % G, r = lane / G;
-    Act3 act;
-    load_act3(act, a, g);
+    // Most warps dot one or two jobs: the activation is read from shared
+    // memory rather than held in registers.
+    const Act3Smem act{a, g};
     for (int it = 0;; ++it) {
       const int j = gw + it * tw;
       if (j >= p.jobs_total) break;
@@ -292,7 +293,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv3_kernel(const GemvArg
       const uint32_t off =
           static_cast<uint32_t>(reinterpret_cast<uintptr_t>(sg.w + static_cast<uint64_t>(row0) * sg.rb) & 15);
       const uint8_t* rowp = wb + static_cast<size_t>(st) * p.stage_bytes + off + static_cast<size_t>(r) * sg.rb;
-      float v = row_dot3(rowp, sg.type, g, G, act);
+      float v = row_dot3v(rowp, sg.type, g, G, act);
       const int row = row0 + r;
       if (g == 0 && r < nrows) {
         if (sg.resid != nullptr) v = __fadd_rn(sg.resid[row], v);

@@ -82,7 +82,6 @@ __device__ __forceinline__ void router_load_row(const RouterArgs& p, float4 (&wv
 // experts and their weights (renormalised when norm_topk, clamped sum
 // 6.103515625e-5) to o_sel/o_wts (shared) and, when `outputs`, to p.sel,
 // p.wts and the trace.  Needs blockDim.x >= 32 and >= k; ends synchronised.
-template <int KP>
 __device__ __forceinline__ void router_select_block(const RouterArgs& p, const float* logits, bool outputs,
                                                     int64_t pos, int* o_sel, float* o_wts) {
   __shared__ __align__(16) float s_prob[kMaxExperts];
@@ -98,10 +97,11 @@ __device__ __forceinline__ void router_select_block(const RouterArgs& p, const f
     s_vals[tid] = 0.f;
   }
   if (warp == 0) {
-    float pr[KP];
+    constexpr int kPer = kMaxExperts / 32;  // experts per lane (absent ones add exact zeros)
+    float pr[kPer];
     float mx = -INFINITY;
 #pragma unroll
-    for (int k = 0; k < KP; ++k) {
+    for (int k = 0; k < kPer; ++k) {
       const int i = lane + 32 * k;
       pr[k] = i < E ? __ldcg(logits + i) : -INFINITY;
       mx = fmaxf(mx, pr[k]);
@@ -109,7 +109,7 @@ __device__ __forceinline__ void router_select_block(const RouterArgs& p, const f
     mx = warp_max(mx);
     double sum = 0.0;
 #pragma unroll
-    for (int k = 0; k < KP; ++k) {
+    for (int k = 0; k < kPer; ++k) {
       const int i = lane + 32 * k;
       pr[k] = i < E ? exp_cw(__fsub_rn(pr[k], mx)) : 0.f;
       sum += static_cast<double>(pr[k]);
@@ -117,7 +117,7 @@ __device__ __forceinline__ void router_select_block(const RouterArgs& p, const f
     sum = warp_sum_d(sum);
     const float inv = static_cast<float>(1.0 / sum);
 #pragma unroll
-    for (int k = 0; k < KP; ++k) {
+    for (int k = 0; k < kPer; ++k) {
       const int i = lane + 32 * k;
       if (i < E) s_prob[i] = __fmul_rn(pr[k], inv);
     }
@@ -169,8 +169,6 @@ __device__ __forceinline__ void router_select_block(const RouterArgs& p, const f
   __syncthreads();
 }
 
-// KP = experts per lane of the softmax / top-k warp (n_expert <= 32*KP).
-template <int KP>
 __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(const RouterArgs p) {
   extern __shared__ __align__(128) uint8_t smem[];
   ActSmem a = carve_act(smem, p.K, true, true);
@@ -206,7 +204,7 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(const RouterA
   if (!s_last) return;
   __shared__ int s_sel[kMaxTopK];
   __shared__ float s_wts[kMaxTopK];
-  router_select_block<KP>(p, p.logits, true, p.state->pos, s_sel, s_wts);
+  router_select_block(p, p.logits, true, p.state->pos, s_sel, s_wts);
 }
 
 // ------------------------------------------------------------------ gate/up
@@ -541,8 +539,9 @@ __device__ __forceinline__ void gu3_prefetch_down(const GateUpArgs& p, const int
 
 // The warp's jobs gw, gw+tw, ... (the first S already issued): returns false
 // when a stage wait expired.
+template <class View>
 __device__ __forceinline__ bool gu3_run(const GateUpArgs& p, const int* s_sel, uint64_t* wbar, uint8_t* wb,
-                                        const Act3& act, int gw, int tw, int lane) {
+                                        const View& act, int gw, int tw, int lane) {
   const int G = p.lpr;
   const int g = lane % G, r = lane / G;
   for (int it = 0;; ++it) {
@@ -555,8 +554,19 @@ __device__ __forceinline__ bool gu3_run(const GateUpArgs& p, const int* s_sel, u
     const uint8_t* buf = wb + static_cast<size_t>(st) * p.stage_bytes;
     const uint32_t og = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p.gate + e * p.gate_nb2 + r0 * p.rb_g) & 15);
     const uint32_t ou = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p.up + e * p.up_nb2 + r0 * p.rb_u) & 15);
-    const float vg = row_dot3(buf + og + r * p.rb_g, p.tg, g, G, act);
-    const float vu = row_dot3(buf + p.up_off + ou + r * p.rb_u, p.tu, g, G, act);
+    // Gate then up through one call site: a single copy of each dot body in
+    // the code (the warps run it once or twice, so instruction fetch, not
+    // issue, is what its size costs).
+    float vg = 0.f, vu = 0.f;
+#pragma unroll 1
+    for (int w = 0; w < 2; ++w) {
+      const float v = row_dot3v(w == 0 ? buf + og + r * p.rb_g : buf + p.up_off + ou + r * p.rb_u,
+                                w == 0 ? p.tg : p.tu, g, G, act);
+      if (w == 0)
+        vg = v;
+      else
+        vu = v;
+    }
     if (g == 0 && r < n) p.ff[static_cast<int64_t>(i) * p.F + r0 + r] = silu_mul(vg, vu);
     __syncwarp();
     const int jn = gw + (it + p.S) * tw;
@@ -596,9 +606,7 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) gate_up3_kernel(const GateU
   gu3_prefetch_down(p, s_sel, warp, lane);
   cluster_wait();
   cluster_prep_act(a, p.h, p.norm != nullptr, true, p.eps, true, false, red, s_part);
-  Act3 act;
-  load_act3(act, a, lane % p.lpr);
-  const bool ok = gu3_run(p, s_sel, wbar, wb, act, gw, tw, lane);
+  const bool ok = gu3_run(p, s_sel, wbar, wb, Act3Smem{a, lane % p.lpr}, gw, tw, lane);
   if (!ok && lane == 0 && p.state != nullptr) atomicCAS(&p.state->error, 0, NH_E_TIMEOUT);
 }
 
@@ -634,8 +642,7 @@ __device__ __forceinline__ bool dn3_run(const DownArgs& p, const int* s_sel, con
   const int G = p.lpr, k = p.topk, Rp = p.R;
   const int g = lane % G, q = lane / G;
   const int ie = q % k, rr = q / k;  // this lane's expert and row within the job
-  Act3 act;
-  load_act3(act, a, ie * G + g);
+  const Act3Smem act{a, ie * G + g};
   const bool dump = p.dump != nullptr && pos >= n_prompt - 1;
   const int rl = lane % Rp;  // the row this lane combines (lanes < n write it)
   for (int it = 0;; ++it) {
@@ -648,7 +655,7 @@ __device__ __forceinline__ bool dn3_run(const DownArgs& p, const int* s_sel, con
     const uint8_t* buf = wb + static_cast<size_t>(st) * p.stage_bytes;
     const uint32_t off =
         static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p.down + s_sel[ie] * p.nb2 + r0 * p.rb) & 15);
-    const float v = row_dot3(buf + ie * p.slot_bytes + off + rr * p.rb, p.td, g, G, act);
+    const float v = row_dot3v(buf + ie * p.slot_bytes + off + rr * p.rb, p.td, g, G, act);
     // ggml_mul by the routing weights, then the chained adds in top-k order.
     float acc = __fmul_rn(__shfl_sync(0xffffffffu, v, (rl * k) * G), s_wts[0]);
     for (int i = 1; i < k; ++i) acc = __fadd_rn(acc, __fmul_rn(__shfl_sync(0xffffffffu, v, (rl * k + i) * G), s_wts[i]));
@@ -778,7 +785,9 @@ __device__ __forceinline__ void quant_act_global(ActSmem& a, const float* src, i
   }
 }
 
-template <int KP>
+// One function serves every weight-type mix (types are dispatched at run
+// time): a single copy of its code stays warm in the instruction caches from
+// layer to layer, which measured faster than per-type variants.
 __global__ void __launch_bounds__(kMoeWarps * 32, 2) moe_fused_kernel(const __grid_constant__ FusedArgs p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -842,19 +851,16 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) moe_fused_kernel(const __gr
     __syncthreads();
     if (threadIdx.x == 0) red_release_gpu(&p.sync[0], 1u);
   }
-  // This warp's gate/up activation, while the logits gather.
-  Act3 act;
-  load_act3(act, a, lane % g.lpr);
   if (threadIdx.x == 0) s_ok = wait_count(&p.sync[0], static_cast<unsigned>(p.router_ctas));
   __syncthreads();
   const bool sel_ok = s_ok != 0;
   if (sel_ok) {
-    router_select_block<KP>(p.r, p.r.logits, blockIdx.x == 0, s_pos, s_sel, s_wts);
+    router_select_block(p.r, p.r.logits, blockIdx.x == 0, s_pos, s_sel, s_wts);
     for (int st = 0; st < g.S; ++st) {
       const int j = gw + st * tw;
       if (j < g.jobs_total) gu3_issue(g, s_sel, gbar, wb, j, st, lane);
     }
-    ok = gu3_run(g, s_sel, gbar, wb, act, gw, tw, lane) && ok;
+    ok = gu3_run(g, s_sel, gbar, wb, Act3Smem{a, lane % g.lpr}, gw, tw, lane) && ok;
     if (ok) {
       for (int st = 0; st < d.S; ++st) {
         const int j = gw + st * tw;
@@ -897,14 +903,13 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) moe_fused_kernel(const __gr
 using namespace nh;
 
 namespace {
-template <int KP>
 int launch_router(const RouterArgs& p, size_t smem, int grid, cudaStream_t st) {
   static size_t configured = 48 * 1024;
-  if (!ensure_smem(router_kernel<KP>, smem, configured)) return NH_E_CUDA;
+  if (!ensure_smem(router_kernel, smem, configured)) return NH_E_CUDA;
   // One cluster shares the preparation when the grid is a power of two <= 8.
   int cluster = prep_cluster_size(p.K, false);
   while (cluster > 1 && grid % cluster != 0) cluster >>= 1;
-  return launch_pdl_cluster(router_kernel<KP>, dim3(grid), dim3(kRouterWarps * 32), smem, st, cluster, p);
+  return launch_pdl_cluster(router_kernel, dim3(grid), dim3(kRouterWarps * 32), smem, st, cluster, p);
 }
 }  // namespace
 
@@ -940,10 +945,7 @@ extern "C" int nh_router_topk(const NhDecodeState* state, const float* h, const 
   const size_t smem = act_smem_bytes(p.K, true, true);
   const int grid = (n_expert + kRouterWarps - 1) / kRouterWarps;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (n_expert <= 32) return launch_router<1>(p, smem, grid, st);
-  if (n_expert <= 64) return launch_router<2>(p, smem, grid, st);
-  if (n_expert <= 128) return launch_router<4>(p, smem, grid, st);
-  return launch_router<8>(p, smem, grid, st);
+  return launch_router(p, smem, grid, st);
 }
 
 namespace {
@@ -1000,6 +1002,26 @@ int pick_stages3(size_t fixed, uint32_t stage_bytes, int jobs) {
   if (s > kMoeMaxStages) s = kMoeMaxStages;
   while (s > 1 && fixed + static_cast<size_t>(kMoeWarps) * s * (stage_bytes + 8) > 110 * 1024) --s;
   return s;
+}
+
+int launch_gate_up3(const GateUpArgs& p, size_t smem, cudaStream_t st) {
+  static size_t configured = 48 * 1024;
+  if (!ensure_smem(gate_up3_kernel, smem, configured)) return NH_E_CUDA;
+  int grid = grid_resident(gate_up3_kernel, p.jobs_total, smem);
+  int cluster = prep_cluster_size(p.K, true);
+  while (cluster > grid) cluster >>= 1;
+  grid = round_grid(grid, cluster);
+  return launch_pdl_cluster(gate_up3_kernel, dim3(grid), dim3(kMoeWarps * 32), smem, st, cluster, p);
+}
+
+int launch_down3(const DownArgs& p, size_t smem, cudaStream_t st) {
+  static size_t configured = 48 * 1024;
+  if (!ensure_smem(down3_kernel, smem, configured)) return NH_E_CUDA;
+  int grid = grid_resident(down3_kernel, p.jobs_total, smem);
+  int cluster = prep_cluster_size(p.topk * p.F, true);
+  while (cluster > grid) cluster >>= 1;
+  grid = round_grid(grid, cluster);
+  return launch_pdl_cluster(down3_kernel, dim3(grid), dim3(kMoeWarps * 32), smem, st, cluster, p);
 }
 
 bool aligned16(const void* p, uint64_t stride) {
@@ -1082,14 +1104,7 @@ extern "C" int nh_moe_gate_up_prefetch(NhDecodeState* state, const float* h, con
     const size_t fixed = ((act_smem_bytes(p.K, true, true) + 15) & ~static_cast<size_t>(15)) + 48 * sizeof(double);
     p.S = pick_stages3(fixed, p.stage_bytes, p.jobs_total);
     const size_t smem = fixed + kMoeWarps * p.S * sizeof(uint64_t) + static_cast<size_t>(kMoeWarps) * p.S * p.stage_bytes;
-    static size_t configured = 48 * 1024;
-    if (!ensure_smem(gate_up3_kernel, smem, configured)) return NH_E_CUDA;
-    int grid = grid_resident(gate_up3_kernel, p.jobs_total, smem);
-    int cluster = prep_cluster_size(p.K, true);
-    while (cluster > grid) cluster >>= 1;
-    grid = round_grid(grid, cluster);
-    return launch_pdl_cluster(gate_up3_kernel, dim3(grid), dim3(kMoeWarps * 32), smem,
-                              static_cast<cudaStream_t>(stream), cluster, p);
+    return launch_gate_up3(p, smem, static_cast<cudaStream_t>(stream));
   }
   if (quant) {
     p.lpr = rowdot_lpr(p.K);
@@ -1164,14 +1179,7 @@ extern "C" int nh_moe_down_combine(const NhDecodeState* state, const float* ff, 
     p.S = pick_stages3(fixed, p.stage_bytes, p.jobs_total);
     const size_t smem = fixed + kMoeWarps * p.S * sizeof(uint64_t) + static_cast<size_t>(kMoeWarps) * p.S * p.stage_bytes;
     if (smem > 220 * 1024) return NH_E_ARG;
-    static size_t configured = 48 * 1024;
-    if (!ensure_smem(down3_kernel, smem, configured)) return NH_E_CUDA;
-    int grid = grid_resident(down3_kernel, p.jobs_total, smem);
-    int cluster = prep_cluster_size(k * p.F, true);
-    while (cluster > grid) cluster >>= 1;
-    grid = round_grid(grid, cluster);
-    return launch_pdl_cluster(down3_kernel, dim3(grid), dim3(kMoeWarps * 32), smem,
-                              static_cast<cudaStream_t>(stream), cluster, p);
+    return launch_down3(p, smem, static_cast<cudaStream_t>(stream));
   }
   if (quant) {
     p.lpr = rowdot_lpr(p.F);
@@ -1213,7 +1221,6 @@ extern "C" int64_t nh_moe_layer_scratch_bytes(int n_expert) { return 64 + 4 * st
 
 namespace {
 
-template <int KP>
 int launch_fused(FusedArgs& p, cudaStream_t st) {
   // Grid: enough warps for one job each (at least the router CTAs), at most
   // two CTAs per SM (the launch bounds); the rings take the remaining jobs.
@@ -1245,15 +1252,15 @@ int launch_fused(FusedArgs& p, cudaStream_t st) {
   const size_t smem = total();
   if (smem > 220 * 1024) return NH_E_ARG;
   static size_t configured = 48 * 1024;
-  if (!ensure_smem(moe_fused_kernel<KP>, smem, configured)) return NH_E_CUDA;
+  if (!ensure_smem(moe_fused_kernel, smem, configured)) return NH_E_CUDA;
   int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, moe_fused_kernel<KP>, kMoeWarps * 32, smem) !=
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, moe_fused_kernel, kMoeWarps * 32, smem) !=
           cudaSuccess ||
       per_sm < 1)
     return NH_E_ARG;
   grid = std::min(grid, per_sm * device_sm_count());
   if (grid < p.router_ctas) return NH_E_ARG;
-  return launch_coop(moe_fused_kernel<KP>, dim3(grid), dim3(kMoeWarps * 32), smem, st, p);
+  return launch_coop(moe_fused_kernel, dim3(grid), dim3(kMoeWarps * 32), smem, st, p);
 }
 
 }  // namespace
@@ -1339,8 +1346,5 @@ extern "C" int nh_moe_layer(const NhMoeLayer* L, void* stream) {
   p.act_bytes = static_cast<uint32_t>(
       (std::max(act_smem_bytes(K, true, true), act_smem_bytes(k * F, false)) + 15) & ~static_cast<size_t>(15));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (E <= 32) return launch_fused<1>(p, st);
-  if (E <= 64) return launch_fused<2>(p, st);
-  if (E <= 128) return launch_fused<4>(p, st);
-  return launch_fused<8>(p, st);
+  return launch_fused(p, st);
 }
