@@ -69,27 +69,27 @@ int64_t nh_attention_scratch_bytes(int n_head, int head_dim, int max_seq);
 int64_t nh_argmax_scratch_bytes(int n_vocab);
 
 /* Embedding row lookup for the token at state->pos (ggml_get_rows on
- * token_embd, forward.cc:94-95, streaming_forward.cc:58-66): dequantises one
+ * token_embd, forward.cc:53-54, streaming_forward.cc:58-66): dequantises one
  * row of `table` ([n_vocab] rows of n_embd) into h_out. */
 int nh_embed_step(const NhDecodeState* state, const int32_t* prompt_ids, const void* table,
                   int32_t type, int64_t n_embd, int64_t n_vocab, float* h_out, void* stream);
 
 /* RMSNorm(h)*attn_norm followed by the Q, K and V projections
- * (attention.cc:128-132): q_out[n_embd], k_out[n_embd_kv], v_out[n_embd_kv].
+ * (attention.cc:79-83): q_out[n_embd], k_out[n_embd_kv], v_out[n_embd_kv].
  * Each weight may be F32, Q4_K or Q6_K independently. */
 int nh_qkv_proj(NhDecodeState* state, const float* h, const float* attn_norm, float eps, const void* wq,
                 int32_t tq, const void* wk, int32_t tk, const void* wv, int32_t tv, int64_t n_embd,
                 int64_t n_embd_kv, float* q_out, float* k_out, float* v_out, void* stream);
 
-/* One decode position of cached attention (attention.cc:133-183): QK-norm
+/* One decode position of cached attention (attention.cc:84-133): QK-norm
  * over the full width (q_norm over n_embd, k_norm over n_embd_kv), NEOX RoPE
  * at state->pos, append post-RoPE K and raw V to the f32 caches
  * ([max_seq][n_embd_kv] per layer, kv_cache.cc:11-22), then causal softmax
  * attention over positions 0..pos split across CTAs with a deterministic
  * combine.  rope_cs is a [max_seq][head_dim/2] table of (cos, sin) pairs for
  * theta_i = pos * base^(-2i/head_dim), theta advanced by repeated f32
- * multiplication as ggml_rope_ext does (attention.cc:137-142); nh_rope_table
- * fills it.  kq_scale = 1/sqrtf(head_dim) (attention.cc:175).  `scratch`
+ * multiplication as ggml_rope_ext does (attention.cc:88-93); nh_rope_table
+ * fills it.  kq_scale = 1/sqrtf(head_dim) (attention.cc:126).  `scratch`
  * holds nh_attention_scratch_bytes() bytes, zeroed once before first use (the
  * kernel leaves its counters zeroed). */
 int nh_attention_step(const NhDecodeState* state, const float* q, const float* k,
@@ -129,11 +129,11 @@ int nh_attention_step_static(const NhDecodeState* state, const float* q, const f
 void nh_rope_table(float base, int head_dim, int max_seq, float* rope_cs_host);
 
 /* h_io[r] = h_io[r] + (W . x)[r]: output projection plus residual
- * (attention.cc:183, forward.cc:106-108). */
+ * (attention.cc:134, forward.cc:65-67). */
 int nh_out_proj_residual(NhDecodeState* state, const float* x, const void* wo, int32_t to,
                          int64_t n_embd, float* h_io, void* stream);
 
-/* Router (moe.cc:16-37, streaming_forward.cc:286-301): RMSNorm(h)*ffn_norm,
+/* Router (moe.cc:16-37, streaming_forward.cc:101-117): RMSNorm(h)*ffn_norm,
  * F32 router GEMV, softmax over n_expert, top-k in descending probability
  * (equal probabilities: lower expert id first), the selected probabilities
  * (renormalised when norm_topk, clamped sum 6.103515625e-5).  Writes sel[k],
@@ -165,7 +165,7 @@ int nh_moe_gate_up_prefetch(NhDecodeState* state, const float* h, const float* f
                             float* ff, const void* down, uint64_t down_nb2, void* stream);
 
 /* Down projections, routing weights and residual (moe.cc:47-60,
- * forward.cc:117-119): h_io[r] = h_io[r] + sum_i wts[i]*(down_e . ff[i])[r],
+ * forward.cc:76-78): h_io[r] = h_io[r] + sum_i wts[i]*(down_e . ff[i])[r],
  * the products rounded before the adds and summed in top-k order.  When
  * dump is not null and state->pos >= n_prompt-1, h_io is also copied to
  * dump[(pos-n_prompt+1)*dump_step_stride + dump_offset + r]. */
@@ -175,7 +175,7 @@ int nh_moe_down_combine(const NhDecodeState* state, const float* ff, const int32
                         float* dump, int64_t dump_step_stride, int64_t dump_offset,
                         void* stream);
 
-/* The whole MoE block of one layer (moe.cc:16-60, forward.cc:111-119) as one
+/* The whole MoE block of one layer (moe.cc:16-60, forward.cc:69-78) as one
  * cooperative kernel: nh_router_topk, nh_moe_gate_up and nh_moe_down_combine
  * in sequence, the same results bit for bit, with the stages separated by
  * device-side waits instead of kernel boundaries.  Q4_K/Q6_K expert tensors
@@ -213,7 +213,47 @@ typedef struct NhMoeLayer {
 int64_t nh_moe_layer_scratch_bytes(int n_expert);
 int nh_moe_layer(const NhMoeLayer* layer, void* stream);
 
-/* Output norm, lm_head GEMV and greedy argmax (forward.cc:123-125,
+/* A whole decoder layer (forward.cc:56-79: attention block, then the MoE
+ * block) as one cooperative kernel: nh_qkv_proj, nh_attention_step,
+ * nh_out_proj_residual and nh_moe_layer in sequence, the same results bit for
+ * bit, the phases separated by device-side grid barriers.  `moe` carries the
+ * MoE block's arguments as for nh_moe_layer (its scratch is not used);
+ * `scratch` holds nh_layer_scratch_bytes(n_expert) bytes, zeroed once (the
+ * kernel leaves it zeroed); attn_scratch as for nh_attention_step.  Covers
+ * Q4_K/Q6_K projections with n_embd/256 and n_head*head_dim/256 in
+ * {1,2,4,8} and the nh_moe_layer shapes; elsewhere (or when the grid cannot
+ * hold every phase's CTAs at once) it returns NH_E_ARG or NH_E_TYPE having
+ * launched nothing. */
+typedef struct NhLayerStep {
+  NhMoeLayer moe;
+  const float* attn_norm;
+  const void* wq;
+  int32_t tq;
+  const void* wk;
+  int32_t tk;
+  const void* wv;
+  int32_t tv;
+  const void* wo;
+  int32_t to;
+  float* q;                 /* [n_head*head_dim] */
+  float* k;                 /* [n_head_kv*head_dim] */
+  float* v;
+  const float* q_norm;
+  const float* k_norm;
+  int n_head, n_head_kv, head_dim;
+  const float* rope_cs;
+  float kq_scale;
+  float* k_cache;
+  float* v_cache;
+  int max_seq;
+  void* attn_scratch;
+  float* attn_out;          /* [n_head*head_dim] */
+  void* scratch;
+} NhLayerStep;
+int64_t nh_layer_scratch_bytes(int n_expert);
+int nh_layer_step(const NhLayerStep* step, void* stream);
+
+/* Output norm, lm_head GEMV and greedy argmax (forward.cc:81-83,
  * generate.cc:93-102): first maximum wins.  Skipped (beyond the state
  * advance) for positions before the last prompt token.  The last CTA writes
  * out_tokens[n_out], feeds the id back into state->token, and advances

@@ -143,11 +143,13 @@ __device__ inline ActSmem carve_act(uint8_t* base, int K, bool need_xf, bool nee
 // issues all its (up to 8) 16-byte loads before its first store, so the row
 // arrives in one memory latency instead of one per loop trip.  Falls back to
 // scalar loads when src or dst is not 16-byte aligned or n is not a multiple
-// of 4.  Does not synchronise.
+// of 4.  Does not synchronise.  CG: load through L2 only (ld.global.cg), for
+// data another CTA of the same grid wrote after a grid-wide barrier.
+template <bool CG = false>
 __device__ inline void copy_to_smem(float* dst, const float* __restrict__ src, int n) {
   const int tid = threadIdx.x, nt = blockDim.x;
   if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) != 0 || (n & 3) != 0) {
-    for (int i = tid; i < n; i += nt) dst[i] = src[i];
+    for (int i = tid; i < n; i += nt) dst[i] = CG ? __ldcg(src + i) : src[i];
     return;
   }
   constexpr int U = 8;
@@ -159,7 +161,7 @@ __device__ inline void copy_to_smem(float* dst, const float* __restrict__ src, i
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int i = base + u * nt;
-      if (i < n4) buf[u] = s4[i];
+      if (i < n4) buf[u] = CG ? __ldcg(s4 + i) : s4[i];
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -247,11 +249,13 @@ __device__ inline void act_load_norm(ActSmem& a, const float* __restrict__ norm_
 // has_norm_w, multiplied by the weight staged by act_load_norm: ggml_rms_norm
 // + ggml_mul, y = (x*scale)*w), left as f32 in xf and Q8_K-quantised when
 // `quant`.  Needs xf.  Ends synchronised.
+// CG: src was written by another CTA of the same grid (see copy_to_smem).
+template <bool CG = false>
 __device__ inline void prep_act(ActSmem& a, const float* __restrict__ src, bool has_norm_w, bool do_norm,
                                 float eps, bool quant, double* red) {
   const int K = a.K;
   const int tid = threadIdx.x, nt = blockDim.x, warp = tid >> 5, lane = tid & 31, nw = nt >> 5;
-  copy_to_smem(a.xf, src, K);
+  copy_to_smem<CG>(a.xf, src, K);
   __syncthreads();
   float scale = 1.f;
   if (do_norm) {

@@ -12,56 +12,9 @@
 
 #include "launch.cuh"
 #include "cluster_prep.cuh"
-#include "rowdot3.cuh"
+#include "gemv3.cuh"
 
 namespace nh {
-
-constexpr int kGemvWarps = 8;
-constexpr int kGemvMaxStages = 4;
-constexpr int kMaxArgmaxBlocks = 2048;
-
-struct GemvSeg {
-  const uint8_t* w;
-  float* out;
-  const float* resid;
-  int32_t rows;
-  int32_t type;
-  uint64_t rb;
-};
-
-struct GemvArgs {
-  GemvSeg seg[3];
-  int nseg;
-  int K;
-  int lpr;  // lanes per row for quantised segments
-  int rpp;  // rows per job for quantised segments (32 / lpr)
-  int jobs_start[4];
-  int jobs_total;
-  uint32_t stage_bytes;
-  int S;  // ring depth (<= kGemvMaxStages)
-  const float* x;
-  const float* norm_w;
-  float eps;
-  int do_norm;
-  int quant;
-  int need_wf;  // stage norm_w in shared memory
-  // lm_head argmax mode
-  int argmax;
-  NhDecodeState* state;
-  float* part_val;
-  int32_t* part_idx;
-  unsigned* ticket;
-  int32_t* out_tokens;
-  float* logits_dump;
-};
-
-__device__ __forceinline__ void gemv_job(const GemvArgs& p, int j, int& s, int& row0, int& nrows) {
-  s = 0;
-  while (s + 1 < p.nseg && j >= p.jobs_start[s + 1]) ++s;
-  const int rpp = p.seg[s].type == NH_TYPE_F32 ? 1 : p.rpp;
-  row0 = (j - p.jobs_start[s]) * rpp;
-  nrows = min(rpp, p.seg[s].rows - row0);
-}
 
 template <int CPL>
 __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const GemvArgs p) {
@@ -374,23 +327,8 @@ int resident_ctas(Kern k, int threads, size_t smem) {
 
 // The lane-per-super-block path: every segment quantised and K <= 2048.
 int gemv3_launch(GemvArgs& p, cudaStream_t stream) {
-  uint64_t rb_max = 0;
-  for (int s = 0; s < p.nseg; ++s) {
-    p.seg[s].rb = row_bytes(p.seg[s].type, p.K);
-    rb_max = rb_max > p.seg[s].rb ? rb_max : p.seg[s].rb;
-  }
-  p.quant = 1;
-  p.need_wf = (p.do_norm != 0 && p.norm_w != nullptr) ? 1 : 0;
-  p.lpr = p.K / QK;      // G: lanes per row
-  p.rpp = 32 / p.lpr;    // P: rows per job (one warp pass)
-  int total = 0;
-  for (int s = 0; s < p.nseg; ++s) {
-    p.jobs_start[s] = total;
-    total += (p.seg[s].rows + p.rpp - 1) / p.rpp;
-  }
-  for (int s = p.nseg; s < 4; ++s) p.jobs_start[s] = total;
-  p.jobs_total = total;
-  p.stage_bytes = static_cast<uint32_t>((rb_max * p.rpp + 32 + 127) & ~127ull);
+  gemv3_shape(p);
+  const int total = p.jobs_total;
   const size_t fixed = ((act_smem_bytes(p.K, true, p.need_wf != 0) + 15) & ~static_cast<size_t>(15)) +
                        48 * sizeof(double);
   p.S = kGemvMaxStages;

@@ -604,7 +604,7 @@ void RouterSoftMax(float* x, int64_t n) {
   for (int64_t i = 0; i < n; ++i) x[i] *= inv;
 }
 
-// Attention of one query over keys 0..n_kv-1 (attention.cc:174-182): scores
+// Attention of one query over keys 0..n_kv-1 (attention.cc:119-133): scores
 // K.q * kq_scale, causal softmax, V.p.  Restated in 64-key splits: a split's
 // exponentials are taken against its own maximum and the splits combined by
 // their maxima, which is the same softmax; one split reduces to ggml's
@@ -759,7 +759,7 @@ void ForwardCached(const Model& m, Kv* kv, const std::vector<int32_t>& tok, bool
   const int n_past = kv->n_past;
   const int64_t group = H / Hkv;
 
-  // ggml_get_rows on token_embd (forward.cc:94-95): dequantised rows.
+  // ggml_get_rows on token_embd (forward.cc:53-54): dequantised rows.
   std::vector<float> h(static_cast<size_t>(T) * d);
   const Tensor* emb = m.T("token_embd.weight");
   for (int t = 0; t < T; ++t) DequantRow(emb->type, emb->data + emb->nb1 * tok[t], d, &h[t * d]);
@@ -776,7 +776,7 @@ void ForwardCached(const Model& m, Kv* kv, const std::vector<int32_t>& tok, bool
     const float* attn_norm = reinterpret_cast<const float*>(m.L(l, "attn_norm.weight")->data);
     const float* q_norm = reinterpret_cast<const float*>(m.L(l, "attn_q_norm.weight")->data);
     const float* k_norm = reinterpret_cast<const float*>(m.L(l, "attn_k_norm.weight")->data);
-    // attention.cc:128-142: norm -> QKV -> QK-norm over the full width -> NEOX RoPE.
+    // attention.cc:79-93: norm -> QKV -> QK-norm over the full width -> NEOX RoPE.
     for (int t = 0; t < T; ++t) {
       RmsNormMul(&h[t * d], attn_norm, d, c.rms_eps, cur.data());
       MatVec(*m.L(l, "attn_q.weight"), 0, cur.data(), &q[t * d]);
@@ -792,11 +792,11 @@ void ForwardCached(const Model& m, Kv* kv, const std::vector<int32_t>& tok, bool
       for (int64_t hh = 0; hh < Hkv; ++hh) {
         RopeNeox(&k[t * dkv + hh * hd], static_cast<int>(hd), n_past + t, c.rope_freq_base);
       }
-      // attention.cc:145-153: the cache holds post-RoPE K and raw V at n_past+t.
+      // attention.cc:95-116: the cache holds post-RoPE K and raw V at n_past+t.
       std::copy(&k[t * dkv], &k[t * dkv] + dkv, kv->k[l].begin() + (n_past + t) * dkv);
       std::copy(&v[t * dkv], &v[t * dkv] + dkv, kv->v[l].begin() + (n_past + t) * dkv);
     }
-    // attention.cc:174-182: kq = K.q * 1/sqrt(hd), causal mask offset n_past, softmax, V.p.
+    // attention.cc:119-133: kq = K.q * 1/sqrt(hd), causal mask offset n_past, softmax, V.p.
     // Query t sees keys 0..n_past+t (the causal mask of ggml_diag_mask_inf).
     Pool::Get().For(H * T, [&](int64_t b, int64_t e) {
       for (int64_t job = b; job < e; ++job) {
@@ -807,7 +807,7 @@ void ForwardCached(const Model& m, Kv* kv, const std::vector<int32_t>& tok, bool
                   static_cast<int>(hd), kq_scale, &att[t * d + hh * hd]);
       }
     });
-    // Output projection and residual (forward.cc:106-108).
+    // Output projection and residual (forward.cc:65-67).
     std::vector<float> o(d);
     for (int t = 0; t < T; ++t) {
       MatVec(*m.L(l, "attn_output.weight"), 0, &att[t * d], o.data());
@@ -892,7 +892,7 @@ void ForwardCached(const Model& m, Kv* kv, const std::vector<int32_t>& tok, bool
       std::copy(&h[(T - 1) * d], &h[(T - 1) * d] + d, obs->hidden_last->begin() + l * d);
     }
   }
-  // Output norm and lm_head (forward.cc:123-125), every position.
+  // Output norm and lm_head (forward.cc:81-83), every position.
   logits->resize(static_cast<size_t>(T) * V);
   const float* onorm = reinterpret_cast<const float*>(m.T("output_norm.weight")->data);
   for (int t = 0; t < T; ++t) {
