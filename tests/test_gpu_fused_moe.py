@@ -44,7 +44,7 @@ FORMS = {"layer": {"NH_FUSED_LAYER": "1"}, "moe": {"NH_FUSED_LAYER": "0"},
 def _run(path, out, env_over, n_prompt, n_predict, norm_topk):
     env = dict(os.environ, **env_over)
     subprocess.run([sys.executable, "-c", SCRIPT, str(path), str(out), str(n_prompt), str(n_predict),
-                    "1" if norm_topk else "0"], env=env, cwd=ROOT, check=True, timeout=900)
+                    "1" if norm_topk else "0"], env=env, cwd=ROOT, check=True, timeout=300)
     return np.load(out)
 
 
