@@ -86,8 +86,11 @@ __device__ __forceinline__ void router_load_row(const RouterArgs& p, float4 (&wv
 // experts and their weights (renormalised when norm_topk, clamped sum
 // 6.103515625e-5) to o_sel/o_wts (shared) and, when `outputs`, to p.sel,
 // p.wts and the trace.  Needs blockDim.x >= 32 and >= k; ends synchronised.
-__device__ __forceinline__ void router_select_block(const RouterArgs& p, const float* logits, bool outputs,
-                                                    int64_t pos, int* o_sel, float* o_wts) {
+// `pr`: in warp 0, lane l's logits of experts l, l+32, ... (-INF beyond E).
+constexpr int kLogitsPerLane = kMaxExperts / 32;  // absent experts add exact zeros to the sums
+
+__device__ __forceinline__ void router_select_core(const RouterArgs& p, float (&pr)[kLogitsPerLane], bool outputs,
+                                                   int64_t pos, int* o_sel, float* o_wts) {
   __shared__ __align__(16) float s_prob[kMaxExperts];
   __shared__ int s_ids[kMaxTopK + 1];
   __shared__ float s_vals[kMaxTopK + 1];
@@ -101,15 +104,10 @@ __device__ __forceinline__ void router_select_block(const RouterArgs& p, const f
     s_vals[tid] = 0.f;
   }
   if (warp == 0) {
-    constexpr int kPer = kMaxExperts / 32;  // experts per lane (absent ones add exact zeros)
-    float pr[kPer];
+    constexpr int kPer = kLogitsPerLane;
     float mx = -INFINITY;
 #pragma unroll
-    for (int k = 0; k < kPer; ++k) {
-      const int i = lane + 32 * k;
-      pr[k] = i < E ? __ldcg(logits + i) : -INFINITY;
-      mx = fmaxf(mx, pr[k]);
-    }
+    for (int k = 0; k < kPer; ++k) mx = fmaxf(mx, pr[k]);
     mx = warp_max(mx);
     double sum = 0.0;
 #pragma unroll
@@ -171,6 +169,20 @@ __device__ __forceinline__ void router_select_block(const RouterArgs& p, const f
     if (lane == 0) p.trace_gap[pos * p.n_layers + p.layer] = g;
   }
   __syncthreads();
+}
+
+// router_select_core on logits in global memory (another CTA wrote them and
+// published them before this CTA's acquire).
+__device__ __forceinline__ void router_select_block(const RouterArgs& p, const float* logits, bool outputs,
+                                                    int64_t pos, int* o_sel, float* o_wts) {
+  float pr[kLogitsPerLane];
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 0; k < kLogitsPerLane; ++k) {
+    const int i = lane + 32 * k;
+    pr[k] = (threadIdx.x < 32 && i < p.E) ? __ldcg(logits + i) : -INFINITY;
+  }
+  router_select_core(p, pr, outputs, pos, o_sel, o_wts);
 }
 
 __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(const RouterArgs p) {
@@ -719,17 +731,21 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) down3_kernel(const DownArgs
 // Router, gate/up and down of one layer in one cooperative grid (every CTA
 // resident at once).  The first router_ctas CTAs compute the logits (one warp
 // per expert, the f32 row staged in shared memory before the preceding kernel
-// ends) and count themselves in sync[0]; every CTA then selects the experts
-// itself from the logits (CTA 0 also writes the router outputs), streams its
+// ends) and publish each as one 64-bit word tagged with the launch (`epoch`
+// + 1); every CTA polls the E words until all carry this launch's tag,
+// selects the experts itself (CTA 0 also writes the router outputs), streams its
 // warps' gate/up jobs and, as soon as a warp's last one is consumed, stages
 // the warp's first down jobs in the same shared-memory region, so the down
 // rows load while the grid gathers at sync[1] behind the last ff row.
-// sync[2] counts exits; the last CTA to leave zeroes the three counters for
-// the next launch.  Every wait is bounded and records NH_E_TIMEOUT.
+// sync[2] counts exits; the last CTA to leave zeroes the counters and
+// advances the epoch for the next launch.  Every wait is bounded and records
+// NH_E_TIMEOUT.
 struct FusedArgs {
   RouterArgs r;
   GateUpArgs g;
   DownArgs d;
+  unsigned long long* tagged;  // [E] logits published as (tag << 32) | f32 bits
+  unsigned* epoch;             // launches completed; this launch's tag is epoch + 1
   unsigned* sync;
   int router_ctas;
   uint32_t act_bytes;     // the shared activation region (gate/up, then down)
@@ -749,6 +765,42 @@ __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
 // thread that acquires the new count.
 __device__ __forceinline__ void red_release_gpu(unsigned* p, unsigned v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;\n" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+constexpr int kLogitSpins = 1 << 21;
+
+// Warp 0: the E logits this launch published (each a single 64-bit word
+// carrying its launch tag, so a word is either this launch's value or is
+// rejected), lane l getting experts l, l+32, ... (-INF beyond E).  Bounded:
+// returns false if they have not all arrived after kLogitSpins polls.
+__device__ __forceinline__ bool collect_logits(const unsigned long long* tagged, int E, unsigned tag, int lane,
+                                               float (&pr)[kLogitsPerLane]) {
+  for (int it = 0; it < kLogitSpins; ++it) {
+    bool mine = true;
+#pragma unroll
+    for (int k = 0; k < kLogitsPerLane; ++k) {
+      const int i = lane + 32 * k;
+      pr[k] = -INFINITY;
+      if (i < E) {
+        const unsigned long long v = ld_relaxed_u64(tagged + i);
+        if (static_cast<unsigned>(v >> 32) == tag)
+          pr[k] = __uint_as_float(static_cast<unsigned>(v));
+        else
+          mine = false;
+      }
+    }
+    if (__all_sync(0xffffffffu, mine)) return true;
+  }
+  return false;
 }
 
 // Bounded wait (one thread) until *p >= target.
@@ -802,6 +854,7 @@ struct MoeShared {
   int sel[kMaxTopK];
   float wts[kMaxTopK];
   int ok, pos, np;
+  unsigned tag;
 };
 
 // Lane 0: initialise the warp's MoE barriers (the caller fences the inits).
@@ -821,11 +874,12 @@ __device__ __forceinline__ void moe_stage_router_row(const FusedArgs& p, const M
 
 // The MoE block of one layer once h is final, block-wide: the normalised,
 // quantised activation; the router warps' logits (router_e >= 0: this warp's
-// expert, its row staged by moe_stage_router_row), counted in sync[0]; the
-// selection in every CTA (CTA 0 writes the router outputs); the gate/up jobs,
+// expert, its row staged by moe_stage_router_row), published tagged with
+// sh.tag; the selection in every CTA once it has collected all E logits (CTA
+// 0 writes the router outputs); the gate/up jobs,
 // then the down rows staged in the same regions; the grid barrier sync[1];
 // the ff activation and the down jobs.  The norm weight must already be in
-// a.wf (act_load_norm) and sh.pos / sh.np set before the call.  Returns false
+// a.wf (act_load_norm) and sh.pos / sh.np / sh.tag set before the call.  Returns false
 // where a bounded wait expired.
 __device__ __forceinline__ bool moe_run(const FusedArgs& p, uint8_t* smem, const MoeWarp& w, bool router_cta,
                                         int router_e, MoeShared& sh, double* red) {
@@ -852,16 +906,21 @@ __device__ __forceinline__ bool moe_run(const FusedArgs& p, uint8_t* smem, const
         sdot = __fadd_rn(sdot, __fmul_rn(wv.w, x.w));
       }
       sdot = warp_sum(sdot);
-      if (lane == 0) p.r.logits[router_e] = sdot;
+      if (lane == 0)
+        st_relaxed_u64(p.tagged + router_e,
+                       (static_cast<unsigned long long>(sh.tag) << 32) | __float_as_uint(sdot));
     }
-    __syncthreads();
-    if (threadIdx.x == 0) red_release_gpu(&p.sync[0], 1u);
   }
-  if (threadIdx.x == 0) sh.ok = wait_count(&p.sync[0], static_cast<unsigned>(p.router_ctas));
+  // Every CTA collects the logits itself (warp 0) and selects.
+  float pr[kLogitsPerLane];
+  if (threadIdx.x < 32) {
+    const bool got = collect_logits(p.tagged, p.r.E, sh.tag, lane, pr);
+    if (lane == 0) sh.ok = got;
+  }
   __syncthreads();
   const bool sel_ok = sh.ok != 0;
   if (sel_ok) {
-    router_select_block(p.r, p.r.logits, blockIdx.x == 0, sh.pos, sh.sel, sh.wts);
+    router_select_core(p.r, pr, blockIdx.x == 0, sh.pos, sh.sel, sh.wts);
     for (int st = 0; st < g.S; ++st) {
       const int j = gw + st * tw;
       if (j < g.jobs_total) gu3_issue(g, sh.sel, w.gbar, w.wb, j, st, lane);
@@ -931,14 +990,15 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) moe_fused_kernel(const __gr
   if (threadIdx.x == 0) {
     sh.pos = p.d.state->pos;
     sh.np = p.d.state->n_prompt;
+    sh.tag = *reinterpret_cast<volatile unsigned*>(p.epoch) + 1u;
   }
   const bool ok = moe_run(p, smem, w, router_cta, router_e, sh, red);
   if (!ok && lane == 0) atomicCAS(&p.d.state->error, 0, NH_E_TIMEOUT);
   __syncthreads();
   if (threadIdx.x == 0 && atomicAdd(&p.sync[2], 1u) == gridDim.x - 1) {
-    p.sync[0] = 0u;
     p.sync[1] = 0u;
     p.sync[2] = 0u;
+    *p.epoch = sh.tag;  // every CTA has read this launch's tag
     __threadfence();
   }
 }
@@ -957,7 +1017,7 @@ struct LayerArgs {
   GemvArgs qkv;   // segments q, k, v; x = h, norm_w = attn_norm
   AttnArgs attn;
   GemvArgs out;   // segment o, resid = out = h; x = attention output
-  FusedArgs moe;  // sync[0] router count, sync[1] ff barrier
+  FusedArgs moe;  // sync[1] ff barrier
   unsigned* lsync;  // [0] q/k/v written, [1] attention written, [2] h written, [3] exits
   int qkv_ctas, out_ctas, attn_cta0, attn_ctas, router_cta0;
   uint32_t attn_off;  // offset of the attention items' shared memory (the staging regions)
@@ -1017,6 +1077,8 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) layer_kernel(const __grid_c
   if (threadIdx.x == 0) {
     sh.pos = *reinterpret_cast<volatile const int*>(&p.d.state->pos);
     sh.np = *reinterpret_cast<volatile const int*>(&p.d.state->n_prompt);
+    // The previous launch's last CTA advanced the epoch before it exited.
+    sh.tag = *reinterpret_cast<volatile unsigned*>(p.epoch) + 1u;
   }
   {
     const int warp = threadIdx.x >> 5;
@@ -1111,7 +1173,7 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) layer_kernel(const __grid_c
   if (!ok && lane == 0) atomicCAS(&p.d.state->error, 0, NH_E_TIMEOUT);
   __syncthreads();
   if (threadIdx.x == 0 && atomicAdd(&L.lsync[3], 1u) == gridDim.x - 1) {
-    p.sync[0] = 0u;
+    *p.epoch = sh.tag;
     p.sync[1] = 0u;
     L.lsync[0] = 0u;
     L.lsync[1] = 0u;
@@ -1440,7 +1502,8 @@ extern "C" int nh_moe_down_combine(const NhDecodeState* state, const float* ff, 
   return cpl <= 1 ? launch_down<1>(p, smem, grid, s) : launch_down<2>(p, smem, grid, s);
 }
 
-extern "C" int64_t nh_moe_layer_scratch_bytes(int n_expert) { return 64 + 4 * static_cast<int64_t>(n_expert) + 64; }
+// 16 counters, then the E tagged logits (8 bytes each).
+extern "C" int64_t nh_moe_layer_scratch_bytes(int n_expert) { return 64 + 8 * static_cast<int64_t>(n_expert) + 64; }
 
 namespace {
 
@@ -1525,7 +1588,9 @@ extern "C" int nh_moe_layer(const NhMoeLayer* L, void* stream) {
   r.trace_sel = L->trace_sel;
   r.trace_gap = L->trace_gap;
   r.ticket = static_cast<unsigned*>(L->scratch);
-  r.logits = reinterpret_cast<float*>(static_cast<uint8_t*>(L->scratch) + 64);
+  r.logits = nullptr;  // published tagged (below), not through the standalone router's array
+  p.tagged = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(L->scratch) + 64);
+  p.epoch = static_cast<unsigned*>(L->scratch) + 15;
   p.sync = static_cast<unsigned*>(L->scratch) + 1;
   p.router_ctas = (E + kMoeWarps - 1) / kMoeWarps;
   GateUpArgs& g = p.g;
@@ -1572,7 +1637,7 @@ extern "C" int nh_moe_layer(const NhMoeLayer* L, void* stream) {
   return launch_fused(p, st);
 }
 
-extern "C" int64_t nh_layer_scratch_bytes(int n_expert) { return 64 + 4 * static_cast<int64_t>(n_expert) + 64; }
+extern "C" int64_t nh_layer_scratch_bytes(int n_expert) { return 64 + 8 * static_cast<int64_t>(n_expert) + 64; }
 
 extern "C" int nh_layer_step(const NhLayerStep* S, void* stream) {
   if (S == nullptr || S->scratch == nullptr || S->attn_norm == nullptr || S->wq == nullptr || S->wk == nullptr ||
@@ -1629,8 +1694,10 @@ extern "C" int nh_layer_step(const NhLayerStep* S, void* stream) {
   r.trace_gap = M->trace_gap;
   unsigned* counters = static_cast<unsigned*>(S->scratch);
   r.ticket = counters;
-  r.logits = reinterpret_cast<float*>(static_cast<uint8_t*>(S->scratch) + 64);
-  p.sync = counters + 1;   // [0] router count, [1] ff barrier
+  r.logits = nullptr;
+  p.tagged = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(S->scratch) + 64);
+  p.epoch = counters + 15;
+  p.sync = counters + 1;   // [1] ff barrier
   L.lsync = counters + 4;  // [0..2] phase barriers, [3] exits
   p.router_ctas = (E + kMoeWarps - 1) / kMoeWarps;
   GateUpArgs& g = p.g;
