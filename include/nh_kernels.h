@@ -183,7 +183,10 @@ int nh_moe_down_combine(const NhDecodeState* state, const float* ff, const int32
  * outside that range (or when the grid cannot be co-resident) it returns
  * NH_E_ARG or NH_E_TYPE having launched nothing, and the three kernels above
  * do the work.  `scratch`: nh_moe_layer_scratch_bytes(n_expert) bytes,
- * zeroed once (the kernel leaves it zeroed). */
+ * zeroed once before the first call.  Between calls it keeps a launch count
+ * and the router logits tagged with it, so keep using the same (unmodified)
+ * scratch, or zero it again, and give calls that may overlap on the GPU
+ * separate scratch. */
 typedef struct NhMoeLayer {
   NhDecodeState* state;
   float* h;                 /* in: the residual stream; out: h + MoE(h) */
@@ -218,8 +221,8 @@ int nh_moe_layer(const NhMoeLayer* layer, void* stream);
  * nh_out_proj_residual and nh_moe_layer in sequence, the same results bit for
  * bit, the phases separated by device-side grid barriers.  `moe` carries the
  * MoE block's arguments as for nh_moe_layer (its scratch is not used);
- * `scratch` holds nh_layer_scratch_bytes(n_expert) bytes, zeroed once (the
- * kernel leaves it zeroed); attn_scratch as for nh_attention_step.  Covers
+ * `scratch` holds nh_layer_scratch_bytes(n_expert) bytes, with the same
+ * rules as nh_moe_layer's; attn_scratch as for nh_attention_step.  Covers
  * Q4_K/Q6_K projections with n_embd/256 and n_head*head_dim/256 in
  * {1,2,4,8} and the nh_moe_layer shapes; elsewhere (or when the grid cannot
  * hold every phase's CTAs at once) it returns NH_E_ARG or NH_E_TYPE having
