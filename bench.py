@@ -46,9 +46,6 @@ GATE_UP_BYTES = 8 * 2 * 1024 * 1152  # one nh_moe_gate_up launch: 8 experts x (g
 # layers: router 524,288 B + gate/up 18,874,368 B + down 8 x 2048 rows of 576 B
 # (Q4_K layers) or 840 B (Q6_K layers), 8 of each.
 MOE_LAYER_BYTES = 524288 + GATE_UP_BYTES + (8 * 2048 * 576 + 8 * 2048 * 840) // 2
-# One nh_layer_step launch: the attention weights (Q4_K Q/K/V/O, Q6_K V on
-# half the layers: 9,437,184 or 10,518,528 B) plus the MoE block above.
-LAYER_BYTES = (9437184 + 10518528) // 2 + MOE_LAYER_BYTES
 
 
 def step_bytes_per_token(cfg_layers=16) -> float:
@@ -410,9 +407,8 @@ def main() -> None:
     # ---- dominant kernel timed alone on the same stream, cycling through all
     # 16 layers so every launch streams its weights from HBM: the fused MoE
     # block (router + gate/up + down) when the step uses it, else gate/up.
-    layer = launches_per_token == 2 + 16
     fused = launches_per_token == 2 + 4 * 16
-    which, kbytes = (4, LAYER_BYTES) if layer else ((3, MOE_LAYER_BYTES) if fused else (0, GATE_UP_BYTES))
+    which, kbytes = (3, MOE_LAYER_BYTES) if fused else (0, GATE_UP_BYTES)
     reps = 20
     k0 = torch.cuda.Event(enable_timing=True)
     k1 = torch.cuda.Event(enable_timing=True)
@@ -425,9 +421,8 @@ def main() -> None:
     k_ms = k0.elapsed_time(k1) / n_k
     peaks = measured_peaks()
     achieved = kbytes / (k_ms / 1000.0) / 1e9
-    traffic = traffic_summary("layer" if layer else ("moe_layer" if fused else "moe_gate_up"))
-    kname = ("nh_layer_step (QKV + attention + out_proj + router + 8 experts, Q4_K/Q6_K)" if layer else
-             "nh_moe_layer (router + 8 experts gate/up + down, Q4_K/Q6_K)" if fused
+    traffic = traffic_summary("moe_layer" if fused else "moe_gate_up")
+    kname = ("nh_moe_layer (router + 8 experts gate/up + down, Q4_K/Q6_K)" if fused
              else "nh_moe_gate_up (8 experts x gate+up, Q4_K)")
     roofline = {"kernel": kname, "bound": "hbm", "achieved": achieved,
                 "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,

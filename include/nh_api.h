@@ -73,8 +73,8 @@ int nh_generate_batch(void* model, const int32_t* prompts, int n_seq, int n_prom
  * as CUDA graph replays on the model's stream; asynchronous.  result: waits
  * and copies the ids of the last run.  stream: the model's cudaStream_t.
  * kernel_loop: enqueues reps passes over all layers of one kernel (0 expert
- * gate/up, 1 expert down, 2 QKV, 3 the fused MoE block nh_moe_layer, 4 the
- * whole-layer kernel nh_layer_step) on that stream; returns launches. */
+ * gate/up, 1 expert down, 2 QKV, 3 the fused MoE block nh_moe_layer) on that
+ * stream; returns launches. */
 int nh_decode_prepare(void* model, const int32_t* prompt, int n_prompt, int n_predict);
 int nh_decode_run(void* model, int n_predict);
 int nh_decode_result(void* model, int n_predict, int32_t* out_tokens);

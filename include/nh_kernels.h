@@ -111,8 +111,11 @@ int nh_attention_step(const NhDecodeState* state, const float* q, const float* k
  *     nh_attention_scratch_bytes(n_head, head_dim, max_seq) exceeds
  *     NH_ATTN_STATIC_SCRATCH_BYTES or n_head > 64 (for head_dim 128 and 16
  *     heads that allows max_seq up to 7,936).
+ *   - Every argument check runs first: a rejected call enqueues nothing.
  *   - The first call on a device looks up the array's device address (with
  *     that device current); make that first call before any stream capture.
+ *     The address is kept for the life of the process; after cudaDeviceReset
+ *     on a device it is stale, so do not call this entry there again.
  *   - Every call clears the array's split counters on `stream`, then runs the
  *     step there.  All calls on a device share its one array and it keeps the
  *     last call's contents: calls that can overlap on the GPU (issued to
@@ -216,45 +219,6 @@ typedef struct NhMoeLayer {
 int64_t nh_moe_layer_scratch_bytes(int n_expert);
 int nh_moe_layer(const NhMoeLayer* layer, void* stream);
 
-/* A whole decoder layer (forward.cc:56-79: attention block, then the MoE
- * block) as one cooperative kernel: nh_qkv_proj, nh_attention_step,
- * nh_out_proj_residual and nh_moe_layer in sequence, the same results bit for
- * bit, the phases separated by device-side grid barriers.  `moe` carries the
- * MoE block's arguments as for nh_moe_layer (its scratch is not used);
- * `scratch` holds nh_layer_scratch_bytes(n_expert) bytes, with the same
- * rules as nh_moe_layer's; attn_scratch as for nh_attention_step.  Covers
- * Q4_K/Q6_K projections with n_embd/256 and n_head*head_dim/256 in
- * {1,2,4,8} and the nh_moe_layer shapes; elsewhere (or when the grid cannot
- * hold every phase's CTAs at once) it returns NH_E_ARG or NH_E_TYPE having
- * launched nothing. */
-typedef struct NhLayerStep {
-  NhMoeLayer moe;
-  const float* attn_norm;
-  const void* wq;
-  int32_t tq;
-  const void* wk;
-  int32_t tk;
-  const void* wv;
-  int32_t tv;
-  const void* wo;
-  int32_t to;
-  float* q;                 /* [n_head*head_dim] */
-  float* k;                 /* [n_head_kv*head_dim] */
-  float* v;
-  const float* q_norm;
-  const float* k_norm;
-  int n_head, n_head_kv, head_dim;
-  const float* rope_cs;
-  float kq_scale;
-  float* k_cache;
-  float* v_cache;
-  int max_seq;
-  void* attn_scratch;
-  float* attn_out;          /* [n_head*head_dim] */
-  void* scratch;
-} NhLayerStep;
-int64_t nh_layer_scratch_bytes(int n_expert);
-int nh_layer_step(const NhLayerStep* step, void* stream);
 
 /* Output norm, lm_head GEMV and greedy argmax (forward.cc:81-83,
  * generate.cc:93-102): first maximum wins.  Skipped (beyond the state

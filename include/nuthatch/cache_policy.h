@@ -9,9 +9,8 @@
 #define NUTHATCH_B200_CACHE_POLICY_H_
 
 #include <cstdint>
-#include <list>
+#include <map>
 #include <unordered_map>
-#include <unordered_set>
 #include <vector>
 
 #include "nuthatch/routing_trace.h"
@@ -35,6 +34,25 @@ class CachePolicy {
 // Replays every access of the trace, in record order (cache_policy.cc:5-18).
 ReplayStats Replay(const RoutingTrace& trace, CachePolicy* policy);
 
+// The building block of every policy below: a set of at most `capacity` keys
+// ordered by last use.  Touch(key) reports whether the key was present and
+// makes it the most recent; a key that is not present is inserted, and when
+// that overfills the set the key touched longest ago leaves.  Each touch
+// stamps the key with the next value of a use clock; `by_stamp_` indexes the
+// keys by stamp, so the oldest is its first entry.  Capacity 0 holds nothing.
+class RecencySet {
+ public:
+  explicit RecencySet(uint64_t capacity = 0) : capacity_(capacity) {}
+  bool Touch(uint64_t key);
+  uint64_t size() const { return stamp_of_.size(); }
+
+ private:
+  uint64_t capacity_;
+  uint64_t clock_ = 0;
+  std::unordered_map<uint64_t, uint64_t> stamp_of_;  // key -> stamp of its last use
+  std::map<uint64_t, uint64_t> by_stamp_;            // stamp -> key
+};
+
 // Per-layer LRU of slots_per_layer experts (lru_policy.cc:5-30).
 class LruPolicy : public CachePolicy {
  public:
@@ -42,12 +60,7 @@ class LruPolicy : public CachePolicy {
   bool Access(uint32_t layer, uint32_t expert) override;
 
  private:
-  struct Layer {
-    std::list<uint32_t> order;  // front = most recent
-    std::unordered_map<uint32_t, std::list<uint32_t>::iterator> pos;
-  };
-  uint32_t slots_;
-  std::vector<Layer> layers_;
+  std::vector<RecencySet> per_layer_;
 };
 
 // One global LRU over (layer, expert) of `capacity` entries: the OS page
@@ -58,9 +71,7 @@ class OsPageCachePolicy : public CachePolicy {
   bool Access(uint32_t layer, uint32_t expert) override;
 
  private:
-  uint64_t cap_;
-  std::list<uint64_t> order_;
-  std::unordered_map<uint64_t, std::list<uint64_t>::iterator> pos_;
+  RecencySet resident_;  // keys (layer << 32) | expert
 };
 
 // Per-layer usage counts (learned_pin_policy.h:14-17).
@@ -81,13 +92,8 @@ class LearnedPinPolicy : public CachePolicy {
   bool Access(uint32_t layer, uint32_t expert) override;
 
  private:
-  struct Layer {
-    std::unordered_set<uint32_t> pinned;
-    std::list<uint32_t> order;
-    std::unordered_map<uint32_t, std::list<uint32_t>::iterator> pos;
-  };
-  uint32_t lru_slots_;
-  std::vector<Layer> layers_;
+  std::vector<std::vector<uint32_t>> pinned_;  // per layer, sorted ascending
+  std::vector<RecencySet> rest_;               // per layer, lru_slots each
 };
 
 // Budget and pin-ratio sweeps (trace_sweep.cc:10-50): learned uses

@@ -1,4 +1,5 @@
-// Routing trace records and file formats (reference: src/trace/routing_trace.h:11-34).
+// Routing trace records and file formats (reference: src/trace/routing_trace.h:11-34;
+// implemented in csrc/host/trace_io.cc).
 // Binary format: magic "NUTHTRC1", u32 version 1, u32 n_layers, u32 n_expert,
 // u64 record count, then per record u32 token, u32 layer, u32 n, n x u32
 // expert ids; native byte order (routing_trace.cc:14-43).  Text format: one

@@ -36,14 +36,6 @@ class NhMoeLayer(C.Structure):
                 ("dump_offset", i64), ("scratch", vp)]
 
 
-class NhLayerStep(C.Structure):
-    _fields_ = [("moe", NhMoeLayer), ("attn_norm", vp), ("wq", vp), ("tq", i32), ("wk", vp), ("tk", i32),
-                ("wv", vp), ("tv", i32), ("wo", vp), ("to", i32), ("q", vp), ("k", vp), ("v", vp),
-                ("q_norm", vp), ("k_norm", vp), ("n_head", C.c_int), ("n_head_kv", C.c_int), ("head_dim", C.c_int),
-                ("rope_cs", vp), ("kq_scale", f32), ("k_cache", vp), ("v_cache", vp), ("max_seq", C.c_int),
-                ("attn_scratch", vp), ("attn_out", vp), ("scratch", vp)]
-
-
 # name -> (restype, argtypes)
 SIGNATURES = {
     # nh_api.h
@@ -108,8 +100,6 @@ SIGNATURES = {
     "nh_moe_down_combine": (C.c_int, [vp, vp, vp, vp, C.c_int, vp, i32, u64, i64, i64, vp, vp, i64, i64, vp]),
     "nh_moe_layer": (C.c_int, [P(NhMoeLayer), vp]),
     "nh_moe_layer_scratch_bytes": (i64, [C.c_int]),
-    "nh_layer_step": (C.c_int, [P(NhLayerStep), vp]),
-    "nh_layer_scratch_bytes": (i64, [C.c_int]),
     "nh_lm_head_argmax": (C.c_int, [vp, vp, vp, f32, vp, i32, i64, i64, vp, vp, vp, vp]),
     "nh_gemv": (C.c_int, [vp, vp, i32, i64, i64, vp, vp, f32, vp, vp]),
     "nh_quantize_q8k": (C.c_int, [vp, i64, vp, vp]),

@@ -38,19 +38,6 @@ bool FusedMoeEnabled() {
   return v != 0;
 }
 
-// Each whole layer runs as one cooperative kernel only when NH_FUSED_LAYER=1
-// (read once; identical results).  Measured on B200 it is slower than the
-// attention kernels plus the fused MoE block (every phase's code is cold in
-// the instruction caches when a warp reaches it), so it is not the default.
-bool FusedLayerEnabled() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = std::getenv("NH_FUSED_LAYER");
-    v = (e != nullptr && e[0] == '1') ? 1 : 0;
-  }
-  return v != 0;
-}
-
 template <typename T>
 void DevFree(T*& p) {
   if (p != nullptr) cudaFree(p);
@@ -176,9 +163,8 @@ void Engine::FreeAll() {
   if (attn_scratch_) cudaFree(attn_scratch_);
   if (router_scratch_) cudaFree(router_scratch_);
   if (moe_scratch_) cudaFree(moe_scratch_);
-  if (layer_scratch_) cudaFree(layer_scratch_);
   if (argmax_scratch_) cudaFree(argmax_scratch_);
-  attn_scratch_ = router_scratch_ = moe_scratch_ = layer_scratch_ = argmax_scratch_ = nullptr;
+  attn_scratch_ = router_scratch_ = moe_scratch_ = argmax_scratch_ = nullptr;
   DevFree(trace_sel_);
   DevFree(trace_gap_);
   DevFree(dump_hidden_);
@@ -230,10 +216,8 @@ int Engine::Reserve(int max_seq, int max_prompt, int max_predict, bool dumps) {
   const int64_t mb = nh_argmax_scratch_bytes(c.n_vocab);
   const int64_t fb = nh_moe_layer_scratch_bytes(c.n_expert);
   if (cudaMalloc(&attn_scratch_, ab) != cudaSuccess || cudaMalloc(&router_scratch_, rb) != cudaSuccess ||
-      cudaMalloc(&moe_scratch_, fb) != cudaSuccess || cudaMalloc(&argmax_scratch_, mb) != cudaSuccess ||
-      cudaMalloc(&layer_scratch_, nh_layer_scratch_bytes(c.n_expert)) != cudaSuccess)
+      cudaMalloc(&moe_scratch_, fb) != cudaSuccess || cudaMalloc(&argmax_scratch_, mb) != cudaSuccess)
     return NH_E_NOMEM;
-  cudaMemset(layer_scratch_, 0, nh_layer_scratch_bytes(c.n_expert));
   cudaMemset(attn_scratch_, 0, ab);
   cudaMemset(router_scratch_, 0, rb);
   cudaMemset(moe_scratch_, 0, fb);
@@ -325,39 +309,6 @@ int Engine::EnqueueFusedMoe(const ModelView& m, int l, bool norm_topk, bool trac
   return nh_moe_layer(&a, stream_);
 }
 
-int Engine::EnqueueLayer(const ModelView& m, int l, bool norm_topk, bool trace, bool dumps) {
-  const OlmoeConfig& c = cfg_;
-  const LayerView& L = m.layers[l];
-  NhLayerStep st{};
-  FillMoeLayer(m, l, norm_topk, trace, dumps, &st.moe);
-  st.attn_norm = L.attn_norm;
-  st.wq = L.wq;
-  st.tq = L.tq;
-  st.wk = L.wk;
-  st.tk = L.tk;
-  st.wv = L.wv;
-  st.tv = L.tv;
-  st.wo = L.wo;
-  st.to = L.to;
-  st.q = q_;
-  st.k = k_;
-  st.v = v_;
-  st.q_norm = L.q_norm;
-  st.k_norm = L.k_norm;
-  st.n_head = static_cast<int>(c.n_head);
-  st.n_head_kv = static_cast<int>(c.n_head_kv);
-  st.head_dim = static_cast<int>(c.head_dim());
-  st.rope_cs = rope_cs_;
-  st.kq_scale = 1.0f / std::sqrt(static_cast<float>(st.head_dim));
-  st.k_cache = kv_->k(l);
-  st.v_cache = kv_->v(l);
-  st.max_seq = max_seq_;
-  st.attn_scratch = attn_scratch_;
-  st.attn_out = attn_;
-  st.scratch = layer_scratch_;
-  return nh_layer_step(&st, stream_);
-}
-
 int Engine::EnqueueAttnPhase(const ModelView& m, int l, bool norm_topk, bool trace) {
   const OlmoeConfig& c = cfg_;
   const LayerView& L = m.layers[l];
@@ -390,14 +341,6 @@ int Engine::EnqueueStep(const ModelView& m, bool norm_topk, bool trace, bool dum
   int launches = 2;  // embed, lm_head
   for (int l = 0; l < static_cast<int>(cfg_.n_layers); ++l) {
     const LayerView& L = m.layers[l];
-    if (FusedLayerEnabled()) {
-      const int rc = EnqueueLayer(m, l, norm_topk, trace, dumps);
-      if (rc == NH_OK) {
-        launches += 1;
-        continue;
-      }
-      if (rc != NH_E_ARG && rc != NH_E_TYPE) return rc;
-    }
     launches += 6;
     if (FusedMoeEnabled()) {
       NH_TRY(EnqueueAttention(m, l));
@@ -488,8 +431,6 @@ int Engine::KernelLoop(const ModelView& m, int which, int reps) {
                             L.up_nb2, c.n_embd, c.n_ff, ff_, stream_);
       } else if (which == 3) {
         rc = EnqueueFusedMoe(m, l, false, false, false);
-      } else if (which == 4) {
-        rc = EnqueueLayer(m, l, false, false, false);
       } else if (which == 1) {
         rc = nh_moe_down_combine(state_, ff_, sel_, wts_, c.n_expert_used, L.down, L.td, L.down_nb2, c.n_ff,
                                  c.n_embd, h_, nullptr, 0, 0, stream_);

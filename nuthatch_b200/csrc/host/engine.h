@@ -69,9 +69,6 @@ class Engine {
   // NH_E_ARG / NH_E_TYPE (nothing enqueued) where that kernel does not cover
   // the shapes.
   int EnqueueFusedMoe(const ModelView& m, int layer, bool norm_topk, bool trace, bool dumps);
-  // The whole layer (attention block and MoE block) in one cooperative
-  // kernel; NH_E_ARG / NH_E_TYPE (nothing enqueued) outside its shapes.
-  int EnqueueLayer(const ModelView& m, int layer, bool norm_topk, bool trace, bool dumps);
   // Phase B over expert weights at gate/up/down with per-slot selection wsel.
   int EnqueueMoePhase(const ModelView& m, int layer, const void* gate, int32_t tg, uint64_t gnb2,
                       const void* up, int32_t tu, uint64_t unb2, const void* down, int32_t td,
@@ -139,7 +136,6 @@ class Engine {
   void* attn_scratch_ = nullptr;
   void* router_scratch_ = nullptr;
   void* moe_scratch_ = nullptr;
-  void* layer_scratch_ = nullptr;
   void* argmax_scratch_ = nullptr;
   int32_t* trace_sel_ = nullptr;
   float* trace_gap_ = nullptr;

@@ -60,12 +60,16 @@ extern "C" void nh_rope_table(float base, int head_dim, int max_seq, float* cs) 
   }
 }
 
-extern "C" int nh_attention_step(const NhDecodeState* state, const float* q, const float* k, const float* v,
-                                 const float* q_norm, const float* k_norm, float eps, int n_head, int n_head_kv,
-                                 int head_dim, const float* rope_cs, float kq_scale, float* k_cache, float* v_cache,
-                                 int max_seq, void* scratch, float* attn_out, void* stream) {
+namespace {
+
+// The host-side checks shared by both attention entries (everything but the
+// scratch buffer); NH_OK when a launch may go ahead.
+int attention_args_ok(const NhDecodeState* state, const float* q, const float* k, const float* v,
+                      const float* q_norm, const float* k_norm, int n_head, int n_head_kv, int head_dim,
+                      const float* rope_cs, const float* k_cache, const float* v_cache, int max_seq,
+                      const float* attn_out) {
   if (state == nullptr || q == nullptr || k == nullptr || v == nullptr || q_norm == nullptr || k_norm == nullptr ||
-      rope_cs == nullptr || k_cache == nullptr || v_cache == nullptr || scratch == nullptr || attn_out == nullptr) {
+      rope_cs == nullptr || k_cache == nullptr || v_cache == nullptr || attn_out == nullptr) {
     return NH_E_ARG;
   }
   // Cache rows are copied whole with 16-byte bulk copies: head_dim*4 must be
@@ -75,6 +79,20 @@ extern "C" int nh_attention_step(const NhDecodeState* state, const float* q, con
       (reinterpret_cast<uintptr_t>(v_cache) & 15) != 0) {
     return NH_E_ARG;
   }
+  if (attn_smem_floats(head_dim, n_head, n_head_kv) * sizeof(float) > 220 * 1024) return NH_E_ARG;
+  return NH_OK;
+}
+
+}  // namespace
+
+extern "C" int nh_attention_step(const NhDecodeState* state, const float* q, const float* k, const float* v,
+                                 const float* q_norm, const float* k_norm, float eps, int n_head, int n_head_kv,
+                                 int head_dim, const float* rope_cs, float kq_scale, float* k_cache, float* v_cache,
+                                 int max_seq, void* scratch, float* attn_out, void* stream) {
+  const int rc = attention_args_ok(state, q, k, v, q_norm, k_norm, n_head, n_head_kv, head_dim, rope_cs, k_cache,
+                                   v_cache, max_seq, attn_out);
+  if (rc != NH_OK) return rc;
+  if (scratch == nullptr) return NH_E_ARG;
   AttnArgs p;
   p.state = const_cast<NhDecodeState*>(state);
   p.q = q;
@@ -103,8 +121,7 @@ extern "C" int nh_attention_step(const NhDecodeState* state, const float* q, con
   p.part_acc = reinterpret_cast<float*>(sc + off);
   p.out = attn_out;
   const size_t smem = attn_smem_floats(head_dim, n_head, n_head_kv) * sizeof(float);
-  if (smem > 220 * 1024) return NH_E_ARG;
-  static size_t configured = 48 * 1024;
+  static SmemLimit configured;
   if (!ensure_smem(attention_kernel, smem, configured)) return NH_E_CUDA;
   return launch_pdl(attention_kernel, dim3(n_head, p.n_split), dim3(kAttnThreads), smem,
                     static_cast<cudaStream_t>(stream), p);
@@ -121,7 +138,10 @@ extern "C" int nh_attention_step(const NhDecodeState* state, const float* q, con
 //
 // In host code `g_attn_static_scratch` names a host-side stand-in, not device
 // memory; the device address comes from cudaGetSymbolAddress, looked up once
-// per device (with that device current) on the first call made there and kept.
+// per device (with that device current) on the first call made there and kept
+// for the life of the process.  cudaDeviceReset on a device destroys the
+// context that address belongs to, so after a reset the kept address is stale:
+// a process that resets a device must not call this entry on it again.
 namespace {
 
 __device__ __align__(256) uint8_t g_attn_static_scratch[NH_ATTN_STATIC_SCRATCH_BYTES];
@@ -150,10 +170,16 @@ extern "C" int nh_attention_step_static(const NhDecodeState* state, const float*
                                         int n_head_kv, int head_dim, const float* rope_cs, float kq_scale,
                                         float* k_cache, float* v_cache, int max_seq, float* attn_out,
                                         void* stream) {
+  // Every check runs before anything is enqueued: a rejected call launches
+  // nothing and leaves the array untouched.  Capacity first (shapes only),
+  // then the arguments nh_attention_step itself checks.
   if (n_head <= 0 || n_head_kv <= 0 || head_dim <= 0 || max_seq <= 0) return NH_E_ARG;
   // The per-head split counters occupy the first 256 bytes: 4 bytes per head.
   if (n_head > 64) return NH_E_CAPACITY;
   if (nh_attention_scratch_bytes(n_head, head_dim, max_seq) > NH_ATTN_STATIC_SCRATCH_BYTES) return NH_E_CAPACITY;
+  const int rc = attention_args_ok(state, q, k, v, q_norm, k_norm, n_head, n_head_kv, head_dim, rope_cs, k_cache,
+                                   v_cache, max_seq, attn_out);
+  if (rc != NH_OK) return rc;
   void* scratch = static_scratch_address();
   if (scratch == nullptr) return NH_E_CUDA;
   // The array keeps whatever the previous call left; the counters must start

@@ -11,7 +11,6 @@
 #include <cstring>
 
 #include "launch.cuh"
-#include "cluster_prep.cuh"
 #include "gemv3.cuh"
 
 namespace nh {
@@ -176,8 +175,6 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv3_kernel(const GemvArg
   __shared__ float s_bv[32];
   __shared__ int s_bi[32];
   __shared__ bool s_last;
-  __shared__ double s_part[8];
-  cluster_arrive_relaxed();
 
   int pos = 0, n_prompt = 0;
   bool skip = false;
@@ -217,17 +214,16 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv3_kernel(const GemvArg
       const int j = gw + st * tw;
       if (j < p.jobs_total) issue(j, st);
     }
-    cluster_load_norm(a, p.norm_w);
+    act_load_norm(a, p.norm_w);
   }
   pdl_wait();
   pdl_trigger();
-  cluster_wait();
 
   float best_v = -INFINITY;
   int best_i = INT_MAX;
   bool failed = false;
   if (!skip) {
-    cluster_prep_act(a, p.x, p.norm_w != nullptr, p.do_norm != 0, p.eps, true, false, red, s_part);
+    prep_act(a, p.x, p.norm_w != nullptr, p.do_norm != 0, p.eps, true, red);
     const int g = lane % G, r = lane / G;
     // Most warps dot one or two jobs: the activation is read from shared
     // memory rather than held in registers.
@@ -311,7 +307,7 @@ bool valid_type(int t) { return t == NH_TYPE_F32 || t == NH_TYPE_Q4_K || t == NH
 
 template <int CPL>
 int gemv_launch_t(GemvArgs& p, size_t smem, int grid, cudaStream_t stream) {
-  static size_t configured = 48 * 1024;
+  static SmemLimit configured;
   if (!ensure_smem(gemv_kernel<CPL>, smem, configured)) return NH_E_CUDA;
   return launch_pdl(gemv_kernel<CPL>, dim3(grid), dim3(kGemvWarps * 32), smem, stream, p);
 }
@@ -334,7 +330,7 @@ int gemv3_launch(GemvArgs& p, cudaStream_t stream) {
   p.S = kGemvMaxStages;
   while (p.S > 1 && fixed + static_cast<size_t>(kGemvWarps) * p.S * (p.stage_bytes + 8) > 110 * 1024) --p.S;
   const size_t smem = fixed + kGemvWarps * p.S * sizeof(uint64_t) + static_cast<size_t>(kGemvWarps) * p.S * p.stage_bytes;
-  static size_t configured = 48 * 1024;
+  static SmemLimit configured;
   if (!ensure_smem(gemv3_kernel, smem, configured)) return NH_E_CUDA;
   const int per_sm = std::min(resident_ctas(gemv3_kernel, kGemvWarps * 32, smem), ctas_per_sm_cap());
   int grid = (total + kGemvWarps - 1) / kGemvWarps;
@@ -342,10 +338,7 @@ int gemv3_launch(GemvArgs& p, cudaStream_t stream) {
   if (grid > cap) grid = cap;
   if (p.argmax && grid > kMaxArgmaxBlocks) grid = kMaxArgmaxBlocks;
   if (grid < 1) grid = 1;
-  int cluster = prep_cluster_size(p.K, true);
-  while (cluster > grid) cluster >>= 1;
-  grid = round_grid(grid, cluster);
-  return launch_pdl_cluster(gemv3_kernel, dim3(grid), dim3(kGemvWarps * 32), smem, stream, cluster, p);
+  return launch_pdl(gemv3_kernel, dim3(grid), dim3(kGemvWarps * 32), smem, stream, p);
 }
 
 int gemv_launch(GemvArgs& p, cudaStream_t stream) {

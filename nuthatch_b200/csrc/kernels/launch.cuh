@@ -3,7 +3,9 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdlib>
+#include <mutex>
 #include <utility>
 
 #include "../../../include/nh_kernels.h"
@@ -70,34 +72,31 @@ inline bool batch_mma_enabled() {
   return v != 0;
 }
 
-// Thread-block clusters that share the activation preparation are used only
-// when NH_CLUSTER=1 (read once).  Measured on B200 they cost more in cluster
-// barriers and scheduling than the shared preparation saves, so the default
-// is one CTA per cluster.
-inline bool clusters_enabled() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = std::getenv("NH_CLUSTER");
-    v = (e != nullptr && e[0] == '1') ? 1 : 0;
+// The dynamic shared-memory limit one kernel has been given on each device.
+// cudaFuncSetAttribute acts on the current device only, so a process that
+// drives several GPUs needs one record per device.  Reads are lock-free; the
+// rare raise is serialised so the attribute only ever grows and the record
+// never claims more than was set.
+struct SmemLimit {
+  static constexpr int kMaxDevices = 64;
+  std::atomic<size_t> limit[kMaxDevices];
+  std::mutex raise;
+  SmemLimit() {
+    for (auto& l : limit) l.store(48 * 1024, std::memory_order_relaxed);
   }
-  return v != 0;
-}
-
-// Largest cluster size C <= 8 (a power of two) with K % (4*C) == 0 and, when
-// the activation is quantised, (K/256) % C == 0; 1 when clusters are off.
-inline int prep_cluster_size(int K, bool quant) {
-  if (!clusters_enabled()) return 1;
-  int c = 8;
-  while (c > 1 && (K % (4 * c) != 0 || (quant && (K / 256) % c != 0))) c >>= 1;
-  return c;
-}
+};
 
 template <typename Kern>
-bool ensure_smem(Kern k, size_t bytes, size_t& configured) {
-  if (bytes <= configured) return true;
+bool ensure_smem(Kern k, size_t bytes, SmemLimit& rec) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= SmemLimit::kMaxDevices) return false;
+  std::atomic<size_t>& cur = rec.limit[dev];
+  if (bytes <= cur.load(std::memory_order_acquire)) return true;
+  std::lock_guard<std::mutex> hold(rec.raise);
+  if (bytes <= cur.load(std::memory_order_relaxed)) return true;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)) != cudaSuccess)
     return false;
-  configured = bytes;
+  cur.store(bytes, std::memory_order_release);
   return true;
 }
 
@@ -120,36 +119,13 @@ int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaS
   return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...) == cudaSuccess ? NH_OK : NH_E_CUDA;
 }
 
-// launch_pdl with a 1-D thread-block cluster of `cluster` CTAs (grid.x must
-// be a multiple of it).
-template <typename... KArgs, typename... Args>
-int launch_pdl_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, int cluster,
-                       Args&&... args) {
-  if (cluster <= 1) return launch_pdl(kern, grid, block, smem, s, std::forward<Args>(args)...);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute at[2];
-  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  at[0].val.programmaticStreamSerializationAllowed = pdl_enabled();
-  at[1].id = cudaLaunchAttributeClusterDimension;
-  at[1].val.clusterDim.x = static_cast<unsigned>(cluster);
-  at[1].val.clusterDim.y = 1;
-  at[1].val.clusterDim.z = 1;
-  cfg.attrs = at;
-  cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...) == cudaSuccess ? NH_OK : NH_E_CUDA;
-}
-
 // Cooperative launch: the runtime admits the grid only if every CTA can be
 // resident at once, so CTAs may wait for one another.  Programmatic dependent
 // launch is requested too; should the runtime refuse the pair, the launch is
 // repeated without it and the pair is not tried again.
 template <typename... KArgs, typename... Args>
 int launch_coop(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
-  static bool pair_ok = true;
+  static std::atomic<bool> pair_ok{true};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -161,20 +137,14 @@ int launch_coop(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cuda
   at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at[1].val.programmaticStreamSerializationAllowed = pdl_enabled();
   cfg.attrs = at;
-  cfg.numAttrs = pair_ok ? 2 : 1;
+  const bool pair = pair_ok.load(std::memory_order_relaxed);
+  cfg.numAttrs = pair ? 2 : 1;
   if (cudaLaunchKernelEx(&cfg, kern, args...) == cudaSuccess) return NH_OK;
-  if (!pair_ok) return NH_E_CUDA;
+  if (!pair) return NH_E_CUDA;
   (void)cudaGetLastError();
-  pair_ok = false;
+  pair_ok.store(false, std::memory_order_relaxed);
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, args...) == cudaSuccess ? NH_OK : NH_E_CUDA;
-}
-
-// Rounds a grid down to a multiple of the cluster size (at least one cluster).
-inline int round_grid(int grid, int cluster) {
-  if (cluster <= 1) return grid;
-  const int g = grid / cluster * cluster;
-  return g < cluster ? cluster : g;
 }
 
 }  // namespace nh

@@ -111,7 +111,7 @@ extern "C" int nh_embed_step(const NhDecodeState* state, const int32_t* prompt_i
   if (type != NH_TYPE_F32 && type != NH_TYPE_Q4_K && type != NH_TYPE_Q6_K) return NH_E_TYPE;
   if (type != NH_TYPE_F32 && n_embd % QK != 0) return NH_E_ARG;
   const size_t smem = row_bytes(type, n_embd) + 32;
-  static size_t configured = 48 * 1024;
+  static SmemLimit configured;
   if (smem > 220 * 1024 || !ensure_smem(embed_kernel, smem, configured)) return NH_E_ARG;
   return launch_pdl(embed_kernel, dim3(1), dim3(256), smem, static_cast<cudaStream_t>(stream), state, prompt_ids,
                     static_cast<const uint8_t*>(table), static_cast<int>(type), n_embd, n_vocab,

@@ -15,7 +15,6 @@
 
 #include "launch.cuh"
 #include "attention.cuh"
-#include "cluster_prep.cuh"
 #include "gemv3.cuh"
 #include "rowdot3.cuh"
 
@@ -189,20 +188,17 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(const RouterA
   extern __shared__ __align__(128) uint8_t smem[];
   ActSmem a = carve_act(smem, p.K, true, true);
   __shared__ double red[48];
-  __shared__ double s_part[8];
   __shared__ bool s_last;
-  cluster_arrive_relaxed();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e = blockIdx.x * kRouterWarps + warp;
   // The router weights do not depend on the preceding kernel: load the row
   // before waiting for it.
   float4 wv[kRouterMaxVec];
   router_load_row(p, wv, e, lane);
-  cluster_load_norm(a, p.norm);
+  act_load_norm(a, p.norm);
   pdl_wait();
   pdl_trigger();
-  cluster_wait();
-  cluster_prep_act(a, p.h, p.norm != nullptr, true, p.eps, false, true, red, s_part);
+  prep_act(a, p.h, p.norm != nullptr, true, p.eps, false, red);
   if (e < p.E) {
     const float v = router_logit(p, wv, a, e, lane);
     if (lane == 0) p.logits[e] = v;
@@ -600,8 +596,6 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) gate_up3_kernel(const GateU
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + act_bytes + 48 * sizeof(double));
   uint8_t* stage = reinterpret_cast<uint8_t*>(bars + kMoeWarps * p.S);
   __shared__ int s_sel[kMaxTopK];
-  __shared__ double s_part[8];
-  cluster_arrive_relaxed();
   const int gw = blockIdx.x * kMoeWarps + warp, tw = gridDim.x * kMoeWarps;
   uint64_t* wbar = bars + warp * p.S;
   uint8_t* wb = stage + static_cast<size_t>(warp) * p.S * p.stage_bytes;
@@ -609,7 +603,7 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) gate_up3_kernel(const GateU
     for (int s = 0; s < p.S; ++s) mbar_init(&wbar[s], 1);
     fence_barrier_init();
   }
-  cluster_load_norm(a, p.norm);
+  act_load_norm(a, p.norm);
   pdl_wait();
   pdl_trigger();
   // The selection is read once; every job then finds its expert in shared memory.
@@ -620,8 +614,7 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) gate_up3_kernel(const GateU
     if (j < p.jobs_total) gu3_issue(p, s_sel, wbar, wb, j, st, lane);
   }
   gu3_prefetch_down(p, s_sel, warp, lane);
-  cluster_wait();
-  cluster_prep_act(a, p.h, p.norm != nullptr, true, p.eps, true, false, red, s_part);
+  prep_act(a, p.h, p.norm != nullptr, true, p.eps, true, red);
   const bool ok = gu3_run(p, s_sel, wbar, wb, Act3Smem{a, lane % p.lpr}, gw, tw, lane);
   if (!ok && lane == 0 && p.state != nullptr) atomicCAS(&p.state->error, 0, NH_E_TIMEOUT);
 }
@@ -699,8 +692,6 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) down3_kernel(const DownArgs
   __shared__ int s_sel[kMaxTopK];
   __shared__ float s_wts[kMaxTopK];
   __shared__ double red[40];
-  __shared__ double s_part[8];
-  cluster_arrive_relaxed();
   const int gw = blockIdx.x * kMoeWarps + warp, tw = gridDim.x * kMoeWarps;
   uint64_t* wbar = bars + warp * p.S;
   uint8_t* wb = stage + static_cast<size_t>(warp) * p.S * p.stage_bytes;
@@ -719,10 +710,8 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) down3_kernel(const DownArgs
     const int j = gw + st * tw;
     if (j < p.jobs_total) dn3_issue(p, s_sel, wbar, wb, j, st, lane);
   }
-  // The activation: the k experts' ff rows, Q8_K-quantised per 256-block,
-  // each CTA of the cluster quantising its share.
-  cluster_wait();
-  cluster_prep_act(a, p.ff, false, false, 0.f, true, false, red, s_part);
+  // The activation: the k experts' ff rows, Q8_K-quantised per 256-block.
+  prep_act(a, p.ff, false, false, 0.f, true, red);
   const bool ok = dn3_run(p, s_sel, s_wts, wbar, wb, a, gw, tw, lane, p.state->pos, p.state->n_prompt, false, 0.f);
   if (!ok && lane == 0) atomicCAS(&p.state->error, 0, NH_E_TIMEOUT);
 }
@@ -1003,198 +992,15 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) moe_fused_kernel(const __gr
   }
 }
 
-// ------------------------------------------------------------------ whole layer
-// One decoder layer in one cooperative grid: QKV projections, attention,
-// output projection + residual, and the MoE block (moe_run), the phases
-// separated by grid barriers instead of kernel boundaries.  Work that needs
-// nothing from this layer starts before the preceding kernel ends: the QKV
-// weight rows (warps [0, qkv jobs)), the cached K/V rows of the first
-// attention item (CTAs [attn_cta0, attn_cta0 + attn_ctas), whose staging
-// regions are otherwise idle) and the router rows (the last router_ctas
-// CTAs).  The out_proj rows are staged as soon as a warp has consumed its
-// QKV rows.  The arithmetic of every phase is that of its standalone kernel.
-struct LayerArgs {
-  GemvArgs qkv;   // segments q, k, v; x = h, norm_w = attn_norm
-  AttnArgs attn;
-  GemvArgs out;   // segment o, resid = out = h; x = attention output
-  FusedArgs moe;  // sync[1] ff barrier
-  unsigned* lsync;  // [0] q/k/v written, [1] attention written, [2] h written, [3] exits
-  int qkv_ctas, out_ctas, attn_cta0, attn_ctas, router_cta0;
-  uint32_t attn_off;  // offset of the attention items' shared memory (the staging regions)
-};
-
-// Block-wide grid barrier on counter c: the writes of every CTA before it
-// are visible to every CTA after it (release add / acquire poll).
-__device__ __forceinline__ bool grid_sync(unsigned* c, int* s_flag) {
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    red_release_gpu(c, 1u);
-    *s_flag = wait_count(c, gridDim.x);
-  }
-  __syncthreads();
-  return *s_flag != 0;
-}
-
-// Values are re-derived inside each phase from the kernel parameters and the
-// shared-memory base rather than held across phases: the attention phase
-// needs most of the register file.
-__device__ __forceinline__ uint64_t* layer_qbar(const LayerArgs& L, uint8_t* smem, int warp) {
-  const FusedArgs& p = L.moe;
-  return reinterpret_cast<uint64_t*>(smem + p.act_bytes + 48 * sizeof(double)) +
-         kMoeWarps * (p.g.S + p.d.S + 1) + warp * L.qkv.S;
-}
-__device__ __forceinline__ uint64_t* layer_obar(const LayerArgs& L, uint8_t* smem, int warp) {
-  const FusedArgs& p = L.moe;
-  return reinterpret_cast<uint64_t*>(smem + p.act_bytes + 48 * sizeof(double)) +
-         kMoeWarps * (p.g.S + p.d.S + 1 + L.qkv.S) + warp * L.out.S;
-}
-__device__ __forceinline__ int layer_router_e(const LayerArgs& L) {
-  const int cta = blockIdx.x, e = (cta - L.router_cta0) * kMoeWarps + (threadIdx.x >> 5);
-  return cta >= L.router_cta0 && cta < L.router_cta0 + L.moe.router_ctas && e < L.moe.r.E ? e : -1;
-}
-
-// Attention items first, first + attn_ctas, ... < n_items of this CTA.
-__device__ __noinline__ void layer_attention_more(const LayerArgs& L, uint8_t* smem, AttnShared& ash, int pos,
-                                                  int first, int n_items) {
-  const int H = L.attn.n_head;
-  const AttnSmem am = carve_attn(reinterpret_cast<float*>(smem + L.attn_off), L.attn.hd, H);
-  for (int it = first; it < n_items; it += L.attn_ctas) {
-    attn_begin(L.attn, it % H, it / H, pos, am, ash);
-    attn_finish(L.attn, it % H, it / H, pos, am, ash);
-  }
-}
-
-__global__ void __launch_bounds__(kMoeWarps * 32, 2) layer_kernel(const __grid_constant__ LayerArgs L) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ MoeShared sh;
-  __shared__ AttnShared ash;
-  __shared__ int s_flag;
-  const FusedArgs& p = L.moe;
-  const int cta = blockIdx.x;
-  const int lane = threadIdx.x & 31;
-  // The cursor was last written by the previous token's argmax, which
-  // completed before this kernel could launch.
-  if (threadIdx.x == 0) {
-    sh.pos = *reinterpret_cast<volatile const int*>(&p.d.state->pos);
-    sh.np = *reinterpret_cast<volatile const int*>(&p.d.state->n_prompt);
-    // The previous launch's last CTA advanced the epoch before it exited.
-    sh.tag = *reinterpret_cast<volatile unsigned*>(p.epoch) + 1u;
-  }
-  {
-    const int warp = threadIdx.x >> 5;
-    const MoeWarp w = moe_warp(p, smem, warp, L.qkv.S + L.out.S);
-    uint64_t* qbar = layer_qbar(L, smem, warp);
-    if (lane == 0) {
-      moe_init_warp(p, w);
-      uint64_t* obar = layer_obar(L, smem, warp);
-      for (int s = 0; s < L.qkv.S; ++s) mbar_init(&qbar[s], 1);
-      for (int s = 0; s < L.out.S; ++s) mbar_init(&obar[s], 1);
-      fence_barrier_init();
-      const int re = layer_router_e(L);
-      if (re >= 0) moe_stage_router_row(p, w, re);
-    }
-    __syncwarp();
-    if (cta < L.qkv_ctas) {
-      const int gw = cta * kMoeWarps + warp, tw = gridDim.x * kMoeWarps;
-      for (int st = 0; st < L.qkv.S; ++st) {
-        const int j = gw + st * tw;
-        if (j < L.qkv.jobs_total) g3_issue(L.qkv, qbar, w.wb, j, st, lane);
-      }
-      ActSmem a = carve_act(smem, L.qkv.K, true, true);
-      act_load_norm(a, L.qkv.norm_w);
-    }
-  }
-  __syncthreads();  // sh.pos
-  if (cta >= L.attn_cta0 && cta < L.attn_cta0 + L.attn_ctas) {
-    const int pos = sh.pos, H = L.attn.n_head;
-    const int item0 = cta - L.attn_cta0;
-    if (item0 < H * ((pos + kAttnSplit) / kAttnSplit))
-      attn_begin(L.attn, item0 % H, item0 / H, pos,
-                 carve_attn(reinterpret_cast<float*>(smem + L.attn_off), L.attn.hd, H), ash);
-  }
-  pdl_wait();
-  pdl_trigger();
-  bool ok = true;
-  // Phase A: q, k, v; then this warp's out_proj rows into its freed region.
-  {
-    const int warp = threadIdx.x >> 5;
-    const int gw = cta * kMoeWarps + warp, tw = gridDim.x * kMoeWarps;
-    const MoeWarp w = moe_warp(p, smem, warp, L.qkv.S + L.out.S);
-    if (cta < L.qkv_ctas) {
-      ActSmem a = carve_act(smem, L.qkv.K, true, true);
-      double* red = reinterpret_cast<double*>(smem + p.act_bytes);
-      prep_act<true>(a, L.qkv.x, L.qkv.norm_w != nullptr, true, L.qkv.eps, true, red);
-      ok = g3_run(L.qkv, layer_qbar(L, smem, warp), w.wb, Act3Smem{a, lane % L.qkv.lpr}, gw, tw, lane);
-    }
-    if (ok && cta < L.out_ctas) {
-      uint64_t* obar = layer_obar(L, smem, warp);
-      for (int st = 0; st < L.out.S; ++st) {
-        const int j = gw + st * tw;
-        if (j < L.out.jobs_total) g3_issue(L.out, obar, w.wb, j, st, lane);
-      }
-    }
-  }
-  ok = grid_sync(&L.lsync[0], &s_flag) && ok;
-  // Phase B: attention items: the first inline, any further ones (contexts
-  // longer than the attention CTAs cover at once) in a called function (an
-  // item loop here would crowd the whole kernel's registers).
-  if (cta >= L.attn_cta0 && cta < L.attn_cta0 + L.attn_ctas) {
-    const int pos = sh.pos, H = L.attn.n_head;
-    const int item0 = cta - L.attn_cta0;
-    const int n_items = H * ((pos + kAttnSplit) / kAttnSplit);
-    if (item0 < n_items)
-      attn_finish(L.attn, item0 % H, item0 / H, pos,
-                  carve_attn(reinterpret_cast<float*>(smem + L.attn_off), L.attn.hd, H), ash);
-    if (item0 + L.attn_ctas < n_items) layer_attention_more(L, smem, ash, pos, item0 + L.attn_ctas, n_items);
-  }
-  ok = grid_sync(&L.lsync[1], &s_flag) && ok;
-  // Phase C: output projection + residual.
-  if (cta < L.out_ctas) {
-    const int warp = threadIdx.x >> 5;
-    const int gw = cta * kMoeWarps + warp, tw = gridDim.x * kMoeWarps;
-    const MoeWarp w = moe_warp(p, smem, warp, L.qkv.S + L.out.S);
-    ActSmem ao = carve_act(smem, L.out.K, true, false);
-    double* red = reinterpret_cast<double*>(smem + p.act_bytes);
-    prep_act<true>(ao, L.out.x, false, false, 0.f, true, red);
-    ok = g3_run(L.out, layer_obar(L, smem, warp), w.wb, Act3Smem{ao, lane % L.out.lpr}, gw, tw, lane) && ok;
-  }
-  ok = grid_sync(&L.lsync[2], &s_flag) && ok;
-  // Phase D: the MoE block.
-  {
-    const int warp = threadIdx.x >> 5;
-    ActSmem a = carve_act(smem, p.g.K, true, true);
-    act_load_norm(a, p.g.norm);
-    const int re = layer_router_e(L);
-    const bool router_cta = cta >= L.router_cta0 && cta < L.router_cta0 + p.router_ctas;
-    ok = moe_run(p, smem, moe_warp(p, smem, warp, L.qkv.S + L.out.S), router_cta, re, sh,
-                 reinterpret_cast<double*>(smem + p.act_bytes)) &&
-         ok;
-  }
-  if (!ok && lane == 0) atomicCAS(&p.d.state->error, 0, NH_E_TIMEOUT);
-  __syncthreads();
-  if (threadIdx.x == 0 && atomicAdd(&L.lsync[3], 1u) == gridDim.x - 1) {
-    *p.epoch = sh.tag;
-    p.sync[1] = 0u;
-    L.lsync[0] = 0u;
-    L.lsync[1] = 0u;
-    L.lsync[2] = 0u;
-    L.lsync[3] = 0u;
-    __threadfence();
-  }
-}
-
 }  // namespace nh
 
 using namespace nh;
 
 namespace {
 int launch_router(const RouterArgs& p, size_t smem, int grid, cudaStream_t st) {
-  static size_t configured = 48 * 1024;
+  static SmemLimit configured;
   if (!ensure_smem(router_kernel, smem, configured)) return NH_E_CUDA;
-  // One cluster shares the preparation when the grid is a power of two <= 8.
-  int cluster = prep_cluster_size(p.K, false);
-  while (cluster > 1 && grid % cluster != 0) cluster >>= 1;
-  return launch_pdl_cluster(router_kernel, dim3(grid), dim3(kRouterWarps * 32), smem, st, cluster, p);
+  return launch_pdl(router_kernel, dim3(grid), dim3(kRouterWarps * 32), smem, st, p);
 }
 }  // namespace
 
@@ -1237,14 +1043,14 @@ namespace {
 
 template <int CPL>
 int launch_gate_up(const GateUpArgs& p, size_t smem, int grid, cudaStream_t s) {
-  static size_t configured = 48 * 1024;
+  static SmemLimit configured;
   if (!ensure_smem(gate_up_kernel<CPL>, smem, configured)) return NH_E_CUDA;
   return launch_pdl(gate_up_kernel<CPL>, dim3(grid), dim3(kMoeWarps * 32), smem, s, p);
 }
 
 template <int CPL>
 int launch_down(const DownArgs& p, size_t smem, int grid, cudaStream_t s) {
-  static size_t configured = 48 * 1024;
+  static SmemLimit configured;
   if (!ensure_smem(down_kernel<CPL>, smem, configured)) return NH_E_CUDA;
   return launch_pdl(down_kernel<CPL>, dim3(grid), dim3(kMoeWarps * 32), smem, s, p);
 }
@@ -1290,23 +1096,17 @@ int pick_stages3(size_t fixed, uint32_t stage_bytes, int jobs) {
 }
 
 int launch_gate_up3(const GateUpArgs& p, size_t smem, cudaStream_t st) {
-  static size_t configured = 48 * 1024;
+  static SmemLimit configured;
   if (!ensure_smem(gate_up3_kernel, smem, configured)) return NH_E_CUDA;
-  int grid = grid_resident(gate_up3_kernel, p.jobs_total, smem);
-  int cluster = prep_cluster_size(p.K, true);
-  while (cluster > grid) cluster >>= 1;
-  grid = round_grid(grid, cluster);
-  return launch_pdl_cluster(gate_up3_kernel, dim3(grid), dim3(kMoeWarps * 32), smem, st, cluster, p);
+  const int grid = grid_resident(gate_up3_kernel, p.jobs_total, smem);
+  return launch_pdl(gate_up3_kernel, dim3(grid), dim3(kMoeWarps * 32), smem, st, p);
 }
 
 int launch_down3(const DownArgs& p, size_t smem, cudaStream_t st) {
-  static size_t configured = 48 * 1024;
+  static SmemLimit configured;
   if (!ensure_smem(down3_kernel, smem, configured)) return NH_E_CUDA;
-  int grid = grid_resident(down3_kernel, p.jobs_total, smem);
-  int cluster = prep_cluster_size(p.topk * p.F, true);
-  while (cluster > grid) cluster >>= 1;
-  grid = round_grid(grid, cluster);
-  return launch_pdl_cluster(down3_kernel, dim3(grid), dim3(kMoeWarps * 32), smem, st, cluster, p);
+  const int grid = grid_resident(down3_kernel, p.jobs_total, smem);
+  return launch_pdl(down3_kernel, dim3(grid), dim3(kMoeWarps * 32), smem, st, p);
 }
 
 bool aligned16(const void* p, uint64_t stride) {
@@ -1537,7 +1337,7 @@ int launch_fused(FusedArgs& p, cudaStream_t st) {
   p.region_bytes = region();
   const size_t smem = total();
   if (smem > 220 * 1024) return NH_E_ARG;
-  static size_t configured = 48 * 1024;
+  static SmemLimit configured;
   if (!ensure_smem(moe_fused_kernel, smem, configured)) return NH_E_CUDA;
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, moe_fused_kernel, kMoeWarps * 32, smem) !=
@@ -1637,191 +1437,3 @@ extern "C" int nh_moe_layer(const NhMoeLayer* L, void* stream) {
   return launch_fused(p, st);
 }
 
-extern "C" int64_t nh_layer_scratch_bytes(int n_expert) { return 64 + 8 * static_cast<int64_t>(n_expert) + 64; }
-
-extern "C" int nh_layer_step(const NhLayerStep* S, void* stream) {
-  if (S == nullptr || S->scratch == nullptr || S->attn_norm == nullptr || S->wq == nullptr || S->wk == nullptr ||
-      S->wv == nullptr || S->wo == nullptr || S->q == nullptr || S->k == nullptr || S->v == nullptr ||
-      S->q_norm == nullptr || S->k_norm == nullptr || S->rope_cs == nullptr || S->k_cache == nullptr ||
-      S->v_cache == nullptr || S->attn_scratch == nullptr || S->attn_out == nullptr)
-    return NH_E_ARG;
-  const NhMoeLayer* M = &S->moe;
-  if (M->state == nullptr || M->h == nullptr || M->router == nullptr || M->gate == nullptr || M->up == nullptr ||
-      M->down == nullptr || M->sel == nullptr || M->wts == nullptr || M->ff == nullptr)
-    return NH_E_ARG;
-  const int E = M->n_expert, k = M->k;
-  if (E <= 0 || E > kMaxExperts || k <= 0 || k > kMaxTopK || k > E) return NH_E_ARG;
-  if (M->n_embd <= 0 || M->n_embd > kMaxK || M->n_ff <= 0 || M->n_ff > kMaxK) return NH_E_ARG;
-  for (int t : {M->tg, M->tu, M->td, S->tq, S->tk, S->tv, S->to})
-    if (t != NH_TYPE_Q4_K && t != NH_TYPE_Q6_K) return NH_E_TYPE;
-  const int K = static_cast<int>(M->n_embd), F = static_cast<int>(M->n_ff);
-  const int H = S->n_head, Hkv = S->n_head_kv, hd = S->head_dim;
-  if (H <= 0 || Hkv <= 0 || H % Hkv != 0 || hd <= 0 || hd % 32 != 0 || hd > 256 || S->max_seq <= 0) return NH_E_ARG;
-  const int dq = H * hd, dkv = Hkv * hd;
-  if (!engine_v3() || !rowdot3_k_ok(K) || !rowdot3_k_ok(dq) || !down3_ok(F, k) ||
-      static_cast<int64_t>(k) * F > 4 * kMaxK)
-    return NH_E_ARG;
-  if ((reinterpret_cast<uintptr_t>(M->router) & 15) != 0 || (reinterpret_cast<uintptr_t>(S->k_cache) & 15) != 0 ||
-      (reinterpret_cast<uintptr_t>(S->v_cache) & 15) != 0)
-    return NH_E_ARG;
-  if ((M->tg == NH_TYPE_Q4_K && !aligned16(M->gate, M->gate_nb2)) ||
-      (M->tu == NH_TYPE_Q4_K && !aligned16(M->up, M->up_nb2)) ||
-      (M->td == NH_TYPE_Q4_K && !aligned16(M->down, M->down_nb2)))
-    return NH_E_ARG;
-  for (const auto& wt : {std::make_pair(S->wq, S->tq), std::make_pair(S->wk, S->tk), std::make_pair(S->wv, S->tv),
-                         std::make_pair(S->wo, S->to)})
-    if (wt.second == NH_TYPE_Q4_K && (reinterpret_cast<uintptr_t>(wt.first) & 15) != 0) return NH_E_ARG;
-
-  LayerArgs L;
-  memset(&L, 0, sizeof(L));
-  // The MoE block, as nh_moe_layer sets it up.
-  FusedArgs& p = L.moe;
-  RouterArgs& r = p.r;
-  r.state = M->state;
-  r.h = M->h;
-  r.norm = M->ffn_norm;
-  r.eps = M->eps;
-  r.router = M->router;
-  r.K = K;
-  r.E = E;
-  r.topk = k;
-  r.norm_topk = M->norm_topk;
-  r.layer = M->layer;
-  r.n_layers = M->n_layers;
-  r.sel = M->sel;
-  r.wts = M->wts;
-  r.trace_sel = M->trace_sel;
-  r.trace_gap = M->trace_gap;
-  unsigned* counters = static_cast<unsigned*>(S->scratch);
-  r.ticket = counters;
-  r.logits = nullptr;
-  p.tagged = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(S->scratch) + 64);
-  p.epoch = counters + 15;
-  p.sync = counters + 1;   // [1] ff barrier
-  L.lsync = counters + 4;  // [0..2] phase barriers, [3] exits
-  p.router_ctas = (E + kMoeWarps - 1) / kMoeWarps;
-  GateUpArgs& g = p.g;
-  g.state = M->state;
-  g.h = M->h;
-  g.norm = M->ffn_norm;
-  g.eps = M->eps;
-  g.wsel = M->sel;
-  g.topk = k;
-  g.gate = static_cast<const uint8_t*>(M->gate);
-  g.up = static_cast<const uint8_t*>(M->up);
-  g.tg = M->tg;
-  g.tu = M->tu;
-  g.gate_nb2 = M->gate_nb2;
-  g.up_nb2 = M->up_nb2;
-  g.K = K;
-  g.F = F;
-  g.rb_g = row_bytes(g.tg, K);
-  g.rb_u = row_bytes(g.tu, K);
-  g.ff = M->ff;
-  shape_gate_up3(g);
-  DownArgs& d = p.d;
-  d.state = M->state;
-  d.ff = M->ff;
-  d.wsel = M->sel;
-  d.wts = M->wts;
-  d.topk = k;
-  d.down = static_cast<const uint8_t*>(M->down);
-  d.td = M->td;
-  d.nb2 = M->down_nb2;
-  d.rb = row_bytes(d.td, F);
-  d.F = F;
-  d.D = K;
-  d.h = M->h;
-  d.dump = M->dump;
-  d.dump_stride = M->dump_step_stride;
-  d.dump_off = M->dump_offset;
-  shape_down3(d);
-  // QKV and output projection.
-  GemvArgs& q = L.qkv;
-  q.nseg = 3;
-  q.K = K;
-  q.seg[0] = {static_cast<const uint8_t*>(S->wq), S->q, nullptr, static_cast<int32_t>(dq), S->tq, 0};
-  q.seg[1] = {static_cast<const uint8_t*>(S->wk), S->k, nullptr, static_cast<int32_t>(dkv), S->tk, 0};
-  q.seg[2] = {static_cast<const uint8_t*>(S->wv), S->v, nullptr, static_cast<int32_t>(dkv), S->tv, 0};
-  q.state = M->state;
-  q.x = M->h;
-  q.norm_w = S->attn_norm;
-  q.eps = M->eps;
-  q.do_norm = 1;
-  gemv3_shape(q);
-  q.S = 1;
-  GemvArgs& o = L.out;
-  o.nseg = 1;
-  o.K = dq;
-  o.seg[0] = {static_cast<const uint8_t*>(S->wo), M->h, M->h, static_cast<int32_t>(K), S->to, 0};
-  o.state = M->state;
-  o.x = S->attn_out;
-  gemv3_shape(o);
-  o.S = 1;
-  // Attention, as nh_attention_step sets it up.
-  AttnArgs& at = L.attn;
-  at.state = M->state;
-  at.q = S->q;
-  at.k = S->k;
-  at.v = S->v;
-  at.q_norm = S->q_norm;
-  at.k_norm = S->k_norm;
-  at.eps = M->eps;
-  at.n_head = H;
-  at.n_head_kv = Hkv;
-  at.hd = hd;
-  at.rope_cs = S->rope_cs;
-  at.kq_scale = S->kq_scale;
-  at.k_cache = S->k_cache;
-  at.v_cache = S->v_cache;
-  at.n_split = attn_splits(S->max_seq);
-  {
-    uint8_t* sc = static_cast<uint8_t*>(S->attn_scratch);
-    at.tickets = reinterpret_cast<unsigned*>(sc);
-    const int64_t slots = static_cast<int64_t>(H) * at.n_split;
-    int64_t off = 256;
-    at.part_l = reinterpret_cast<double*>(sc + off);
-    off += slots * 8;
-    at.part_m = reinterpret_cast<float*>(sc + off);
-    off += slots * 4;
-    off = (off + 15) & ~15ll;
-    at.part_acc = reinterpret_cast<float*>(sc + off);
-  }
-  at.out = S->attn_out;
-
-  // Grid and roles: two CTAs per SM; QKV jobs on the first CTAs (one job per
-  // warp), out_proj jobs on the first of those, the router rows on the last
-  // CTAs and the attention items on the CTAs in between.
-  const int grid = 2 * device_sm_count();
-  const int warps = grid * kMoeWarps;
-  if (q.jobs_total > warps || o.jobs_total > warps) return NH_E_ARG;
-  L.qkv_ctas = (q.jobs_total + kMoeWarps - 1) / kMoeWarps;
-  L.out_ctas = (o.jobs_total + kMoeWarps - 1) / kMoeWarps;
-  L.router_cta0 = grid - p.router_ctas;
-  L.attn_cta0 = std::max(L.qkv_ctas, L.out_ctas);
-  L.attn_ctas = L.router_cta0 - L.attn_cta0;
-  if (L.attn_ctas < 1) return NH_E_ARG;
-  p.g.S = std::min(kMoeMaxStages, std::max(1, (g.jobs_total + warps - 1) / warps));
-  p.d.S = std::min(kMoeMaxStages, std::max(1, (d.jobs_total + warps - 1) / warps));
-  p.act_bytes = static_cast<uint32_t>(
-      (std::max({act_smem_bytes(K, true, true), act_smem_bytes(dq, true, false), act_smem_bytes(k * F, false)}) +
-       15) &
-      ~static_cast<size_t>(15));
-  const uint64_t region = std::max({static_cast<uint64_t>(p.g.S) * g.stage_bytes,
-                                    static_cast<uint64_t>(p.d.S) * d.stage_bytes, static_cast<uint64_t>(q.stage_bytes),
-                                    static_cast<uint64_t>(o.stage_bytes), static_cast<uint64_t>(K) * 4});
-  p.region_bytes = static_cast<uint32_t>((region + 127) & ~127ull);
-  const size_t regions_base =
-      p.act_bytes + 48 * sizeof(double) + kMoeWarps * (p.g.S + p.d.S + 1 + q.S + o.S) * sizeof(uint64_t);
-  L.attn_off = static_cast<uint32_t>(regions_base);
-  const size_t smem = std::max(regions_base + static_cast<size_t>(kMoeWarps) * p.region_bytes,
-                               regions_base + attn_smem_floats(hd, H, Hkv) * sizeof(float));
-  if (smem > 220 * 1024) return NH_E_ARG;
-  static size_t configured = 48 * 1024;
-  if (!ensure_smem(layer_kernel, smem, configured)) return NH_E_CUDA;
-  int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, layer_kernel, kMoeWarps * 32, smem) != cudaSuccess ||
-      per_sm < 2)
-    return NH_E_ARG;
-  return launch_coop(layer_kernel, dim3(grid), dim3(kMoeWarps * 32), smem, static_cast<cudaStream_t>(stream), L);
-}

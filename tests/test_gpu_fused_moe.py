@@ -1,11 +1,9 @@
-"""The fused forms of resident decode against the separate kernels they
-replace: the whole-layer cooperative kernel (nh_layer_step: QKV, attention,
-output projection and the MoE block in one grid), the MoE-block kernel
-(nh_moe_layer: router, gate/up and down in one grid) and the six separate
-kernels per layer.  Greedy ids, per-layer hidden states, logits and routing
-records are identical bit for bit across the three, with CUDA graphs and
-eagerly.  Each form runs in its own process (NH_FUSED_LAYER / NH_FUSED_MOE are
-read once per process)."""
+"""The fused form of resident decode against the separate kernels it
+replaces: the MoE-block kernel (nh_moe_layer: router, gate/up and down in one
+grid) and the six separate kernels per layer.  Greedy ids, per-layer hidden
+states, logits and routing records are identical bit for bit across the two,
+with CUDA graphs and eagerly.  Each form runs in its own process
+(NH_FUSED_MOE is read once per process)."""
 from __future__ import annotations
 
 import os
@@ -37,8 +35,7 @@ np.savez(out, tokens=np.array(g["tokens"]), hidden=g["hidden"], logits=g["logits
          launches=np.array(lib().nh_generate_launches(m._h)))
 """
 
-FORMS = {"layer": {"NH_FUSED_LAYER": "1"}, "moe": {"NH_FUSED_LAYER": "0"},
-         "split": {"NH_FUSED_LAYER": "0", "NH_FUSED_MOE": "0"}}
+FORMS = {"moe": {}, "split": {"NH_FUSED_MOE": "0"}}
 
 
 def _run(path, out, env_over, n_prompt, n_predict, norm_topk):
@@ -60,10 +57,9 @@ def test_fused_forms_match_separate_kernels(gpu, synth_dir, tmp_path, spec_name,
     path = synth.cached(getattr(synth, spec_name), synth_dir)
     res = {k: _run(path, tmp_path / f"{k}.npz", env, n_prompt, n_predict, norm_topk) for k, env in FORMS.items()}
     n_layers = getattr(synth, spec_name).n_layers
-    # The forms really differ: 1, 4 and 6 kernels per layer (plus embed and lm_head).
-    assert [int(res[k]["launches"]) for k in FORMS] == [2 + n_layers, 2 + 4 * n_layers, 2 + 6 * n_layers]
-    for form in ("layer", "moe"):
-        for key in ("tokens", "hidden", "logits", "sel", "e_tokens", "e_hidden", "e_sel"):
-            assert np.array_equal(res[form][key], res["split"][key]), (form, key)
-    assert np.array_equal(res["layer"]["tokens"], res["layer"]["e_tokens"])
-    assert np.array_equal(res["layer"]["hidden"], res["layer"]["e_hidden"])
+    # The forms really differ: 4 and 6 kernels per layer (plus embed and lm_head).
+    assert [int(res[k]["launches"]) for k in FORMS] == [2 + 4 * n_layers, 2 + 6 * n_layers]
+    for key in ("tokens", "hidden", "logits", "sel", "e_tokens", "e_hidden", "e_sel"):
+        assert np.array_equal(res["moe"][key], res["split"][key]), key
+    assert np.array_equal(res["moe"]["tokens"], res["moe"]["e_tokens"])
+    assert np.array_equal(res["moe"]["hidden"], res["moe"]["e_hidden"])

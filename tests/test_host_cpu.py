@@ -7,6 +7,7 @@ from __future__ import annotations
 import ctypes as C
 import json
 import math
+import os
 import re
 from pathlib import Path
 
@@ -186,10 +187,13 @@ def test_expert_reader_slices_match_gguf_py(mini):
     assert r.ExpertBytes("no.such.tensor") == 0
 
 
-GRANITE = Path("/root/reference/data/granite3moe.trace.txt")
+# The reference's recorded granite-3-MoE routing trace, found through the
+# reference checkout named by NUTHATCH_REFERENCE (the test skips without it).
+GRANITE = (Path(os.environ["NUTHATCH_REFERENCE"]) / "data" / "granite3moe.trace.txt"
+           if os.environ.get("NUTHATCH_REFERENCE") else None)
 
 
-@pytest.mark.skipif(not GRANITE.exists() or not oracle.ref_available(),
+@pytest.mark.skipif(GRANITE is None or not GRANITE.exists() or not oracle.ref_available(),
                     reason="the reference's granite routing trace is not available")
 def test_granite_trace_sweep_matches_reference_and_published_rates():
     """The reference's recorded granite-3-MoE routing trace: LRU and OS page
@@ -235,34 +239,3 @@ def test_moe_layer_declines_uncovered_shapes_before_any_launch():
     assert rc(router=fake + 4) == -1                       # router rows are bulk-copied
     assert rc(gate=fake + 8) == -1                         # Q4_K rows are read 16 bytes at a time
     assert lib().nh_moe_layer_scratch_bytes(64) >= 64 + 4 * 64
-
-
-def test_layer_step_declines_uncovered_shapes_before_any_launch():
-    """nh_layer_step validates every phase's shapes on the host and returns
-    NH_E_ARG / NH_E_TYPE, launching nothing, where the whole-layer kernel does
-    not cover the layer (the engine then issues the per-phase kernels); the fake
-    device pointers are never dereferenced."""
-    from nuthatch_b200._lib import NhLayerStep, NhMoeLayer
-
-    fake = 1 << 20
-    moe = dict(state=fake, h=fake, ffn_norm=fake, eps=1e-5, router=fake, n_embd=2048, n_ff=1024, n_expert=64, k=8,
-               n_layers=16, gate=fake, tg=12, gate_nb2=1024 * 8 * 144, up=fake, tu=12, up_nb2=1024 * 8 * 144,
-               down=fake, td=14, down_nb2=2048 * 4 * 210, sel=fake, wts=fake, ff=fake)
-    base = dict(attn_norm=fake, wq=fake, tq=12, wk=fake, tk=12, wv=fake, tv=14, wo=fake, to=12, q=fake, k=fake, v=fake,
-                q_norm=fake, k_norm=fake, n_head=16, n_head_kv=16, head_dim=128, rope_cs=fake, kq_scale=0.088,
-                k_cache=fake, v_cache=fake, max_seq=4096, attn_scratch=fake, attn_out=fake, scratch=fake)
-
-    def rc(moe_kw=None, **kw):
-        s = NhLayerStep(moe=NhMoeLayer(**{**moe, **(moe_kw or {})}), **{**base, **kw})
-        return lib().nh_layer_step(C.byref(s), None)
-
-    assert lib().nh_layer_step(None, None) == -1
-    assert rc(scratch=None) == -1 and rc(attn_scratch=None) == -1
-    assert rc(tq=0) == -3 and rc(to=0) == -3                 # F32 projections
-    assert rc(moe_kw=dict(td=0)) == -3                       # F32 experts
-    assert rc(head_dim=96) == -1                             # n_head*head_dim/256 not a power of two <= 8
-    assert rc(n_head=16, n_head_kv=5) == -1                  # heads not a multiple of the KV heads
-    assert rc(k_cache=fake + 4) == -1                        # cache rows are bulk-copied
-    assert rc(wo=fake + 8) == -1                             # Q4_K rows are read 16 bytes at a time
-    assert rc(moe_kw=dict(n_ff=768)) == -1                   # the MoE block's own limits apply
-    assert lib().nh_layer_scratch_bytes(64) >= 64 + 4 * 64

@@ -22,6 +22,7 @@ pytestmark = pytest.mark.gpu
 
 REL_TOL = 2e-2
 NH_E_CAPACITY = -7
+NH_E_ARG = -1
 
 
 def _rel_err(a, b) -> float:
@@ -94,3 +95,7 @@ def test_static_scratch_rejects_sizes_beyond_its_capacity(gpu):
                                       null, 8192, null, null) == NH_E_CAPACITY
     assert L.nh_attention_step_static(null, null, null, null, null, null, 1e-5, 65, 65, 64, null, 0.125, null,
                                       null, 64, null, null) == NH_E_CAPACITY
+    # Within capacity, a call with missing buffers is refused by the argument
+    # checks, which run before the counters are cleared on the stream.
+    assert L.nh_attention_step_static(null, null, null, null, null, null, 1e-5, 16, 16, 128, null, 0.088, null,
+                                      null, 64, null, null) == NH_E_ARG
