@@ -302,6 +302,14 @@ int nh_batch_attention(const NhDecodeState* state, const float* qr, int n_seq, i
 int nh_batch_router(const float* xn, const float* router, int n_seq, int64_t n_embd, int n_expert, int k,
                     int norm_topk, int32_t* sel, float* wts, void* stream);
 
+/* nh_batch_router that also records row b as the routing of position
+ * trace_pos0 + b in layer `layer` (trace_sel[((trace_pos0+b)*n_layers +
+ * layer)*k + i], trace_gap[(trace_pos0+b)*n_layers + layer], the layout of
+ * nh_router_topk's trace; both may be null). */
+int nh_batch_router_trace(const float* xn, const float* router, int n_seq, int64_t n_embd, int n_expert, int k,
+                          int norm_topk, int32_t* sel, float* wts, int32_t* trace_sel, float* trace_gap,
+                          int trace_pos0, int layer, int n_layers, void* stream);
+
 /* Per-expert token lists of sel [n_seq][k] in (token, slot) order: off/cnt
  * [n_expert], act_idx[j] = token, out_idx[j] = token*k + slot. */
 int nh_batch_moe_plan(const int32_t* sel, int n_seq, int k, int n_expert, int32_t* off, int32_t* cnt,
@@ -315,6 +323,34 @@ int nh_batch_combine(const float* y, const float* wts, int n_seq, int k, int64_t
  * last CTA advances state->pos.  scratch: 64 zeroed bytes. */
 int nh_batch_argmax(NhDecodeState* state, const float* logits, int n_seq, int64_t n_vocab, int32_t* fed,
                     int32_t* out_tokens, int n_predict, void* scratch, void* stream);
+
+/* ---- prompt prefill: the n_tok positions pos0 .. pos0+n_tok-1 of ONE
+ * sequence as rows of the batched kernels (the reference forwards the whole
+ * prompt in its first GreedyGenerateCached step, generate.cc:63-91;
+ * forward.cc:45-79).  Per position the arithmetic equals the batch-1
+ * kernels', so the K/V rows and ids that follow are identical to a
+ * position-by-position prompt.  The caches are one sequence's
+ * [max_seq][n_head_kv*head_dim] per layer. */
+
+/* h[r] = embedding row of ids[r] (ggml_get_rows, forward.cc:53-54); an id
+ * outside the vocabulary reads row 0 and sets *err to NH_E_ARG (err may be
+ * null). */
+int nh_prefill_embed(const int32_t* ids, int n_tok, const void* table, int32_t type, int64_t n_embd,
+                     int64_t n_vocab, float* h, int32_t* err, void* stream);
+
+/* nh_batch_qk for prefill rows: row r is at position pos0 + r; QK-norm, NEOX
+ * RoPE and the K/V append at that position (attention.cc:84-116). */
+int nh_prefill_qk(const float* q, const float* k, const float* v, const float* q_norm, const float* k_norm, float eps,
+                  int n_tok, int pos0, int n_head, int n_head_kv, int head_dim, const float* rope_cs,
+                  float* k_cache, float* v_cache, int max_seq, float* qr, void* stream);
+
+/* Causal attention of the prefill rows (attention.cc:119-133 with the mask
+ * offset n_past = pos0): row r attends cache positions 0..pos0+r, in the
+ * 64-position splits of nh_attention_step combined in the same order.
+ * head_dim a multiple of 32, at most 128; caches and qr 16-byte aligned. */
+int nh_prefill_attention(const float* qr, int n_tok, int pos0, int n_head, int n_head_kv, int head_dim,
+                         float kq_scale, const float* k_cache, const float* v_cache, int max_seq, float* out,
+                         void* stream);
 
 /* ---- standalone forms used by the parity tests ---- */
 

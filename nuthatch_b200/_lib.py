@@ -101,6 +101,13 @@ SIGNATURES = {
     "nh_moe_layer": (C.c_int, [P(NhMoeLayer), vp]),
     "nh_moe_layer_scratch_bytes": (i64, [C.c_int]),
     "nh_lm_head_argmax": (C.c_int, [vp, vp, vp, f32, vp, i32, i64, i64, vp, vp, vp, vp]),
+    "nh_prefill_embed": (C.c_int, [vp, C.c_int, vp, i32, i64, i64, vp, vp, vp]),
+    "nh_prefill_qk": (C.c_int, [vp, vp, vp, vp, vp, f32, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp, vp,
+                                C.c_int, vp, vp]),
+    "nh_prefill_attention": (C.c_int, [vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, f32, vp, vp, C.c_int, vp,
+                                       vp]),
+    "nh_batch_router_trace": (C.c_int, [vp, vp, C.c_int, i64, C.c_int, C.c_int, C.c_int, vp, vp, vp, vp, C.c_int,
+                                        C.c_int, C.c_int, vp]),
     "nh_gemv": (C.c_int, [vp, vp, i32, i64, i64, vp, vp, f32, vp, vp]),
     "nh_quantize_q8k": (C.c_int, [vp, i64, vp, vp]),
     "nh_dequantize": (C.c_int, [vp, i32, i64, i64, vp, vp]),

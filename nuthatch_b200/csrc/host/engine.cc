@@ -236,12 +236,13 @@ int Engine::Reserve(int max_seq, int max_prompt, int max_predict, bool dumps) {
   return cudaDeviceSynchronize() == cudaSuccess ? NH_OK : NH_E_CUDA;
 }
 
-int Engine::Begin(const int32_t* prompt, int n_prompt, int n_predict) {
+int Engine::Begin(const int32_t* prompt, int n_prompt, int n_predict, int start_pos) {
   if (n_prompt <= 0 || n_prompt > max_prompt_ || n_predict <= 0 || n_predict > max_predict_ ||
       n_prompt + n_predict > max_seq_)
     return NH_E_CAPACITY;
+  if (start_pos < 0 || start_pos >= n_prompt) return NH_E_ARG;
   std::memcpy(prompt_host_, prompt, static_cast<size_t>(n_prompt) * 4);
-  *state_host_ = NhDecodeState{0, n_prompt, n_predict, 0, 0, 0, 0, 0};
+  *state_host_ = NhDecodeState{start_pos, n_prompt, n_predict, 0, 0, 0, 0, 0};
   if (cudaMemcpyAsync(prompt_, prompt_host_, static_cast<size_t>(n_prompt) * 4, cudaMemcpyHostToDevice,
                       stream_) != cudaSuccess ||
       cudaMemcpyAsync(state_, state_host_, sizeof(NhDecodeState), cudaMemcpyHostToDevice, stream_) != cudaSuccess)

@@ -47,6 +47,19 @@ struct ModelView {
 template <typename M>
 bool BuildView(const M& m, bool experts, ModelView* v);
 
+// Device buffers of a chunk of prefill rows (Engine::Prefill), sized for
+// `rows` token positions.
+struct PrefillBuffers {
+  ~PrefillBuffers();
+  int Reserve(const OlmoeConfig& c, int rows);
+  void Release();
+  int rows = 0;
+  float *h = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *qr = nullptr, *att = nullptr, *xn = nullptr;
+  float *wts = nullptr, *ff = nullptr, *y = nullptr;
+  uint8_t *q8 = nullptr, *q8ff = nullptr;
+  int32_t *sel = nullptr, *off = nullptr, *cnt = nullptr, *act_idx = nullptr, *out_idx = nullptr;
+};
+
 class Engine {
  public:
   explicit Engine(const OlmoeConfig& cfg);
@@ -57,8 +70,23 @@ class Engine {
   // buffers when `dumps`.  Returns NH_OK or an error code.
   int Reserve(int max_seq, int max_prompt, int max_predict, bool dumps);
 
-  // Uploads the prompt and resets the decode cursor (async on stream()).
-  int Begin(const int32_t* prompt, int n_prompt, int n_predict);
+  // Uploads the prompt and resets the decode cursor to start_pos (async on
+  // stream()); start_pos > 0 when Prefill fills positions 0..start_pos-1.
+  int Begin(const int32_t* prompt, int n_prompt, int n_predict, int start_pos = 0);
+
+  // One-shot prompt prefill, the reference's first GreedyGenerateCached step
+  // (generate.cc:63-91, forward.cc:45-79): positions 0..n_tok-1 of the
+  // uploaded prompt run through the batched kernels in chunks of up to
+  // kPrefillChunk positions (grouped expert products, causal prefill
+  // attention), writing their K/V rows and, with `trace`, their routing.  Per
+  // position the arithmetic is that of the batch-1 step, so the cache and the
+  // ids that follow are identical.  No logits are formed for these positions
+  // (only the last prompt position's are used, and the batch-1 step forms
+  // them).
+  static constexpr int kPrefillChunk = 512;
+  int Prefill(const ModelView& m, int n_tok, bool norm_topk, bool trace);
+  // Whether the batched kernels cover this model's shapes and weight types.
+  static bool PrefillSupported(const ModelView& m);
 
   int EnqueueEmbed(const ModelView& m);
   // QKV, attention and the output projection of one layer.
@@ -110,6 +138,7 @@ class Engine {
  private:
   void FreeAll();
   OlmoeConfig cfg_;
+  std::unique_ptr<PrefillBuffers> pf_;
   cudaStream_t stream_ = nullptr;
   int max_seq_ = 0, max_prompt_ = 0, max_predict_ = 0;
   bool dumps_ = false;

@@ -7,6 +7,20 @@
 
 namespace nuthatch {
 
+namespace {
+
+// The batched prompt prefill is on unless NH_PREFILL=0 (read once).
+bool PrefillEnabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("NH_PREFILL");
+    v = (e != nullptr && e[0] == '0') ? 0 : 1;
+  }
+  return v != 0;
+}
+
+}  // namespace
+
 std::vector<int32_t> GreedyGenerateCachedEx(const OlmoeModel& model, const std::vector<int32_t>& ids,
                                             int n_predict, bool norm_topk, GenerateOptions* opt) {
   GenerateOptions local;
@@ -31,9 +45,16 @@ std::vector<int32_t> GreedyGenerateCachedEx(const OlmoeModel& model, const std::
   const bool dumps = o.hidden != nullptr || o.logits != nullptr;
   const bool trace = o.trace != nullptr || o.trace_gap != nullptr;
   int rc = e.Reserve(P + n_predict + 1, P, n_predict, dumps);
-  if (rc == NH_OK) rc = e.Begin(ids.data(), P, n_predict);
+  // The prompt is forwarded at once, as the reference's first step does
+  // (generate.cc:63-91): positions 0..P-2 through the batched prefill, then
+  // the last prompt position as the first batch-1 step.  Models outside the
+  // batched kernels' shapes (and NH_PREFILL=0) take the prompt one position
+  // per step; the ids are the same either way.
+  const int start = P > 1 && PrefillEnabled() && Engine::PrefillSupported(ws->view) ? P - 1 : 0;
+  if (rc == NH_OK) rc = e.Begin(ids.data(), P, n_predict, start);
+  if (rc == NH_OK && start > 0) rc = e.Prefill(ws->view, start, norm_topk, trace);
   const int steps = P + n_predict - 1;
-  if (rc == NH_OK) rc = e.RunSteps(ws->view, steps, norm_topk, trace, dumps, o.use_graph);
+  if (rc == NH_OK) rc = e.RunSteps(ws->view, steps - start, norm_topk, trace, dumps, o.use_graph);
   if (rc == NH_OK) rc = e.Finish(n_predict, &out);
   if (rc != NH_OK) {
     o.status = rc;

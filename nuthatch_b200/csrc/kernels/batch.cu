@@ -32,30 +32,13 @@ constexpr int kBatchTokTile = 32;  // tokens staged per CTA
 constexpr int kBMaxTopK = 32;
 
 // ---------------------------------------------------------------- embed
-__global__ void batch_embed_kernel(const NhDecodeState* state, const int32_t* prompts, int n_prompt,
-                                   const int32_t* fed, const uint8_t* table, int type, int n_embd, int n_vocab,
-                                   uint64_t rb, float* h) {
-  const int b = blockIdx.x;
-  __shared__ int s_tok;
-  pdl_wait();
-  pdl_trigger();
-  if (threadIdx.x == 0) {
-    const int pos = state->pos;
-    int tok = pos < n_prompt ? prompts[static_cast<int64_t>(b) * n_prompt + pos] : fed[b];
-    if (tok < 0 || tok >= n_vocab) {
-      atomicCAS(const_cast<int32_t*>(&state->error), 0, NH_E_ARG);
-      tok = 0;
-    }
-    s_tok = tok;
-  }
-  __syncthreads();
-  const uint8_t* row = table + static_cast<uint64_t>(s_tok) * rb;
-  float* out = h + static_cast<int64_t>(b) * n_embd;
+// Dequantises one embedding row (the element formulas of the batch-1
+// embedding, dequantize_row_*) into out[0..n_embd), block-strided.
+__device__ __forceinline__ void embed_row(const uint8_t* row, int type, int n_embd, float* out) {
   for (int i = threadIdx.x; i < n_embd; i += blockDim.x) {
     if (type == NH_TYPE_F32) {
       out[i] = reinterpret_cast<const float*>(row)[i];
     } else {
-      // Same element formulas as the batch-1 embedding (dequantize_row_*).
       const int64_t blk = i / QK;
       const int e = i % QK;
       if (type == NH_TYPE_Q4_K) {
@@ -81,6 +64,41 @@ __global__ void batch_embed_kernel(const NhDecodeState* state, const int32_t* pr
       }
     }
   }
+}
+
+__global__ void batch_embed_kernel(const NhDecodeState* state, const int32_t* prompts, int n_prompt,
+                                   const int32_t* fed, const uint8_t* table, int type, int n_embd, int n_vocab,
+                                   uint64_t rb, float* h) {
+  const int b = blockIdx.x;
+  __shared__ int s_tok;
+  pdl_wait();
+  pdl_trigger();
+  if (threadIdx.x == 0) {
+    const int pos = state->pos;
+    int tok = pos < n_prompt ? prompts[static_cast<int64_t>(b) * n_prompt + pos] : fed[b];
+    if (tok < 0 || tok >= n_vocab) {
+      atomicCAS(const_cast<int32_t*>(&state->error), 0, NH_E_ARG);
+      tok = 0;
+    }
+    s_tok = tok;
+  }
+  __syncthreads();
+  embed_row(table + static_cast<uint64_t>(s_tok) * rb, type, n_embd, h + static_cast<int64_t>(b) * n_embd);
+}
+
+// Row r of h = embedding row of ids[r] (the prompt positions of a prefill).
+// Ids outside the vocabulary read row 0 and raise *err (when not null).
+__global__ void rows_embed_kernel(const int32_t* ids, const uint8_t* table, int type, int n_embd, int n_vocab,
+                                  uint64_t rb, float* h, int32_t* err) {
+  const int r = blockIdx.x;
+  pdl_wait();
+  pdl_trigger();
+  int tok = ids[r];
+  if (tok < 0 || tok >= n_vocab) {
+    if (threadIdx.x == 0 && err != nullptr) atomicCAS(err, 0, NH_E_ARG);
+    tok = 0;
+  }
+  embed_row(table + static_cast<uint64_t>(tok) * rb, type, n_embd, h + static_cast<int64_t>(r) * n_embd);
 }
 
 // ---------------------------------------------------------------- prep
@@ -596,17 +614,23 @@ __global__ void __launch_bounds__(kBatchWarps * 32, 2) batch_mma_kernel(const Gr
 // One CTA per sequence: QK-norm over the full q (and k) width, NEOX RoPE at
 // the shared position, the rotated q to qr, and the new K (rotated) and V
 // rows appended to the sequence's cache ([B][max_seq][n_embd_kv] per layer).
+//
+// Row b is at position base + b*pos_step (base = state->pos, or pos0 when
+// state is null) and appends to cache sequence b*seq_step: decode rows are
+// independent sequences at the shared cursor (pos_step 0, seq_step 1);
+// prefill rows are consecutive positions of one sequence (1, 0).
 __global__ void __launch_bounds__(128) batch_qk_kernel(const NhDecodeState* state, const float* q, const float* k,
                                                        const float* v, const float* q_norm, const float* k_norm,
                                                        float eps, int n_head, int n_head_kv, int hd,
                                                        const float* rope_cs, float* k_cache, float* v_cache,
-                                                       int max_seq, float* qr) {
+                                                       int max_seq, float* qr, int pos0, int pos_step, int seq_step) {
   const int b = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
   const int dq = n_head * hd, dkv = n_head_kv * hd, half = hd / 2;
   __shared__ double red[16];
   pdl_wait();
   pdl_trigger();
-  const int pos = state->pos;
+  const int pos = (state != nullptr ? state->pos : pos0) + b * pos_step;
+  const int64_t seq = static_cast<int64_t>(b) * seq_step;
   extern __shared__ __align__(16) float qk_s[];  // [dq] q row, [dkv] k row
   copy_to_smem(qk_s, q + static_cast<int64_t>(b) * dq, dq);
   copy_to_smem(qk_s + dq, k + static_cast<int64_t>(b) * dkv, dkv);
@@ -640,8 +664,8 @@ __global__ void __launch_bounds__(128) batch_qk_kernel(const NhDecodeState* stat
     qo[h * hd + i] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
     qo[h * hd + i + half] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
   }
-  float* kd = k_cache + (static_cast<int64_t>(b) * max_seq + pos) * dkv;
-  float* vd = v_cache + (static_cast<int64_t>(b) * max_seq + pos) * dkv;
+  float* kd = k_cache + (seq * max_seq + pos) * dkv;
+  float* vd = v_cache + (seq * max_seq + pos) * dkv;
   for (int j = tid; j < n_head_kv * half; j += blockDim.x) {
     const int h = j / half, i = j % half;
     const float c = cs[2 * i], s = cs[2 * i + 1];
@@ -822,13 +846,185 @@ __global__ void __launch_bounds__(kBAttnThreads) batch_attention_kernel(const BA
   if (tid == 0) p.tickets[bh] = 0u;
 }
 
+// ---------------------------------------------------------------- prefill attention
+// Causal attention of the n_tok prompt positions pos0 .. pos0+n_tok-1 of one
+// sequence (query t attends keys 0..pos0+t), with the decode kernels'
+// arithmetic for every query: 64-key splits, each with its own maximum,
+// exponentials and double sum, combined in split order against the global
+// maximum (a single split normalises directly).  A CTA owns kPAttnQ queries
+// of one head and walks the splits twice: the first pass finds each query's
+// global maximum (scores only), the second re-forms each split and folds it
+// into the running combination, so no per-split partials leave the CTA.
+constexpr int kPAttnThreads = 128;
+constexpr int kPAttnQ = 16;
+constexpr int kPAttnSplit = 64;
+constexpr int kPAttnOut = kPAttnQ * 128 / kPAttnThreads;  // outputs per thread at head_dim 128
+
+struct PAttnArgs {
+  const float* qr;       // [n_tok][n_head*hd] QK-normed, rotated queries
+  const float* k_cache;  // [max_seq][n_head_kv*hd] post-RoPE keys of this sequence
+  const float* v_cache;
+  float* out;            // [n_tok][n_head*hd]
+  int n_tok, pos0, n_head, n_head_kv, hd;
+  float kq_scale;
+};
+
+__device__ __forceinline__ int pattn_keys_in_split(int n_kv, int s) {
+  return max(0, min(kPAttnSplit, n_kv - s * kPAttnSplit));
+}
+
+__global__ void __launch_bounds__(kPAttnThreads) prefill_attention_kernel(const PAttnArgs p) {
+  const int h = blockIdx.x, t0 = blockIdx.y * kPAttnQ;
+  const int nq = min(kPAttnQ, p.n_tok - t0);
+  const int hd = p.hd, kst = hd + 4;
+  const int kh = h / (p.n_head / p.n_head_kv);
+  const int dq = p.n_head * hd, dkv = p.n_head_kv * hd;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  extern __shared__ __align__(16) float sm[];
+  float* Ks = sm;                      // [64][hd+4]: padded rows for conflict-free 16-byte reads
+  float* Vs = Ks + kPAttnSplit * kst;  // [64][hd]
+  float* Qs = Vs + kPAttnSplit * hd;   // [kPAttnQ][hd]
+  float* S = Qs + kPAttnQ * hd;        // [kPAttnQ][64] scores, then exponentials
+  __shared__ float s_max2[2][kPAttnQ];
+  __shared__ float s_M[kPAttnQ], s_w[kPAttnQ];
+  __shared__ double s_L[kPAttnQ];
+  pdl_wait();
+  pdl_trigger();
+  const int h4 = hd / 4;
+  for (int i = tid; i < kPAttnQ * h4; i += blockDim.x) {
+    const int q = i / h4, c = i % h4;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (q < nq) v = reinterpret_cast<const float4*>(p.qr + static_cast<int64_t>(t0 + q) * dq + h * hd)[c];
+    reinterpret_cast<float4*>(Qs + q * hd)[c] = v;
+  }
+  if (tid < kPAttnQ) s_L[tid] = 0.0;
+  const int kv_last = p.pos0 + t0 + nq;  // keys the block's last query sees
+  const int n_splits = (kv_last + kPAttnSplit - 1) / kPAttnSplit;
+  auto n_kv = [&](int q) { return p.pos0 + t0 + q + 1; };
+  auto load = [&](int s, bool with_v) {
+    const int nk = pattn_keys_in_split(kv_last, s);
+    const int64_t r0 = static_cast<int64_t>(s) * kPAttnSplit;
+    for (int i = tid; i < nk * h4; i += blockDim.x) {
+      const int r = i / h4, c = i % h4;
+      const int64_t g = (r0 + r) * dkv + kh * hd;
+      reinterpret_cast<float4*>(Ks + r * kst)[c] = __ldg(reinterpret_cast<const float4*>(p.k_cache + g) + c);
+      if (with_v) reinterpret_cast<float4*>(Vs + r * hd)[c] = __ldg(reinterpret_cast<const float4*>(p.v_cache + g) + c);
+    }
+  };
+  // Scores of the thread's (key j, query q) pairs: j = tid % 64, q = tid / 64 + 2i.
+  const int j = tid & (kPAttnSplit - 1), qh = tid >> 6;
+
+  // ---- pass 1: each query's maximum over all its keys
+  float run[kPAttnQ / 2];
+#pragma unroll
+  for (int i = 0; i < kPAttnQ / 2; ++i) run[i] = -INFINITY;
+  for (int s = 0; s < n_splits; ++s) {
+    __syncthreads();
+    load(s, false);
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < kPAttnQ / 2; ++i) {
+      const int q = qh + 2 * i;
+      if (q < nq && j < pattn_keys_in_split(n_kv(q), s))
+        run[i] = fmaxf(run[i], __fmul_rn(bscore_thread(Ks + j * kst, Qs + q * hd, hd), p.kq_scale));
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kPAttnQ / 2; ++i) {
+    const float m = warp_max(run[i]);
+    if (lane == 0) s_max2[warp & 1][qh + 2 * i] = m;
+  }
+  __syncthreads();
+  if (tid < kPAttnQ) s_M[tid] = fmaxf(s_max2[0][tid], s_max2[1][tid]);
+
+  // ---- pass 2: form each split and fold it in, in split order
+  float acc_out[kPAttnOut];
+#pragma unroll
+  for (int i = 0; i < kPAttnOut; ++i) acc_out[i] = 0.f;
+  const int n_out = kPAttnQ * hd / kPAttnThreads;
+  for (int s = 0; s < n_splits; ++s) {
+    __syncthreads();
+    load(s, true);
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < kPAttnQ / 2; ++i) {
+      const int q = qh + 2 * i;
+      if (q < nq && j < pattn_keys_in_split(n_kv(q), s))
+        S[q * kPAttnSplit + j] = __fmul_rn(bscore_thread(Ks + j * kst, Qs + q * hd, hd), p.kq_scale);
+    }
+    __syncthreads();
+    // Per query (warp w: queries w, w+4, ...; lane: keys lane and lane+32).
+    for (int q = warp; q < nq; q += kPAttnThreads / 32) {
+      const int n = pattn_keys_in_split(n_kv(q), s);
+      if (n == 0) continue;
+      float* sq = S + q * kPAttnSplit;
+      const float a = lane < n ? sq[lane] : -INFINITY;
+      const float b = lane + 32 < n ? sq[lane + 32] : -INFINITY;
+      const float m = warp_max(fmaxf(a, b));
+      const float ea = lane < n ? exp_cw(__fsub_rn(a, m)) : 0.f;
+      const float eb = lane + 32 < n ? exp_cw(__fsub_rn(b, m)) : 0.f;
+      const double la = warp_sum_d(lane < n ? static_cast<double>(ea) : 0.0);
+      const double lb = warp_sum_d(lane + 32 < n ? static_cast<double>(eb) : 0.0);
+      double l = 0.0;
+      l += la;
+      l += lb;
+      const bool single = n_kv(q) <= kPAttnSplit;
+      if (single) {
+        const float inv = static_cast<float>(1.0 / l);
+        if (lane < n) sq[lane] = __fmul_rn(ea, inv);
+        if (lane + 32 < n) sq[lane + 32] = __fmul_rn(eb, inv);
+      } else {
+        if (lane < n) sq[lane] = ea;
+        if (lane + 32 < n) sq[lane + 32] = eb;
+        if (lane == 0) {
+          const float w = exp_cw(__fsub_rn(m, s_M[q]));
+          s_w[q] = w;
+          s_L[q] += l * static_cast<double>(w);
+        }
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int it = 0; it < kPAttnOut; ++it) {
+      if (it >= n_out) break;
+      const int idx = tid + it * kPAttnThreads, q = idx / hd, i = idx % hd;
+      if (q >= nq) continue;
+      const int n = pattn_keys_in_split(n_kv(q), s);
+      if (n == 0) continue;
+      const float* sq = S + q * kPAttnSplit;
+      float acc = 0.f;
+      for (int jj = 0; jj < n; ++jj) acc = __fadd_rn(acc, __fmul_rn(Vs[jj * hd + i], sq[jj]));
+      acc_out[it] = n_kv(q) <= kPAttnSplit ? acc : __fadd_rn(acc_out[it], __fmul_rn(acc, s_w[q]));
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int it = 0; it < kPAttnOut; ++it) {
+    if (it >= n_out) break;
+    const int idx = tid + it * kPAttnThreads, q = idx / hd, i = idx % hd;
+    if (q >= nq) continue;
+    const float v = n_kv(q) <= kPAttnSplit ? acc_out[it] : __fmul_rn(acc_out[it], static_cast<float>(1.0 / s_L[q]));
+    p.out[static_cast<int64_t>(t0 + q) * dq + h * hd + i] = v;
+  }
+}
+
 // ---------------------------------------------------------------- router
 // One CTA per token: the E logits from the normalised f32 row (the batch-1
 // router's dot order), then softmax and top-(k+1) by rank in warp 0.
+//
+// With trace_sel/trace_gap, row b is also recorded as the routing of position
+// trace_pos0 + b in layer `layer` (the batch-1 router's trace layout).
+struct RouterTrace {
+  int32_t* sel;
+  float* gap;
+  int pos0, layer, n_layers;
+};
+
 template <int KP>
 __global__ void __launch_bounds__(256) batch_router_kernel(const float* xn,
                                                            const float* router, int K, int E, int topk,
-                                                           int norm_topk, int32_t* sel, float* wts) {
+                                                           int norm_topk, int32_t* sel, float* wts,
+                                                           const RouterTrace tr) {
   const int b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __shared__ float lg[32 * KP];
   __shared__ int s_ids[kBMaxTopK + 1];
@@ -941,44 +1137,84 @@ __global__ void __launch_bounds__(256) batch_router_kernel(const float* xn,
     sel[b * topk + t] = s_ids[t];
     wts[b * topk + t] = norm_topk ? __fdiv_rn(s_vals[t], ws) : s_vals[t];
   }
+  if (tr.sel != nullptr) {
+    const int64_t rec = static_cast<int64_t>(tr.pos0 + b) * tr.n_layers + tr.layer;
+    for (int t = lane; t < topk; t += 32) tr.sel[rec * topk + t] = s_ids[t];
+    if (tr.gap != nullptr) {
+      // Smallest gap between adjacent probabilities of the descending top-(k+1).
+      float g = 1.f;
+      for (int t = lane; t + 1 < kk; t += 32) g = fminf(g, __fsub_rn(s_vals[t], s_vals[t + 1]));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) g = fminf(g, __shfl_xor_sync(0xffffffffu, g, o));
+      if (lane == 0) tr.gap[rec] = g;
+    }
+  }
 }
 
 // ---------------------------------------------------------------- expert plan
-// One CTA: for the B*k (token, slot) pairs, per-expert counts, offsets and
+// One CTA: for the n_pairs (token, slot) pairs, per-expert counts, offsets and
 // the token lists in (token, slot) order: act_idx = token, out_idx = token*k
-// + slot.
-__global__ void __launch_bounds__(512) batch_moe_plan_kernel(const int32_t* sel, int n_pairs, int E, int topk,
-                                                             int32_t* off, int32_t* cnt, int32_t* act_idx,
-                                                             int32_t* out_idx) {
-  extern __shared__ int sh[];  // [E] counts, [E] offsets, [n_pairs] selection
+// + slot.  A stable counting sort: pairs are taken 512 at a time; within a
+// chunk a pair's rank among earlier pairs of the same expert is its rank in
+// its warp's match set plus the same-expert counts of the earlier warps.
+constexpr int kPlanThreads = 512;
+constexpr int kPlanWarps = kPlanThreads / 32;
+
+__global__ void __launch_bounds__(kPlanThreads) batch_moe_plan_kernel(const int32_t* sel, int n_pairs, int E,
+                                                                      int topk, int32_t* off, int32_t* cnt,
+                                                                      int32_t* act_idx, int32_t* out_idx) {
+  extern __shared__ int sh[];  // [E] counts, [E] next free index, [kPlanWarps][E] chunk counts
   int* c = sh;
-  int* o = sh + E;
-  int* s = sh + 2 * E;
+  int* next = sh + E;
+  int* wc = sh + 2 * E;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   pdl_wait();
   pdl_trigger();
-  for (int e = threadIdx.x; e < E; e += blockDim.x) c[e] = 0;
-  for (int j = threadIdx.x; j < n_pairs; j += blockDim.x) s[j] = sel[j];
+  for (int e = tid; e < E; e += blockDim.x) c[e] = 0;
+  for (int i = tid; i < kPlanWarps * E; i += blockDim.x) wc[i] = 0;
   __syncthreads();
-  for (int j = threadIdx.x; j < n_pairs; j += blockDim.x) atomicAdd(&c[s[j]], 1);
+  for (int j = tid; j < n_pairs; j += blockDim.x) {
+    const int e = sel[j];
+    if (e >= 0 && e < E) atomicAdd(&c[e], 1);
+  }
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (tid == 0) {
     int acc = 0;
     for (int e = 0; e < E; ++e) {
-      o[e] = acc;
+      next[e] = acc;
       acc += c[e];
     }
   }
   __syncthreads();
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {
-    off[e] = o[e];
+  for (int e = tid; e < E; e += blockDim.x) {
+    off[e] = next[e];
     cnt[e] = c[e];
   }
-  for (int j = threadIdx.x; j < n_pairs; j += blockDim.x) {
-    const int e = s[j];
-    int rank = 0;
-    for (int q = 0; q < j; ++q) rank += s[q] == e ? 1 : 0;
-    act_idx[o[e] + rank] = j / topk;
-    out_idx[o[e] + rank] = j;
+  const unsigned lt = (1u << lane) - 1u;
+  for (int base = 0; base < n_pairs; base += kPlanThreads) {
+    const int j = base + tid;
+    const int e = j < n_pairs ? sel[j] : -1;
+    const bool valid = e >= 0 && e < E;
+    const unsigned same = __match_any_sync(0xffffffffu, valid ? e : -1);
+    const int in_warp = __popc(same & lt);
+    if (valid && in_warp == 0) wc[warp * E + e] = __popc(same);
+    __syncthreads();
+    if (valid) {
+      int rank = next[e] + in_warp;
+      for (int w = 0; w < warp; ++w) rank += wc[w * E + e];
+      act_idx[rank] = j / topk;
+      out_idx[rank] = j;
+    }
+    __syncthreads();
+    for (int x = tid; x < E; x += blockDim.x) {
+      int add = 0;
+      for (int w = 0; w < kPlanWarps; ++w) {
+        add += wc[w * E + x];
+        wc[w * E + x] = 0;
+      }
+      next[x] += add;
+    }
+    __syncthreads();
   }
 }
 
@@ -1064,7 +1300,7 @@ extern "C" int nh_batch_prep(const float* x, int64_t x_stride, int64_t rows, con
   if (x == nullptr || rows <= 0 || n <= 0 || n > kMaxK || (q8 == nullptr && xn == nullptr)) return NH_E_ARG;
   if (q8 != nullptr && n % QK != 0) return NH_E_ARG;
   const size_t smem = act_smem_bytes(static_cast<int>(n), true, norm_w != nullptr && do_norm);
-  static size_t configured = 48 * 1024;
+  static SmemLimit configured;
   if (!ensure_smem(batch_prep_kernel, smem, configured)) return NH_E_CUDA;
   return launch_pdl(batch_prep_kernel, dim3(static_cast<unsigned>(rows)), dim3(256), smem,
                     static_cast<cudaStream_t>(stream), x, x_stride, norm_w, eps, do_norm, static_cast<int>(n),
@@ -1134,7 +1370,7 @@ extern "C" int nh_batch_rowdot(const NhGroupedRowDot* g, void* stream) {
   }
   const int tiles = (max_tok + p.tok_tile - 1) / p.tok_tile;
   const size_t smem = static_cast<size_t>(p.tok_tile) * (p.K / QK) * kQ8Stride;
-  static size_t configured = 48 * 1024;
+  static SmemLimit configured;
   if (!ensure_smem(batch_rowdot_kernel, smem, configured)) return NH_E_CUDA;
   return launch_pdl(batch_rowdot_kernel, dim3(p.n_groups * p.row_blocks, std::max(1, tiles)), dim3(kBatchWarps * 32),
                     smem, static_cast<cudaStream_t>(stream), p);
@@ -1149,10 +1385,11 @@ extern "C" int nh_batch_qk(const NhDecodeState* state, const float* q, const flo
       head_dim % 2 != 0 || n_head % n_head_kv != 0)
     return NH_E_ARG;
   const size_t smem = static_cast<size_t>(n_head + n_head_kv) * head_dim * sizeof(float);
-  static size_t configured = 48 * 1024;
+  static SmemLimit configured;
   if (smem > 220 * 1024 || !ensure_smem(batch_qk_kernel, smem, configured)) return NH_E_ARG;
   return launch_pdl(batch_qk_kernel, dim3(n_seq), dim3(128), smem, static_cast<cudaStream_t>(stream), state, q, k, v,
-                    q_norm, k_norm, eps, n_head, n_head_kv, head_dim, rope_cs, k_cache, v_cache, max_seq, qr);
+                    q_norm, k_norm, eps, n_head, n_head_kv, head_dim, rope_cs, k_cache, v_cache, max_seq, qr, 0, 0,
+                    1);
 }
 
 extern "C" int64_t nh_batch_attention_scratch_bytes(int n_seq, int n_head, int head_dim, int max_seq) {
@@ -1192,30 +1429,92 @@ extern "C" int nh_batch_attention(const NhDecodeState* state, const float* qr, i
   p.out = out;
   const size_t smem = static_cast<size_t>(kBAttnSplit * (head_dim + 4) + kBAttnSplit * head_dim + head_dim +
                                           kBAttnSplit) * sizeof(float);
-  static size_t configured = 48 * 1024;
+  static SmemLimit configured;
   if (!ensure_smem(batch_attention_kernel, smem, configured)) return NH_E_CUDA;
   return launch_pdl(batch_attention_kernel, dim3(n_head, p.n_split, n_seq), dim3(kBAttnThreads), smem,
                     static_cast<cudaStream_t>(stream), p);
 }
 
-extern "C" int nh_batch_router(const float* xn, const float* router, int n_seq, int64_t n_embd, int n_expert, int k,
-                               int norm_topk, int32_t* sel, float* wts, void* stream) {
+extern "C" int nh_prefill_embed(const int32_t* ids, int n_tok, const void* table, int32_t type, int64_t n_embd,
+                                int64_t n_vocab, float* h, int32_t* err, void* stream) {
+  if (ids == nullptr || table == nullptr || h == nullptr || n_tok <= 0) return NH_E_ARG;
+  if (type != NH_TYPE_F32 && type != NH_TYPE_Q4_K && type != NH_TYPE_Q6_K) return NH_E_TYPE;
+  if (type != NH_TYPE_F32 && n_embd % QK != 0) return NH_E_ARG;
+  return launch_pdl(rows_embed_kernel, dim3(n_tok), dim3(256), 0, static_cast<cudaStream_t>(stream), ids,
+                    static_cast<const uint8_t*>(table), static_cast<int>(type), static_cast<int>(n_embd),
+                    static_cast<int>(n_vocab), static_cast<uint64_t>(row_bytes(type, n_embd)), h, err);
+}
+
+extern "C" int nh_prefill_qk(const float* q, const float* k, const float* v, const float* q_norm, const float* k_norm,
+                             float eps, int n_tok, int pos0, int n_head, int n_head_kv, int head_dim,
+                             const float* rope_cs, float* k_cache, float* v_cache, int max_seq, float* qr,
+                             void* stream) {
+  if (q == nullptr || k == nullptr || v == nullptr || q_norm == nullptr || k_norm == nullptr || rope_cs == nullptr ||
+      k_cache == nullptr || v_cache == nullptr || qr == nullptr || n_tok <= 0 || pos0 < 0 || head_dim % 2 != 0 ||
+      n_head <= 0 || n_head_kv <= 0 || n_head % n_head_kv != 0 || pos0 + n_tok > max_seq)
+    return NH_E_ARG;
+  const size_t smem = static_cast<size_t>(n_head + n_head_kv) * head_dim * sizeof(float);
+  static SmemLimit configured;
+  if (smem > 220 * 1024 || !ensure_smem(batch_qk_kernel, smem, configured)) return NH_E_ARG;
+  return launch_pdl(batch_qk_kernel, dim3(n_tok), dim3(128), smem, static_cast<cudaStream_t>(stream),
+                    static_cast<const NhDecodeState*>(nullptr), q, k, v, q_norm, k_norm, eps, n_head, n_head_kv,
+                    head_dim, rope_cs, k_cache, v_cache, max_seq, qr, pos0, 1, 0);
+}
+
+extern "C" int nh_prefill_attention(const float* qr, int n_tok, int pos0, int n_head, int n_head_kv, int head_dim,
+                                    float kq_scale, const float* k_cache, const float* v_cache, int max_seq,
+                                    float* out, void* stream) {
+  if (qr == nullptr || k_cache == nullptr || v_cache == nullptr || out == nullptr || n_tok <= 0 || pos0 < 0 ||
+      pos0 + n_tok > max_seq || n_head <= 0 || n_head_kv <= 0 || n_head % n_head_kv != 0 || head_dim % 32 != 0 ||
+      head_dim > 128 || (reinterpret_cast<uintptr_t>(k_cache) & 15) != 0 ||
+      (reinterpret_cast<uintptr_t>(v_cache) & 15) != 0 || (reinterpret_cast<uintptr_t>(qr) & 15) != 0)
+    return NH_E_ARG;
+  PAttnArgs p;
+  p.qr = qr;
+  p.k_cache = k_cache;
+  p.v_cache = v_cache;
+  p.out = out;
+  p.n_tok = n_tok;
+  p.pos0 = pos0;
+  p.n_head = n_head;
+  p.n_head_kv = n_head_kv;
+  p.hd = head_dim;
+  p.kq_scale = kq_scale;
+  const size_t smem = static_cast<size_t>(kPAttnSplit * (head_dim + 4) + kPAttnSplit * head_dim +
+                                          kPAttnQ * head_dim + kPAttnQ * kPAttnSplit) * sizeof(float);
+  static SmemLimit configured;
+  if (!ensure_smem(prefill_attention_kernel, smem, configured)) return NH_E_CUDA;
+  return launch_pdl(prefill_attention_kernel, dim3(n_head, (n_tok + kPAttnQ - 1) / kPAttnQ), dim3(kPAttnThreads),
+                    smem, static_cast<cudaStream_t>(stream), p);
+}
+
+extern "C" int nh_batch_router_trace(const float* xn, const float* router, int n_seq, int64_t n_embd, int n_expert,
+                                     int k, int norm_topk, int32_t* sel, float* wts, int32_t* trace_sel,
+                                     float* trace_gap, int trace_pos0, int layer, int n_layers, void* stream) {
   if (xn == nullptr || router == nullptr || sel == nullptr || wts == nullptr || n_seq <= 0 || n_expert <= 0 ||
       n_expert > 256 || k <= 0 || k > kBMaxTopK || k > n_expert || n_embd % 4 != 0)
     return NH_E_ARG;
+  if (trace_sel != nullptr && (trace_pos0 < 0 || layer < 0 || layer >= n_layers)) return NH_E_ARG;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int K = static_cast<int>(n_embd);
+  const RouterTrace tr{trace_sel, trace_sel != nullptr ? trace_gap : nullptr, trace_pos0, layer, n_layers};
   if (n_expert <= 32)
     return launch_pdl(batch_router_kernel<1>, dim3(n_seq), dim3(256), 0, st, xn, router, K, n_expert, k, norm_topk,
-                      sel, wts);
+                      sel, wts, tr);
   if (n_expert <= 64)
     return launch_pdl(batch_router_kernel<2>, dim3(n_seq), dim3(256), 0, st, xn, router, K, n_expert, k, norm_topk,
-                      sel, wts);
+                      sel, wts, tr);
   if (n_expert <= 128)
     return launch_pdl(batch_router_kernel<4>, dim3(n_seq), dim3(256), 0, st, xn, router, K, n_expert, k, norm_topk,
-                      sel, wts);
+                      sel, wts, tr);
   return launch_pdl(batch_router_kernel<8>, dim3(n_seq), dim3(256), 0, st, xn, router, K, n_expert, k, norm_topk,
-                    sel, wts);
+                    sel, wts, tr);
+}
+
+extern "C" int nh_batch_router(const float* xn, const float* router, int n_seq, int64_t n_embd, int n_expert, int k,
+                               int norm_topk, int32_t* sel, float* wts, void* stream) {
+  return nh_batch_router_trace(xn, router, n_seq, n_embd, n_expert, k, norm_topk, sel, wts, nullptr, nullptr, 0, 0, 1,
+                               stream);
 }
 
 extern "C" int nh_batch_moe_plan(const int32_t* sel, int n_seq, int k, int n_expert, int32_t* off, int32_t* cnt,
@@ -1224,10 +1523,10 @@ extern "C" int nh_batch_moe_plan(const int32_t* sel, int n_seq, int k, int n_exp
       k <= 0 || n_expert <= 0)
     return NH_E_ARG;
   const int n_pairs = n_seq * k;
-  const size_t smem = static_cast<size_t>(2 * n_expert + n_pairs) * sizeof(int);
+  const size_t smem = static_cast<size_t>(2 + kPlanWarps) * n_expert * sizeof(int);
   if (smem > 48 * 1024) return NH_E_CAPACITY;
-  return launch_pdl(batch_moe_plan_kernel, dim3(1), dim3(512), smem, static_cast<cudaStream_t>(stream), sel, n_pairs,
-                    n_expert, k, off, cnt, act_idx, out_idx);
+  return launch_pdl(batch_moe_plan_kernel, dim3(1), dim3(kPlanThreads), smem, static_cast<cudaStream_t>(stream), sel,
+                    n_pairs, n_expert, k, off, cnt, act_idx, out_idx);
 }
 
 extern "C" int nh_batch_combine(const float* y, const float* wts, int n_seq, int k, int64_t n_embd, float* h,
