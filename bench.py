@@ -294,6 +294,65 @@ def run_batched(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_ep_batched(args, dist, rank: int, world: int, local_rank: int, path: str, full_model) -> dict | None:
+    """Expert-parallel batched decode (the configuration-3 workload: bs64,
+    2048-token seeded contexts, 128 greedy steps) over the `world` GPUs of
+    this job: experts sharded n_expert/world per GPU (each rank loads only its
+    shard), sequences split evenly (data-parallel attention), NCCL all-gather
+    of the tokens' Q8_K rows and selections and an all-to-all of the pick rows
+    per MoE layer.  Device-timed decode part, max over ranks; value = global
+    sequences x decoded ids / time.  Rank 0 checks its first sequence against
+    the single-GPU GreedyGenerateCached of it."""
+    import torch
+
+    import nuthatch_b200 as nh
+
+    cfg = full_model.config()
+    B, ctx, n_pred = args.batch_seqs, args.batch_context, args.batch_steps
+    if B % world != 0 or cfg.n_expert % world != 0:
+        return None
+    box = [nh.ExpertGroup.new_id() if rank == 0 else None]
+    if dist is not None:
+        dist.broadcast_object_list(box, src=0)
+    ep = nh.ExpertGroup(box[0], world, rank)
+    first, count = nh.ExpertGroup.shard(cfg.n_expert, world, rank)
+    shard = nh.OlmoeModel.LoadExpertShard(path, first, count)
+    if shard is None:
+        raise SystemExit("expert shard load failed")
+    prompts = np.random.default_rng(3).integers(0, cfg.n_vocab, (B, ctx)).tolist()
+    per = B // world
+    mine = prompts[rank * per:(rank + 1) * per]
+    # Warm-up call (kernel configuration, NCCL connections), then the run.
+    nh.generate_batch_ex(shard, [p[:8] for p in mine], 2, False, ep=ep)
+    clocks = ClockSampler(local_rank)
+    r = nh.generate_batch_ex(shard, mine, n_pred, False, ep=ep)
+    clk = clocks.stop()
+    ms = max_over_ranks(r["decode_ms"], dist)
+    subset_ok = None
+    if rank == 0:
+        subset_ok = r["tokens"][0] == nh.GreedyGenerateCached(full_model, mine[0], n_pred, False)
+    shard.close()
+    ep.close()
+    value = B * n_pred / (ms / 1000.0)
+    pos_mean = ctx - 1 + (n_pred - 1) / 2.0
+    kv = per * cfg.n_layers * (pos_mean + 1) * 2 * cfg.n_head_kv * (cfg.n_embd // cfg.n_head) * 4
+    # Per rank and step: replicated attention weights, router and lm_head, its
+    # own experts (every expert a step touches, all of them at bs64), its KV.
+    weights = (8 * 9437184 + 8 * 10518528 + 16 * 524288 + 84510720 +
+               (8 * 64 * 3538944 + 8 * 64 * 4079616) // world)
+    peaks = measured_peaks()
+    achieved = (kv + weights) / (ms / 1000.0 / n_pred) / 1e9
+    return {"metric": f"OLMoE Q4_K_M expert-parallel batched decode tok/s (bs{B}, {ctx}-token contexts)",
+            "value": value, "unit": "tok/s", "n_gpus": world, "ms_per_step": ms / n_pred,
+            "experts_per_gpu": count, "sequences_per_gpu": per, "steps": n_pred,
+            "collectives": "per MoE layer: NCCL all-gather of Q8_K rows + top-k ids, all-to-all of pick rows",
+            "timing": "device time of the decode part (CUDA events on the decode stream), max over ranks",
+            "clocks": clk,
+            "step_roofline_per_gpu": {"bytes_per_step": kv + weights, "achieved": achieved, "peak": peaks["hbm_gbs"],
+                                      "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"]},
+            "subset_matches_single_gpu": subset_ok}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -311,6 +370,7 @@ def main() -> None:
     ap.add_argument("--batch-steps", type=int, default=128)
     ap.add_argument("--budgets", type=int, nargs="*", default=[4, 8, 16, 32])
     ap.add_argument("--stream-tokens", type=int, default=256)
+    ap.add_argument("--no-ep", action="store_true", help="skip the expert-parallel batched section")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.workload == "batched":
@@ -449,6 +509,8 @@ def main() -> None:
            "h2d_bytes_per_step": N_PROMPT * 4 + 32, "d2h_bytes_per_step": N_PREDICT * 4 + 32,
            "api": "GreedyGenerateCached (nh_generate, mode 0)"}
 
+    ep_line = None if args.no_ep else run_ep_batched(args, dist, rank, world, local_rank, path, m)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
@@ -466,7 +528,7 @@ def main() -> None:
                            "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                            "step": f"{N_PREDICT} decode positions", "l2": "inputs larger than L2 (4.2 GB weights)"},
                 "clocks": clk, "roofline": roofline, "step_roofline": step_roofline, "e2e": e2e,
-                "gpu_launches": gpu_launches, "cpu_baseline": cpu}
+                "gpu_launches": gpu_launches, "cpu_baseline": cpu, "ep_batched": ep_line}
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()

@@ -66,6 +66,25 @@ int nh_generate_launches(const void* model);
 int nh_generate_batch(void* model, const int32_t* prompts, int n_seq, int n_prompt, int n_predict, int norm_topk,
                       int use_graph, int32_t* out_tokens, double* decode_ms);
 
+/* Expert parallelism over the GPUs of one node (no reference counterpart; the
+ * EP configuration {world, rank, communicator} of the drop-in boundary, see
+ * include/nuthatch/expert_parallel.h).  One process per GPU:
+ *   rank 0: nh_ep_new_id(id) and hand the 128 id bytes to every rank;
+ *   every rank: ep = nh_ep_create(id, world, rank) on its device (collective),
+ *   model = nh_model_load_expert_shard(path, rank * E/world, E/world), then
+ *   nh_generate_batch_ep(model, ep, its own n_seq prompts, ...) on all ranks
+ *   at once (the same n_seq, n_prompt and n_predict everywhere); free the
+ *   model and nh_ep_free(ep) before the process group that carried the id.
+ * nh_ep_new_id returns NH_E_STATE when NCCL cannot be loaded; nh_ep_create
+ * and the shard load return NULL on failure.  The shard model serves only
+ * nh_generate_batch_ep; the single-GPU generate calls refuse it (NH_E_STATE). */
+int nh_ep_new_id(uint8_t* id);
+void* nh_ep_create(const uint8_t* id, int world, int rank);
+void nh_ep_free(void* ep);
+void* nh_model_load_expert_shard(const char* path, uint32_t first, uint32_t count);
+int nh_generate_batch_ep(void* model, const void* ep, const int32_t* prompts, int n_seq, int n_prompt, int n_predict,
+                         int norm_topk, int use_graph, int32_t* out_tokens, double* decode_ms);
+
 /* Decode replay for timing (no reference counterpart; the reference times
  * whole generate calls).  prepare: runs the prompt's first n_prompt-1
  * positions and saves the cursor (synchronises).  run: restores the cursor

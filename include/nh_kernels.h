@@ -315,6 +315,20 @@ int nh_batch_router_trace(const float* xn, const float* router, int n_seq, int64
 int nh_batch_moe_plan(const int32_t* sel, int n_seq, int k, int n_expert, int32_t* off, int32_t* cnt,
                       int32_t* act_idx, int32_t* out_idx, void* stream);
 
+/* nh_batch_moe_plan over experts [e_first, e_first + n_expert) only (group
+ * e - e_first); pairs that selected other experts are left out.  Expert
+ * parallelism plans a rank's own shard over every rank's tokens with it. */
+int nh_batch_moe_plan_range(const int32_t* sel, int n_seq, int k, int e_first, int n_expert, int32_t* off,
+                            int32_t* cnt, int32_t* act_idx, int32_t* out_idx, void* stream);
+
+/* Expert-parallel combine (moe.cc:51-60 on the token's home GPU): h[b] +=
+ * sum_i wts[b][i] * row(b, i), products rounded, in top-k order, where
+ * row(b, i) is row b*k+i of block sel[b][i] / experts_per_rank of y_recv
+ * (n_src blocks of src_stride floats: the pick rows each expert-owning rank
+ * returned). */
+int nh_ep_combine(const float* y_recv, int64_t src_stride, int n_src, const int32_t* sel, const float* wts, int n_seq,
+                  int k, int64_t n_embd, int experts_per_rank, float* h, void* stream);
+
 /* h[b] += sum_i wts[b][i] * y[b*k+i] (products rounded, top-k order). */
 int nh_batch_combine(const float* y, const float* wts, int n_seq, int k, int64_t n_embd, float* h, void* stream);
 

@@ -50,10 +50,17 @@ std::vector<int32_t> GreedyGenerateCachedEx(const OlmoeModel& model, const std::
 // boundary needs for many independent sequences).  All prompts must have the
 // same length; each sequence advances one position per step in lockstep with
 // its own KV cache, and its ids equal GreedyGenerateCached on it alone.
+//
+// Expert parallelism (ep set): every rank of the group calls this at once with
+// its own share of the sequences (the same count on every rank) and a model
+// holding the rank's expert shard (OlmoeModel::LoadExpertShard with
+// ExpertShard::Of) or all experts; see nuthatch/expert_parallel.h.
+class ExpertGroup;
 struct BatchOptions {
-  bool use_graph = true;  // replay a captured CUDA graph per step
-  double decode_ms = 0;   // out: device time from the last prompt position to the end
-  int status = 0;         // out: NH_OK or the first error code
+  bool use_graph = true;            // replay a captured CUDA graph per step
+  const ExpertGroup* ep = nullptr;  // expert-parallel group, or single GPU
+  double decode_ms = 0;             // out: device time from the last prompt position to the end
+  int status = 0;                   // out: NH_OK or the first error code
 };
 std::vector<std::vector<int32_t>> GreedyGenerateCachedBatch(const OlmoeModel& model,
                                                             const std::vector<std::vector<int32_t>>& prompts,

@@ -54,6 +54,12 @@ class OlmoeModel {
   // device allocation/copy failure (olmoe_model.h:43-44).  Uses the current
   // CUDA device.
   static std::unique_ptr<OlmoeModel> Load(const std::string& path);
+  // Expert-parallel load (no reference counterpart): every non-expert tensor,
+  // and of each ffn_{gate,up,down}_exps tensor only experts [first, first +
+  // count), whose DTensor then has ne[2] == count and starts at expert
+  // `first`.  Such a model serves GreedyGenerateCachedBatch with an
+  // ExpertGroup; the single-GPU entry points refuse it.
+  static std::unique_ptr<OlmoeModel> LoadExpertShard(const std::string& path, uint32_t first, uint32_t count);
   ~OlmoeModel();
 
   OlmoeModel(const OlmoeModel&) = delete;
@@ -65,6 +71,11 @@ class OlmoeModel {
 
   int device() const { return device_; }
   size_t device_bytes() const { return bytes_; }
+  // The experts held in device memory: [expert_first, expert_first +
+  // expert_count); all of them (0, n_expert) after Load.
+  uint32_t expert_first() const { return expert_first_; }
+  uint32_t expert_count() const { return expert_count_; }
+  bool holds_all_experts() const { return expert_first_ == 0 && expert_count_ == cfg_.n_expert; }
 
   // Reusable device workspace of the decode engine (KV cache, activations,
   // captured step graph); owned here so repeated generate calls do not
@@ -76,6 +87,7 @@ class OlmoeModel {
   OlmoeModel() = default;
   OlmoeConfig cfg_;
   int device_ = 0;
+  uint32_t expert_first_ = 0, expert_count_ = 0;
   void* base_ = nullptr;
   size_t bytes_ = 0;
   std::unordered_map<std::string, DTensor> tensors_;

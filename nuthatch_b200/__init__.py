@@ -21,7 +21,7 @@ __all__ = ["OlmoeConfig", "OlmoeModel", "StreamingModel", "GreedyGenerate", "Gre
            "GreedyGenerateCachedTrace", "StreamingGenerate", "generate_ex", "streaming_generate_ex",
            "RoutingRecord", "RoutingTrace", "WriteRoutingTrace", "ReadRoutingTrace", "ReadRoutingTraceText",
            "ReplayStats", "LruPolicy", "OsPageCachePolicy", "LearnedPinPolicy", "BuildUsage", "Replay",
-           "SweepBudgets", "SweepPinRatio", "ExpertReader", "ExpertSlotCache", "NhError"]
+           "SweepBudgets", "SweepPinRatio", "ExpertReader", "ExpertSlotCache", "NhError", "ExpertGroup"]
 
 
 class NhError(RuntimeError):
@@ -80,6 +80,13 @@ class OlmoeModel:
     @staticmethod
     def Load(path: str) -> Optional["OlmoeModel"]:
         h = lib().nh_model_load(str(path).encode())
+        return OlmoeModel(h) if h else None
+
+    @staticmethod
+    def LoadExpertShard(path: str, first: int, count: int) -> Optional["OlmoeModel"]:
+        """Non-expert tensors and experts [first, first+count) of each layer
+        (expert parallelism); serves only generate_batch_ex with an ExpertGroup."""
+        h = lib().nh_model_load_expert_shard(str(path).encode(), int(first), int(count))
         return OlmoeModel(h) if h else None
 
     def config(self) -> OlmoeConfig:
@@ -196,18 +203,59 @@ def GreedyGenerateCachedTrace(model: OlmoeModel, ids: Sequence[int], n_predict: 
     return r["tokens"]
 
 
+class ExpertGroup:
+    """The communicator of an expert-parallel job (one process per GPU).
+
+    Rank 0 makes the id with ExpertGroup.new_id(); every rank then calls
+    ExpertGroup(id, world, rank) on its device at the same time."""
+
+    ID_BYTES = 128
+
+    @staticmethod
+    def new_id() -> bytes:
+        buf = (C.c_uint8 * ExpertGroup.ID_BYTES)()
+        _check(lib().nh_ep_new_id(buf), "nh_ep_new_id (NCCL not loadable)")
+        return bytes(buf)
+
+    def __init__(self, group_id: bytes, world: int, rank: int):
+        if len(group_id) != self.ID_BYTES:
+            raise ValueError("group id must be 128 bytes")
+        buf = (C.c_uint8 * self.ID_BYTES).from_buffer_copy(group_id)
+        self._h = lib().nh_ep_create(buf, int(world), int(rank))
+        if not self._h:
+            raise NhError("nh_ep_create: " + lib().nh_last_error().decode())
+        self.world, self.rank = int(world), int(rank)
+
+    @staticmethod
+    def shard(n_expert: int, world: int, rank: int) -> tuple[int, int]:
+        """(first, count) of the experts rank owns (equal contiguous shares)."""
+        per = n_expert // world
+        return per * rank, per
+
+    def close(self) -> None:
+        if self._h:
+            lib().nh_ep_free(self._h)
+            self._h = None
+
+
 def generate_batch_ex(model: OlmoeModel, prompts: Sequence[Sequence[int]], n_predict: int, norm_topk: bool,
-                      use_graph: bool = True) -> dict:
+                      use_graph: bool = True, ep: Optional[ExpertGroup] = None) -> dict:
     """Batched greedy decode of equal-length prompts; ids per sequence and the
-    device time of the decode part."""
+    device time of the decode part.  With ep, every rank passes its own
+    sequences (the same count everywhere) at the same time."""
     p = np.ascontiguousarray(np.asarray(prompts, dtype=np.int32))
     if p.ndim != 2:
         raise ValueError("prompts must all have the same length")
     n_seq, n_prompt = p.shape
     out = np.zeros((n_seq, n_predict), dtype=np.int32)
     ms = C.c_double(0.0)
-    _check(lib().nh_generate_batch(model._h, _ptr(p, C.c_int32), n_seq, n_prompt, n_predict, int(norm_topk),
-                                   int(use_graph), _ptr(out, C.c_int32), C.byref(ms)), "nh_generate_batch")
+    if ep is None:
+        _check(lib().nh_generate_batch(model._h, _ptr(p, C.c_int32), n_seq, n_prompt, n_predict, int(norm_topk),
+                                       int(use_graph), _ptr(out, C.c_int32), C.byref(ms)), "nh_generate_batch")
+    else:
+        _check(lib().nh_generate_batch_ep(model._h, ep._h, _ptr(p, C.c_int32), n_seq, n_prompt, n_predict,
+                                          int(norm_topk), int(use_graph), _ptr(out, C.c_int32), C.byref(ms)),
+               "nh_generate_batch_ep")
     return {"tokens": out.tolist(), "decode_ms": ms.value}
 
 

@@ -52,6 +52,12 @@ SIGNATURES = {
     "nh_generate_launches": (C.c_int, [vp]),
     "nh_generate_batch": (C.c_int, [vp, P(i32), C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, P(i32),
                                     P(C.c_double)]),
+    "nh_ep_new_id": (C.c_int, [vp]),
+    "nh_ep_create": (vp, [vp, C.c_int, C.c_int]),
+    "nh_ep_free": (None, [vp]),
+    "nh_model_load_expert_shard": (vp, [cp, C.c_uint32, C.c_uint32]),
+    "nh_generate_batch_ep": (C.c_int, [vp, vp, P(i32), C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, P(i32),
+                                       P(C.c_double)]),
     "nh_batch_q8_bytes": (i64, [i64, i64]),
     "nh_batch_attention_scratch_bytes": (i64, [C.c_int, C.c_int, C.c_int, C.c_int]),
     "nh_decode_prepare": (C.c_int, [vp, P(i32), C.c_int, C.c_int]),

@@ -10,6 +10,8 @@
 #include <cstring>
 
 #include "engine.h"
+#include "nccl_api.h"
+#include "nuthatch/expert_parallel.h"
 #include "nuthatch/generate.h"
 #include "nuthatch/gguf_file.h"
 
@@ -42,6 +44,33 @@ class BatchBuffers {
  private:
   std::vector<void*> owned_;
 };
+
+// All-gather of every rank's Q8_K activation rows and top-k selections
+// (rank r's block at r * the block size).
+int ExchangeTokens(const ExpertGroup& ep, const uint8_t* q8, size_t q8_bytes, uint8_t* q8_all, const int32_t* sel,
+                   size_t n_sel, int32_t* sel_all, cudaStream_t s) {
+  const NcclApi& n = Nccl();
+  ncclComm_t comm = static_cast<ncclComm_t>(ep.comm());
+  if (n.GroupStart() != ncclSuccess) return NH_E_CUDA;
+  const bool ok = n.AllGather(q8, q8_all, q8_bytes, ncclUint8, comm, s) == ncclSuccess &&
+                  n.AllGather(sel, sel_all, n_sel, ncclInt32, comm, s) == ncclSuccess;
+  return n.GroupEnd() == ncclSuccess && ok ? NH_OK : NH_E_CUDA;
+}
+
+// All-to-all of the pick rows: block r of y (rank r's tokens' picks, rows
+// (token, slot) in order; only picks of experts this rank owns are
+// meaningful) goes to rank r, and block q of y_recv arrives from rank q.
+int ReturnPicks(const ExpertGroup& ep, const float* y, size_t block, float* y_recv, cudaStream_t s) {
+  const NcclApi& n = Nccl();
+  ncclComm_t comm = static_cast<ncclComm_t>(ep.comm());
+  if (n.GroupStart() != ncclSuccess) return NH_E_CUDA;
+  bool ok = true;
+  for (int r = 0; r < ep.world() && ok; ++r) {
+    ok = n.Send(y + r * block, block, ncclFloat32, r, comm, s) == ncclSuccess &&
+         n.Recv(y_recv + r * block, block, ncclFloat32, r, comm, s) == ncclSuccess;
+  }
+  return n.GroupEnd() == ncclSuccess && ok ? NH_OK : NH_E_CUDA;
+}
 
 #define NH_B_TRY(x)             \
   do {                          \
@@ -80,8 +109,27 @@ std::vector<std::vector<int32_t>> GreedyGenerateCachedBatch(const OlmoeModel& mo
   }
   const int64_t d = c.n_embd, hd = c.head_dim(), dkv = static_cast<int64_t>(c.n_head_kv) * hd, F = c.n_ff,
                 E = c.n_expert, K = c.n_expert_used, V = c.n_vocab, L = c.n_layers;
+  // Expert parallelism: this rank owns experts [shard.first, +count) and the
+  // B sequences given here; all W ranks' tokens meet at every MoE layer.
+  const ExpertGroup* ep = o.ep;
+  const int W = ep != nullptr ? ep->world() : 1;
+  const ExpertShard shard = ep != nullptr ? ExpertShard::Of(c.n_expert, W, ep->rank()) : ExpertShard{0, c.n_expert};
+  if (ep != nullptr && (c.n_expert % W != 0 || !Nccl().ok)) {
+    o.status = NH_E_ARG;
+    return out;
+  }
+  // The expert weights of the owned shard: the model holds exactly the shard
+  // (its tensors start at expert shard.first) or all experts.
+  uint64_t e_skip = 0;
+  if (model.holds_all_experts()) {
+    e_skip = shard.first;
+  } else if (model.expert_first() != shard.first || model.expert_count() != shard.count) {
+    o.status = NH_E_STATE;
+    return out;
+  }
   const int max_seq = P + n_predict;
   const int BK = B * static_cast<int>(K);
+  const int BW = B * W, BKW = BK * W;  // rows of every rank's tokens / picks
   BatchBuffers bb;
   NhDecodeState* state = bb.Alloc<NhDecodeState>(1);
   int32_t* prm = bb.Alloc<int32_t>(static_cast<size_t>(B) * P);
@@ -94,16 +142,22 @@ std::vector<std::vector<int32_t>> GreedyGenerateCachedBatch(const OlmoeModel& mo
   float* qr = bb.Alloc<float>(B * d);
   float* att = bb.Alloc<float>(B * d);
   float* xn = bb.Alloc<float>(B * d);
-  uint8_t* q8 = bb.Alloc<uint8_t>(nh_batch_q8_bytes(B, d));
+  const int64_t q8_row = nh_batch_q8_bytes(1, d);
+  uint8_t* q8 = bb.Alloc<uint8_t>(q8_row * B);
   int32_t* sel = bb.Alloc<int32_t>(BK);
   float* wts = bb.Alloc<float>(BK);
   int32_t* off = bb.Alloc<int32_t>(E);
   int32_t* cnt = bb.Alloc<int32_t>(E);
-  int32_t* act_idx = bb.Alloc<int32_t>(BK);
-  int32_t* out_idx = bb.Alloc<int32_t>(BK);
-  float* ff = bb.Alloc<float>(static_cast<size_t>(BK) * F);
-  uint8_t* q8ff = bb.Alloc<uint8_t>(nh_batch_q8_bytes(BK, F));
-  float* y = bb.Alloc<float>(static_cast<size_t>(BK) * d);
+  int32_t* act_idx = bb.Alloc<int32_t>(BKW);
+  int32_t* out_idx = bb.Alloc<int32_t>(BKW);
+  float* ff = bb.Alloc<float>(static_cast<size_t>(BKW) * F);
+  uint8_t* q8ff = bb.Alloc<uint8_t>(nh_batch_q8_bytes(BKW, F));
+  float* y = bb.Alloc<float>(static_cast<size_t>(BKW) * d);
+  // Expert-parallel exchange buffers: every rank's activation rows and
+  // selections (all-gathered), and the pick rows returned by each rank.
+  uint8_t* q8_all = W > 1 ? bb.Alloc<uint8_t>(q8_row * BW) : q8;
+  int32_t* sel_all = W > 1 ? bb.Alloc<int32_t>(BKW) : sel;
+  float* y_recv = W > 1 ? bb.Alloc<float>(static_cast<size_t>(BKW) * d) : y;
   float* logits = bb.Alloc<float>(static_cast<size_t>(B) * V);
   float* rope = bb.Alloc<float>(static_cast<size_t>(max_seq) * hd);
   const int64_t attn_bytes = nh_batch_attention_scratch_bytes(B, c.n_head, static_cast<int>(hd), max_seq);
@@ -127,7 +181,11 @@ std::vector<std::vector<int32_t>> GreedyGenerateCachedBatch(const OlmoeModel& mo
                cudaMemcpy(rope, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
                cudaMemcpy(state, &st0, sizeof(st0), cudaMemcpyHostToDevice) == cudaSuccess &&
                cudaMemset(attn_scratch, 0, attn_bytes) == cudaSuccess && cudaMemset(ticket, 0, 64) == cudaSuccess &&
-               cudaMemset(fed, 0, B * 4) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess &&
+               cudaMemset(fed, 0, B * 4) == cudaSuccess &&
+               cudaMemset(ff, 0, static_cast<size_t>(BKW) * F * 4) == cudaSuccess &&
+               cudaMemset(y, 0, static_cast<size_t>(BKW) * d * 4) == cudaSuccess &&
+               cudaMemset(y_recv, 0, static_cast<size_t>(BKW) * d * 4) == cudaSuccess &&
+               cudaDeviceSynchronize() == cudaSuccess &&
                cudaStreamCreateWithFlags(&bb.stream_, cudaStreamNonBlocking) == cudaSuccess;
   if (!setup) {
     o.status = NH_E_CUDA;
@@ -174,48 +232,60 @@ std::vector<std::vector<int32_t>> GreedyGenerateCachedBatch(const OlmoeModel& mo
       NH_B_TRY(nh_batch_prep(h, d, B, Lv.ffn_norm, eps, 1, d, q8, xn, s));
       NH_B_TRY(nh_batch_router(xn, Lv.router, B, d, static_cast<int>(E), static_cast<int>(K), norm_topk ? 1 : 0,
                                sel, wts, s));
-      NH_B_TRY(nh_batch_moe_plan(sel, B, static_cast<int>(K), static_cast<int>(E), off, cnt, act_idx, out_idx, s));
+      if (W > 1) NH_B_TRY(ExchangeTokens(*ep, q8, q8_row * B, q8_all, sel, BK, sel_all, s));
+      // The owned experts over every rank's tokens: token j of the
+      // gathered rows is rank j / B's sequence j % B.
+      NH_B_TRY(nh_batch_moe_plan_range(sel_all, BW, static_cast<int>(K), static_cast<int>(shard.first),
+                                       static_cast<int>(shard.count), off, cnt, act_idx, out_idx, s));
       NhGroupedRowDot g;
       std::memset(&g, 0, sizeof(g));
-      g.w = Lv.gate;
-      g.w2 = Lv.up;
+      g.w = static_cast<const uint8_t*>(Lv.gate) + e_skip * Lv.gate_nb2;
+      g.w2 = static_cast<const uint8_t*>(Lv.up) + e_skip * Lv.up_nb2;
       g.mstride = Lv.gate_nb2;
       g.mstride2 = Lv.up_nb2;
       g.type = Lv.tg;
       g.type2 = Lv.tu;
       g.n = d;
       g.rows = F;
-      g.n_groups = static_cast<int32_t>(E);
+      g.n_groups = static_cast<int32_t>(shard.count);
       g.off = off;
       g.cnt = cnt;
       g.act_idx = act_idx;
       g.out_idx = out_idx;
-      g.max_tokens = B;
-      g.q8 = q8;
+      g.max_tokens = BW;
+      g.q8 = q8_all;
       g.out = ff;
       g.out_stride = F;
       g.mode = NH_ROWDOT_SWIGLU;
       NH_B_TRY(nh_batch_rowdot(&g, s));
-      NH_B_TRY(nh_batch_prep(ff, F, BK, nullptr, eps, 0, F, q8ff, nullptr, s));
+      NH_B_TRY(nh_batch_prep(ff, F, BKW, nullptr, eps, 0, F, q8ff, nullptr, s));
       std::memset(&g, 0, sizeof(g));
-      g.w = Lv.down;
+      g.w = static_cast<const uint8_t*>(Lv.down) + e_skip * Lv.down_nb2;
       g.mstride = Lv.down_nb2;
       g.type = Lv.td;
       g.type2 = Lv.td;
       g.n = F;
       g.rows = d;
-      g.n_groups = static_cast<int32_t>(E);
+      g.n_groups = static_cast<int32_t>(shard.count);
       g.off = off;
       g.cnt = cnt;
       g.act_idx = out_idx;  // the ff row of pair j is its (token, slot) index
       g.out_idx = out_idx;
-      g.max_tokens = B;
+      g.max_tokens = BW;
       g.q8 = q8ff;
       g.out = y;
       g.out_stride = d;
       g.mode = NH_ROWDOT_STORE;
       NH_B_TRY(nh_batch_rowdot(&g, s));
-      NH_B_TRY(nh_batch_combine(y, wts, B, static_cast<int>(K), d, h, s));
+      if (W > 1) {
+        // Rows of rank r's picks go back to rank r; the combine takes each
+        // pick's row from the block of the rank that owns its expert.
+        NH_B_TRY(ReturnPicks(*ep, y, static_cast<size_t>(BK) * d, y_recv, s));
+        NH_B_TRY(nh_ep_combine(y_recv, static_cast<int64_t>(BK) * d, W, sel, wts, B, static_cast<int>(K), d,
+                               static_cast<int>(shard.count), h, s));
+      } else {
+        NH_B_TRY(nh_batch_combine(y, wts, B, static_cast<int>(K), d, h, s));
+      }
     }
     NH_B_TRY(nh_batch_prep(h, d, B, m.out_norm, eps, 1, d, q8, nullptr, s));
     NH_B_TRY(dense(m.out, m.tout, V, d, q8, logits, V, NH_ROWDOT_STORE));

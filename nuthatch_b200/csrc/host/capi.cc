@@ -6,6 +6,7 @@
 
 #include "../../../include/nh_api.h"
 #include "nuthatch/cache_policy.h"
+#include "nuthatch/expert_parallel.h"
 #include "nuthatch/expert_reader.h"
 #include "nuthatch/expert_slot_cache.h"
 #include "nuthatch/generate.h"
@@ -177,10 +178,54 @@ int nh_generate_batch(void* model, const int32_t* prompts, int n_seq, int n_prom
   return NH_OK;
 }
 
+void* nh_model_load_expert_shard(const char* path, uint32_t first, uint32_t count) {
+  if (path == nullptr) {
+    SetErr("nh_model_load_expert_shard: null path");
+    return nullptr;
+  }
+  auto m = OlmoeModel::LoadExpertShard(path, first, count);
+  if (m == nullptr) SetErr(std::string("nh_model_load_expert_shard: failed to load ") + path);
+  return m.release();
+}
+
+int nh_ep_new_id(uint8_t* id) { return ExpertGroup::NewId(id) ? NH_OK : NH_E_STATE; }
+
+void* nh_ep_create(const uint8_t* id, int world, int rank) {
+  auto g = ExpertGroup::Create(id, world, rank);
+  if (g == nullptr) SetErr("nh_ep_create: NCCL communicator could not be created");
+  return g.release();
+}
+
+void nh_ep_free(void* ep) { delete static_cast<ExpertGroup*>(ep); }
+
+int nh_generate_batch_ep(void* model, const void* ep, const int32_t* prompts, int n_seq, int n_prompt, int n_predict,
+                         int norm_topk, int use_graph, int32_t* out_tokens, double* decode_ms) {
+  if (model == nullptr || prompts == nullptr || out_tokens == nullptr || n_seq <= 0 || n_prompt <= 0 ||
+      n_predict <= 0) {
+    SetErr("nh_generate_batch_ep: bad argument");
+    return NH_E_ARG;
+  }
+  std::vector<std::vector<int32_t>> p(n_seq);
+  for (int b = 0; b < n_seq; ++b)
+    p[b].assign(prompts + static_cast<size_t>(b) * n_prompt, prompts + static_cast<size_t>(b + 1) * n_prompt);
+  BatchOptions o;
+  o.use_graph = use_graph != 0;
+  o.ep = static_cast<const ExpertGroup*>(ep);
+  const auto ids = GreedyGenerateCachedBatch(*static_cast<const OlmoeModel*>(model), p, n_predict, norm_topk != 0, &o);
+  if (o.status != NH_OK) {
+    SetErr("nh_generate_batch_ep: failed with code " + std::to_string(o.status));
+    return o.status;
+  }
+  for (int b = 0; b < n_seq; ++b)
+    std::memcpy(out_tokens + static_cast<size_t>(b) * n_predict, ids[b].data(), static_cast<size_t>(n_predict) * 4);
+  if (decode_ms != nullptr) *decode_ms = o.decode_ms;
+  return NH_OK;
+}
+
 int nh_decode_prepare(void* model, const int32_t* prompt, int n_prompt, int n_predict) {
   if (model == nullptr || prompt == nullptr || n_prompt <= 0 || n_predict <= 0) return NH_E_ARG;
   OlmoeModel::Workspace* ws = static_cast<OlmoeModel*>(model)->workspace();
-  if (ws == nullptr || !ws->view_ok) return NH_E_STATE;
+  if (ws == nullptr || !ws->view_ok || !static_cast<OlmoeModel*>(model)->holds_all_experts()) return NH_E_STATE;
   Engine& e = ws->engine;
   int rc = e.Reserve(n_prompt + n_predict + 1, n_prompt, n_predict, false);
   if (rc == NH_OK) rc = e.Begin(prompt, n_prompt, n_predict);

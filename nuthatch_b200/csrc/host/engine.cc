@@ -57,6 +57,9 @@ void HostFree(T*& p) {
 
 }  // namespace
 
+uint32_t HeldExperts(const OlmoeModel& m) { return m.expert_count(); }
+uint32_t HeldExperts(const StreamingModel& m) { return m.config().n_expert; }
+
 template <typename M>
 bool BuildView(const M& m, bool experts, ModelView* v) {
   const OlmoeConfig& c = m.config();
@@ -108,8 +111,8 @@ bool BuildView(const M& m, bool experts, ModelView* v) {
     L.router = static_cast<const float*>(r->data);
     if (experts) {
       const DTensor *g = T("ffn_gate_exps.weight"), *u = T("ffn_up_exps.weight"), *dn = T("ffn_down_exps.weight");
-      if (!need(g, d, c.n_ff, c.n_expert) || !need(u, d, c.n_ff, c.n_expert) || !need(dn, c.n_ff, d, c.n_expert))
-        return false;
+      const int64_t ne = HeldExperts(m);
+      if (!need(g, d, c.n_ff, ne) || !need(u, d, c.n_ff, ne) || !need(dn, c.n_ff, d, ne)) return false;
       L.gate = g->data;
       L.tg = g->type;
       L.gate_nb2 = g->nb[2];

@@ -29,7 +29,7 @@ std::vector<int32_t> GreedyGenerateCachedEx(const OlmoeModel& model, const std::
   std::vector<int32_t> out;
   if (ids.empty() || n_predict <= 0) return out;
   OlmoeModel::Workspace* ws = model.workspace();
-  if (ws == nullptr || !ws->view_ok) {
+  if (ws == nullptr || !ws->view_ok || !model.holds_all_experts()) {
     o.status = NH_E_STATE;
     return out;
   }

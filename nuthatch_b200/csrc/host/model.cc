@@ -100,15 +100,37 @@ OlmoeConfig ParseOlmoeConfig(const GgufFile& g) {
 
 namespace {
 
+// Which experts of each expert tensor go to the device: none (streaming),
+// all, or a contiguous shard [first, first + count) (expert parallelism).
+struct ExpertPick {
+  bool skip = false;
+  uint32_t first = 0, count = 0;  // count 0: all
+};
+
+// Bytes of tensor t that are uploaded, and where they start in the file.
+void Slice(const GgufTensorInfo& t, const ExpertPick& pick, uint64_t* offset, size_t* nbytes) {
+  *offset = t.offset;
+  *nbytes = t.nbytes;
+  if (pick.count != 0 && IsExpertTensor(t.name)) {
+    *offset = t.offset + static_cast<uint64_t>(pick.first) * t.nb[2];
+    *nbytes = static_cast<size_t>(pick.count) * t.nb[2];
+  }
+}
+
 // Allocates one device region for the selected tensors and uploads them.
-bool UploadTensors(const std::string& path, const GgufFile& g, bool skip_experts,
+bool UploadTensors(const std::string& path, const GgufFile& g, const ExpertPick& pick,
                    std::unordered_map<std::string, DTensor>* out, void** base, size_t* bytes) {
   size_t total = 0;
   std::vector<std::pair<const GgufTensorInfo*, size_t>> plan;
   for (const GgufTensorInfo& t : g.tensors()) {
-    if (skip_experts && IsExpertTensor(t.name)) continue;
+    if (pick.skip && IsExpertTensor(t.name)) continue;
+    if (pick.count != 0 && IsExpertTensor(t.name) && (t.ne[2] < pick.first + pick.count || t.nb[2] == 0))
+      return false;
+    uint64_t off = 0;
+    size_t nb = 0;
+    Slice(t, pick, &off, &nb);
     plan.push_back({&t, total});
-    total += AlignUp(t.nbytes, kAlignDev);
+    total += AlignUp(nb, kAlignDev);
   }
   total += kTailPad;
   void* dev = nullptr;
@@ -126,7 +148,10 @@ bool UploadTensors(const std::string& path, const GgufFile& g, bool skip_experts
     if (!ok) break;
     const GgufTensorInfo& t = *pt.first;
     uint8_t* dst = static_cast<uint8_t*>(dev) + pt.second;
-    ok = up.Copy(*src, t.offset, t.nbytes, dst);
+    uint64_t off = 0;
+    size_t nb = 0;
+    Slice(t, pick, &off, &nb);
+    ok = up.Copy(*src, off, nb, dst);
     DTensor d;
     d.name = t.name;
     d.type = t.type;
@@ -134,8 +159,9 @@ bool UploadTensors(const std::string& path, const GgufFile& g, bool skip_experts
       d.ne[i] = t.ne[i];
       d.nb[i] = t.nb[i];
     }
+    if (pick.count != 0 && IsExpertTensor(t.name)) d.ne[2] = pick.count;
     d.data = dst;
-    d.nbytes = t.nbytes;
+    d.nbytes = nb;
     (*out)[t.name] = d;
   }
   ok = up.Sync() && ok;
@@ -156,8 +182,27 @@ std::unique_ptr<OlmoeModel> OlmoeModel::Load(const std::string& path) {
   if (g == nullptr) return nullptr;
   std::unique_ptr<OlmoeModel> m(new OlmoeModel());
   m->cfg_ = ParseOlmoeConfig(*g);
+  m->expert_count_ = m->cfg_.n_expert;
   cudaGetDevice(&m->device_);
-  if (!UploadTensors(path, *g, false, &m->tensors_, &m->base_, &m->bytes_)) return nullptr;
+  if (!UploadTensors(path, *g, ExpertPick{}, &m->tensors_, &m->base_, &m->bytes_)) return nullptr;
+  m->ws_.reset(new Workspace(m->cfg_));
+  m->ws_->view_ok = BuildView(*m, true, &m->ws_->view);
+  return m;
+}
+
+std::unique_ptr<OlmoeModel> OlmoeModel::LoadExpertShard(const std::string& path, uint32_t first, uint32_t count) {
+  auto g = GgufFile::Open(path);
+  if (g == nullptr || count == 0) return nullptr;
+  std::unique_ptr<OlmoeModel> m(new OlmoeModel());
+  m->cfg_ = ParseOlmoeConfig(*g);
+  if (first + count > m->cfg_.n_expert) return nullptr;
+  m->expert_first_ = first;
+  m->expert_count_ = count;
+  cudaGetDevice(&m->device_);
+  ExpertPick pick;
+  pick.first = first;
+  pick.count = count;
+  if (!UploadTensors(path, *g, pick, &m->tensors_, &m->base_, &m->bytes_)) return nullptr;
   m->ws_.reset(new Workspace(m->cfg_));
   m->ws_->view_ok = BuildView(*m, true, &m->ws_->view);
   return m;
@@ -242,7 +287,9 @@ std::unique_ptr<StreamingModel> StreamingModel::Load(const std::string& path, bo
   if (g == nullptr) return nullptr;
   std::unique_ptr<StreamingModel> m(new StreamingModel());
   m->cfg_ = ParseOlmoeConfig(*g);
-  if (!UploadTensors(path, *g, true, &m->tensors_, &m->base_, &m->bytes_)) return nullptr;
+  ExpertPick none;
+  none.skip = true;
+  if (!UploadTensors(path, *g, none, &m->tensors_, &m->base_, &m->bytes_)) return nullptr;
   m->reader_ = ExpertReader::Open(path);
   if (m->reader_ == nullptr) return nullptr;
   const OlmoeConfig& c = m->cfg_;

@@ -1160,8 +1160,12 @@ __global__ void __launch_bounds__(256) batch_router_kernel(const float* xn,
 constexpr int kPlanThreads = 512;
 constexpr int kPlanWarps = kPlanThreads / 32;
 
-__global__ void __launch_bounds__(kPlanThreads) batch_moe_plan_kernel(const int32_t* sel, int n_pairs, int E,
-                                                                      int topk, int32_t* off, int32_t* cnt,
+//
+// Only experts [e_first, e_first + E) are planned (group e - e_first); pairs
+// that selected other experts are left out (expert parallelism: another rank
+// owns them).
+__global__ void __launch_bounds__(kPlanThreads) batch_moe_plan_kernel(const int32_t* sel, int n_pairs, int e_first,
+                                                                      int E, int topk, int32_t* off, int32_t* cnt,
                                                                       int32_t* act_idx, int32_t* out_idx) {
   extern __shared__ int sh[];  // [E] counts, [E] next free index, [kPlanWarps][E] chunk counts
   int* c = sh;
@@ -1174,7 +1178,7 @@ __global__ void __launch_bounds__(kPlanThreads) batch_moe_plan_kernel(const int3
   for (int i = tid; i < kPlanWarps * E; i += blockDim.x) wc[i] = 0;
   __syncthreads();
   for (int j = tid; j < n_pairs; j += blockDim.x) {
-    const int e = sel[j];
+    const int e = sel[j] - e_first;
     if (e >= 0 && e < E) atomicAdd(&c[e], 1);
   }
   __syncthreads();
@@ -1193,7 +1197,7 @@ __global__ void __launch_bounds__(kPlanThreads) batch_moe_plan_kernel(const int3
   const unsigned lt = (1u << lane) - 1u;
   for (int base = 0; base < n_pairs; base += kPlanThreads) {
     const int j = base + tid;
-    const int e = j < n_pairs ? sel[j] : -1;
+    const int e = j < n_pairs ? sel[j] - e_first : -1;
     const bool valid = e >= 0 && e < E;
     const unsigned same = __match_any_sync(0xffffffffu, valid ? e : -1);
     const int in_warp = __popc(same & lt);
@@ -1215,6 +1219,28 @@ __global__ void __launch_bounds__(kPlanThreads) batch_moe_plan_kernel(const int3
       next[x] += add;
     }
     __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------- expert-parallel combine
+// h[b][r] += sum_i wts[b][i] * y_src[b*k+i][r], where y_src is the block that
+// the rank owning expert sel[b][i] returned (block = sel / per_rank, blocks
+// src_stride floats apart): the batch_combine arithmetic, in top-k order.
+__global__ void ep_combine_kernel(const float* y_recv, int64_t src_stride, int n_src, const int32_t* sel,
+                                  const float* wts, int topk, int D, int per_rank, float* h) {
+  const int b = blockIdx.x;
+  pdl_wait();
+  pdl_trigger();
+  const float* wb = wts + b * topk;
+  const int32_t* sb = sel + b * topk;
+  for (int r = blockIdx.y * blockDim.x + threadIdx.x; r < D; r += gridDim.y * blockDim.x) {
+    auto y = [&](int i) {
+      const int src = min(max(sb[i] / per_rank, 0), n_src - 1);
+      return y_recv[static_cast<int64_t>(src) * src_stride + (static_cast<int64_t>(b) * topk + i) * D + r];
+    };
+    float acc = __fmul_rn(y(0), wb[0]);
+    for (int i = 1; i < topk; ++i) acc = __fadd_rn(acc, __fmul_rn(y(i), wb[i]));
+    h[static_cast<int64_t>(b) * D + r] = __fadd_rn(h[static_cast<int64_t>(b) * D + r], acc);
   }
 }
 
@@ -1517,16 +1543,31 @@ extern "C" int nh_batch_router(const float* xn, const float* router, int n_seq, 
                                stream);
 }
 
-extern "C" int nh_batch_moe_plan(const int32_t* sel, int n_seq, int k, int n_expert, int32_t* off, int32_t* cnt,
-                                 int32_t* act_idx, int32_t* out_idx, void* stream) {
+extern "C" int nh_batch_moe_plan_range(const int32_t* sel, int n_seq, int k, int e_first, int n_expert,
+                                       int32_t* off, int32_t* cnt, int32_t* act_idx, int32_t* out_idx, void* stream) {
   if (sel == nullptr || off == nullptr || cnt == nullptr || act_idx == nullptr || out_idx == nullptr || n_seq <= 0 ||
-      k <= 0 || n_expert <= 0)
+      k <= 0 || n_expert <= 0 || e_first < 0)
     return NH_E_ARG;
   const int n_pairs = n_seq * k;
   const size_t smem = static_cast<size_t>(2 + kPlanWarps) * n_expert * sizeof(int);
   if (smem > 48 * 1024) return NH_E_CAPACITY;
   return launch_pdl(batch_moe_plan_kernel, dim3(1), dim3(kPlanThreads), smem, static_cast<cudaStream_t>(stream), sel,
-                    n_pairs, n_expert, k, off, cnt, act_idx, out_idx);
+                    n_pairs, e_first, n_expert, k, off, cnt, act_idx, out_idx);
+}
+
+extern "C" int nh_batch_moe_plan(const int32_t* sel, int n_seq, int k, int n_expert, int32_t* off, int32_t* cnt,
+                                 int32_t* act_idx, int32_t* out_idx, void* stream) {
+  return nh_batch_moe_plan_range(sel, n_seq, k, 0, n_expert, off, cnt, act_idx, out_idx, stream);
+}
+
+extern "C" int nh_ep_combine(const float* y_recv, int64_t src_stride, int n_src, const int32_t* sel, const float* wts,
+                             int n_seq, int k, int64_t n_embd, int experts_per_rank, float* h, void* stream) {
+  if (y_recv == nullptr || sel == nullptr || wts == nullptr || h == nullptr || n_seq <= 0 || k <= 0 || n_src <= 0 ||
+      experts_per_rank <= 0 || src_stride < static_cast<int64_t>(n_seq) * k * n_embd)
+    return NH_E_ARG;
+  return launch_pdl(ep_combine_kernel, dim3(n_seq, static_cast<unsigned>((n_embd + 255) / 256)), dim3(256), 0,
+                    static_cast<cudaStream_t>(stream), y_recv, src_stride, n_src, sel, wts, k,
+                    static_cast<int>(n_embd), experts_per_rank, h);
 }
 
 extern "C" int nh_batch_combine(const float* y, const float* wts, int n_seq, int k, int64_t n_embd, float* h,
