@@ -67,8 +67,8 @@ def measured_peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return {"hbm_gbs": d["hbm_gbs"], "source": "measured"}
-    return {"hbm_gbs": 6650.0, "source": "fallback"}
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d.get("bf16_tflops", 1590.0), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
 def traffic_summary(kernel: str) -> float | None:
@@ -294,6 +294,68 @@ def run_batched(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_prefill(args) -> None:
+    """Prompt prefill + decode (the configuration-4 workload on one GPU): 8
+    sequences of 4096 seeded random ids, each through GreedyGenerateCached
+    with 64 greedy ids.  The prompt runs as one batched prefill (grouped
+    expert products, causal prefill attention), then batch-1 decode steps.
+    Device-timed parts; value = prefill tokens/s."""
+    import torch
+
+    import nuthatch_b200 as nh
+    from nuthatch_b200 import build, synth
+    from nuthatch_b200._lib import lib
+
+    build.build_product()
+    torch.cuda.set_device(0)
+    path = str(synth.cached(synth.OLMOE_1B7B))
+    m = nh.OlmoeModel.Load(path)
+    cfg = m.config()
+    n_seq, n_prompt, n_pred = args.prefill_seqs, args.prefill_tokens, args.prefill_decode
+    prompts = np.random.default_rng(4).integers(0, cfg.n_vocab, (n_seq, n_prompt), dtype=np.int32)
+    L = lib()
+    out = np.zeros(n_pred, dtype=np.int32)
+    pf, dc = C.c_double(0), C.c_double(0)
+
+    def one(p):
+        pc = np.ascontiguousarray(p)
+        assert L.nh_generate_timed(m._h, pc.ctypes.data_as(C.POINTER(C.c_int32)), pc.size, n_pred, 0,
+                                   out.ctypes.data_as(C.POINTER(C.c_int32)), C.byref(pf), C.byref(dc)) == 0
+        return pf.value, dc.value, out.tolist()
+
+    one(prompts[0][:600])  # warm-up: buffers, kernel attributes, graphs
+    clocks = ClockSampler(0)
+    pre_ms = dec_ms = 0.0
+    ids = []
+    for b in range(n_seq):
+        a, d, t = one(prompts[b])
+        pre_ms += a
+        dec_ms += d
+        ids.append(t)
+    clk = clocks.stop()
+    n_pre = n_seq * (n_prompt - 1)
+    # Per prefill token: 2 x active parameters (attention 4 d^2, router d E,
+    # 8 experts x 3 d F, per layer) + causal attention 4 x (p+1) x d per layer.
+    active = cfg.n_layers * (4 * cfg.n_embd ** 2 + cfg.n_embd * cfg.n_expert +
+                             cfg.n_expert_used * 3 * cfg.n_embd * cfg.n_ff)
+    attn = cfg.n_layers * 4 * cfg.n_embd * (n_prompt / 2.0)
+    flops = n_pre * (2 * active + attn)
+    peaks = measured_peaks()
+    tflops = flops / (pre_ms / 1000.0) / 1e12
+    line = {"metric": f"OLMoE Q4_K_M prompt prefill tok/s ({n_seq} x {n_prompt} tokens) + decode",
+            "value": n_pre / (pre_ms / 1000.0), "unit": "tok/s", "n_gpus": 1, "steps": n_seq, "warmup": 1,
+            "ms_per_step": pre_ms / n_seq, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "q4k/q6k x q8k int dot, f32 accumulate, f32 KV",
+            "data": "synthetic (seeded random-init GGUF of the OLMoE-1B-7B shape, seeded random-id prompts)",
+            "config": {"workload": f"olmoe-1b7b-q4km-prefill ({n_seq} x {n_prompt} prompt, {n_pred} greedy ids)",
+                       "parallelism": "single GPU", "step": "one sequence's prompt prefill"},
+            "clocks": clk, "decode_tok_s": n_seq * n_pred / (dec_ms / 1000.0),
+            "prefill_roofline": {"bound": "tensor", "flops": flops, "achieved": tflops,
+                                 "peak": peaks.get("bf16_tflops"), "unit": "TFLOP/s",
+                                 "note": "int8 tensor-core products against the measured bf16 dense peak"}}
+    print(json.dumps(line), flush=True)
+
+
 def run_ep_batched(args, dist, rank: int, world: int, local_rank: int, path: str, full_model) -> dict | None:
     """Expert-parallel batched decode (the configuration-3 workload: bs64,
     2048-token seeded contexts, 128 greedy steps) over the `world` GPUs of
@@ -364,17 +426,23 @@ def main() -> None:
                     help="prefill, warm-up, then exactly one timed-step's decode and exit (for ncu launch lists)")
     ap.add_argument("--profile-layers", type=int, default=0,
                     help="with --profile: the same OLMoE-1B-7B width cut to this many layers (small ncu captures)")
-    ap.add_argument("--workload", default="resident", choices=["resident", "streaming", "batched"])
+    ap.add_argument("--workload", default="resident", choices=["resident", "streaming", "batched", "prefill"])
     ap.add_argument("--batch-seqs", type=int, default=64)
     ap.add_argument("--batch-context", type=int, default=2048)
     ap.add_argument("--batch-steps", type=int, default=128)
     ap.add_argument("--budgets", type=int, nargs="*", default=[4, 8, 16, 32])
     ap.add_argument("--stream-tokens", type=int, default=256)
     ap.add_argument("--no-ep", action="store_true", help="skip the expert-parallel batched section")
+    ap.add_argument("--prefill-seqs", type=int, default=8)
+    ap.add_argument("--prefill-tokens", type=int, default=4096)
+    ap.add_argument("--prefill-decode", type=int, default=64)
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.workload == "batched":
         run_batched(args)
+        return
+    if args.workload == "prefill":
+        run_prefill(args)
         return
     if args.workload == "streaming":
         args.steps = min(args.steps, 3)

@@ -56,6 +56,12 @@ int nh_model_tensor(const void* model, const char* name, int64_t ne[4], int32_t*
 int nh_generate(void* model, int mode, const int32_t* prompt, int n_prompt, int n_predict, int norm_topk,
                 int use_graph, int32_t* out_tokens, int32_t* trace_sel, float* trace_gap, float* hidden,
                 float* logits);
+/* GreedyGenerateCached (mode 0 of nh_generate) with the device time of its
+ * two parts: the batched prefill of the prompt positions before the last
+ * (prefill_ms; 0 when the prompt ran position by position) and the batch-1
+ * steps from the last prompt position on (decode_ms).  Either may be NULL. */
+int nh_generate_timed(void* model, const int32_t* prompt, int n_prompt, int n_predict, int norm_topk,
+                      int32_t* out_tokens, double* prefill_ms, double* decode_ms);
 /* Kernel launches per decode step of this model. */
 int nh_generate_launches(const void* model);
 

@@ -27,6 +27,10 @@ struct GenerateOptions {
   std::vector<float>* hidden = nullptr;     // per step, per layer h after the MoE residual [n_predict][L][d]
   std::vector<float>* logits = nullptr;     // per step logits [n_predict][V]
   int status = 0;                            // NH_OK or the first error code
+  // Out, when timed: device time (CUDA events on the decode stream) of the
+  // batched prompt prefill and of the batch-1 steps after it.
+  bool timed = false;
+  double prefill_ms = 0, decode_ms = 0;
 };
 
 // Full recompute of the sequence every step (generate.cc:10-53).

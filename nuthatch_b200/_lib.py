@@ -52,6 +52,8 @@ SIGNATURES = {
     "nh_generate_launches": (C.c_int, [vp]),
     "nh_generate_batch": (C.c_int, [vp, P(i32), C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, P(i32),
                                     P(C.c_double)]),
+    "nh_generate_timed": (C.c_int, [vp, P(i32), C.c_int, C.c_int, C.c_int, P(i32), P(C.c_double),
+                                    P(C.c_double)]),
     "nh_ep_new_id": (C.c_int, [vp]),
     "nh_ep_create": (vp, [vp, C.c_int, C.c_int]),
     "nh_ep_free": (None, [vp]),

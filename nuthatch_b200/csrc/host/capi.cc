@@ -145,6 +145,25 @@ int nh_generate(void* model, int mode, const int32_t* prompt, int n_prompt, int 
   return NH_OK;
 }
 
+int nh_generate_timed(void* model, const int32_t* prompt, int n_prompt, int n_predict, int norm_topk,
+                      int32_t* out_tokens, double* prefill_ms, double* decode_ms) {
+  if (model == nullptr || prompt == nullptr || out_tokens == nullptr || n_prompt <= 0 || n_predict <= 0)
+    return NH_E_ARG;
+  GenerateOptions o;
+  o.timed = true;
+  std::vector<int32_t> ids(prompt, prompt + n_prompt);
+  const std::vector<int32_t> out =
+      GreedyGenerateCachedEx(*static_cast<OlmoeModel*>(model), ids, n_predict, norm_topk != 0, &o);
+  if (o.status != NH_OK) {
+    SetErr("GreedyGenerateCached failed");
+    return o.status;
+  }
+  std::memcpy(out_tokens, out.data(), out.size() * 4);
+  if (prefill_ms != nullptr) *prefill_ms = o.prefill_ms;
+  if (decode_ms != nullptr) *decode_ms = o.decode_ms;
+  return NH_OK;
+}
+
 int nh_generate_launches(const void* model) {
   if (model == nullptr) return NH_E_ARG;
   // The count the last resident step enqueued (four or six kernels per

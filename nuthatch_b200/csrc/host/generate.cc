@@ -52,9 +52,24 @@ std::vector<int32_t> GreedyGenerateCachedEx(const OlmoeModel& model, const std::
   // per step; the ids are the same either way.
   const int start = P > 1 && PrefillEnabled() && Engine::PrefillSupported(ws->view) ? P - 1 : 0;
   if (rc == NH_OK) rc = e.Begin(ids.data(), P, n_predict, start);
+  cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
+  if (o.timed)
+    for (cudaEvent_t& x : ev) cudaEventCreate(&x);
+  if (o.timed) cudaEventRecord(ev[0], e.stream());
   if (rc == NH_OK && start > 0) rc = e.Prefill(ws->view, start, norm_topk, trace);
+  if (o.timed) cudaEventRecord(ev[1], e.stream());
   const int steps = P + n_predict - 1;
   if (rc == NH_OK) rc = e.RunSteps(ws->view, steps - start, norm_topk, trace, dumps, o.use_graph);
+  if (o.timed) {
+    cudaEventRecord(ev[2], e.stream());
+    float a = 0.f, b = 0.f;
+    if (cudaEventSynchronize(ev[2]) == cudaSuccess && cudaEventElapsedTime(&a, ev[0], ev[1]) == cudaSuccess &&
+        cudaEventElapsedTime(&b, ev[1], ev[2]) == cudaSuccess) {
+      o.prefill_ms = a;
+      o.decode_ms = b;
+    }
+    for (cudaEvent_t x : ev) cudaEventDestroy(x);
+  }
   if (rc == NH_OK) rc = e.Finish(n_predict, &out);
   if (rc != NH_OK) {
     o.status = rc;

@@ -369,11 +369,14 @@ float DotQ4K(const uint8_t* w, const Q8K* y, int64_t n) {
     for (int j = 0; j < 8; ++j) {
       int sc, m;
       Q4KScaleMin(blk + 4, j, &sc, &m);
-      const int c = j / 2, hi = j % 2;
+      const int c = j / 2;
+      const uint8_t* qc = qs + 32 * c;
+      const int8_t* yq = y[b].qs + 32 * j;
       int32_t s = 0;
-      for (int l = 0; l < 32; ++l) {
-        const int q = hi ? (qs[32 * c + l] >> 4) : (qs[32 * c + l] & 15);
-        s += q * y[b].qs[32 * j + l];
+      if (j % 2 != 0) {
+        for (int l = 0; l < 32; ++l) s += (qc[l] >> 4) * yq[l];
+      } else {
+        for (int l = 0; l < 32; ++l) s += (qc[l] & 15) * yq[l];
       }
       sumi += sc * s;
       summ += m * (y[b].bsums[2 * j] + y[b].bsums[2 * j + 1]);
