@@ -133,6 +133,13 @@ int64_t nh_replay(int kind, uint32_t n_layers, uint32_t n_expert, int64_t n_reco
 int nh_sweep_budgets(uint32_t n_layers, uint32_t n_expert, int64_t n_records, const uint32_t* layer,
                      const int64_t* offsets, const uint32_t* experts, const uint32_t* budgets, int n_budgets,
                      double* out);
+/* SweepBudgetsCalibrated (no reference counterpart; the out-of-sample form):
+ * learned pin's usage histogram from the calibration trace (cal_*), every
+ * policy replaying the evaluation trace; out as nh_sweep_budgets. */
+int nh_sweep_budgets_calibrated(uint32_t n_layers, uint32_t n_expert, int64_t cal_records, const uint32_t* cal_layer,
+                                const int64_t* cal_offsets, const uint32_t* cal_experts, int64_t n_records,
+                                const uint32_t* layer, const int64_t* offsets, const uint32_t* experts,
+                                const uint32_t* budgets, int n_budgets, double* out);
 /* SweepPinRatio (trace_sweep.cc:36-50): out[pin] = learned hit rate. */
 int nh_sweep_pin_ratio(uint32_t n_layers, uint32_t n_expert, int64_t n_records, const uint32_t* layer,
                        const int64_t* offsets, const uint32_t* experts, uint32_t budget, double* out);
@@ -151,6 +158,10 @@ void* nh_expert_reader_open(const char* gguf_path);
 void nh_expert_reader_free(void* reader);
 uint64_t nh_expert_reader_bytes(const void* reader, const char* tensor);
 int nh_expert_reader_read(const void* reader, const char* tensor, int expert, void* out);
+/* Host-side fault injection for tests (no reference counterpart): after n more
+ * successful expert reads every read of this reader fails as a short read
+ * would; n < 0 turns it off (ExpertReader::FailReadsAfter). */
+int nh_expert_reader_fail_after(void* reader, int64_t n);
 
 /* ExpertSlotCache (expert_slot_cache.cc:7-104) over a reader; policy as in
  * nh_stream_generate.  ensure: writes the slot of each of the n ids. */

@@ -279,8 +279,26 @@ typedef struct NhGroupedRowDot {
   float* out;
   int64_t out_stride;
   int32_t mode;
+  int32_t engine;  /* NH_ROWDOT_ENGINE_*: which implementation (all give identical results) */
+  int32_t* err;    /* optional: NH_E_TIMEOUT is recorded here if a bounded device wait expires */
 } NhGroupedRowDot;
+#define NH_ROWDOT_ENGINE_AUTO 0  /* tensor cores (tcgen05) for Q4_K at >= 128 tokens, else mma.sync */
+#define NH_ROWDOT_ENGINE_DP4A 1  /* CUDA-core integer dots */
+#define NH_ROWDOT_ENGINE_MMA 2   /* mma.sync m16n8k32 / m16n8k16 int8, accumulators in registers */
+#define NH_ROWDOT_ENGINE_TC 3    /* tcgen05.mma kind::i8, accumulators in tensor memory (Q4_K only) */
 int nh_batch_rowdot(const NhGroupedRowDot* g, void* stream);
+
+/* The tcgen05 form directly (ggml_mul_mat_id on the 5th-generation tensor
+ * cores): Q4_K weights (both matrices for SwiGLU), n a power-of-two multiple
+ * of 256 up to 2048, 16-byte aligned weights, strides and Q8 rows.  One 32-value
+ * sub-block per kind::i8 MMA into its own tensor-memory accumulator, scales
+ * applied in registers in the row-dot order: results identical to the other
+ * engines.  NH_E_TYPE / NH_E_ARG (nothing launched) outside that.  A CTA owns
+ * 128 rows x 32 tokens of one group; grid (groups x row tiles, max_tokens/32). */
+int nh_batch_rowdot_tc(const NhGroupedRowDot* g, void* stream);
+/* 1 unless the environment sets NH_TC=0 (read once): whether
+ * NH_ROWDOT_ENGINE_AUTO may pick the tensor-core form. */
+int nh_tc_enabled(void);
 
 /* Per sequence: QK-norm over the full q/k width, NEOX RoPE at state->pos,
  * rotated q into qr [n_seq][n_head*head_dim], and the new K/V rows appended to

@@ -21,7 +21,7 @@ __all__ = ["OlmoeConfig", "OlmoeModel", "StreamingModel", "GreedyGenerate", "Gre
            "GreedyGenerateCachedTrace", "StreamingGenerate", "generate_ex", "streaming_generate_ex",
            "RoutingRecord", "RoutingTrace", "WriteRoutingTrace", "ReadRoutingTrace", "ReadRoutingTraceText",
            "ReplayStats", "LruPolicy", "OsPageCachePolicy", "LearnedPinPolicy", "BuildUsage", "Replay",
-           "SweepBudgets", "SweepPinRatio", "ExpertReader", "ExpertSlotCache", "NhError", "ExpertGroup"]
+           "SweepBudgets", "SweepBudgetsCalibrated", "SweepPinRatio", "ExpertReader", "ExpertSlotCache", "NhError", "ExpertGroup"]
 
 
 class NhError(RuntimeError):
@@ -442,6 +442,24 @@ def SweepBudgets(trace: RoutingTrace, budgets: Sequence[int]) -> list[tuple]:
     return [(kept[i], out[3 * i], out[3 * i + 1], out[3 * i + 2]) for i in range(n)]
 
 
+def SweepBudgetsCalibrated(calibration: RoutingTrace, trace: RoutingTrace, budgets: Sequence[int]) -> list[tuple]:
+    """Out-of-sample sweep: learned pin's usage from `calibration` (e.g. a
+    trace written by an earlier run and read back), every policy replaying
+    `trace`; rows (budget, learned, lru, os) as SweepBudgets."""
+    _, cl, co, ce = calibration.flat()
+    _, layer, offsets, experts = trace.flat()
+    b = np.asarray(budgets, dtype=np.uint32)
+    out = np.zeros(3 * max(len(b), 1), dtype=np.float64)
+    n = lib().nh_sweep_budgets_calibrated(
+        trace.n_layers, trace.n_expert, len(calibration.records), _ptr(cl, C.c_uint32), _ptr(co, C.c_int64),
+        _ptr(ce, C.c_uint32), len(trace.records), _ptr(layer, C.c_uint32), _ptr(offsets, C.c_int64),
+        _ptr(experts, C.c_uint32), _ptr(b, C.c_uint32), len(b), _ptr(out, C.c_double))
+    if n < 0:
+        raise NhError(f"nh_sweep_budgets_calibrated failed with code {n}")
+    kept = [x for x in budgets if x != 0]
+    return [(kept[i], out[3 * i], out[3 * i + 1], out[3 * i + 2]) for i in range(n)]
+
+
 def SweepPinRatio(trace: RoutingTrace, budget: int) -> list[tuple]:
     token, layer, offsets, experts = trace.flat()
     out = np.zeros(budget + 1, dtype=np.float64)
@@ -474,6 +492,11 @@ class ExpertReader:
         if lib().nh_expert_reader_read(self._h, name.encode(), idx, buf) != 0:
             return None
         return buf.raw
+
+    def FailReadsAfter(self, n: int) -> None:
+        """Host-side fault injection for tests: after n more successful reads
+        every read fails as a short read would; n < 0 turns it off."""
+        _check(lib().nh_expert_reader_fail_after(self._h, int(n)), "nh_expert_reader_fail_after")
 
     def __del__(self):
         try:

@@ -75,12 +75,15 @@ SIGNATURES = {
     "nh_replay": (i64, [C.c_int, u32, u32, i64, P(u32), P(i64), P(u32), u32, u32, P(u64), P(i64)]),
     "nh_sweep_budgets": (C.c_int, [u32, u32, i64, P(u32), P(i64), P(u32), P(u32), C.c_int, P(C.c_double)]),
     "nh_sweep_pin_ratio": (C.c_int, [u32, u32, i64, P(u32), P(i64), P(u32), u32, P(C.c_double)]),
+    "nh_sweep_budgets_calibrated": (C.c_int, [u32, u32, i64, P(u32), P(i64), P(u32), i64, P(u32), P(i64), P(u32),
+                                              P(u32), C.c_int, P(C.c_double)]),
     "nh_trace_write": (C.c_int, [cp, u32, u32, i64, P(u32), P(u32), P(i64), P(u32)]),
     "nh_trace_read": (i64, [cp, C.c_int, P(u32), P(u32), P(i64), i64, i64, P(u32), P(u32), P(i64), P(u32)]),
     "nh_expert_reader_open": (vp, [cp]),
     "nh_expert_reader_free": (None, [vp]),
     "nh_expert_reader_bytes": (u64, [vp, cp]),
     "nh_expert_reader_read": (C.c_int, [vp, cp, C.c_int, vp]),
+    "nh_expert_reader_fail_after": (C.c_int, [vp, i64]),
     "nh_slot_cache_create": (vp, [P(NhConfig), C.c_int, C.c_int, vp, C.c_int, C.c_int, P(u64)]),
     "nh_slot_cache_free": (None, [vp]),
     "nh_slot_cache_ensure": (C.c_int, [vp, P(i32), C.c_int, P(i32)]),

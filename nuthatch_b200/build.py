@@ -96,14 +96,14 @@ def build_checker(verbose: bool = False) -> None:
     # The same g++ as the product (libstdc++ linked as a shared library): a
     # checker with its own static copy misbehaves once the process has also
     # loaded the shared libstdc++ (numpy and torch do).
-    _run(["make", "-s", "-C", str(ROOT / "oracle"), "CXX=g++"])
+    _run(["make", "-s", "-C", str(ROOT / "oracle"), "ORACLE_CXX=g++"])
     # oracle/_ref is built only where the reference checkout is named by the
     # NUTHATCH_REFERENCE environment variable; the tests that use it skip
     # when it has not been built.
     ref_env = os.environ.get("NUTHATCH_REFERENCE", "")
     ref = Path(ref_env) if ref_env else None
     if ref is not None and (ref / "src" / "cache" / "cache_policy.cc").exists():
-        _run(["make", "-s", "-C", str(ROOT / "oracle"), "ref", f"REF={ref}", "CXX=g++"])
+        _run(["make", "-s", "-C", str(ROOT / "oracle"), "ref", f"REF={ref}", "ORACLE_CXX=g++"])
     if verbose:
         print("built oracle")
 

@@ -366,6 +366,25 @@ int nh_sweep_budgets(uint32_t n_layers, uint32_t n_expert, int64_t n_records, co
   return static_cast<int>(rows.size());
 }
 
+int nh_sweep_budgets_calibrated(uint32_t n_layers, uint32_t n_expert, int64_t cal_records, const uint32_t* cal_layer,
+                                const int64_t* cal_offsets, const uint32_t* cal_experts, int64_t n_records,
+                                const uint32_t* layer, const int64_t* offsets, const uint32_t* experts,
+                                const uint32_t* budgets, int n_budgets, double* out) {
+  if ((cal_records > 0 && (cal_layer == nullptr || cal_offsets == nullptr)) ||
+      (n_records > 0 && (layer == nullptr || offsets == nullptr)) || (n_budgets > 0 && budgets == nullptr) ||
+      out == nullptr)
+    return NH_E_ARG;
+  const RoutingTrace cal = MakeTrace(n_layers, n_expert, cal_records, nullptr, cal_layer, cal_offsets, cal_experts);
+  const RoutingTrace t = MakeTrace(n_layers, n_expert, n_records, nullptr, layer, offsets, experts);
+  const auto rows = SweepBudgetsCalibrated(cal, t, std::vector<uint32_t>(budgets, budgets + n_budgets));
+  for (size_t i = 0; i < rows.size(); ++i) {
+    out[3 * i] = rows[i].learned;
+    out[3 * i + 1] = rows[i].lru;
+    out[3 * i + 2] = rows[i].os;
+  }
+  return static_cast<int>(rows.size());
+}
+
 int nh_sweep_pin_ratio(uint32_t n_layers, uint32_t n_expert, int64_t n_records, const uint32_t* layer,
                        const int64_t* offsets, const uint32_t* experts, uint32_t budget, double* out) {
   const RoutingTrace t = MakeTrace(n_layers, n_expert, n_records, nullptr, layer, offsets, experts);
@@ -465,6 +484,12 @@ int nh_slot_cache_ensure(void* cache, const int32_t* ids, int n, int32_t* slots)
   if (h->cache->Commit(h->stream) != NH_OK || cudaStreamSynchronize(h->stream) != cudaSuccess) return NH_E_CUDA;
   if (slots != nullptr)
     for (int i = 0; i < n; ++i) slots[i] = m[ids[i]];
+  return NH_OK;
+}
+
+int nh_expert_reader_fail_after(void* reader, int64_t n) {
+  if (reader == nullptr) return NH_E_ARG;
+  static_cast<ExpertReader*>(reader)->FailReadsAfter(n);
   return NH_OK;
 }
 

@@ -143,6 +143,7 @@ int Engine::Prefill(const ModelView& m, int n_tok, bool norm_topk, bool trace) {
       g.out = out;
       g.out_stride = stride;
       g.mode = mode;
+      g.err = &state_->error;
       return nh_batch_rowdot(&g, s);
     };
     NH_PF_TRY(nh_prefill_embed(prompt_ + p0, T, m.embd, m.te, d, c.n_vocab, b.h, &state_->error, s));
@@ -184,6 +185,7 @@ int Engine::Prefill(const ModelView& m, int n_tok, bool norm_topk, bool trace) {
       g.out = b.ff;
       g.out_stride = F;
       g.mode = NH_ROWDOT_SWIGLU;
+      g.err = &state_->error;
       NH_PF_TRY(nh_batch_rowdot(&g, s));
       NH_PF_TRY(nh_batch_prep(b.ff, F, static_cast<int64_t>(T) * K, nullptr, eps, 0, F, b.q8ff, nullptr, s));
       std::memset(&g, 0, sizeof(g));
@@ -203,6 +205,7 @@ int Engine::Prefill(const ModelView& m, int n_tok, bool norm_topk, bool trace) {
       g.out = b.y;
       g.out_stride = d;
       g.mode = NH_ROWDOT_STORE;
+      g.err = &state_->error;
       NH_PF_TRY(nh_batch_rowdot(&g, s));
       NH_PF_TRY(nh_batch_combine(b.y, b.wts, T, K, d, b.h, s));
     }

@@ -1333,9 +1333,22 @@ extern "C" int nh_batch_prep(const float* x, int64_t x_stride, int64_t rows, con
                     static_cast<uint8_t*>(q8), xn);
 }
 
+// Products of at least this many tokens per call go to the tensor-core form
+// (below it the per-CTA token tiles would be mostly empty).
+constexpr int kTcMinTokens = 128;
+
 extern "C" int nh_batch_rowdot(const NhGroupedRowDot* g, void* stream) {
   if (g == nullptr || g->w == nullptr || g->q8 == nullptr || g->out == nullptr || g->rows <= 0 || g->n_groups <= 0)
     return NH_E_ARG;
+  const int eng = g->engine;
+  if (eng < NH_ROWDOT_ENGINE_AUTO || eng > NH_ROWDOT_ENGINE_TC) return NH_E_ARG;
+  if (eng == NH_ROWDOT_ENGINE_TC ||
+      (eng == NH_ROWDOT_ENGINE_AUTO && nh_tc_enabled() && g->max_tokens >= kTcMinTokens)) {
+    const int rc = nh_batch_rowdot_tc(g, stream);
+    // Outside the tensor-core form's types and shapes (it launched nothing),
+    // the automatic choice falls back to the forms below.
+    if (rc == NH_OK || eng == NH_ROWDOT_ENGINE_TC || (rc != NH_E_TYPE && rc != NH_E_ARG)) return rc;
+  }
   if (!rowdot3_k_ok(static_cast<int>(g->n))) return NH_E_ARG;
   for (int32_t t : {g->type, g->type2})
     if (t != NH_TYPE_Q4_K && t != NH_TYPE_Q6_K) return NH_E_TYPE;
@@ -1382,7 +1395,7 @@ extern "C" int nh_batch_rowdot(const NhGroupedRowDot* g, void* stream) {
   while (p.tok_tile > 8 && static_cast<int64_t>(p.n_groups) * p.row_blocks * ((max_tok + p.tok_tile - 1) / p.tok_tile) <
                                4 * sms)
     p.tok_tile >>= 1;
-  if (batch_mma_enabled()) {
+  if (eng == NH_ROWDOT_ENGINE_MMA || (eng == NH_ROWDOT_ENGINE_AUTO && batch_mma_enabled())) {
     // Tensor-core form: one warp per 16-row tile; ungrouped products also
     // split their token tiles over grid.y to fill the GPU.
     const int row_tiles = (p.rows + 15) / 16;

@@ -221,6 +221,21 @@ def replay(kind: int, records, n_layers: int, n_expert: int, a: int, b: int = 0,
     return int(hits), int(acc.value)
 
 
+def ref_replay_pin_usage(records, n_layers: int, n_expert: int, pin: int, lru: int, usage) -> tuple[int, int]:
+    """The reference's compiled LearnedPinPolicy(pin, lru) over the records with
+    a given usage histogram (dense [n_layers][n_expert] counts): (hits, accesses)."""
+    layer, offsets, experts = flat_trace(records, n_layers)
+    u = np.ascontiguousarray(np.asarray(usage, dtype=np.uint64).reshape(n_layers, n_expert))
+    acc = C.c_int64()
+    fn = rlib().ref_replay_pin_usage
+    fn.restype = C.c_int64
+    fn.argtypes = [C.c_uint32, C.c_uint32, C.c_int64, P(C.c_uint32), P(C.c_int64), P(C.c_uint32), C.c_uint32,
+                   C.c_uint32, P(C.c_uint64), P(C.c_int64)]
+    hits = fn(n_layers, n_expert, len(records), _ptr(layer, C.c_uint32), _ptr(offsets, C.c_int64),
+              _ptr(experts, C.c_uint32), pin, lru, _ptr(u, C.c_uint64), C.byref(acc))
+    return int(hits), int(acc.value)
+
+
 def ref_sweep_budgets(records, n_layers, n_expert, budgets):
     layer, offsets, experts = flat_trace(records, n_layers)
     b = np.asarray(budgets, dtype=np.uint32)

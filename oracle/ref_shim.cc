@@ -61,6 +61,25 @@ int64_t ref_replay(int kind, uint32_t n_layers, uint32_t n_expert, int64_t n_rec
   return static_cast<int64_t>(s.hits);
 }
 
+// LearnedPinPolicy(n_layers, pin, lru, usage) with the usage histogram given
+// as dense counts usage[n_layers][n_expert] (a calibration run's, not the
+// replayed trace's).  Returns hits, *accesses set.
+int64_t ref_replay_pin_usage(uint32_t n_layers, uint32_t n_expert, int64_t n_records, const uint32_t* layer,
+                             const int64_t* offsets, const uint32_t* experts, uint32_t pin, uint32_t lru,
+                             const uint64_t* usage, int64_t* accesses) {
+  const nuthatch::RoutingTrace t =
+      MakeTrace(n_layers, n_expert, n_records, nullptr, layer, offsets, experts);
+  nuthatch::UsageHistogram u;
+  u.per_layer.resize(n_layers);
+  for (uint32_t l = 0; l < n_layers; ++l)
+    for (uint32_t e = 0; e < n_expert; ++e)
+      if (usage[static_cast<size_t>(l) * n_expert + e] != 0) u.per_layer[l][e] = usage[static_cast<size_t>(l) * n_expert + e];
+  nuthatch::LearnedPinPolicy p(n_layers, pin, lru, u);
+  const nuthatch::ReplayStats s = nuthatch::Replay(t, &p);
+  *accesses = static_cast<int64_t>(s.accesses);
+  return static_cast<int64_t>(s.hits);
+}
+
 // SweepBudgets: out rows of (learned, lru, os) hit rates, one per budget.
 int ref_sweep_budgets(uint32_t n_layers, uint32_t n_expert, int64_t n_records,
                       const uint32_t* layer, const int64_t* offsets, const uint32_t* experts,

@@ -83,6 +83,32 @@ def assert_token_parity(gpu_tokens, ora: dict, n_prompt: int):
     assert gaps and min(gaps) < NEAR_TIE, f"greedy ids diverge at step {s} without a near-tie: {g} vs {o} {gaps}"
 
 
+def agreeing_steps(gpu_tokens, ora_tokens) -> int:
+    """Generated steps whose inputs agree: every step up to and including the
+    first one whose chosen id differs (its hidden states and logits were
+    formed from the same ids), or all of them."""
+    for i, (a, b) in enumerate(zip(gpu_tokens, ora_tokens)):
+        if a != b:
+            return i + 1
+    return len(ora_tokens)
+
+
+def assert_prefix_parity(g: dict, ora: dict, n_prompt: int, per_layer: bool = False):
+    """Hidden states, logits and routing records over the agreeing steps
+    (all of them unless the ids diverge at a near-tie)."""
+    s = agreeing_steps(g["tokens"], ora["tokens"])
+    if per_layer:
+        for l in range(g["hidden"].shape[1]):
+            assert_matches(g["hidden"][:s, l], ora["hidden"][:s, l], f"layer {l}")
+    else:
+        assert_matches(g["hidden"][:s], ora["hidden"][:s])
+    if "logits" in g and "logits" in ora:
+        assert_matches(g["logits"][:s], ora["logits"][:s])
+    if "sel" in g and "sel" in ora:
+        n_tok = n_prompt + s - 1  # processed tokens whose inputs agree
+        assert_trace_parity(g["sel"][:n_tok], ora["sel"][:n_tok], ora["gap"][:n_tok])
+
+
 def assert_trace_parity(g_sel, o_sel, o_gap):
     """Routing records (ids in descending probability) are bit-exact wherever the
     oracle's top-(k+1) has no adjacent gap below NEAR_TIE."""
@@ -183,10 +209,7 @@ def test_mini_generate_matches_oracle(gpu, mini_models, norm_topk):
     ora = om.generate(prompt, n, norm_topk=norm_topk, mode=0, trace=True, hidden=True, logits=True)
     g = nh.generate_ex(m, prompt, n, norm_topk, trace=True, hidden=True, logits=True)
     assert_token_parity(g["tokens"], ora, len(prompt))
-    if g["tokens"] == ora["tokens"]:
-        assert_matches(g["hidden"], ora["hidden"])
-        assert_matches(g["logits"], ora["logits"])
-        assert_trace_parity(g["sel"], ora["sel"], ora["gap"])
+    assert_prefix_parity(g, ora, len(prompt))
     # Graph replay and eager launches run the same kernels: identical bits.
     e = nh.generate_ex(m, prompt, n, norm_topk, use_graph=False, hidden=True)
     assert e["tokens"] == g["tokens"]
@@ -356,11 +379,7 @@ def test_olmoe_1b7b_resident_decode_matches_oracle(gpu, olmoe_path):
     ora = om.generate(prompt, 24, mode=0, trace=True, hidden=True, logits=True)
     g = nh.generate_ex(m, prompt, 24, False, trace=True, hidden=True, logits=True)
     assert_token_parity(g["tokens"], ora, len(prompt))
-    if g["tokens"] == ora["tokens"]:
-        for l in range(cfg.n_layers):
-            assert_matches(g["hidden"][:, l], ora["hidden"][:, l], f"layer {l}")
-        assert_matches(g["logits"], ora["logits"])
-        assert_trace_parity(g["sel"], ora["sel"], ora["gap"])
+    assert_prefix_parity(g, ora, len(prompt), per_layer=True)
 
 
 def test_olmoe_streaming_fresh_learned_pin_pools_match_resident(gpu, synth_dir):

@@ -120,6 +120,7 @@ def _run(path, out, prefill, n_prompt, n_predict, norm_topk):
     ("MINI_GQA", 40, 6, False, True),
     ("MINI", 700, 4, False, False),        # two prefill chunks (512 + 187 rows), eleven splits
     ("OLMOE_1B7B", 16, 24, False, True),   # the benchmark workload
+    ("OLMOE_1B7B", 300, 4, False, False),  # >= 128 rows: Q4_K products on tcgen05, Q6_K on mma.sync
 ])
 def test_generation_with_prefill_matches_position_by_position(gpu, synth_dir, tmp_path, spec_name, n_prompt,
                                                               n_predict, norm_topk, with_oracle):
