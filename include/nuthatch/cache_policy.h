@@ -107,6 +107,14 @@ struct SweepRow {
 };
 std::vector<SweepRow> SweepBudgets(const RoutingTrace& trace, const std::vector<uint32_t>& budgets);
 
+// The out-of-sample form of SweepBudgets (no reference counterpart; the
+// cross-input evaluation the reference's analysis calls for): learned pin
+// takes its usage histogram from `calibration` (e.g. a routing trace written
+// by an earlier run with WriteRoutingTrace and read back), and every policy
+// replays `eval`.  With calibration == eval it equals SweepBudgets.
+std::vector<SweepRow> SweepBudgetsCalibrated(const RoutingTrace& calibration, const RoutingTrace& eval,
+                                             const std::vector<uint32_t>& budgets);
+
 struct PinRatioRow {
   uint32_t pin;
   uint32_t lru;

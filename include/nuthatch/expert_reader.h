@@ -28,6 +28,12 @@ class ExpertReader {
   // Reads expert `expert_idx` of `tensor_name` into out (>= ExpertBytes bytes).
   bool ReadExpert(const std::string& tensor_name, int expert_idx, void* out) const;
 
+  // Host-side fault injection for tests (no reference counterpart): after n
+  // more successful ReadExpert calls every read fails as a short read would;
+  // n < 0 turns it off.  Lets the failure handling of the slot cache be tested
+  // without a failing disk.
+  void FailReadsAfter(int64_t n) const { fail_after_ = n; }
+
  private:
   struct Info {
     uint64_t file_offset;
@@ -39,6 +45,7 @@ class ExpertReader {
       : src_(std::move(src)), info_(std::move(info)) {}
   std::unique_ptr<TensorSource> src_;
   std::unordered_map<std::string, Info> info_;
+  mutable int64_t fail_after_ = -1;
 };
 
 }  // namespace nuthatch

@@ -82,7 +82,11 @@ class ExpertSlotCache {
   void Restart();
   // Event recorded after the last fill of the latest Ensure (cudaEvent_t).
   void* fills_done_event() const { return fill_event_; }
-  // false once a fill failed; the slot involved is left empty.
+  // false when a fill of the last Ensure failed (a read error or short read
+  // of the expert reader, or a copy that could not be enqueued); the slot
+  // involved is left empty and mapped to no expert, so a later Ensure of the
+  // same id misses and fills it again.  The reference ignores a failed read
+  // (expert_slot_cache.cc:96) and maps the slot regardless.
   bool ok() const { return ok_; }
 
   const DTensor* gate_slots() const { return &gate_; }  // [n_embd, n_ff, slots]

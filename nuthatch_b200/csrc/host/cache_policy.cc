@@ -105,7 +105,13 @@ bool LearnedPinPolicy::Access(uint32_t layer, uint32_t expert) {
 }
 
 std::vector<SweepRow> SweepBudgets(const RoutingTrace& trace, const std::vector<uint32_t>& budgets) {
-  const UsageHistogram usage = BuildUsage(trace);
+  return SweepBudgetsCalibrated(trace, trace, budgets);
+}
+
+std::vector<SweepRow> SweepBudgetsCalibrated(const RoutingTrace& calibration, const RoutingTrace& trace,
+                                             const std::vector<uint32_t>& budgets) {
+  UsageHistogram usage = BuildUsage(calibration);
+  usage.per_layer.resize(std::max<size_t>(usage.per_layer.size(), trace.n_layers));
   const auto rate = [&trace](CachePolicy&& p) { return Replay(trace, &p).hit_rate(); };
   std::vector<SweepRow> rows;
   for (uint32_t budget : budgets) {

@@ -278,6 +278,8 @@ bool ExpertReader::ReadExpert(const std::string& name, int expert_idx, void* out
   if (it == info_.end()) return false;
   const Info& in = it->second;
   if (expert_idx < 0 || expert_idx >= in.n_experts) return false;
+  if (fail_after_ == 0) return false;
+  if (fail_after_ > 0) --fail_after_;
   return src_->ReadAt(in.file_offset + static_cast<size_t>(expert_idx) * in.expert_bytes, in.expert_bytes, out);
 }
 

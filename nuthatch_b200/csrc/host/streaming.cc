@@ -185,6 +185,7 @@ int ExpertSlotCache::AcquireLru() {
 std::unordered_map<int, int> ExpertSlotCache::Ensure(const std::vector<int>& expert_ids) {
   std::unordered_map<int, int> result;
   pending_.clear();
+  ok_ = true;
   // Distinct non-pinned ids of this batch: when they fit in the LRU part no
   // access can evict an expert this batch still needs, and misses load
   // straight into their slot; otherwise they go through staging slots.
@@ -214,7 +215,13 @@ std::unordered_map<int, int> ExpertSlotCache::Ensure(const std::vector<int>& exp
     ++misses_;
     const int lru = AcquireLru();
     if (direct && lru >= 0) {
-      if (!Fill(lru, id)) ok_ = false;
+      if (!Fill(lru, id)) {
+        // A failed fill leaves the slot empty (AcquireLru already unmapped
+        // its previous expert), so no later request takes its bytes for id.
+        ok_ = false;
+        result[id] = lru;
+        continue;
+      }
       slot_to_id_[lru] = id;
       id_to_slot_[id] = lru;
       slot_tick_[lru] = ++tick_;
@@ -229,8 +236,11 @@ std::unordered_map<int, int> ExpertSlotCache::Ensure(const std::vector<int>& exp
       continue;
     }
     const int st = next_stage++;
-    if (!Fill(st, id)) ok_ = false;
     result[id] = st;
+    if (!Fill(st, id)) {
+      ok_ = false;  // the expert does not join the LRU part either
+      continue;
+    }
     if (lru >= 0) {
       slot_to_id_[lru] = id;
       id_to_slot_[id] = lru;

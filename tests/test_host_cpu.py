@@ -239,3 +239,28 @@ def test_moe_layer_declines_uncovered_shapes_before_any_launch():
     assert rc(router=fake + 4) == -1                       # router rows are bulk-copied
     assert rc(gate=fake + 8) == -1                         # Q4_K rows are read 16 bytes at a time
     assert lib().nh_moe_layer_scratch_bytes(64) >= 64 + 4 * 64
+
+
+def test_calibrated_sweep_persists_through_trace_files(tmp_path):
+    """The learned-pin calibration lifecycle: a calibration trace written with
+    WriteRoutingTrace and read back gives the same usage histogram; the
+    out-of-sample sweep with calibration == evaluation equals SweepBudgets,
+    and learned pin calibrated on another trace is scored on the evaluation
+    trace (LRU and OS columns do not depend on the calibration)."""
+    cal = _trace("zipf_l4_e64_k8")
+    L, E, recs = _random_trace(3, L=cal.n_layers, E=cal.n_expert, k=8, n_tok=150)
+    ev = nh.RoutingTrace(L, E, [nh.RoutingRecord(t, l, ex) for t, l, ex in recs])
+    path = tmp_path / "cal.bin"
+    assert nh.WriteRoutingTrace(cal, str(path))
+    back = nh.RoutingTrace()
+    assert nh.ReadRoutingTrace(str(path), back)
+    assert np.array_equal(nh.BuildUsage(back, E).counts, nh.BuildUsage(cal, E).counts)
+    budgets = [4, 8, 16]
+    assert nh.SweepBudgetsCalibrated(cal, cal, budgets) == nh.SweepBudgets(cal, budgets)
+    out = nh.SweepBudgetsCalibrated(back, ev, budgets)
+    ins = nh.SweepBudgets(ev, budgets)
+    assert [r[2:] for r in out] == [r[2:] for r in ins]
+    for (b, learned, _, _) in out:
+        pin = int(math.ceil(0.75 * b))
+        want = nh.Replay(ev, nh.LearnedPinPolicy(L, pin, b - pin, nh.BuildUsage(back, E))).hit_rate()
+        assert learned == pytest.approx(want, abs=0)
