@@ -120,6 +120,18 @@ int nh_stream_generate(void* model, const int32_t* prompt, int n_prompt, int n_p
                        int capacity, int policy, int pin_slots, const uint64_t* usage, int32_t* out_tokens,
                        int64_t* hits, int64_t* misses, uint64_t* h2d_bytes, int32_t* trace_sel);
 
+/* StreamingGenerateBatch (no reference counterpart): n_seq prompts of n_prompt
+ * ids decoded in lockstep with every layer's experts streamed through a slot
+ * pool of `capacity` (policy, pin_slots, usage as nh_stream_generate); layers
+ * whose batch selects more distinct experts than the pool holds run in waves.
+ * out_tokens [n_seq][n_predict]; hits/misses [n_layers] (per wave's Ensure);
+ * waves: slot-pool waves over all layers and steps; decode_ms: device time
+ * from the last prompt position on.  Optional outputs may be NULL. */
+int nh_stream_generate_batch(void* model, const int32_t* prompts, int n_seq, int n_prompt, int n_predict,
+                             int norm_topk, int capacity, int policy, int pin_slots, const uint64_t* usage,
+                             int32_t* out_tokens, int64_t* hits, int64_t* misses, uint64_t* h2d_bytes, int64_t* waves,
+                             double* decode_ms);
+
 /* Cache policies over a flat trace: record r has layer[r] and experts
  * experts[offsets[r]..offsets[r+1]).  kind 0 LruPolicy(n_layers, a)
  * (lru_policy.cc), 1 OsPageCachePolicy(a) (os_page_cache_policy.cc), 2

@@ -94,6 +94,10 @@ class ExpertSlotCache {
   const DTensor* down_slots() const { return &down_; }
 
   int capacity() const { return capacity_; }
+  // Slots of the LRU part (capacity minus the pinned experts): the most
+  // distinct unpinned experts one Ensure can hold without staging.
+  int lru_slots() const { return lru_slots_; }
+  bool is_pinned(int expert) const { return pinned_.count(expert) != 0; }
   int64_t hits() const { return hits_; }
   int64_t misses() const { return misses_; }
   uint64_t h2d_bytes() const { return h2d_bytes_; }

@@ -14,6 +14,7 @@
 
 #include "nuthatch/cache_policy.h"
 #include "nuthatch/expert_slot_cache.h"
+#include "nuthatch/generate.h"
 #include "nuthatch/routing_trace.h"
 #include "nuthatch/streaming_model.h"
 
@@ -24,6 +25,7 @@ struct StreamingStats {
   std::vector<int64_t> misses;  // per layer
   uint64_t h2d_bytes = 0;
   double fill_ms = 0;           // host time between phase A readback and phase B launch, summed
+  int64_t waves = 0;            // batched form: slot-pool waves over all layers and steps
   int status = 0;
 };
 
@@ -43,6 +45,25 @@ std::vector<int32_t> StreamingGenerate(const StreamingModel& model, std::vector<
 std::vector<int32_t> StreamingGenerateEx(const StreamingModel& model, const std::vector<int32_t>& ids,
                                          int n_predict, bool norm_topk, int capacity,
                                          const StreamingOptions& opt);
+
+// Batched streaming decode (no reference counterpart; the reference streams
+// one sequence and requires distinct(ids) <= capacity per layer,
+// expert_slot_cache.h:21).  B sequences of equal prompt length advance in
+// lockstep through the batched kernels while each layer's experts stream
+// through a slot pool of `capacity` slots (policy as in StreamingOptions).
+// When the batch selects more distinct experts than the pool holds, the layer
+// runs in waves: the distinct unpinned experts, in order of first selection,
+// lru_slots at a time, each wave made resident by one Ensure and its
+// (token, pick) products run before the next wave's fills; the top-k-order
+// combine follows the last wave.  Every sequence's ids equal the resident
+// batched decode.  Hits and misses count per Ensure of each wave (the
+// reference defines none for this case).  opt.trace is not filled; bopt gives
+// the decode device time (its ep must be null; the host decides every
+// layer's slots, so no CUDA graph is used).
+std::vector<std::vector<int32_t>> StreamingGenerateBatch(const StreamingModel& model,
+                                                         const std::vector<std::vector<int32_t>>& prompts,
+                                                         int n_predict, bool norm_topk, int capacity,
+                                                         const StreamingOptions& opt, BatchOptions* bopt = nullptr);
 
 }  // namespace nuthatch
 

@@ -320,6 +320,33 @@ def streaming_generate_ex(model: StreamingModel, ids: Sequence[int], n_predict: 
     return out
 
 
+def streaming_generate_batch_ex(model: StreamingModel, prompts: Sequence[Sequence[int]], n_predict: int,
+                                norm_topk: bool, capacity: int, *, policy: str = "lru", pin_slots: int = 0,
+                                usage: np.ndarray | None = None) -> dict:
+    """Batched streaming decode (StreamingGenerateBatch): ids per sequence,
+    per-layer hits/misses (one count per wave's Ensure), H2D bytes, the number
+    of slot-pool waves and the decode device time."""
+    cfg = model.config()
+    p = np.ascontiguousarray(np.asarray(prompts, dtype=np.int32))
+    if p.ndim != 2:
+        raise ValueError("prompts must all have the same length")
+    n_seq, n_prompt = p.shape
+    toks = np.zeros((n_seq, n_predict), dtype=np.int32)
+    hits = np.zeros(cfg.n_layers, dtype=np.int64)
+    misses = np.zeros(cfg.n_layers, dtype=np.int64)
+    h2d, waves, ms = C.c_uint64(0), C.c_int64(0), C.c_double(0)
+    u = None
+    if policy == "learned_pin":
+        u = np.ascontiguousarray(np.asarray(usage, dtype=np.uint64).reshape(cfg.n_layers, cfg.n_expert))
+    _check(lib().nh_stream_generate_batch(model._h, _ptr(p, C.c_int32), n_seq, n_prompt, n_predict, int(norm_topk),
+                                          capacity, 1 if policy == "learned_pin" else 0, pin_slots,
+                                          _ptr(u, C.c_uint64), _ptr(toks, C.c_int32), _ptr(hits, C.c_int64),
+                                          _ptr(misses, C.c_int64), C.byref(h2d), C.byref(waves), C.byref(ms)),
+           "nh_stream_generate_batch")
+    return {"tokens": toks.tolist(), "hits": hits, "misses": misses, "h2d_bytes": h2d.value, "waves": waves.value,
+            "decode_ms": ms.value}
+
+
 def StreamingGenerate(model: StreamingModel, ids: Sequence[int], n_predict: int, norm_topk: bool,
                       capacity: int) -> list[int]:
     """Two-phase streaming greedy decode with an LRU slot cache (streaming_forward.cc:228-253)."""

@@ -6,12 +6,19 @@
 // replayed.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstring>
+#include <unordered_map>
 
 #include "engine.h"
 #include "nccl_api.h"
 #include "nuthatch/expert_parallel.h"
+#include "nuthatch/expert_slot_cache.h"
+#include "nuthatch/streaming_forward.h"
+#include "nuthatch/streaming_model.h"
+#include "workspace.h"
 #include "nuthatch/generate.h"
 #include "nuthatch/gguf_file.h"
 
@@ -24,7 +31,9 @@ class BatchBuffers {
  public:
   ~BatchBuffers() {
     for (void* p : owned_) cudaFree(p);
+    for (void* p : host_owned_) cudaFreeHost(p);
     if (graph_ != nullptr) cudaGraphExecDestroy(graph_);
+    if (event_ != nullptr) cudaEventDestroy(event_);
     if (stream_ != nullptr) cudaStreamDestroy(stream_);
   }
   template <typename T>
@@ -37,12 +46,25 @@ class BatchBuffers {
     owned_.push_back(p);
     return static_cast<T*>(p);
   }
+  // Pinned host memory (freed with the buffers).
+  template <typename T>
+  T* HostAlloc(size_t count) {
+    void* p = nullptr;
+    if (cudaHostAlloc(&p, std::max<size_t>(count, 1) * sizeof(T), cudaHostAllocDefault) != cudaSuccess) {
+      ok_ = false;
+      return nullptr;
+    }
+    host_owned_.push_back(p);
+    return static_cast<T*>(p);
+  }
   bool ok_ = true;
   cudaStream_t stream_ = nullptr;
   cudaGraphExec_t graph_ = nullptr;
+  cudaEvent_t event_ = nullptr;
 
  private:
   std::vector<void*> owned_;
+  std::vector<void*> host_owned_;
 };
 
 // All-gather of every rank's Q8_K activation rows and top-k selections
@@ -78,55 +100,45 @@ int ReturnPicks(const ExpertGroup& ep, const float* y, size_t block, float* y_re
     if (rc_ != NH_OK) return rc_; \
   } while (0)
 
-}  // namespace
+// Prompts of equal, non-zero length with ids inside the vocabulary.
+int CheckPrompts(const std::vector<std::vector<int32_t>>& prompts, const OlmoeConfig& c) {
+  const size_t P = prompts[0].size();
+  for (const auto& p : prompts) {
+    if (p.size() != P || P == 0) return NH_E_ARG;
+    for (int32_t t : p)
+      if (t < 0 || static_cast<uint32_t>(t) >= c.n_vocab) return NH_E_ARG;
+  }
+  return NH_OK;
+}
 
-std::vector<std::vector<int32_t>> GreedyGenerateCachedBatch(const OlmoeModel& model,
-                                                            const std::vector<std::vector<int32_t>>& prompts,
-                                                            int n_predict, bool norm_topk, BatchOptions* opt) {
-  BatchOptions local;
-  BatchOptions& o = opt != nullptr ? *opt : local;
-  o.status = NH_OK;
+// Experts streamed through per-layer slot pools (the batched streaming form):
+// the caches, the stream their fills run on, and the wave statistics.
+struct StreamedExperts {
+  std::vector<ExpertSlotCache*> caches;
+  cudaStream_t copy_stream = nullptr;
+  int64_t waves = 0;      // out: slot-pool waves over all layers and steps
+  double host_ms = 0;     // out: host time spent in slot decisions and waits
+};
+
+int StreamedMoe(StreamedExperts& se, int l, const LayerView& Lv, const OlmoeConfig& c, int B, const int32_t* sel,
+                const float* wts, int32_t* sel_host, int32_t* plan_host, int32_t* off, int32_t* cnt,
+                int32_t* act_idx, int32_t* out_idx, const uint8_t* q8, float* ff, uint8_t* q8ff, float* y, float* h,
+                cudaEvent_t compute_done, cudaStream_t s);
+
+// The batched decode shared by the resident (and expert-parallel) form and the
+// streaming form: `se` null means the experts are resident in `m` (offset by
+// e_skip experts), else they are streamed through se's slot pools.
+std::vector<std::vector<int32_t>> RunBatch(const ModelView& m, const OlmoeConfig& c,
+                                           const std::vector<std::vector<int32_t>>& prompts, int n_predict,
+                                           bool norm_topk, BatchOptions& o, ExpertShard shard, uint64_t e_skip,
+                                           StreamedExperts* se) {
   std::vector<std::vector<int32_t>> out;
   const int B = static_cast<int>(prompts.size());
-  if (B == 0 || n_predict <= 0) return out;
   const int P = static_cast<int>(prompts[0].size());
-  const OlmoeConfig& c = model.config();
-  for (const auto& p : prompts) {
-    if (static_cast<int>(p.size()) != P || P == 0) {
-      o.status = NH_E_ARG;
-      return out;
-    }
-    for (int32_t t : p)
-      if (t < 0 || static_cast<uint32_t>(t) >= c.n_vocab) {
-        o.status = NH_E_ARG;
-        return out;
-      }
-  }
-  ModelView m;
-  if (!BuildView(model, true, &m)) {
-    o.status = NH_E_STATE;
-    return out;
-  }
   const int64_t d = c.n_embd, hd = c.head_dim(), dkv = static_cast<int64_t>(c.n_head_kv) * hd, F = c.n_ff,
                 E = c.n_expert, K = c.n_expert_used, V = c.n_vocab, L = c.n_layers;
-  // Expert parallelism: this rank owns experts [shard.first, +count) and the
-  // B sequences given here; all W ranks' tokens meet at every MoE layer.
   const ExpertGroup* ep = o.ep;
   const int W = ep != nullptr ? ep->world() : 1;
-  const ExpertShard shard = ep != nullptr ? ExpertShard::Of(c.n_expert, W, ep->rank()) : ExpertShard{0, c.n_expert};
-  if (ep != nullptr && (c.n_expert % W != 0 || !Nccl().ok)) {
-    o.status = NH_E_ARG;
-    return out;
-  }
-  // The expert weights of the owned shard: the model holds exactly the shard
-  // (its tensors start at expert shard.first) or all experts.
-  uint64_t e_skip = 0;
-  if (model.holds_all_experts()) {
-    e_skip = shard.first;
-  } else if (model.expert_first() != shard.first || model.expert_count() != shard.count) {
-    o.status = NH_E_STATE;
-    return out;
-  }
   const int max_seq = P + n_predict;
   const int BK = B * static_cast<int>(K);
   const int BW = B * W, BKW = BK * W;  // rows of every rank's tokens / picks
@@ -158,6 +170,16 @@ std::vector<std::vector<int32_t>> GreedyGenerateCachedBatch(const OlmoeModel& mo
   uint8_t* q8_all = W > 1 ? bb.Alloc<uint8_t>(q8_row * BW) : q8;
   int32_t* sel_all = W > 1 ? bb.Alloc<int32_t>(BKW) : sel;
   float* y_recv = W > 1 ? bb.Alloc<float>(static_cast<size_t>(BKW) * d) : y;
+  // Streaming: the selections read back per layer and the per-wave expert
+  // lists (up to one wave per expert), in pinned host memory.
+  int32_t* sel_host = nullptr;
+  int32_t* plan_host = nullptr;
+  if (se != nullptr) {
+    sel_host = bb.HostAlloc<int32_t>(BK);
+    plan_host = bb.HostAlloc<int32_t>(static_cast<size_t>(E) * (2 * E + 2 * BK));
+    if (cudaEventCreateWithFlags(&bb.event_, cudaEventDisableTiming) != cudaSuccess) bb.ok_ = false;
+    o.use_graph = false;  // the host decides every layer's slots
+  }
   float* logits = bb.Alloc<float>(static_cast<size_t>(B) * V);
   float* rope = bb.Alloc<float>(static_cast<size_t>(max_seq) * hd);
   const int64_t attn_bytes = nh_batch_attention_scratch_bytes(B, c.n_head, static_cast<int>(hd), max_seq);
@@ -232,6 +254,11 @@ std::vector<std::vector<int32_t>> GreedyGenerateCachedBatch(const OlmoeModel& mo
       NH_B_TRY(nh_batch_prep(h, d, B, Lv.ffn_norm, eps, 1, d, q8, xn, s));
       NH_B_TRY(nh_batch_router(xn, Lv.router, B, d, static_cast<int>(E), static_cast<int>(K), norm_topk ? 1 : 0,
                                sel, wts, s));
+      if (se != nullptr) {
+        NH_B_TRY(StreamedMoe(*se, l, Lv, c, B, sel, wts, sel_host, plan_host, off, cnt, act_idx, out_idx, q8, ff, q8ff,
+                             y, h, bb.event_, s));
+        continue;
+      }
       if (W > 1) NH_B_TRY(ExchangeTokens(*ep, q8, q8_row * B, q8_all, sel, BK, sel_all, s));
       // The owned experts over every rank's tokens: token j of the
       // gathered rows is rank j / B's sequence j % B.
@@ -339,6 +366,230 @@ std::vector<std::vector<int32_t>> GreedyGenerateCachedBatch(const OlmoeModel& mo
   out.resize(B);
   for (int b = 0; b < B; ++b) out[b].assign(ids.begin() + static_cast<size_t>(b) * n_predict,
                                             ids.begin() + static_cast<size_t>(b + 1) * n_predict);
+  return out;
+}
+
+// One MoE layer of the batched streaming form.  The router's selections are
+// read back and the batch's distinct unpinned experts are split, in order of
+// first selection, into waves of at most lru_slots (pinned experts, always
+// resident, join the first wave): each wave's experts are made resident with
+// one Ensure (which then never evicts an expert of the same wave), the
+// grouped gate/up and down products run over the slot pool for that wave's
+// (token, pick) pairs, and the next wave's fills wait for those products.
+// After the last wave every pick row is in y and the combine adds them in
+// top-k order, so each token's arithmetic equals the resident batch's.
+int StreamedMoe(StreamedExperts& se, int l, const LayerView& Lv, const OlmoeConfig& c, int B, const int32_t* sel,
+                const float* wts, int32_t* sel_host, int32_t* plan_host, int32_t* off, int32_t* cnt,
+                int32_t* act_idx, int32_t* out_idx, const uint8_t* q8, float* ff, uint8_t* q8ff, float* y, float* h,
+                cudaEvent_t compute_done, cudaStream_t s) {
+  (void)Lv;
+  ExpertSlotCache& cache = *se.caches[l];
+  const int K = static_cast<int>(c.n_expert_used), E = static_cast<int>(c.n_expert), BK = B * K;
+  const int64_t d = c.n_embd, F = c.n_ff;
+  const auto t0 = std::chrono::steady_clock::now();
+  if (cudaMemcpyAsync(sel_host, sel, static_cast<size_t>(BK) * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return NH_E_CUDA;
+  std::vector<int> wave_of(E, -1);
+  std::vector<std::vector<int>> waves;
+  const int per = cache.lru_slots();
+  for (int j = 0; j < BK; ++j) {
+    const int e = sel_host[j];
+    if (e < 0 || e >= E) return NH_E_STATE;
+    if (cache.is_pinned(e) || wave_of[e] >= 0) continue;
+    if (per <= 0) return NH_E_CAPACITY;
+    if (waves.empty() || static_cast<int>(waves.back().size()) == per) waves.emplace_back();
+    waves.back().push_back(e);
+    wave_of[e] = static_cast<int>(waves.size()) - 1;
+  }
+  if (waves.empty()) waves.emplace_back();
+  const int slots = static_cast<int>(cache.gate_slots()->ne[2]);
+  if (slots > E) return NH_E_CAPACITY;
+  const size_t plan_stride = static_cast<size_t>(2 * E + 2 * BK);
+  for (size_t w = 0; w < waves.size(); ++w) {
+    std::vector<int> ids = waves[w];
+    if (w == 0) {
+      std::vector<char> seen(E, 0);
+      for (int j = 0; j < BK; ++j) {
+        const int e = sel_host[j];
+        if (cache.is_pinned(e) && !seen[e]) {
+          seen[e] = 1;
+          ids.push_back(e);
+        }
+      }
+    } else {
+      // The previous wave's products still read slots this wave may refill.
+      if (cudaEventRecord(compute_done, s) != cudaSuccess ||
+          cudaStreamWaitEvent(se.copy_stream, compute_done, 0) != cudaSuccess)
+        return NH_E_CUDA;
+    }
+    const std::unordered_map<int, int> slot_of = cache.Ensure(ids);
+    if (!cache.ok()) return NH_E_IO;
+    // This wave's pairs grouped by slot, (token, pick) order within a slot.
+    int32_t* hoff = plan_host + w * plan_stride;
+    int32_t* hcnt = hoff + E;
+    int32_t* hact = hcnt + E;
+    int32_t* hout = hact + BK;
+    std::fill(hcnt, hcnt + slots, 0);
+    auto in_wave = [&](int e) { return cache.is_pinned(e) ? w == 0 : wave_of[e] == static_cast<int>(w); };
+    for (int j = 0; j < BK; ++j)
+      if (in_wave(sel_host[j])) ++hcnt[slot_of.at(sel_host[j])];
+    int n = 0;
+    for (int g = 0; g < slots; ++g) {
+      hoff[g] = n;
+      n += hcnt[g];
+    }
+    std::vector<int> cursor(hoff, hoff + slots);
+    for (int j = 0; j < BK; ++j) {
+      if (!in_wave(sel_host[j])) continue;
+      const int pos = cursor[slot_of.at(sel_host[j])]++;
+      hact[pos] = j / K;
+      hout[pos] = j;
+    }
+    if (cudaMemcpyAsync(off, hoff, static_cast<size_t>(slots) * 4, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+        cudaMemcpyAsync(cnt, hcnt, static_cast<size_t>(slots) * 4, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+        cudaMemcpyAsync(act_idx, hact, static_cast<size_t>(std::max(n, 1)) * 4, cudaMemcpyHostToDevice, s) !=
+            cudaSuccess ||
+        cudaMemcpyAsync(out_idx, hout, static_cast<size_t>(std::max(n, 1)) * 4, cudaMemcpyHostToDevice, s) !=
+            cudaSuccess ||
+        cudaStreamWaitEvent(s, static_cast<cudaEvent_t>(cache.fills_done_event()), 0) != cudaSuccess)
+      return NH_E_CUDA;
+    const DTensor *gs = cache.gate_slots(), *us = cache.up_slots(), *ds = cache.down_slots();
+    NhGroupedRowDot g;
+    std::memset(&g, 0, sizeof(g));
+    g.w = gs->data;
+    g.w2 = us->data;
+    g.mstride = gs->nb[2];
+    g.mstride2 = us->nb[2];
+    g.type = gs->type;
+    g.type2 = us->type;
+    g.n = d;
+    g.rows = F;
+    g.n_groups = slots;
+    g.off = off;
+    g.cnt = cnt;
+    g.act_idx = act_idx;
+    g.out_idx = out_idx;
+    g.max_tokens = B;
+    g.q8 = q8;
+    g.out = ff;
+    g.out_stride = F;
+    g.mode = NH_ROWDOT_SWIGLU;
+    NH_B_TRY(nh_batch_rowdot(&g, s));
+    NH_B_TRY(nh_batch_prep(ff, F, BK, nullptr, c.rms_eps, 0, F, q8ff, nullptr, s));
+    std::memset(&g, 0, sizeof(g));
+    g.w = ds->data;
+    g.mstride = ds->nb[2];
+    g.type = ds->type;
+    g.type2 = ds->type;
+    g.n = F;
+    g.rows = d;
+    g.n_groups = slots;
+    g.off = off;
+    g.cnt = cnt;
+    g.act_idx = out_idx;
+    g.out_idx = out_idx;
+    g.max_tokens = B;
+    g.q8 = q8ff;
+    g.out = y;
+    g.out_stride = d;
+    g.mode = NH_ROWDOT_STORE;
+    NH_B_TRY(nh_batch_rowdot(&g, s));
+    NH_B_TRY(cache.Commit(s));
+  }
+  se.waves += static_cast<int64_t>(waves.size());
+  se.host_ms += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+  return nh_batch_combine(y, wts, B, K, d, h, s);
+}
+
+}  // namespace
+
+std::vector<std::vector<int32_t>> GreedyGenerateCachedBatch(const OlmoeModel& model,
+                                                            const std::vector<std::vector<int32_t>>& prompts,
+                                                            int n_predict, bool norm_topk, BatchOptions* opt) {
+  BatchOptions local;
+  BatchOptions& o = opt != nullptr ? *opt : local;
+  o.status = NH_OK;
+  if (prompts.empty() || n_predict <= 0) return {};
+  const OlmoeConfig& c = model.config();
+  o.status = CheckPrompts(prompts, c);
+  if (o.status != NH_OK) return {};
+  ModelView m;
+  if (!BuildView(model, true, &m)) {
+    o.status = NH_E_STATE;
+    return {};
+  }
+  // Expert parallelism: this rank owns experts [shard.first, +count) and the
+  // sequences given here; all ranks' tokens meet at every MoE layer.
+  const ExpertGroup* ep = o.ep;
+  const int W = ep != nullptr ? ep->world() : 1;
+  const ExpertShard shard = ep != nullptr ? ExpertShard::Of(c.n_expert, W, ep->rank()) : ExpertShard{0, c.n_expert};
+  if (ep != nullptr && (c.n_expert % W != 0 || !Nccl().ok)) {
+    o.status = NH_E_ARG;
+    return {};
+  }
+  // The expert weights of the owned shard: the model holds exactly the shard
+  // (its tensors start at expert shard.first) or all experts.
+  uint64_t e_skip = 0;
+  if (model.holds_all_experts()) {
+    e_skip = shard.first;
+  } else if (model.expert_first() != shard.first || model.expert_count() != shard.count) {
+    o.status = NH_E_STATE;
+    return {};
+  }
+  return RunBatch(m, c, prompts, n_predict, norm_topk, o, shard, e_skip, nullptr);
+}
+
+std::vector<std::vector<int32_t>> StreamingGenerateBatch(const StreamingModel& model,
+                                                         const std::vector<std::vector<int32_t>>& prompts,
+                                                         int n_predict, bool norm_topk, int capacity,
+                                                         const StreamingOptions& opt, BatchOptions* bopt) {
+  BatchOptions local;
+  BatchOptions& o = bopt != nullptr ? *bopt : local;
+  StreamingStats local_stats;
+  StreamingStats& stats = opt.stats != nullptr ? *opt.stats : local_stats;
+  o.status = stats.status = NH_OK;
+  if (prompts.empty() || n_predict <= 0) return {};
+  const OlmoeConfig& c = model.config();
+  StreamingModel::Workspace* ws = model.workspace();
+  o.status = ws == nullptr || !ws->view_ok ? NH_E_STATE : capacity <= 0 ? NH_E_ARG : CheckPrompts(prompts, c);
+  if (o.ep != nullptr) o.status = NH_E_ARG;  // experts stream through one GPU's pool here
+  if (o.status != NH_OK) {
+    stats.status = o.status;
+    return {};
+  }
+  const int L = static_cast<int>(c.n_layers);
+  std::vector<std::unique_ptr<ExpertSlotCache>> owned;
+  StreamedExperts se;
+  se.copy_stream = ws->copy_stream;
+  const uint32_t pin_slots =
+      opt.pin_slots > 0 ? opt.pin_slots : LearnedPinSlots(static_cast<uint32_t>(capacity));
+  for (int l = 0; l < L; ++l) {
+    SlotCacheOptions so;
+    so.policy = opt.policy;
+    so.usage = opt.usage;
+    so.pin_slots = std::min<uint32_t>(pin_slots, static_cast<uint32_t>(capacity));
+    so.copy_stream = ws->copy_stream;
+    owned.push_back(ExpertSlotCache::Create(c, l, capacity, model.reader(), model.host_store(l), so));
+    if (owned.back() == nullptr) {
+      o.status = stats.status = NH_E_NOMEM;
+      return {};
+    }
+    se.caches.push_back(owned.back().get());
+  }
+  auto out = RunBatch(ws->view, c, prompts, n_predict, norm_topk, o, ExpertShard{0, c.n_expert}, 0, &se);
+  cudaStreamSynchronize(ws->copy_stream);
+  stats.hits.assign(L, 0);
+  stats.misses.assign(L, 0);
+  stats.h2d_bytes = 0;
+  for (int l = 0; l < L; ++l) {
+    stats.hits[l] = owned[l]->hits();
+    stats.misses[l] = owned[l]->misses();
+    stats.h2d_bytes += owned[l]->h2d_bytes();
+  }
+  stats.fill_ms = se.host_ms;
+  stats.waves = se.waves;
+  stats.status = o.status;
   return out;
 }
 

@@ -334,6 +334,48 @@ int nh_stream_generate(void* model, const int32_t* prompt, int n_prompt, int n_p
   return NH_OK;
 }
 
+int nh_stream_generate_batch(void* model, const int32_t* prompts, int n_seq, int n_prompt, int n_predict,
+                             int norm_topk, int capacity, int policy, int pin_slots, const uint64_t* usage,
+                             int32_t* out_tokens, int64_t* hits, int64_t* misses, uint64_t* h2d_bytes, int64_t* waves,
+                             double* decode_ms) {
+  if (model == nullptr || prompts == nullptr || out_tokens == nullptr || n_seq <= 0 || n_prompt <= 0 ||
+      n_predict <= 0 || (policy == 1 && usage == nullptr)) {
+    SetErr("nh_stream_generate_batch: bad argument");
+    return NH_E_ARG;
+  }
+  const StreamingModel& m = *static_cast<StreamingModel*>(model);
+  const OlmoeConfig& c = m.config();
+  std::vector<std::vector<int32_t>> p(n_seq);
+  for (int b = 0; b < n_seq; ++b)
+    p[b].assign(prompts + static_cast<size_t>(b) * n_prompt, prompts + static_cast<size_t>(b + 1) * n_prompt);
+  StreamingOptions o;
+  StreamingStats st;
+  o.stats = &st;
+  UsageHistogram u;
+  if (policy == 1) {
+    u = DenseUsage(usage, c.n_layers, c.n_expert);
+    o.policy = SlotPolicy::kLearnedPin;
+    o.usage = &u;
+    o.pin_slots = pin_slots > 0 ? static_cast<uint32_t>(pin_slots) : 0;
+  }
+  BatchOptions bo;
+  const auto ids = StreamingGenerateBatch(m, p, n_predict, norm_topk != 0, capacity, o, &bo);
+  if (st.status != NH_OK) {
+    SetErr("StreamingGenerateBatch failed with code " + std::to_string(st.status));
+    return st.status;
+  }
+  for (int b = 0; b < n_seq; ++b)
+    std::memcpy(out_tokens + static_cast<size_t>(b) * n_predict, ids[b].data(), static_cast<size_t>(n_predict) * 4);
+  for (uint32_t l = 0; l < c.n_layers && l < st.hits.size(); ++l) {
+    if (hits != nullptr) hits[l] = st.hits[l];
+    if (misses != nullptr) misses[l] = st.misses[l];
+  }
+  if (h2d_bytes != nullptr) *h2d_bytes = st.h2d_bytes;
+  if (waves != nullptr) *waves = st.waves;
+  if (decode_ms != nullptr) *decode_ms = bo.decode_ms;
+  return NH_OK;
+}
+
 int64_t nh_replay(int kind, uint32_t n_layers, uint32_t n_expert, int64_t n_records, const uint32_t* layer,
                   const int64_t* offsets, const uint32_t* experts, uint32_t a, uint32_t b, const uint64_t* usage,
                   int64_t* accesses) {
