@@ -855,10 +855,52 @@ __global__ void __launch_bounds__(kBAttnThreads) batch_attention_kernel(const BA
 // of one head and walks the splits twice: the first pass finds each query's
 // global maximum (scores only), the second re-forms each split and folds it
 // into the running combination, so no per-split partials leave the CTA.
-constexpr int kPAttnThreads = 128;
-constexpr int kPAttnQ = 16;
+constexpr int kPAttnThreads = 256;
+constexpr int kPAttnQ = 32;
 constexpr int kPAttnSplit = 64;
-constexpr int kPAttnOut = kPAttnQ * 128 / kPAttnThreads;  // outputs per thread at head_dim 128
+constexpr int kPAttnGroups = kPAttnThreads / kPAttnSplit;   // query groups (threads per key: one per group)
+constexpr int kPAttnPerThread = kPAttnQ / kPAttnGroups;     // queries each thread scores per key
+constexpr int kPAttnOut = kPAttnQ * 128 / kPAttnThreads;    // outputs per thread at head_dim 128
+
+// Two queries' scores against one key row with bscore_thread's operation
+// order for each (32 lane-strided partial sums over head_dim, then the same
+// butterfly), so every score equals bscore_thread(kr, qa/qb) bit for bit;
+// each 16-byte chunk of the key row is loaded once for both queries.
+__device__ __forceinline__ void bscore_pair(const float* kr, const float* qa, const float* qb, int hd, float& sa,
+                                            float& sb) {
+  float pa[32], pb[32];
+#pragma unroll
+  for (int l = 0; l < 32; ++l) {
+    pa[l] = 0.f;
+    pb[l] = 0.f;
+  }
+  for (int base = 0; base < hd; base += 32) {
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      const float4 kv = *reinterpret_cast<const float4*>(kr + base + 4 * t);
+      const float4 va = *reinterpret_cast<const float4*>(qa + base + 4 * t);
+      const float4 vb = *reinterpret_cast<const float4*>(qb + base + 4 * t);
+      pa[4 * t + 0] = __fadd_rn(pa[4 * t + 0], __fmul_rn(kv.x, va.x));
+      pa[4 * t + 1] = __fadd_rn(pa[4 * t + 1], __fmul_rn(kv.y, va.y));
+      pa[4 * t + 2] = __fadd_rn(pa[4 * t + 2], __fmul_rn(kv.z, va.z));
+      pa[4 * t + 3] = __fadd_rn(pa[4 * t + 3], __fmul_rn(kv.w, va.w));
+      pb[4 * t + 0] = __fadd_rn(pb[4 * t + 0], __fmul_rn(kv.x, vb.x));
+      pb[4 * t + 1] = __fadd_rn(pb[4 * t + 1], __fmul_rn(kv.y, vb.y));
+      pb[4 * t + 2] = __fadd_rn(pb[4 * t + 2], __fmul_rn(kv.z, vb.z));
+      pb[4 * t + 3] = __fadd_rn(pb[4 * t + 3], __fmul_rn(kv.w, vb.w));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+    for (int l = 0; l < o; ++l) {
+      pa[l] = __fadd_rn(pa[l], pa[l + o]);
+      pb[l] = __fadd_rn(pb[l], pb[l + o]);
+    }
+  }
+  sa = pa[0];
+  sb = pb[0];
+}
 
 struct PAttnArgs {
   const float* qr;       // [n_tok][n_head*hd] QK-normed, rotated queries
@@ -873,7 +915,7 @@ __device__ __forceinline__ int pattn_keys_in_split(int n_kv, int s) {
   return max(0, min(kPAttnSplit, n_kv - s * kPAttnSplit));
 }
 
-__global__ void __launch_bounds__(kPAttnThreads) prefill_attention_kernel(const PAttnArgs p) {
+__global__ void __launch_bounds__(kPAttnThreads, 2) prefill_attention_kernel(const PAttnArgs p) {
   const int h = blockIdx.x, t0 = blockIdx.y * kPAttnQ;
   const int nq = min(kPAttnQ, p.n_tok - t0);
   const int hd = p.hd, kst = hd + 4;
@@ -911,28 +953,36 @@ __global__ void __launch_bounds__(kPAttnThreads) prefill_attention_kernel(const 
       if (with_v) reinterpret_cast<float4*>(Vs + r * hd)[c] = __ldg(reinterpret_cast<const float4*>(p.v_cache + g) + c);
     }
   };
-  // Scores of the thread's (key j, query q) pairs: j = tid % 64, q = tid / 64 + 2i.
+  // Scores of the thread's (key j, query q) pairs: j = tid % 64, q = tid / 64
+  // + kPAttnGroups * i, two queries per pass over the key row.  Queries past
+  // nq read zero rows of Qs; keys past a split's rows are never used.
   const int j = tid & (kPAttnSplit - 1), qh = tid >> 6;
+  auto qrow = [&](int i) { return qh + kPAttnGroups * i; };
 
   // ---- pass 1: each query's maximum over all its keys
-  float run[kPAttnQ / 2];
+  float run[kPAttnPerThread];
 #pragma unroll
-  for (int i = 0; i < kPAttnQ / 2; ++i) run[i] = -INFINITY;
+  for (int i = 0; i < kPAttnPerThread; ++i) run[i] = -INFINITY;
   for (int s = 0; s < n_splits; ++s) {
     __syncthreads();
     load(s, false);
     __syncthreads();
 #pragma unroll
-    for (int i = 0; i < kPAttnQ / 2; ++i) {
-      const int q = qh + 2 * i;
-      if (q < nq && j < pattn_keys_in_split(n_kv(q), s))
-        run[i] = fmaxf(run[i], __fmul_rn(bscore_thread(Ks + j * kst, Qs + q * hd, hd), p.kq_scale));
+    for (int i = 0; i < kPAttnPerThread; i += 2) {
+      const int qa = qrow(i), qb = qrow(i + 1);
+      const bool va = qa < nq && j < pattn_keys_in_split(n_kv(qa), s);
+      const bool vb = qb < nq && j < pattn_keys_in_split(n_kv(qb), s);
+      if (!va && !vb) continue;
+      float sa, sb;
+      bscore_pair(Ks + j * kst, Qs + qa * hd, Qs + qb * hd, hd, sa, sb);
+      if (va) run[i] = fmaxf(run[i], __fmul_rn(sa, p.kq_scale));
+      if (vb) run[i + 1] = fmaxf(run[i + 1], __fmul_rn(sb, p.kq_scale));
     }
   }
 #pragma unroll
-  for (int i = 0; i < kPAttnQ / 2; ++i) {
+  for (int i = 0; i < kPAttnPerThread; ++i) {
     const float m = warp_max(run[i]);
-    if (lane == 0) s_max2[warp & 1][qh + 2 * i] = m;
+    if (lane == 0) s_max2[warp & 1][qrow(i)] = m;
   }
   __syncthreads();
   if (tid < kPAttnQ) s_M[tid] = fmaxf(s_max2[0][tid], s_max2[1][tid]);
@@ -947,10 +997,15 @@ __global__ void __launch_bounds__(kPAttnThreads) prefill_attention_kernel(const 
     load(s, true);
     __syncthreads();
 #pragma unroll
-    for (int i = 0; i < kPAttnQ / 2; ++i) {
-      const int q = qh + 2 * i;
-      if (q < nq && j < pattn_keys_in_split(n_kv(q), s))
-        S[q * kPAttnSplit + j] = __fmul_rn(bscore_thread(Ks + j * kst, Qs + q * hd, hd), p.kq_scale);
+    for (int i = 0; i < kPAttnPerThread; i += 2) {
+      const int qa = qrow(i), qb = qrow(i + 1);
+      const bool va = qa < nq && j < pattn_keys_in_split(n_kv(qa), s);
+      const bool vb = qb < nq && j < pattn_keys_in_split(n_kv(qb), s);
+      if (!va && !vb) continue;
+      float sa, sb;
+      bscore_pair(Ks + j * kst, Qs + qa * hd, Qs + qb * hd, hd, sa, sb);
+      if (va) S[qa * kPAttnSplit + j] = __fmul_rn(sa, p.kq_scale);
+      if (vb) S[qb * kPAttnSplit + j] = __fmul_rn(sb, p.kq_scale);
     }
     __syncthreads();
     // Per query (warp w: queries w, w+4, ...; lane: keys lane and lane+32).

@@ -23,6 +23,7 @@
 // issues the 8 (or 16) MMAs and commits them to an mbarrier; 8 warps read the
 // accumulators (warp w: lanes 32*(w%4).., tokens 16*(w/4)..) and form the
 // values.  All waits are bounded; an expired wait records NH_E_TIMEOUT.
+#include <algorithm>
 #include <cstring>
 
 #include "launch.cuh"
@@ -48,7 +49,9 @@ constexpr int kOffAOp = 0;
 constexpr int kOffBOp = kOffAOp + 2 * kAOpBytes;
 constexpr int kOffARaw = kOffBOp + 2 * kBOpBytes;
 constexpr int kOffBMeta = kOffARaw + 2 * 2 * kARawBytes;
-constexpr int kOffBar = kOffBMeta + 2 * kBMetaBytes;
+constexpr int kOffBsp = kOffBMeta + 2 * kBMetaBytes;      // [kTcTok][8] int
+constexpr int kOffBar = kOffBsp + kTcTok * 8 * 4;
+static_assert(kTcThreads == kTcTok * 8, "one thread per (token, sub-block) sum");
 constexpr int kTcSmemBytes = kOffBar + 64 + 1024;      // + alignment slack
 
 struct TcArgs {
@@ -145,16 +148,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_q4k_tc_kernel(const TcA
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kOffBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + kOffBar + 16);
+  int32_t* bsp = reinterpret_cast<int32_t*>(sm + kOffBsp);  // [kTcTok][8] sub-block sums of the activation
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int e = blockIdx.x / p.row_tiles, rt = blockIdx.x % p.row_tiles;
   pdl_wait();
   pdl_trigger();
   const int t_off = p.off != nullptr ? p.off[e] : 0;
   const int t_cnt = p.off != nullptr ? p.cnt[e] : p.n_tok;
-  const int tok_base = blockIdx.y * kTcTok;
-  if (tok_base >= t_cnt) return;  // an empty tile: nothing allocated yet
+  // Token tiles blockIdx.y, blockIdx.y + gridDim.y, ... of this group.
+  const int n_tiles = (t_cnt + kTcTok - 1) / kTcTok;
+  const int my_tiles = n_tiles > static_cast<int>(blockIdx.y)
+                           ? (n_tiles - static_cast<int>(blockIdx.y) + static_cast<int>(gridDim.y) - 1) /
+                                 static_cast<int>(gridDim.y)
+                           : 0;
+  if (my_tiles == 0) return;  // nothing allocated yet
   const int row0 = rt * kTcRows;
   const int nsb = p.K / QK;
+  const int total = my_tiles * nsb;  // (tile, super-block) iterations
   constexpr uint32_t kCols = NMAT == 2 ? 512u : 256u;
 
   if (tid == 0) {
@@ -172,30 +182,34 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_q4k_tc_kernel(const TcA
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  // Token rows of this tile (clamped to the last valid token past the end).
-  auto act_row = [&](int t) {
+  auto tile_base = [&](int it) { return (static_cast<int>(blockIdx.y) + (it / nsb) * static_cast<int>(gridDim.y)) * kTcTok; };
+  // Token rows of a tile (clamped to the last valid token past the end).
+  auto act_row = [&](int tok_base, int t) {
     const int tc = min(tok_base + t, t_cnt - 1);
     const int a = p.act_idx != nullptr ? p.act_idx[t_off + tc] : tc;
-    return p.q8 + static_cast<int64_t>(a) * (p.K / QK) * kTcQ8Stride;
+    return p.q8 + static_cast<int64_t>(a) * nsb * kTcQ8Stride;
   };
   const uint8_t* wmat[2] = {p.w + static_cast<uint64_t>(e) * p.mstride,
                             NMAT == 2 ? p.w2 + static_cast<uint64_t>(e) * p.mstride2 : nullptr};
 
-  // Copies of super-block sb into stage st: raw weight blocks, activation
-  // quants in MMA layout, activation sums and scale.
-  auto issue = [&](int sb, int st) {
-    const uint32_t araw = smem_u32(sm + kOffARaw + st * 2 * kARawBytes);
-    for (int i = tid; i < NMAT * kTcRows * 9; i += kTcThreads) {
-      const int m = i / (kTcRows * 9), rem = i % (kTcRows * 9), r = rem / 9, c = rem % 9;
+  // Copies of iteration it into stage st: raw weight blocks (thread = row,
+  // nine 16-byte chunks), activation quants in MMA layout, activation sums
+  // and scale.
+  auto issue = [&](int it, int st) {
+    const int sb = it % nsb, tok_base = tile_base(it);
+    if (tid < NMAT * kTcRows) {
+      const int m = tid / kTcRows, r = tid % kTcRows;
       const int row = min(row0 + r, p.rows - 1);
-      cp_async16(araw + (m * kTcRows + r) * kARawRow + c * 16,
-                 wmat[m] + static_cast<uint64_t>(row) * p.rb + sb * kARawRow + c * 16);
+      const uint32_t dst = smem_u32(sm + kOffARaw + st * 2 * kARawBytes + (m * kTcRows + r) * kARawRow);
+      const uint8_t* src = wmat[m] + static_cast<uint64_t>(row) * p.rb + sb * kARawRow;
+#pragma unroll
+      for (int c = 0; c < 9; ++c) cp_async16(dst + c * 16, src + c * 16);
     }
     const uint32_t bop = smem_u32(sm + kOffBOp + st * kBOpBytes);
     const uint32_t bmeta = smem_u32(sm + kOffBMeta + st * kBMetaBytes);
     for (int i = tid; i < kTcTok * 19; i += kTcThreads) {
-      const int t = i / 19, c = i % 19;
-      const uint8_t* src = act_row(t) + sb * kTcQ8Stride + c * 16;
+      const int t = i / 19, c = i - t * 19;
+      const uint8_t* src = act_row(tok_base, t) + sb * kTcQ8Stride + c * 16;
       if (c < 16)
         cp_async16(bop + (c >> 1) * (kTcTok * 32) + core_off(t, c & 1), src);
       else
@@ -209,15 +223,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_q4k_tc_kernel(const TcA
   const int erow = q4 * 32 + lane;  // this thread's accumulator row (tensor-memory lane)
   bool ok = true;
   issue(0, 0);
-  for (int sb = 0; sb < nsb; ++sb) {
-    const int st = sb & 1;
+  for (int it = 0; it < total; ++it) {
+    const int st = it & 1, sb = it % nsb, tok_base = tile_base(it);
     cp_async_wait_all();
     __syncthreads();
-    if (sb + 1 < nsb) issue(sb + 1, st ^ 1);
-    // Widen this stage's 4-bit weight quants into the MMA layout.
+    if (it + 1 < total) issue(it + 1, st ^ 1);
+    // Widen this stage's 4-bit weight quants into the MMA layout, and form
+    // each token's eight 32-value sums of its activation quants.
     const uint8_t* araw = sm + kOffARaw + st * 2 * kARawBytes;
-    for (int i = tid; i < NMAT * kTcRows; i += kTcThreads) {
-      const int m = i / kTcRows, r = i % kTcRows;
+    const uint8_t* meta = sm + kOffBMeta + st * kBMetaBytes;
+    if (tid < NMAT * kTcRows) {
+      const int m = tid / kTcRows, r = tid % kTcRows;
       const uint4* qsrc = reinterpret_cast<const uint4*>(araw + (m * kTcRows + r) * kARawRow + 16);
       uint8_t* aop = sm + kOffAOp + m * kAOpBytes;
 #pragma unroll
@@ -233,6 +249,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_q4k_tc_kernel(const TcA
         }
       }
     }
+    {
+      const int t = tid >> 3, j = tid & 7;  // kTcThreads == kTcTok * 8
+      const int w = reinterpret_cast<const int*>(meta + t * 48)[j];
+      bsp[t * 8 + j] = lo16(w) + hi16(w);
+    }
     fence_async_smem();
     __syncthreads();
     if (tid == 0) {
@@ -247,13 +268,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_q4k_tc_kernel(const TcA
                  smem_desc(aop0 + m * kAOpBytes + j * (kTcRows * 32)), smem_desc(bop0 + j * (kTcTok * 32)));
       tc_commit(bar);
     }
-    if (!mbar_wait(bar, static_cast<uint32_t>(sb & 1))) {
+    if (!mbar_wait(bar, static_cast<uint32_t>(it & 1))) {
       ok = false;
       break;
     }
     tc_fence_after();
     // Epilogue of super-block sb.
-    const uint8_t* meta = sm + kOffBMeta + st * kBMetaBytes;
 #pragma unroll
     for (int m = 0; m < NMAT; ++m) {
       const uint4 h = *reinterpret_cast<const uint4*>(araw + (m * kTcRows + erow) * kARawRow);
@@ -274,21 +294,44 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_q4k_tc_kernel(const TcA
         for (int t = 0; t < 16; ++t) sumi[t] += s * v[t];
       }
       const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
+      int mn[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) mn[j] = byte_of(j < 4 ? mna : mnb, j & 3);
 #pragma unroll
       for (int t = 0; t < 16; ++t) {
-        const uint8_t* mt = meta + (th * 16 + t) * 48;
-        const int4 bs0 = *reinterpret_cast<const int4*>(mt);
-        const int4 bs1 = *reinterpret_cast<const int4*>(mt + 16);
-        const float yd = *reinterpret_cast<const float*>(mt + 32);
-        const int bsw[8] = {bs0.x, bs0.y, bs0.z, bs0.w, bs1.x, bs1.y, bs1.z, bs1.w};
-        int summ = 0;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) summ += byte_of(j < 4 ? mna : mnb, j & 3) * (lo16(bsw[j]) + hi16(bsw[j]));
+        const int tok = th * 16 + t;
+        const int4 b0 = *reinterpret_cast<const int4*>(bsp + tok * 8);
+        const int4 b1 = *reinterpret_cast<const int4*>(bsp + tok * 8 + 4);
+        const float yd = *reinterpret_cast<const float*>(meta + tok * 48 + 32);
+        const int summ = mn[0] * b0.x + mn[1] * b0.y + mn[2] * b0.z + mn[3] * b0.w + mn[4] * b1.x + mn[5] * b1.y +
+                         mn[6] * b1.z + mn[7] * b1.w;
         tree[m][t].add(sb, __fsub_rn(__fmul_rn(__fmul_rn(d, yd), static_cast<float>(sumi[t])),
                                      __fmul_rn(__fmul_rn(dmin, yd), static_cast<float>(summ))));
       }
     }
     tc_fence_before();
+    if (sb == nsb - 1) {
+      // The tile is complete: its outputs.
+      const int row = row0 + erow;
+      if (row < p.rows) {
+#pragma unroll
+        for (int t = 0; t < 16; ++t) {
+          const int tok = tok_base + th * 16 + t;
+          if (tok >= t_cnt) break;
+          const int o = p.out_idx != nullptr ? p.out_idx[t_off + tok] : tok;
+          float* dst = p.out + static_cast<int64_t>(o) * p.out_stride + row;
+          const float v = tree[0][t].r;
+          if (p.mode == 0) {
+            *dst = v;
+          } else if (p.mode == 1) {
+            *dst = __fadd_rn(*dst, v);
+          } else if (NMAT == 2) {
+            const float sl = __fdiv_rn(v, __fadd_rn(1.0f, exp_cw(-v)));
+            *dst = __fmul_rn(sl, tree[NMAT - 1][t].r);
+          }
+        }
+      }
+    }
   }
   cp_async_wait_all();
   if (!ok) {
@@ -297,26 +340,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_q4k_tc_kernel(const TcA
     // tensor memory is released.
     (void)mbar_wait(bar, 0u);
     (void)mbar_wait(bar, 1u);
-  } else {
-    const int row = row0 + erow;
-    if (row < p.rows) {
-#pragma unroll
-      for (int t = 0; t < 16; ++t) {
-        const int tok = tok_base + th * 16 + t;
-        if (tok >= t_cnt) break;
-        const int o = p.out_idx != nullptr ? p.out_idx[t_off + tok] : tok;
-        float* dst = p.out + static_cast<int64_t>(o) * p.out_stride + row;
-        const float v = tree[0][t].r;
-        if (p.mode == 0) {
-          *dst = v;
-        } else if (p.mode == 1) {
-          *dst = __fadd_rn(*dst, v);
-        } else if (NMAT == 2) {
-          const float sl = __fdiv_rn(v, __fadd_rn(1.0f, exp_cw(-v)));
-          *dst = __fmul_rn(sl, tree[NMAT - 1][t].r);
-        }
-      }
-    }
   }
   tc_fence_before();
   __syncthreads();
@@ -375,8 +398,12 @@ extern "C" int nh_batch_rowdot_tc(const NhGroupedRowDot* g, void* stream) {
   p.out = g->out;
   p.out_stride = g->out_stride;
   p.err = g->err;
+  // Grouped products: a CTA walks its group's token tiles y, y + grid.y, ...;
+  // two CTAs per (group, row tile) cover the usual per-expert token counts
+  // without launching mostly-empty tiles.  Dense products: one tile each.
+  const int tiles = (g->max_tokens + kTcTok - 1) / kTcTok;
   const dim3 grid(static_cast<unsigned>(g->n_groups * p.row_tiles),
-                  static_cast<unsigned>((g->max_tokens + kTcTok - 1) / kTcTok));
+                  static_cast<unsigned>(g->off != nullptr ? std::min(tiles, 2) : tiles));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (swiglu) {
     static SmemLimit configured;
