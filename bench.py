@@ -295,44 +295,98 @@ def run_batched(args) -> None:
 
 
 def run_prefill(args) -> None:
-    """Prompt prefill + decode (the configuration-4 workload on one GPU): 8
-    sequences of 4096 seeded random ids, each through GreedyGenerateCached
-    with 64 greedy ids.  The prompt runs as one batched prefill (grouped
-    expert products, causal prefill attention), then batch-1 decode steps.
-    Device-timed parts; value = prefill tokens/s."""
+    """Configuration 4: 8 sequences of 4096 seeded random ids, prompt prefill
+    then 64 greedy ids each, through GreedyGenerateCachedBatch: the prompt
+    positions of all sequences run as 512-row chunks of the batched kernels
+    (tcgen05 grouped expert products, causal prefill attention), then the
+    batched decode steps.  Under torchrun (N ranks, one GPU each) the
+    sequences are split over the ranks (attention data-parallel) and the
+    experts sharded E/N per GPU with NCCL all-gather / all-to-all per MoE
+    layer: the total work is fixed, so scaling is strong.  Device-timed
+    parts (CUDA events on the decode stream), max over ranks; value = prefill
+    tokens of all sequences / prefill time.  At N=1 the same prompts are
+    also run one sequence at a time (GreedyGenerateCached), for comparison."""
+    import datetime
+
     import torch
 
     import nuthatch_b200 as nh
     from nuthatch_b200 import build, synth
     from nuthatch_b200._lib import lib
 
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local_rank))
     build.build_product()
-    torch.cuda.set_device(0)
-    path = str(synth.cached(synth.OLMOE_1B7B))
-    m = nh.OlmoeModel.Load(path)
-    cfg = m.config()
-    n_seq, n_prompt, n_pred = args.prefill_seqs, args.prefill_tokens, args.prefill_decode
-    prompts = np.random.default_rng(4).integers(0, cfg.n_vocab, (n_seq, n_prompt), dtype=np.int32)
     L = lib()
-    out = np.zeros(n_pred, dtype=np.int32)
-    pf, dc = C.c_double(0), C.c_double(0)
+    assert L.nh_set_device(local_rank) == 0
+    if rank == 0:
+        synth.cached(synth.OLMOE_1B7B)
+    if dist is not None:
+        dist.barrier()
+    path = str(synth.cached(synth.OLMOE_1B7B))
+    cfg_model = nh.OlmoeModel.Load(path) if world == 1 else None
+    n_seq, n_prompt, n_pred = args.prefill_seqs, args.prefill_tokens, args.prefill_decode
+    from nuthatch_b200._lib import NhConfig
 
-    def one(p):
-        pc = np.ascontiguousarray(p)
-        assert L.nh_generate_timed(m._h, pc.ctypes.data_as(C.POINTER(C.c_int32)), pc.size, n_pred, 0,
-                                   out.ctypes.data_as(C.POINTER(C.c_int32)), C.byref(pf), C.byref(dc)) == 0
-        return pf.value, dc.value, out.tolist()
-
-    one(prompts[0][:600])  # warm-up: buffers, kernel attributes, graphs
-    clocks = ClockSampler(0)
-    pre_ms = dec_ms = 0.0
-    ids = []
-    for b in range(n_seq):
-        a, d, t = one(prompts[b])
-        pre_ms += a
-        dec_ms += d
-        ids.append(t)
+    cfg = NhConfig()
+    assert L.nh_gguf_probe(path.encode(), C.byref(cfg)) == 0
+    if n_seq % world != 0 or cfg.n_expert % world != 0:
+        if rank == 0:
+            print(json.dumps({"workload": "prefill", "unavailable": f"{n_seq} sequences / {cfg.n_expert} experts "
+                                                                    f"do not split over {world} GPUs"}))
+        return
+    prompts = np.random.default_rng(4).integers(0, cfg.n_vocab, (n_seq, n_prompt), dtype=np.int32)
+    per = n_seq // world
+    mine = prompts[rank * per:(rank + 1) * per].tolist()
+    ep = None
+    if world > 1:
+        box = [nh.ExpertGroup.new_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        ep = nh.ExpertGroup(box[0], world, rank)
+        first, count = nh.ExpertGroup.shard(cfg.n_expert, world, rank)
+        model = nh.OlmoeModel.LoadExpertShard(path, first, count)
+    else:
+        model = cfg_model
+    if model is None:
+        raise SystemExit("model load failed")
+    # Warm-up: buffers, kernel attributes, NCCL connections, graphs.
+    nh.generate_batch_ex(model, [p[:600] for p in mine], 2, False, ep=ep)
+    clocks = ClockSampler(local_rank)
+    r = nh.generate_batch_ex(model, mine, n_pred, False, ep=ep)
     clk = clocks.stop()
+    pre_ms = max_over_ranks(r["prefill_ms"], dist)
+    dec_ms = max_over_ranks(r["decode_ms"], dist)
+    single = None
+    if world == 1:
+        out = np.zeros(n_pred, dtype=np.int32)
+        pf, dc = C.c_double(0), C.c_double(0)
+        s_pre = s_dec = 0.0
+        same = True
+        for b in range(n_seq):
+            pc = np.ascontiguousarray(prompts[b])
+            assert L.nh_generate_timed(model._h, pc.ctypes.data_as(C.POINTER(C.c_int32)), pc.size, n_pred, 0,
+                                       out.ctypes.data_as(C.POINTER(C.c_int32)), C.byref(pf), C.byref(dc)) == 0
+            s_pre += pf.value
+            s_dec += dc.value
+            same = same and out.tolist() == r["tokens"][b]
+        single = {"api": "GreedyGenerateCached per sequence (nh_generate_timed)",
+                  "prefill_tok_s": n_seq * (n_prompt - 1) / (s_pre / 1000.0),
+                  "decode_tok_s": n_seq * n_pred / (s_dec / 1000.0), "ids_equal_batched": same}
+    if ep is not None:
+        model.close()
+        ep.close()
+    if rank != 0:
+        if dist is not None:
+            dist.destroy_process_group()
+        return
     n_pre = n_seq * (n_prompt - 1)
     # Per prefill token: 2 x active parameters (attention 4 d^2, router d E,
     # 8 experts x 3 d F, per layer) + causal attention 4 x (p+1) x d per layer.
@@ -343,17 +397,22 @@ def run_prefill(args) -> None:
     peaks = measured_peaks()
     tflops = flops / (pre_ms / 1000.0) / 1e12
     line = {"metric": f"OLMoE Q4_K_M prompt prefill tok/s ({n_seq} x {n_prompt} tokens) + decode",
-            "value": n_pre / (pre_ms / 1000.0), "unit": "tok/s", "n_gpus": 1, "steps": n_seq, "warmup": 1,
-            "ms_per_step": pre_ms / n_seq, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "value": n_pre / (pre_ms / 1000.0), "unit": "tok/s", "n_gpus": world, "steps": 1, "warmup": 1,
+            "ms_per_step": pre_ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "q4k/q6k x q8k int dot, f32 accumulate, f32 KV",
             "data": "synthetic (seeded random-init GGUF of the OLMoE-1B-7B shape, seeded random-id prompts)",
             "config": {"workload": f"olmoe-1b7b-q4km-prefill ({n_seq} x {n_prompt} prompt, {n_pred} greedy ids)",
-                       "parallelism": "single GPU", "step": "one sequence's prompt prefill"},
-            "clocks": clk, "decode_tok_s": n_seq * n_pred / (dec_ms / 1000.0),
+                       "parallelism": f"ep{world} (experts {cfg.n_expert // world} per GPU, "
+                                      f"{per} sequences per GPU)" if world > 1 else "single GPU",
+                       "step": "the prompt prefill of all sequences (512-row chunks)"},
+            "clocks": clk, "decode_tok_s": n_seq * n_pred / (dec_ms / 1000.0), "decode_ms": dec_ms,
             "prefill_roofline": {"bound": "tensor", "flops": flops, "achieved": tflops,
                                  "peak": peaks.get("bf16_tflops"), "unit": "TFLOP/s",
-                                 "note": "int8 tensor-core products against the measured bf16 dense peak"}}
+                                 "note": "int8 tensor-core products against the measured bf16 dense peak"},
+            "one_sequence_at_a_time": single}
     print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
 
 
 def run_granite(args) -> None:

@@ -91,6 +91,14 @@ void* nh_model_load_expert_shard(const char* path, uint32_t first, uint32_t coun
 int nh_generate_batch_ep(void* model, const void* ep, const int32_t* prompts, int n_seq, int n_prompt, int n_predict,
                          int norm_topk, int use_graph, int32_t* out_tokens, double* decode_ms);
 
+/* Both batched forms with the device time split in two (ep NULL: one GPU):
+ * the chunked prefill of the prompt positions before the last (prefill_ms, 0
+ * when the prompt ran one position per step) and the steps from the last
+ * prompt position on (decode_ms).  Either pointer may be NULL. */
+int nh_generate_batch_timed(void* model, const void* ep, const int32_t* prompts, int n_seq, int n_prompt,
+                            int n_predict, int norm_topk, int use_graph, int32_t* out_tokens, double* prefill_ms,
+                            double* decode_ms);
+
 /* Decode replay for timing (no reference counterpart; the reference times
  * whole generate calls).  prepare: runs the prompt's first n_prompt-1
  * positions and saves the cursor (synchronises).  run: restores the cursor

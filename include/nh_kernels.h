@@ -384,6 +384,19 @@ int nh_prefill_attention(const float* qr, int n_tok, int pos0, int n_head, int n
                          float kq_scale, const float* k_cache, const float* v_cache, int max_seq, float* out,
                          void* stream);
 
+/* The same three over n_seq sequences in one launch each, every sequence
+ * contributing n_tok rows at positions pos0..pos0+n_tok-1 (row r is
+ * sequence r / n_tok): ids of sequence s at ids + s*ids_stride; q, k, v, qr
+ * and out [n_seq*n_tok][...]; caches [n_seq][max_seq][n_head_kv*head_dim]. */
+int nh_prefill_embed_seqs(const int32_t* ids, int64_t ids_stride, int n_seq, int n_tok, const void* table,
+                          int32_t type, int64_t n_embd, int64_t n_vocab, float* h, int32_t* err, void* stream);
+int nh_prefill_qk_seqs(const float* q, const float* k, const float* v, const float* q_norm, const float* k_norm,
+                       float eps, int n_seq, int n_tok, int pos0, int n_head, int n_head_kv, int head_dim,
+                       const float* rope_cs, float* k_cache, float* v_cache, int max_seq, float* qr, void* stream);
+int nh_prefill_attention_seqs(const float* qr, int n_seq, int n_tok, int pos0, int n_head, int n_head_kv,
+                              int head_dim, float kq_scale, const float* k_cache, const float* v_cache, int max_seq,
+                              float* out, void* stream);
+
 /* ---- standalone forms used by the parity tests ---- */
 
 /* y[r] = (W . x)[r] for r < rows (ggml_mul_mat for one activation row); when

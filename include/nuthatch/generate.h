@@ -52,8 +52,10 @@ std::vector<int32_t> GreedyGenerateCachedEx(const OlmoeModel& model, const std::
 
 // Batched greedy decode (no reference counterpart: the batched overload the
 // boundary needs for many independent sequences).  All prompts must have the
-// same length; each sequence advances one position per step in lockstep with
-// its own KV cache, and its ids equal GreedyGenerateCached on it alone.
+// same length; positions 0..P-2 of every sequence are prefilled in chunks of
+// up to 512 rows (NH_BATCH_PREFILL=0: one position per step instead), then
+// each sequence advances one position per step in lockstep with its own KV
+// cache, and its ids equal GreedyGenerateCached on it alone.
 //
 // Expert parallelism (ep set): every rank of the group calls this at once with
 // its own share of the sequences (the same count on every rank) and a model
@@ -64,6 +66,7 @@ struct BatchOptions {
   bool use_graph = true;            // replay a captured CUDA graph per step
   const ExpertGroup* ep = nullptr;  // expert-parallel group, or single GPU
   double decode_ms = 0;             // out: device time from the last prompt position to the end
+  double prefill_ms = 0;            // out: device time of the chunked prompt prefill (0 without one)
   int status = 0;                   // out: NH_OK or the first error code
 };
 std::vector<std::vector<int32_t>> GreedyGenerateCachedBatch(const OlmoeModel& model,

@@ -241,22 +241,19 @@ class ExpertGroup:
 def generate_batch_ex(model: OlmoeModel, prompts: Sequence[Sequence[int]], n_predict: int, norm_topk: bool,
                       use_graph: bool = True, ep: Optional[ExpertGroup] = None) -> dict:
     """Batched greedy decode of equal-length prompts; ids per sequence and the
-    device time of the decode part.  With ep, every rank passes its own
-    sequences (the same count everywhere) at the same time."""
+    device time of the chunked prompt prefill and of the decode part.  With
+    ep, every rank passes its own sequences (the same count everywhere) at the
+    same time."""
     p = np.ascontiguousarray(np.asarray(prompts, dtype=np.int32))
     if p.ndim != 2:
         raise ValueError("prompts must all have the same length")
     n_seq, n_prompt = p.shape
     out = np.zeros((n_seq, n_predict), dtype=np.int32)
-    ms = C.c_double(0.0)
-    if ep is None:
-        _check(lib().nh_generate_batch(model._h, _ptr(p, C.c_int32), n_seq, n_prompt, n_predict, int(norm_topk),
-                                       int(use_graph), _ptr(out, C.c_int32), C.byref(ms)), "nh_generate_batch")
-    else:
-        _check(lib().nh_generate_batch_ep(model._h, ep._h, _ptr(p, C.c_int32), n_seq, n_prompt, n_predict,
-                                          int(norm_topk), int(use_graph), _ptr(out, C.c_int32), C.byref(ms)),
-               "nh_generate_batch_ep")
-    return {"tokens": out.tolist(), "decode_ms": ms.value}
+    pre, ms = C.c_double(0.0), C.c_double(0.0)
+    _check(lib().nh_generate_batch_timed(model._h, None if ep is None else ep._h, _ptr(p, C.c_int32), n_seq,
+                                         n_prompt, n_predict, int(norm_topk), int(use_graph), _ptr(out, C.c_int32),
+                                         C.byref(pre), C.byref(ms)), "nh_generate_batch")
+    return {"tokens": out.tolist(), "prefill_ms": pre.value, "decode_ms": ms.value}
 
 
 def GreedyGenerateCachedBatch(model: OlmoeModel, prompts: Sequence[Sequence[int]], n_predict: int,

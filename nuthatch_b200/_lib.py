@@ -54,6 +54,8 @@ SIGNATURES = {
                                     P(C.c_double)]),
     "nh_generate_timed": (C.c_int, [vp, P(i32), C.c_int, C.c_int, C.c_int, P(i32), P(C.c_double),
                                     P(C.c_double)]),
+    "nh_generate_batch_timed": (C.c_int, [vp, vp, P(i32), C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, P(i32),
+                                          P(C.c_double), P(C.c_double)]),
     "nh_ep_new_id": (C.c_int, [vp]),
     "nh_ep_create": (vp, [vp, C.c_int, C.c_int]),
     "nh_ep_free": (None, [vp]),
@@ -120,6 +122,11 @@ SIGNATURES = {
                                 C.c_int, vp, vp]),
     "nh_prefill_attention": (C.c_int, [vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, f32, vp, vp, C.c_int, vp,
                                        vp]),
+    "nh_prefill_embed_seqs": (C.c_int, [vp, i64, C.c_int, C.c_int, vp, i32, i64, i64, vp, vp, vp]),
+    "nh_prefill_qk_seqs": (C.c_int, [vp, vp, vp, vp, vp, f32, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                     vp, vp, vp, C.c_int, vp, vp]),
+    "nh_prefill_attention_seqs": (C.c_int, [vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, f32, vp, vp,
+                                            C.c_int, vp, vp]),
     "nh_batch_router_trace": (C.c_int, [vp, vp, C.c_int, i64, C.c_int, C.c_int, C.c_int, vp, vp, vp, vp, C.c_int,
                                         C.c_int, C.c_int, vp]),
     "nh_gemv": (C.c_int, [vp, vp, i32, i64, i64, vp, vp, f32, vp, vp]),

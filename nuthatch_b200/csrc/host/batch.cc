@@ -9,6 +9,7 @@
 #include <algorithm>
 #include <chrono>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <unordered_map>
 
@@ -100,6 +101,16 @@ int ReturnPicks(const ExpertGroup& ep, const float* y, size_t block, float* y_re
     if (rc_ != NH_OK) return rc_; \
   } while (0)
 
+// The chunked prompt prefill of the batched decode is on unless
+// NH_BATCH_PREFILL=0 (read at every call).
+bool BatchPrefillEnabled() {
+  const char* e = std::getenv("NH_BATCH_PREFILL");
+  return !(e != nullptr && e[0] == '0');
+}
+
+// Rows of one prefill chunk (sequences x positions), at most.
+constexpr int kBatchPrefillRows = 512;
+
 // Prompts of equal, non-zero length with ids inside the vocabulary.
 int CheckPrompts(const std::vector<std::vector<int32_t>>& prompts, const OlmoeConfig& c) {
   const size_t P = prompts[0].size();
@@ -140,43 +151,53 @@ std::vector<std::vector<int32_t>> RunBatch(const ModelView& m, const OlmoeConfig
   const ExpertGroup* ep = o.ep;
   const int W = ep != nullptr ? ep->world() : 1;
   const int max_seq = P + n_predict;
-  const int BK = B * static_cast<int>(K);
-  const int BW = B * W, BKW = BK * W;  // rows of every rank's tokens / picks
+  // Chunked prompt prefill (the reference forwards the whole prompt in its
+  // first step, generate.cc:63-91): positions 0..P-2 of every local sequence,
+  // C positions at a time as B*C rows, through the batched kernels; the last
+  // prompt position is the first decode step, which forms the logits.  Every
+  // rank of an expert-parallel group has the same B and P, so the same C and
+  // the same collectives.  The streaming form keeps the position-by-position
+  // prompt (its slot decisions are made per step).
+  const bool prefill = se == nullptr && P > 1 && BatchPrefillEnabled() && Engine::PrefillSupported(m);
+  const int C = prefill ? std::max(1, std::min(P - 1, kBatchPrefillRows / B)) : 1;
+  const int R = prefill ? std::max(B, B * C) : B;  // rows of the largest pass
+  const int RK = R * static_cast<int>(K);
+  const int RW = R * W, RKW = RK * W;  // rows of every rank's tokens / picks
   BatchBuffers bb;
   NhDecodeState* state = bb.Alloc<NhDecodeState>(1);
   int32_t* prm = bb.Alloc<int32_t>(static_cast<size_t>(B) * P);
   int32_t* fed = bb.Alloc<int32_t>(B);
   int32_t* outs = bb.Alloc<int32_t>(static_cast<size_t>(B) * n_predict);
-  float* h = bb.Alloc<float>(B * d);
-  float* q = bb.Alloc<float>(B * d);
-  float* kk = bb.Alloc<float>(B * dkv);
-  float* v = bb.Alloc<float>(B * dkv);
-  float* qr = bb.Alloc<float>(B * d);
-  float* att = bb.Alloc<float>(B * d);
-  float* xn = bb.Alloc<float>(B * d);
+  float* h = bb.Alloc<float>(static_cast<size_t>(R) * d);
+  float* q = bb.Alloc<float>(static_cast<size_t>(R) * d);
+  float* kk = bb.Alloc<float>(static_cast<size_t>(R) * dkv);
+  float* v = bb.Alloc<float>(static_cast<size_t>(R) * dkv);
+  float* qr = bb.Alloc<float>(static_cast<size_t>(R) * d);
+  float* att = bb.Alloc<float>(static_cast<size_t>(R) * d);
+  float* xn = bb.Alloc<float>(static_cast<size_t>(R) * d);
   const int64_t q8_row = nh_batch_q8_bytes(1, d);
-  uint8_t* q8 = bb.Alloc<uint8_t>(q8_row * B);
-  int32_t* sel = bb.Alloc<int32_t>(BK);
-  float* wts = bb.Alloc<float>(BK);
+  uint8_t* q8 = bb.Alloc<uint8_t>(q8_row * R);
+  int32_t* sel = bb.Alloc<int32_t>(RK);
+  float* wts = bb.Alloc<float>(RK);
   int32_t* off = bb.Alloc<int32_t>(E);
   int32_t* cnt = bb.Alloc<int32_t>(E);
-  int32_t* act_idx = bb.Alloc<int32_t>(BKW);
-  int32_t* out_idx = bb.Alloc<int32_t>(BKW);
-  float* ff = bb.Alloc<float>(static_cast<size_t>(BKW) * F);
-  uint8_t* q8ff = bb.Alloc<uint8_t>(nh_batch_q8_bytes(BKW, F));
-  float* y = bb.Alloc<float>(static_cast<size_t>(BKW) * d);
+  int32_t* act_idx = bb.Alloc<int32_t>(RKW);
+  int32_t* out_idx = bb.Alloc<int32_t>(RKW);
+  float* ff = bb.Alloc<float>(static_cast<size_t>(RKW) * F);
+  uint8_t* q8ff = bb.Alloc<uint8_t>(nh_batch_q8_bytes(RKW, F));
+  float* y = bb.Alloc<float>(static_cast<size_t>(RKW) * d);
   // Expert-parallel exchange buffers: every rank's activation rows and
   // selections (all-gathered), and the pick rows returned by each rank.
-  uint8_t* q8_all = W > 1 ? bb.Alloc<uint8_t>(q8_row * BW) : q8;
-  int32_t* sel_all = W > 1 ? bb.Alloc<int32_t>(BKW) : sel;
-  float* y_recv = W > 1 ? bb.Alloc<float>(static_cast<size_t>(BKW) * d) : y;
+  uint8_t* q8_all = W > 1 ? bb.Alloc<uint8_t>(q8_row * RW) : q8;
+  int32_t* sel_all = W > 1 ? bb.Alloc<int32_t>(RKW) : sel;
+  float* y_recv = W > 1 ? bb.Alloc<float>(static_cast<size_t>(RKW) * d) : y;
   // Streaming: the selections read back per layer and the per-wave expert
   // lists (up to one wave per expert), in pinned host memory.
   int32_t* sel_host = nullptr;
   int32_t* plan_host = nullptr;
   if (se != nullptr) {
-    sel_host = bb.HostAlloc<int32_t>(BK);
-    plan_host = bb.HostAlloc<int32_t>(static_cast<size_t>(E) * (2 * E + 2 * BK));
+    sel_host = bb.HostAlloc<int32_t>(RK);
+    plan_host = bb.HostAlloc<int32_t>(static_cast<size_t>(E) * (2 * E + 2 * RK));
     if (cudaEventCreateWithFlags(&bb.event_, cudaEventDisableTiming) != cudaSuccess) bb.ok_ = false;
     o.use_graph = false;  // the host decides every layer's slots
   }
@@ -199,14 +220,15 @@ std::vector<std::vector<int32_t>> RunBatch(const ModelView& m, const OlmoeConfig
   std::memset(&st0, 0, sizeof(st0));
   st0.n_prompt = P;
   st0.n_predict = n_predict;
+  st0.pos = prefill ? P - 1 : 0;  // the decode steps start after the prefilled positions
   bool setup = cudaMemcpy(prm, flat.data(), flat.size() * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
                cudaMemcpy(rope, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
                cudaMemcpy(state, &st0, sizeof(st0), cudaMemcpyHostToDevice) == cudaSuccess &&
                cudaMemset(attn_scratch, 0, attn_bytes) == cudaSuccess && cudaMemset(ticket, 0, 64) == cudaSuccess &&
                cudaMemset(fed, 0, B * 4) == cudaSuccess &&
-               cudaMemset(ff, 0, static_cast<size_t>(BKW) * F * 4) == cudaSuccess &&
-               cudaMemset(y, 0, static_cast<size_t>(BKW) * d * 4) == cudaSuccess &&
-               cudaMemset(y_recv, 0, static_cast<size_t>(BKW) * d * 4) == cudaSuccess &&
+               cudaMemset(ff, 0, static_cast<size_t>(RKW) * F * 4) == cudaSuccess &&
+               cudaMemset(y, 0, static_cast<size_t>(RKW) * d * 4) == cudaSuccess &&
+               cudaMemset(y_recv, 0, static_cast<size_t>(RKW) * d * 4) == cudaSuccess &&
                cudaDeviceSynchronize() == cudaSuccess &&
                cudaStreamCreateWithFlags(&bb.stream_, cudaStreamNonBlocking) == cudaSuccess;
   if (!setup) {
@@ -217,8 +239,9 @@ std::vector<std::vector<int32_t>> RunBatch(const ModelView& m, const OlmoeConfig
   const float eps = c.rms_eps;
   const float kq_scale = 1.0f / std::sqrt(static_cast<float>(hd));
 
+  // Product of one weight with nt activation rows.
   auto dense = [&](const void* w, int32_t type, int64_t rows, int64_t n, const void* act, float* o_, int64_t stride,
-                   int mode) {
+                   int mode, int nt) {
     NhGroupedRowDot g;
     std::memset(&g, 0, sizeof(g));
     g.w = w;
@@ -227,13 +250,101 @@ std::vector<std::vector<int32_t>> RunBatch(const ModelView& m, const OlmoeConfig
     g.n = n;
     g.rows = rows;
     g.n_groups = 1;
-    g.n_tok = B;
-    g.max_tokens = B;
+    g.n_tok = nt;
+    g.max_tokens = nt;
     g.q8 = act;
     g.out = o_;
     g.out_stride = stride;
     g.mode = mode;
     return nh_batch_rowdot(&g, s);
+  };
+  // The MoE block of layer l over the first r rows of h (moe.cc:7-63).
+  auto moe = [&](int l, const LayerView& Lv, int r) -> int {
+    const int rk = r * static_cast<int>(K);
+    NH_B_TRY(nh_batch_prep(h, d, r, Lv.ffn_norm, eps, 1, d, q8, xn, s));
+    NH_B_TRY(nh_batch_router(xn, Lv.router, r, d, static_cast<int>(E), static_cast<int>(K), norm_topk ? 1 : 0, sel,
+                             wts, s));
+    if (se != nullptr)
+      return StreamedMoe(*se, l, Lv, c, r, sel, wts, sel_host, plan_host, off, cnt, act_idx, out_idx, q8, ff, q8ff, y,
+                         h, bb.event_, s);
+    if (W > 1) NH_B_TRY(ExchangeTokens(*ep, q8, q8_row * r, q8_all, sel, rk, sel_all, s));
+    // The owned experts over every rank's rows: row j of the gathered rows
+    // is rank j / r's row j % r.
+    NH_B_TRY(nh_batch_moe_plan_range(sel_all, r * W, static_cast<int>(K), static_cast<int>(shard.first),
+                                     static_cast<int>(shard.count), off, cnt, act_idx, out_idx, s));
+    NhGroupedRowDot g;
+    std::memset(&g, 0, sizeof(g));
+    g.w = static_cast<const uint8_t*>(Lv.gate) + e_skip * Lv.gate_nb2;
+    g.w2 = static_cast<const uint8_t*>(Lv.up) + e_skip * Lv.up_nb2;
+    g.mstride = Lv.gate_nb2;
+    g.mstride2 = Lv.up_nb2;
+    g.type = Lv.tg;
+    g.type2 = Lv.tu;
+    g.n = d;
+    g.rows = F;
+    g.n_groups = static_cast<int32_t>(shard.count);
+    g.off = off;
+    g.cnt = cnt;
+    g.act_idx = act_idx;
+    g.out_idx = out_idx;
+    g.max_tokens = r * W;
+    g.q8 = q8_all;
+    g.out = ff;
+    g.out_stride = F;
+    g.mode = NH_ROWDOT_SWIGLU;
+    NH_B_TRY(nh_batch_rowdot(&g, s));
+    NH_B_TRY(nh_batch_prep(ff, F, static_cast<int64_t>(rk) * W, nullptr, eps, 0, F, q8ff, nullptr, s));
+    std::memset(&g, 0, sizeof(g));
+    g.w = static_cast<const uint8_t*>(Lv.down) + e_skip * Lv.down_nb2;
+    g.mstride = Lv.down_nb2;
+    g.type = Lv.td;
+    g.type2 = Lv.td;
+    g.n = F;
+    g.rows = d;
+    g.n_groups = static_cast<int32_t>(shard.count);
+    g.off = off;
+    g.cnt = cnt;
+    g.act_idx = out_idx;  // the ff row of pair j is its (row, slot) index
+    g.out_idx = out_idx;
+    g.max_tokens = r * W;
+    g.q8 = q8ff;
+    g.out = y;
+    g.out_stride = d;
+    g.mode = NH_ROWDOT_STORE;
+    NH_B_TRY(nh_batch_rowdot(&g, s));
+    if (W > 1) {
+      // Rows of rank q's picks go back to rank q; the combine takes each
+      // pick's row from the block of the rank that owns its expert.
+      NH_B_TRY(ReturnPicks(*ep, y, static_cast<size_t>(rk) * d, y_recv, s));
+      return nh_ep_combine(y_recv, static_cast<int64_t>(rk) * d, W, sel, wts, r, static_cast<int>(K), d,
+                           static_cast<int>(shard.count), h, s);
+    }
+    return nh_batch_combine(y, wts, r, static_cast<int>(K), d, h, s);
+  };
+  // Prompt positions p0..p0+cc-1 of every local sequence as B*cc rows (row
+  // b*cc + i is sequence b's position p0 + i): QK-norm, RoPE, the K/V append
+  // and causal attention into each sequence's own cache, everything else over
+  // all rows at once; no logits are formed for these positions.
+  auto prefill_chunk = [&](int p0, int cc) -> int {
+    const int r = B * cc;
+    NH_B_TRY(nh_prefill_embed_seqs(prm + p0, P, B, cc, m.embd, m.te, d, V, h, &state->error, s));
+    for (int l = 0; l < static_cast<int>(L); ++l) {
+      const LayerView& Lv = m.layers[l];
+      float* kc = kv + static_cast<size_t>(2 * l) * B * max_seq * dkv;
+      float* vc = kv + static_cast<size_t>(2 * l + 1) * B * max_seq * dkv;
+      NH_B_TRY(nh_batch_prep(h, d, r, Lv.attn_norm, eps, 1, d, q8, nullptr, s));
+      NH_B_TRY(dense(Lv.wq, Lv.tq, d, d, q8, q, d, NH_ROWDOT_STORE, r));
+      NH_B_TRY(dense(Lv.wk, Lv.tk, dkv, d, q8, kk, dkv, NH_ROWDOT_STORE, r));
+      NH_B_TRY(dense(Lv.wv, Lv.tv, dkv, d, q8, v, dkv, NH_ROWDOT_STORE, r));
+      NH_B_TRY(nh_prefill_qk_seqs(q, kk, v, Lv.q_norm, Lv.k_norm, eps, B, cc, p0, c.n_head, c.n_head_kv,
+                                  static_cast<int>(hd), rope, kc, vc, max_seq, qr, s));
+      NH_B_TRY(nh_prefill_attention_seqs(qr, B, cc, p0, c.n_head, c.n_head_kv, static_cast<int>(hd), kq_scale, kc, vc,
+                                         max_seq, att, s));
+      NH_B_TRY(nh_batch_prep(att, d, r, nullptr, eps, 0, d, q8, nullptr, s));
+      NH_B_TRY(dense(Lv.wo, Lv.to, d, d, q8, h, d, NH_ROWDOT_RESIDUAL, r));
+      NH_B_TRY(moe(l, Lv, r));
+    }
+    return NH_OK;
   };
   auto step = [&]() -> int {
     NH_B_TRY(nh_batch_embed(state, prm, P, fed, B, m.embd, m.te, d, V, h, s));
@@ -242,80 +353,19 @@ std::vector<std::vector<int32_t>> RunBatch(const ModelView& m, const OlmoeConfig
       float* kc = kv + static_cast<size_t>(2 * l) * B * max_seq * dkv;
       float* vc = kv + static_cast<size_t>(2 * l + 1) * B * max_seq * dkv;
       NH_B_TRY(nh_batch_prep(h, d, B, Lv.attn_norm, eps, 1, d, q8, nullptr, s));
-      NH_B_TRY(dense(Lv.wq, Lv.tq, d, d, q8, q, d, NH_ROWDOT_STORE));
-      NH_B_TRY(dense(Lv.wk, Lv.tk, dkv, d, q8, kk, dkv, NH_ROWDOT_STORE));
-      NH_B_TRY(dense(Lv.wv, Lv.tv, dkv, d, q8, v, dkv, NH_ROWDOT_STORE));
+      NH_B_TRY(dense(Lv.wq, Lv.tq, d, d, q8, q, d, NH_ROWDOT_STORE, B));
+      NH_B_TRY(dense(Lv.wk, Lv.tk, dkv, d, q8, kk, dkv, NH_ROWDOT_STORE, B));
+      NH_B_TRY(dense(Lv.wv, Lv.tv, dkv, d, q8, v, dkv, NH_ROWDOT_STORE, B));
       NH_B_TRY(nh_batch_qk(state, q, kk, v, Lv.q_norm, Lv.k_norm, eps, B, c.n_head, c.n_head_kv,
                            static_cast<int>(hd), rope, kc, vc, max_seq, qr, s));
       NH_B_TRY(nh_batch_attention(state, qr, B, c.n_head, c.n_head_kv, static_cast<int>(hd), kq_scale, kc, vc,
                                   max_seq, attn_scratch, att, s));
       NH_B_TRY(nh_batch_prep(att, d, B, nullptr, eps, 0, d, q8, nullptr, s));
-      NH_B_TRY(dense(Lv.wo, Lv.to, d, d, q8, h, d, NH_ROWDOT_RESIDUAL));
-      NH_B_TRY(nh_batch_prep(h, d, B, Lv.ffn_norm, eps, 1, d, q8, xn, s));
-      NH_B_TRY(nh_batch_router(xn, Lv.router, B, d, static_cast<int>(E), static_cast<int>(K), norm_topk ? 1 : 0,
-                               sel, wts, s));
-      if (se != nullptr) {
-        NH_B_TRY(StreamedMoe(*se, l, Lv, c, B, sel, wts, sel_host, plan_host, off, cnt, act_idx, out_idx, q8, ff, q8ff,
-                             y, h, bb.event_, s));
-        continue;
-      }
-      if (W > 1) NH_B_TRY(ExchangeTokens(*ep, q8, q8_row * B, q8_all, sel, BK, sel_all, s));
-      // The owned experts over every rank's tokens: token j of the
-      // gathered rows is rank j / B's sequence j % B.
-      NH_B_TRY(nh_batch_moe_plan_range(sel_all, BW, static_cast<int>(K), static_cast<int>(shard.first),
-                                       static_cast<int>(shard.count), off, cnt, act_idx, out_idx, s));
-      NhGroupedRowDot g;
-      std::memset(&g, 0, sizeof(g));
-      g.w = static_cast<const uint8_t*>(Lv.gate) + e_skip * Lv.gate_nb2;
-      g.w2 = static_cast<const uint8_t*>(Lv.up) + e_skip * Lv.up_nb2;
-      g.mstride = Lv.gate_nb2;
-      g.mstride2 = Lv.up_nb2;
-      g.type = Lv.tg;
-      g.type2 = Lv.tu;
-      g.n = d;
-      g.rows = F;
-      g.n_groups = static_cast<int32_t>(shard.count);
-      g.off = off;
-      g.cnt = cnt;
-      g.act_idx = act_idx;
-      g.out_idx = out_idx;
-      g.max_tokens = BW;
-      g.q8 = q8_all;
-      g.out = ff;
-      g.out_stride = F;
-      g.mode = NH_ROWDOT_SWIGLU;
-      NH_B_TRY(nh_batch_rowdot(&g, s));
-      NH_B_TRY(nh_batch_prep(ff, F, BKW, nullptr, eps, 0, F, q8ff, nullptr, s));
-      std::memset(&g, 0, sizeof(g));
-      g.w = static_cast<const uint8_t*>(Lv.down) + e_skip * Lv.down_nb2;
-      g.mstride = Lv.down_nb2;
-      g.type = Lv.td;
-      g.type2 = Lv.td;
-      g.n = F;
-      g.rows = d;
-      g.n_groups = static_cast<int32_t>(shard.count);
-      g.off = off;
-      g.cnt = cnt;
-      g.act_idx = out_idx;  // the ff row of pair j is its (token, slot) index
-      g.out_idx = out_idx;
-      g.max_tokens = BW;
-      g.q8 = q8ff;
-      g.out = y;
-      g.out_stride = d;
-      g.mode = NH_ROWDOT_STORE;
-      NH_B_TRY(nh_batch_rowdot(&g, s));
-      if (W > 1) {
-        // Rows of rank r's picks go back to rank r; the combine takes each
-        // pick's row from the block of the rank that owns its expert.
-        NH_B_TRY(ReturnPicks(*ep, y, static_cast<size_t>(BK) * d, y_recv, s));
-        NH_B_TRY(nh_ep_combine(y_recv, static_cast<int64_t>(BK) * d, W, sel, wts, B, static_cast<int>(K), d,
-                               static_cast<int>(shard.count), h, s));
-      } else {
-        NH_B_TRY(nh_batch_combine(y, wts, B, static_cast<int>(K), d, h, s));
-      }
+      NH_B_TRY(dense(Lv.wo, Lv.to, d, d, q8, h, d, NH_ROWDOT_RESIDUAL, B));
+      NH_B_TRY(moe(l, Lv, B));
     }
     NH_B_TRY(nh_batch_prep(h, d, B, m.out_norm, eps, 1, d, q8, nullptr, s));
-    NH_B_TRY(dense(m.out, m.tout, V, d, q8, logits, V, NH_ROWDOT_STORE));
+    NH_B_TRY(dense(m.out, m.tout, V, d, q8, logits, V, NH_ROWDOT_STORE, B));
     return nh_batch_argmax(state, logits, B, V, fed, outs, n_predict, ticket, s);
   };
 
@@ -324,9 +374,16 @@ std::vector<std::vector<int32_t>> RunBatch(const ModelView& m, const OlmoeConfig
   cudaEventCreate(&ev0);
   cudaEventCreate(&ev1);
   int rc = NH_OK;
-  for (int t = 0; t < steps && rc == NH_OK; ++t) {
+  cudaEvent_t ev_pre = nullptr;
+  if (prefill) {
+    cudaEventCreate(&ev_pre);
+    cudaEventRecord(ev_pre, s);
+    for (int p0 = 0; p0 < P - 1 && rc == NH_OK; p0 += C) rc = prefill_chunk(p0, std::min(C, P - 1 - p0));
+  }
+  const int t_start = prefill ? P - 1 : 0;
+  for (int t = t_start; t < steps && rc == NH_OK; ++t) {
     if (t == P - 1) cudaEventRecord(ev0, s);  // decode: from the last prompt position on
-    if (t == 0 || !o.use_graph) {
+    if (t == t_start || !o.use_graph) {
       // The first step runs eagerly: it configures the kernels' shared-memory
       // limits outside of stream capture.
       rc = step();
@@ -349,6 +406,11 @@ std::vector<std::vector<int32_t>> RunBatch(const ModelView& m, const OlmoeConfig
   if (cudaStreamSynchronize(s) != cudaSuccess && rc == NH_OK) rc = NH_E_CUDA;
   float ms = 0.f;
   if (rc == NH_OK && cudaEventElapsedTime(&ms, ev0, ev1) == cudaSuccess) o.decode_ms = ms;
+  o.prefill_ms = 0;
+  if (ev_pre != nullptr) {
+    if (rc == NH_OK && cudaEventElapsedTime(&ms, ev_pre, ev0) == cudaSuccess) o.prefill_ms = ms;
+    cudaEventDestroy(ev_pre);
+  }
   cudaEventDestroy(ev0);
   cudaEventDestroy(ev1);
   NhDecodeState st;

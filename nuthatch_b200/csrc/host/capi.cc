@@ -174,8 +174,9 @@ int nh_generate_launches(const void* model) {
   return n > 0 ? n : 2 + 6 * static_cast<int>(m->config().n_layers);
 }
 
-int nh_generate_batch(void* model, const int32_t* prompts, int n_seq, int n_prompt, int n_predict, int norm_topk,
-                      int use_graph, int32_t* out_tokens, double* decode_ms) {
+int nh_generate_batch_timed(void* model, const void* ep, const int32_t* prompts, int n_seq, int n_prompt,
+                            int n_predict, int norm_topk, int use_graph, int32_t* out_tokens, double* prefill_ms,
+                            double* decode_ms) {
   if (model == nullptr || prompts == nullptr || out_tokens == nullptr || n_seq <= 0 || n_prompt <= 0 ||
       n_predict <= 0) {
     SetErr("nh_generate_batch: bad argument");
@@ -186,6 +187,7 @@ int nh_generate_batch(void* model, const int32_t* prompts, int n_seq, int n_prom
     p[b].assign(prompts + static_cast<size_t>(b) * n_prompt, prompts + static_cast<size_t>(b + 1) * n_prompt);
   BatchOptions o;
   o.use_graph = use_graph != 0;
+  o.ep = static_cast<const ExpertGroup*>(ep);
   const auto ids = GreedyGenerateCachedBatch(*static_cast<const OlmoeModel*>(model), p, n_predict, norm_topk != 0, &o);
   if (o.status != NH_OK) {
     SetErr("nh_generate_batch: failed with code " + std::to_string(o.status));
@@ -193,8 +195,15 @@ int nh_generate_batch(void* model, const int32_t* prompts, int n_seq, int n_prom
   }
   for (int b = 0; b < n_seq; ++b)
     std::memcpy(out_tokens + static_cast<size_t>(b) * n_predict, ids[b].data(), static_cast<size_t>(n_predict) * 4);
+  if (prefill_ms != nullptr) *prefill_ms = o.prefill_ms;
   if (decode_ms != nullptr) *decode_ms = o.decode_ms;
   return NH_OK;
+}
+
+int nh_generate_batch(void* model, const int32_t* prompts, int n_seq, int n_prompt, int n_predict, int norm_topk,
+                      int use_graph, int32_t* out_tokens, double* decode_ms) {
+  return nh_generate_batch_timed(model, nullptr, prompts, n_seq, n_prompt, n_predict, norm_topk, use_graph,
+                                 out_tokens, nullptr, decode_ms);
 }
 
 void* nh_model_load_expert_shard(const char* path, uint32_t first, uint32_t count) {
@@ -219,26 +228,12 @@ void nh_ep_free(void* ep) { delete static_cast<ExpertGroup*>(ep); }
 
 int nh_generate_batch_ep(void* model, const void* ep, const int32_t* prompts, int n_seq, int n_prompt, int n_predict,
                          int norm_topk, int use_graph, int32_t* out_tokens, double* decode_ms) {
-  if (model == nullptr || prompts == nullptr || out_tokens == nullptr || n_seq <= 0 || n_prompt <= 0 ||
-      n_predict <= 0) {
-    SetErr("nh_generate_batch_ep: bad argument");
+  if (ep == nullptr) {
+    SetErr("nh_generate_batch_ep: null group");
     return NH_E_ARG;
   }
-  std::vector<std::vector<int32_t>> p(n_seq);
-  for (int b = 0; b < n_seq; ++b)
-    p[b].assign(prompts + static_cast<size_t>(b) * n_prompt, prompts + static_cast<size_t>(b + 1) * n_prompt);
-  BatchOptions o;
-  o.use_graph = use_graph != 0;
-  o.ep = static_cast<const ExpertGroup*>(ep);
-  const auto ids = GreedyGenerateCachedBatch(*static_cast<const OlmoeModel*>(model), p, n_predict, norm_topk != 0, &o);
-  if (o.status != NH_OK) {
-    SetErr("nh_generate_batch_ep: failed with code " + std::to_string(o.status));
-    return o.status;
-  }
-  for (int b = 0; b < n_seq; ++b)
-    std::memcpy(out_tokens + static_cast<size_t>(b) * n_predict, ids[b].data(), static_cast<size_t>(n_predict) * 4);
-  if (decode_ms != nullptr) *decode_ms = o.decode_ms;
-  return NH_OK;
+  return nh_generate_batch_timed(model, ep, prompts, n_seq, n_prompt, n_predict, norm_topk, use_graph, out_tokens,
+                                 nullptr, decode_ms);
 }
 
 int nh_decode_prepare(void* model, const int32_t* prompt, int n_prompt, int n_predict) {

@@ -88,12 +88,14 @@ __global__ void batch_embed_kernel(const NhDecodeState* state, const int32_t* pr
 
 // Row r of h = embedding row of ids[r] (the prompt positions of a prefill).
 // Ids outside the vocabulary read row 0 and raise *err (when not null).
-__global__ void rows_embed_kernel(const int32_t* ids, const uint8_t* table, int type, int n_embd, int n_vocab,
-                                  uint64_t rb, float* h, int32_t* err) {
+// Row r is id i = r % n_tok of sequence r / n_tok, read at ids[seq *
+// ids_stride + i].
+__global__ void rows_embed_kernel(const int32_t* ids, int n_tok, int64_t ids_stride, const uint8_t* table, int type,
+                                  int n_embd, int n_vocab, uint64_t rb, float* h, int32_t* err) {
   const int r = blockIdx.x;
   pdl_wait();
   pdl_trigger();
-  int tok = ids[r];
+  int tok = ids[static_cast<int64_t>(r / n_tok) * ids_stride + r % n_tok];
   if (tok < 0 || tok >= n_vocab) {
     if (threadIdx.x == 0 && err != nullptr) atomicCAS(err, 0, NH_E_ARG);
     tok = 0;
@@ -615,22 +617,22 @@ __global__ void __launch_bounds__(kBatchWarps * 32, 2) batch_mma_kernel(const Gr
 // the shared position, the rotated q to qr, and the new K (rotated) and V
 // rows appended to the sequence's cache ([B][max_seq][n_embd_kv] per layer).
 //
-// Row b is at position base + b*pos_step (base = state->pos, or pos0 when
-// state is null) and appends to cache sequence b*seq_step: decode rows are
-// independent sequences at the shared cursor (pos_step 0, seq_step 1);
-// prefill rows are consecutive positions of one sequence (1, 0).
+// Row b is position base + b % rows_per_seq (base = state->pos, or pos0 when
+// state is null) of cache sequence b / rows_per_seq: decode rows are
+// independent sequences at the shared cursor (rows_per_seq 1); prefill rows
+// are runs of rows_per_seq consecutive positions, one run per sequence.
 __global__ void __launch_bounds__(128) batch_qk_kernel(const NhDecodeState* state, const float* q, const float* k,
                                                        const float* v, const float* q_norm, const float* k_norm,
                                                        float eps, int n_head, int n_head_kv, int hd,
                                                        const float* rope_cs, float* k_cache, float* v_cache,
-                                                       int max_seq, float* qr, int pos0, int pos_step, int seq_step) {
+                                                       int max_seq, float* qr, int pos0, int rows_per_seq) {
   const int b = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
   const int dq = n_head * hd, dkv = n_head_kv * hd, half = hd / 2;
   __shared__ double red[16];
   pdl_wait();
   pdl_trigger();
-  const int pos = (state != nullptr ? state->pos : pos0) + b * pos_step;
-  const int64_t seq = static_cast<int64_t>(b) * seq_step;
+  const int pos = (state != nullptr ? state->pos : pos0) + b % rows_per_seq;
+  const int64_t seq = b / rows_per_seq;
   extern __shared__ __align__(16) float qk_s[];  // [dq] q row, [dkv] k row
   copy_to_smem(qk_s, q + static_cast<int64_t>(b) * dq, dq);
   copy_to_smem(qk_s + dq, k + static_cast<int64_t>(b) * dkv, dkv);
@@ -903,11 +905,11 @@ __device__ __forceinline__ void bscore_pair(const float* kr, const float* qa, co
 }
 
 struct PAttnArgs {
-  const float* qr;       // [n_tok][n_head*hd] QK-normed, rotated queries
-  const float* k_cache;  // [max_seq][n_head_kv*hd] post-RoPE keys of this sequence
+  const float* qr;       // [n_seq][n_tok][n_head*hd] QK-normed, rotated queries
+  const float* k_cache;  // [n_seq][max_seq][n_head_kv*hd] post-RoPE keys
   const float* v_cache;
-  float* out;            // [n_tok][n_head*hd]
-  int n_tok, pos0, n_head, n_head_kv, hd;
+  float* out;            // [n_seq][n_tok][n_head*hd]
+  int n_tok, pos0, n_head, n_head_kv, hd, max_seq;
   float kq_scale;
 };
 
@@ -915,12 +917,15 @@ __device__ __forceinline__ int pattn_keys_in_split(int n_kv, int s) {
   return max(0, min(kPAttnSplit, n_kv - s * kPAttnSplit));
 }
 
+// Grid (head, query block, sequence).
 __global__ void __launch_bounds__(kPAttnThreads, 2) prefill_attention_kernel(const PAttnArgs p) {
   const int h = blockIdx.x, t0 = blockIdx.y * kPAttnQ;
   const int nq = min(kPAttnQ, p.n_tok - t0);
   const int hd = p.hd, kst = hd + 4;
   const int kh = h / (p.n_head / p.n_head_kv);
   const int dq = p.n_head * hd, dkv = p.n_head_kv * hd;
+  const int64_t row0 = static_cast<int64_t>(blockIdx.z) * p.n_tok;  // the sequence's first row
+  const int64_t kv0 = static_cast<int64_t>(blockIdx.z) * p.max_seq * dkv;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   extern __shared__ __align__(16) float sm[];
   float* Ks = sm;                      // [64][hd+4]: padded rows for conflict-free 16-byte reads
@@ -936,7 +941,7 @@ __global__ void __launch_bounds__(kPAttnThreads, 2) prefill_attention_kernel(con
   for (int i = tid; i < kPAttnQ * h4; i += blockDim.x) {
     const int q = i / h4, c = i % h4;
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (q < nq) v = reinterpret_cast<const float4*>(p.qr + static_cast<int64_t>(t0 + q) * dq + h * hd)[c];
+    if (q < nq) v = reinterpret_cast<const float4*>(p.qr + (row0 + t0 + q) * dq + h * hd)[c];
     reinterpret_cast<float4*>(Qs + q * hd)[c] = v;
   }
   if (tid < kPAttnQ) s_L[tid] = 0.0;
@@ -948,7 +953,7 @@ __global__ void __launch_bounds__(kPAttnThreads, 2) prefill_attention_kernel(con
     const int64_t r0 = static_cast<int64_t>(s) * kPAttnSplit;
     for (int i = tid; i < nk * h4; i += blockDim.x) {
       const int r = i / h4, c = i % h4;
-      const int64_t g = (r0 + r) * dkv + kh * hd;
+      const int64_t g = kv0 + (r0 + r) * dkv + kh * hd;
       reinterpret_cast<float4*>(Ks + r * kst)[c] = __ldg(reinterpret_cast<const float4*>(p.k_cache + g) + c);
       if (with_v) reinterpret_cast<float4*>(Vs + r * hd)[c] = __ldg(reinterpret_cast<const float4*>(p.v_cache + g) + c);
     }
@@ -1059,7 +1064,7 @@ __global__ void __launch_bounds__(kPAttnThreads, 2) prefill_attention_kernel(con
     const int idx = tid + it * kPAttnThreads, q = idx / hd, i = idx % hd;
     if (q >= nq) continue;
     const float v = n_kv(q) <= kPAttnSplit ? acc_out[it] : __fmul_rn(acc_out[it], static_cast<float>(1.0 / s_L[q]));
-    p.out[static_cast<int64_t>(t0 + q) * dq + h * hd + i] = v;
+    p.out[(row0 + t0 + q) * dq + h * hd + i] = v;
   }
 }
 
@@ -1482,8 +1487,7 @@ extern "C" int nh_batch_qk(const NhDecodeState* state, const float* q, const flo
   static SmemLimit configured;
   if (smem > 220 * 1024 || !ensure_smem(batch_qk_kernel, smem, configured)) return NH_E_ARG;
   return launch_pdl(batch_qk_kernel, dim3(n_seq), dim3(128), smem, static_cast<cudaStream_t>(stream), state, q, k, v,
-                    q_norm, k_norm, eps, n_head, n_head_kv, head_dim, rope_cs, k_cache, v_cache, max_seq, qr, 0, 0,
-                    1);
+                    q_norm, k_norm, eps, n_head, n_head_kv, head_dim, rope_cs, k_cache, v_cache, max_seq, qr, 0, 1);
 }
 
 extern "C" int64_t nh_batch_attention_scratch_bytes(int n_seq, int n_head, int head_dim, int max_seq) {
@@ -1529,39 +1533,58 @@ extern "C" int nh_batch_attention(const NhDecodeState* state, const float* qr, i
                     static_cast<cudaStream_t>(stream), p);
 }
 
-extern "C" int nh_prefill_embed(const int32_t* ids, int n_tok, const void* table, int32_t type, int64_t n_embd,
-                                int64_t n_vocab, float* h, int32_t* err, void* stream) {
-  if (ids == nullptr || table == nullptr || h == nullptr || n_tok <= 0) return NH_E_ARG;
+extern "C" int nh_prefill_embed_seqs(const int32_t* ids, int64_t ids_stride, int n_seq, int n_tok, const void* table,
+                                     int32_t type, int64_t n_embd, int64_t n_vocab, float* h, int32_t* err,
+                                     void* stream) {
+  if (ids == nullptr || table == nullptr || h == nullptr || n_tok <= 0 || n_seq <= 0 ||
+      (n_seq > 1 && ids_stride < n_tok) || static_cast<int64_t>(n_seq) * n_tok > INT32_MAX)
+    return NH_E_ARG;
   if (type != NH_TYPE_F32 && type != NH_TYPE_Q4_K && type != NH_TYPE_Q6_K) return NH_E_TYPE;
   if (type != NH_TYPE_F32 && n_embd % QK != 0) return NH_E_ARG;
-  return launch_pdl(rows_embed_kernel, dim3(n_tok), dim3(256), 0, static_cast<cudaStream_t>(stream), ids,
-                    static_cast<const uint8_t*>(table), static_cast<int>(type), static_cast<int>(n_embd),
-                    static_cast<int>(n_vocab), static_cast<uint64_t>(row_bytes(type, n_embd)), h, err);
+  return launch_pdl(rows_embed_kernel, dim3(n_seq * n_tok), dim3(256), 0, static_cast<cudaStream_t>(stream), ids,
+                    n_tok, ids_stride, static_cast<const uint8_t*>(table), static_cast<int>(type),
+                    static_cast<int>(n_embd), static_cast<int>(n_vocab),
+                    static_cast<uint64_t>(row_bytes(type, n_embd)), h, err);
+}
+
+extern "C" int nh_prefill_embed(const int32_t* ids, int n_tok, const void* table, int32_t type, int64_t n_embd,
+                                int64_t n_vocab, float* h, int32_t* err, void* stream) {
+  return nh_prefill_embed_seqs(ids, n_tok, 1, n_tok, table, type, n_embd, n_vocab, h, err, stream);
+}
+
+extern "C" int nh_prefill_qk_seqs(const float* q, const float* k, const float* v, const float* q_norm,
+                                  const float* k_norm, float eps, int n_seq, int n_tok, int pos0, int n_head,
+                                  int n_head_kv, int head_dim, const float* rope_cs, float* k_cache, float* v_cache,
+                                  int max_seq, float* qr, void* stream) {
+  if (q == nullptr || k == nullptr || v == nullptr || q_norm == nullptr || k_norm == nullptr || rope_cs == nullptr ||
+      k_cache == nullptr || v_cache == nullptr || qr == nullptr || n_seq <= 0 || n_tok <= 0 || pos0 < 0 ||
+      head_dim % 2 != 0 || n_head <= 0 || n_head_kv <= 0 || n_head % n_head_kv != 0 || pos0 + n_tok > max_seq ||
+      static_cast<int64_t>(n_seq) * n_tok > INT32_MAX)
+    return NH_E_ARG;
+  const size_t smem = static_cast<size_t>(n_head + n_head_kv) * head_dim * sizeof(float);
+  static SmemLimit configured;
+  if (smem > 220 * 1024 || !ensure_smem(batch_qk_kernel, smem, configured)) return NH_E_ARG;
+  return launch_pdl(batch_qk_kernel, dim3(n_seq * n_tok), dim3(128), smem, static_cast<cudaStream_t>(stream),
+                    static_cast<const NhDecodeState*>(nullptr), q, k, v, q_norm, k_norm, eps, n_head, n_head_kv,
+                    head_dim, rope_cs, k_cache, v_cache, max_seq, qr, pos0, n_tok);
 }
 
 extern "C" int nh_prefill_qk(const float* q, const float* k, const float* v, const float* q_norm, const float* k_norm,
                              float eps, int n_tok, int pos0, int n_head, int n_head_kv, int head_dim,
                              const float* rope_cs, float* k_cache, float* v_cache, int max_seq, float* qr,
                              void* stream) {
-  if (q == nullptr || k == nullptr || v == nullptr || q_norm == nullptr || k_norm == nullptr || rope_cs == nullptr ||
-      k_cache == nullptr || v_cache == nullptr || qr == nullptr || n_tok <= 0 || pos0 < 0 || head_dim % 2 != 0 ||
-      n_head <= 0 || n_head_kv <= 0 || n_head % n_head_kv != 0 || pos0 + n_tok > max_seq)
-    return NH_E_ARG;
-  const size_t smem = static_cast<size_t>(n_head + n_head_kv) * head_dim * sizeof(float);
-  static SmemLimit configured;
-  if (smem > 220 * 1024 || !ensure_smem(batch_qk_kernel, smem, configured)) return NH_E_ARG;
-  return launch_pdl(batch_qk_kernel, dim3(n_tok), dim3(128), smem, static_cast<cudaStream_t>(stream),
-                    static_cast<const NhDecodeState*>(nullptr), q, k, v, q_norm, k_norm, eps, n_head, n_head_kv,
-                    head_dim, rope_cs, k_cache, v_cache, max_seq, qr, pos0, 1, 0);
+  return nh_prefill_qk_seqs(q, k, v, q_norm, k_norm, eps, 1, n_tok, pos0, n_head, n_head_kv, head_dim, rope_cs,
+                            k_cache, v_cache, max_seq, qr, stream);
 }
 
-extern "C" int nh_prefill_attention(const float* qr, int n_tok, int pos0, int n_head, int n_head_kv, int head_dim,
-                                    float kq_scale, const float* k_cache, const float* v_cache, int max_seq,
-                                    float* out, void* stream) {
-  if (qr == nullptr || k_cache == nullptr || v_cache == nullptr || out == nullptr || n_tok <= 0 || pos0 < 0 ||
-      pos0 + n_tok > max_seq || n_head <= 0 || n_head_kv <= 0 || n_head % n_head_kv != 0 || head_dim % 32 != 0 ||
-      head_dim > 128 || (reinterpret_cast<uintptr_t>(k_cache) & 15) != 0 ||
-      (reinterpret_cast<uintptr_t>(v_cache) & 15) != 0 || (reinterpret_cast<uintptr_t>(qr) & 15) != 0)
+extern "C" int nh_prefill_attention_seqs(const float* qr, int n_seq, int n_tok, int pos0, int n_head, int n_head_kv,
+                                         int head_dim, float kq_scale, const float* k_cache, const float* v_cache,
+                                         int max_seq, float* out, void* stream) {
+  if (qr == nullptr || k_cache == nullptr || v_cache == nullptr || out == nullptr || n_seq <= 0 || n_seq > 65535 ||
+      n_tok <= 0 || pos0 < 0 || pos0 + n_tok > max_seq || n_head <= 0 || n_head_kv <= 0 ||
+      n_head % n_head_kv != 0 || head_dim % 32 != 0 || head_dim > 128 ||
+      (reinterpret_cast<uintptr_t>(k_cache) & 15) != 0 || (reinterpret_cast<uintptr_t>(v_cache) & 15) != 0 ||
+      (reinterpret_cast<uintptr_t>(qr) & 15) != 0)
     return NH_E_ARG;
   PAttnArgs p;
   p.qr = qr;
@@ -1573,13 +1596,21 @@ extern "C" int nh_prefill_attention(const float* qr, int n_tok, int pos0, int n_
   p.n_head = n_head;
   p.n_head_kv = n_head_kv;
   p.hd = head_dim;
+  p.max_seq = max_seq;
   p.kq_scale = kq_scale;
   const size_t smem = static_cast<size_t>(kPAttnSplit * (head_dim + 4) + kPAttnSplit * head_dim +
                                           kPAttnQ * head_dim + kPAttnQ * kPAttnSplit) * sizeof(float);
   static SmemLimit configured;
   if (!ensure_smem(prefill_attention_kernel, smem, configured)) return NH_E_CUDA;
-  return launch_pdl(prefill_attention_kernel, dim3(n_head, (n_tok + kPAttnQ - 1) / kPAttnQ), dim3(kPAttnThreads),
-                    smem, static_cast<cudaStream_t>(stream), p);
+  return launch_pdl(prefill_attention_kernel, dim3(n_head, (n_tok + kPAttnQ - 1) / kPAttnQ, n_seq),
+                    dim3(kPAttnThreads), smem, static_cast<cudaStream_t>(stream), p);
+}
+
+extern "C" int nh_prefill_attention(const float* qr, int n_tok, int pos0, int n_head, int n_head_kv, int head_dim,
+                                    float kq_scale, const float* k_cache, const float* v_cache, int max_seq,
+                                    float* out, void* stream) {
+  return nh_prefill_attention_seqs(qr, 1, n_tok, pos0, n_head, n_head_kv, head_dim, kq_scale, k_cache, v_cache,
+                                   max_seq, out, stream);
 }
 
 extern "C" int nh_batch_router_trace(const float* xn, const float* router, int n_seq, int64_t n_embd, int n_expert,

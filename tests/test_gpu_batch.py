@@ -51,3 +51,29 @@ def test_batch_rejects_ragged_prompts(gpu, synth_dir):
     m = nh.OlmoeModel.Load(str(synth.cached(synth.MINI, synth_dir)))
     with pytest.raises(ValueError):
         nh.generate_batch_ex(m, [[1, 2, 3], [4, 5]], 2, False)
+
+
+@pytest.mark.parametrize("spec_name,n_seq,n_prompt,n_predict", [
+    ("MINI", 3, 200, 4),        # two chunks of 170 + 29 positions
+    ("MINI_GQA", 64, 20, 3),    # 8 positions x 64 sequences per chunk, a ragged last chunk
+    ("MINI", 520, 3, 2),        # more sequences than one chunk's rows: one position per chunk
+    ("OLMOE_1B7B", 8, 150, 4),  # configuration 4's shape, cut short: 512-row chunks on the tensor cores
+])
+def test_batched_prefill_matches_position_by_position(gpu, synth_dir, monkeypatch, spec_name, n_seq, n_prompt,
+                                                      n_predict):
+    """The chunked prompt prefill (positions 0..P-2 of every sequence as rows
+    of the batched kernels) gives the same ids as running the prompt one
+    position per step (NH_BATCH_PREFILL=0)."""
+    path = str(synth.cached(getattr(synth, spec_name), synth_dir))
+    m = nh.OlmoeModel.Load(path)
+    prompts = _prompts(n_seq, n_prompt, m.config().n_vocab, 300 + n_seq)
+    got = nh.generate_batch_ex(m, prompts, n_predict, False)
+    assert got["prefill_ms"] > 0
+    monkeypatch.setenv("NH_BATCH_PREFILL", "0")
+    ref = nh.generate_batch_ex(m, prompts, n_predict, False)
+    monkeypatch.delenv("NH_BATCH_PREFILL")
+    assert ref["prefill_ms"] == 0
+    assert got["tokens"] == ref["tokens"]
+    for b in (0, n_seq - 1):
+        assert got["tokens"][b] == nh.GreedyGenerateCached(m, prompts[b], n_predict, False), b
+    m.close()

@@ -85,6 +85,69 @@ def test_prefill_attention_matches_position_by_position(gpu, n_head, n_head_kv, 
     assert np.array_equal(vc["pf"].cpu().numpy(), vc["step"].cpu().numpy())
 
 
+@pytest.mark.parametrize("n_seq,n_tok,pos0", [(3, 40, 0), (5, 17, 90), (2, 70, 33)])
+def test_prefill_seqs_match_one_sequence_at_a_time(gpu, n_seq, n_tok, pos0):
+    """The one-launch forms over n_seq sequences (embed with strided ids,
+    QK/append into per-sequence caches, causal attention) equal the
+    single-sequence forms called once per sequence."""
+    import torch
+
+    L = lib()
+    dev = torch.device("cuda")
+    rng = np.random.default_rng(7 * n_seq + n_tok)
+    n_head, n_head_kv, head_dim = 16, 8, 64
+    dq, dkv = n_head * head_dim, n_head_kv * head_dim
+    max_seq = pos0 + n_tok + 5
+    n_vocab, P_ids = 300, pos0 + n_tok + 3
+    eps, scale = 1e-5, 1.0 / float(np.sqrt(head_dim))
+    cs = np.zeros(max_seq * head_dim, dtype=np.float32)
+    L.nh_rope_table(10000.0, head_dim, max_seq, cs.ctypes.data_as(C.POINTER(C.c_float)))
+    rope = torch.from_numpy(cs).to(dev)
+    qn = torch.from_numpy(rng.uniform(0.5, 1.5, dq).astype(np.float32)).to(dev)
+    kn = torch.from_numpy(rng.uniform(0.5, 1.5, dkv).astype(np.float32)).to(dev)
+    R = n_seq * n_tok
+    q = torch.from_numpy(rng.standard_normal((R, dq)).astype(np.float32)).to(dev)
+    k = torch.from_numpy(rng.standard_normal((R, dkv)).astype(np.float32)).to(dev)
+    v = torch.from_numpy(rng.standard_normal((R, dkv)).astype(np.float32)).to(dev)
+    cache0 = rng.standard_normal((2, n_seq, max_seq, dkv)).astype(np.float32)
+    kc = {n: torch.from_numpy(cache0[0].copy()).to(dev) for n in ("all", "one")}
+    vc = {n: torch.from_numpy(cache0[1].copy()).to(dev) for n in ("all", "one")}
+    table = torch.from_numpy(rng.standard_normal((n_vocab, dq)).astype(np.float32)).to(dev)
+    ids = torch.from_numpy(rng.integers(0, n_vocab, (n_seq, P_ids)).astype(np.int32)).to(dev)
+    P = lambda t: C.c_void_p(t.data_ptr())
+    s = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    h_all, qr_all, out_all = (torch.empty(R, dq, device=dev) for _ in range(3))
+    assert L.nh_prefill_embed_seqs(C.c_void_p(ids.data_ptr() + 4 * pos0), P_ids, n_seq, n_tok, P(table), 0, dq,
+                                   n_vocab, P(h_all), P(err), s) == 0
+    assert L.nh_prefill_qk_seqs(P(q), P(k), P(v), P(qn), P(kn), eps, n_seq, n_tok, pos0, n_head, n_head_kv, head_dim,
+                                P(rope), P(kc["all"]), P(vc["all"]), max_seq, P(qr_all), s) == 0
+    assert L.nh_prefill_attention_seqs(P(qr_all), n_seq, n_tok, pos0, n_head, n_head_kv, head_dim, scale,
+                                       P(kc["all"]), P(vc["all"]), max_seq, P(out_all), s) == 0
+
+    h_one, qr_one, out_one = (torch.empty(R, dq, device=dev) for _ in range(3))
+    for b in range(n_seq):
+        rows = slice(b * n_tok, (b + 1) * n_tok)
+        assert L.nh_prefill_embed(C.c_void_p(ids[b].data_ptr() + 4 * pos0), n_tok, P(table), 0, dq, n_vocab,
+                                  P(h_one[rows]), P(err), s) == 0
+        assert L.nh_prefill_qk(P(q[rows]), P(k[rows]), P(v[rows]), P(qn), P(kn), eps, n_tok, pos0, n_head,
+                               n_head_kv, head_dim, P(rope), P(kc["one"][b]), P(vc["one"][b]), max_seq,
+                               P(qr_one[rows]), s) == 0
+        assert L.nh_prefill_attention(P(qr_one[rows]), n_tok, pos0, n_head, n_head_kv, head_dim, scale,
+                                      P(kc["one"][b]), P(vc["one"][b]), max_seq, P(out_one[rows]), s) == 0
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    want_h = table.cpu().numpy()[ids.cpu().numpy()[:, pos0:pos0 + n_tok].reshape(-1)]
+    assert np.array_equal(h_all.cpu().numpy(), want_h)
+    assert np.array_equal(h_all.cpu().numpy(), h_one.cpu().numpy())
+    assert np.array_equal(qr_all.cpu().numpy(), qr_one.cpu().numpy())
+    assert np.all(np.isfinite(out_all.cpu().numpy()))
+    assert np.array_equal(out_all.cpu().numpy(), out_one.cpu().numpy())
+    assert np.array_equal(kc["all"].cpu().numpy(), kc["one"].cpu().numpy())
+    assert np.array_equal(vc["all"].cpu().numpy(), vc["one"].cpu().numpy())
+
+
 def test_prefill_rejects_shapes_it_does_not_cover(gpu):
     L = lib()
     null = None
