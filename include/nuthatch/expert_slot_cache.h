@@ -113,7 +113,13 @@ class ExpertSlotCache {
   std::string gate_name_, up_name_, down_name_;
   DTensor gate_, up_, down_;
   void* base_ = nullptr;
-  void* bounce_ = nullptr;  // pinned bounce buffer for reader fills
+  // Reader fills: a ring of pinned bounce buffers, each reused only after the
+  // event recorded behind its last copies has completed, so the disk read of
+  // one fill overlaps the host-to-device copies of the previous ones.
+  static constexpr int kBounce = 3;
+  void* bounce_[kBounce] = {nullptr, nullptr, nullptr};
+  void* bounce_done_[kBounce] = {nullptr, nullptr, nullptr};
+  int bounce_next_ = 0;
   void* copy_stream_ = nullptr;
   void* fill_event_ = nullptr;
   int capacity_ = 0;

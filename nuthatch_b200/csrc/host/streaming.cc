@@ -90,7 +90,12 @@ std::unique_ptr<ExpertSlotCache> ExpertSlotCache::Create(const OlmoeConfig& cfg,
   c->slot_to_id_.assign(slots, -1);
   c->slot_tick_.assign(slots, 0);
   if (!c->has_store_) {
-    if (cudaHostAlloc(&c->bounce_, gb + ub + db, cudaHostAllocDefault) != cudaSuccess) return nullptr;
+    for (int i = 0; i < kBounce; ++i) {
+      if (cudaHostAlloc(&c->bounce_[i], gb + ub + db, cudaHostAllocDefault) != cudaSuccess ||
+          cudaEventCreateWithFlags(reinterpret_cast<cudaEvent_t*>(&c->bounce_done_[i]), cudaEventDisableTiming) !=
+              cudaSuccess)
+        return nullptr;
+    }
   }
   cudaEventCreateWithFlags(reinterpret_cast<cudaEvent_t*>(&c->fill_event_), cudaEventDisableTiming);
   // Learned pin: preload the hottest experts into the pinned slots.
@@ -115,7 +120,10 @@ ExpertSlotCache::~ExpertSlotCache() {
   else cudaDeviceSynchronize();
   if (fill_event_ != nullptr) cudaEventDestroy(static_cast<cudaEvent_t>(fill_event_));
   if (base_ != nullptr) cudaFree(base_);
-  if (bounce_ != nullptr) cudaFreeHost(bounce_);
+  for (int i = 0; i < kBounce; ++i) {
+    if (bounce_[i] != nullptr) cudaFreeHost(bounce_[i]);
+    if (bounce_done_[i] != nullptr) cudaEventDestroy(static_cast<cudaEvent_t>(bounce_done_[i]));
+  }
 }
 
 void ExpertSlotCache::Restart() {
@@ -151,18 +159,22 @@ bool ExpertSlotCache::Fill(int slot, int expert) {
     if (ok) h2d_bytes_ += store_.gate_bytes + store_.up_bytes + store_.down_bytes;
     return ok;
   }
-  // Disk -> pinned bounce buffer -> HBM (the bounce buffer is reused, so wait
-  // for the previous fill out of it first).
-  cudaStreamSynchronize(st);
+  // Disk -> the next pinned bounce buffer of the ring -> HBM.  The buffer's
+  // previous copies must have left it before the disk read overwrites it.
+  const int i = bounce_next_;
+  bounce_next_ = (bounce_next_ + 1) % kBounce;
+  cudaEvent_t done = static_cast<cudaEvent_t>(bounce_done_[i]);
+  if (cudaEventSynchronize(done) != cudaSuccess) return false;
   const size_t gb = reader_->ExpertBytes(gate_name_), ub = reader_->ExpertBytes(up_name_),
                db = reader_->ExpertBytes(down_name_);
-  uint8_t* b = static_cast<uint8_t*>(bounce_);
+  uint8_t* b = static_cast<uint8_t*>(bounce_[i]);
   if (!reader_->ReadExpert(gate_name_, expert, b) || !reader_->ReadExpert(up_name_, expert, b + gb) ||
       !reader_->ReadExpert(down_name_, expert, b + gb + ub))
     return false;
   const bool ok = cudaMemcpyAsync(g, b, gb, cudaMemcpyHostToDevice, st) == cudaSuccess &&
                   cudaMemcpyAsync(u, b + gb, ub, cudaMemcpyHostToDevice, st) == cudaSuccess &&
-                  cudaMemcpyAsync(d, b + gb + ub, db, cudaMemcpyHostToDevice, st) == cudaSuccess;
+                  cudaMemcpyAsync(d, b + gb + ub, db, cudaMemcpyHostToDevice, st) == cudaSuccess &&
+                  cudaEventRecord(done, st) == cudaSuccess;
   if (ok) h2d_bytes_ += gb + ub + db;
   return ok;
 }

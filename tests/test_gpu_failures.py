@@ -7,6 +7,8 @@ are made by the host, as a failing disk read or a truncated file would).
   stays resident, and a later Ensure of the failed id misses and fills it
   with the right bytes.  (The reference ignores a failed read and maps the
   slot regardless, expert_slot_cache.cc:96.)
+* Streaming straight from disk (no pinned host store) through the slot
+  cache's ring of bounce buffers: ids equal the resident decode.
 * GGUF files cut short in the header or in the tensor data: probing and
   loading return an error / nullptr instead of a model.
 """
@@ -58,6 +60,23 @@ def test_slot_cache_failed_fill_leaves_no_mapping(gpu, mini):
         want = rd.ReadExpert(name, 2)
         assert cache.slot_bytes(which, s2, len(want)) == want, name
         assert cache.slot_bytes(which, s1, len(want)) == rd.ReadExpert(name, 1), name
+
+
+def test_disk_backed_streaming_matches_resident(gpu, mini):
+    """Streaming without the pinned host store: every miss reads the expert
+    from disk into one of the slot cache's pinned bounce buffers (a ring of
+    three, each reused only after its copies finished) and copies it to its
+    slot; the ids equal the resident decode."""
+    prompt = np.random.default_rng(31).integers(0, 1000, 9).tolist()
+    m = nh.OlmoeModel.Load(str(mini))
+    ref = nh.GreedyGenerateCached(m, prompt, 10, False)
+    m.close()
+    sm = nh.StreamingModel.Load(str(mini), pinned_store=False)
+    for cap in (4, 6):
+        r = nh.streaming_generate_ex(sm, prompt, 10, False, cap)
+        assert r["tokens"] == ref, cap
+        assert int(r["misses"].sum()) > 0 and r["h2d_bytes"] > 0
+    sm.close()
 
 
 def test_truncated_gguf_is_refused(gpu, mini, tmp_path):
