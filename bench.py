@@ -337,7 +337,7 @@ def run_prefill(args) -> None:
     from nuthatch_b200._lib import NhConfig
 
     cfg = NhConfig()
-    assert L.nh_gguf_probe(path.encode(), C.byref(cfg)) == 0
+    assert L.nh_gguf_probe(path.encode(), C.byref(cfg)) > 0
     if n_seq % world != 0 or cfg.n_expert % world != 0:
         if rank == 0:
             print(json.dumps({"workload": "prefill", "unavailable": f"{n_seq} sequences / {cfg.n_expert} experts "
