@@ -303,6 +303,21 @@ __device__ inline void prep_act(ActSmem& a, const float* __restrict__ src, bool 
   __syncthreads();
 }
 
+// Block-wide: Q8_K quantisation of the f32 row already in a.xf (left there by
+// prep_act with quant = false), each warp its 256-value blocks: the same
+// values and arithmetic as prep_act with quant = true.  Ends synchronised.
+__device__ inline void quant_act_smem(ActSmem& a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int b = warp; b < a.K / QK; b += nw) {
+    const float* xb = a.xf + b * QK + lane * 8;
+    const float4 v0 = *reinterpret_cast<const float4*>(xb);
+    const float4 v1 = *reinterpret_cast<const float4*>(xb + 4);
+    const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    quantize_block_warp(v, b, a, lane);
+  }
+  __syncthreads();
+}
+
 // ------------------------------------------------------------ super-block dots
 // One lane computes one whole super-block's contribution.  `blk` points into
 // shared memory; `q8` is the base of the activation's quants, `b` the

@@ -877,7 +877,9 @@ __device__ __forceinline__ bool moe_run(const FusedArgs& p, uint8_t* smem, const
   const DownArgs& d = p.d;
   ActSmem a = carve_act(smem, g.K, true, true);
   const int gw = blockIdx.x * kMoeWarps + (threadIdx.x >> 5), tw = gridDim.x * kMoeWarps;
-  prep_act<true>(a, g.h, g.norm != nullptr, true, g.eps, true, red);
+  // The normalised f32 row first: the router reads it; its Q8_K form (for
+  // gate/up only) is made while the logits travel between CTAs.
+  prep_act<true>(a, g.h, g.norm != nullptr, true, g.eps, false, red);
   bool ok = true;
   if (router_cta) {
     if (router_e >= 0) {
@@ -900,6 +902,7 @@ __device__ __forceinline__ bool moe_run(const FusedArgs& p, uint8_t* smem, const
                        (static_cast<unsigned long long>(sh.tag) << 32) | __float_as_uint(sdot));
     }
   }
+  quant_act_smem(a);
   // Every CTA collects the logits itself (warp 0) and selects.
   float pr[kLogitsPerLane];
   if (threadIdx.x < 32) {
