@@ -165,12 +165,47 @@ __device__ inline void attn_finish(const AttnArgs& p, int h, int sp, int pos, co
   float* const kfull = m.kfull;
   double* const red = sh.red;
 
-  // q (and, for the CTA holding the current position, k and v) as one batch
-  // of vector loads into shared memory.
-  copy_to_smem<true>(qfull, p.q, dq);
-  if (covers_cur) {
-    copy_to_smem<true>(kfull, p.k, dkv);
-    copy_to_smem<true>(vc, p.v + kh * hd, hd);
+  // q (and, for the CTA holding the current position, k and v) into shared
+  // memory, every thread's loads of all three in flight before its first
+  // store: one L2 latency instead of one per row.
+  {
+    const float* vsrc = p.v + kh * hd;
+    const bool vec = ((reinterpret_cast<uintptr_t>(p.q) | reinterpret_cast<uintptr_t>(p.k) |
+                       reinterpret_cast<uintptr_t>(vsrc)) & 15) == 0;
+    if (vec) {
+      const int nq4 = dq / 4, nk4 = covers_cur ? dkv / 4 : 0, nv4 = covers_cur ? hd / 4 : 0;
+      const int tot = nq4 + nk4 + nv4, nthr = blockDim.x;
+      auto src = [&](int i) -> const float4* {
+        return i < nq4 ? reinterpret_cast<const float4*>(p.q) + i
+               : i < nq4 + nk4 ? reinterpret_cast<const float4*>(p.k) + (i - nq4)
+                               : reinterpret_cast<const float4*>(vsrc) + (i - nq4 - nk4);
+      };
+      auto dst = [&](int i) -> float4* {
+        return i < nq4 ? reinterpret_cast<float4*>(qfull) + i
+               : i < nq4 + nk4 ? reinterpret_cast<float4*>(kfull) + (i - nq4)
+                               : reinterpret_cast<float4*>(vc) + (i - nq4 - nk4);
+      };
+      constexpr int U = 9;
+      for (int base = tid; base < tot; base += U * nthr) {
+        float4 buf[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int i = base + u * nthr;
+          if (i < tot) buf[u] = __ldcg(src(i));
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int i = base + u * nthr;
+          if (i < tot) *dst(i) = buf[u];
+        }
+      }
+    } else {
+      copy_to_smem<true>(qfull, p.q, dq);
+      if (covers_cur) {
+        copy_to_smem<true>(kfull, p.k, dkv);
+        copy_to_smem<true>(vc, vsrc, hd);
+      }
+    }
   }
   __syncthreads();
   // RMS of the full q (and k) rows, sums of squares in double: per thread,
@@ -195,7 +230,7 @@ __device__ inline void attn_finish(const AttnArgs& p, int h, int sp, int pos, co
       tq += red[w];
       tk += red[8 + w];
     }
-    const float scq = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(tq / static_cast<double>(dq)), p.eps)));
+    const float scq = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(div_count(tq, dq)), p.eps)));
     // Normalise and rotate (NEOX pairs i, i + hd/2) in one step.
     for (int i = tid; i < half; i += nt) {
       const float c = cs[2 * i], s = cs[2 * i + 1];
@@ -206,7 +241,7 @@ __device__ inline void attn_finish(const AttnArgs& p, int h, int sp, int pos, co
     }
     if (covers_cur) {
       const float sck =
-          __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(tk / static_cast<double>(dkv)), p.eps)));
+          __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(div_count(tk, dkv)), p.eps)));
       for (int i = tid; i < half; i += nt) {
         const float c = cs[2 * i], s = cs[2 * i + 1];
         const float x0 = __fmul_rn(__fmul_rn(kfull[kh * hd + i], sck), kn[i]);

@@ -654,8 +654,8 @@ __global__ void __launch_bounds__(128) batch_qk_kernel(const NhDecodeState* stat
     tq += red[w];
     tk += red[8 + w];
   }
-  const float scq = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(tq / static_cast<double>(dq)), eps)));
-  const float sck = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(tk / static_cast<double>(dkv)), eps)));
+  const float scq = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(div_count(tq, dq)), eps)));
+  const float sck = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(div_count(tk, dkv)), eps)));
   const float* cs = rope_cs + static_cast<int64_t>(pos) * hd;
   float* qo = qr + static_cast<int64_t>(b) * dq;
   for (int j = tid; j < n_head * half; j += blockDim.x) {

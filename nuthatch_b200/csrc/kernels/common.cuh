@@ -37,6 +37,17 @@ __device__ __forceinline__ float half_bits_to_float(uint32_t bits16) {
 }
 
 __device__ __forceinline__ int q8_rot(int b) { return (b & 15) * 16; }
+
+// t / n, the mean of an RMSNorm's sum of squares.  For n a power of two,
+// t * 2^-log2(n) and t / n are the same exact real number rounded once, so
+// the multiplication gives the same double as the division.
+__device__ __forceinline__ double div_count(double t, int n) {
+  if (n > 0 && (n & (n - 1)) == 0) {
+    const int e = __ffs(n) - 1;
+    return t * __longlong_as_double(static_cast<long long>(1023 - e) << 52);
+  }
+  return t / static_cast<double>(n);
+}
 __device__ __forceinline__ int q8_off(int b, int L) { return b * QK + ((L + q8_rot(b)) & (QK - 1)); }
 
 // exp_cw: exp(x) = 2^k * e^r with k = nearest(x / ln 2) and r = x - k*ln 2
@@ -190,52 +201,82 @@ __device__ inline float block_rms_scale(const float* x, int K, float eps, double
     if (tid == 0) red[32] = t;
   }
   __syncthreads();
-  const float mean = static_cast<float>(red[32] / static_cast<double>(K));
+  const float mean = static_cast<float>(div_count(red[32], K));
   return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
 }
 
-// quantize_row_q8_K semantics for one 256-value block held 8 per lane
-// (v[k] = element lane*8 + k): the first element of largest magnitude maps to
-// -127 (iscale = -127/max, d = 1/iscale), round half to even, clamp at +127,
-// 16 partial sums.  Writes block b of the activation (rotated layout).
-__device__ __forceinline__ void quantize_block_warp(const float (&v)[8], int b, ActSmem& a, int lane) {
-  // Largest magnitude over the block, then the first element (lowest index:
+// quantize_row_q8_K semantics for NB 256-value blocks held 8 per lane
+// (v[i][k] = element lane*8 + k of block blk[i]): the first element of
+// largest magnitude maps to -127 (iscale = -127/max, d = 1/iscale), round
+// half to even, clamp at +127, 16 partial sums.  Writes the blocks with
+// live[i] (warp-uniform) into the activation (rotated layout).  The NB
+// blocks' steps are interleaved, so their shuffle and division latencies
+// overlap; each block's arithmetic is the single-block one.
+template <int NB>
+__device__ __forceinline__ void quantize_blocks_warp(const float (&v)[NB][8], const int (&blk)[NB],
+                                                     const bool (&live)[NB], ActSmem& a, int lane) {
+  // Largest magnitude over each block, then the first element (lowest index:
   // lowest lane, then lowest k) that has it; mx is that element's value.
-  float amax = 0.f;
+  float amax[NB], mx[NB];
 #pragma unroll
-  for (int k = 0; k < 8; ++k) amax = fmaxf(amax, fabsf(v[k]));
+  for (int i = 0; i < NB; ++i) {
+    amax[i] = 0.f;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  float cand = 0.f;
-  bool has = false;
+    for (int k = 0; k < 8; ++k) amax[i] = fmaxf(amax[i], fabsf(v[i][k]));
+  }
 #pragma unroll
-  for (int k = 7; k >= 0; --k) {
-    if (fabsf(v[k]) == amax) {
-      cand = v[k];
-      has = true;
+  for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+    for (int i = 0; i < NB; ++i) amax[i] = fmaxf(amax[i], __shfl_xor_sync(0xffffffffu, amax[i], o));
+  }
+#pragma unroll
+  for (int i = 0; i < NB; ++i) {
+    float cand = 0.f;
+    bool has = false;
+#pragma unroll
+    for (int k = 7; k >= 0; --k) {
+      if (fabsf(v[i][k]) == amax[i]) {
+        cand = v[i][k];
+        has = true;
+      }
+    }
+    const unsigned who = __ballot_sync(0xffffffffu, has);
+    mx[i] = __shfl_sync(0xffffffffu, cand, who != 0u ? __ffs(who) - 1 : 0);
+  }
+#pragma unroll
+  for (int i = 0; i < NB; ++i) {
+    uint32_t w0 = 0, w1 = 0;
+    int part = 0;
+    float dq = 0.f;
+    if (amax[i] != 0.f) {
+      const float iscale = __fdiv_rn(-127.f, mx[i]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int q = min(127, __float2int_rn(__fmul_rn(iscale, v[i][k])));
+        part += q;
+        const uint32_t byte = static_cast<uint32_t>(q & 0xFF);
+        if (k < 4) w0 |= byte << (8 * k);
+        else w1 |= byte << (8 * (k - 4));
+      }
+      dq = __fdiv_rn(1.f, iscale);
+    }
+    part += __shfl_xor_sync(0xffffffffu, part, 1);
+    if (live[i]) {
+      const int b = blk[i];
+      *reinterpret_cast<uint2*>(a.qs + q8_off(b, lane * 8)) = make_uint2(w0, w1);
+      if ((lane & 1) == 0) a.bsums[b * 16 + (lane >> 1)] = static_cast<int16_t>(part);
+      if (lane == 0) a.d[b] = dq;
     }
   }
-  const unsigned who = __ballot_sync(0xffffffffu, has);
-  const float mx = __shfl_sync(0xffffffffu, cand, who != 0u ? __ffs(who) - 1 : 0);
-  uint32_t w0 = 0, w1 = 0;
-  int part = 0;
-  float dq = 0.f;
-  if (amax != 0.f) {
-    const float iscale = __fdiv_rn(-127.f, mx);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int q = min(127, __float2int_rn(__fmul_rn(iscale, v[k])));
-      part += q;
-      const uint32_t byte = static_cast<uint32_t>(q & 0xFF);
-      if (k < 4) w0 |= byte << (8 * k);
-      else w1 |= byte << (8 * (k - 4));
-    }
-    dq = __fdiv_rn(1.f, iscale);
-  }
-  *reinterpret_cast<uint2*>(a.qs + q8_off(b, lane * 8)) = make_uint2(w0, w1);
-  part += __shfl_xor_sync(0xffffffffu, part, 1);
-  if ((lane & 1) == 0) a.bsums[b * 16 + (lane >> 1)] = static_cast<int16_t>(part);
-  if (lane == 0) a.d[b] = dq;
+}
+
+// One block (quantize_blocks_warp with NB = 1): block b, v[k] = element
+// lane*8 + k.
+__device__ __forceinline__ void quantize_block_warp(const float (&v)[8], int b, ActSmem& a, int lane) {
+  const float (&vv)[1][8] = *reinterpret_cast<const float (*)[1][8]>(&v);
+  const int blk[1] = {b};
+  const bool live[1] = {true};
+  quantize_blocks_warp<1>(vv, blk, live, a, lane);
 }
 
 // Stages the RMSNorm weight of an activation (static model data, so callers
@@ -271,7 +312,7 @@ __device__ inline void prep_act(ActSmem& a, const float* __restrict__ src, bool 
     __syncthreads();
     double t = 0.0;
     for (int w = 0; w < nw; ++w) t += red[w];
-    const float mean = static_cast<float>(t / static_cast<double>(K));
+    const float mean = static_cast<float>(div_count(t, K));
     scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
   }
   const bool w = do_norm && has_norm_w && a.wf != nullptr;

@@ -749,13 +749,6 @@ __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
   return v;
 }
 
-// Adds to a grid counter with release semantics: this CTA's earlier writes
-// (ordered before the calling thread by a CTA barrier) are visible to any
-// thread that acquires the new count.
-__device__ __forceinline__ void red_release_gpu(unsigned* p, unsigned v) {
-  asm volatile("red.release.gpu.global.add.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
-}
-
 __device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
   asm volatile("st.relaxed.gpu.global.b64 [%0], %1;\n" ::"l"(p), "l"(v) : "memory");
 }
@@ -792,6 +785,13 @@ __device__ __forceinline__ bool collect_logits(const unsigned long long* tagged,
   return false;
 }
 
+// Adds to a grid counter with release semantics: this CTA's earlier writes
+// (ordered before the calling thread by a CTA barrier) are visible to any
+// thread that acquires the new count.
+__device__ __forceinline__ void red_release_gpu(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+
 // Bounded wait (one thread) until *p >= target.
 __device__ __forceinline__ bool wait_count(const unsigned* p, unsigned target) {
   for (int i = 0; i < kGridSpins; ++i) {
@@ -808,25 +808,23 @@ __device__ __forceinline__ void quant_act_global(ActSmem& a, const float* src, i
   constexpr int kAhead = 4;  // blocks per warp whose loads are all in flight at once
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   for (int b0 = warp; b0 < n_blocks; b0 += kAhead * nw) {
-    float4 v4[kAhead][2];
+    float v[kAhead][8];
+    int blk[kAhead];
+    bool live[kAhead];
 #pragma unroll
     for (int i = 0; i < kAhead; ++i) {
-      const int b = b0 + i * nw;
-      if (b < n_blocks) {
-        const float4* s4 = reinterpret_cast<const float4*>(src + b * QK + lane * 8);
-        v4[i][0] = __ldcg(s4);
-        v4[i][1] = __ldcg(s4 + 1);
+      blk[i] = b0 + i * nw;
+      live[i] = blk[i] < n_blocks;
+      float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
+      if (live[i]) {
+        const float4* s4 = reinterpret_cast<const float4*>(src + blk[i] * QK + lane * 8);
+        lo = __ldcg(s4);
+        hi = __ldcg(s4 + 1);
       }
+      v[i][0] = lo.x, v[i][1] = lo.y, v[i][2] = lo.z, v[i][3] = lo.w;
+      v[i][4] = hi.x, v[i][5] = hi.y, v[i][6] = hi.z, v[i][7] = hi.w;
     }
-#pragma unroll
-    for (int i = 0; i < kAhead; ++i) {
-      const int b = b0 + i * nw;
-      if (b < n_blocks) {
-        float v[8] = {v4[i][0].x, v4[i][0].y, v4[i][0].z, v4[i][0].w,
-                      v4[i][1].x, v4[i][1].y, v4[i][1].z, v4[i][1].w};
-        quantize_block_warp(v, b, a, lane);
-      }
-    }
+    quantize_blocks_warp<kAhead>(v, blk, live, a, lane);
   }
 }
 
@@ -929,11 +927,16 @@ __device__ __forceinline__ bool moe_run(const FusedArgs& p, uint8_t* smem, const
   // them), read ahead of the grid barrier.
   float h0 = 0.f;
   if (gw < d.jobs_total && lane < min(d.R, d.D - gw * d.R)) h0 = __ldcg(d.h + gw * d.R + lane);
-  // Grid barrier: every ff row written before any CTA quantises ff.
+  // Grid barrier: every ff row written before any CTA quantises ff.  Launches
+  // alternate between two arrival counters by the parity of their tag; CTA 0
+  // zeroed this launch's counter at the start of the previous launch.
   __syncthreads();
   if (threadIdx.x == 0) {
-    red_release_gpu(&p.sync[1], 1u);
-    sh.ok = wait_count(&p.sync[1], gridDim.x);
+    unsigned* arrived = &p.sync[1 + (sh.tag & 1u)];
+    red_release_gpu(arrived, 1u);
+    sh.ok = wait_count(arrived, gridDim.x);
+    // Every CTA read the epoch before arriving: CTA 0 advances it.
+    if (blockIdx.x == 0) *p.epoch = sh.tag;
   }
   __syncthreads();
   bool ok_dn = ok && sel_ok && sh.ok != 0;
@@ -983,16 +986,12 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) moe_fused_kernel(const __gr
     sh.pos = p.d.state->pos;
     sh.np = p.d.state->n_prompt;
     sh.tag = *reinterpret_cast<volatile unsigned*>(p.epoch) + 1u;
+    // The other arrival counter was last used by the previous launch, which
+    // has completed; the next launch uses it.
+    if (blockIdx.x == 0) p.sync[1 + ((sh.tag + 1u) & 1u)] = 0u;
   }
   const bool ok = moe_run(p, smem, w, router_cta, router_e, sh, red);
   if (!ok && lane == 0) atomicCAS(&p.d.state->error, 0, NH_E_TIMEOUT);
-  __syncthreads();
-  if (threadIdx.x == 0 && atomicAdd(&p.sync[2], 1u) == gridDim.x - 1) {
-    p.sync[1] = 0u;
-    p.sync[2] = 0u;
-    *p.epoch = sh.tag;  // every CTA has read this launch's tag
-    __threadfence();
-  }
 }
 
 }  // namespace nh
