@@ -38,6 +38,7 @@ constexpr int kTcTok = 32;      // tokens per CTA = accumulator columns
 constexpr int kTcThreads = 256;
 constexpr int kTcQ8Stride = 304;  // Q8 activation block: qs[256], sums int16[16], d f32, pad
 constexpr int kTcKBlocks = 8;     // 32-value sub-blocks per super-block
+constexpr int kTcLdBatch = 4;     // accumulator loads per tensor-memory wait (divides kTcKBlocks)
 
 // Shared-memory layout (bytes from a 1024-aligned base).
 constexpr int kAOpBytes = kTcKBlocks * kTcRows * 32;   // one matrix, one super-block: 32 KB
@@ -51,8 +52,10 @@ constexpr int kOffARaw = kOffBOp + 2 * kBOpBytes;
 constexpr int kOffBMeta = kOffARaw + 2 * 2 * kARawBytes;
 constexpr int kOffBsp = kOffBMeta + 2 * kBMetaBytes;      // [kTcTok][8] int
 constexpr int kOffBar = kOffBsp + kTcTok * 8 * 4;
+constexpr int kTcRowTabTiles = 16;                        // token tiles whose rows are tabulated
+constexpr int kOffRowTab = kOffBar + 64;                  // [kTcRowTabTiles][kTcTok] activation rows
 static_assert(kTcThreads == kTcTok * 8, "one thread per (token, sub-block) sum");
-constexpr int kTcSmemBytes = kOffBar + 64 + 1024;      // + alignment slack
+constexpr int kTcSmemBytes = kOffRowTab + kTcRowTabTiles * kTcTok * 4 + 1024;  // + alignment slack
 
 struct TcArgs {
   const uint8_t* w;
@@ -107,15 +110,17 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(smem_u32(bar))
                : "memory");
 }
-__device__ __forceinline__ void tc_ld16(uint32_t taddr, int (&v)[16]) {
+// 16 consecutive accumulator columns of the warp's 32 lanes; the registers
+// hold them only after tc_wait_ld.
+__device__ __forceinline__ void tc_ld16_issue(uint32_t taddr, int (&v)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
       : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
         "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
       : "r"(taddr)
       : "memory");
-  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 }
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
 
 // Pairwise super-block tree, one value at a time (the row-dot kernels' order).
 struct Tree {
@@ -167,6 +172,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_q4k_tc_kernel(const TcA
   const int total = my_tiles * nsb;  // (tile, super-block) iterations
   constexpr uint32_t kCols = NMAT == 2 ? 512u : 256u;
 
+  auto tile_base = [&](int it) { return (static_cast<int>(blockIdx.y) + (it / nsb) * static_cast<int>(gridDim.y)) * kTcTok; };
+  // Activation row of token t of a tile (clamped to the last valid token past
+  // the end), from global memory.
+  auto act_index = [&](int tok_base, int t) {
+    const int tc = min(tok_base + t, t_cnt - 1);
+    return p.act_idx != nullptr ? p.act_idx[t_off + tc] : tc;
+  };
+  // The rows of this CTA's first kTcRowTabTiles tiles, read once here (the
+  // barrier after the tensor-memory allocation orders them), so the copies
+  // issued per super-block wait on no global load.
+  int32_t* row_tab = reinterpret_cast<int32_t*>(sm + kOffRowTab);
+  for (int i = tid; i < min(my_tiles, kTcRowTabTiles) * kTcTok; i += kTcThreads) {
+    const int k = i / kTcTok;
+    row_tab[i] = act_index((static_cast<int>(blockIdx.y) + k * static_cast<int>(gridDim.y)) * kTcTok, i % kTcTok);
+  }
   if (tid == 0) {
     mbar_init(bar, 1);
     fence_barrier_init();
@@ -182,11 +202,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_q4k_tc_kernel(const TcA
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  auto tile_base = [&](int it) { return (static_cast<int>(blockIdx.y) + (it / nsb) * static_cast<int>(gridDim.y)) * kTcTok; };
-  // Token rows of a tile (clamped to the last valid token past the end).
-  auto act_row = [&](int tok_base, int t) {
-    const int tc = min(tok_base + t, t_cnt - 1);
-    const int a = p.act_idx != nullptr ? p.act_idx[t_off + tc] : tc;
+  auto act_row = [&](int it, int t) {
+    const int k = it / nsb;
+    const int a = k < kTcRowTabTiles ? row_tab[k * kTcTok + t] : act_index(tile_base(it), t);
     return p.q8 + static_cast<int64_t>(a) * nsb * kTcQ8Stride;
   };
   const uint8_t* wmat[2] = {p.w + static_cast<uint64_t>(e) * p.mstride,
@@ -196,7 +214,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_q4k_tc_kernel(const TcA
   // nine 16-byte chunks), activation quants in MMA layout, activation sums
   // and scale.
   auto issue = [&](int it, int st) {
-    const int sb = it % nsb, tok_base = tile_base(it);
+    const int sb = it % nsb;
     if (tid < NMAT * kTcRows) {
       const int m = tid / kTcRows, r = tid % kTcRows;
       const int row = min(row0 + r, p.rows - 1);
@@ -209,7 +227,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_q4k_tc_kernel(const TcA
     const uint32_t bmeta = smem_u32(sm + kOffBMeta + st * kBMetaBytes);
     for (int i = tid; i < kTcTok * 19; i += kTcThreads) {
       const int t = i / 19, c = i - t * 19;
-      const uint8_t* src = act_row(tok_base, t) + sb * kTcQ8Stride + c * 16;
+      const uint8_t* src = act_row(it, t) + sb * kTcQ8Stride + c * 16;
       if (c < 16)
         cp_async16(bop + (c >> 1) * (kTcTok * 32) + core_off(t, c & 1), src);
       else
@@ -283,15 +301,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_q4k_tc_kernel(const TcA
       int sumi[16];
 #pragma unroll
       for (int t = 0; t < 16; ++t) sumi[t] = 0;
+      // kTcLdBatch sub-block accumulators per tensor-memory round trip; the
+      // integer sums still run over j in order.
 #pragma unroll
-      for (int j = 0; j < kTcKBlocks; ++j) {
-        int v[16];
-        tc_ld16(tmem + (static_cast<uint32_t>(q4 * 32) << 16) +
-                    static_cast<uint32_t>((m * kTcKBlocks + j) * kTcTok + th * 16),
-                v);
-        const int s = byte_of(j < 4 ? sca : scb, j & 3);
+      for (int j0 = 0; j0 < kTcKBlocks; j0 += kTcLdBatch) {
+        int v[kTcLdBatch][16];
 #pragma unroll
-        for (int t = 0; t < 16; ++t) sumi[t] += s * v[t];
+        for (int u = 0; u < kTcLdBatch; ++u)
+          tc_ld16_issue(tmem + (static_cast<uint32_t>(q4 * 32) << 16) +
+                            static_cast<uint32_t>((m * kTcKBlocks + j0 + u) * kTcTok + th * 16),
+                        v[u]);
+        tc_wait_ld();
+#pragma unroll
+        for (int u = 0; u < kTcLdBatch; ++u) {
+          const int j = j0 + u;
+          const int s = byte_of(j < 4 ? sca : scb, j & 3);
+#pragma unroll
+          for (int t = 0; t < 16; ++t) sumi[t] += s * v[u][t];
+        }
       }
       const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
       int mn[8];
