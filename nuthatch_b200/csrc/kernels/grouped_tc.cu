@@ -23,6 +23,9 @@
 // issues the 8 (or 16) MMAs and commits them to an mbarrier; 8 warps read the
 // accumulators (warp w: lanes 32*(w%4).., tokens 16*(w/4)..) and form the
 // values.  All waits are bounded; an expired wait records NH_E_TIMEOUT.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <algorithm>
 #include <cstring>
 
@@ -58,6 +61,10 @@ static_assert(kTcThreads == kTcTok * 8, "one thread per (token, sub-block) sum")
 constexpr int kTcSmemBytes = kOffRowTab + kTcRowTabTiles * kTcTok * 4 + 1024;  // + alignment slack
 
 struct TcArgs {
+  // Tensor maps of the weights (2-D: row bytes x group rows, boxes of one
+  // Q4_K block x kTcRows rows), used when use_tma; else cp.async per row.
+  CUtensorMap tmap[2];
+  int use_tma;
   const uint8_t* w;
   const uint8_t* w2;
   uint64_t mstride, mstride2, rb;
@@ -122,6 +129,16 @@ __device__ __forceinline__ void tc_ld16_issue(uint32_t taddr, int (&v)[16]) {
 }
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
 
+// One box of a 2-D tensor map into shared memory, completing on `bar`
+// (no multicast).  x is in bytes of the row (a multiple of 16), y the row.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];\n" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Pairwise super-block tree, one value at a time (the row-dot kernels' order).
 struct Tree {
   float p, q, o, r;
@@ -148,11 +165,12 @@ struct Tree {
 };
 
 template <int NMAT>
-__global__ void __launch_bounds__(kTcThreads, 1) grouped_q4k_tc_kernel(const TcArgs p) {
+__global__ void __launch_bounds__(kTcThreads, 1) grouped_q4k_tc_kernel(const __grid_constant__ TcArgs p) {
   extern __shared__ uint8_t tc_smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kOffBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + kOffBar + 16);
+  uint64_t* sbar = reinterpret_cast<uint64_t*>(sm + kOffBar + 32);  // [2] weight stages (tensor-map loads)
   int32_t* bsp = reinterpret_cast<int32_t*>(sm + kOffBsp);  // [kTcTok][8] sub-block sums of the activation
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int e = blockIdx.x / p.row_tiles, rt = blockIdx.x % p.row_tiles;
@@ -189,6 +207,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_q4k_tc_kernel(const TcA
   }
   if (tid == 0) {
     mbar_init(bar, 1);
+    mbar_init(&sbar[0], 1);
+    mbar_init(&sbar[1], 1);
     fence_barrier_init();
   }
   if (warp == 0) {
@@ -215,7 +235,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_q4k_tc_kernel(const TcA
   // and scale.
   auto issue = [&](int it, int st) {
     const int sb = it % nsb;
-    if (tid < NMAT * kTcRows) {
+    if (p.use_tma) {
+      if (tid == 0) {
+        // The stage's previous contents were read through the generic proxy
+        // (ordered before this thread by the CTA barrier): order them before
+        // the tensor-map writes.
+        fence_async_smem();
+        mbar_expect_tx(&sbar[st], static_cast<uint32_t>(NMAT * kARawBytes));
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m)
+          tma_load_2d(smem_u32(sm + kOffARaw + st * 2 * kARawBytes + m * kARawBytes), &p.tmap[m], sb * kARawRow,
+                      e * p.rows + row0, &sbar[st]);
+      }
+    } else if (tid < NMAT * kTcRows) {
       const int m = tid / kTcRows, r = tid % kTcRows;
       const int row = min(row0 + r, p.rows - 1);
       const uint32_t dst = smem_u32(sm + kOffARaw + st * 2 * kARawBytes + (m * kTcRows + r) * kARawRow);
@@ -244,7 +276,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_q4k_tc_kernel(const TcA
   for (int it = 0; it < total; ++it) {
     const int st = it & 1, sb = it % nsb, tok_base = tile_base(it);
     cp_async_wait_all();
-    __syncthreads();
+    if (p.use_tma && !mbar_wait(&sbar[st], static_cast<uint32_t>((it >> 1) & 1))) ok = false;
+    // CTA-uniform: a wait that expired in any thread ends the loop for all.
+    if (__syncthreads_or(!ok)) break;
     if (it + 1 < total) issue(it + 1, st ^ 1);
     // Widen this stage's 4-bit weight quants into the MMA layout, and form
     // each token's eight 32-value sums of its activation quants.
@@ -286,10 +320,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_q4k_tc_kernel(const TcA
                  smem_desc(aop0 + m * kAOpBytes + j * (kTcRows * 32)), smem_desc(bop0 + j * (kTcTok * 32)));
       tc_commit(bar);
     }
-    if (!mbar_wait(bar, static_cast<uint32_t>(it & 1))) {
-      ok = false;
-      break;
-    }
+    if (!mbar_wait(bar, static_cast<uint32_t>(it & 1))) ok = false;
+    if (__syncthreads_or(!ok)) break;
     tc_fence_after();
     // Epilogue of super-block sb.
 #pragma unroll
@@ -363,16 +395,63 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_q4k_tc_kernel(const TcA
   cp_async_wait_all();
   if (!ok) {
     if (lane == 0 && p.err != nullptr) atomicCAS(p.err, 0, NH_E_TIMEOUT);
-    // Give the in-flight MMAs a last bounded chance to finish before the
-    // tensor memory is released.
+    // Give the in-flight MMAs and tensor-map loads a last bounded chance to
+    // finish before the tensor memory and the CTA's shared memory are released.
     (void)mbar_wait(bar, 0u);
     (void)mbar_wait(bar, 1u);
+    if (p.use_tma) {
+      for (int s2 = 0; s2 < 2; ++s2) {
+        (void)mbar_wait(&sbar[s2], 0u);
+        (void)mbar_wait(&sbar[s2], 1u);
+      }
+    }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (warp == 0)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kCols) : "memory");
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (the
+// library does not link the driver API); null when unavailable.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// A 2-D tensor map over n_rows rows of rb bytes (Q4_K rows) read in boxes of
+// one 144-byte block x kTcRows rows; rows past the end read as zero.
+bool encode_q4k_rows(CUtensorMap* m, const void* base, uint64_t rb, uint64_t n_rows) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (enc == nullptr || n_rows == 0 || n_rows > 0x7fffffffull || rb % 16 != 0 ||
+      (reinterpret_cast<uintptr_t>(base) & 15) != 0)
+    return false;
+  const cuuint64_t dims[2] = {rb, n_rows};
+  const cuuint64_t strides[1] = {rb};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kARawRow), static_cast<cuuint32_t>(kTcRows)};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Tensor-map weight loads are on unless NH_TC_TMA=0 (read once).
+bool tc_tma_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* s = std::getenv("NH_TC_TMA");
+    v = (s != nullptr && s[0] == '0') ? 0 : 1;
+  }
+  return v != 0;
 }
 
 // Whether the tensor-core form is enabled (NH_TC=0 turns it off; read once).
@@ -425,6 +504,18 @@ extern "C" int nh_batch_rowdot_tc(const NhGroupedRowDot* g, void* stream) {
   p.out = g->out;
   p.out_stride = g->out_stride;
   p.err = g->err;
+  // The weight tiles come by tensor-map loads when every group's rows are
+  // contiguous (group g's rows start g * rows * rb after the first), else by
+  // per-row cp.async (e.g. slot pools with padded slots).
+  {
+    const uint64_t groups = static_cast<uint64_t>(g->n_groups);
+    const uint64_t span = static_cast<uint64_t>(p.rows) * rb;
+    const bool contiguous = groups == 1 || (g->mstride == span && (!swiglu || g->mstride2 == span));
+    p.use_tma = tc_tma_enabled() && contiguous && encode_q4k_rows(&p.tmap[0], g->w, rb, groups * p.rows) &&
+                (!swiglu || encode_q4k_rows(&p.tmap[1], g->w2, rb, groups * p.rows))
+                    ? 1
+                    : 0;
+  }
   // Grouped products: a CTA walks its group's token tiles y, y + grid.y, ...;
   // two CTAs per (group, row tile) cover the usual per-expert token counts
   // without launching mostly-empty tiles.  Dense products: one tile each.
