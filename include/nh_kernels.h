@@ -68,6 +68,15 @@ int nh_device_sm_count(int device);
 int64_t nh_attention_scratch_bytes(int n_head, int head_dim, int max_seq);
 int64_t nh_argmax_scratch_bytes(int n_vocab);
 
+/* The k selected expert ids of a router step handed to the host without a
+ * stream synchronisation (no reference counterpart: the two-phase streaming
+ * form's selection read-back, streaming_forward.cc:228-236): copies sel[0..k)
+ * to host_sel and then writes seq to *host_seq, both in mapped pinned host
+ * memory (device addresses from cudaHostGetDevicePointer), with a
+ * system-scope fence between; the host waits until *host_seq == seq.  k <= 32. */
+int nh_publish_selection(const int32_t* sel, int k, int32_t* host_sel, uint32_t* host_seq, uint32_t seq,
+                         void* stream);
+
 /* Embedding row lookup for the token at state->pos (ggml_get_rows on
  * token_embd, forward.cc:53-54, streaming_forward.cc:58-66): dequantises one
  * row of `table` ([n_vocab] rows of n_embd) into h_out. */

@@ -101,6 +101,7 @@ SIGNATURES = {
     "nh_argmax_scratch_bytes": (i64, [C.c_int]),
     "nh_router_scratch_bytes": (i64, [C.c_int]),
     "nh_rope_table": (None, [f32, C.c_int, C.c_int, P(f32)]),
+    "nh_publish_selection": (C.c_int, [vp, C.c_int, vp, vp, u32, vp]),
     "nh_embed_step": (C.c_int, [vp, vp, vp, i32, i64, i64, vp, vp]),
     "nh_qkv_proj": (C.c_int, [vp, vp, vp, f32, vp, i32, vp, i32, vp, i32, i64, i64, vp, vp, vp, vp]),
     "nh_attention_step": (C.c_int, [vp, vp, vp, vp, vp, vp, f32, C.c_int, C.c_int, C.c_int, vp, f32, vp, vp,

@@ -1,6 +1,9 @@
 // Device workspace and per-token kernel sequence.
 #include "engine.h"
 
+#include <algorithm>
+#include <atomic>
+#include <chrono>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -43,6 +46,18 @@ void DevFree(T*& p) {
   if (p != nullptr) cudaFree(p);
   p = nullptr;
 }
+// Pinned host memory the device can address (for flags and small hand-overs).
+template <typename T>
+int MappedAlloc(T** host, T** dev, size_t count) {
+  *host = nullptr;
+  *dev = nullptr;
+  if (cudaHostAlloc(reinterpret_cast<void**>(host), std::max<size_t>(count, 1) * sizeof(T), cudaHostAllocMapped) !=
+      cudaSuccess)
+    return NH_E_NOMEM;
+  std::memset(*host, 0, std::max<size_t>(count, 1) * sizeof(T));
+  return cudaHostGetDevicePointer(reinterpret_cast<void**>(dev), *host, 0) == cudaSuccess ? NH_OK : NH_E_CUDA;
+}
+
 template <typename T>
 void HostFree(T*& p) {
   if (p != nullptr) cudaFreeHost(p);
@@ -160,6 +175,10 @@ void Engine::FreeAll() {
   DevFree(wsel_);
   HostFree(sel_host_);
   HostFree(wsel_host_);
+  HostFree(pub_sel_);
+  HostFree(pub_seq_);
+  pub_sel_dev_ = nullptr;
+  pub_seq_dev_ = nullptr;
   DevFree(wts_);
   DevFree(ff_);
   DevFree(rope_cs_);
@@ -208,6 +227,9 @@ int Engine::Reserve(int max_seq, int max_prompt, int max_predict, bool dumps) {
   NH_TRY(DevAlloc(&wsel_, K));
   NH_TRY(HostAlloc(&sel_host_, K));
   NH_TRY(HostAlloc(&wsel_host_, K));
+  NH_TRY(MappedAlloc(&pub_sel_, &pub_sel_dev_, K));
+  NH_TRY(MappedAlloc(&pub_seq_, &pub_seq_dev_, 1));
+  *pub_seq_ = pub_count_;
   NH_TRY(DevAlloc(&wts_, K));
   NH_TRY(DevAlloc(&ff_, K * c.n_ff));
   std::vector<float> cs(static_cast<size_t>(max_seq) * hd);
@@ -320,6 +342,25 @@ int Engine::EnqueueAttnPhase(const ModelView& m, int l, bool norm_topk, bool tra
   return nh_router_topk(state_, h_, L.ffn_norm, c.rms_eps, L.router, c.n_embd, c.n_expert, c.n_expert_used,
                         norm_topk ? 1 : 0, sel_, wts_, trace ? trace_sel_ : nullptr, trace ? trace_gap_ : nullptr, l,
                         c.n_layers, router_scratch_, stream_);
+}
+
+int Engine::AwaitSelection(double timeout_s) {
+  const int K = static_cast<int>(cfg_.n_expert_used);
+  const uint32_t seq = ++pub_count_;
+  NH_TRY(nh_publish_selection(sel_, K, pub_sel_dev_, pub_seq_dev_, seq, stream_));
+  const volatile uint32_t* flag = pub_seq_;
+  const auto t0 = std::chrono::steady_clock::now();
+  for (uint64_t spins = 0; *flag != seq; ++spins) {
+    if ((spins & 4095) == 4095 &&
+        std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > timeout_s) {
+      // A failed launch never publishes: report the stream's error if any.
+      return cudaStreamSynchronize(stream_) != cudaSuccess ? NH_E_CUDA : NH_E_TIMEOUT;
+    }
+  }
+  std::atomic_thread_fence(std::memory_order_acquire);
+  const volatile int32_t* ids = pub_sel_;
+  for (int i = 0; i < K; ++i) sel_host_[i] = ids[i];
+  return NH_OK;
 }
 
 int Engine::EnqueueMoePhase(const ModelView& m, int l, const void* gate, int32_t tg, uint64_t gnb2, const void* up,

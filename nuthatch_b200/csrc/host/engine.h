@@ -93,6 +93,11 @@ class Engine {
   int EnqueueAttention(const ModelView& m, int layer);
   // EnqueueAttention plus the router (phase A of the two-phase form).
   int EnqueueAttnPhase(const ModelView& m, int layer, bool norm_topk, bool trace);
+  // After a phase A: enqueues the hand-over of the router's selection to
+  // mapped host memory, then waits on the host (spinning, at most timeout_s)
+  // until it has arrived and copies it to sel_host().  No stream
+  // synchronisation: work enqueued before the call keeps running.
+  int AwaitSelection(double timeout_s);
   // The whole MoE block of a resident layer in one cooperative kernel;
   // NH_E_ARG / NH_E_TYPE (nothing enqueued) where that kernel does not cover
   // the shapes.
@@ -159,6 +164,13 @@ class Engine {
   int32_t* wsel_ = nullptr;
   int32_t* sel_host_ = nullptr;
   int32_t* wsel_host_ = nullptr;
+  // Mapped pinned host memory the selection is published into: ids, then a
+  // sequence number (host and device addresses), and the last number used.
+  int32_t* pub_sel_ = nullptr;
+  uint32_t* pub_seq_ = nullptr;
+  int32_t* pub_sel_dev_ = nullptr;
+  uint32_t* pub_seq_dev_ = nullptr;
+  uint32_t pub_count_ = 0;
   float* wts_ = nullptr;
   float* ff_ = nullptr;
   float* rope_cs_ = nullptr;

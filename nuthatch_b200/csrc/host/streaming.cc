@@ -285,6 +285,10 @@ int ExpertSlotCache::Commit(void* stream) {
   return NH_OK;
 }
 
+// Longest host wait for one layer's selection before the step is abandoned
+// (a healthy phase A takes tens of microseconds).
+constexpr double kSelectionTimeoutS = 30.0;
+
 // ------------------------------------------------------------------ driver
 std::vector<int32_t> StreamingGenerateEx(const StreamingModel& model, const std::vector<int32_t>& ids, int n_predict,
                                          bool norm_topk, int capacity, const StreamingOptions& opt) {
@@ -357,14 +361,11 @@ std::vector<int32_t> StreamingGenerateEx(const StreamingModel& model, const std:
   for (int t = 0; t < steps && rc == NH_OK; ++t) {
     rc = e.EnqueueEmbed(ws->view);
     for (int l = 0; l < L && rc == NH_OK; ++l) {
-      // Phase A: attention + residual + router; read the selected ids back.
+      // Phase A: attention + residual + router; the selected ids come back
+      // through mapped host memory (no stream synchronisation).
       rc = e.EnqueueAttnPhase(ws->view, l, norm_topk, false);
+      if (rc == NH_OK) rc = e.AwaitSelection(kSelectionTimeoutS);
       if (rc != NH_OK) break;
-      if (cudaMemcpyAsync(e.sel_host(), e.sel_dev(), K * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
-          cudaStreamSynchronize(s) != cudaSuccess) {
-        rc = NH_E_CUDA;
-        break;
-      }
       const auto t0 = std::chrono::steady_clock::now();
       std::vector<int> sel(e.sel_host(), e.sel_host() + K);
       if (opt.trace != nullptr) {

@@ -33,6 +33,18 @@ __device__ __forceinline__ float dequant_elem(const uint8_t* row, int type, int6
   return __fmul_rn(__fmul_rn(d, static_cast<float>(sc)), static_cast<float>(q));
 }
 
+// One warp: the k selected ids to mapped host memory, then (after a
+// system-scope fence) the sequence number the host waits for.
+__global__ void publish_kernel(const int32_t* sel, int k, int32_t* host_sel, unsigned* host_seq, unsigned seq) {
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+  const int lane = threadIdx.x;
+  if (lane < k) host_sel[lane] = sel[lane];
+  __threadfence_system();
+  __syncwarp();
+  if (lane == 0) *reinterpret_cast<volatile unsigned*>(host_seq) = seq;
+}
+
 __global__ void embed_kernel(const NhDecodeState* state, const int32_t* prompt, const uint8_t* table,
                              int type, int64_t n_embd, int64_t n_vocab, uint64_t rb, float* h) {
   __shared__ int s_tok;
@@ -103,6 +115,13 @@ extern "C" int nh_exp_cw(const float* x, int64_t n, float* y, void* stream) {
   const int grid = static_cast<int>(std::min<int64_t>(1024, (n + 255) / 256));
   exp_cw_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, n, y);
   return cudaGetLastError() == cudaSuccess ? NH_OK : NH_E_CUDA;
+}
+
+extern "C" int nh_publish_selection(const int32_t* sel, int k, int32_t* host_sel, uint32_t* host_seq, uint32_t seq,
+                                    void* stream) {
+  if (sel == nullptr || host_sel == nullptr || host_seq == nullptr || k <= 0 || k > 32) return NH_E_ARG;
+  return launch_pdl(publish_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), sel, k, host_sel,
+                    static_cast<unsigned*>(host_seq), static_cast<unsigned>(seq));
 }
 
 extern "C" int nh_embed_step(const NhDecodeState* state, const int32_t* prompt_ids, const void* table,
