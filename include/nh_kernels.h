@@ -187,6 +187,19 @@ int nh_moe_down_combine(const NhDecodeState* state, const float* ff, const int32
                         float* dump, int64_t dump_step_stride, int64_t dump_offset,
                         void* stream);
 
+/* nh_moe_gate_up_prefetch and nh_moe_down_combine with the k selected slots
+ * given in HOST memory (slots[0..k), read during the call and passed with the
+ * launch), for the streaming form whose host decides the slots: no copy of
+ * the selection has to reach the device before the kernels run. */
+int nh_moe_gate_up_slots(NhDecodeState* state, const float* h, const float* ffn_norm, float eps,
+                         const int32_t* slots, int k, const void* gate, int32_t tg, uint64_t gate_nb2,
+                         const void* up, int32_t tu, uint64_t up_nb2, int64_t n_embd, int64_t n_ff,
+                         float* ff, const void* down, uint64_t down_nb2, void* stream);
+int nh_moe_down_combine_slots(const NhDecodeState* state, const float* ff, const int32_t* slots,
+                              const float* wts, int k, const void* down, int32_t td, uint64_t down_nb2,
+                              int64_t n_ff, int64_t n_embd, float* h_io, float* dump,
+                              int64_t dump_step_stride, int64_t dump_offset, void* stream);
+
 /* The whole MoE block of one layer (moe.cc:16-60, forward.cc:69-78) as one
  * cooperative kernel: nh_router_topk, nh_moe_gate_up and nh_moe_down_combine
  * in sequence, the same results bit for bit, with the stages separated by

@@ -115,6 +115,10 @@ SIGNATURES = {
     "nh_moe_gate_up_prefetch": (C.c_int, [vp, vp, vp, f32, vp, C.c_int, vp, i32, u64, vp, i32, u64, i64, i64, vp,
                                           vp, u64, vp]),
     "nh_moe_down_combine": (C.c_int, [vp, vp, vp, vp, C.c_int, vp, i32, u64, i64, i64, vp, vp, i64, i64, vp]),
+    "nh_moe_gate_up_slots": (C.c_int, [vp, vp, vp, f32, vp, C.c_int, vp, i32, u64, vp, i32, u64, i64, i64, vp,
+                                       vp, u64, vp]),
+    "nh_moe_down_combine_slots": (C.c_int, [vp, vp, vp, vp, C.c_int, vp, i32, u64, i64, i64, vp, vp, i64, i64,
+                                            vp]),
     "nh_moe_layer": (C.c_int, [P(NhMoeLayer), vp]),
     "nh_moe_layer_scratch_bytes": (i64, [C.c_int]),
     "nh_lm_head_argmax": (C.c_int, [vp, vp, vp, f32, vp, i32, i64, i64, vp, vp, vp, vp]),

@@ -365,15 +365,23 @@ int Engine::AwaitSelection(double timeout_s) {
 
 int Engine::EnqueueMoePhase(const ModelView& m, int l, const void* gate, int32_t tg, uint64_t gnb2, const void* up,
                             int32_t tu, uint64_t unb2, const void* down, int32_t td, uint64_t dnb2,
-                            const int32_t* wsel, bool dumps) {
+                            const int32_t* wsel, bool dumps, const int32_t* slots_host) {
   const OlmoeConfig& c = cfg_;
   const LayerView& L = m.layers[l];
+  const int64_t d = c.n_embd;
+  float* dump = dumps ? dump_hidden_ : nullptr;
+  const int64_t dstride = static_cast<int64_t>(c.n_layers) * d;
   // gate/up also starts this layer's selected down slices towards L2.
+  if (slots_host != nullptr) {
+    NH_TRY(nh_moe_gate_up_slots(state_, h_, L.ffn_norm, c.rms_eps, slots_host, c.n_expert_used, gate, tg, gnb2, up,
+                                tu, unb2, c.n_embd, c.n_ff, ff_, down, dnb2, stream_));
+    return nh_moe_down_combine_slots(state_, ff_, slots_host, wts_, c.n_expert_used, down, td, dnb2, c.n_ff, d, h_,
+                                     dump, dstride, l * d, stream_);
+  }
   NH_TRY(nh_moe_gate_up_prefetch(state_, h_, L.ffn_norm, c.rms_eps, wsel, c.n_expert_used, gate, tg, gnb2, up, tu,
                                  unb2, c.n_embd, c.n_ff, ff_, down, dnb2, stream_));
-  const int64_t d = c.n_embd;
-  return nh_moe_down_combine(state_, ff_, wsel, wts_, c.n_expert_used, down, td, dnb2, c.n_ff, d, h_,
-                             dumps ? dump_hidden_ : nullptr, static_cast<int64_t>(c.n_layers) * d, l * d, stream_);
+  return nh_moe_down_combine(state_, ff_, wsel, wts_, c.n_expert_used, down, td, dnb2, c.n_ff, d, h_, dump, dstride,
+                             l * d, stream_);
 }
 
 int Engine::EnqueueFinal(const ModelView& m, bool dumps) {

@@ -102,10 +102,11 @@ class Engine {
   // NH_E_ARG / NH_E_TYPE (nothing enqueued) where that kernel does not cover
   // the shapes.
   int EnqueueFusedMoe(const ModelView& m, int layer, bool norm_topk, bool trace, bool dumps);
-  // Phase B over expert weights at gate/up/down with per-slot selection wsel.
+  // Phase B over expert weights at gate/up/down with per-slot selection
+  // wsel (device memory) or, when slots_host is not null, the host's slots.
   int EnqueueMoePhase(const ModelView& m, int layer, const void* gate, int32_t tg, uint64_t gnb2,
                       const void* up, int32_t tu, uint64_t unb2, const void* down, int32_t td,
-                      uint64_t dnb2, const int32_t* wsel, bool dumps);
+                      uint64_t dnb2, const int32_t* wsel, bool dumps, const int32_t* slots_host = nullptr);
   int EnqueueFinal(const ModelView& m, bool dumps);
   int EnqueueStep(const ModelView& m, bool norm_topk, bool trace, bool dumps);
 

@@ -381,9 +381,9 @@ std::vector<int32_t> StreamingGenerateEx(const StreamingModel& model, const std:
         rc = NH_E_IO;
         break;
       }
+      // The slots travel with the phase B launches (no copy before them).
       for (int i = 0; i < K; ++i) e.wsel_host()[i] = slot[sel[i]];
-      if (cudaMemcpyAsync(e.wsel_dev(), e.wsel_host(), K * 4, cudaMemcpyHostToDevice, s) != cudaSuccess ||
-          cudaStreamWaitEvent(s, static_cast<cudaEvent_t>(caches[l]->fills_done_event()), 0) != cudaSuccess) {
+      if (cudaStreamWaitEvent(s, static_cast<cudaEvent_t>(caches[l]->fills_done_event()), 0) != cudaSuccess) {
         rc = NH_E_CUDA;
         break;
       }
@@ -393,7 +393,7 @@ std::vector<int32_t> StreamingGenerateEx(const StreamingModel& model, const std:
       rc = e.EnqueueMoePhase(ws->view, l, sc.gate_slots()->data, sc.gate_slots()->type, sc.gate_slots()->nb[2],
                              sc.up_slots()->data, sc.up_slots()->type, sc.up_slots()->nb[2],
                              sc.down_slots()->data, sc.down_slots()->type, sc.down_slots()->nb[2], e.wsel_dev(),
-                             false);
+                             false, e.wsel_host());
       if (rc == NH_OK) rc = caches[l]->Commit(s);
     }
     if (rc == NH_OK) rc = e.EnqueueFinal(ws->view, false);

@@ -220,12 +220,19 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(const RouterA
 }
 
 // ------------------------------------------------------------------ gate/up
+// The k selected experts (or slots): wsel in device memory, or, when wsel is
+// null, the copy in wsel_inline passed with the launch.
+__device__ __forceinline__ int sel_at(const int32_t* wsel, const int32_t (&inl)[kMaxTopK], int i) {
+  return wsel != nullptr ? wsel[i] : inl[i];
+}
+
 struct GateUpArgs {
   NhDecodeState* state;
   const float* h;
   const float* norm;
   float eps;
   const int32_t* wsel;
+  int32_t wsel_inline[kMaxTopK];
   int topk;
   const uint8_t* gate;
   const uint8_t* up;
@@ -276,7 +283,7 @@ __global__ void __launch_bounds__(kMoeWarps * 32) gate_up_kernel(const GateUpArg
     i = j / p.jobs_per_expert;
     r0 = (j % p.jobs_per_expert) * p.R;
     n = min(p.R, p.F - r0);
-    e = p.wsel[i];
+    e = sel_at(p.wsel, p.wsel_inline, i);
   };
   auto issue = [&](int j, int st) {
     if (!quant || lane != 0) return;
@@ -297,7 +304,7 @@ __global__ void __launch_bounds__(kMoeWarps * 32) gate_up_kernel(const GateUpArg
   }
   // Warm L2 with this layer's chosen down rows for the next kernel.
   if (p.down != nullptr && threadIdx.x < p.topk) {
-    const int e = p.wsel[threadIdx.x];
+    const int e = sel_at(p.wsel, p.wsel_inline, threadIdx.x);
     const uint64_t per = p.down_nb2 / gridDim.x;
     const uint64_t beg = (per * blockIdx.x) & ~static_cast<uint64_t>(15);
     const uint64_t end = blockIdx.x + 1 == gridDim.x ? p.down_nb2 : ((per * (blockIdx.x + 1)) & ~static_cast<uint64_t>(15));
@@ -352,6 +359,7 @@ struct DownArgs {
   NhDecodeState* state;
   const float* ff;
   const int32_t* wsel;
+  int32_t wsel_inline[kMaxTopK];
   const float* wts;
   int topk;
   const uint8_t* down;
@@ -402,7 +410,7 @@ __global__ void __launch_bounds__(kMoeWarps * 32) down_kernel(const DownArgs p) 
     const uint8_t* srcs[kMaxTopK];
     for (int i = 0; i < p.topk; ++i) {
       uint32_t off;
-      srcs[i] = span16(p.down + p.wsel[i] * p.nb2 + r0 * p.rb, n * p.rb, &lens[i], &off);
+      srcs[i] = span16(p.down + sel_at(p.wsel, p.wsel_inline, i) * p.nb2 + r0 * p.rb, n * p.rb, &lens[i], &off);
       total += lens[i];
     }
     mbar_expect_tx(&wbar[st], total);
@@ -472,7 +480,8 @@ __global__ void __launch_bounds__(kMoeWarps * 32) down_kernel(const DownArgs p) 
         const int q = q0 + kr;
         const int i = min(q / p.R, p.topk - 1), rr = q % p.R;
         const uint32_t off =
-            static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p.down + p.wsel[i] * p.nb2 + r0 * p.rb) & 15);
+            static_cast<uint32_t>(
+                reinterpret_cast<uintptr_t>(p.down + sel_at(p.wsel, p.wsel_inline, i) * p.nb2 + r0 * p.rb) & 15);
         ActReg<CPL> ar;
         load_act<CPL>(ar, a, i * nsb, jl, p.lpr);
         const float v = row_dot_reg<CPL>(buf + i * p.slot_bytes + off + rr * p.rb, p.td, jl, p.lpr, ar);
@@ -480,7 +489,7 @@ __global__ void __launch_bounds__(kMoeWarps * 32) down_kernel(const DownArgs p) 
       }
     } else {
       for (int i = 0; i < p.topk; ++i) {
-        const float* w = reinterpret_cast<const float*>(p.down + p.wsel[i] * p.nb2 + r0 * p.rb);
+        const float* w = reinterpret_cast<const float*>(p.down + sel_at(p.wsel, p.wsel_inline, i) * p.nb2 + r0 * p.rb);
         const float v = row_dot_f32(w, a.xf + i * p.F, p.F, lane);
         if (lane == 0) yw[i * p.R] = v;
       }
@@ -607,7 +616,7 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) gate_up3_kernel(const GateU
   pdl_wait();
   pdl_trigger();
   // The selection is read once; every job then finds its expert in shared memory.
-  if (threadIdx.x < p.topk) s_sel[threadIdx.x] = p.wsel[threadIdx.x];
+  if (threadIdx.x < p.topk) s_sel[threadIdx.x] = sel_at(p.wsel, p.wsel_inline, threadIdx.x);
   __syncthreads();
   for (int st = 0; st < p.S; ++st) {
     const int j = gw + st * tw;
@@ -702,7 +711,7 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) down3_kernel(const DownArgs
   pdl_wait();
   pdl_trigger();
   if (threadIdx.x < p.topk) {
-    s_sel[threadIdx.x] = p.wsel[threadIdx.x];
+    s_sel[threadIdx.x] = sel_at(p.wsel, p.wsel_inline, threadIdx.x);
     s_wts[threadIdx.x] = p.wts[threadIdx.x];
   }
   __syncthreads();
@@ -1151,11 +1160,15 @@ void shape_down3(DownArgs& p) {
 
 }  // namespace
 
-extern "C" int nh_moe_gate_up_prefetch(NhDecodeState* state, const float* h, const float* ffn_norm, float eps,
-                                       const int32_t* wsel, int k, const void* gate, int32_t tg, uint64_t gate_nb2,
-                                       const void* up, int32_t tu, uint64_t up_nb2, int64_t n_embd, int64_t n_ff,
-                                       float* ff, const void* down, uint64_t down_nb2, void* stream) {
-  if (h == nullptr || wsel == nullptr || gate == nullptr || up == nullptr || ff == nullptr) return NH_E_ARG;
+// The selection comes from device memory (wsel) or, when slots_host is not
+// null, from host memory, copied into the launch's arguments.
+static int gate_up_entry(NhDecodeState* state, const float* h, const float* ffn_norm, float eps, const int32_t* wsel,
+                         const int32_t* slots_host, int k, const void* gate, int32_t tg, uint64_t gate_nb2,
+                         const void* up, int32_t tu, uint64_t up_nb2, int64_t n_embd, int64_t n_ff, float* ff,
+                         const void* down, uint64_t down_nb2, void* stream) {
+  if (h == nullptr || (wsel == nullptr && slots_host == nullptr) || gate == nullptr || up == nullptr ||
+      ff == nullptr)
+    return NH_E_ARG;
   if (k <= 0 || k > kMaxTopK || n_embd <= 0 || n_embd > kMaxK || n_ff <= 0) return NH_E_ARG;
   const bool quant = tg != NH_TYPE_F32;
   if ((tg == NH_TYPE_F32) != (tu == NH_TYPE_F32)) return NH_E_TYPE;
@@ -1169,7 +1182,8 @@ extern "C" int nh_moe_gate_up_prefetch(NhDecodeState* state, const float* h, con
   p.h = h;
   p.norm = ffn_norm;
   p.eps = eps;
-  p.wsel = wsel;
+  p.wsel = slots_host != nullptr ? nullptr : wsel;
+  for (int i = 0; i < kMaxTopK; ++i) p.wsel_inline[i] = slots_host != nullptr && i < k ? slots_host[i] : 0;
   p.topk = k;
   p.gate = static_cast<const uint8_t*>(gate);
   p.up = static_cast<const uint8_t*>(up);
@@ -1224,6 +1238,24 @@ extern "C" int nh_moe_gate_up_prefetch(NhDecodeState* state, const float* h, con
   return cpl <= 1 ? launch_gate_up<1>(p, smem, grid, s) : launch_gate_up<2>(p, smem, grid, s);
 }
 
+extern "C" int nh_moe_gate_up_prefetch(NhDecodeState* state, const float* h, const float* ffn_norm, float eps,
+                                       const int32_t* wsel, int k, const void* gate, int32_t tg, uint64_t gate_nb2,
+                                       const void* up, int32_t tu, uint64_t up_nb2, int64_t n_embd, int64_t n_ff,
+                                       float* ff, const void* down, uint64_t down_nb2, void* stream) {
+  if (wsel == nullptr) return NH_E_ARG;
+  return gate_up_entry(state, h, ffn_norm, eps, wsel, nullptr, k, gate, tg, gate_nb2, up, tu, up_nb2, n_embd, n_ff,
+                       ff, down, down_nb2, stream);
+}
+
+extern "C" int nh_moe_gate_up_slots(NhDecodeState* state, const float* h, const float* ffn_norm, float eps,
+                                    const int32_t* slots, int k, const void* gate, int32_t tg, uint64_t gate_nb2,
+                                    const void* up, int32_t tu, uint64_t up_nb2, int64_t n_embd, int64_t n_ff,
+                                    float* ff, const void* down, uint64_t down_nb2, void* stream) {
+  if (slots == nullptr) return NH_E_ARG;
+  return gate_up_entry(state, h, ffn_norm, eps, nullptr, slots, k, gate, tg, gate_nb2, up, tu, up_nb2, n_embd, n_ff,
+                       ff, down, down_nb2, stream);
+}
+
 extern "C" int nh_moe_gate_up(NhDecodeState* state, const float* h, const float* ffn_norm, float eps,
                               const int32_t* wsel, int k, const void* gate, int32_t tg, uint64_t gate_nb2,
                               const void* up, int32_t tu, uint64_t up_nb2, int64_t n_embd, int64_t n_ff, float* ff,
@@ -1232,11 +1264,12 @@ extern "C" int nh_moe_gate_up(NhDecodeState* state, const float* h, const float*
                                  ff, nullptr, 0, stream);
 }
 
-extern "C" int nh_moe_down_combine(const NhDecodeState* state, const float* ff, const int32_t* wsel, const float* wts,
-                                   int k, const void* down, int32_t td, uint64_t down_nb2, int64_t n_ff,
-                                   int64_t n_embd, float* h_io, float* dump, int64_t dump_step_stride,
-                                   int64_t dump_offset, void* stream) {
-  if (state == nullptr || ff == nullptr || wsel == nullptr || wts == nullptr || down == nullptr || h_io == nullptr)
+static int down_entry(const NhDecodeState* state, const float* ff, const int32_t* wsel, const int32_t* slots_host,
+                      const float* wts, int k, const void* down, int32_t td, uint64_t down_nb2, int64_t n_ff,
+                      int64_t n_embd, float* h_io, float* dump, int64_t dump_step_stride, int64_t dump_offset,
+                      void* stream) {
+  if (state == nullptr || ff == nullptr || (wsel == nullptr && slots_host == nullptr) || wts == nullptr ||
+      down == nullptr || h_io == nullptr)
     return NH_E_ARG;
   if (k <= 0 || k > kMaxTopK || n_ff <= 0 || n_embd <= 0) return NH_E_ARG;
   if (td != NH_TYPE_F32 && td != NH_TYPE_Q4_K && td != NH_TYPE_Q6_K) return NH_E_TYPE;
@@ -1247,7 +1280,8 @@ extern "C" int nh_moe_down_combine(const NhDecodeState* state, const float* ff, 
   DownArgs p;
   p.state = const_cast<NhDecodeState*>(state);
   p.ff = ff;
-  p.wsel = wsel;
+  p.wsel = slots_host != nullptr ? nullptr : wsel;
+  for (int i = 0; i < kMaxTopK; ++i) p.wsel_inline[i] = slots_host != nullptr && i < k ? slots_host[i] : 0;
   p.wts = wts;
   p.topk = k;
   p.down = static_cast<const uint8_t*>(down);
@@ -1302,6 +1336,24 @@ extern "C" int nh_moe_down_combine(const NhDecodeState* state, const float* ff, 
   const int cpl = quant ? (p.F / 64 + 31) / 32 : 1;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return cpl <= 1 ? launch_down<1>(p, smem, grid, s) : launch_down<2>(p, smem, grid, s);
+}
+
+extern "C" int nh_moe_down_combine(const NhDecodeState* state, const float* ff, const int32_t* wsel, const float* wts,
+                                   int k, const void* down, int32_t td, uint64_t down_nb2, int64_t n_ff,
+                                   int64_t n_embd, float* h_io, float* dump, int64_t dump_step_stride,
+                                   int64_t dump_offset, void* stream) {
+  if (wsel == nullptr) return NH_E_ARG;
+  return down_entry(state, ff, wsel, nullptr, wts, k, down, td, down_nb2, n_ff, n_embd, h_io, dump, dump_step_stride,
+                    dump_offset, stream);
+}
+
+extern "C" int nh_moe_down_combine_slots(const NhDecodeState* state, const float* ff, const int32_t* slots,
+                                         const float* wts, int k, const void* down, int32_t td, uint64_t down_nb2,
+                                         int64_t n_ff, int64_t n_embd, float* h_io, float* dump,
+                                         int64_t dump_step_stride, int64_t dump_offset, void* stream) {
+  if (slots == nullptr) return NH_E_ARG;
+  return down_entry(state, ff, nullptr, slots, wts, k, down, td, down_nb2, n_ff, n_embd, h_io, dump,
+                    dump_step_stride, dump_offset, stream);
 }
 
 // 16 counters, then the E tagged logits (8 bytes each).
