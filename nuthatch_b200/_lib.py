@@ -6,10 +6,14 @@ library is an error: there is no fallback implementation.
 from __future__ import annotations
 
 import ctypes as C
+import os
 from pathlib import Path
 
 LIB_DIR = Path(__file__).resolve().parent / "lib"
 LIB_PATH = LIB_DIR / "libnuthatch_b200.so"
+# The phase-timestamp diagnostic build of the same library, loaded instead
+# when NH_PHASE_TRACE_LIB=1 at the first lib() call (nuthatch_b200.phase_trace).
+PHASE_TRACE_LIB_PATH = LIB_DIR / "libnuthatch_b200_phase_trace.so"
 
 i32, i64, u32, u64, f32 = C.c_int32, C.c_int64, C.c_uint32, C.c_uint64, C.c_float
 vp, cp = C.c_void_p, C.c_char_p
@@ -147,10 +151,11 @@ def lib() -> C.CDLL:
     """Loads the native library (raises if it has not been built)."""
     global _lib
     if _lib is None:
-        if not LIB_PATH.exists():
-            raise RuntimeError(f"{LIB_PATH} is missing: run `python -m nuthatch_b200.build` "
+        path = PHASE_TRACE_LIB_PATH if os.environ.get("NH_PHASE_TRACE_LIB") == "1" else LIB_PATH
+        if not path.exists():
+            raise RuntimeError(f"{path} is missing: run `python -m nuthatch_b200.build` "
                                "(there is no non-native implementation)")
-        handle = C.CDLL(str(LIB_PATH))
+        handle = C.CDLL(str(path))
         for name, (res, args) in SIGNATURES.items():
             fn = getattr(handle, name)
             fn.restype = res

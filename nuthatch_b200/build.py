@@ -1,11 +1,14 @@
 """In-tree build of the native libraries.
 
-    python -m nuthatch_b200.build          # product + synthetic-model writer
-    python -m nuthatch_b200.build --all    # also the checker (oracle/, oracle/_ref)
+    python -m nuthatch_b200.build                # product + synthetic-model writer
+    python -m nuthatch_b200.build --all          # also the checker (oracle/, oracle/_ref)
+    python -m nuthatch_b200.build --phase-trace  # also the phase-timestamp diagnostic library
 
 Outputs (git-ignored, shipped with the tree):
-    nuthatch_b200/lib/libnuthatch_b200.so  kernels (sm_100a) + host C++ + C ABI
-    nuthatch_b200/lib/libnh_synth.so       seeded synthetic GGUF writer
+    nuthatch_b200/lib/libnuthatch_b200.so              kernels (sm_100a) + host C++ + C ABI
+    nuthatch_b200/lib/libnh_synth.so                   seeded synthetic GGUF writer
+    nuthatch_b200/lib/libnuthatch_b200_phase_trace.so  the same with per-CTA phase timestamps
+                                                       (python -m nuthatch_b200.phase_trace)
 """
 from __future__ import annotations
 
@@ -50,25 +53,29 @@ def _headers() -> list[Path]:
     return sorted(list(INCLUDE.rglob("*.h")) + list(CSRC.rglob("*.h")) + list(CSRC.rglob("*.cuh")))
 
 
-def build_product(verbose: bool = False) -> Path:
-    """Compiles kernels/*.cu (nvcc, sm_100a) and host/*.cc, links the shared library."""
+def build_product(verbose: bool = False, phase_trace: bool = False) -> Path:
+    """Compiles kernels/*.cu (nvcc, sm_100a) and host/*.cc, links the shared library
+    (with phase_trace: the diagnostic variant, NH_PHASE_TRACE defined)."""
+    name = "libnuthatch_b200_phase_trace" if phase_trace else "libnuthatch_b200"
+    obj = OBJ / "phase_trace" if phase_trace else OBJ
     LIB.mkdir(parents=True, exist_ok=True)
-    OBJ.mkdir(parents=True, exist_ok=True)
-    out = LIB / "libnuthatch_b200.so"
+    obj.mkdir(parents=True, exist_ok=True)
+    out = LIB / f"{name}.so"
+    nvcc_flags = NVCC_FLAGS + (["-DNH_PHASE_TRACE"] if phase_trace else [])
     cu = sorted((CSRC / "kernels").glob("*.cu"))
     cc = sorted((CSRC / "host").glob("*.cc"))
-    stamp = LIB / "libnuthatch_b200.stamp"
-    digest = _digest(cu + cc + _headers(), " ".join(NVCC_FLAGS + CXX_FLAGS))
+    stamp = LIB / f"{name}.stamp"
+    digest = _digest(cu + cc + _headers(), " ".join(nvcc_flags + CXX_FLAGS))
     if out.exists() and stamp.exists() and stamp.read_text() == digest:
         return out
     jobs = []
     for src in cu:
-        jobs.append([NVCC, *NVCC_FLAGS, "-c", str(src), "-o", str(OBJ / (src.stem + ".cu.o"))])
+        jobs.append([NVCC, *nvcc_flags, "-c", str(src), "-o", str(obj / (src.stem + ".cu.o"))])
     for src in cc:
-        jobs.append(["g++", *CXX_FLAGS, "-c", str(src), "-o", str(OBJ / (src.stem + ".cc.o"))])
+        jobs.append(["g++", *CXX_FLAGS, "-c", str(src), "-o", str(obj / (src.stem + ".cc.o"))])
     with cf.ThreadPoolExecutor(max_workers=max(1, min(8, os.cpu_count() or 4))) as ex:
         list(ex.map(_run, jobs))
-    objs = [str(OBJ / (s.stem + ".cu.o")) for s in cu] + [str(OBJ / (s.stem + ".cc.o")) for s in cc]
+    objs = [str(obj / (s.stem + ".cu.o")) for s in cu] + [str(obj / (s.stem + ".cc.o")) for s in cc]
     _run([NVCC, *ARCH, "-shared", "-o", str(out), *objs, "-lcudart_static", "-lrt", "-ldl", "-lpthread"])
     stamp.write_text(digest)
     if verbose:
@@ -120,3 +127,5 @@ if __name__ == "__main__":
     else:
         build_synth(verbose=True)
         build_product(verbose=True)
+    if "--phase-trace" in sys.argv:
+        build_product(verbose=True, phase_trace=True)

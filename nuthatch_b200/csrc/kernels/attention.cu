@@ -27,14 +27,17 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
   const int pos = *reinterpret_cast<volatile const int*>(&p.state->pos);
   const int n_active = (pos + 1 + kAttnSplit - 1) / kAttnSplit;
   if (sp >= n_active) return;
+  const unsigned ph_idx = phase_begin();
   extern __shared__ __align__(128) float sm[];
   __shared__ AttnShared sh;
   const AttnSmem m = carve_attn(sm, p.hd, p.n_head);
   // Cached K/V rows and norm weights do not depend on the preceding kernel.
   attn_begin(p, h, sp, pos, m, sh);
   pdl_wait();
+  phase_stamp(1);
   pdl_trigger();
   attn_finish(p, h, sp, pos, m, sh);
+  phase_end_sync(kPhAttention, ph_idx);
 }
 
 
@@ -188,3 +191,5 @@ extern "C" int nh_attention_step_static(const NhDecodeState* state, const float*
   return nh_attention_step(state, q, k, v, q_norm, k_norm, eps, n_head, n_head_kv, head_dim, rope_cs, kq_scale,
                            k_cache, v_cache, max_seq, scratch, attn_out, stream);
 }
+
+NH_PHASE_TRACE_SETTER(attention)

@@ -208,6 +208,7 @@ __device__ inline void attn_finish(const AttnArgs& p, int h, int sp, int pos, co
     }
   }
   __syncthreads();
+  phase_stamp(2);
   // RMS of the full q (and k) rows, sums of squares in double: per thread,
   // per warp, then the warp partials in order.
   if (part) {
@@ -266,6 +267,7 @@ __device__ inline void attn_finish(const AttnArgs& p, int h, int sp, int pos, co
   const bool ok = mbar_wait(&sh.bar, 0);
   if (!ok && tid == 0) atomicCAS(&p.state->error, 0, NH_E_TIMEOUT);
   __syncthreads();
+  phase_stamp(3);
 
   // Scores kq = K.q * kq_scale.
   float my = -INFINITY;  // this thread's score (thread j: position p0 + j)
@@ -302,6 +304,7 @@ __device__ inline void attn_finish(const AttnArgs& p, int h, int sp, int pos, co
   for (int w = 0; w < nw; ++w) l += red[16 + w];
   if (tid < n) sc[tid] = n_active == 1 ? __fmul_rn(e, static_cast<float>(1.0 / l)) : e;
   __syncthreads();
+  phase_stamp(4);
 
   float* out = p.out + h * hd;
   if (n_active == 1) {

@@ -166,6 +166,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const GemvArgs p)
 // P = 32/G rows of one segment, all computed in one warp pass.
 __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv3_kernel(const GemvArgs p) {
   extern __shared__ __align__(128) uint8_t smem[];
+  const unsigned ph_idx = phase_begin();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   ActSmem a = carve_act(smem, p.K, true, p.need_wf != 0);
   const size_t act_bytes = (act_smem_bytes(p.K, true, p.need_wf != 0) + 15) & ~static_cast<size_t>(15);
@@ -217,6 +218,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv3_kernel(const GemvArg
     act_load_norm(a, p.norm_w);
   }
   pdl_wait();
+  phase_stamp(1);
   pdl_trigger();
 
   float best_v = -INFINITY;
@@ -224,6 +226,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv3_kernel(const GemvArg
   bool failed = false;
   if (!skip) {
     prep_act(a, p.x, p.norm_w != nullptr, p.do_norm != 0, p.eps, true, red);
+    phase_stamp(2);
     const int g = lane % G, r = lane / G;
     // Most warps dot one or two jobs: the activation is read from shared
     // memory rather than held in registers.
@@ -239,6 +242,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv3_kernel(const GemvArg
         failed = true;
         break;
       }
+      if (it == 0) phase_stamp(3);
       const uint32_t off =
           static_cast<uint32_t>(reinterpret_cast<uintptr_t>(sg.w + static_cast<uint64_t>(row0) * sg.rb) & 15);
       const uint8_t* rowp = wb + static_cast<size_t>(st) * p.stage_bytes + off + static_cast<size_t>(r) * sg.rb;
@@ -260,6 +264,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv3_kernel(const GemvArg
       if (jn < p.jobs_total) issue(jn, st);
     }
   }
+  phase_end_sync(p.argmax ? kPhLmHead : kPhQkvOrOut, ph_idx);
   if (failed && lane == 0 && p.state != nullptr) atomicCAS(&p.state->error, 0, NH_E_TIMEOUT);
   if (!p.argmax) return;
 
@@ -478,3 +483,5 @@ extern "C" int nh_gemv(NhDecodeState* state, const void* w, int32_t type, int64_
   p.do_norm = norm_w != nullptr ? 1 : 0;
   return gemv_launch(p, static_cast<cudaStream_t>(stream));
 }
+
+NH_PHASE_TRACE_SETTER(gemv)

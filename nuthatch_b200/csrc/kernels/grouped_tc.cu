@@ -185,6 +185,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_q4k_tc_kernel(const __g
                                  static_cast<int>(gridDim.y)
                            : 0;
   if (my_tiles == 0) return;  // nothing allocated yet
+  const unsigned ph_idx = phase_begin();
+  PhaseAcc ph;  // wait for the stage / widen / MMA / epilogue, per iteration
+  ph.start();
   const int row0 = rt * kTcRows;
   const int nsb = p.K / QK;
   const int total = my_tiles * nsb;  // (tile, super-block) iterations
@@ -279,6 +282,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_q4k_tc_kernel(const __g
     if (p.use_tma && !mbar_wait(&sbar[st], static_cast<uint32_t>((it >> 1) & 1))) ok = false;
     // CTA-uniform: a wait that expired in any thread ends the loop for all.
     if (__syncthreads_or(!ok)) break;
+    ph.mark(0);
     if (it + 1 < total) issue(it + 1, st ^ 1);
     // Widen this stage's 4-bit weight quants into the MMA layout, and form
     // each token's eight 32-value sums of its activation quants.
@@ -308,6 +312,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_q4k_tc_kernel(const __g
     }
     fence_async_smem();
     __syncthreads();
+    ph.mark(1);
     if (tid == 0) {
       tc_fence_after();
       const uint32_t aop0 = smem_u32(sm + kOffAOp);
@@ -323,6 +328,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_q4k_tc_kernel(const __g
     if (!mbar_wait(bar, static_cast<uint32_t>(it & 1))) ok = false;
     if (__syncthreads_or(!ok)) break;
     tc_fence_after();
+    ph.mark(2);
     // Epilogue of super-block sb.
 #pragma unroll
     for (int m = 0; m < NMAT; ++m) {
@@ -369,6 +375,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_q4k_tc_kernel(const __g
       }
     }
     tc_fence_before();
+    ph.mark(3);
     if (sb == nsb - 1) {
       // The tile is complete: its outputs.
       const int row = row0 + erow;
@@ -406,6 +413,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_q4k_tc_kernel(const __g
       }
     }
   }
+  ph.store();
+  phase_value(6, static_cast<unsigned long long>(total));
+  phase_value(7, static_cast<unsigned long long>(NMAT));
+  phase_end(kPhGroupedTc, ph_idx);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -534,3 +545,5 @@ extern "C" int nh_batch_rowdot_tc(const NhGroupedRowDot* g, void* stream) {
 }
 
 extern "C" int nh_tc_enabled(void) { return tc_enabled() ? 1 : 0; }
+
+NH_PHASE_TRACE_SETTER(grouped_tc)

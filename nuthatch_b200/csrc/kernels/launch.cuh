@@ -9,6 +9,7 @@
 #include <utility>
 
 #include "../../../include/nh_kernels.h"
+#include "phase_trace.cuh"
 
 namespace nh {
 

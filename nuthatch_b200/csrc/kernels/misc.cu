@@ -47,6 +47,7 @@ __global__ void publish_kernel(const int32_t* sel, int k, int32_t* host_sel, uns
 
 __global__ void embed_kernel(const NhDecodeState* state, const int32_t* prompt, const uint8_t* table,
                              int type, int64_t n_embd, int64_t n_vocab, uint64_t rb, float* h) {
+  phase_end(kPhEmbed, phase_begin());
   __shared__ int s_tok;
   // The fed-back id comes from the preceding argmax.
   asm volatile("griddepcontrol.wait;\n" ::: "memory");
@@ -155,3 +156,5 @@ extern "C" int nh_quantize_q8k(const float* x, int64_t n, void* out, void* strea
       x, n, static_cast<uint8_t*>(out));
   return cudaGetLastError() == cudaSuccess ? NH_OK : NH_E_CUDA;
 }
+
+NH_PHASE_TRACE_SETTER(misc)

@@ -185,6 +185,7 @@ __device__ __forceinline__ void router_select_block(const RouterArgs& p, const f
 }
 
 __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(const RouterArgs p) {
+  const unsigned ph_idx = phase_begin();
   extern __shared__ __align__(128) uint8_t smem[];
   ActSmem a = carve_act(smem, p.K, true, true);
   __shared__ double red[48];
@@ -197,6 +198,7 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(const RouterA
   router_load_row(p, wv, e, lane);
   act_load_norm(a, p.norm);
   pdl_wait();
+  phase_stamp(1);
   pdl_trigger();
   prep_act(a, p.h, p.norm != nullptr, true, p.eps, false, red);
   if (e < p.E) {
@@ -213,6 +215,7 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(const RouterA
     }
   }
   __syncthreads();
+  phase_end(kPhRouter, ph_idx);
   if (!s_last) return;
   __shared__ int s_sel[kMaxTopK];
   __shared__ float s_wts[kMaxTopK];
@@ -572,6 +575,7 @@ __device__ __forceinline__ bool gu3_run(const GateUpArgs& p, const int* s_sel, u
     int i, e, r0, n;
     gu3_job(p, s_sel, j, i, e, r0, n);
     if (!mbar_wait(&wbar[st], (it / p.S) & 1)) return false;
+    if (it == 0) phase_stamp(10);
     const uint8_t* buf = wb + static_cast<size_t>(st) * p.stage_bytes;
     const uint32_t og = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p.gate + e * p.gate_nb2 + r0 * p.rb_g) & 15);
     const uint32_t ou = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p.up + e * p.up_nb2 + r0 * p.rb_u) & 15);
@@ -597,6 +601,7 @@ __device__ __forceinline__ bool gu3_run(const GateUpArgs& p, const int* s_sel, u
 }
 
 __global__ void __launch_bounds__(kMoeWarps * 32, 2) gate_up3_kernel(const GateUpArgs p) {
+  const unsigned ph_idx = phase_begin();
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   ActSmem a = carve_act(smem, p.K, true, true);
@@ -614,6 +619,7 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) gate_up3_kernel(const GateU
   }
   act_load_norm(a, p.norm);
   pdl_wait();
+  phase_stamp(1);
   pdl_trigger();
   // The selection is read once; every job then finds its expert in shared memory.
   if (threadIdx.x < p.topk) s_sel[threadIdx.x] = sel_at(p.wsel, p.wsel_inline, threadIdx.x);
@@ -626,6 +632,7 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) gate_up3_kernel(const GateU
   prep_act(a, p.h, p.norm != nullptr, true, p.eps, true, red);
   const bool ok = gu3_run(p, s_sel, wbar, wb, Act3Smem{a, lane % p.lpr}, gw, tw, lane);
   if (!ok && lane == 0 && p.state != nullptr) atomicCAS(&p.state->error, 0, NH_E_TIMEOUT);
+  phase_end(kPhGateUp, ph_idx);
 }
 
 // down + combine: G = F/256 lanes per row and P = 32/G row groups per pass;
@@ -670,6 +677,7 @@ __device__ __forceinline__ bool dn3_run(const DownArgs& p, const int* s_sel, con
     const int r0 = j * Rp;
     const int n = min(Rp, p.D - r0);
     if (!mbar_wait(&wbar[st], (it / p.S) & 1)) return false;
+    if (it == 0) phase_stamp(8);
     const uint8_t* buf = wb + static_cast<size_t>(st) * p.stage_bytes;
     const uint32_t off =
         static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p.down + s_sel[ie] * p.nb2 + r0 * p.rb) & 15);
@@ -691,6 +699,7 @@ __device__ __forceinline__ bool dn3_run(const DownArgs& p, const int* s_sel, con
 }
 
 __global__ void __launch_bounds__(kMoeWarps * 32, 2) down3_kernel(const DownArgs p) {
+  const unsigned ph_idx = phase_begin();
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int KF = p.topk * p.F;
@@ -709,6 +718,7 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) down3_kernel(const DownArgs
     fence_barrier_init();
   }
   pdl_wait();
+  phase_stamp(1);
   pdl_trigger();
   if (threadIdx.x < p.topk) {
     s_sel[threadIdx.x] = sel_at(p.wsel, p.wsel_inline, threadIdx.x);
@@ -723,6 +733,7 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) down3_kernel(const DownArgs
   prep_act(a, p.ff, false, false, 0.f, true, red);
   const bool ok = dn3_run(p, s_sel, s_wts, wbar, wb, a, gw, tw, lane, p.state->pos, p.state->n_prompt, false, 0.f);
   if (!ok && lane == 0) atomicCAS(&p.state->error, 0, NH_E_TIMEOUT);
+  phase_end(kPhDown, ph_idx);
 }
 
 // ------------------------------------------------------------------ fused layer
@@ -887,6 +898,7 @@ __device__ __forceinline__ bool moe_run(const FusedArgs& p, uint8_t* smem, const
   // The normalised f32 row first: the router reads it; its Q8_K form (for
   // gate/up only) is made while the logits travel between CTAs.
   prep_act<true>(a, g.h, g.norm != nullptr, true, g.eps, false, red);
+  phase_stamp(2);
   bool ok = true;
   if (router_cta) {
     if (router_e >= 0) {
@@ -917,6 +929,7 @@ __device__ __forceinline__ bool moe_run(const FusedArgs& p, uint8_t* smem, const
     if (lane == 0) sh.ok = got;
   }
   __syncthreads();
+  phase_stamp(3);
   const bool sel_ok = sh.ok != 0;
   if (sel_ok) {
     router_select_core(p.r, pr, blockIdx.x == 0, sh.pos, sh.sel, sh.wts);
@@ -925,6 +938,7 @@ __device__ __forceinline__ bool moe_run(const FusedArgs& p, uint8_t* smem, const
       if (j < g.jobs_total) gu3_issue(g, sh.sel, w.gbar, w.wb, j, st, lane);
     }
     ok = gu3_run(g, sh.sel, w.gbar, w.wb, Act3Smem{a, lane % g.lpr}, gw, tw, lane) && ok;
+    phase_stamp(4);
     if (ok) {
       for (int st = 0; st < d.S; ++st) {
         const int j = gw + st * tw;
@@ -948,12 +962,14 @@ __device__ __forceinline__ bool moe_run(const FusedArgs& p, uint8_t* smem, const
     if (blockIdx.x == 0) *p.epoch = sh.tag;
   }
   __syncthreads();
+  phase_stamp(5);
   bool ok_dn = ok && sel_ok && sh.ok != 0;
   if (sh.ok != 0 && sel_ok) {
     // The gate/up activation is no longer read: the ff activation takes its place.
     ActSmem af = carve_act(smem, d.topk * d.F, false);
     quant_act_global(af, d.ff, d.topk * d.F / QK);
     __syncthreads();
+    phase_stamp(6);
     if (ok_dn) ok_dn = dn3_run(d, sh.sel, sh.wts, w.dbar, w.wb, af, gw, tw, lane, sh.pos, sh.np, true, h0);
   }
   return ok_dn;
@@ -975,6 +991,7 @@ __device__ __forceinline__ MoeWarp moe_warp(const FusedArgs& p, uint8_t* smem, i
 // layer to layer, which measured faster than per-type variants.
 __global__ void __launch_bounds__(kMoeWarps * 32, 2) moe_fused_kernel(const __grid_constant__ FusedArgs p) {
   extern __shared__ __align__(128) uint8_t smem[];
+  const unsigned ph_idx = phase_begin();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   ActSmem a = carve_act(smem, p.g.K, true, true);
   double* red = reinterpret_cast<double*>(smem + p.act_bytes);
@@ -990,6 +1007,7 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) moe_fused_kernel(const __gr
   }
   act_load_norm(a, p.g.norm);
   pdl_wait();
+  phase_stamp(1);
   pdl_trigger();
   if (threadIdx.x == 0) {
     sh.pos = p.d.state->pos;
@@ -1000,6 +1018,8 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 2) moe_fused_kernel(const __gr
     if (blockIdx.x == 0) p.sync[1 + ((sh.tag + 1u) & 1u)] = 0u;
   }
   const bool ok = moe_run(p, smem, w, router_cta, router_e, sh, red);
+  phase_stamp(7);
+  phase_end_sync(kPhMoeFused, ph_idx);
   if (!ok && lane == 0) atomicCAS(&p.d.state->error, 0, NH_E_TIMEOUT);
 }
 
@@ -1491,3 +1511,5 @@ extern "C" int nh_moe_layer(const NhMoeLayer* L, void* stream) {
   return launch_fused(p, st);
 }
 
+
+NH_PHASE_TRACE_SETTER(moe)
