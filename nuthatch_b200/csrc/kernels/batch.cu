@@ -262,6 +262,8 @@ struct GroupArgs {
   int64_t out_stride;
   int mode;
   int tok_tile;  // tokens staged per CTA (<= kBatchTokTile)
+  int32_t* err;  // NH_E_TIMEOUT when a bounded wait expires (may be null)
+  int stages;    // batch_mma_staged_kernel: weight stages per warp
 };
 
 __global__ void __launch_bounds__(kBatchWarps * 32, 2) batch_rowdot_kernel(const GroupArgs p) {
@@ -377,30 +379,24 @@ struct SbTree {
   }
 };
 
-// One 16x8 tile of one Q4_K matrix over K (nsb super-blocks): out[r][t] for
-// rows (g, g+8) and tokens (2*tig, 2*tig+1) of the tile.
-__device__ __forceinline__ void tile_q4k_mma(const uint8_t* w_r0, const uint8_t* w_r1, uint64_t rb, int nsb,
-                                             const uint8_t* act_g, const uint8_t* act_t0, const uint8_t* act_t1,
-                                             int tig, float (&out)[2][2]) {
-  (void)rb;
-  SbTree tree[2][2];
+// Super-block s of the tile: rows (g, g+8) at w0 / w1 (the super-block's
+// 144 bytes, global or shared memory), the activation blocks of tokens g,
+// 2*tig and 2*tig+1 at ag / a0p / a1p; the values join tree[row][token].
+__device__ __forceinline__ void sb_q4k_mma(const uint8_t* w0, const uint8_t* w1, const uint8_t* ag,
+                                           const uint8_t* a0p, const uint8_t* a1p, int tig, int s,
+                                           SbTree (&tree)[2][2]) {
   const uint32_t m4 = 0x0F0F0F0Fu;
-  for (int s = 0; s < nsb; ++s) {
-    const uint8_t* w0 = w_r0 + s * kQ4KBytes;
-    const uint8_t* w1 = w_r1 + s * kQ4KBytes;
-    const uint4 h0 = __ldg(reinterpret_cast<const uint4*>(w0));
-    const uint4 h1 = __ldg(reinterpret_cast<const uint4*>(w1));
+  {
+    const uint4 h0 = *reinterpret_cast<const uint4*>(w0);
+    const uint4 h1 = *reinterpret_cast<const uint4*>(w1);
     uint32_t q0[4][2], q1[4][2];
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-      q0[c][0] = __ldg(reinterpret_cast<const uint32_t*>(w0 + 16 + 32 * c + 4 * tig));
-      q0[c][1] = __ldg(reinterpret_cast<const uint32_t*>(w0 + 16 + 32 * c + 16 + 4 * tig));
-      q1[c][0] = __ldg(reinterpret_cast<const uint32_t*>(w1 + 16 + 32 * c + 4 * tig));
-      q1[c][1] = __ldg(reinterpret_cast<const uint32_t*>(w1 + 16 + 32 * c + 16 + 4 * tig));
+      q0[c][0] = *reinterpret_cast<const uint32_t*>(w0 + 16 + 32 * c + 4 * tig);
+      q0[c][1] = *reinterpret_cast<const uint32_t*>(w0 + 16 + 32 * c + 16 + 4 * tig);
+      q1[c][0] = *reinterpret_cast<const uint32_t*>(w1 + 16 + 32 * c + 4 * tig);
+      q1[c][1] = *reinterpret_cast<const uint32_t*>(w1 + 16 + 32 * c + 16 + 4 * tig);
     }
-    const uint8_t* ag = act_g + s * kQ8Stride;
-    const uint8_t* a0p = act_t0 + s * kQ8Stride;
-    const uint8_t* a1p = act_t1 + s * kQ8Stride;
     // Scales and mins (6 bits, one per byte) of both rows.
     const uint32_t sc0a = h0.y & 0x3F3F3F3Fu, m0a = h0.z & 0x3F3F3F3Fu;
     const uint32_t sc0b = (h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u);
@@ -450,6 +446,18 @@ __device__ __forceinline__ void tile_q4k_mma(const uint8_t* w_r0, const uint8_t*
                                   __fmul_rn(__fmul_rn(dmin1, yd), static_cast<float>(summ1))));
     }
   }
+}
+
+// One 16x8 tile of one Q4_K matrix over K (nsb super-blocks) read from global
+// memory: out[r][t] for rows (g, g+8) and tokens (2*tig, 2*tig+1).
+__device__ __forceinline__ void tile_q4k_mma(const uint8_t* w_r0, const uint8_t* w_r1, uint64_t rb, int nsb,
+                                             const uint8_t* act_g, const uint8_t* act_t0, const uint8_t* act_t1,
+                                             int tig, float (&out)[2][2]) {
+  (void)rb;
+  SbTree tree[2][2];
+  for (int s = 0; s < nsb; ++s)
+    sb_q4k_mma(w_r0 + s * kQ4KBytes, w_r1 + s * kQ4KBytes, act_g + s * kQ8Stride, act_t0 + s * kQ8Stride,
+               act_t1 + s * kQ8Stride, tig, s, tree);
 #pragma unroll
   for (int r = 0; r < 2; ++r)
 #pragma unroll
@@ -468,12 +476,13 @@ __device__ __forceinline__ void mma_s8_k16(int (&d)[4], uint32_t a0, uint32_t a1
 // (d*yd)*sumi per super-block and the pairwise tree, as sb_dot_q6k3 forms it.
 // Super-blocks are 210 bytes, so rows start 2-byte aligned: words are
 // assembled from aligned loads with funnel shifts.
-__device__ __forceinline__ void tile_q6k_mma(const uint8_t* w_r0, const uint8_t* w_r1, int nsb,
-                                             const uint8_t* act_g, const uint8_t* act_t0, const uint8_t* act_t1,
-                                             int tig, float (&out)[2][2]) {
-  SbTree tree[2][2];
-  for (int s = 0; s < nsb; ++s) {
-    const uint8_t* wr[2] = {w_r0 + s * kQ6KBytes, w_r1 + s * kQ6KBytes};
+// Super-block s of the tile (rows at w0 / w1: the super-block's 210 bytes,
+// global or shared memory, 2-byte aligned), as sb_q4k_mma.
+__device__ __forceinline__ void sb_q6k_mma(const uint8_t* w0, const uint8_t* w1, const uint8_t* ag,
+                                           const uint8_t* a0p, const uint8_t* a1p, int tig, int s,
+                                           SbTree (&tree)[2][2]) {
+  {
+    const uint8_t* wr[2] = {w0, w1};
     const uint32_t* base[2];
     uint32_t sh[2];
 #pragma unroll
@@ -482,7 +491,7 @@ __device__ __forceinline__ void tile_q6k_mma(const uint8_t* w_r0, const uint8_t*
       base[r] = reinterpret_cast<const uint32_t*>(addr & ~static_cast<uintptr_t>(3));
       sh[r] = static_cast<uint32_t>(addr & 3) * 8;
     }
-    auto word = [&](int r, int i) { return __funnelshift_r(__ldg(base[r] + i), __ldg(base[r] + i + 1), sh[r]); };
+    auto word = [&](int r, int i) { return __funnelshift_r(base[r][i], base[r][i + 1], sh[r]); };
     uint32_t scw[2][4];
     float dd[2];
 #pragma unroll
@@ -491,8 +500,7 @@ __device__ __forceinline__ void tile_q6k_mma(const uint8_t* w_r0, const uint8_t*
       for (int w = 0; w < 4; ++w) scw[r][w] = word(r, 48 + w);
       dd[r] = half_bits_to_float(word(r, 52));
     }
-    const uint8_t* ag = act_g + s * kQ8Stride;
-    const uint8_t* at[2] = {act_t0 + s * kQ8Stride, act_t1 + s * kQ8Stride};
+    const uint8_t* at[2] = {a0p, a1p};
     int bsw[2][8];
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
@@ -536,6 +544,16 @@ __device__ __forceinline__ void tile_q6k_mma(const uint8_t* w_r0, const uint8_t*
         tree[r][t].add(s, __fmul_rn(__fmul_rn(dd[r], yd), static_cast<float>(sumi[r][t])));
     }
   }
+}
+
+// One 16x8 tile of one Q6_K matrix over K read from global memory.
+__device__ __forceinline__ void tile_q6k_mma(const uint8_t* w_r0, const uint8_t* w_r1, int nsb,
+                                             const uint8_t* act_g, const uint8_t* act_t0, const uint8_t* act_t1,
+                                             int tig, float (&out)[2][2]) {
+  SbTree tree[2][2];
+  for (int s = 0; s < nsb; ++s)
+    sb_q6k_mma(w_r0 + s * kQ6KBytes, w_r1 + s * kQ6KBytes, act_g + s * kQ8Stride, act_t0 + s * kQ8Stride,
+               act_t1 + s * kQ8Stride, tig, s, tree);
 #pragma unroll
   for (int r = 0; r < 2; ++r)
 #pragma unroll
@@ -550,7 +568,9 @@ __global__ void __launch_bounds__(kBatchWarps * 32, 2) batch_mma_kernel(const Gr
   const int ctas_per_group = (tiles_per_group + kBatchWarps - 1) / kBatchWarps;
   const int e = blockIdx.x / ctas_per_group;
   const int rt = (blockIdx.x % ctas_per_group) * kBatchWarps + warp;
+  const unsigned ph_idx = phase_begin();
   pdl_wait();
+  phase_stamp(1);
   pdl_trigger();
   if (rt >= tiles_per_group) return;
   const int t_off = p.off != nullptr ? p.off[e] : 0;
@@ -561,6 +581,20 @@ __global__ void __launch_bounds__(kBatchWarps * 32, 2) batch_mma_kernel(const Gr
   const uint8_t* W = p.w + static_cast<uint64_t>(e) * p.mstride;
   const uint8_t* W2 = p.w2 != nullptr ? p.w2 + static_cast<uint64_t>(e) * p.mstride2 : nullptr;
   const int blk_bytes = nsb * kQ8Stride;
+  // The tile's rows are one contiguous slab per matrix: start it towards L2
+  // in one request, so the per-super-block loads below hit L2 instead of
+  // waiting for DRAM one super-block at a time.
+  if (lane == 0) {
+    const int nrows = min(16, p.rows - rt * 16);
+    const uint8_t* s1 = W + static_cast<uint64_t>(rt) * 16 * p.rb;
+    const uint64_t n1 = static_cast<uint64_t>(nrows) * p.rb;
+    if (((reinterpret_cast<uintptr_t>(s1) | n1) & 15) == 0) prefetch_l2(s1, static_cast<uint32_t>(n1));
+    if (W2 != nullptr) {
+      const uint8_t* s2 = W2 + static_cast<uint64_t>(rt) * 16 * p.rb2;
+      const uint64_t n2 = static_cast<uint64_t>(nrows) * p.rb2;
+      if (((reinterpret_cast<uintptr_t>(s2) | n2) & 15) == 0) prefetch_l2(s2, static_cast<uint32_t>(n2));
+    }
+  }
   // Token tiles of 8: ungrouped products split them over blockIdx.y.
   const int n_tt = (t_cnt + 7) / 8;
   for (int tt = blockIdx.y; tt < n_tt; tt += gridDim.y) {
@@ -609,7 +643,186 @@ __global__ void __launch_bounds__(kBatchWarps * 32, 2) batch_mma_kernel(const Gr
         }
       }
     }
+    if (tt == static_cast<int>(blockIdx.y)) phase_stamp(2);  // warp 0's first token tile done
   }
+  phase_value(6, static_cast<unsigned long long>(n_tt));
+  phase_value(7, static_cast<unsigned long long>(t_cnt));
+  phase_value(8, static_cast<unsigned long long>(p.rows) << 32 | static_cast<unsigned>(p.K));
+  phase_value(10, reinterpret_cast<uintptr_t>(p.w));  // identifies the launch's weight
+  phase_end(kPhBatchMma, ph_idx);
+}
+
+// The tensor-core form with its operands in shared memory.  Each warp owns a
+// 16-row tile (as batch_mma_kernel) and a ring of `stages` shared-memory
+// stages: stage = the tile's 16 rows (of each matrix) for one super-block,
+// one bulk copy per row (lane = row; Q6_K blocks through their covering
+// 16-byte span), completed on the stage's mbarrier, so the copies of the next
+// super-blocks are in flight while this one is multiplied.  The 8 tokens of a
+// token tile are copied once per tile into shared memory for all warps.  The
+// arithmetic is sb_q4k_mma / sb_q6k_mma's, so results equal batch_mma_kernel's.
+constexpr int kMmaSlotQ4 = kQ4KBytes;  // 144: Q4_K blocks start 16-byte aligned
+// A 210-byte Q6_K block's covering 16-byte span is at most 224 bytes; the
+// reader assembles 4-byte words from an aligned base up to 216 bytes past a
+// block start that sits up to 14 bytes into the span: 240 bytes per slot.
+constexpr int kMmaSlotQ6 = 240;
+
+__host__ __device__ inline int mma_slot_bytes(int type) { return type == NH_TYPE_Q4_K ? kMmaSlotQ4 : kMmaSlotQ6; }
+
+__global__ void __launch_bounds__(kBatchWarps * 32, 2) batch_mma_staged_kernel(const GroupArgs p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, tig = lane & 3;
+  const int nsb = p.K / QK, S = p.stages;
+  const int nmat = p.w2 != nullptr ? 2 : 1;
+  const int slot0 = mma_slot_bytes(p.type), slot1 = mma_slot_bytes(p.type2);
+  const int bb0 = p.type == NH_TYPE_Q4_K ? kQ4KBytes : kQ6KBytes;
+  const int bb1 = p.type2 == NH_TYPE_Q4_K ? kQ4KBytes : kQ6KBytes;
+  const int stage_bytes = 16 * (slot0 + (nmat == 2 ? slot1 : 0));
+  const int blk_bytes = nsb * kQ8Stride;
+  uint8_t* act_s = smem;                                    // [8 tokens][nsb][kQ8Stride]
+  uint64_t* abar = reinterpret_cast<uint64_t*>(smem + 8 * blk_bytes);
+  uint64_t* wbar = abar + 1 + warp * S;                     // this warp's stage barriers
+  uint8_t* ring = smem + ((8 * blk_bytes + 8 * (1 + kBatchWarps * S) + 127) & ~127) +
+                  static_cast<size_t>(warp) * S * stage_bytes;
+  const int tiles_per_group = (p.rows + 15) / 16;
+  const int ctas_per_group = (tiles_per_group + kBatchWarps - 1) / kBatchWarps;
+  const int e = blockIdx.x / ctas_per_group;
+  const int rt = (blockIdx.x % ctas_per_group) * kBatchWarps + warp;
+  const bool has_rows = rt < tiles_per_group;  // warps without rows still meet the CTA barriers
+  const uint8_t* W = p.w + static_cast<uint64_t>(e) * p.mstride;
+  const uint8_t* W2 = p.w2 != nullptr ? p.w2 + static_cast<uint64_t>(e) * p.mstride2 : nullptr;
+  if (threadIdx.x == 0) mbar_init(abar, 1);
+  if (lane == 0)
+    for (int i = 0; i < S; ++i) mbar_init(&wbar[i], 1);
+  fence_barrier_init();
+  __syncthreads();
+  // Stage k of this warp's copies: super-block s into ring stage k % S.
+  auto issue = [&](int k, int s) {
+    const int st = k % S;
+    uint32_t len = 0, off = 0;
+    const uint8_t* src = nullptr;
+    uint8_t* dst = nullptr;
+    if (lane < nmat * 16) {
+      const int m = lane >> 4, r = lane & 15;
+      const int row = min(rt * 16 + r, p.rows - 1);
+      const uint8_t* wb = m == 0 ? W + static_cast<uint64_t>(row) * p.rb + s * bb0
+                                 : W2 + static_cast<uint64_t>(row) * p.rb2 + s * bb1;
+      src = span16(wb, m == 0 ? bb0 : bb1, &len, &off);
+      dst = ring + static_cast<size_t>(st) * stage_bytes + (m == 0 ? r * slot0 : 16 * slot0 + r * slot1);
+    }
+    uint32_t total = len;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+    if (lane == 0) mbar_expect_tx(&wbar[st], total);
+    __syncwarp();
+    if (lane < nmat * 16) bulk_g2s(dst, src, len, &wbar[st]);
+  };
+  int k_issued = 0, k_used = 0;  // this warp's stages issued / consumed (all tiles)
+  bool failed = false;
+  const bool dense = p.off == nullptr;
+  // Dense products: the weights do not depend on the previous kernel.
+  const int first_tile = blockIdx.y;
+  if (dense && has_rows)
+    for (int s = 0; s < min(S, nsb); ++s) issue(k_issued++, s);
+  pdl_wait();
+  pdl_trigger();
+  const int t_off = p.off != nullptr ? p.off[e] : 0;
+  const int t_cnt = p.off != nullptr ? p.cnt[e] : p.n_tok;
+  const int n_tt = (t_cnt + 7) / 8;
+  int it_tile = 0;
+  for (int tt = first_tile; tt < n_tt; tt += gridDim.y, ++it_tile) {
+    const int tbase = tt * 8;
+    if (has_rows && !(dense && it_tile == 0))
+      for (int s = 0; s < min(S, nsb); ++s) issue(k_issued++, s);
+    // The tile's 8 activation rows (clamped past the end), once for all warps.
+    __syncthreads();  // every warp is done with the previous tile's rows
+    if (warp == 0) {
+      uint32_t len = 0;
+      const uint8_t* src = nullptr;
+      if (lane < 8) {
+        const int tc = min(tbase + lane, t_cnt - 1);
+        const int a = p.act_idx != nullptr ? p.act_idx[t_off + tc] : tc;
+        src = p.q8 + static_cast<int64_t>(a) * blk_bytes;
+        len = static_cast<uint32_t>(blk_bytes);
+      }
+      if (lane == 0) mbar_expect_tx(abar, 8u * static_cast<uint32_t>(blk_bytes));
+      __syncwarp();
+      if (lane < 8) bulk_g2s(act_s + lane * blk_bytes, src, len, abar);
+    }
+    if (!mbar_wait(abar, static_cast<uint32_t>(it_tile & 1))) failed = true;
+    float v[2][2] = {{0.f, 0.f}, {0.f, 0.f}}, v2[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+    if (has_rows) {
+      SbTree tree[2][2][2];
+      const uint8_t* ag = act_s + g * blk_bytes;
+      const uint8_t* a0 = act_s + (2 * tig) * blk_bytes;
+      const uint8_t* a1 = act_s + (2 * tig + 1) * blk_bytes;
+      for (int s = 0; s < nsb; ++s) {
+        const int st = k_used % S;
+        if (!mbar_wait(&wbar[st], static_cast<uint32_t>((k_used / S) & 1))) failed = true;
+        ++k_used;
+        const uint8_t* stage = ring + static_cast<size_t>(st) * stage_bytes;
+        const int r0 = min(rt * 16 + g, p.rows - 1), r1 = min(rt * 16 + g + 8, p.rows - 1);
+#pragma unroll
+        for (int m = 0; m < 2; ++m) {
+          if (m >= nmat) break;
+          const uint8_t* wm = m == 0 ? W : W2;
+          const uint64_t rb = m == 0 ? p.rb : p.rb2;
+          const int bb = m == 0 ? bb0 : bb1, sl = m == 0 ? slot0 : slot1;
+          const uint8_t* base = stage + (m == 0 ? 0 : 16 * slot0);
+          // Offsets of the two rows' blocks inside their 16-byte spans.
+          const uint32_t o0 =
+              static_cast<uint32_t>(reinterpret_cast<uintptr_t>(wm + static_cast<uint64_t>(r0) * rb + s * bb) & 15);
+          const uint32_t o1 =
+              static_cast<uint32_t>(reinterpret_cast<uintptr_t>(wm + static_cast<uint64_t>(r1) * rb + s * bb) & 15);
+          const uint8_t* w0 = base + (r0 - rt * 16) * sl + o0;
+          const uint8_t* w1 = base + (r1 - rt * 16) * sl + o1;
+          const int type = m == 0 ? p.type : p.type2;
+          if (type == NH_TYPE_Q4_K)
+            sb_q4k_mma(w0, w1, ag + s * kQ8Stride, a0 + s * kQ8Stride, a1 + s * kQ8Stride, tig, s, tree[m]);
+          else
+            sb_q6k_mma(w0, w1, ag + s * kQ8Stride, a0 + s * kQ8Stride, a1 + s * kQ8Stride, tig, s, tree[m]);
+        }
+        __syncwarp();
+        if (s + S < nsb) issue(k_issued++, s + S);
+      }
+#pragma unroll
+      for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          v[r][t] = tree[0][r][t].r;
+          v2[r][t] = tree[1][r][t].r;
+        }
+      const int row0 = rt * 16 + g, row1 = row0 + 8;
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const int row = r == 0 ? row0 : row1;
+        if (row >= p.rows) continue;
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          const int tok = tbase + 2 * tig + t;
+          if (tok >= t_cnt) continue;
+          const int o = p.out_idx != nullptr ? p.out_idx[t_off + tok] : tok;
+          float* dst = p.out + static_cast<int64_t>(o) * p.out_stride + row;
+          if (p.mode == kStore) {
+            *dst = v[r][t];
+          } else if (p.mode == kResidual) {
+            *dst = __fadd_rn(*dst, v[r][t]);
+          } else {
+            const float gv = v[r][t];
+            const float sl = __fdiv_rn(gv, __fadd_rn(1.0f, exp_cw(-gv)));
+            *dst = __fmul_rn(sl, v2[r][t]);
+          }
+        }
+      }
+    }
+  }
+  // Copies issued for a tile that never started (dense prefetch with no
+  // token tile for this CTA) must land before the CTA exits.
+  while (k_used < k_issued) {
+    if (!mbar_wait(&wbar[k_used % S], static_cast<uint32_t>((k_used / S) & 1))) failed = true;
+    ++k_used;
+  }
+  if (failed && lane == 0 && p.err != nullptr) atomicCAS(p.err, 0, NH_E_TIMEOUT);
 }
 
 // ---------------------------------------------------------------- QK-norm, RoPE, KV append
@@ -1397,6 +1610,20 @@ extern "C" int nh_batch_prep(const float* x, int64_t x_stride, int64_t rows, con
 // (below it the per-CTA token tiles would be mostly empty).
 constexpr int kTcMinTokens = 128;
 
+
+namespace {
+// The shared-memory staged form of the tensor-core products is used unless
+// NH_MMA_STAGED=0 (read once; both forms give identical results).
+bool mma_staged_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* s = std::getenv("NH_MMA_STAGED");
+    v = (s != nullptr && s[0] == '0') ? 0 : 1;
+  }
+  return v != 0;
+}
+}  // namespace
+
 extern "C" int nh_batch_rowdot(const NhGroupedRowDot* g, void* stream) {
   if (g == nullptr || g->w == nullptr || g->q8 == nullptr || g->out == nullptr || g->rows <= 0 || g->n_groups <= 0)
     return NH_E_ARG;
@@ -1438,6 +1665,7 @@ extern "C" int nh_batch_rowdot(const NhGroupedRowDot* g, void* stream) {
   p.out = g->out;
   p.out_stride = g->out_stride;
   p.mode = g->mode;
+  p.err = g->err;
   // Work split: row blocks of whole warp passes (8 warps x P rows) and token
   // tiles, aiming at about eight CTAs per SM over all groups so that each
   // warp has only a few passes; smaller token tiles when the row blocks alone
@@ -1464,6 +1692,40 @@ extern "C" int nh_batch_rowdot(const NhGroupedRowDot* g, void* stream) {
     int gy = 1;
     if (p.off == nullptr)
       while (gy < tok_tiles && static_cast<int64_t>(ctas_per_group) * p.n_groups * gy < 4 * sms) ++gy;
+    // The staged form copies whole blocks by their 16-byte spans: Q4_K blocks
+    // must start 16-byte aligned (span = block), Q6_K blocks 2-byte aligned
+    // (span <= 224 bytes), and the activation rows 16-byte aligned.
+    auto blocks_ok = [](const void* w, uint64_t mstride, int type) {
+      const uintptr_t a = reinterpret_cast<uintptr_t>(w);
+      return type == NH_TYPE_Q4_K ? (a & 15) == 0 && (mstride & 15) == 0 : (a & 1) == 0 && (mstride & 1) == 0;
+    };
+    const bool staged_ok = blocks_ok(p.w, p.mstride, p.type) &&
+                           (g->w2 == nullptr || blocks_ok(p.w2, p.mstride2, p.type2)) &&
+                           (reinterpret_cast<uintptr_t>(p.q8) & 15) == 0;
+    if (staged_ok && mma_staged_enabled()) {
+      // Shared-memory operands: the token tile's rows, the barriers and each
+      // warp's ring of weight stages (as many as fit two CTAs per SM, 2..4).
+      const int nsb = p.K / QK;
+      const size_t act = static_cast<size_t>(8) * nsb * kQ8Stride;
+      const size_t stage = static_cast<size_t>(16) *
+                           (mma_slot_bytes(p.type) + (g->w2 != nullptr ? mma_slot_bytes(p.type2) : 0));
+      auto bytes = [&](int S) {
+        return ((act + 8 * (1 + kBatchWarps * S) + 127) & ~static_cast<size_t>(127)) +
+               static_cast<size_t>(kBatchWarps) * S * stage;
+      };
+      int S = 4;
+      while (S > 2 && bytes(S) > 110 * 1024) --S;
+      p.stages = S;
+      const size_t smem = bytes(S);
+      static SmemLimit configured_staged;
+      if (smem <= 220 * 1024 && ensure_smem(batch_mma_staged_kernel, smem, configured_staged)) {
+        // Grouped products: a second CTA per (group, row block) takes every
+        // other token tile, so experts with many tokens are not walked by one.
+        if (p.off != nullptr) gy = std::min(tok_tiles, 2);
+        return launch_pdl(batch_mma_staged_kernel, dim3(p.n_groups * ctas_per_group, gy),
+                          dim3(kBatchWarps * 32), smem, static_cast<cudaStream_t>(stream), p);
+      }
+    }
     return launch_pdl(batch_mma_kernel, dim3(p.n_groups * ctas_per_group, gy), dim3(kBatchWarps * 32), 0,
                       static_cast<cudaStream_t>(stream), p);
   }
@@ -1685,3 +1947,5 @@ extern "C" int nh_batch_argmax(NhDecodeState* state, const float* logits, int n_
   return launch_pdl(batch_argmax_kernel, dim3(n_seq), dim3(256), 0, static_cast<cudaStream_t>(stream), state, logits,
                     static_cast<int>(n_vocab), fed, out_tokens, n_predict, static_cast<unsigned*>(scratch));
 }
+
+NH_PHASE_TRACE_SETTER(batch)

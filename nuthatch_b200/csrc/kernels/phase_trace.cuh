@@ -110,6 +110,7 @@ enum PhaseKernel : int {
   kPhRouter = 7,
   kPhGateUp = 8,
   kPhDown = 9,
+  kPhBatchMma = 10,
 };
 
 }  // namespace nh

@@ -4,6 +4,7 @@
     python -m nuthatch_b200.phase_trace decode      # batch-1 resident decode (configuration 1)
     python -m nuthatch_b200.phase_trace prefill     # tcgen05 products of a 1024-token prefill
     python -m nuthatch_b200.phase_trace streaming   # two-phase streaming decode, budget 32
+    python -m nuthatch_b200.phase_trace batched     # mma.sync grouped products of a bs64 decode step
 
 The diagnostic library records, per CTA of the stamped kernels, %globaltimer
 stamps at fixed points (kernel entry, after griddepcontrol.wait, after the
@@ -21,9 +22,9 @@ import time
 
 import numpy as np
 
-UNITS = ("gemv", "attention", "moe", "misc", "grouped_tc")
+UNITS = ("gemv", "attention", "moe", "misc", "grouped_tc", "batch")
 KERNELS = {1: "gemv3", 2: "attention", 3: "moe_fused", 4: "embed", 5: "lm_head", 6: "grouped_tc", 7: "router",
-           8: "gate_up", 9: "down"}
+           8: "gate_up", 9: "down", 10: "batch_mma"}
 RING = 1 << 20  # records (kPhaseTraceCap); 128 bytes each
 
 
@@ -202,8 +203,51 @@ def streaming(args):
                   f"(mean {np.mean(d['gap']) if d['gap'] else 0:6.2f})")
 
 
+def batched(args):
+    """64 sequences, context 64, 4 decode steps after warm-up: per product of
+    the mma.sync grouped kernel (by weight shape), the median launch span,
+    the CTA lifetimes (median / max), warp 0's first token tile, and how the
+    lifetimes follow the number of token tiles a CTA walks."""
+    import torch
+
+    from . import OlmoeModel, generate_batch_ex, synth
+
+    torch.cuda.set_device(0)
+    ring = Ring()
+    m = OlmoeModel.Load(str(synth.cached(synth.OLMOE_1B7B)))
+    prompts = np.random.default_rng(3).integers(0, m.config().n_vocab, (64, 64)).tolist()
+    generate_batch_ex(m, prompts, 4, False)
+    ring.reset()
+    r = generate_batch_ex(m, prompts, 4, False)
+    kid, t = ring.records()
+    names = {(1024, 2048): "gate/up (grouped, SwiGLU)", (2048, 1024): "down (grouped)",
+             (2048, 2048): "q / out_proj", (50304, 2048): "lm_head"}
+    per = {}
+    s = kid == 10
+    t = t[s]
+    # One launch = consecutive records with the same weight pointer (stamp 10);
+    # the decode steps' launches come last: 16 layers x 6 products + lm_head per step.
+    cut = [0] + [i for i in range(1, len(t)) if t[i, 10] != t[i - 1, 10]] + [len(t)]
+    mma = [t[a:b] for a, b in zip(cut[:-1], cut[1:])]
+    for tt in mma[-4 * 97:]:
+        rows, K = int(tt[0, 8]) >> 32, int(tt[0, 8]) & 0xFFFFFFFF
+        per.setdefault(names.get((rows, K), f"rows {rows} K {K}"), []).append(tt)
+    print(json.dumps({"workload": "olmoe-1b7b bs64, context 64, 4 decode steps (+ chunked prefill)",
+                      "decode_ms": r["decode_ms"], "prefill_ms": r["prefill_ms"]}))
+    for name, ls in per.items():
+        span = [(x[:, 9].max() - x[:, 0].min()) / 1e3 for x in ls]
+        life = np.concatenate([(x[:, 9] - x[:, 1]) / 1e3 for x in ls])
+        first = np.concatenate([(x[:, 2] - x[:, 1]) / 1e3 for x in ls if (x[:, 2] > 0).all()] or [np.zeros(1)])
+        ntt = np.concatenate([x[:, 6] for x in ls])
+        line = (f"{name:26s} launches {len(ls):4d}  span median {np.median(span):7.1f} us  CTA life median "
+                f"{np.median(life):6.1f} max {life.max():6.1f} us  first tile {np.median(first):5.1f} us")
+        for n in sorted(set(ntt.tolist()))[:4]:
+            line += f"  [{int(n)} tiles: {np.median(life[ntt == n]):.1f} us x{int((ntt == n).sum())}]"
+        print(line)
+
+
 def main() -> None:
-    modes = {"decode": decode, "prefill": prefill, "streaming": streaming}
+    modes = {"decode": decode, "prefill": prefill, "streaming": streaming, "batched": batched}
     mode = sys.argv[1] if len(sys.argv) > 1 else "decode"
     if mode not in modes:
         raise SystemExit(f"usage: python -m nuthatch_b200.phase_trace [{'|'.join(modes)}]")
