@@ -691,6 +691,7 @@ __global__ void __launch_bounds__(kBatchWarps * 32, 2) batch_mma_staged_kernel(c
   const bool has_rows = rt < tiles_per_group;  // warps without rows still meet the CTA barriers
   const uint8_t* W = p.w + static_cast<uint64_t>(e) * p.mstride;
   const uint8_t* W2 = p.w2 != nullptr ? p.w2 + static_cast<uint64_t>(e) * p.mstride2 : nullptr;
+  const unsigned ph_idx = phase_begin();
   if (threadIdx.x == 0) mbar_init(abar, 1);
   if (lane == 0)
     for (int i = 0; i < S; ++i) mbar_init(&wbar[i], 1);
@@ -725,11 +726,14 @@ __global__ void __launch_bounds__(kBatchWarps * 32, 2) batch_mma_staged_kernel(c
   if (dense && has_rows)
     for (int s = 0; s < min(S, nsb); ++s) issue(k_issued++, s);
   pdl_wait();
+  phase_stamp(1);
   pdl_trigger();
   const int t_off = p.off != nullptr ? p.off[e] : 0;
   const int t_cnt = p.off != nullptr ? p.cnt[e] : p.n_tok;
   const int n_tt = (t_cnt + 7) / 8;
   int it_tile = 0;
+  PhaseAcc ph;  // waits for the token rows / for weight stages / multiply
+  ph.start();
   for (int tt = first_tile; tt < n_tt; tt += gridDim.y, ++it_tile) {
     const int tbase = tt * 8;
     if (has_rows && !(dense && it_tile == 0))
@@ -750,6 +754,7 @@ __global__ void __launch_bounds__(kBatchWarps * 32, 2) batch_mma_staged_kernel(c
       if (lane < 8) bulk_g2s(act_s + lane * blk_bytes, src, len, abar);
     }
     if (!mbar_wait(abar, static_cast<uint32_t>(it_tile & 1))) failed = true;
+    ph.mark(0);
     float v[2][2] = {{0.f, 0.f}, {0.f, 0.f}}, v2[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
     if (has_rows) {
       SbTree tree[2][2][2];
@@ -760,6 +765,7 @@ __global__ void __launch_bounds__(kBatchWarps * 32, 2) batch_mma_staged_kernel(c
         const int st = k_used % S;
         if (!mbar_wait(&wbar[st], static_cast<uint32_t>((k_used / S) & 1))) failed = true;
         ++k_used;
+        ph.mark(1);
         const uint8_t* stage = ring + static_cast<size_t>(st) * stage_bytes;
         const int r0 = min(rt * 16 + g, p.rows - 1), r1 = min(rt * 16 + g + 8, p.rows - 1);
 #pragma unroll
@@ -784,6 +790,7 @@ __global__ void __launch_bounds__(kBatchWarps * 32, 2) batch_mma_staged_kernel(c
         }
         __syncwarp();
         if (s + S < nsb) issue(k_issued++, s + S);
+        ph.mark(2);
       }
 #pragma unroll
       for (int r = 0; r < 2; ++r)
@@ -823,6 +830,12 @@ __global__ void __launch_bounds__(kBatchWarps * 32, 2) batch_mma_staged_kernel(c
     ++k_used;
   }
   if (failed && lane == 0 && p.err != nullptr) atomicCAS(p.err, 0, NH_E_TIMEOUT);
+  ph.store();
+  phase_value(6, static_cast<unsigned long long>(n_tt));
+  phase_value(7, static_cast<unsigned long long>(t_cnt));
+  phase_value(8, static_cast<unsigned long long>(p.rows) << 32 | static_cast<unsigned>(p.K));
+  phase_value(10, reinterpret_cast<uintptr_t>(p.w));
+  phase_end(kPhBatchMmaStaged, ph_idx);
 }
 
 // ---------------------------------------------------------------- QK-norm, RoPE, KV append

@@ -111,6 +111,7 @@ enum PhaseKernel : int {
   kPhGateUp = 8,
   kPhDown = 9,
   kPhBatchMma = 10,
+  kPhBatchMmaStaged = 11,
 };
 
 }  // namespace nh

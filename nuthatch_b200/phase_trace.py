@@ -223,7 +223,8 @@ def batched(args):
     names = {(1024, 2048): "gate/up (grouped, SwiGLU)", (2048, 1024): "down (grouped)",
              (2048, 2048): "q / out_proj", (50304, 2048): "lm_head"}
     per = {}
-    s = kid == 10
+    staged = bool((kid == 11).any())
+    s = kid == (11 if staged else 10)
     t = t[s]
     # One launch = consecutive records with the same weight pointer (stamp 10);
     # the decode steps' launches come last: 16 layers x 6 products + lm_head per step.
@@ -233,14 +234,21 @@ def batched(args):
         rows, K = int(tt[0, 8]) >> 32, int(tt[0, 8]) & 0xFFFFFFFF
         per.setdefault(names.get((rows, K), f"rows {rows} K {K}"), []).append(tt)
     print(json.dumps({"workload": "olmoe-1b7b bs64, context 64, 4 decode steps (+ chunked prefill)",
-                      "decode_ms": r["decode_ms"], "prefill_ms": r["prefill_ms"]}))
+                      "decode_ms": r["decode_ms"], "prefill_ms": r["prefill_ms"],
+                      "kernel": "batch_mma_staged_kernel" if staged else "batch_mma_kernel"}))
     for name, ls in per.items():
         span = [(x[:, 9].max() - x[:, 0].min()) / 1e3 for x in ls]
         life = np.concatenate([(x[:, 9] - x[:, 1]) / 1e3 for x in ls])
         first = np.concatenate([(x[:, 2] - x[:, 1]) / 1e3 for x in ls if (x[:, 2] > 0).all()] or [np.zeros(1)])
         ntt = np.concatenate([x[:, 6] for x in ls])
         line = (f"{name:26s} launches {len(ls):4d}  span median {np.median(span):7.1f} us  CTA life median "
-                f"{np.median(life):6.1f} max {life.max():6.1f} us  first tile {np.median(first):5.1f} us")
+                f"{np.median(life):6.1f} max {life.max():6.1f} us")
+        if staged:
+            cat = np.concatenate(ls)
+            tot = cat[:, 2:5].sum(axis=0) / max(1, len(cat)) / 1e3
+            line += f"  per CTA: rows wait {tot[0]:.1f} us, stage waits {tot[1]:.1f} us, multiply {tot[2]:.1f} us"
+        else:
+            line += f"  first tile {np.median(first):5.1f} us"
         for n in sorted(set(ntt.tolist()))[:4]:
             line += f"  [{int(n)} tiles: {np.median(life[ntt == n]):.1f} us x{int((ntt == n).sum())}]"
         print(line)
