@@ -346,7 +346,16 @@ __device__ inline void attn_finish(const AttnArgs& p, int h, int sp, int pos, co
   __syncthreads();
   if (!sh.s_last) return;
   __threadfence();
-  // Combine the splits in order: weights exp(m_s - M) staged in shared memory.
+  // Combine the splits in order.  The staged K and V rows are no longer read:
+  // they hold the weights and sums (up to 64*(hd+4) floats / 32*hd doubles).
+  if (n_active <= kAttnSplit * (hd + 4) && n_active <= (kAttnSplit / 2) * hd) {
+    const int64_t base = static_cast<int64_t>(h) * p.n_split;
+    combine_splits(p.part_m + base, p.part_l + base, p.part_acc + base * hd, n_active, hd, Ks,
+                   reinterpret_cast<double*>(Vs), out, tid, nt, part);
+    if (tid == 0) p.tickets[h] = 0u;
+    __syncthreads();
+    return;
+  }
   const volatile float* pm = p.part_m;
   const volatile double* pl = p.part_l;
   float M = -INFINITY;

@@ -955,6 +955,7 @@ __global__ void __launch_bounds__(kBAttnThreads) batch_attention_kernel(const BA
   const int n_kv = pos + 1;
   const int n_active = (n_kv + kBAttnSplit - 1) / kBAttnSplit;
   if (sp >= n_active) return;
+  const unsigned ph_idx = phase_begin();
   extern __shared__ __align__(128) float sm[];
   const int hd = p.hd, kst = hd + 4;
   float* Ks = sm;
@@ -977,6 +978,7 @@ __global__ void __launch_bounds__(kBAttnThreads) batch_attention_kernel(const BA
   }
   __syncthreads();
   pdl_wait();
+  phase_stamp(1);
   pdl_trigger();
   // Every row of the range, including the current position, is in the cache.
   if (tid == 0) mbar_expect_tx(&bar, 2u * row * static_cast<uint32_t>(n));
@@ -993,6 +995,7 @@ __global__ void __launch_bounds__(kBAttnThreads) batch_attention_kernel(const BA
   const bool ok = mbar_wait(&bar, 0);
   if (!ok && tid == 0) atomicCAS(&p.state->error, 0, NH_E_TIMEOUT);
   __syncthreads();
+  phase_stamp(2);
   float my = -INFINITY;
   if ((hd & 31) == 0) {
     if (tid < n) {
@@ -1022,6 +1025,8 @@ __global__ void __launch_bounds__(kBAttnThreads) batch_attention_kernel(const BA
   for (int w = 0; w < nw; ++w) l += red[w];
   if (tid < n) sc[tid] = n_active == 1 ? __fmul_rn(e, static_cast<float>(1.0 / l)) : e;
   __syncthreads();
+  phase_stamp(3);
+  phase_value(6, static_cast<unsigned long long>(n_active));
   float* out = p.out + static_cast<int64_t>(b) * dq + h * hd;
   if (n_active == 1) {
     for (int i = tid; i < hd; i += blockDim.x) {
@@ -1029,6 +1034,7 @@ __global__ void __launch_bounds__(kBAttnThreads) batch_attention_kernel(const BA
       for (int j = 0; j < n; ++j) acc = __fadd_rn(acc, __fmul_rn(Vs[j * hd + i], sc[j]));
       out[i] = acc;
     }
+    phase_end_sync(kPhBatchAttention, ph_idx);
     return;
   }
   const int64_t bh = static_cast<int64_t>(b) * p.n_head + h;
@@ -1043,13 +1049,28 @@ __global__ void __launch_bounds__(kBAttnThreads) batch_attention_kernel(const BA
     p.part_l[slot] = l;
   }
   __syncthreads();
+  phase_stamp(4);
   if (tid == 0) {
     __threadfence();
     s_last = atomicAdd(&p.tickets[bh], 1u) == static_cast<unsigned>(n_active - 1);
   }
   __syncthreads();
-  if (!s_last) return;
+  phase_stamp(5);
+  if (!s_last) {
+    phase_end(kPhBatchAttention, ph_idx);
+    return;
+  }
+  phase_value(7, 1);
   __threadfence();
+  // The staged K and V rows are no longer read: they hold the split weights
+  // and sums (up to 64*(hd+4) floats / 32*hd doubles).
+  if (n_active <= kBAttnSplit * kst && n_active <= (kBAttnSplit / 2) * hd) {
+    combine_splits(p.part_m + bh * p.n_split, p.part_l + bh * p.n_split, p.part_acc + bh * p.n_split * hd,
+                   n_active, hd, Ks, reinterpret_cast<double*>(Vs), out, tid, blockDim.x, true);
+    if (tid == 0) p.tickets[bh] = 0u;
+    phase_end_sync(kPhBatchAttention, ph_idx);
+    return;
+  }
   const volatile float* pm = p.part_m + bh * p.n_split;
   const volatile double* pl = p.part_l + bh * p.n_split;
   float M = -INFINITY;
@@ -1072,6 +1093,7 @@ __global__ void __launch_bounds__(kBAttnThreads) batch_attention_kernel(const BA
     out[i] = __fmul_rn(acc, inv);
   }
   if (tid == 0) p.tickets[bh] = 0u;
+  phase_end_sync(kPhBatchAttention, ph_idx);
 }
 
 // ---------------------------------------------------------------- prefill attention

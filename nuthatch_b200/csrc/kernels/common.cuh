@@ -114,6 +114,43 @@ __device__ __forceinline__ const uint8_t* stage_bytes_warp(uint8_t* dst, const u
   return dst + off;
 }
 
+// ------------------------------------------------------------ split combination
+// The n_active split partials of one attention head (maximum m_s, double
+// sum l_s, weighted V sums acc_s[hd], written by other CTAs and read through
+// L2) combined in split order: M = max_s m_s, w_s = exp_cw(m_s - M),
+// L = sum_s l_s * w_s (double, in order), out[i] = (sum_s acc_s[i] * w_s, in
+// order) * (1/L).  The maxima/weights (ws, n_active floats) and the sums (ls,
+// n_active doubles) are staged in shared memory first, all loads in flight at
+// once.  Block-wide; threads with part = false only meet the barriers.
+__device__ inline void combine_splits(const float* part_m, const double* part_l, const float* part_acc, int n_active,
+                                      int hd, float* ws, double* ls, float* out, int tid, int nt, bool part) {
+  for (int s = tid; s < n_active; s += nt) {
+    if (!part) break;
+    ws[s] = __ldcg(part_m + s);
+    ls[s] = __ldcg(part_l + s);
+  }
+  __syncthreads();
+  float M = -INFINITY;
+  for (int s = 0; s < n_active; ++s) M = fmaxf(M, ws[s]);
+  __syncthreads();
+  for (int s = tid; s < n_active; s += nt) {
+    if (!part) break;
+    ws[s] = exp_cw(__fsub_rn(ws[s], M));
+  }
+  __syncthreads();
+  double L = 0.0;
+  for (int s = 0; s < n_active; ++s) L += ls[s] * static_cast<double>(ws[s]);
+  const float inv = static_cast<float>(1.0 / L);
+  if (part) {
+    for (int i = tid; i < hd; i += nt) {
+      float acc = 0.f;
+      for (int s = 0; s < n_active; ++s)
+        acc = __fadd_rn(acc, __fmul_rn(__ldcg(part_acc + static_cast<int64_t>(s) * hd + i), ws[s]));
+      out[i] = __fmul_rn(acc, inv);
+    }
+  }
+}
+
 // ------------------------------------------------------------ activation (smem)
 // One activation row in shared memory: its f32 values (the staged input, then
 // the normalised row), the staged RMSNorm weight, and, for quantised weights,

@@ -112,6 +112,7 @@ enum PhaseKernel : int {
   kPhDown = 9,
   kPhBatchMma = 10,
   kPhBatchMmaStaged = 11,
+  kPhBatchAttention = 12,
 };
 
 }  // namespace nh

@@ -5,6 +5,7 @@
     python -m nuthatch_b200.phase_trace prefill     # tcgen05 products of a 1024-token prefill
     python -m nuthatch_b200.phase_trace streaming   # two-phase streaming decode, budget 32
     python -m nuthatch_b200.phase_trace batched     # mma.sync grouped products of a bs64 decode step
+    python -m nuthatch_b200.phase_trace battention  # batched decode attention at 2048-token contexts
 
 The diagnostic library records, per CTA of the stamped kernels, %globaltimer
 stamps at fixed points (kernel entry, after griddepcontrol.wait, after the
@@ -31,7 +32,7 @@ RING = 1 << 20  # records (kPhaseTraceCap); 128 bytes each
 class Ring:
     """The device ring and its counter, registered with every stamped unit."""
 
-    def __init__(self):
+    def __init__(self, units=UNITS):
         import torch
 
         from ._lib import lib
@@ -40,7 +41,7 @@ class Ring:
         self.buf = torch.zeros(RING * 16, dtype=torch.int64, device="cuda")
         self.count = torch.zeros(1, dtype=torch.int32, device="cuda")
         L = lib()
-        for unit in UNITS:
+        for unit in units:
             fn = getattr(L, f"nh_phase_trace_set_{unit}")
             fn.argtypes = [C.c_void_p, C.c_void_p]
             fn.restype = None
@@ -254,8 +255,45 @@ def batched(args):
         print(line)
 
 
+def battention(args):
+    """4 sequences with 2048-token contexts, 2 decode steps: per launch of the
+    batched attention kernel (one (head, 64-position split, sequence) per CTA)
+    the span, and per CTA the time from its wait to the staged K/V rows, the
+    scores and softmax, the V sums and partials, the ticket, and (for the last
+    CTA of a (head, sequence)) the split combination."""
+    import torch
+
+    from . import OlmoeModel, generate_batch_ex, synth
+
+    torch.cuda.set_device(0)
+    ring = Ring(units=("batch",))  # the batched kernels only
+    m = OlmoeModel.Load(str(synth.cached(synth.OLMOE_1B7B)))
+    prompts = np.random.default_rng(3).integers(0, m.config().n_vocab, (4, 2048)).tolist()
+    generate_batch_ex(m, [p[:64] for p in prompts], 2, False)
+    ring.reset()
+    r = generate_batch_ex(m, prompts, 2, False)
+    kid, t = ring.records()
+    s = kid == 12
+    t = t[s]
+    # Decode steps only: the last two steps x 16 layers of launches.
+    gaps = np.where(np.diff(t[:, 0]) > 20_000)[0]
+    starts = [0] + (gaps + 1).tolist()
+    ls = [t[a:b] for a, b in zip(starts, starts[1:] + [len(t)])][-32:]
+    span = [(x[:, 9].max() - x[:, 0].min()) / 1e3 for x in ls]
+    cat = np.concatenate(ls)
+    ph = lambda a, b: np.median((cat[:, b] - cat[:, a])[(cat[:, a] > 0) & (cat[:, b] > 0)]) / 1e3
+    last = cat[cat[:, 7] == 1]
+    print(json.dumps({"workload": "olmoe-1b7b batched decode, 4 x 2048 contexts, 2 steps",
+                      "decode_ms": r["decode_ms"], "launches": len(ls), "ctas_per_launch": int(np.median([len(x) for x in ls]))}))
+    print(f"launch span median {np.median(span):.1f} us; per CTA (median): entry->wait {ph(0, 1):.2f}, "
+          f"wait->K/V staged {ph(1, 2):.2f}, scores+softmax {ph(2, 3):.2f}, V sums+partials {ph(3, 4):.2f}, "
+          f"ticket {ph(4, 5):.2f}, non-last end {ph(5, 9):.2f} us; combine (last CTAs) "
+          f"{np.median((last[:, 9] - last[:, 5]) / 1e3) if len(last) else 0:.2f} us; CTA life {ph(0, 9):.2f} us")
+
+
 def main() -> None:
-    modes = {"decode": decode, "prefill": prefill, "streaming": streaming, "batched": batched}
+    modes = {"decode": decode, "prefill": prefill, "streaming": streaming, "batched": batched,
+             "battention": battention}
     mode = sys.argv[1] if len(sys.argv) > 1 else "decode"
     if mode not in modes:
         raise SystemExit(f"usage: python -m nuthatch_b200.phase_trace [{'|'.join(modes)}]")
