@@ -518,6 +518,9 @@ def run_ep_batched(args, dist, rank: int, world: int, local_rank: int, path: str
                (8 * 64 * 3538944 + 8 * 64 * 4079616) // world)
     peaks = measured_peaks()
     achieved = (kv + weights) / (ms / 1000.0 / n_pred) / 1e9
+    coll = ep_collective_times(dist, world, per, cfg) if dist is not None else None
+    if coll is not None:
+        coll["share_of_step"] = coll["per_step_ms"] / (ms / n_pred)
     return {"metric": f"OLMoE Q4_K_M expert-parallel batched decode tok/s (bs{B}, {ctx}-token contexts)",
             "value": value, "unit": "tok/s", "n_gpus": world, "ms_per_step": ms / n_pred,
             "experts_per_gpu": count, "sequences_per_gpu": per, "steps": n_pred,
@@ -526,7 +529,44 @@ def run_ep_batched(args, dist, rank: int, world: int, local_rank: int, path: str
             "clocks": clk,
             "step_roofline_per_gpu": {"bytes_per_step": kv + weights, "achieved": achieved, "peak": peaks["hbm_gbs"],
                                       "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"]},
-            "subset_matches_single_gpu": subset_ok}
+            "subset_matches_single_gpu": subset_ok, "collective_times": coll}
+
+
+def ep_collective_times(dist, world: int, per: int, cfg) -> dict:
+    """The two exchanges of one expert-parallel MoE layer at the decode's
+    sizes, timed alone with torch's NCCL process group (CUDA events, 20
+    repetitions after 3, max over ranks): the all-gather of every rank's
+    Q8_K rows (2432 bytes per token at n_embd 2048) and the all-to-all of
+    pick rows ([per][k][n_embd] f32 per rank pair).  The library issues the
+    same two collectives from its own NCCL communicator inside the step."""
+    import torch
+
+    q8_row = (cfg.n_embd // 256) * 304
+    ag_src = torch.zeros(per * q8_row, dtype=torch.uint8, device="cuda")
+    ag_dst = torch.zeros(world * per * q8_row, dtype=torch.uint8, device="cuda")
+    blk = per * cfg.n_expert_used * cfg.n_embd
+    a2a_src = torch.zeros(world * blk, dtype=torch.float32, device="cuda")
+    a2a_dst = torch.zeros(world * blk, dtype=torch.float32, device="cuda")
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(20):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return max_over_ranks(e0.elapsed_time(e1) * 1000.0 / 20, dist)
+
+    ag = timed(lambda: dist.all_gather_into_tensor(ag_dst, ag_src))
+    a2a = timed(lambda: dist.all_to_all_single(a2a_dst, a2a_src))
+    per_layer = ag + a2a
+    return {"all_gather_us": ag, "all_to_all_us": a2a, "per_layer_us": per_layer,
+            "per_step_ms": per_layer * cfg.n_layers / 1000.0,
+            "limiting": "all_to_all of pick rows" if a2a >= ag else "all_gather of Q8_K rows",
+            "bytes": {"all_gather_per_rank": per * q8_row, "all_to_all_per_rank_pair": blk * 4}}
 
 
 def main() -> None:
