@@ -43,6 +43,15 @@ def test_library_exports_every_declared_symbol(header):
     assert not missing, missing
 
 
+def test_product_library_has_no_phase_trace_hooks():
+    """The per-CTA phase timestamps exist only in the diagnostic build
+    (python -m nuthatch_b200.build --phase-trace); the product library's
+    kernels record nothing and export no ring setters."""
+    so = C.CDLL(str(LIB_PATH))
+    units = ("gemv", "attention", "moe", "misc", "grouped_tc", "batch")
+    assert not any(hasattr(so, f"nh_phase_trace_set_{u}") for u in units)
+
+
 def _trace(name):
     L, E, recs = traces()[name]
     return nh.RoutingTrace(L, E, [nh.RoutingRecord(t, l, ex) for t, l, ex in recs])
