@@ -416,58 +416,116 @@ def run_prefill(args) -> None:
 
 
 def run_granite(args) -> None:
-    """Configuration 5 on one GPU: a Granite-3-MoE-shaped seeded GGUF (24
-    layers, n_embd 1024, GQA 16/8 x 64, 32 experts top-8, FFN 512), batched
-    streaming decode of 32 sequences with 1024-token seeded contexts and 256
-    greedy steps, every layer's experts streamed through a slot pool of 8
-    (LRU, and learned pin calibrated on a resident trace of another prompt).
-    A step's batch selects more distinct experts than the pool holds, so each
-    layer runs in waves.  Device-timed decode part; value = sequences x ids /
-    time.  Parity: two sequences against the resident batched decode of a
-    shorter run of the same prompts."""
+    """Configuration 5: a Granite-3-MoE-shaped seeded GGUF (24 layers, n_embd
+    1024, GQA 16/8 x 64, 32 experts top-8, FFN 512), batched streaming decode
+    of 32 sequences with 1024-token seeded contexts and 256 greedy steps,
+    every layer's experts streamed through a slot budget of 8 per layer for
+    the whole job (LRU, and learned pin calibrated on a resident trace of
+    another prompt).  A step's batch selects more distinct experts than the
+    pool holds, so each layer runs in waves.  Under torchrun (N ranks, one GPU
+    each) the budget is split 8/N slots per GPU, each GPU streaming only its
+    32/N experts (expert parallelism: NCCL all-gather of the tokens' rows and
+    selections, all-to-all of the pick rows) and decoding 32/N sequences: the
+    total work and budget are fixed, so scaling is strong.  Device-timed
+    decode part, max over ranks; value = sequences x ids / time.  Parity:
+    each rank's first two sequences against the resident batched decode of a
+    shorter run of the same prompts (through the same expert group)."""
+    import datetime
+
     import torch
 
     import nuthatch_b200 as nh
     from nuthatch_b200 import build, synth
+    from nuthatch_b200._lib import lib
 
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local_rank))
     build.build_product()
-    torch.cuda.set_device(0)
+    assert lib().nh_set_device(local_rank) == 0
+    if rank == 0:
+        synth.cached(synth.GRANITE_MOE)
+    if dist is not None:
+        dist.barrier()
     path = str(synth.cached(synth.GRANITE_MOE))
     B, ctx, n_pred, budget = args.granite_seqs, args.granite_context, args.granite_steps, args.granite_budget
     m = nh.OlmoeModel.Load(path)
     cfg = m.config()
+    if B % world != 0 or cfg.n_expert % world != 0 or budget % world != 0:
+        if rank == 0:
+            print(json.dumps({"workload": "granite", "unavailable": f"{B} sequences / {cfg.n_expert} experts / "
+                                                                    f"budget {budget} do not split over {world} GPUs"}))
+        if dist is not None:
+            dist.destroy_process_group()
+        return
+    cap = budget // world
+    per = B // world
     prompts = np.random.default_rng(5).integers(0, cfg.n_vocab, (B, ctx)).tolist()
+    mine = prompts[rank * per:(rank + 1) * per]
     cal = nh.RoutingTrace()
     nh.GreedyGenerateCachedTrace(m, np.random.default_rng(6).integers(0, cfg.n_vocab, 64).tolist(), 64, False, cal)
     usage = nh.BuildUsage(cal, cfg.n_expert).counts
-    check = nh.generate_batch_ex(m, prompts[:2], 8, False)["tokens"]
+    check = nh.generate_batch_ex(m, mine[:2], 8, False)["tokens"]
     m.close()
+    ep = None
+    if world > 1:
+        box = [nh.ExpertGroup.new_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        ep = nh.ExpertGroup(box[0], world, rank)
+
+    def job_sum(v: float) -> float:
+        if dist is None:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t)
+        return float(t.item())
+
     sm = nh.StreamingModel.Load(path)
     rows = {}
     for policy in ("lru", "learned_pin"):
-        kw = dict(policy="learned_pin", pin_slots=(budget * 3 + 3) // 4, usage=usage) if policy == "learned_pin" \
-            else {}
-        ok = nh.streaming_generate_batch_ex(sm, prompts[:2], 8, False, budget, **kw)["tokens"] == check
-        clocks = ClockSampler(0)
-        r = nh.streaming_generate_batch_ex(sm, prompts, n_pred, False, budget, **kw)
+        # Learned pin keeps at least one LRU slot per GPU for the waves.
+        pin = min((cap * 3 + 3) // 4, cap - 1)
+        if policy == "learned_pin" and pin < 1:
+            rows[policy] = {"unavailable": f"{cap} slot per GPU leaves no LRU slot beside a pinned one"}
+            continue
+        kw = dict(policy="learned_pin", pin_slots=pin, usage=usage) if policy == "learned_pin" else {}
+        ok = nh.streaming_generate_batch_ex(sm, mine[:2], 8, False, cap, ep=ep, **kw)["tokens"] == check
+        clocks = ClockSampler(local_rank)
+        r = nh.streaming_generate_batch_ex(sm, mine, n_pred, False, cap, ep=ep, **kw)
         clk = clocks.stop()
-        acc = int((r["hits"] + r["misses"]).sum())
-        rows[policy] = {"tok_s": B * n_pred / (r["decode_ms"] / 1000.0), "decode_ms": r["decode_ms"],
-                        "hit_rate": int(r["hits"].sum()) / max(acc, 1), "waves": r["waves"],
-                        "h2d_gb": r["h2d_bytes"] / 1e9, "subset_matches_resident": ok, "clocks": clk}
+        ms = max_over_ranks(r["decode_ms"], dist)
+        hits, acc = job_sum(int(r["hits"].sum())), job_sum(int((r["hits"] + r["misses"]).sum()))
+        rows[policy] = {"tok_s": B * n_pred / (ms / 1000.0), "decode_ms": ms, "hit_rate": hits / max(acc, 1),
+                        "waves_per_gpu": job_sum(r["waves"]) / world, "h2d_gb": job_sum(r["h2d_bytes"]) / 1e9,
+                        "slots_per_gpu": cap, "pinned_per_gpu": pin if policy == "learned_pin" else 0,
+                        "subset_matches_resident": job_sum(0.0 if ok else 1.0) == 0.0, "clocks": clk}
     sm.close()
-    line = {"metric": f"Granite-shaped Q4_K_M batched streaming decode tok/s (bs{B}, {ctx}-token contexts, "
-                      f"budget {budget} of {cfg.n_expert})",
-            "value": rows["lru"]["tok_s"], "unit": "tok/s", "n_gpus": 1, "steps": n_pred, "warmup": 1,
-            "ms_per_step": rows["lru"]["decode_ms"] / n_pred, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "q4k/q6k x q8k int dot, f32 accumulate, f32 KV",
-            "data": "synthetic (seeded random-init Granite-3-MoE-shaped GGUF, seeded random-id contexts)",
-            "config": {"workload": f"granite-shape-batched-streaming (bs{B}, context {ctx}, {n_pred} greedy steps, "
-                                   f"slot budget {budget})", "parallelism": "single GPU",
-                       "experts": "pinned host store -> HBM slot pool per layer, waves when the batch's distinct "
-                                  "experts exceed the pool"},
-            "policies": rows}
-    print(json.dumps(line), flush=True)
+    if ep is not None:
+        ep.close()
+    if rank == 0:
+        line = {"metric": f"Granite-shaped Q4_K_M batched streaming decode tok/s (bs{B}, {ctx}-token contexts, "
+                          f"budget {budget} of {cfg.n_expert})",
+                "value": rows["lru"]["tok_s"], "unit": "tok/s", "n_gpus": world, "steps": n_pred, "warmup": 1,
+                "ms_per_step": rows["lru"]["decode_ms"] / n_pred, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "q4k/q6k x q8k int dot, f32 accumulate, f32 KV",
+                "data": "synthetic (seeded random-init Granite-3-MoE-shaped GGUF, seeded random-id contexts)",
+                "config": {"workload": f"granite-shape-batched-streaming (bs{B}, context {ctx}, {n_pred} greedy "
+                                       f"steps, slot budget {budget} per layer for the job)",
+                           "parallelism": f"ep{world} ({cfg.n_expert // world} experts and {cap} slots per layer "
+                                          f"per GPU, {per} sequences per GPU)" if world > 1 else "single GPU",
+                           "experts": "pinned host store -> HBM slot pool per layer, waves when the batch's "
+                                      "distinct experts exceed the pool"},
+                "policies": rows}
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
 
 
 def run_ep_batched(args, dist, rank: int, world: int, local_rank: int, path: str, full_model) -> dict | None:

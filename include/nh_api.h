@@ -140,6 +140,17 @@ int nh_stream_generate_batch(void* model, const int32_t* prompts, int n_seq, int
                              int32_t* out_tokens, int64_t* hits, int64_t* misses, uint64_t* h2d_bytes, int64_t* waves,
                              double* decode_ms);
 
+/* nh_stream_generate_batch with expert parallelism (ep from nh_ep_create, or
+ * NULL for one GPU): every rank calls it at once with its own n_seq prompts
+ * (the same n_seq, n_prompt and n_predict everywhere); each rank streams only
+ * its expert shard (n_expert / world experts) through `capacity` slots per
+ * layer, learned pin choosing among those experts.  hits, misses, h2d_bytes
+ * and waves are this rank's. */
+int nh_stream_generate_batch_ep(void* model, const void* ep, const int32_t* prompts, int n_seq, int n_prompt,
+                                int n_predict, int norm_topk, int capacity, int policy, int pin_slots,
+                                const uint64_t* usage, int32_t* out_tokens, int64_t* hits, int64_t* misses,
+                                uint64_t* h2d_bytes, int64_t* waves, double* decode_ms);
+
 /* Cache policies over a flat trace: record r has layer[r] and experts
  * experts[offsets[r]..offsets[r+1]).  kind 0 LruPolicy(n_layers, a)
  * (lru_policy.cc), 1 OsPageCachePolicy(a) (os_page_cache_policy.cc), 2

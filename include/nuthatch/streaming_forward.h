@@ -58,8 +58,14 @@ std::vector<int32_t> StreamingGenerateEx(const StreamingModel& model, const std:
 // combine follows the last wave.  Every sequence's ids equal the resident
 // batched decode.  Hits and misses count per Ensure of each wave (the
 // reference defines none for this case).  opt.trace is not filled; bopt gives
-// the decode device time (its ep must be null; the host decides every
-// layer's slots, so no CUDA graph is used).
+// the decode device time (the host decides every layer's slots, so no CUDA
+// graph is used).  With bopt->ep set, every rank of the group calls this at
+// once with its own sequences (the same count and lengths everywhere): each
+// rank streams only its expert shard (E/N experts) through its own
+// `capacity` slots per layer, learned pin choosing among those experts, and
+// serves every rank's picks of them; tokens and selections are all-gathered
+// and pick rows return by all-to-all as in GreedyGenerateCachedBatch, so the
+// ids equal the single-GPU batch.  Hits, misses and waves are this rank's.
 std::vector<std::vector<int32_t>> StreamingGenerateBatch(const StreamingModel& model,
                                                          const std::vector<std::vector<int32_t>>& prompts,
                                                          int n_predict, bool norm_topk, int capacity,

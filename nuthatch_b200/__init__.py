@@ -319,10 +319,12 @@ def streaming_generate_ex(model: StreamingModel, ids: Sequence[int], n_predict: 
 
 def streaming_generate_batch_ex(model: StreamingModel, prompts: Sequence[Sequence[int]], n_predict: int,
                                 norm_topk: bool, capacity: int, *, policy: str = "lru", pin_slots: int = 0,
-                                usage: np.ndarray | None = None) -> dict:
+                                usage: np.ndarray | None = None, ep: Optional[ExpertGroup] = None) -> dict:
     """Batched streaming decode (StreamingGenerateBatch): ids per sequence,
     per-layer hits/misses (one count per wave's Ensure), H2D bytes, the number
-    of slot-pool waves and the decode device time."""
+    of slot-pool waves and the decode device time.  With ep, every rank
+    passes its own sequences at the same time and streams only its expert
+    shard through `capacity` slots per layer; the counts are this rank's."""
     cfg = model.config()
     p = np.ascontiguousarray(np.asarray(prompts, dtype=np.int32))
     if p.ndim != 2:
@@ -335,11 +337,12 @@ def streaming_generate_batch_ex(model: StreamingModel, prompts: Sequence[Sequenc
     u = None
     if policy == "learned_pin":
         u = np.ascontiguousarray(np.asarray(usage, dtype=np.uint64).reshape(cfg.n_layers, cfg.n_expert))
-    _check(lib().nh_stream_generate_batch(model._h, _ptr(p, C.c_int32), n_seq, n_prompt, n_predict, int(norm_topk),
-                                          capacity, 1 if policy == "learned_pin" else 0, pin_slots,
-                                          _ptr(u, C.c_uint64), _ptr(toks, C.c_int32), _ptr(hits, C.c_int64),
-                                          _ptr(misses, C.c_int64), C.byref(h2d), C.byref(waves), C.byref(ms)),
-           "nh_stream_generate_batch")
+    _check(lib().nh_stream_generate_batch_ep(model._h, None if ep is None else ep._h, _ptr(p, C.c_int32), n_seq,
+                                             n_prompt, n_predict, int(norm_topk), capacity,
+                                             1 if policy == "learned_pin" else 0, pin_slots, _ptr(u, C.c_uint64),
+                                             _ptr(toks, C.c_int32), _ptr(hits, C.c_int64), _ptr(misses, C.c_int64),
+                                             C.byref(h2d), C.byref(waves), C.byref(ms)),
+           "nh_stream_generate_batch_ep")
     return {"tokens": toks.tolist(), "hits": hits, "misses": misses, "h2d_bytes": h2d.value, "waves": waves.value,
             "decode_ms": ms.value}
 

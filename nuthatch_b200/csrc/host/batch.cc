@@ -123,18 +123,19 @@ int CheckPrompts(const std::vector<std::vector<int32_t>>& prompts, const OlmoeCo
 }
 
 // Experts streamed through per-layer slot pools (the batched streaming form):
-// the caches, the stream their fills run on, and the wave statistics.
+// the caches, the stream their fills run on, the experts this GPU serves
+// (all of them, or its expert-parallel shard) and the wave statistics.
 struct StreamedExperts {
   std::vector<ExpertSlotCache*> caches;
   cudaStream_t copy_stream = nullptr;
+  ExpertShard shard;
   int64_t waves = 0;      // out: slot-pool waves over all layers and steps
   double host_ms = 0;     // out: host time spent in slot decisions and waits
 };
 
-int StreamedMoe(StreamedExperts& se, int l, const LayerView& Lv, const OlmoeConfig& c, int B, const int32_t* sel,
-                const float* wts, int32_t* sel_host, int32_t* plan_host, int32_t* off, int32_t* cnt,
-                int32_t* act_idx, int32_t* out_idx, const uint8_t* q8, float* ff, uint8_t* q8ff, float* y, float* h,
-                cudaEvent_t compute_done, cudaStream_t s);
+int StreamedMoe(StreamedExperts& se, int l, const OlmoeConfig& c, int B, const int32_t* sel, int32_t* sel_host,
+                int32_t* plan_host, int32_t* off, int32_t* cnt, int32_t* act_idx, int32_t* out_idx,
+                const uint8_t* q8, float* ff, uint8_t* q8ff, float* y, cudaEvent_t compute_done, cudaStream_t s);
 
 // The batched decode shared by the resident (and expert-parallel) form and the
 // streaming form: `se` null means the experts are resident in `m` (offset by
@@ -196,8 +197,8 @@ std::vector<std::vector<int32_t>> RunBatch(const ModelView& m, const OlmoeConfig
   int32_t* sel_host = nullptr;
   int32_t* plan_host = nullptr;
   if (se != nullptr) {
-    sel_host = bb.HostAlloc<int32_t>(RK);
-    plan_host = bb.HostAlloc<int32_t>(static_cast<size_t>(E) * (2 * E + 2 * RK));
+    sel_host = bb.HostAlloc<int32_t>(RKW);
+    plan_host = bb.HostAlloc<int32_t>(static_cast<size_t>(E) * (2 * E + 2 * RKW));
     if (cudaEventCreateWithFlags(&bb.event_, cudaEventDisableTiming) != cudaSuccess) bb.ok_ = false;
     o.use_graph = false;  // the host decides every layer's slots
   }
@@ -264,10 +265,19 @@ std::vector<std::vector<int32_t>> RunBatch(const ModelView& m, const OlmoeConfig
     NH_B_TRY(nh_batch_prep(h, d, r, Lv.ffn_norm, eps, 1, d, q8, xn, s));
     NH_B_TRY(nh_batch_router(xn, Lv.router, r, d, static_cast<int>(E), static_cast<int>(K), norm_topk ? 1 : 0, sel,
                              wts, s));
-    if (se != nullptr)
-      return StreamedMoe(*se, l, Lv, c, r, sel, wts, sel_host, plan_host, off, cnt, act_idx, out_idx, q8, ff, q8ff, y,
-                         h, bb.event_, s);
     if (W > 1) NH_B_TRY(ExchangeTokens(*ep, q8, q8_row * r, q8_all, sel, rk, sel_all, s));
+    if (se != nullptr) {
+      // The served experts stream through this GPU's pools in waves; the
+      // pick rows then take the same return and combine as the resident form.
+      NH_B_TRY(StreamedMoe(*se, l, c, r * W, sel_all, sel_host, plan_host, off, cnt, act_idx, out_idx, q8_all, ff,
+                           q8ff, y, bb.event_, s));
+      if (W > 1) {
+        NH_B_TRY(ReturnPicks(*ep, y, static_cast<size_t>(rk) * d, y_recv, s));
+        return nh_ep_combine(y_recv, static_cast<int64_t>(rk) * d, W, sel, wts, r, static_cast<int>(K), d,
+                             static_cast<int>(shard.count), h, s);
+      }
+      return nh_batch_combine(y, wts, r, static_cast<int>(K), d, h, s);
+    }
     // The owned experts over every rank's rows: row j of the gathered rows
     // is rank j / r's row j % r.
     NH_B_TRY(nh_batch_moe_plan_range(sel_all, r * W, static_cast<int>(K), static_cast<int>(shard.first),
@@ -431,23 +441,24 @@ std::vector<std::vector<int32_t>> RunBatch(const ModelView& m, const OlmoeConfig
   return out;
 }
 
-// One MoE layer of the batched streaming form.  The router's selections are
-// read back and the batch's distinct unpinned experts are split, in order of
-// first selection, into waves of at most lru_slots (pinned experts, always
-// resident, join the first wave): each wave's experts are made resident with
-// one Ensure (which then never evicts an expert of the same wave), the
-// grouped gate/up and down products run over the slot pool for that wave's
-// (token, pick) pairs, and the next wave's fills wait for those products.
-// After the last wave every pick row is in y and the combine adds them in
-// top-k order, so each token's arithmetic equals the resident batch's.
-int StreamedMoe(StreamedExperts& se, int l, const LayerView& Lv, const OlmoeConfig& c, int B, const int32_t* sel,
-                const float* wts, int32_t* sel_host, int32_t* plan_host, int32_t* off, int32_t* cnt,
-                int32_t* act_idx, int32_t* out_idx, const uint8_t* q8, float* ff, uint8_t* q8ff, float* y, float* h,
-                cudaEvent_t compute_done, cudaStream_t s) {
-  (void)Lv;
+// The expert products of one MoE layer in the batched streaming form, over
+// B token rows (every rank's rows under expert parallelism).  The selections
+// are read back and the distinct unpinned experts this GPU serves are split,
+// in order of first selection, into waves of at most lru_slots (pinned
+// experts, always resident, join the first wave): each wave's experts are
+// made resident with one Ensure (which then never evicts an expert of the same
+// wave), the grouped gate/up and down products run over the slot pool for
+// that wave's (token, pick) pairs, and the next wave's fills wait for those
+// products.  After the last wave row j of y holds pick j's expert output for
+// every pick of a served expert; the caller's combine adds them in top-k
+// order, so each token's arithmetic equals the resident batch's.
+int StreamedMoe(StreamedExperts& se, int l, const OlmoeConfig& c, int B, const int32_t* sel, int32_t* sel_host,
+                int32_t* plan_host, int32_t* off, int32_t* cnt, int32_t* act_idx, int32_t* out_idx,
+                const uint8_t* q8, float* ff, uint8_t* q8ff, float* y, cudaEvent_t compute_done, cudaStream_t s) {
   ExpertSlotCache& cache = *se.caches[l];
   const int K = static_cast<int>(c.n_expert_used), E = static_cast<int>(c.n_expert), BK = B * K;
   const int64_t d = c.n_embd, F = c.n_ff;
+  const int e_lo = static_cast<int>(se.shard.first), e_hi = e_lo + static_cast<int>(se.shard.count);
   const auto t0 = std::chrono::steady_clock::now();
   if (cudaMemcpyAsync(sel_host, sel, static_cast<size_t>(BK) * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
       cudaStreamSynchronize(s) != cudaSuccess)
@@ -458,7 +469,7 @@ int StreamedMoe(StreamedExperts& se, int l, const LayerView& Lv, const OlmoeConf
   for (int j = 0; j < BK; ++j) {
     const int e = sel_host[j];
     if (e < 0 || e >= E) return NH_E_STATE;
-    if (cache.is_pinned(e) || wave_of[e] >= 0) continue;
+    if (e < e_lo || e >= e_hi || cache.is_pinned(e) || wave_of[e] >= 0) continue;
     if (per <= 0) return NH_E_CAPACITY;
     if (waves.empty() || static_cast<int>(waves.back().size()) == per) waves.emplace_back();
     waves.back().push_back(e);
@@ -561,7 +572,7 @@ int StreamedMoe(StreamedExperts& se, int l, const LayerView& Lv, const OlmoeConf
   }
   se.waves += static_cast<int64_t>(waves.size());
   se.host_ms += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
-  return nh_batch_combine(y, wts, B, K, d, h, s);
+  return NH_OK;
 }
 
 }  // namespace
@@ -615,7 +626,12 @@ std::vector<std::vector<int32_t>> StreamingGenerateBatch(const StreamingModel& m
   const OlmoeConfig& c = model.config();
   StreamingModel::Workspace* ws = model.workspace();
   o.status = ws == nullptr || !ws->view_ok ? NH_E_STATE : capacity <= 0 ? NH_E_ARG : CheckPrompts(prompts, c);
-  if (o.ep != nullptr) o.status = NH_E_ARG;  // experts stream through one GPU's pool here
+  // Expert parallelism: this GPU streams only its shard's experts through its
+  // own `capacity` slots per layer and serves every rank's picks of them.
+  const ExpertGroup* ep = o.ep;
+  const int W = ep != nullptr ? ep->world() : 1;
+  const ExpertShard shard = ep != nullptr ? ExpertShard::Of(c.n_expert, W, ep->rank()) : ExpertShard{0, c.n_expert};
+  if (ep != nullptr && (c.n_expert % W != 0 || !Nccl().ok)) o.status = NH_E_ARG;
   if (o.status != NH_OK) {
     stats.status = o.status;
     return {};
@@ -624,12 +640,23 @@ std::vector<std::vector<int32_t>> StreamingGenerateBatch(const StreamingModel& m
   std::vector<std::unique_ptr<ExpertSlotCache>> owned;
   StreamedExperts se;
   se.copy_stream = ws->copy_stream;
+  se.shard = shard;
   const uint32_t pin_slots =
       opt.pin_slots > 0 ? opt.pin_slots : LearnedPinSlots(static_cast<uint32_t>(capacity));
+  // Learned pin chooses among the served experts only.
+  UsageHistogram shard_usage;
+  const UsageHistogram* usage = opt.usage;
+  if (usage != nullptr && W > 1) {
+    shard_usage.per_layer.resize(usage->per_layer.size());
+    for (size_t l = 0; l < usage->per_layer.size(); ++l)
+      for (const auto& kv : usage->per_layer[l])
+        if (kv.first >= shard.first && kv.first < shard.first + shard.count) shard_usage.per_layer[l].insert(kv);
+    usage = &shard_usage;
+  }
   for (int l = 0; l < L; ++l) {
     SlotCacheOptions so;
     so.policy = opt.policy;
-    so.usage = opt.usage;
+    so.usage = usage;
     so.pin_slots = std::min<uint32_t>(pin_slots, static_cast<uint32_t>(capacity));
     so.copy_stream = ws->copy_stream;
     owned.push_back(ExpertSlotCache::Create(c, l, capacity, model.reader(), model.host_store(l), so));
@@ -639,7 +666,7 @@ std::vector<std::vector<int32_t>> StreamingGenerateBatch(const StreamingModel& m
     }
     se.caches.push_back(owned.back().get());
   }
-  auto out = RunBatch(ws->view, c, prompts, n_predict, norm_topk, o, ExpertShard{0, c.n_expert}, 0, &se);
+  auto out = RunBatch(ws->view, c, prompts, n_predict, norm_topk, o, shard, 0, &se);
   cudaStreamSynchronize(ws->copy_stream);
   stats.hits.assign(L, 0);
   stats.misses.assign(L, 0);

@@ -329,10 +329,10 @@ int nh_stream_generate(void* model, const int32_t* prompt, int n_prompt, int n_p
   return NH_OK;
 }
 
-int nh_stream_generate_batch(void* model, const int32_t* prompts, int n_seq, int n_prompt, int n_predict,
-                             int norm_topk, int capacity, int policy, int pin_slots, const uint64_t* usage,
-                             int32_t* out_tokens, int64_t* hits, int64_t* misses, uint64_t* h2d_bytes, int64_t* waves,
-                             double* decode_ms) {
+int nh_stream_generate_batch_ep(void* model, const void* ep, const int32_t* prompts, int n_seq, int n_prompt,
+                                int n_predict, int norm_topk, int capacity, int policy, int pin_slots,
+                                const uint64_t* usage, int32_t* out_tokens, int64_t* hits, int64_t* misses,
+                                uint64_t* h2d_bytes, int64_t* waves, double* decode_ms) {
   if (model == nullptr || prompts == nullptr || out_tokens == nullptr || n_seq <= 0 || n_prompt <= 0 ||
       n_predict <= 0 || (policy == 1 && usage == nullptr)) {
     SetErr("nh_stream_generate_batch: bad argument");
@@ -354,6 +354,7 @@ int nh_stream_generate_batch(void* model, const int32_t* prompts, int n_seq, int
     o.pin_slots = pin_slots > 0 ? static_cast<uint32_t>(pin_slots) : 0;
   }
   BatchOptions bo;
+  bo.ep = static_cast<const ExpertGroup*>(ep);
   const auto ids = StreamingGenerateBatch(m, p, n_predict, norm_topk != 0, capacity, o, &bo);
   if (st.status != NH_OK) {
     SetErr("StreamingGenerateBatch failed with code " + std::to_string(st.status));
@@ -369,6 +370,14 @@ int nh_stream_generate_batch(void* model, const int32_t* prompts, int n_seq, int
   if (waves != nullptr) *waves = st.waves;
   if (decode_ms != nullptr) *decode_ms = bo.decode_ms;
   return NH_OK;
+}
+
+int nh_stream_generate_batch(void* model, const int32_t* prompts, int n_seq, int n_prompt, int n_predict,
+                             int norm_topk, int capacity, int policy, int pin_slots, const uint64_t* usage,
+                             int32_t* out_tokens, int64_t* hits, int64_t* misses, uint64_t* h2d_bytes, int64_t* waves,
+                             double* decode_ms) {
+  return nh_stream_generate_batch_ep(model, nullptr, prompts, n_seq, n_prompt, n_predict, norm_topk, capacity, policy,
+                                     pin_slots, usage, out_tokens, hits, misses, h2d_bytes, waves, decode_ms);
 }
 
 int64_t nh_replay(int kind, uint32_t n_layers, uint32_t n_expert, int64_t n_records, const uint32_t* layer,
