@@ -141,6 +141,19 @@ def test_oracle_causality(tiny):
     assert not np.array_equal(l0[3], l1[3])
 
 
+def test_oracle_full_forward_last_row_equals_cached_step(tiny, mini):
+    """The top-5 tool's logits (one cached step after a one-pass prompt) are
+    the last row of the full-sequence forward (olmoe_forward_main.cc:39-52),
+    bit for bit, with and without norm_topk."""
+    for path in (tiny, str(mini)):
+        om = oracle.OracleModel(path)
+        for toks in ([3, 7, 1, 4], [5], [1, 2, 3, 4, 5, 6, 7, 8, 9]):
+            for nt in (False, True):
+                full = om.forward(toks, norm_topk=nt)[-1]
+                step = om.generate(toks, 1, norm_topk=nt, mode=0, logits=True)["logits"][0]
+                assert np.array_equal(full, step)
+
+
 def test_oracle_thread_count_does_not_change_results(mini):
     om = oracle.OracleModel(str(mini))
     outs = []

@@ -227,6 +227,23 @@ def test_mini_gqa_and_all_experts(gpu, synth_dir):
     assert_matches(g["hidden"], ora["hidden"])
 
 
+def test_top5_tool_matches_oracle_full_forward(gpu, mini_models, mini_path, capsys):
+    """olmoe_forward (olmoe_forward_main.cc:17-65): the last position's logits
+    equal the oracle's full-sequence forward bit for bit, and the printed top 5
+    are its five largest."""
+    from nuthatch_b200 import olmoe_forward
+
+    m, om = mini_models
+    toks = np.random.default_rng(21).integers(0, 1000, 9).tolist()
+    full = om.forward(toks)[-1]
+    assert np.array_equal(olmoe_forward.last_logits(m, toks), full)
+    best = olmoe_forward.top_k(full)
+    assert olmoe_forward.main(["olmoe_forward", str(mini_path)] + [str(t) for t in toks]) == 0
+    out = capsys.readouterr().out.splitlines()
+    assert out[0].startswith("loaded: layers=2 ") and out[1] == "top-5 next-token logits (after pos 8):"
+    assert out[2:] == [f"  tok {i:<6d} logit {v:.4f}" for i, v in best]
+
+
 def test_long_context_split_attention(gpu, mini_models):
     # A prompt longer than one attention split (256 positions) exercises the
     # multi-CTA softmax combine.

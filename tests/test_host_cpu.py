@@ -273,3 +273,14 @@ def test_calibrated_sweep_persists_through_trace_files(tmp_path):
         pin = int(math.ceil(0.75 * b))
         want = nh.Replay(ev, nh.LearnedPinPolicy(L, pin, b - pin, nh.BuildUsage(back, E))).hit_rate()
         assert learned == pytest.approx(want, abs=0)
+
+
+def test_top5_tool_usage_and_tie_order(capsys):
+    """olmoe_forward (olmoe_forward_main.cc:17-65): usage on too few
+    arguments; the top 5 ordered by logit, ties to the lower id."""
+    from nuthatch_b200 import olmoe_forward
+
+    assert olmoe_forward.main(["olmoe_forward", "model.gguf"]) == 1
+    assert "usage:" in capsys.readouterr().err
+    lg = np.array([0.5, 2.0, 2.0, -1.0, 3.0, 0.5, 2.0], dtype=np.float32)
+    assert olmoe_forward.top_k(lg) == [(4, 3.0), (1, 2.0), (2, 2.0), (6, 2.0), (0, 0.5)]
