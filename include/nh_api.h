@@ -151,6 +151,24 @@ int nh_stream_generate_batch_ep(void* model, const void* ep, const int32_t* prom
                                 const uint64_t* usage, int32_t* out_tokens, int64_t* hits, int64_t* misses,
                                 uint64_t* h2d_bytes, int64_t* waves, double* decode_ms);
 
+/* The slot-pool waves of one layer of the batched streaming form (host only,
+ * no GPU needed): over n_picks selections sel [token][k], the distinct
+ * unpinned experts in [e_lo, e_hi) in order of first selection, `per` to a
+ * wave, with the selected pinned experts (pinned[e] != 0) joining wave 0
+ * after its unpinned ones.  wave_of [n_expert]: each expert's wave or -1;
+ * wave_size [n_expert] and wave_experts [n_expert]: the waves' id lists, one
+ * after the other.  Returns the wave count (>= 1), NH_E_STATE for a selection
+ * outside [0, n_expert), NH_E_CAPACITY for an unpinned expert with per <= 0. */
+int nh_plan_waves(const int32_t* sel, int n_picks, int n_expert, int e_lo, int e_hi, int per, const uint8_t* pinned,
+                  int32_t* wave_of, int32_t* wave_size, int32_t* wave_experts);
+
+/* The pairs of wave w grouped by slot (slot_of [n_expert]: each expert's slot
+ * after that wave's Ensure): off/cnt [slots]; for pair i in slot order,
+ * (token, pick) order within a slot, act[i] = j / k and out[i] = j.  Returns
+ * the pair count, or NH_E_STATE when an expert of the wave has no slot. */
+int nh_group_wave_pairs(const int32_t* sel, int n_picks, int k, int n_expert, const int32_t* wave_of, int w,
+                        const int32_t* slot_of, int slots, int32_t* off, int32_t* cnt, int32_t* act, int32_t* out);
+
 /* Cache policies over a flat trace: record r has layer[r] and experts
  * experts[offsets[r]..offsets[r+1]).  kind 0 LruPolicy(n_layers, a)
  * (lru_policy.cc), 1 OsPageCachePolicy(a) (os_page_cache_policy.cc), 2

@@ -347,6 +347,48 @@ def streaming_generate_batch_ex(model: StreamingModel, prompts: Sequence[Sequenc
             "decode_ms": ms.value}
 
 
+def plan_waves(sel: Sequence[int], n_expert: int, per: int, pinned: Sequence[int] | None = None,
+               shard: tuple[int, int] | None = None) -> tuple[list[list[int]], list[int]]:
+    """The slot-pool waves of one batched streaming layer (nh_plan_waves):
+    (id list per wave, wave of every expert or -1).  shard = (first, count)
+    of the experts served here (all by default)."""
+    s = np.ascontiguousarray(np.asarray(sel, dtype=np.int32).ravel())
+    pin = np.zeros(n_expert, dtype=np.uint8)
+    if pinned is not None:
+        pin[np.asarray(list(pinned), dtype=np.int64)] = 1
+    first, count = shard if shard is not None else (0, n_expert)
+    wave_of = np.zeros(n_expert, dtype=np.int32)
+    size = np.zeros(n_expert, dtype=np.int32)
+    ids = np.zeros(n_expert, dtype=np.int32)
+    n = lib().nh_plan_waves(_ptr(s, C.c_int32), int(s.size), n_expert, first, first + count, per,
+                            _ptr(pin, C.c_uint8), _ptr(wave_of, C.c_int32), _ptr(size, C.c_int32),
+                            _ptr(ids, C.c_int32))
+    _check(min(n, 0), "nh_plan_waves")
+    waves, k = [], 0
+    for w in range(n):
+        waves.append(ids[k:k + size[w]].tolist())
+        k += int(size[w])
+    return waves, wave_of.tolist()
+
+
+def group_wave_pairs(sel: Sequence[int], k: int, wave_of: Sequence[int], w: int, slot_of: Sequence[int],
+                     slots: int) -> tuple[list[int], list[int], list[int], list[int]]:
+    """The pairs of wave w grouped by slot (nh_group_wave_pairs): off, cnt per
+    slot, then the token row and pick index of every pair in slot order."""
+    s = np.ascontiguousarray(np.asarray(sel, dtype=np.int32).ravel())
+    wo = np.ascontiguousarray(np.asarray(wave_of, dtype=np.int32))
+    so = np.ascontiguousarray(np.asarray(slot_of, dtype=np.int32))
+    off = np.zeros(slots, dtype=np.int32)
+    cnt = np.zeros(slots, dtype=np.int32)
+    act = np.zeros(max(s.size, 1), dtype=np.int32)
+    out = np.zeros(max(s.size, 1), dtype=np.int32)
+    n = lib().nh_group_wave_pairs(_ptr(s, C.c_int32), int(s.size), k, int(wo.size), _ptr(wo, C.c_int32), w,
+                                  _ptr(so, C.c_int32), slots, _ptr(off, C.c_int32), _ptr(cnt, C.c_int32),
+                                  _ptr(act, C.c_int32), _ptr(out, C.c_int32))
+    _check(min(n, 0), "nh_group_wave_pairs")
+    return off.tolist(), cnt.tolist(), act[:n].tolist(), out[:n].tolist()
+
+
 def StreamingGenerate(model: StreamingModel, ids: Sequence[int], n_predict: int, norm_topk: bool,
                       capacity: int) -> list[int]:
     """Two-phase streaming greedy decode with an LRU slot cache (streaming_forward.cc:228-253)."""

@@ -84,6 +84,10 @@ SIGNATURES = {
     "nh_stream_generate_batch_ep": (C.c_int, [vp, vp, P(i32), C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                               C.c_int, P(u64), P(i32), P(i64), P(i64), P(u64), P(i64),
                                               P(C.c_double)]),
+    "nh_plan_waves": (C.c_int, [P(i32), C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, P(C.c_uint8), P(i32), P(i32),
+                                P(i32)]),
+    "nh_group_wave_pairs": (C.c_int, [P(i32), C.c_int, C.c_int, C.c_int, P(i32), C.c_int, P(i32), C.c_int, P(i32),
+                                      P(i32), P(i32), P(i32)]),
     "nh_replay": (i64, [C.c_int, u32, u32, i64, P(u32), P(i64), P(u32), u32, u32, P(u64), P(i64)]),
     "nh_sweep_budgets": (C.c_int, [u32, u32, i64, P(u32), P(i64), P(u32), P(u32), C.c_int, P(C.c_double)]),
     "nh_sweep_pin_ratio": (C.c_int, [u32, u32, i64, P(u32), P(i64), P(u32), u32, P(C.c_double)]),

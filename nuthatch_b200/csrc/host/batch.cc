@@ -19,6 +19,7 @@
 #include "nuthatch/expert_slot_cache.h"
 #include "nuthatch/streaming_forward.h"
 #include "nuthatch/streaming_model.h"
+#include "wave_plan.h"
 #include "workspace.h"
 #include "nuthatch/generate.h"
 #include "nuthatch/gguf_file.h"
@@ -463,62 +464,33 @@ int StreamedMoe(StreamedExperts& se, int l, const OlmoeConfig& c, int B, const i
   if (cudaMemcpyAsync(sel_host, sel, static_cast<size_t>(BK) * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
       cudaStreamSynchronize(s) != cudaSuccess)
     return NH_E_CUDA;
-  std::vector<int> wave_of(E, -1);
+  std::vector<char> pinned(E, 0);
+  for (int e = 0; e < E; ++e) pinned[e] = cache.is_pinned(e) ? 1 : 0;
   std::vector<std::vector<int>> waves;
-  const int per = cache.lru_slots();
-  for (int j = 0; j < BK; ++j) {
-    const int e = sel_host[j];
-    if (e < 0 || e >= E) return NH_E_STATE;
-    if (e < e_lo || e >= e_hi || cache.is_pinned(e) || wave_of[e] >= 0) continue;
-    if (per <= 0) return NH_E_CAPACITY;
-    if (waves.empty() || static_cast<int>(waves.back().size()) == per) waves.emplace_back();
-    waves.back().push_back(e);
-    wave_of[e] = static_cast<int>(waves.size()) - 1;
-  }
-  if (waves.empty()) waves.emplace_back();
+  std::vector<int> wave_of;
+  const int n_waves = PlanWaves(sel_host, BK, E, e_lo, e_hi, cache.lru_slots(), pinned, &waves, &wave_of);
+  if (n_waves < 0) return n_waves;
   const int slots = static_cast<int>(cache.gate_slots()->ne[2]);
   if (slots > E) return NH_E_CAPACITY;
   const size_t plan_stride = static_cast<size_t>(2 * E + 2 * BK);
-  for (size_t w = 0; w < waves.size(); ++w) {
-    std::vector<int> ids = waves[w];
-    if (w == 0) {
-      std::vector<char> seen(E, 0);
-      for (int j = 0; j < BK; ++j) {
-        const int e = sel_host[j];
-        if (cache.is_pinned(e) && !seen[e]) {
-          seen[e] = 1;
-          ids.push_back(e);
-        }
-      }
-    } else {
+  std::vector<int> slot_of(E, -1);
+  for (int w = 0; w < n_waves; ++w) {
+    if (w > 0) {
       // The previous wave's products still read slots this wave may refill.
       if (cudaEventRecord(compute_done, s) != cudaSuccess ||
           cudaStreamWaitEvent(se.copy_stream, compute_done, 0) != cudaSuccess)
         return NH_E_CUDA;
     }
-    const std::unordered_map<int, int> slot_of = cache.Ensure(ids);
+    const std::unordered_map<int, int> resident = cache.Ensure(waves[w]);
     if (!cache.ok()) return NH_E_IO;
+    for (const auto& kv : resident) slot_of[kv.first] = kv.second;
     // This wave's pairs grouped by slot, (token, pick) order within a slot.
     int32_t* hoff = plan_host + w * plan_stride;
     int32_t* hcnt = hoff + E;
     int32_t* hact = hcnt + E;
     int32_t* hout = hact + BK;
-    std::fill(hcnt, hcnt + slots, 0);
-    auto in_wave = [&](int e) { return cache.is_pinned(e) ? w == 0 : wave_of[e] == static_cast<int>(w); };
-    for (int j = 0; j < BK; ++j)
-      if (in_wave(sel_host[j])) ++hcnt[slot_of.at(sel_host[j])];
-    int n = 0;
-    for (int g = 0; g < slots; ++g) {
-      hoff[g] = n;
-      n += hcnt[g];
-    }
-    std::vector<int> cursor(hoff, hoff + slots);
-    for (int j = 0; j < BK; ++j) {
-      if (!in_wave(sel_host[j])) continue;
-      const int pos = cursor[slot_of.at(sel_host[j])]++;
-      hact[pos] = j / K;
-      hout[pos] = j;
-    }
+    const int n = GroupWavePairs(sel_host, BK, K, wave_of, w, slot_of, slots, hoff, hcnt, hact, hout);
+    if (n < 0) return n;
     if (cudaMemcpyAsync(off, hoff, static_cast<size_t>(slots) * 4, cudaMemcpyHostToDevice, s) != cudaSuccess ||
         cudaMemcpyAsync(cnt, hcnt, static_cast<size_t>(slots) * 4, cudaMemcpyHostToDevice, s) != cudaSuccess ||
         cudaMemcpyAsync(act_idx, hact, static_cast<size_t>(std::max(n, 1)) * 4, cudaMemcpyHostToDevice, s) !=
@@ -570,7 +542,7 @@ int StreamedMoe(StreamedExperts& se, int l, const OlmoeConfig& c, int B, const i
     NH_B_TRY(nh_batch_rowdot(&g, s));
     NH_B_TRY(cache.Commit(s));
   }
-  se.waves += static_cast<int64_t>(waves.size());
+  se.waves += n_waves;
   se.host_ms += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
   return NH_OK;
 }

@@ -15,6 +15,7 @@
 #include "nuthatch/routing_trace.h"
 #include "nuthatch/streaming_forward.h"
 #include "nuthatch/streaming_model.h"
+#include "wave_plan.h"
 #include "workspace.h"
 
 using namespace nuthatch;
@@ -553,6 +554,31 @@ int nh_slot_cache_read_slot(const void* cache, int which, int slot, void* out, u
                  cudaSuccess
              ? NH_OK
              : NH_E_CUDA;
+}
+
+int nh_plan_waves(const int32_t* sel, int n_picks, int n_expert, int e_lo, int e_hi, int per, const uint8_t* pinned,
+                  int32_t* wave_of, int32_t* wave_size, int32_t* wave_experts) {
+  if (n_expert <= 0 || pinned == nullptr || wave_of == nullptr || wave_size == nullptr || wave_experts == nullptr)
+    return NH_E_ARG;
+  std::vector<char> pin(pinned, pinned + n_expert);
+  std::vector<std::vector<int>> waves;
+  std::vector<int> of;
+  const int n = PlanWaves(sel, n_picks, n_expert, e_lo, e_hi, per, pin, &waves, &of);
+  if (n < 0) return n;
+  size_t k = 0;
+  for (int w = 0; w < n; ++w) {
+    wave_size[w] = static_cast<int32_t>(waves[w].size());
+    for (int e : waves[w]) wave_experts[k++] = e;
+  }
+  for (int e = 0; e < n_expert; ++e) wave_of[e] = of[e];
+  return n;
+}
+
+int nh_group_wave_pairs(const int32_t* sel, int n_picks, int k, int n_expert, const int32_t* wave_of, int w,
+                        const int32_t* slot_of, int slots, int32_t* off, int32_t* cnt, int32_t* act, int32_t* out) {
+  if (n_expert <= 0 || wave_of == nullptr || slot_of == nullptr) return NH_E_ARG;
+  return GroupWavePairs(sel, n_picks, k, std::vector<int>(wave_of, wave_of + n_expert), w,
+                        std::vector<int>(slot_of, slot_of + n_expert), slots, off, cnt, act, out);
 }
 
 }  // extern "C"

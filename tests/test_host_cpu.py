@@ -284,3 +284,70 @@ def test_top5_tool_usage_and_tie_order(capsys):
     assert "usage:" in capsys.readouterr().err
     lg = np.array([0.5, 2.0, 2.0, -1.0, 3.0, 0.5, 2.0], dtype=np.float32)
     assert olmoe_forward.top_k(lg) == [(4, 3.0), (1, 2.0), (2, 2.0), (6, 2.0), (0, 0.5)]
+
+
+def _plan_waves_restated(sel, n_expert, per, pinned, first, count):
+    """The wave rules written out plainly: served unpinned experts in order of
+    first selection, `per` to a wave; selected pinned experts join wave 0
+    after its unpinned ones."""
+    waves, wave_of, pins = [], [-1] * n_expert, []
+    for e in sel:
+        if not first <= e < first + count or wave_of[e] >= 0:
+            continue
+        if e in pinned:
+            wave_of[e] = 0
+            pins.append(e)
+            continue
+        if not waves or len(waves[-1]) == per:
+            waves.append([])
+        waves[-1].append(e)
+        wave_of[e] = len(waves) - 1
+    if not waves:
+        waves.append([])
+    waves[0] += pins
+    return waves, wave_of
+
+
+def test_wave_plan_matches_restated_rules():
+    """Batched streaming waves (nh_plan_waves, nh_group_wave_pairs) on seeded
+    selections: mini, OLMoE and Granite expert counts, with pinned experts and
+    expert-parallel shards; every pick of a served expert lands in exactly one
+    wave's pairs, in slot order and (token, pick) order within a slot."""
+    rng = np.random.default_rng(17)
+    for n_expert, k, n_tok in ((16, 4, 6), (64, 8, 64), (32, 8, 32), (8, 8, 3)):
+        for world in (1, 2, 4):
+            for rank in range(world):
+                count = n_expert // world
+                first = rank * count
+                for per in (1, 2, 5, 8):
+                    sel = np.stack([rng.choice(n_expert, k, replace=False) for _ in range(n_tok)]).ravel()
+                    pinned = set(rng.choice(np.arange(first, first + count), min(2, count), replace=False).tolist())
+                    waves, wave_of = nh.plan_waves(sel, n_expert, per, pinned=sorted(pinned), shard=(first, count))
+                    assert (waves, wave_of) == _plan_waves_restated(sel.tolist(), n_expert, per, pinned, first,
+                                                                    count)
+                    assert all(len([e for e in w if e not in pinned]) <= per for w in waves)
+                    # Slots as an Ensure would give them: one per expert of the wave.
+                    covered = []
+                    for w, ids in enumerate(waves):
+                        slot_of = [-1] * n_expert
+                        for s, e in enumerate(ids):
+                            slot_of[e] = s
+                        off, cnt, act, out = nh.group_wave_pairs(sel, k, wave_of, w, slot_of, max(len(ids), 1))
+                        want = [j for s in range(len(ids)) for j in range(sel.size) if sel[j] == ids[s]]
+                        assert out == want and act == [j // k for j in want]
+                        assert off == [sum(cnt[:s]) for s in range(len(cnt))]
+                        covered += out
+                    served = [j for j in range(sel.size) if first <= sel[j] < first + count]
+                    assert sorted(covered) == served
+
+
+def test_wave_plan_rejections():
+    with pytest.raises(nh.NhError):
+        nh.plan_waves([0, 16], 16, 2)                 # a selection outside [0, n_expert)
+    with pytest.raises(nh.NhError):
+        nh.plan_waves([0, 1], 16, 0)                  # unpinned experts and no LRU slot
+    waves, _ = nh.plan_waves([3, 3], 16, 0, pinned=[3])  # pinned only: no LRU slot needed
+    assert waves == [[3]]
+    assert nh.plan_waves([5, 6], 16, 4, shard=(8, 8))[0] == [[]]  # nothing served here: one empty wave
+    with pytest.raises(nh.NhError):
+        nh.group_wave_pairs([1, 2], 2, [0] * 16, 0, [-1] * 16, 2)  # an expert of the wave without a slot
