@@ -51,6 +51,9 @@ std::vector<int32_t> StreamingGenerateEx(const StreamingModel& model, const std:
 // expert_slot_cache.h:21).  B sequences of equal prompt length advance in
 // lockstep through the batched kernels while each layer's experts stream
 // through a slot pool of `capacity` slots (policy as in StreamingOptions).
+// The prompt runs as GreedyGenerateCachedBatch's does (positions 0..P-2 of
+// every sequence in chunks of up to 512 rows), each chunk's experts streamed
+// like a decode step's.
 // When the batch selects more distinct experts than the pool holds, the layer
 // runs in waves: the distinct unpinned experts, in order of first selection,
 // lru_slots at a time, each wave made resident by one Ensure and its

@@ -158,9 +158,9 @@ std::vector<std::vector<int32_t>> RunBatch(const ModelView& m, const OlmoeConfig
   // C positions at a time as B*C rows, through the batched kernels; the last
   // prompt position is the first decode step, which forms the logits.  Every
   // rank of an expert-parallel group has the same B and P, so the same C and
-  // the same collectives.  The streaming form keeps the position-by-position
-  // prompt (its slot decisions are made per step).
-  const bool prefill = se == nullptr && P > 1 && BatchPrefillEnabled() && Engine::PrefillSupported(m);
+  // the same collectives.  In the streaming form each chunk's experts stream
+  // through the slot pools in waves, as in a decode step.
+  const bool prefill = P > 1 && BatchPrefillEnabled() && Engine::PrefillSupported(m, se == nullptr);
   const int C = prefill ? std::max(1, std::min(P - 1, kBatchPrefillRows / B)) : 1;
   const int R = prefill ? std::max(B, B * C) : B;  // rows of the largest pass
   const int RK = R * static_cast<int>(K);

@@ -86,7 +86,9 @@ class Engine {
   static constexpr int kPrefillChunk = 512;
   int Prefill(const ModelView& m, int n_tok, bool norm_topk, bool trace);
   // Whether the batched kernels cover this model's shapes and weight types.
-  static bool PrefillSupported(const ModelView& m);
+  // experts_resident false: the view has no expert tensors (they stream
+  // through slot pools); only the other tensors are checked.
+  static bool PrefillSupported(const ModelView& m, bool experts_resident = true);
 
   int EnqueueEmbed(const ModelView& m);
   // QKV, attention and the output projection of one layer.

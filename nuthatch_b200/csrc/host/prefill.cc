@@ -97,7 +97,7 @@ int PrefillBuffers::Reserve(const OlmoeConfig& c, int n) {
   return NH_OK;
 }
 
-bool Engine::PrefillSupported(const ModelView& m) {
+bool Engine::PrefillSupported(const ModelView& m, bool experts_resident) {
   const OlmoeConfig& c = m.cfg;
   const int64_t hd = c.head_dim();
   if (!RowLenOk(c.n_embd) || !RowLenOk(c.n_ff) || hd % 32 != 0 || hd > 128 || c.n_expert == 0 ||
@@ -105,7 +105,10 @@ bool Engine::PrefillSupported(const ModelView& m) {
     return false;
   if (!QuantType(m.te) && m.te != NH_TYPE_F32) return false;
   for (const LayerView& L : m.layers) {
-    for (int32_t t : {L.tq, L.tk, L.tv, L.to, L.tg, L.tu, L.td})
+    for (int32_t t : {L.tq, L.tk, L.tv, L.to})
+      if (!QuantType(t)) return false;
+    if (!experts_resident) continue;  // streamed experts: the slot pools' products take any row count
+    for (int32_t t : {L.tg, L.tu, L.td})
       if (!QuantType(t)) return false;
     if (L.gate == nullptr || L.up == nullptr || L.down == nullptr) return false;
   }

@@ -6,9 +6,10 @@ batched streaming form.
 * Resident batch-1 decode and streaming at a budget of 8 of 32 experts per
   layer (LRU and learned pin) against the oracle; streaming hit counts
   against the reference's compiled policies over the GPU's own routing.
-* Batched streaming (StreamingGenerateBatch): when a step's batch selects
-  more distinct experts than the slot pool holds (a precondition violation
-  for the reference, expert_slot_cache.h:21) each layer runs in waves; every
+* Batched streaming (StreamingGenerateBatch): when a step's batch (or a
+  chunk of the prompt) selects more distinct experts than the slot pool
+  holds (a precondition violation for the reference,
+  expert_slot_cache.h:21) each layer runs in waves; every
   sequence's ids equal the resident batched decode, on the mini model and on
   the Granite shape, with LRU and learned-pin pools.
 """
@@ -101,6 +102,9 @@ def test_batched_streaming_waves_match_resident_batch(gpu, synth_dir, spec_name,
     r = nh.streaming_generate_batch_ex(sm, prompts, n_predict, False, capacity, **kw)
     sm.close()
     assert r["tokens"] == ref
-    steps = n_prompt + n_predict - 1
-    assert r["waves"] > steps * cfg.n_layers  # more distinct experts than slots: more than one wave per layer
+    # Passes over the layers: the prompt's 512-row chunks (positions 0..P-2 of
+    # every sequence), then one per decoded id.
+    chunk = min(n_prompt - 1, 512 // n_seq)
+    passes = -(-(n_prompt - 1) // chunk) + n_predict
+    assert r["waves"] > passes * cfg.n_layers  # more distinct experts than slots: more than one wave per layer
     assert int((r["hits"] + r["misses"]).sum()) > 0 and r["h2d_bytes"] > 0
