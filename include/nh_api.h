@@ -164,8 +164,9 @@ int nh_plan_waves(const int32_t* sel, int n_picks, int n_expert, int e_lo, int e
 
 /* The pairs of wave w grouped by slot (slot_of [n_expert]: each expert's slot
  * after that wave's Ensure): off/cnt [slots]; for pair i in slot order,
- * (token, pick) order within a slot, act[i] = j / k and out[i] = j.  Returns
- * the pair count, or NH_E_STATE when an expert of the wave has no slot. */
+ * (token, pick) order within a slot, act[i] = j / k and out[i] = j (act and
+ * out hold up to n_picks entries).  Returns the pair count, or NH_E_STATE
+ * when an expert of the wave has no slot in [0, slots). */
 int nh_group_wave_pairs(const int32_t* sel, int n_picks, int k, int n_expert, const int32_t* wave_of, int w,
                         const int32_t* slot_of, int slots, int32_t* off, int32_t* cnt, int32_t* act, int32_t* out);
 
