@@ -351,3 +351,86 @@ def test_wave_plan_rejections():
     assert nh.plan_waves([5, 6], 16, 4, shard=(8, 8))[0] == [[]]  # nothing served here: one empty wave
     with pytest.raises(nh.NhError):
         nh.group_wave_pairs([1, 2], 2, [0] * 16, 0, [-1] * 16, 2)  # an expert of the wave without a slot
+
+
+REF_TRACE_REPLAY = ROOT / "oracle" / "_ref" / "trace_replay"
+
+
+def _tool_rows(argv, capsys):
+    from nuthatch_b200 import trace_replay
+
+    assert trace_replay.main(argv) == 0
+    return capsys.readouterr().out.splitlines()
+
+
+def _rows_with(lines, suffix):
+    return [ln for ln in lines if ln.rstrip().endswith(suffix)]
+
+
+def test_trace_replay_tool_budget_and_pin_curves(tmp_path, capsys):
+    """trace_replay (trace_replay_main.cc): binary and text traces, default
+    and given budgets, and the pin/LRU split; the rows carry SweepBudgets /
+    SweepPinRatio's numbers in the reference tool's row formats."""
+    tr = _trace("zipf_l4_e64_k8")
+    path = tmp_path / "t.bin"
+    assert nh.WriteRoutingTrace(tr, str(path))
+    text = tmp_path / "t.txt"
+    text.write_text("".join(f"{r.layer} {' '.join(map(str, r.experts))}\n" for r in tr.records))
+    head = f"trace: {len(tr.records)} records, 4 layers, 64 experts/layer"
+    for argv, want in ((["trace_replay", str(path)], [4, 8, 12, 16, 24, 32]),
+                       (["trace_replay", "--text", str(text), "6", "20"], [6, 20])):
+        out = _tool_rows(argv, capsys)
+        assert out[0] == head
+        rows = _rows_with(out, " pp")
+        assert len(rows) == len(want)
+        for ln, (b, learned, lru, osp) in zip(rows, nh.SweepBudgets(tr, want)):
+            assert ln == (f"{b:6d}    {100 * learned:6.1f}%   {100 * lru:6.1f}%   {100 * osp:6.1f}%    "
+                          f"{100 * (learned - lru):+.1f} pp")
+    out = _tool_rows(["trace_replay", str(path), "pin", "8"], capsys)
+    rows = _rows_with(out, "%")
+    assert rows == [f"{p:5d} {lru:4d}   {100 * h:6.1f}%" for p, lru, h in nh.SweepPinRatio(tr, 8)]
+
+
+def test_trace_replay_tool_rejections(tmp_path, capsys):
+    from nuthatch_b200 import trace_replay
+
+    assert trace_replay.main(["trace_replay"]) == 1
+    assert trace_replay.main(["trace_replay", str(tmp_path / "missing.bin")]) == 1
+    assert "read trace failed" in capsys.readouterr().err
+    tr = _trace("uniform_l2_e16_k4")
+    path = tmp_path / "t.bin"
+    assert nh.WriteRoutingTrace(tr, str(path))
+    assert trace_replay.main(["trace_replay", str(path), "eight"]) == 1
+    assert trace_replay.main(["trace_replay", str(path), "pin", "-2"]) == 1
+
+
+@pytest.mark.skipif(not REF_TRACE_REPLAY.exists(), reason="oracle/_ref/trace_replay (the reference tool) not built")
+@pytest.mark.parametrize("name", ["zipf_l4_e64_k8", "phased_l3_e32_k8"])
+def test_trace_replay_tool_rows_equal_reference_tool(tmp_path, capsys, name):
+    """The numeric rows equal the reference's own trace_replay compiled from
+    its sources, except the learned column where the pin cut falls on a count
+    tie (the reference breaks it by hash-map order, this build by expert id)."""
+    import subprocess
+
+    L, E, recs = traces()[name]
+    tr = _trace(name)
+    path = tmp_path / "t.bin"
+    assert nh.WriteRoutingTrace(tr, str(path))
+    exact = 0
+    for args in (["4", "8", "16", "24"], ["pin", "12"]):
+        ref = subprocess.run([str(REF_TRACE_REPLAY), str(path), *args], capture_output=True, text=True, timeout=60)
+        assert ref.returncode == 0, ref.stderr
+        theirs = _rows_with(ref.stdout.splitlines(), " pp" if args[0] != "pin" else "%")
+        ours = _rows_with(_tool_rows(["trace_replay", str(path), *args], capsys), " pp" if args[0] != "pin" else "%")
+        assert len(ours) == len(theirs) > 0
+        assert ref.stdout.splitlines()[0] == f"trace: {len(recs)} records, {L} layers, {E} experts/layer"
+        for a, b in zip(ours, theirs):
+            pin = int(b.split()[0]) if args[0] == "pin" else int(math.ceil(0.75 * int(b.split()[0])))
+            if pin_has_tie(recs, L, pin):
+                # Pin rows: the split only; budget rows: the lru and os columns.
+                cols = slice(0, 2) if args[0] == "pin" else slice(2, 4)
+                assert a.split()[cols] == b.split()[cols]
+                continue
+            assert a == b
+            exact += 1
+    assert exact >= 4
