@@ -170,6 +170,22 @@ int nh_plan_waves(const int32_t* sel, int n_picks, int n_expert, int e_lo, int e
 int nh_group_wave_pairs(const int32_t* sel, int n_picks, int k, int n_expert, const int32_t* wave_of, int w,
                         const int32_t* slot_of, int slots, int32_t* off, int32_t* cnt, int32_t* act, int32_t* out);
 
+/* Tokenizer (tokenizer.h; the reference's src/tokenizer/tokenizer.h).  Load
+ * reads tokenizer.ggml.tokens / .merges of a GGUF (NULL without a
+ * vocabulary); from_lists takes NUL-terminated strings.  encode / decode /
+ * token return the full count of ids or bytes and write at most `cap` of
+ * them; split returns the pre-split chunk count and writes [begin, end) byte
+ * offsets of at most `cap` chunks (2 entries each).  Host only. */
+void* nh_tokenizer_load(const char* path);
+void* nh_tokenizer_from_lists(const char* const* vocab, int64_t n_vocab, const char* const* merges,
+                              int64_t n_merges);
+void nh_tokenizer_free(void* tok);
+int64_t nh_tokenizer_vocab_size(const void* tok);
+int64_t nh_tokenizer_encode(const void* tok, const char* text, int64_t len, int32_t* ids, int64_t cap);
+int64_t nh_tokenizer_decode(const void* tok, const int32_t* ids, int64_t n, char* out, int64_t cap);
+int64_t nh_tokenizer_token(const void* tok, int32_t id, char* out, int64_t cap);
+int64_t nh_tokenizer_split(const char* text, int64_t len, int64_t* bounds, int64_t cap);
+
 /* Cache policies over a flat trace: record r has layer[r] and experts
  * experts[offsets[r]..offsets[r+1]).  kind 0 LruPolicy(n_layers, a)
  * (lru_policy.cc), 1 OsPageCachePolicy(a) (os_page_cache_policy.cc), 2

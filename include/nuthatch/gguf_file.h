@@ -54,6 +54,13 @@ class GgufFile {
   std::unordered_map<std::string, size_t> index_;
 };
 
+// The string arrays stored under `keys` in a GGUF file's metadata (the
+// tensor infos are not read, so any tensor types are fine).  Keys that are
+// absent or hold another type are left out of *out.  false on a missing
+// file, a bad header or truncated metadata.
+bool ReadGgufStringArrays(const std::string& path, const std::vector<std::string>& keys,
+                          std::unordered_map<std::string, std::vector<std::string>>* out);
+
 }  // namespace nuthatch
 
 #endif  // NUTHATCH_B200_GGUF_FILE_H_

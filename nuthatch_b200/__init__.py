@@ -21,7 +21,7 @@ __all__ = ["OlmoeConfig", "OlmoeModel", "StreamingModel", "GreedyGenerate", "Gre
            "GreedyGenerateCachedTrace", "StreamingGenerate", "generate_ex", "streaming_generate_ex",
            "RoutingRecord", "RoutingTrace", "WriteRoutingTrace", "ReadRoutingTrace", "ReadRoutingTraceText",
            "ReplayStats", "LruPolicy", "OsPageCachePolicy", "LearnedPinPolicy", "BuildUsage", "Replay",
-           "SweepBudgets", "SweepBudgetsCalibrated", "SweepPinRatio", "ExpertReader", "ExpertSlotCache", "NhError", "ExpertGroup"]
+           "SweepBudgets", "SweepBudgetsCalibrated", "SweepPinRatio", "ExpertReader", "ExpertSlotCache", "NhError", "ExpertGroup", "Tokenizer"]
 
 
 class NhError(RuntimeError):
@@ -345,6 +345,81 @@ def streaming_generate_batch_ex(model: StreamingModel, prompts: Sequence[Sequenc
            "nh_stream_generate_batch_ep")
     return {"tokens": toks.tolist(), "hits": hits, "misses": misses, "h2d_bytes": h2d.value, "waves": waves.value,
             "decode_ms": ms.value}
+
+
+class Tokenizer:
+    """GPT-2 byte-level BPE tokenizer of an OLMoE GGUF (tokenizer.h:13-44):
+    Encode(text) -> ids, Decode(ids) -> text; the rules are in
+    include/nuthatch/tokenizer.h.  Host only."""
+
+    def __init__(self, handle):
+        self._h = handle
+
+    @staticmethod
+    def Load(path: str) -> Optional["Tokenizer"]:
+        h = lib().nh_tokenizer_load(str(path).encode())
+        return Tokenizer(h) if h else None
+
+    @staticmethod
+    def FromLists(vocab: Sequence[str | bytes], merges: Sequence[str | bytes] = ()) -> "Tokenizer":
+        enc = [v.encode() if isinstance(v, str) else bytes(v) for v in vocab]
+        mer = [m.encode() if isinstance(m, str) else bytes(m) for m in merges]
+        va = (C.c_char_p * max(len(enc), 1))(*enc)
+        ma = (C.c_char_p * max(len(mer), 1))(*mer)
+        h = lib().nh_tokenizer_from_lists(va, len(enc), ma, len(mer))
+        if not h:
+            raise NhError("nh_tokenizer_from_lists failed")
+        return Tokenizer(h)
+
+    def vocab_size(self) -> int:
+        return int(lib().nh_tokenizer_vocab_size(self._h))
+
+    def token(self, id_: int) -> bytes:
+        n = lib().nh_tokenizer_token(self._h, int(id_), None, 0)
+        buf = C.create_string_buffer(max(n, 1))
+        lib().nh_tokenizer_token(self._h, int(id_), buf, n)
+        return buf.raw[:n]
+
+    def Encode(self, text: str | bytes) -> list[int]:
+        raw = text.encode() if isinstance(text, str) else bytes(text)
+        n = lib().nh_tokenizer_encode(self._h, raw, len(raw), None, 0)
+        _check(min(int(n), 0), "nh_tokenizer_encode")
+        ids = np.zeros(max(n, 1), dtype=np.int32)
+        lib().nh_tokenizer_encode(self._h, raw, len(raw), _ptr(ids, C.c_int32), n)
+        return ids[:n].tolist()
+
+    def DecodeBytes(self, ids: Sequence[int]) -> bytes:
+        a = np.ascontiguousarray(np.asarray(list(ids), dtype=np.int32))
+        n = lib().nh_tokenizer_decode(self._h, _ptr(a, C.c_int32), a.size, None, 0)
+        _check(min(int(n), 0), "nh_tokenizer_decode")
+        buf = C.create_string_buffer(max(n, 1))
+        lib().nh_tokenizer_decode(self._h, _ptr(a, C.c_int32), a.size, buf, n)
+        return buf.raw[:n]
+
+    def Decode(self, ids: Sequence[int]) -> str:
+        """The decoded bytes as text (bytes that are not UTF-8 become U+FFFD)."""
+        return self.DecodeBytes(ids).decode("utf-8", errors="replace")
+
+    @staticmethod
+    def Split(text: str | bytes) -> list[tuple[int, int]]:
+        """Pre-split chunks of the text as [begin, end) byte offsets."""
+        raw = text.encode() if isinstance(text, str) else bytes(text)
+        n = lib().nh_tokenizer_split(raw, len(raw), None, 0)
+        _check(min(int(n), 0), "nh_tokenizer_split")
+        b = np.zeros(max(2 * n, 2), dtype=np.int64)
+        lib().nh_tokenizer_split(raw, len(raw), _ptr(b, C.c_int64), n)
+        return [(int(b[2 * i]), int(b[2 * i + 1])) for i in range(n)]
+
+    def close(self) -> None:
+        if self._h:
+            lib().nh_tokenizer_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def plan_waves(sel: Sequence[int], n_expert: int, per: int, pinned: Sequence[int] | None = None,

@@ -88,6 +88,14 @@ SIGNATURES = {
                                 P(i32)]),
     "nh_group_wave_pairs": (C.c_int, [P(i32), C.c_int, C.c_int, C.c_int, P(i32), C.c_int, P(i32), C.c_int, P(i32),
                                       P(i32), P(i32), P(i32)]),
+    "nh_tokenizer_load": (vp, [cp]),
+    "nh_tokenizer_from_lists": (vp, [P(C.c_char_p), i64, P(C.c_char_p), i64]),
+    "nh_tokenizer_free": (None, [vp]),
+    "nh_tokenizer_vocab_size": (i64, [vp]),
+    "nh_tokenizer_encode": (i64, [vp, C.c_char_p, i64, P(i32), i64]),
+    "nh_tokenizer_decode": (i64, [vp, P(i32), i64, C.c_char_p, i64]),
+    "nh_tokenizer_token": (i64, [vp, C.c_int32, C.c_char_p, i64]),
+    "nh_tokenizer_split": (i64, [C.c_char_p, i64, P(i64), i64]),
     "nh_replay": (i64, [C.c_int, u32, u32, i64, P(u32), P(i64), P(u32), u32, u32, P(u64), P(i64)]),
     "nh_sweep_budgets": (C.c_int, [u32, u32, i64, P(u32), P(i64), P(u32), P(u32), C.c_int, P(C.c_double)]),
     "nh_sweep_pin_ratio": (C.c_int, [u32, u32, i64, P(u32), P(i64), P(u32), u32, P(C.c_double)]),

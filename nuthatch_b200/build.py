@@ -50,7 +50,8 @@ def _digest(paths: list[Path], extra: str) -> str:
 
 
 def _headers() -> list[Path]:
-    return sorted(list(INCLUDE.rglob("*.h")) + list(CSRC.rglob("*.h")) + list(CSRC.rglob("*.cuh")))
+    return sorted(list(INCLUDE.rglob("*.h")) + list(CSRC.rglob("*.h")) + list(CSRC.rglob("*.cuh")) +
+                  list(CSRC.rglob("*.inc")))
 
 
 def build_product(verbose: bool = False, phase_trace: bool = False) -> Path:

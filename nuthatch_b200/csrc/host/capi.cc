@@ -1,6 +1,7 @@
 // extern "C" wrappers over the C++ surface (include/nh_api.h).
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstring>
 #include <string>
 
@@ -15,6 +16,7 @@
 #include "nuthatch/routing_trace.h"
 #include "nuthatch/streaming_forward.h"
 #include "nuthatch/streaming_model.h"
+#include "nuthatch/tokenizer.h"
 #include "wave_plan.h"
 #include "workspace.h"
 
@@ -579,6 +581,62 @@ int nh_group_wave_pairs(const int32_t* sel, int n_picks, int k, int n_expert, co
   if (n_expert <= 0 || wave_of == nullptr || slot_of == nullptr) return NH_E_ARG;
   return GroupWavePairs(sel, n_picks, k, std::vector<int>(wave_of, wave_of + n_expert), w,
                         std::vector<int>(slot_of, slot_of + n_expert), slots, off, cnt, act, out);
+}
+
+void* nh_tokenizer_load(const char* path) {
+  if (path == nullptr) return nullptr;
+  auto t = Tokenizer::Load(path);
+  if (t == nullptr) SetErr(std::string("nh_tokenizer_load: no vocabulary in ") + path);
+  return t.release();
+}
+
+void* nh_tokenizer_from_lists(const char* const* vocab, int64_t n_vocab, const char* const* merges,
+                              int64_t n_merges) {
+  if ((vocab == nullptr && n_vocab > 0) || (merges == nullptr && n_merges > 0) || n_vocab < 0 || n_merges < 0)
+    return nullptr;
+  std::vector<std::string> v(vocab, vocab + n_vocab), m(merges, merges + n_merges);
+  return Tokenizer::FromLists(std::move(v), std::move(m)).release();
+}
+
+void nh_tokenizer_free(void* tok) { delete static_cast<Tokenizer*>(tok); }
+
+int64_t nh_tokenizer_vocab_size(const void* tok) {
+  return tok != nullptr ? static_cast<const Tokenizer*>(tok)->vocab_size() : NH_E_ARG;
+}
+
+int64_t nh_tokenizer_encode(const void* tok, const char* text, int64_t len, int32_t* ids, int64_t cap) {
+  if (tok == nullptr || (text == nullptr && len > 0) || len < 0 || (ids == nullptr && cap > 0)) return NH_E_ARG;
+  const auto v = static_cast<const Tokenizer*>(tok)->Encode(std::string(text != nullptr ? text : "", len));
+  const int64_t n = static_cast<int64_t>(v.size());
+  if (n > 0 && cap > 0) std::memcpy(ids, v.data(), static_cast<size_t>(std::min(n, cap)) * 4);
+  return n;
+}
+
+int64_t nh_tokenizer_decode(const void* tok, const int32_t* ids, int64_t n, char* out, int64_t cap) {
+  if (tok == nullptr || (ids == nullptr && n > 0) || n < 0 || (out == nullptr && cap > 0)) return NH_E_ARG;
+  const std::string s = static_cast<const Tokenizer*>(tok)->Decode(std::vector<int32_t>(ids, ids + n));
+  const int64_t len = static_cast<int64_t>(s.size());
+  if (len > 0 && cap > 0) std::memcpy(out, s.data(), static_cast<size_t>(std::min(len, cap)));
+  return len;
+}
+
+int64_t nh_tokenizer_token(const void* tok, int32_t id, char* out, int64_t cap) {
+  if (tok == nullptr || (out == nullptr && cap > 0)) return NH_E_ARG;
+  const std::string& s = static_cast<const Tokenizer*>(tok)->token(id);
+  const int64_t len = static_cast<int64_t>(s.size());
+  if (len > 0 && cap > 0) std::memcpy(out, s.data(), static_cast<size_t>(std::min(len, cap)));
+  return len;
+}
+
+int64_t nh_tokenizer_split(const char* text, int64_t len, int64_t* bounds, int64_t cap) {
+  if ((text == nullptr && len > 0) || len < 0 || (bounds == nullptr && cap > 0)) return NH_E_ARG;
+  const auto ch = Tokenizer::Split(std::string(text != nullptr ? text : "", len));
+  const int64_t n = static_cast<int64_t>(ch.size());
+  for (int64_t i = 0; i < n && i < cap; ++i) {
+    bounds[2 * i] = static_cast<int64_t>(ch[i].first);
+    bounds[2 * i + 1] = static_cast<int64_t>(ch[i].second);
+  }
+  return n;
 }
 
 }  // extern "C"

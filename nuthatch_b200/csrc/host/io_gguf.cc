@@ -3,6 +3,7 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <cstring>
 #include <vector>
 
@@ -169,6 +170,44 @@ std::unique_ptr<GgufFile> GgufFile::Open(const std::string& path) {
     g->index_[t.name] = i;
   }
   return g;
+}
+
+bool ReadGgufStringArrays(const std::string& path, const std::vector<std::string>& keys,
+                          std::unordered_map<std::string, std::vector<std::string>>* out) {
+  out->clear();
+  auto src = TensorSource::Open(path);
+  if (src == nullptr) return false;
+  Reader r(*src);
+  char magic[4];
+  if (!r.Bytes(magic, 4) || std::memcmp(magic, "GGUF", 4) != 0) return false;
+  const uint32_t version = r.Get<uint32_t>();
+  if (version != 2 && version != 3) return false;
+  r.Get<uint64_t>();  // tensor count
+  const uint64_t n_kv = r.Get<uint64_t>();
+  if (!r.ok() || n_kv > (1u << 24)) return false;
+  for (uint64_t i = 0; i < n_kv && r.ok(); ++i) {
+    std::string key;
+    if (!r.Str(&key)) return false;
+    const uint32_t type = r.Get<uint32_t>();
+    const bool wanted = std::find(keys.begin(), keys.end(), key) != keys.end();
+    if (wanted && type == 9) {
+      const uint32_t et = r.Get<uint32_t>();
+      const uint64_t n = r.Get<uint64_t>();
+      if (!r.ok() || n > (1ull << 28)) return false;
+      if (et == 8) {
+        std::vector<std::string> v(n);
+        for (uint64_t j = 0; j < n; ++j)
+          if (!r.Str(&v[j])) return false;
+        (*out)[key] = std::move(v);
+        continue;
+      }
+      for (uint64_t j = 0; j < n && r.ok(); ++j) r.Skip(et, 1);
+      if (!r.ok()) return false;
+      continue;
+    }
+    if (!r.Skip(type)) return false;
+  }
+  return r.ok();
 }
 
 bool GgufFile::GetU32(const std::string& key, uint32_t* out) const {
