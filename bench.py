@@ -528,6 +528,77 @@ def run_granite(args) -> None:
         dist.destroy_process_group()
 
 
+def run_tokenizer(args) -> None:
+    """The tokenizer (host only, no GPU): Encode throughput over seeded
+    multi-script text of about 8 MB (words of Latin, Cyrillic, Greek, Arabic,
+    Devanagari and CJK scripts, digits, punctuation, emoji, mixed whitespace)
+    with a 16,000-entry byte-level BPE vocabulary trained on the same kind of
+    text by the HF `tokenizers` trainer (the real OLMoE vocabulary is not
+    available offline).  value = input MB/s on one host thread; the oracle's
+    restatement (Python, rescanning merges) is timed on a 200 KB sample."""
+    import json as _json
+
+    from tokenizers import Tokenizer as HfTokenizer, models, pre_tokenizers, trainers
+
+    import nuthatch_b200 as nh
+    from nuthatch_b200 import build
+    from oracle.tokenizer import OracleTokenizer
+
+    build.build_product()
+    words = ["the", "quick", "brown", "fox", "jumps", "over", "lazy", "dog", "Paris", "naïve", "café", "Straße",
+             "東京", "数据", "Москва", "λόγος", "مرحبا", "हिन्दी", "2024", "3.14", "don't", "it's", "we're", "!!", "?",
+             "...", "(x)", "#1", "😀", "€5"]
+    spaces = [" "] * 12 + ["\n", "\n\n", "  ", "\t"]
+    rng = np.random.default_rng(7)
+
+    def text(n_words: int) -> str:
+        w = rng.integers(len(words), size=n_words)
+        sp = rng.integers(len(spaces), size=n_words)
+        return "".join(words[a] + spaces[b] for a, b in zip(w, sp))
+
+    hf = HfTokenizer(models.BPE())
+    hf.pre_tokenizer = pre_tokenizers.ByteLevel(add_prefix_space=False)
+    hf.train_from_iterator([text(200) for _ in range(2000)],
+                           trainers.BpeTrainer(vocab_size=16000, show_progress=False,
+                                               initial_alphabet=pre_tokenizers.ByteLevel.alphabet()))
+    model = _json.loads(hf.to_str())["model"]
+    vocab = [t for t, _ in sorted(model["vocab"].items(), key=lambda kv: kv[1])]
+    merges = [m if isinstance(m, str) else " ".join(m) for m in model["merges"]]
+    tok = nh.Tokenizer.FromLists(vocab, merges)
+    body = text(1_200_000)
+    raw = body.encode()
+    tok.Encode(body[:10000])
+    times = []
+    for _ in range(max(1, args.steps)):
+        t0 = time.perf_counter()
+        ids = tok.Encode(raw)
+        times.append(time.perf_counter() - t0)
+    best = min(times)
+    t0 = time.perf_counter()
+    hf.encode(body)
+    hf_s = time.perf_counter() - t0
+    sample = body[:200_000]
+    ora = OracleTokenizer(vocab, merges)
+    t0 = time.perf_counter()
+    ora_ids = ora.encode(sample)
+    ora_s = time.perf_counter() - t0
+    same = tok.Encode(sample) == ora_ids
+    line = {"metric": "tokenizer Encode MB/s (GPT-2 byte-level BPE, 16k vocabulary)", "value": len(raw) / best / 1e6,
+            "unit": "MB/s", "n_gpus": 0, "steps": len(times), "warmup": 1, "ms_per_step": best * 1000.0,
+            "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "bytes",
+            "data": "synthetic (seeded multi-script text; vocabulary trained on the same kind of text)",
+            "config": {"workload": f"tokenizer-encode ({len(raw) / 1e6:.1f} MB, {len(ids)} ids)",
+                       "parallelism": "one host thread"},
+            "tokens_per_s": len(ids) / best,
+            "hf_tokenizers_mb_s": {"value": len(raw) / hf_s / 1e6,
+                                   "note": "HF tokenizers' encode of the same text (GPT-2 pre-split, one call), "
+                                           "for context"},
+            "cpu_baseline": {"value": len(sample.encode()) / ora_s / 1e6, "unit": "MB/s", "cores": 1, "kind": "port",
+                             "sample": "200 KB of the same text through oracle/tokenizer.py",
+                             "ids_equal": same}}
+    print(json.dumps(line), flush=True)
+
+
 def run_ep_batched(args, dist, rank: int, world: int, local_rank: int, path: str, full_model) -> dict | None:
     """Expert-parallel batched decode (the configuration-3 workload: bs64,
     2048-token seeded contexts, 128 greedy steps) over the `world` GPUs of
@@ -638,7 +709,8 @@ def main() -> None:
                     help="prefill, warm-up, then exactly one timed-step's decode and exit (for ncu launch lists)")
     ap.add_argument("--profile-layers", type=int, default=0,
                     help="with --profile: the same OLMoE-1B-7B width cut to this many layers (small ncu captures)")
-    ap.add_argument("--workload", default="resident", choices=["resident", "streaming", "batched", "prefill", "granite"])
+    ap.add_argument("--workload", default="resident", choices=["resident", "streaming", "batched", "prefill", "granite",
+                                                                     "tokenizer"])
     ap.add_argument("--batch-seqs", type=int, default=64)
     ap.add_argument("--batch-context", type=int, default=2048)
     ap.add_argument("--batch-steps", type=int, default=128)
@@ -662,6 +734,9 @@ def main() -> None:
         return
     if args.workload == "granite":
         run_granite(args)
+        return
+    if args.workload == "tokenizer":
+        run_tokenizer(args)
         return
     if args.workload == "streaming":
         args.steps = min(args.steps, 3)

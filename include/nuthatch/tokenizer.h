@@ -20,6 +20,7 @@
 
 #include <cstdint>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <unordered_map>
 #include <utility>
@@ -56,11 +57,19 @@ class Tokenizer {
   Tokenizer(std::vector<std::string> vocab, std::vector<std::string> merges);
   void EncodeChunk(const char* p, size_t n, std::vector<int32_t>* out) const;
 
+  // Symbols (every string the merges can form, and the vocabulary) are
+  // interned as integers: a merge "A B" of rank r is the pair (A, B) ->
+  // (r, AB).  Byte-level symbols never hold U+0020, so a merge string with
+  // other than one space can never apply and is left out.
   std::vector<std::string> vocab_;
-  std::unordered_map<std::string, int32_t> id_of_;
-  std::unordered_map<std::string, int> merge_rank_;  // "A B" -> rank
-  std::string byte_sym_[256];                        // byte -> its byte-level character (UTF-8)
-  std::unordered_map<uint32_t, uint8_t> sym_byte_;   // byte-level code point -> byte
+  std::vector<int32_t> sym_id_;                               // symbol -> vocabulary id or -1
+  std::unordered_map<uint64_t, std::pair<int, int>> merge_;  // (A << 32 | B) -> (rank, AB)
+  int byte_sym_[256];                                         // byte -> symbol of its byte-level character
+  std::unordered_map<uint32_t, uint8_t> char_byte_;           // byte-level code point -> byte
+  // Ids of recently seen chunks (words repeat); bounded, guarded for
+  // concurrent Encode calls.
+  mutable std::mutex cache_mu_;
+  mutable std::unordered_map<std::string, std::vector<int32_t>> cache_;
 };
 
 }  // namespace nuthatch

@@ -382,10 +382,9 @@ class Tokenizer:
 
     def Encode(self, text: str | bytes) -> list[int]:
         raw = text.encode() if isinstance(text, str) else bytes(text)
-        n = lib().nh_tokenizer_encode(self._h, raw, len(raw), None, 0)
+        ids = np.empty(max(len(raw), 1), dtype=np.int32)  # every id covers at least one byte
+        n = lib().nh_tokenizer_encode(self._h, raw, len(raw), _ptr(ids, C.c_int32), ids.size)
         _check(min(int(n), 0), "nh_tokenizer_encode")
-        ids = np.zeros(max(n, 1), dtype=np.int32)
-        lib().nh_tokenizer_encode(self._h, raw, len(raw), _ptr(ids, C.c_int32), n)
         return ids[:n].tolist()
 
     def DecodeBytes(self, ids: Sequence[int]) -> bytes:

@@ -176,15 +176,32 @@ std::vector<std::pair<size_t, size_t>> Tokenizer::Split(const std::string& text)
 }
 
 Tokenizer::Tokenizer(std::vector<std::string> vocab, std::vector<std::string> merges) : vocab_(std::move(vocab)) {
+  std::unordered_map<std::string, int> sym_of;
+  auto intern = [&](const std::string& text) {
+    return sym_of.emplace(text, static_cast<int>(sym_of.size())).first->second;
+  };
   int extra = 0;
   for (int b = 0; b < 256; ++b) {
     const uint32_t cp = ByteLevelCodePoint(b, &extra);
-    byte_sym_[b] = EncodeUtf8(cp);
-    sym_byte_[cp] = static_cast<uint8_t>(b);
+    byte_sym_[b] = intern(EncodeUtf8(cp));
+    char_byte_[cp] = static_cast<uint8_t>(b);
   }
-  // The first occurrence of a string or a merge keeps its id / rank.
-  for (size_t i = 0; i < vocab_.size(); ++i) id_of_.emplace(vocab_[i], static_cast<int32_t>(i));
-  for (size_t i = 0; i < merges.size(); ++i) merge_rank_.emplace(merges[i], static_cast<int>(i));
+  for (const std::string& v : vocab_) intern(v);
+  for (size_t r = 0; r < merges.size(); ++r) {
+    const std::string& m = merges[r];
+    const size_t sp = m.find(' ');
+    if (sp == std::string::npos || sp == 0 || sp + 1 == m.size() || m.find(' ', sp + 1) != std::string::npos) continue;
+    const std::string a = m.substr(0, sp), b = m.substr(sp + 1);
+    const uint64_t key = static_cast<uint64_t>(intern(a)) << 32 | static_cast<uint32_t>(intern(b));
+    const int ab = intern(a + b);
+    merge_.emplace(key, std::make_pair(static_cast<int>(r), ab));  // the first rank of a pair stays
+  }
+  // The first occurrence of a vocabulary string keeps its id.
+  sym_id_.assign(sym_of.size(), -1);
+  for (size_t i = 0; i < vocab_.size(); ++i) {
+    int32_t& id = sym_id_[sym_of.at(vocab_[i])];
+    if (id < 0) id = static_cast<int32_t>(i);
+  }
 }
 
 Tokenizer::~Tokenizer() = default;
@@ -213,12 +230,21 @@ const std::string& Tokenizer::token(int32_t id) const {
 // a min-heap holds every adjacent pair that has a merge, keyed by (rank,
 // position of the left symbol), so the pair merged next is the lowest rank,
 // leftmost among equal ranks, as a full rescan would pick.  Entries made
-// stale by an earlier merge are recognised by the symbols' versions.
+// stale by an earlier merge are recognised by the symbols' versions.  Chunks
+// seen before take their ids from the cache.
 void Tokenizer::EncodeChunk(const char* p, size_t n, std::vector<int32_t>* out) const {
   if (n == 0) return;
+  const std::string chunk(p, n);
+  {
+    std::lock_guard<std::mutex> hold(cache_mu_);
+    auto hit = cache_.find(chunk);
+    if (hit != cache_.end()) {
+      out->insert(out->end(), hit->second.begin(), hit->second.end());
+      return;
+    }
+  }
   struct Sym {
-    std::string text;
-    int prev, next;
+    int sym, prev, next;
     unsigned version;
   };
   std::vector<Sym> sym(n);
@@ -226,27 +252,25 @@ void Tokenizer::EncodeChunk(const char* p, size_t n, std::vector<int32_t>* out) 
     sym[i] = {byte_sym_[static_cast<unsigned char>(p[i])], static_cast<int>(i) - 1,
               i + 1 < n ? static_cast<int>(i) + 1 : -1, 0};
   struct Cand {
-    int rank, left, right;
+    int rank, left, right, merged;
     unsigned vl, vr;
     bool operator>(const Cand& o) const { return rank != o.rank ? rank > o.rank : left > o.left; }
   };
   std::priority_queue<Cand, std::vector<Cand>, std::greater<Cand>> heap;
-  std::string key;
   auto offer = [&](int l) {
     const int r = l >= 0 ? sym[l].next : -1;
-    if (l < 0 || r < 0) return;
-    key.assign(sym[l].text).append(1, ' ').append(sym[r].text);
-    auto it = merge_rank_.find(key);
-    if (it != merge_rank_.end()) heap.push({it->second, l, r, sym[l].version, sym[r].version});
+    if (r < 0) return;
+    auto it = merge_.find(static_cast<uint64_t>(sym[l].sym) << 32 | static_cast<uint32_t>(sym[r].sym));
+    if (it != merge_.end()) heap.push({it->second.first, l, r, it->second.second, sym[l].version, sym[r].version});
   };
   for (int i = 0; i + 1 < static_cast<int>(n); ++i) offer(i);
   while (!heap.empty()) {
     const Cand c = heap.top();
     heap.pop();
     Sym& L = sym[c.left];
-    if (L.next != c.right || L.version != c.vl || sym[c.right].version != c.vr) continue;
     Sym& R = sym[c.right];
-    L.text += R.text;
+    if (L.next != c.right || L.version != c.vl || R.version != c.vr) continue;
+    L.sym = c.merged;
     ++L.version;
     ++R.version;  // R leaves the list
     L.next = R.next;
@@ -254,10 +278,13 @@ void Tokenizer::EncodeChunk(const char* p, size_t n, std::vector<int32_t>* out) 
     offer(L.prev);
     offer(c.left);
   }
-  for (int i = 0; i >= 0; i = sym[i].next) {
-    auto it = id_of_.find(sym[i].text);
-    if (it != id_of_.end()) out->push_back(it->second);
-  }
+  std::vector<int32_t> ids;
+  for (int i = 0; i >= 0; i = sym[i].next)
+    if (sym_id_[sym[i].sym] >= 0) ids.push_back(sym_id_[sym[i].sym]);
+  out->insert(out->end(), ids.begin(), ids.end());
+  std::lock_guard<std::mutex> hold(cache_mu_);
+  if (cache_.size() >= (1u << 16)) cache_.clear();
+  cache_.emplace(chunk, std::move(ids));
 }
 
 std::vector<int32_t> Tokenizer::Encode(const std::string& text) const {
@@ -290,8 +317,8 @@ std::string Tokenizer::Decode(const std::vector<int32_t>& ids) const {
         len = 3;
       }
       i += len;
-      auto it = sym_byte_.find(cp);
-      if (it != sym_byte_.end()) out += static_cast<char>(it->second);
+      auto it = char_byte_.find(cp);
+      if (it != char_byte_.end()) out += static_cast<char>(it->second);
     }
   }
   return out;
