@@ -193,7 +193,9 @@ bool ReadGgufStringArrays(const std::string& path, const std::vector<std::string
     if (wanted && type == 9) {
       const uint32_t et = r.Get<uint32_t>();
       const uint64_t n = r.Get<uint64_t>();
-      if (!r.ok() || n > (1ull << 28)) return false;
+      // Every string takes at least its 8-byte length: a count beyond what
+      // the file holds is corrupt (and must not size an allocation).
+      if (!r.ok() || n > (src->file_size() - r.pos()) / 8) return false;
       if (et == 8) {
         std::vector<std::string> v(n);
         for (uint64_t j = 0; j < n; ++j)

@@ -104,6 +104,14 @@ def test_returns_null_without_vocab(tmp_path):
     bad = tmp_path / "bad.gguf"
     bad.write_bytes(b"GGUF\x03\x00\x00\x00")  # truncated header
     assert nh.Tokenizer.Load(str(bad)) is None
+    # A string array claiming more entries than the file can hold.
+    import struct
+
+    key = b"tokenizer.ggml.tokens"
+    huge = tmp_path / "huge.gguf"
+    huge.write_bytes(b"GGUF" + struct.pack("<IQQ", 3, 0, 1) + struct.pack("<Q", len(key)) + key +
+                     struct.pack("<IIQ", 9, 8, 1 << 27))
+    assert nh.Tokenizer.Load(str(huge)) is None
 
 
 # ------------------------------------------------------------------ pre-split
