@@ -1,6 +1,6 @@
 /* nh_api.h — C ABI of the host library (libnuthatch_b200.so) for FFI
  * callers (ctypes, cgo, JNI).  Each function wraps the C++ surface in
- * include/nuthatch/*.h, which mirrors the reference's C++ API (namespace
+ * the headers of include/nuthatch/, which mirror the reference's C++ API (namespace
  * nuthatch); citations are to the reference function each one replaces.
  *
  * Conventions: objects are opaque pointers, NULL on failure (as the
