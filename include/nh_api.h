@@ -172,7 +172,7 @@ int nh_group_wave_pairs(const int32_t* sel, int n_picks, int k, int n_expert, co
 
 /* Tokenizer (tokenizer.h; the reference's src/tokenizer/tokenizer.h).  Load
  * reads tokenizer.ggml.tokens / .merges of a GGUF (NULL without a
- * vocabulary); from_lists takes NUL-terminated strings.  encode / decode /
+ * vocabulary); from_lists takes NUL-terminated strings (NULL if any is NULL).  encode / decode /
  * token return the full count of ids or bytes and write at most `cap` of
  * them; split returns the pre-split chunk count and writes [begin, end) byte
  * offsets of at most `cap` chunks (2 entries each).  Host only. */

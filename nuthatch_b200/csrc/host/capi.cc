@@ -594,6 +594,10 @@ void* nh_tokenizer_from_lists(const char* const* vocab, int64_t n_vocab, const c
                               int64_t n_merges) {
   if ((vocab == nullptr && n_vocab > 0) || (merges == nullptr && n_merges > 0) || n_vocab < 0 || n_merges < 0)
     return nullptr;
+  for (int64_t i = 0; i < n_vocab; ++i)
+    if (vocab[i] == nullptr) return nullptr;
+  for (int64_t i = 0; i < n_merges; ++i)
+    if (merges[i] == nullptr) return nullptr;
   std::vector<std::string> v(vocab, vocab + n_vocab), m(merges, merges + n_merges);
   return Tokenizer::FromLists(std::move(v), std::move(m)).release();
 }
