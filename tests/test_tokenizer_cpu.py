@@ -114,6 +114,32 @@ def test_returns_null_without_vocab(tmp_path):
     assert nh.Tokenizer.Load(str(huge)) is None
 
 
+def test_vocabulary_of_another_type_is_no_vocabulary(tmp_path):
+    """tokenizer.ggml.tokens must be a string array; merges of another type
+    count as absent (tokenizer.cc:74-85)."""
+    import gguf
+
+    p1 = tmp_path / "ints.gguf"
+    w = gguf.GGUFWriter(str(p1), "olmoe")
+    w.add_array("tokenizer.ggml.tokens", [1, 2, 3])
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    assert nh.Tokenizer.Load(str(p1)) is None
+    p2 = tmp_path / "intmerges.gguf"
+    w = gguf.GGUFWriter(str(p2), "olmoe")
+    w.add_token_list(["h", "i", "hi"])
+    w.add_array("tokenizer.ggml.merges", [7, 8])
+    w.add_array("tokenizer.ggml.token_type", [1, 1, 1])
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    tk = nh.Tokenizer.Load(str(p2))
+    assert tk is not None and tk.vocab_size() == 3 and tk.Encode("hi") == [0, 1]
+
+
 # ------------------------------------------------------------------ pre-split
 def test_split_matches_the_pattern_on_random_text():
     rng = np.random.default_rng(11)
