@@ -1,6 +1,6 @@
 // Batched greedy decode: GreedyGenerateCachedBatch (no reference
-// counterpart; the batched form of generate.cc:55-106 that the survey's
-// boundary calls for).  B sequences of equal prompt length advance one
+// counterpart; the batched form of generate.cc:55-106 for serving many
+// sequences at once).  B sequences of equal prompt length advance one
 // position per step in lockstep; every step is one sequence of kernel
 // launches (nh_batch_* in nh_kernels.h), captured once as a CUDA graph and
 // replayed.
