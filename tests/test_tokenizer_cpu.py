@@ -217,3 +217,28 @@ def test_decode_follows_reference_byte_rules():
         ids = rng.integers(-3, 320, int(rng.integers(0, 12))).tolist()
         assert tk.DecodeBytes(ids) == ora.decode(ids)
     assert tk.token(0) == vocab[0].encode() and tk.token(-1) == b"" and tk.token(300) == b""
+
+
+def test_c_entries_report_full_counts_and_write_at_most_cap(trained):
+    """nh_tokenizer_encode / decode / token / split return the full count and
+    write no more than `cap` entries."""
+    import ctypes as C
+
+    from nuthatch_b200._lib import lib
+
+    _, vocab, merges = trained
+    tk = nh.Tokenizer.FromLists(vocab, merges)
+    text = "the quick brown fox jumps over the lazy dog".encode()
+    full = tk.Encode(text)
+    ids = (C.c_int32 * 8)(*([-7] * 8))
+    n = lib().nh_tokenizer_encode(tk._h, text, len(text), ids, 3)
+    assert n == len(full) and list(ids[:3]) == full[:3] and list(ids[3:]) == [-7] * 5
+    arr = (C.c_int32 * len(full))(*full)
+    buf = C.create_string_buffer(b"#" * 16, 16)
+    m = lib().nh_tokenizer_decode(tk._h, arr, len(full), buf, 5)
+    assert m == len(text) and buf.raw[:5] == text[:5] and buf.raw[5:] == b"#" * 11
+    bounds = (C.c_int64 * 4)(*([-1] * 4))
+    k = lib().nh_tokenizer_split(text, len(text), bounds, 1)
+    assert k == 9 and list(bounds) == [0, 3, -1, -1]
+    assert lib().nh_tokenizer_encode(None, text, len(text), None, 0) < 0
+    assert lib().nh_tokenizer_from_lists((C.c_char_p * 2)(b"a", None), 2, None, 0) is None
